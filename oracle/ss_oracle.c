@@ -1,0 +1,517 @@
+/*
+ * ss_oracle.c -- CPU restatement of SlipStream's decode path (llama variant).
+ *
+ * TEST INFRASTRUCTURE ONLY (see ss_oracle.h).  Reference = harrisonfar123/
+ * PhoneMap, SlipStream/ (abbreviated SS/ below).  Scope is the path the CUDA
+ * backend replaces: embedding -> L x (RMSNorm, Q/K/V GEMV, RoPE, int8 KV
+ * encode, GQA attention, O GEMV + residual, RMSNorm, gate/up GEMV, SwiGLU, down
+ * GEMV + residual) -> final RMSNorm -> lm_head, plus greedy argmax.  The
+ * Gemma/Qwen/Phi/NeoX branches of the reference are out of scope.
+ *
+ * Arithmetic order is the reference's: every dot product is one sequential
+ * fp32 sum (the Accelerate stand-in used to build the reference on Linux),
+ * every product and sum is rounded separately (gcc -O2, no FMA), and libm's
+ * expf/powf/cosf/sinf/roundf/sqrtf are called as the reference calls them.
+ * Rows of a matvec and heads of attention are independent, so they run on
+ * OpenMP threads without changing any result.
+ */
+#include "ss_oracle.h"
+
+#include <fcntl.h>
+#include <float.h>
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+enum { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8 };
+
+/* ---------------------------------------------------------------- numerics */
+
+/* SS/src/core/quantize.c:20-56 (IEEE half -> float, subnormals normalised). */
+float sso_f16_to_f32(uint16_t h) {
+    uint32_t sign = (uint32_t)(h & 0x8000) << 16;
+    uint32_t e = (h >> 10) & 0x1F, m = h & 0x3FF, bits;
+    if (e == 0) {
+        if (m == 0) {
+            bits = sign;
+        } else {
+            e = 1;
+            while (!(m & 0x400)) { m <<= 1; e--; }
+            m &= 0x3FF;
+            bits = sign | ((e + 112) << 23) | (m << 13);
+        }
+    } else if (e == 31) {
+        bits = sign | 0x7F800000u | (m << 13);
+    } else {
+        bits = sign | ((e + 112) << 23) | (m << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+static size_t type_size(int t) { return t == T_F32 ? 4 : t == T_F16 ? 2 : t == T_Q4_0 ? 18 : t == T_Q8_0 ? 34 : 0; }
+static int block_size(int t) { return (t == T_Q4_0 || t == T_Q8_0) ? 32 : 1; }
+
+/* SS/src/core/quantize.c:60-72 (Q4_0) and :139-149 (Q8_0), F32 passthrough
+ * (:391-393), F16 (dequant_f16). */
+void sso_dequantize(const void *src, float *dst, int32_t n, int32_t type) {
+    const uint8_t *p = (const uint8_t *)src;
+    if (type == T_F32) { memcpy(dst, src, (size_t)n * 4); return; }
+    if (type == T_F16) {
+        for (int32_t i = 0; i < n; i++) {
+            uint16_t h; memcpy(&h, p + 2 * i, 2);
+            dst[i] = sso_f16_to_f32(h);
+        }
+        return;
+    }
+    for (int32_t b = 0; b < n / 32; b++) {
+        uint16_t dh;
+        if (type == T_Q4_0) {
+            const uint8_t *blk = p + (size_t)b * 18;
+            memcpy(&dh, blk, 2);
+            float scale = sso_f16_to_f32(dh);
+            for (int i = 0; i < 16; i++) {
+                uint8_t byte = blk[2 + i];
+                dst[b * 32 + i] = scale * ((int32_t)(byte & 0xF) - 8);
+                dst[b * 32 + i + 16] = scale * ((int32_t)(byte >> 4) - 8);
+            }
+        } else if (type == T_Q8_0) {
+            const uint8_t *blk = p + (size_t)b * 34;
+            memcpy(&dh, blk, 2);
+            float scale = sso_f16_to_f32(dh);
+            for (int i = 0; i < 32; i++) dst[b * 32 + i] = scale * (int8_t)blk[2 + i];
+        } else {
+            memset(dst, 0, (size_t)n * 4);
+            return;
+        }
+    }
+}
+
+/* Sequential fp32 dot: the order the reference's vDSP_dotpr calls get. */
+static float dot_seq(const float *a, const float *b, int32_t n) {
+    float s = 0.0f;
+    for (int32_t i = 0; i < n; i++) s += a[i] * b[i];
+    return s;
+}
+
+/* SS/src/core/quantize.c:446-494: per row, dequantize into a temp, then
+ * vDSP_dotpr(tmp, x).  F32 matrices use ss_matvec -> ss_neon_dot scalar
+ * (SS/src/backends/cpu_neon.c:55-62), the same sequential sum. */
+void sso_dequant_matvec(float *out, const void *w, const float *x, int32_t rows,
+                        int32_t cols, int32_t type) {
+    size_t row_bytes = (size_t)(cols / block_size(type)) * type_size(type);
+    #pragma omp parallel
+    {
+        float *tmp = (float *)malloc((size_t)cols * sizeof(float));
+        #pragma omp for schedule(static)
+        for (int32_t r = 0; r < rows; r++) {
+            sso_dequantize((const uint8_t *)w + (size_t)r * row_bytes, tmp, cols, type);
+            out[r] = dot_seq(tmp, x, cols);
+        }
+        free(tmp);
+    }
+}
+
+/* SS/src/backends/cpu_neon.c:109-115 (scalar ss_neon_rmsnorm, reached from
+ * ss_rmsnorm SS/src/core/tensor.c:114-118 for F32 weights). */
+void sso_rmsnorm(float *out, const float *x, const float *w, int32_t n, float eps) {
+    float ss = 0.0f;
+    for (int32_t i = 0; i < n; i++) ss += x[i] * x[i];
+    float scale = 1.0f / sqrtf(ss / (float)n + eps);
+    for (int32_t i = 0; i < n; i++) out[i] = x[i] * scale * w[i];
+}
+
+/* SS/src/core/tensor.c:249-274 (non-NeoX RoPE: rotate pairs (i, i+1)). */
+void sso_rope(float *q, float *k, int32_t nh, int32_t nkv, int32_t hd, int32_t rope_dim,
+              int32_t pos, float theta) {
+    for (int32_t i = 0; i < rope_dim; i += 2) {
+        float freq = 1.0f / powf(theta, (float)i / (float)rope_dim);
+        float angle = (float)pos * freq;
+        float c = cosf(angle), s = sinf(angle);
+        for (int32_t h = 0; h < nh; h++) {
+            float *v = q + h * hd;
+            float a = v[i], b = v[i + 1];
+            v[i] = a * c - b * s;
+            v[i + 1] = a * s + b * c;
+        }
+        for (int32_t h = 0; h < nkv; h++) {
+            float *v = k + h * hd;
+            float a = v[i], b = v[i + 1];
+            v[i] = a * c - b * s;
+            v[i + 1] = a * s + b * c;
+        }
+    }
+}
+
+/* SS/src/core/layer_scheduler.c:101-118 (kv_turboquant_encode): one symmetric
+ * int8 scale over the whole kv_dim vector. */
+void sso_kv_encode(const float *src, int8_t *dst, float *scale_out, int32_t n) {
+    float mx = 0.0f;
+    for (int32_t i = 0; i < n; i++) {
+        float v = fabsf(src[i]);
+        if (v > mx) mx = v;
+    }
+    float scale = mx / 127.0f;
+    *scale_out = scale;
+    float inv = scale > 0.0f ? 1.0f / scale : 0.0f;
+    for (int32_t i = 0; i < n; i++) dst[i] = (int8_t)roundf(src[i] * inv);
+}
+
+/* SS/src/core/tensor.c:154-173. */
+void sso_softmax(float *x, int32_t n) {
+    float mx = -FLT_MAX;
+    for (int32_t i = 0; i < n; i++) if (x[i] > mx) mx = x[i];
+    float sum = 0.0f;
+    for (int32_t i = 0; i < n; i++) { x[i] = expf(x[i] - mx); sum += x[i]; }
+    float inv = 1.0f / sum;
+    for (int32_t i = 0; i < n; i++) x[i] *= inv;
+}
+
+/* SS/src/core/tensor.c:318-328: strict '>' so the lowest index wins ties. */
+int32_t sso_argmax(const float *x, int32_t n) {
+    int32_t best = 0;
+    float mv = x[0];
+    for (int32_t i = 1; i < n; i++) if (x[i] > mv) { mv = x[i]; best = i; }
+    return best;
+}
+
+/* ------------------------------------------------------------------ model */
+
+typedef struct { const uint8_t *data; int type; uint64_t rows, cols; } tref_t;
+
+typedef struct {
+    tref_t attn_norm, wq, wk, wv, wo, ffn_norm, wgate, wup, wdown;
+} layer_t;
+
+struct sso_model {
+    uint8_t *map; size_t map_size;
+    int32_t vocab, d, L, nh, nkv, hd, rope_dim, ff, max_seq, kvd;
+    float eps, theta;
+    tref_t embd, out_norm, out;
+    layer_t *layers;
+    /* KV cache, SS/src/core/layer_scheduler.h:19-34 */
+    int8_t *kc, *vc;
+    float *ks, *vs;
+    /* working state, SS/src/core/layer_scheduler.h:38-65 */
+    float *hidden, *residual, *attn_out, *ffn_buf, *ffn_gate, *q, *k, *v, *logits;
+};
+
+typedef struct { const uint8_t *p, *end; int ok; } rd_t;
+static uint64_t rd_u(rd_t *r, int n) {
+    uint64_t v = 0;
+    if (r->p + n > r->end) { r->ok = 0; return 0; }
+    memcpy(&v, r->p, (size_t)n);
+    r->p += n;
+    return v;
+}
+static const char *rd_s(rd_t *r, uint64_t *len) {
+    *len = rd_u(r, 8);
+    const char *s = (const char *)r->p;
+    if (r->p + *len > r->end) { r->ok = 0; return ""; }
+    r->p += *len;
+    return s;
+}
+static void rd_skip(rd_t *r, uint32_t type) {
+    static const int sz[13] = {1, 1, 2, 2, 4, 4, 4, 1, 0, 0, 8, 8, 8};
+    uint64_t len;
+    if (type == 8) { rd_s(r, &len); return; }
+    if (type == 9) {
+        uint32_t at = (uint32_t)rd_u(r, 4);
+        uint64_t n = rd_u(r, 8);
+        for (uint64_t i = 0; i < n && r->ok; i++) rd_skip(r, at);
+        return;
+    }
+    if (type < 13) r->p += sz[type]; else r->ok = 0;
+}
+static int ends_with(const char *s, size_t n, const char *suf) {
+    size_t m = strlen(suf);
+    return n >= m && memcmp(s + n - m, suf, m) == 0;
+}
+
+/* Header/KV/tensor-info walk of SS/src/core/gguf_loader.c:250-431 restated for
+ * the keys this path reads; defaults from :370-379. */
+sso_model_t *sso_load(const char *path, uint32_t context_size, int cap512) {
+    int fd = open(path, O_RDONLY);
+    if (fd < 0) return NULL;
+    struct stat st;
+    if (fstat(fd, &st) != 0) { close(fd); return NULL; }
+    uint8_t *map = (uint8_t *)mmap(NULL, (size_t)st.st_size, PROT_READ, MAP_SHARED, fd, 0);
+    close(fd);
+    if (map == MAP_FAILED) return NULL;
+    sso_model_t *m = (sso_model_t *)calloc(1, sizeof(*m));
+    m->map = map; m->map_size = (size_t)st.st_size;
+    rd_t r = {map, map + st.st_size, 1};
+    if (rd_u(&r, 4) != 0x46554747u) goto fail;
+    rd_u(&r, 4);
+    uint64_t n_t = rd_u(&r, 8), n_kv = rd_u(&r, 8);
+    uint32_t ctx_len = 0, vocab_kv = 0, key_len = 0, rope_dim = 0;
+    for (uint64_t i = 0; i < n_kv && r.ok; i++) {
+        uint64_t kl;
+        const char *k = rd_s(&r, &kl);
+        uint32_t t = (uint32_t)rd_u(&r, 4);
+        #define U32(suf, dst) else if (t == 4 && ends_with(k, kl, suf)) dst = (uint32_t)rd_u(&r, 4)
+        if (0) {}
+        U32(".embedding_length", m->d);
+        U32(".attention.head_count_kv", m->nkv);
+        U32(".attention.head_count", m->nh);
+        U32(".context_length", ctx_len);
+        U32(".feed_forward_length", m->ff);
+        U32(".block_count", m->L);
+        U32(".vocab_size", vocab_kv);
+        U32(".attention.key_length", key_len);
+        U32(".rope.dimension_count", rope_dim);
+        else if (t == 6 && ends_with(k, kl, ".rope.freq_base")) { uint32_t b = (uint32_t)rd_u(&r, 4); memcpy(&m->theta, &b, 4); }
+        else if (t == 6 && ends_with(k, kl, ".attention.layer_norm_rms_epsilon")) { uint32_t b = (uint32_t)rd_u(&r, 4); memcpy(&m->eps, &b, 4); }
+        else rd_skip(&r, t);
+        #undef U32
+    }
+    if (m->eps == 0.0f) m->eps = 1e-5f;
+    if (m->theta == 0.0f) m->theta = 10000.0f;
+    if (ctx_len == 0) ctx_len = 2048;
+    if (m->nkv == 0) m->nkv = m->nh;
+    m->layers = (layer_t *)calloc((size_t)m->L, sizeof(layer_t));
+    typedef struct { const char *name; uint64_t nl; uint64_t d0, d1; int nd, type; uint64_t off; } ti_t;
+    ti_t *ti = (ti_t *)calloc((size_t)n_t, sizeof(ti_t));
+    for (uint64_t i = 0; i < n_t && r.ok; i++) {
+        ti[i].name = rd_s(&r, &ti[i].nl);
+        ti[i].nd = (int)rd_u(&r, 4);
+        ti[i].d1 = 1;
+        for (int j = 0; j < ti[i].nd; j++) {
+            uint64_t v = rd_u(&r, 8);
+            if (j == 0) ti[i].d0 = v; else if (j == 1) ti[i].d1 = v;
+        }
+        ti[i].type = (int)rd_u(&r, 4);
+        ti[i].off = rd_u(&r, 8);
+    }
+    if (!r.ok) { free(ti); goto fail; }
+    uint64_t data_off = ((uint64_t)(r.p - map) + 31) & ~(uint64_t)31;  /* gguf_loader.c:426 */
+    uint32_t vocab = vocab_kv;
+    for (uint64_t i = 0; i < n_t; i++) {
+        char name[256];
+        size_t nl = ti[i].nl < 255 ? ti[i].nl : 255;
+        memcpy(name, ti[i].name, nl); name[nl] = 0;
+        tref_t tr = {map + data_off + ti[i].off, ti[i].type, ti[i].d1, ti[i].d0};
+        if (!strcmp(name, "token_embd.weight")) {
+            m->embd = tr;
+            if (vocab == 0 && ti[i].nd == 2) vocab = (uint32_t)ti[i].d1;  /* :410-412 */
+        } else if (!strcmp(name, "output_norm.weight")) m->out_norm = tr;
+        else if (!strcmp(name, "output.weight")) m->out = tr;
+        else if (!strncmp(name, "blk.", 4)) {
+            int l = atoi(name + 4);
+            const char *suf = strchr(name + 4, '.');
+            if (l < 0 || l >= m->L || !suf) continue;
+            layer_t *ly = &m->layers[l];
+            if (!strcmp(suf, ".attn_norm.weight")) ly->attn_norm = tr;
+            else if (!strcmp(suf, ".attn_q.weight")) ly->wq = tr;
+            else if (!strcmp(suf, ".attn_k.weight")) ly->wk = tr;
+            else if (!strcmp(suf, ".attn_v.weight")) ly->wv = tr;
+            else if (!strcmp(suf, ".attn_output.weight")) ly->wo = tr;
+            else if (!strcmp(suf, ".ffn_norm.weight")) ly->ffn_norm = tr;
+            else if (!strcmp(suf, ".ffn_gate.weight")) ly->wgate = tr;
+            else if (!strcmp(suf, ".ffn_up.weight")) ly->wup = tr;
+            else if (!strcmp(suf, ".ffn_down.weight")) ly->wdown = tr;
+        }
+    }
+    free(ti);
+    if (!m->embd.data || !m->L || !m->layers[0].wq.data) goto fail;
+    /* head_dim / rope_dim / vocab clamp: SS/src/core/layer_scheduler.c:161-197 */
+    m->hd = key_len ? (int32_t)key_len : (int32_t)(m->layers[0].wq.rows / (uint64_t)m->nh);
+    m->rope_dim = rope_dim ? (int32_t)rope_dim : m->hd;
+    m->vocab = (int32_t)vocab;
+    if (m->out.data && (int32_t)m->out.rows < m->vocab) m->vocab = (int32_t)m->out.rows;
+    if ((int32_t)m->embd.rows < m->vocab) m->vocab = (int32_t)m->embd.rows;
+    /* context: engine.c:99-106 then the scheduler's 512 cap (layer_scheduler.c:199-202) */
+    uint32_t ctx = context_size ? context_size : ctx_len;
+    if (ctx == 0 || ctx > 8192) ctx = 8192;
+    m->max_seq = (int32_t)ctx;
+    if (cap512 && m->max_seq > 512) m->max_seq = 512;
+    m->kvd = m->nkv * m->hd;
+    size_t nv = (size_t)m->L * m->max_seq;
+    m->kc = (int8_t *)calloc(nv * m->kvd, 1);
+    m->vc = (int8_t *)calloc(nv * m->kvd, 1);
+    m->ks = (float *)calloc(nv, 4);
+    m->vs = (float *)calloc(nv, 4);
+    m->hidden = (float *)calloc((size_t)m->d, 4);
+    m->residual = (float *)calloc((size_t)m->d, 4);
+    m->attn_out = (float *)calloc((size_t)(m->d > m->nh * m->hd ? m->d : m->nh * m->hd), 4);
+    m->ffn_buf = (float *)calloc((size_t)m->ff, 4);
+    m->ffn_gate = (float *)calloc((size_t)m->ff, 4);
+    m->q = (float *)calloc((size_t)(m->nh * m->hd), 4);
+    m->k = (float *)calloc((size_t)m->kvd, 4);
+    m->v = (float *)calloc((size_t)m->kvd, 4);
+    m->logits = (float *)calloc((size_t)m->vocab, 4);
+    return m;
+fail:
+    sso_free(m);
+    return NULL;
+}
+
+void sso_free(sso_model_t *m) {
+    if (!m) return;
+    if (m->map) munmap(m->map, m->map_size);
+    free(m->layers); free(m->kc); free(m->vc); free(m->ks); free(m->vs);
+    free(m->hidden); free(m->residual); free(m->attn_out); free(m->ffn_buf);
+    free(m->ffn_gate); free(m->q); free(m->k); free(m->v); free(m->logits);
+    free(m);
+}
+
+void sso_dims(const sso_model_t *m, int32_t *dims) {
+    dims[0] = m->vocab; dims[1] = m->d; dims[2] = m->L; dims[3] = m->nh;
+    dims[4] = m->nkv; dims[5] = m->hd; dims[6] = m->ff; dims[7] = m->max_seq;
+}
+
+/* SS/src/core/layer_scheduler.c:917-936 */
+void sso_reset(sso_model_t *m) {
+    size_t nv = (size_t)m->L * m->max_seq;
+    memset(m->kc, 0, nv * m->kvd);
+    memset(m->vc, 0, nv * m->kvd);
+    memset(m->ks, 0, nv * 4);
+    memset(m->vs, 0, nv * 4);
+    memset(m->hidden, 0, (size_t)m->d * 4);
+}
+
+void sso_kv_row(const sso_model_t *m, int32_t layer, int32_t pos, int8_t *k, int8_t *v,
+                float *ks, float *vs) {
+    size_t vi = (size_t)layer * m->max_seq + pos;
+    memcpy(k, m->kc + vi * m->kvd, (size_t)m->kvd);
+    memcpy(v, m->vc + vi * m->kvd, (size_t)m->kvd);
+    *ks = m->ks[vi];
+    *vs = m->vs[vi];
+}
+
+static void matvec(float *out, const tref_t *w, const float *x, int32_t rows, int32_t cols) {
+    sso_dequant_matvec(out, w->data, x, rows, cols, w->type);
+}
+
+/* SS/src/core/layer_scheduler.c:291-567 (process_layer, llama branch). */
+static void process_layer(sso_model_t *m, int32_t l, int32_t pos) {
+    layer_t *ly = &m->layers[l];
+    int32_t d = m->d, hd = m->hd, nh = m->nh, nkv = m->nkv, kvd = m->kvd;
+    memcpy(m->residual, m->hidden, (size_t)d * 4);                       /* :325 */
+    sso_rmsnorm(m->hidden, m->residual, (const float *)ly->attn_norm.data, d, m->eps);
+    matvec(m->q, &ly->wq, m->hidden, nh * hd, d);                        /* :356-358 */
+    matvec(m->k, &ly->wk, m->hidden, kvd, d);
+    matvec(m->v, &ly->wv, m->hidden, kvd, d);
+    sso_rope(m->q, m->k, nh, nkv, hd, m->rope_dim, pos, m->theta);       /* :405 */
+    size_t vi = (size_t)l * m->max_seq + pos;                            /* :410-413 */
+    sso_kv_encode(m->k, m->kc + vi * kvd, &m->ks[vi], kvd);
+    sso_kv_encode(m->v, m->vc + vi * kvd, &m->vs[vi], kvd);
+    int32_t seq_len = pos + 1, hpk = nh / nkv;                           /* :416-421 */
+    memset(m->attn_out, 0, (size_t)d * 4);
+    float scale = 1.0f / sqrtf((float)hd);
+    #pragma omp parallel for schedule(static)
+    for (int32_t h = 0; h < nh; h++) {                                   /* :424-468 */
+        const float *q = m->q + h * hd;
+        int32_t kh = h / hpk;
+        float *scores = (float *)malloc((size_t)seq_len * 4);
+        float *tmp = (float *)malloc((size_t)hd * 4);
+        for (int32_t t = 0; t < seq_len; t++) {
+            size_t ti = (size_t)l * m->max_seq + t;
+            const int8_t *kq = m->kc + ti * kvd + kh * hd;
+            float ksc = m->ks[ti];
+            for (int32_t i = 0; i < hd; i++) tmp[i] = (float)kq[i] * ksc;
+            scores[t] = dot_seq(q, tmp, hd) * scale;
+        }
+        sso_softmax(scores, seq_len);
+        float *dst = m->attn_out + h * hd;
+        for (int32_t i = 0; i < hd; i++) dst[i] = 0.0f;
+        for (int32_t t = 0; t < seq_len; t++) {
+            float w = scores[t];
+            size_t ti = (size_t)l * m->max_seq + t;
+            const int8_t *vq = m->vc + ti * kvd + kh * hd;
+            float vsc = m->vs[ti];
+            for (int32_t i = 0; i < hd; i++) tmp[i] = (float)vq[i] * vsc;
+            for (int32_t i = 0; i < hd; i++) dst[i] += w * tmp[i];       /* saxpy */
+        }
+        free(scores);
+        free(tmp);
+    }
+    matvec(m->hidden, &ly->wo, m->attn_out, d, nh * hd);                 /* :471-472 */
+    for (int32_t i = 0; i < d; i++) m->hidden[i] = m->hidden[i] + m->residual[i];  /* :484 */
+    memcpy(m->residual, m->hidden, (size_t)d * 4);                       /* :490 */
+    sso_rmsnorm(m->hidden, m->residual, (const float *)ly->ffn_norm.data, d, m->eps);
+    matvec(m->ffn_gate, &ly->wgate, m->hidden, m->ff, d);                /* :512-513 */
+    matvec(m->ffn_buf, &ly->wup, m->hidden, m->ff, d);
+    for (int32_t i = 0; i < m->ff; i++) {                                /* :533-549 */
+        float g = m->ffn_gate[i];
+        m->ffn_buf[i] *= g / (1.0f + expf(-g));
+    }
+    matvec(m->hidden, &ly->wdown, m->ffn_buf, d, m->ff);                 /* :553-554 */
+    for (int32_t i = 0; i < d; i++) m->hidden[i] = m->hidden[i] + m->residual[i];  /* :566 */
+}
+
+static void embed_row(sso_model_t *m, int32_t token, float *dst) {   /* :584-595 */
+    size_t rb = (size_t)(m->d / block_size(m->embd.type)) * type_size(m->embd.type);
+    sso_dequantize(m->embd.data + (size_t)token * rb, dst, m->d, m->embd.type);
+}
+
+static void head(sso_model_t *m, float *logits_out) {                   /* :634-662 */
+    if (m->out_norm.data)
+        sso_rmsnorm(m->hidden, m->hidden, (const float *)m->out_norm.data, m->d, m->eps);
+    const tref_t *lm = m->out.data ? &m->out : &m->embd;
+    matvec(m->logits, lm, m->hidden, m->vocab, m->d);
+    if (logits_out) memcpy(logits_out, m->logits, (size_t)m->vocab * 4);
+}
+
+/* SS/src/core/layer_scheduler.c:571-679 */
+int sso_forward(sso_model_t *m, int32_t token, int32_t pos, float *logits_out) {
+    if (token < 0 || token >= (int32_t)m->embd.rows || pos < 0 || pos >= m->max_seq) return -1;
+    embed_row(m, token, m->hidden);
+    for (int32_t l = 0; l < m->L; l++) process_layer(m, l, pos);
+    head(m, logits_out);
+    return 0;
+}
+
+/* SS/src/core/layer_scheduler.c:681-803: layer-major over the prompt, final
+ * norm and lm_head for the last token only. */
+int sso_prefill(sso_model_t *m, const int32_t *tokens, int32_t n, int32_t start_pos,
+                float *logits_out) {
+    if (n <= 0 || start_pos < 0 || start_pos + n > m->max_seq) return -1;
+    float *bh = (float *)malloc((size_t)n * m->d * 4);
+    for (int32_t i = 0; i < n; i++) {
+        if (tokens[i] < 0 || tokens[i] >= (int32_t)m->embd.rows) { free(bh); return -1; }
+        embed_row(m, tokens[i], bh + (size_t)i * m->d);
+    }
+    for (int32_t l = 0; l < m->L; l++)
+        for (int32_t i = 0; i < n; i++) {
+            memcpy(m->hidden, bh + (size_t)i * m->d, (size_t)m->d * 4);
+            process_layer(m, l, start_pos + i);
+            memcpy(bh + (size_t)i * m->d, m->hidden, (size_t)m->d * 4);
+        }
+    memcpy(m->hidden, bh + (size_t)(n - 1) * m->d, (size_t)m->d * 4);
+    free(bh);
+    head(m, logits_out);
+    return 0;
+}
+
+/* SS/src/core/layer_scheduler.c:805-915: positions from 0, final norm on every
+ * token, mean pool, L2 normalise. */
+int sso_embed(sso_model_t *m, const int32_t *tokens, int32_t n, float *out) {
+    if (n <= 0 || n > m->max_seq) return -1;
+    int32_t d = m->d;
+    float *bh = (float *)malloc((size_t)n * d * 4);
+    for (int32_t i = 0; i < n; i++) embed_row(m, tokens[i], bh + (size_t)i * d);
+    for (int32_t l = 0; l < m->L; l++)
+        for (int32_t i = 0; i < n; i++) {
+            memcpy(m->hidden, bh + (size_t)i * d, (size_t)d * 4);
+            process_layer(m, l, i);
+            memcpy(bh + (size_t)i * d, m->hidden, (size_t)d * 4);
+        }
+    if (m->out_norm.data)
+        for (int32_t i = 0; i < n; i++)
+            sso_rmsnorm(bh + (size_t)i * d, bh + (size_t)i * d, (const float *)m->out_norm.data,
+                        d, m->eps);
+    for (int32_t j = 0; j < d; j++) out[j] = 0.0f;
+    for (int32_t i = 0; i < n; i++)
+        for (int32_t j = 0; j < d; j++) out[j] += bh[(size_t)i * d + j];
+    float inv = 1.0f / (float)n, l2 = 0.0f;
+    for (int32_t j = 0; j < d; j++) { out[j] *= inv; l2 += out[j] * out[j]; }
+    float sc = 1.0f / (sqrtf(l2) + 1e-12f);
+    for (int32_t j = 0; j < d; j++) out[j] *= sc;
+    free(bh);
+    return 0;
+}

@@ -1,0 +1,155 @@
+#!/usr/bin/env python3
+"""Generate the golden fixtures in tests/golden/ from the REFERENCE build.
+
+Runs the reference's own CPU path (oracle/_ref, compiled from the PhoneMap
+sources by oracle/build_ref.py) on the seeded synthetic GGUF models and records:
+
+* ``<config>.npz`` -- prompt, greedy token IDs (temperature 0) for N steps,
+  logits at a few steps, a fingerprint of the GGUF bytes, and the int8 K/V rows
+  plus scales of one (layer, position).
+* ``ops.npz`` -- small known-answer vectors of the single ops: Q4_0/Q8_0
+  dequantization of seeded blocks (including edge blocks: zero scale, extreme
+  nibbles, subnormal/negative scales), dequant-matvec, RMSNorm, RoPE, softmax,
+  argmax ties.
+
+Usage: python tests/golden/make_golden.py [config ...]   (default: small set)
+Needs /root/reference (the reference sources) -- fixtures are committed so the
+tests never need it.
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, ROOT)
+
+import oracle  # noqa: E402
+from phonemap_b200 import configs, synth  # noqa: E402
+from tests.golden.fingerprint import gguf_fingerprint  # noqa: E402
+
+OUT = os.path.dirname(os.path.abspath(__file__))
+
+STEPS = {"tiny": 24, "tiny-mha": 20, "tiny-q8": 20, "tinyllama": 64, "llama2-7b": 64}
+
+
+def make_model_fixture(name: str) -> None:
+    cfg = configs.get(name)
+    steps = STEPS.get(name, 64)
+    path = synth.ensure_gguf(cfg)
+    ref = oracle.RefModel(path, cfg.ctx)
+    prompt = synth.prompt_tokens(cfg)
+    keep = sorted({0, 1, steps // 2, steps - 1})
+    ids, kept = ref.greedy(prompt, steps, keep_logits=keep)
+    layer, pos = min(1, cfg.n_layers - 1), len(prompt) - 1
+    k, v, ks, vs = ref.kv_row(layer, pos)
+    np.savez_compressed(
+        os.path.join(OUT, f"{name}.npz"),
+        prompt=np.array(prompt, np.int32), ids=np.array(ids, np.int32),
+        logit_steps=np.array(keep, np.int32),
+        logits=np.stack([kept[s] for s in keep]).astype(np.float32),
+        fingerprint=np.frombuffer(gguf_fingerprint(path), np.uint8),
+        kv_layer=np.int32(layer), kv_pos=np.int32(pos), k_row=k, v_row=v,
+        kv_scales=np.array([ks, vs], np.float32), ctx=np.int32(cfg.ctx))
+    ref.close()
+    print(f"{name}: {steps} steps, ids[:8]={ids[:8]}")
+
+
+def _blocks_q4(rng, nblk):
+    b = np.zeros((nblk, 18), np.uint8)
+    d = (rng.standard_normal(nblk) * 0.01).astype(np.float16)
+    b[:, 0:2] = d.view(np.uint8).reshape(nblk, 2)
+    b[:, 2:] = rng.integers(0, 256, size=(nblk, 16), dtype=np.uint8)
+    # edge blocks: zero scale, all-0x00 / all-0xFF nibbles, negative, subnormal,
+    # max-normal fp16 scales
+    specials = [0x0000, 0x8000, 0x0001, 0x83FF, 0x7BFF, 0xFBFF, 0x3C00]
+    for i, h in enumerate(specials):
+        b[i, 0:2] = np.array([h], np.uint16).view(np.uint8)
+    b[0, 2:] = 0x00
+    b[1, 2:] = 0xFF
+    b[2, 2:] = 0x88
+    return b
+
+
+def _blocks_q8(rng, nblk):
+    b = np.zeros((nblk, 34), np.uint8)
+    d = (rng.standard_normal(nblk) * 0.01).astype(np.float16)
+    b[:, 0:2] = d.view(np.uint8).reshape(nblk, 2)
+    b[:, 2:] = rng.integers(0, 256, size=(nblk, 32), dtype=np.uint8)
+    specials = [0x0000, 0x8000, 0x0001, 0x83FF, 0x7BFF, 0xFBFF, 0x3C00]
+    for i, h in enumerate(specials):
+        b[i, 0:2] = np.array([h], np.uint16).view(np.uint8)
+    b[0, 2:] = 0x80
+    b[1, 2:] = 0x7F
+    return b
+
+
+def make_ops_fixture() -> None:
+    import ctypes
+    lib = oracle.ref_ops()
+    rng = np.random.default_rng(2024)
+    fx = {}
+    f32p = ctypes.POINTER(ctypes.c_float)
+    for name, mk, t in (("q4_0", _blocks_q4, 2), ("q8_0", _blocks_q8, 8)):
+        rows, cols = 24, 256
+        blocks = mk(rng, rows * cols // 32)
+        raw = np.ascontiguousarray(blocks.reshape(-1))
+        deq = np.empty(rows * cols, np.float32)
+        lib.ssr_dequantize(raw.ctypes.data, deq.ctypes.data_as(f32p), rows * cols, t)
+        x = rng.standard_normal(cols).astype(np.float32)
+        mv = np.empty(rows, np.float32)
+        lib.ssr_dequant_matvec(mv.ctypes.data_as(f32p), raw.ctypes.data,
+                               x.ctypes.data_as(f32p), rows, cols, t)
+        fx[f"{name}_raw"] = raw
+        fx[f"{name}_deq"] = deq
+        fx[f"{name}_x"] = x
+        fx[f"{name}_mv"] = mv
+    halfs = np.array([0x0000, 0x3C00, 0xBC00, 0x3800, 0x0001, 0x03FF, 0x0400, 0x7BFF,
+                      0xFBFF, 0x8001, 0x7C00, 0xFC00], np.uint16)
+    fx["f16_in"] = halfs
+    fx["f16_out"] = np.array([lib.ssr_f16_to_f32(int(h)) for h in halfs], np.float32)
+    n = 300
+    x = rng.standard_normal(n).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+    out = np.empty(n, np.float32)
+    lib.ssr_rmsnorm(out.ctypes.data_as(f32p), x.ctypes.data_as(f32p),
+                    w.ctypes.data_as(f32p), n, np.float32(1e-5))
+    fx.update(rms_x=x, rms_w=w, rms_out=out)
+    nh, nkv, hd = 4, 2, 16
+    q = rng.standard_normal(nh * hd).astype(np.float32)
+    k = rng.standard_normal(nkv * hd).astype(np.float32)
+    fx.update(rope_q_in=q.copy(), rope_k_in=k.copy())
+    for pos, theta in ((0, 10000.0), (7, 10000.0), (383, 10000.0), (1000, 500000.0)):
+        qq, kk = q.copy(), k.copy()
+        lib.ssr_rope(qq.ctypes.data_as(f32p), kk.ctypes.data_as(f32p), nh, nkv, hd, hd, pos,
+                     np.float32(theta))
+        fx[f"rope_q_{pos}"] = qq
+        fx[f"rope_k_{pos}"] = kk
+    s = (rng.standard_normal(77) * 3).astype(np.float32)
+    fx["softmax_in"] = s.copy()
+    lib.ssr_softmax(s.ctypes.data_as(f32p), len(s))
+    fx["softmax_out"] = s
+    ties = np.array([1.0, 5.0, 2.0, 5.0, 5.0, -1.0], np.float32)
+    fx["argmax_ties_in"] = ties
+    fx["argmax_ties_out"] = np.int32(lib.ssr_argmax(ties.ctypes.data_as(f32p), len(ties)))
+    np.savez_compressed(os.path.join(OUT, "ops.npz"), **fx)
+    print("ops: written")
+
+
+def main() -> int:
+    if not oracle.ref_available() and not oracle.build_ref():
+        print("reference build unavailable", file=sys.stderr)
+        return 2
+    names = sys.argv[1:] or ["ops", "tiny", "tiny-mha", "tiny-q8", "tinyllama"]
+    for n in names:
+        if n == "ops":
+            make_ops_fixture()
+        else:
+            make_model_fixture(n)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
