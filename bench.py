@@ -1,0 +1,370 @@
+#!/usr/bin/env python3
+"""Decode throughput of SlipStream's per-token loop on B200.
+
+One *step* = one greedy decode token of the workload (batch 1): embedding, all
+layers (RMSNorm, Q/K/V GEMV + RoPE, int8-KV attention, O GEMV, RMSNorm,
+gate/up GEMV + SwiGLU, down GEMV), final RMSNorm, lm_head, argmax -- one CUDA
+graph replay.  Default workload: the Llama-2-7B-shaped Q4_0 model, prompt of
+128 seeded tokens, greedy decode at batch 1, ctx 2048 (the configuration the
+headline metric is quoted on).  The weights (3.7 GB per step) are far larger
+than L2, so no L2 flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line on rank 0.  --impl reference times the reference's own CPU
+path (oracle/_ref, or the repository's C restatement when the reference build is
+absent) on the host cores instead.  With --gpus N (torchrun) every rank decodes
+an independent replica on its own GPU; time is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+
+NVML_REASONS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+    0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+    0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+    0x100: "display_clock_setting",
+}
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=240)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="llama2-7b")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# --------------------------------------------------------------------- helpers
+
+def hbm_peak() -> tuple[float, str]:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def read_profile_traffic(kernel: str, config: str):
+    """DRAM bytes per launch from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}_{config}.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML every ~10 ms."""
+
+    def __init__(self, device_index: int):
+        self.samples = []  # (t, sm_mhz, reasons_bits)
+        self.window = None
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._h = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = self._handle(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._h = None
+
+    def _handle(self, idx):
+        import torch
+        nv = self._nv
+        try:
+            uuid = str(torch.cuda.get_device_properties(idx).uuid)
+            return nv.nvmlDeviceGetHandleByUUID(("GPU-" + uuid).encode())
+        except Exception:
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            if vis:
+                idx = int(vis.split(",")[idx])
+            return nv.nvmlDeviceGetHandleByIndex(idx)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                try:
+                    r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                except AttributeError:
+                    r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+                self.samples.append((time.perf_counter(), mhz, r))
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._h is not None:
+            self._t.join(timeout=1)
+
+    def summary(self):
+        if self._h is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        t0, t1 = self.window or (0, float("inf"))
+        inside = [s for s in self.samples if t0 <= s[0] <= t1] or self.samples[-5:]
+        bits = 0
+        for s in inside:
+            bits |= s[2]
+        reasons = [n for b, n in NVML_REASONS.items() if bits & b and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(s[1] for s in inside) if inside else None,
+                "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(inside)}
+
+
+def cpu_reference_run(cfg, path, n_max, budget_s=20.0):
+    """Times the reference CPU path (oracle/_ref) -- or the C restatement when
+    the reference build is absent -- on the host cores: one warm-up token at
+    position 0, then up to n_max tokens (bounded to ~budget_s) at positions 1..
+    Returns (tokens/s, cores, kind, sample description)."""
+    import numpy as np
+
+    import oracle
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    if oracle.ref_available(cfg.ctx > 512):
+        model, kind = oracle.RefModel(path, cfg.ctx), "reference"
+    else:
+        model, kind = oracle.OracleModel(path, cfg.ctx), "port"
+    tok = synth_prompt(cfg)[0]
+    t = time.perf_counter()
+    logits = model.forward(tok, 0)
+    t_warm = time.perf_counter() - t
+    n = int(max(2, min(n_max, budget_s / max(t_warm, 1e-3))))
+    t = time.perf_counter()
+    for i in range(n):
+        tok = int(np.argmax(logits))
+        logits = model.forward(tok, 1 + i)
+    dt = time.perf_counter() - t
+    model.close()
+    sample = (f"{n} greedy decode tokens at positions 1..{n} (after 1 warm-up token at "
+              f"position 0, no prompt prefill) of the same GGUF, {cores} OpenMP threads, "
+              f"{'reference C code built from the PhoneMap sources' if kind == 'reference' else 'C restatement of the reference'}")
+    return n / dt, cores, kind, sample
+
+
+def synth_prompt(cfg):
+    from phonemap_b200 import synth
+    return synth.prompt_tokens(cfg)
+
+
+# ---------------------------------------------------------------- main paths
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+    return world, rank, local, pg
+
+
+def workload(cfg, args):
+    return {
+        "workload": (f"{cfg.name}-shaped llama decoder, {'Q4_0' if cfg.wtype == 2 else 'Q8_0'} "
+                     f"weights, greedy decode at batch 1 after a {cfg.prompt}-token prompt"),
+        "weights": "Q4_0" if cfg.wtype == 2 else "Q8_0",
+        "prompt_tokens": cfg.prompt,
+        "decode_positions": [cfg.prompt + args.warmup, cfg.prompt + args.warmup + args.steps - 1],
+        "batch": 1,
+        "ctx": cfg.ctx,
+        "l2": "inputs larger than L2 (weights streamed per step exceed the 126 MB L2)",
+        "parallelism": "replicas" if args.gpus > 1 else "single GPU",
+    }
+
+
+def run_reference(args):
+    world, rank, _, pg = dist_setup(args)
+    if rank != 0:
+        return 0
+    from phonemap_b200 import configs, synth
+    cfg = configs.get(args.config)
+    path = synth.ensure_gguf(cfg)
+    n_max = max(1, args.steps)
+    value, cores, kind, sample = cpu_reference_run(cfg, path, n_max, budget_s=90.0)
+    line = {
+        "metric": "decode tokens/s (batch 1)", "value": round(value, 4), "unit": "tokens/s",
+        "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000.0 / value, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init GGUF)",
+        "config": workload(cfg, args),
+        "cpu_baseline": {"value": round(value, 4), "unit": "tokens/s", "cores": cores,
+                         "kind": kind, "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    world, rank, local, pg = dist_setup(args)
+    import numpy as np
+    import torch
+
+    from phonemap_b200 import configs, runtime, synth
+    cfg = configs.get(args.config)
+    if rank == 0:
+        path = synth.ensure_gguf(cfg)
+    if pg:
+        pg.barrier()
+    path = synth.ensure_gguf(cfg)
+    torch.cuda.set_device(local)
+    m = runtime.CudaModel(path, cfg.ctx, device=local)
+    prompt = synth.prompt_tokens(cfg)
+    P, W, K = len(prompt), args.warmup, args.steps
+    if P + W + K + 1 > cfg.ctx:
+        raise SystemExit("prompt + warmup + steps exceed the context")
+    stream = torch.cuda.ExternalStream(m.stream(), device=torch.device("cuda", local))
+
+    # ---- device-resident decode loop (inputs already in HBM)
+    first = m.prefill(prompt, 0)
+    m.decode_begin(first, P)
+    m.decode_steps(W)
+    m.decode_read(P + 1, 1)
+    sampler = ClockSampler(local)
+    with sampler:
+        time.sleep(0.05)
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        t_w0 = time.perf_counter()
+        ev0.record(stream)
+        m.decode_steps(K)
+        ev1.record(stream)
+        ev1.synchronize()
+        t_w1 = time.perf_counter()
+        torch.cuda.synchronize()
+        sampler.window = (t_w0, t_w1)
+        time.sleep(0.02)
+    ms = ev0.elapsed_time(ev1)
+    ids = m.decode_read(P + 1, W + K)
+    if pg:
+        t = torch.tensor([ms], device="cuda")
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+        pg.barrier()
+    ms_per_step = ms / K
+    value = world * K / (ms / 1000.0)
+    stats = m.stats()
+
+    # ---- end to end through the public C ABI with host buffers: per step the
+    # token and position go host->device, the logits and argmax device->host
+    e2e = None
+    if not args.no_e2e:
+        m.reset()
+        logits = np.empty(m.vocab, np.float32)
+        tok = m.prefill(prompt, 0)
+        pos = P
+        for _ in range(W):
+            tok = m.forward(tok, pos, logits=logits)
+            pos += 1
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(K):
+            tok = m.forward(tok, pos, logits=logits)
+            pos += 1
+        dt = time.perf_counter() - t0
+        if pg:
+            t = torch.tensor([dt], device="cuda")
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            dt = float(t.item())
+        e2e = {"value": round(world * K / dt, 2), "unit": "tokens/s",
+               "h2d_bytes_per_step": 4 + 8, "d2h_bytes_per_step": 4 * m.vocab + 4 + 4,
+               "api": "ss_cuda_forward (host token in, host logits + argmax out, synchronous)"}
+
+    # ---- roofline of the dominant kernel (gate/up GEMV: 2*ff*d Q4_0 weights),
+    # timed live: isolated back-to-back launches cycling through the layers
+    peak, peak_kind = hbm_peak()
+    bpw = 18 / 32 if cfg.wtype == 2 else 34 / 32
+    gu_bytes = 2 * cfg.ffn * cfg.d_model * bpw + cfg.d_model * 4 * 2 + cfg.ffn * 4
+    gu_ms = m.time_kernel("gate_up", 3 * cfg.n_layers)
+    achieved = gu_bytes / (gu_ms / 1000.0) / 1e9
+    step_bytes = cfg.token_bytes(P + W + (K - 1) / 2.0)
+    step_gbs = step_bytes / (ms_per_step / 1000.0) / 1e9
+    m.close()
+
+    line = None
+    if rank == 0:
+        line = {
+            "metric": "decode tokens/s (batch 1)", "value": round(value, 2), "unit": "tokens/s",
+            "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random-init GGUF, N(0,0.02) quantized)",
+            "config": workload(cfg, args),
+            "roofline": {"bound": "hbm", "kernel": "gate/up GEMV + RMSNorm + SwiGLU",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                         "bytes_per_launch": int(gu_bytes), "ms_per_launch": round(gu_ms, 5),
+                         "traffic": read_profile_traffic("gemv_gate_up", cfg.name)},
+            "step_roofline": {"bytes_per_step": int(step_bytes), "achieved": round(step_gbs, 1),
+                              "frac": round(step_gbs / peak, 4), "unit": "GB/s",
+                              "peak_source": peak_kind},
+            "e2e": e2e,
+            "gpu_launches": int(stats["kernels_per_step"] * K),
+            "clocks": sampler.summary(),
+            "pdl": bool(stats["pdl"]),
+            "first_ids": ids[:8],
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            v, cores, kind, sample = cpu_reference_run(cfg, path, K)
+            line["cpu_baseline"] = {"value": round(v, 4), "unit": "tokens/s", "cores": cores,
+                                    "kind": kind, "sample": sample}
+        print(json.dumps(line), flush=True)
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,175 @@
+/*
+ * slipstream_cuda.h -- CUDA (sm_100a) backend for SlipStream's decode path.
+ *
+ * A sibling of SlipStream's Metal backend (SlipStream/src/backends/
+ * metal_backend.h:21-75), reached from the same call sites:
+ *   - ss_model_load creates it next to ss_metal_init (SlipStream/src/core/
+ *     engine.c:87-96) and ss_model_free frees it (engine.c:467-469);
+ *   - ss_matmul_dispatch calls the op-level matvecs (SlipStream/src/core/
+ *     layer_scheduler.c:248-279), with the begin/end batch brackets of
+ *     layer_scheduler.c:352-362 and :508-517;
+ *   - ss_scheduler_forward / _prefill / _reset (layer_scheduler.h:107-132)
+ *     hand whole tokens to ss_cuda_scheduler_* so activations stay on the GPU.
+ *
+ * Plain C types only.  Every entry point is synchronous unless it says
+ * otherwise.  On failure the bool/pointer entry points return false/NULL and
+ * the int ones a negative SS_CUDA_ERROR_* code (the values of ss_error_t,
+ * SlipStream/include/slipstream.h:32-43); ss_cuda_last_error() describes the
+ * most recent failure on the calling thread.  There is no CPU fallback: a
+ * failure is reported, never silently computed elsewhere.
+ *
+ * Threading: one caller thread per context (as the reference's scheduler).
+ * ss_cuda_cancel may be called from any thread.
+ */
+#ifndef SLIPSTREAM_CUDA_H
+#define SLIPSTREAM_CUDA_H
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SS_CUDA_ABI_VERSION 1
+
+/* Error codes: same values as ss_error_t (SlipStream/include/slipstream.h:32-43). */
+#define SS_CUDA_OK 0
+#define SS_CUDA_ERROR_FILE_NOT_FOUND (-1)
+#define SS_CUDA_ERROR_INVALID_MODEL (-2)
+#define SS_CUDA_ERROR_OUT_OF_MEMORY (-3)
+#define SS_CUDA_ERROR_INVALID_PARAMS (-5)
+#define SS_CUDA_ERROR_CANCELLED (-6)
+#define SS_CUDA_ERROR_BACKEND (-7)
+
+/* Backend id to add to ss_backend_t (slipstream.h:47-51). */
+#define SS_BACKEND_CUDA 3
+
+typedef struct ss_cuda_ctx ss_cuda_ctx_t;
+
+typedef struct {
+    uint32_t struct_size;      /* sizeof(ss_cuda_options_t) */
+    int32_t device;            /* CUDA ordinal; -1 = $SS_CUDA_DEVICE or 0 */
+    uint32_t context_size;     /* positions (0 = GGUF context_length), capped at 8192 as engine.c:103-106 */
+    uint32_t max_batch;        /* sequences decoded together (>= 1) */
+    uint64_t hbm_budget_bytes; /* 0 = every layer resident in HBM */
+    uint32_t flags;            /* SS_CUDA_FLAG_* */
+} ss_cuda_options_t;
+
+#define SS_CUDA_FLAG_NO_PDL 1u   /* launch without programmatic dependent launch */
+#define SS_CUDA_FLAG_NO_GRAPH 2u /* launch kernels one by one instead of a CUDA graph */
+
+/* Fills defaults: device -1, context 0, batch 1, no budget, no flags. */
+void ss_cuda_default_options(ss_cuda_options_t *opts);
+
+/* ---- lifecycle (twin of ss_metal_init / ss_metal_free, metal_backend.h:21,75) ----
+ * Uploads and repacks every weight tensor of the llama GGUF held in
+ * [gguf_base, gguf_base + gguf_size) (the loader's mmap: ss_gguf_file_t
+ * mmap_base / file_size, SlipStream/src/core/gguf_loader.h:84-85) and
+ * allocates the int8 KV cache.  The mapping may be unmapped afterwards.
+ * Returns NULL on failure. */
+ss_cuda_ctx_t *ss_cuda_init(const void *gguf_base, uint64_t gguf_size,
+                            const ss_cuda_options_t *opts);
+/* Same, mapping the file itself. */
+ss_cuda_ctx_t *ss_cuda_init_file(const char *gguf_path, const ss_cuda_options_t *opts);
+void ss_cuda_free(ss_cuda_ctx_t *ctx);
+
+const char *ss_cuda_last_error(void);
+int ss_cuda_abi_version(void);
+
+/* dims[0..11] = vocab, hidden, layers, heads, kv_heads, head_dim, ffn,
+ * context (positions), rope_dim, weight type, max_batch, device. */
+int ss_cuda_model_dims(const ss_cuda_ctx_t *ctx, int32_t *dims);
+
+/* Counters (no reference counterpart; profiling aid like the recap at
+ * engine.c:291-302): out[0] kernels launched per decode step, [1] device weight
+ * bytes, [2] device KV-cache bytes, [3] attention position splits, [4] 1 when
+ * the step graph chains kernels with programmatic dependent launch, [5] decode
+ * steps run, [6] CTAs of the QKV GEMV, [7] CTAs of the down GEMV. */
+int ss_cuda_stats(const ss_cuda_ctx_t *ctx, int64_t *out, int32_t n);
+
+/* Measurement aid, no reference counterpart: times `iters` back-to-back
+ * launches (no programmatic overlap) of one kernel of the decode step --
+ * which = 0 QKV GEMV, 1 attention, 2 O GEMV, 3 gate/up GEMV, 4 down GEMV,
+ * 5 lm_head GEMV -- cycling through the layers so weights stream from HBM, and
+ * writes the average milliseconds per launch.  Clobbers the activations and the
+ * current position's K/V; call ss_cuda_reset before decoding again. */
+int ss_cuda_time_kernel(ss_cuda_ctx_t *ctx, int32_t which, int32_t iters, float *ms_per_launch);
+/* Device bytes of the weights one launch of kernel `which` streams (layer 0;
+ * repacked layout, i.e. the GGUF bytes plus row padding); -1 if not a GEMV. */
+int64_t ss_cuda_kernel_bytes(const ss_cuda_ctx_t *ctx, int32_t which);
+
+/* ---- op level: twins of ss_metal_should_use_gpu / ss_metal_matvec* ----
+ * (metal_backend.h:27-58).  out[rows] = W[rows x cols] . vec[cols] with host
+ * pointers.  W is a GGUF tensor's bytes (Q4_0: 18 B per 32 weights, Q8_0: 34 B,
+ * F32: 4 B per weight); its device copy is cached by host address, as the
+ * Metal backend caches its zero-copy buffers (metal_backend.m:190-235).
+ * Returns true when `out` has been written (at ss_cuda_end_batch when called
+ * inside a batch). */
+bool ss_cuda_should_use_gpu(int32_t rows, int32_t cols);
+bool ss_cuda_matvec(ss_cuda_ctx_t *ctx, float *out, const float *mat, const float *vec,
+                    int32_t rows, int32_t cols);
+bool ss_cuda_matvec_q4_0(ss_cuda_ctx_t *ctx, float *out, const void *mat, const float *vec,
+                         int32_t rows, int32_t cols);
+bool ss_cuda_matvec_q8_0(ss_cuda_ctx_t *ctx, float *out, const void *mat, const float *vec,
+                         int32_t rows, int32_t cols);
+/* Twins of ss_metal_begin_batch / ss_metal_end_batch (metal_backend.h:64-70). */
+void ss_cuda_begin_batch(ss_cuda_ctx_t *ctx);
+void ss_cuda_end_batch(ss_cuda_ctx_t *ctx);
+
+/* ---- scheduler level: twins of ss_scheduler_forward / _prefill / _reset ----
+ * (layer_scheduler.h:107-132).  The returned fp32 logits[vocab] live in a host
+ * buffer owned by the context and stay valid until the next call; NULL on
+ * error or cancellation.  Positions must satisfy 0 <= pos < context. */
+float *ss_cuda_scheduler_forward(ss_cuda_ctx_t *ctx, int32_t token_id, int32_t pos);
+float *ss_cuda_scheduler_prefill(ss_cuda_ctx_t *ctx, const int32_t *tokens, int32_t n,
+                                 int32_t start_pos);
+void ss_cuda_scheduler_reset(ss_cuda_ctx_t *ctx);
+
+/* ---- coarse entry points (activations and tokens stay on the device) ----
+ * One decode step for the sequence at `pos`: token_ids[0] in, optional logits
+ * out (host, vocab floats) and greedy argmax out (host, lowest index wins ties
+ * as ss_argmax, SlipStream/src/core/tensor.c:318-328). */
+int ss_cuda_forward(ss_cuda_ctx_t *ctx, const int32_t *token_ids, int32_t n_seq, int32_t pos,
+                    float *logits_out, int32_t *argmax_out);
+/* Prompt ingestion at positions start_pos..start_pos+n-1; logits of the last
+ * token to logits_out (nullable); returns the greedy next token (>= 0). */
+int ss_cuda_prefill(ss_cuda_ctx_t *ctx, const int32_t *tokens, int32_t n, int32_t start_pos,
+                    float *logits_out);
+/* Greedy decode of n_steps tokens, each fed back on the device without a host
+ * round trip: the token at start_pos is `token`, ids_out[i] receives the token
+ * generated at position start_pos + 1 + i. */
+int ss_cuda_decode_greedy(ss_cuda_ctx_t *ctx, int32_t token, int32_t start_pos, int32_t n_steps,
+                          int32_t *ids_out);
+/* Asynchronous pieces of ss_cuda_decode_greedy, for timing with events on
+ * ss_cuda_stream(): begin (host->device of the token and position), steps
+ * (enqueue n replays of the step graph, no synchronisation), read (wait, then
+ * copy the tokens of positions [first_pos, first_pos + n) to the host). */
+int ss_cuda_decode_begin(ss_cuda_ctx_t *ctx, int32_t token, int32_t pos);
+int ss_cuda_decode_steps(ss_cuda_ctx_t *ctx, int32_t n_steps);
+int ss_cuda_decode_read(ss_cuda_ctx_t *ctx, int32_t first_pos, int32_t n, int32_t *ids_out);
+/* The cudaStream_t all work of this context runs on. */
+void *ss_cuda_stream(ss_cuda_ctx_t *ctx);
+/* Clears the KV cache (ss_scheduler_reset, layer_scheduler.c:917-936). */
+void ss_cuda_reset(ss_cuda_ctx_t *ctx);
+/* Thread-safe; the next scheduler/forward call returns SS_CUDA_ERROR_CANCELLED
+ * (ss_cancel, engine.c:372-379). */
+void ss_cuda_cancel(ss_cuda_ctx_t *ctx);
+
+/* ---- inspection (parity tests) ----
+ * fp32 dequantisation of an uploaded weight tensor by GGUF name, rows in GGUF
+ * order (n = rows * cols floats), computed on the device from the repacked
+ * layout -- bit-identical to ss_dequantize (SlipStream/src/core/quantize.c:
+ * 389-442) for Q4_0 / Q8_0. */
+int ss_cuda_dequantize_tensor(ss_cuda_ctx_t *ctx, const char *name, float *out, int64_t n);
+/* Device dequantisation of raw GGUF blocks (host in, host out); no context. */
+int ss_cuda_dequantize(int32_t type, const void *blocks, int64_t n, float *out);
+/* int8 K/V row and scales of (layer, pos) (layer_scheduler.h:19-34 layout). */
+int ss_cuda_kv_row(ss_cuda_ctx_t *ctx, int32_t layer, int32_t pos, int8_t *k, int8_t *v,
+                   float *k_scale, float *v_scale);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SLIPSTREAM_CUDA_H */

@@ -1,0 +1,401 @@
+// gemv.cuh -- batch-1 dequantize-and-matvec for Q4_0 / Q8_0 weights on sm_100a.
+//
+// Replaces SlipStream's per-row "dequantize into a temp, then dot" CPU loop
+// (SlipStream/src/core/quantize.c:446-494) and the one-thread-per-row Metal
+// kernel (SlipStream/src/backends/metal_backend.m:55-91).  Same math -- every
+// weight is d * (q - 8) (Q4_0) or d * q (Q8_0) with d the block's fp16 scale
+// widened exactly to fp32, products and sums in fp32 -- in a different
+// summation order.
+//
+// Layout ("row-interleaved"): the uploader repacks each GGUF matrix so that row
+// r occupies `row_stride` bytes at `data + r * row_stride`:
+//     [nb blocks of quants, 16 B (Q4_0) or 32 B (Q8_0) each]
+//     [nb fp16 scales][zero pad to 16 B]
+// The quant bytes of a block are the GGUF block's bytes unchanged (Q4_0 byte j
+// holds q[j] in its low nibble and q[j+16] in its high nibble), so every weight
+// decodes to the same value as the reference's dequantizer.  Bytes per weight
+// are the GGUF ones (18/32, 34/32) plus < 16 B of padding per row.
+//
+// Work split ("x-stationary"): a CTA has one thread per 32-column block
+// (blockDim = nb rounded up to a warp).  Each thread keeps its block's 32
+// activations in registers for every row the CTA owns, streams that block of
+// each row with one 128-bit load (two for Q8_0), and the CTA reduces each row
+// once at the end.  A CTA owns a contiguous range of rows, so one bulk L2
+// prefetch covers its whole share of the matrix; it is issued before the
+// programmatic-dependent-launch wait so the weight stream overlaps the tail of
+// the previous kernel.
+//
+// Dequantisation without int->float conversion: a nibble/byte masked into the
+// mantissa of 2^23 (bit pattern 0x4B000000 | q << s) is the float 2^23 + q*2^s;
+// subtracting the constant 2^23 + zero_point*2^s leaves 2^s * (q - zp) exactly.
+// The 2^s factor is cancelled by pre-scaling the matching activation by 2^-s
+// (exact), so each product equals (q - zp) * x bit for bit.
+#pragma once
+#include "common.cuh"
+
+namespace ss {
+
+struct QMatrix {
+  const uint8_t* data;
+  int rows, cols;
+  int row_stride;  // bytes per row
+  int scale_off;   // byte offset of the fp16 scales within a row
+  int type;        // kQ4_0 or kQ8_0
+};
+
+enum class XSrc : int { Plain = 0, RmsNorm = 1 };
+enum class Epi : int { Store = 0, Residual = 1, QKV = 2, SwiGLU = 3, Argmax = 4 };
+
+struct GemvParams {
+  QMatrix w;
+  const float* x;        // Plain: the input vector; RmsNorm: the residual stream h
+  const float* norm_w;   // RmsNorm weight (fp32, cols)
+  float eps;
+  float* out;            // Store/Residual/QKV: [rows]; SwiGLU: [rows/2]; Argmax: logits (nullable)
+  const float* residual; // Residual: out[r] = acc + residual[r]
+  // QKV epilogue: RoPE on the q and k rows, |k| and |v| maxima for the int8 cache
+  int q_rows, kv_rows, head_dim, rope_dim;
+  const float2* rope_tab;    // [ctx][rope_dim/2] (cos, sin)
+  const int* d_pos;
+  unsigned int* amax_k;      // slot for (layer, pos) = amax_k[pos] (already offset by layer)
+  unsigned int* amax_v;
+  // Argmax epilogue
+  unsigned long long* am_part;  // one packed (value, index) per CTA
+  unsigned int* am_count;
+  int* seq_tokens;              // token of every position
+  const int* fixed_until;       // positions below this hold prompt tokens
+  int* d_pos_rw;                // advanced by one after the step
+  int ctx;
+  int* err;
+  int rows_per_cta;
+  int prefetch;
+};
+
+// ---- per-block dot products --------------------------------------------
+// Order in which a Q4_0 thread consumes the 8 nibbles of word t of its block,
+// as (index of the weight inside the block, bit offset s of the mantissa slot).
+//   k:     0      1        2       3         4       5        6        7
+//   j:    4t   16+4t     4t+1   17+4t      4t+2   18+4t     4t+3    19+4t
+//   s:     0      4        8      12        16       8       12       16
+// (k = 5..7 come from the word shifted right by 12.)
+SS_DEVINL int q4_weight_index(int t, int k) { return (k & 1 ? 16 : 0) + 4 * t + (k >> 1); }
+SS_DEVINL int q4_slot_shift(int k) {
+  return k == 0 ? 0 : k == 1 ? 4 : k == 2 ? 8 : k == 3 ? 12 : k == 4 ? 16 : k == 5 ? 8 : k == 6 ? 12 : 16;
+}
+// Q8_0 word t holds weights 4t..4t+3; bytes 2,3 come from the word >> 16.
+SS_DEVINL int q8_slot_shift(int i) { return (i & 1) ? 8 : 0; }
+
+constexpr unsigned kMagic = 0x4B000000u;  // 2^23
+SS_DEVINL float pow2_neg(int s) {  // 2^-s, exact
+  return s == 0 ? 1.0f : s == 4 ? 0.0625f : s == 8 ? 0.00390625f : s == 12 ? 0.000244140625f
+                                                                    : 0.0000152587890625f;
+}
+
+// Q4_0: sum_j (q_j - 8) * x_j over one block, 2 accumulation chains.
+SS_DEVINL float dot_q4_block(const uint4 q, const float* __restrict__ xr) {
+  float a0 = 0.0f, a1 = 0.0f;
+  const unsigned w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int t = 0; t < 4; t++) {
+    const unsigned w = w4[t];
+    const unsigned u = w >> 12;
+    const float* x = xr + 8 * t;
+    a0 = fmaf(__uint_as_float((w & 0x0000000Fu) | kMagic) - 8388616.0f, x[0], a0);
+    a1 = fmaf(__uint_as_float((w & 0x000000F0u) | kMagic) - 8388736.0f, x[1], a1);
+    a0 = fmaf(__uint_as_float((w & 0x00000F00u) | kMagic) - 8390656.0f, x[2], a0);
+    a1 = fmaf(__uint_as_float((w & 0x0000F000u) | kMagic) - 8421376.0f, x[3], a1);
+    a0 = fmaf(__uint_as_float((w & 0x000F0000u) | kMagic) - 8912896.0f, x[4], a0);
+    a1 = fmaf(__uint_as_float((u & 0x00000F00u) | kMagic) - 8390656.0f, x[5], a1);
+    a0 = fmaf(__uint_as_float((u & 0x0000F000u) | kMagic) - 8421376.0f, x[6], a0);
+    a1 = fmaf(__uint_as_float((u & 0x000F0000u) | kMagic) - 8912896.0f, x[7], a1);
+  }
+  return a0 + a1;
+}
+
+// Q8_0: sum_j q_j * x_j; bytes are biased by 128 (xor 0x80) to be unsigned.
+SS_DEVINL float dot_q8_block(const uint4 qa, const uint4 qb, const float* __restrict__ xr) {
+  float a0 = 0.0f, a1 = 0.0f;
+  const unsigned w8[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+  for (int t = 0; t < 8; t++) {
+    const unsigned v = w8[t] ^ 0x80808080u;
+    const unsigned u = v >> 16;
+    const float* x = xr + 4 * t;
+    a0 = fmaf(__uint_as_float((v & 0x00FFu) | kMagic) - 8388736.0f, x[0], a0);
+    a1 = fmaf(__uint_as_float((v & 0xFF00u) | kMagic) - 8421376.0f, x[1], a1);
+    a0 = fmaf(__uint_as_float((u & 0x00FFu) | kMagic) - 8388736.0f, x[2], a0);
+    a1 = fmaf(__uint_as_float((u & 0xFF00u) | kMagic) - 8421376.0f, x[3], a1);
+  }
+  return a0 + a1;
+}
+
+// ---- warp "transpose" reductions -----------------------------------------
+// Reduce G per-lane values over the 32 lanes in G + 5 - log2(G)... shuffles:
+// after the call, lanes with (lane & (32/G - 1)) == 0 hold the sum of value
+// index row_of_lane(lane).
+template <int G>
+SS_DEVINL float warp_reduce_rows(float (&a)[G], int lane);
+
+template <>
+SS_DEVINL float warp_reduce_rows<1>(float (&a)[1], int lane) {
+  return warp_sum(a[0]);
+}
+template <>
+SS_DEVINL float warp_reduce_rows<2>(float (&a)[2], int lane) {
+  const bool hi = lane & 16;
+  float v = (hi ? a[1] : a[0]) + __shfl_xor_sync(0xffffffffu, hi ? a[0] : a[1], 16);
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+template <>
+SS_DEVINL float warp_reduce_rows<4>(float (&a)[4], int lane) {
+  const bool b4 = lane & 16, b3 = lane & 8;
+  float b0 = (b4 ? a[2] : a[0]) + __shfl_xor_sync(0xffffffffu, b4 ? a[0] : a[2], 16);
+  float b1 = (b4 ? a[3] : a[1]) + __shfl_xor_sync(0xffffffffu, b4 ? a[1] : a[3], 16);
+  float v = (b3 ? b1 : b0) + __shfl_xor_sync(0xffffffffu, b3 ? b0 : b1, 8);
+#pragma unroll
+  for (int o = 4; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+template <>
+SS_DEVINL float warp_reduce_rows<8>(float (&a)[8], int lane) {
+  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+  float b[4], c[2];
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+    b[i] = (b4 ? a[i + 4] : a[i]) + __shfl_xor_sync(0xffffffffu, b4 ? a[i] : a[i + 4], 16);
+#pragma unroll
+  for (int i = 0; i < 2; i++)
+    c[i] = (b3 ? b[i + 2] : b[i]) + __shfl_xor_sync(0xffffffffu, b3 ? b[i] : b[i + 2], 8);
+  float v = (b2 ? c[1] : c[0]) + __shfl_xor_sync(0xffffffffu, b2 ? c[0] : c[1], 4);
+  v += __shfl_xor_sync(0xffffffffu, v, 2);
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  return v;
+}
+template <int G>
+SS_DEVINL int row_of_lane(int lane) {
+  if (G == 1) return 0;
+  if (G == 2) return (lane >> 4) & 1;
+  if (G == 4) return ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
+  return ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+}
+
+// Packs (value, index) so that unsigned max picks the larger value and, among
+// equal values, the lower index (ss_argmax, SlipStream/src/core/tensor.c:318-328).
+SS_DEVINL unsigned long long pack_argmax(float v, int idx) {
+  unsigned b = __float_as_uint(v);
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  if (v != v) b = 0;  // NaN never wins
+  return ((unsigned long long)b << 32) | (unsigned)(0x7fffffff - idx);
+}
+SS_DEVINL int unpack_argmax_index(unsigned long long p) {
+  return 0x7fffffff - (int)(unsigned)(p & 0xffffffffu);
+}
+
+// ---- the kernel ------------------------------------------------------------
+template <int TYPE, XSrc XS, Epi EPI, int G>
+__global__ void __launch_bounds__(1024) gemv_kernel(const GemvParams p) {
+  extern __shared__ float smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nw = blockDim.x >> 5;
+  const int nb = p.w.cols >> 5;
+  const int r0 = blockIdx.x * p.rows_per_cta;
+  const int r1 = min(r0 + p.rows_per_cta, p.w.rows);
+  const int nrows = r1 - r0;
+  float* red = smem;                               // [nw][rows_per_cta]
+  float* scratch = smem + nw * p.rows_per_cta;     // 64 floats
+
+  if (p.prefetch && tid == 0 && nrows > 0)
+    prefetch_l2_bulk(p.w.data + (size_t)r0 * p.w.row_stride, (uint32_t)(nrows * p.w.row_stride));
+  pdl_wait();
+
+  // ---- prologue: this thread's 32 activations, pre-scaled per mantissa slot
+  const int blk = tid;
+  const bool active = blk < nb;
+  float xr[32];
+  {
+    float scale = 1.0f;
+    if constexpr (XS == XSrc::RmsNorm) {
+      // SlipStream/src/backends/cpu_neon.c:109-115: ss = sum x^2,
+      // scale = 1 / sqrtf(ss / n + eps), out = x * scale * w.
+      float ss = 0.0f;
+      for (int i = tid * 4; i < p.w.cols; i += blockDim.x * 4) {
+        const float4 v = *reinterpret_cast<const float4*>(p.x + i);
+        ss = fmaf(v.x, v.x, ss); ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss); ss = fmaf(v.w, v.w, ss);
+      }
+      ss = block_sum(ss, scratch);
+      scale = 1.0f / sqrtf(ss / (float)p.w.cols + p.eps);
+    }
+    if (active) {
+      float xv[32];
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(p.x + blk * 32 + i);
+        xv[i] = v.x; xv[i + 1] = v.y; xv[i + 2] = v.z; xv[i + 3] = v.w;
+      }
+      if constexpr (XS == XSrc::RmsNorm) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 wv = *reinterpret_cast<const float4*>(p.norm_w + blk * 32 + i);
+          xv[i] = __fmul_rn(__fmul_rn(xv[i], scale), wv.x);
+          xv[i + 1] = __fmul_rn(__fmul_rn(xv[i + 1], scale), wv.y);
+          xv[i + 2] = __fmul_rn(__fmul_rn(xv[i + 2], scale), wv.z);
+          xv[i + 3] = __fmul_rn(__fmul_rn(xv[i + 3], scale), wv.w);
+        }
+      }
+      if constexpr (TYPE == kQ4_0) {
+#pragma unroll
+        for (int t = 0; t < 4; t++)
+#pragma unroll
+          for (int k = 0; k < 8; k++)
+            xr[8 * t + k] = __fmul_rn(xv[q4_weight_index(t, k)], pow2_neg(q4_slot_shift(k)));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; j++) xr[j] = __fmul_rn(xv[j], pow2_neg(q8_slot_shift(j & 3)));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j++) xr[j] = 0.0f;
+    }
+  }
+  pdl_trigger();
+
+  // ---- main loop: G rows at a time
+  const uint8_t* base = p.w.data + (size_t)r0 * p.w.row_stride;
+  for (int lr = 0; lr < nrows; lr += G) {
+    float acc[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+      acc[g] = 0.0f;
+      if (active && lr + g < nrows) {
+        const uint8_t* rowp = base + (size_t)(lr + g) * p.w.row_stride;
+        const float d = half_bits_to_float(ldg_u16(rowp + p.w.scale_off + blk * 2));
+        float s;
+        if constexpr (TYPE == kQ4_0) {
+          s = dot_q4_block(ldg_stream(rowp + blk * 16), xr);
+        } else {
+          s = dot_q8_block(ldg_stream(rowp + blk * 32), ldg_stream(rowp + blk * 32 + 16), xr);
+        }
+        acc[g] = d * s;
+      }
+    }
+    const float v = warp_reduce_rows<G>(acc, lane);
+    const int rr = lr + row_of_lane<G>(lane);
+    if ((lane & (32 / G - 1)) == 0 && rr < nrows) red[warp * p.rows_per_cta + rr] = v;
+  }
+  __syncthreads();
+
+  // ---- epilogue
+  auto row_sum = [&](int lr_) {
+    float s = 0.0f;
+    for (int w = 0; w < nw; w++) s += red[w * p.rows_per_cta + lr_];
+    return s;
+  };
+
+  if constexpr (EPI == Epi::Store || EPI == Epi::Residual) {
+    for (int lr = tid; lr < nrows; lr += blockDim.x) {
+      const int r = r0 + lr;
+      float v = row_sum(lr);
+      if constexpr (EPI == Epi::Residual) v = __fadd_rn(v, p.residual[r]);
+      p.out[r] = v;
+    }
+  } else if constexpr (EPI == Epi::SwiGLU) {
+    // rows 2i (gate) and 2i+1 (up); SlipStream/src/core/layer_scheduler.c:533-549:
+    // up *= g / (1 + expf(-g)).
+    for (int lp = tid; lp * 2 < nrows; lp += blockDim.x) {
+      const float g = row_sum(2 * lp), u = row_sum(2 * lp + 1);
+      p.out[(r0 >> 1) + lp] = __fmul_rn(u, __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+    }
+  } else if constexpr (EPI == Epi::QKV) {
+    // RoPE (non-NeoX, SlipStream/src/core/tensor.c:249-274) on q and k rows,
+    // then the |k| / |v| maxima feeding the int8 cache scale
+    // (layer_scheduler.c:101-111).
+    const int pos = *p.d_pos;
+    if (pos < 0 || pos >= p.ctx) return;  // host bounds positions; never index past the table
+    float mk = 0.0f, mv = 0.0f;
+    for (int lp = tid; lp * 2 < nrows; lp += blockDim.x) {
+      const int r = r0 + 2 * lp;
+      float a = row_sum(2 * lp), b = row_sum(2 * lp + 1);
+      if (r < p.q_rows + p.kv_rows) {
+        const int i = r % p.head_dim;
+        if (i < p.rope_dim) {
+          const float2 cs = p.rope_tab[(size_t)pos * (p.rope_dim >> 1) + (i >> 1)];
+          const float na = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
+          const float nb2 = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
+          a = na; b = nb2;
+        }
+        if (r >= p.q_rows) mk = fmaxf(mk, fmaxf(fabsf(a), fabsf(b)));
+      } else {
+        mv = fmaxf(mv, fmaxf(fabsf(a), fabsf(b)));
+      }
+      p.out[r] = a;
+      p.out[r + 1] = b;
+    }
+    mk = warp_max(mk);
+    mv = warp_max(mv);
+    __syncthreads();
+    if (lane == 0) { scratch[warp] = mk; scratch[32 + warp] = mv; }
+    __syncthreads();
+    if (tid == 0) {
+      float a = 0.0f, b = 0.0f;
+      for (int w = 0; w < nw; w++) { a = fmaxf(a, scratch[w]); b = fmaxf(b, scratch[32 + w]); }
+      if (a > 0.0f) atomicMax(p.amax_k + pos, float_as_ordered(a));
+      if (b > 0.0f) atomicMax(p.amax_v + pos, float_as_ordered(b));
+    }
+  } else if constexpr (EPI == Epi::Argmax) {
+    unsigned long long best = 0;
+    for (int lr = tid; lr < nrows; lr += blockDim.x) {
+      const int r = r0 + lr;
+      const float v = row_sum(lr);
+      if (p.out) p.out[r] = v;
+      const unsigned long long pk = pack_argmax(v, r);
+      best = pk > best ? pk : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
+    }
+    __shared__ unsigned long long wbest[32];
+    __shared__ bool is_last;
+    if (lane == 0) wbest[warp] = best;
+    __syncthreads();
+    if (tid == 0) {
+      unsigned long long b = 0;
+      for (int w = 0; w < nw; w++) b = wbest[w] > b ? wbest[w] : b;
+      p.am_part[blockIdx.x] = b;
+      __threadfence();
+      is_last = atomicAdd(p.am_count, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (is_last) {
+      __threadfence();
+      unsigned long long b = 0;
+      for (int i = tid; i < (int)gridDim.x; i += blockDim.x) {
+        const unsigned long long v = *((volatile unsigned long long*)p.am_part + i);
+        b = v > b ? v : b;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, b, o);
+        b = other > b ? other : b;
+      }
+      if (lane == 0) wbest[warp] = b;
+      __syncthreads();
+      if (tid == 0) {
+        unsigned long long bb = 0;
+        for (int w = 0; w < nw; w++) bb = wbest[w] > bb ? wbest[w] : bb;
+        const int tok = unpack_argmax_index(bb);
+        const int pos = *p.d_pos_rw;
+        if (pos + 1 < p.ctx && pos + 1 >= *p.fixed_until) p.seq_tokens[pos + 1] = tok;
+        p.seq_tokens[p.ctx] = tok;  // last argmax, whatever the position
+        *p.d_pos_rw = pos + 1;
+        *p.am_count = 0;
+      }
+    }
+  }
+}
+
+}  // namespace ss

@@ -1,0 +1,1105 @@
+// ss_cuda_api.cu -- the C ABI of the CUDA backend (include/slipstream_cuda.h).
+//
+// Host side of SlipStream's decode path on sm_100a: parses the GGUF, uploads
+// and repacks the weights, allocates the int8 KV cache, and runs one decode
+// step as a CUDA graph of 5 kernels per layer plus the embedding gather and
+// the lm_head (RMSNorm + GEMV + greedy argmax), chained with programmatic
+// dependent launch.  The position and the token of every position live on the
+// device, so consecutive steps need no host round trip.
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+#include "gguf_view.h"
+#include "slipstream_cuda.h"
+#include "ss_cuda_internal.h"
+
+#define SS_API extern "C" __attribute__((visibility("default")))
+
+namespace ss {
+namespace {
+
+thread_local std::string g_err;
+
+struct Error : std::runtime_error {
+  int code;
+  Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+[[noreturn]] void fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  throw Error(code, buf);
+}
+
+#define CK(call)                                                                          \
+  do {                                                                                    \
+    cudaError_t e_ = (call);                                                              \
+    if (e_ != cudaSuccess) {                                                              \
+      fail(e_ == cudaErrorMemoryAllocation ? SS_CUDA_ERROR_OUT_OF_MEMORY                  \
+                                           : SS_CUDA_ERROR_BACKEND,                       \
+           "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__);   \
+    }                                                                                     \
+  } while (0)
+
+template <typename F>
+int guard(F&& f) {
+  try {
+    f();
+    return SS_CUDA_OK;
+  } catch (const Error& e) {
+    g_err = e.what();
+    return e.code;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return SS_CUDA_ERROR_BACKEND;
+  }
+}
+
+template <typename T>
+T* dev_alloc(Context* c, size_t n) {
+  void* p = nullptr;
+  if (n == 0) n = 1;
+  CK(cudaMalloc(&p, n * sizeof(T)));
+  c->allocations.push_back(p);
+  return static_cast<T*>(p);
+}
+
+int round_up(int a, int b) { return (a + b - 1) / b * b; }
+
+// ---------------------------------------------------------------- launches
+
+template <typename... KArgs, typename... Args>
+void launch(void (*fn)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+            Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  CK(cudaLaunchKernelEx(&cfg, fn, std::forward<Args>(args)...));
+}
+
+using GemvFn = void (*)(const GemvParams);
+
+template <int TYPE, XSrc XS, Epi EPI, int G>
+GemvFn gemv_fn() {
+  return &gemv_kernel<TYPE, XS, EPI, G>;
+}
+
+template <XSrc XS, Epi EPI, int G>
+GemvFn gemv_fn_type(int type) {
+  if (type == kQ4_0) return gemv_fn<kQ4_0, XS, EPI, G>();
+  if (type == kQ8_0) return gemv_fn<kQ8_0, XS, EPI, G>();
+  fail(SS_CUDA_ERROR_INVALID_MODEL, "unsupported weight type %d (Q4_0 and Q8_0 only)", type);
+}
+
+constexpr int kG = 4;  // rows per warp iteration
+
+// Geometry: one thread per 32-column block; as many CTAs as fit on the GPU at
+// once (capped by the row count), each owning a contiguous multiple-of-kG
+// range of rows.
+GemvLaunch plan_gemv(Context* c, GemvFn fn, const DevMatrix& m) {
+  GemvLaunch g;
+  g.fn = (const void*)fn;
+  const int nb = m.cols / 32;
+  if (nb < 1 || nb > 1024)
+    fail(SS_CUDA_ERROR_INVALID_MODEL, "matrix with %d columns is outside 32..32768", m.cols);
+  g.threads = round_up(nb, 32);
+  const int nw = g.threads / 32;
+  int occ = 0;
+  // smem depends on rows_per_cta; estimate with a first pass then refine.
+  const int groups = (m.rows + kG - 1) / kG;
+  size_t smem_guess = (size_t)nw * 64 * sizeof(float) + 64 * sizeof(float);
+  CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, g.threads, smem_guess));
+  occ = std::max(occ, 1);
+  int ctas = std::min(groups, c->sm_count * occ);
+  int rpc = round_up((m.rows + ctas - 1) / ctas, kG);
+  g.rows_per_cta = rpc;
+  g.ctas = (m.rows + rpc - 1) / rpc;
+  g.smem = (size_t)nw * rpc * sizeof(float) + 64 * sizeof(float);
+  if (g.smem > 200 * 1024) fail(SS_CUDA_ERROR_INVALID_MODEL, "GEMV reduction buffer too large");
+  return g;
+}
+
+void run_gemv(Context* c, const GemvLaunch& g, GemvParams p, bool pdl) {
+  p.rows_per_cta = g.rows_per_cta;
+  launch((GemvFn)g.fn, dim3(g.ctas), dim3(g.threads), g.smem, c->stream, pdl, p);
+}
+
+// ------------------------------------------------------------- weight upload
+
+DevMatrix layout(int rows, int cols, int type) {
+  DevMatrix m;
+  m.rows = rows;
+  m.cols = cols;
+  m.type = type;
+  const int nb = cols / 32;
+  const int qsz = type == kQ4_0 ? 16 : 32;
+  m.scale_off = nb * qsz;
+  m.row_stride = m.scale_off + round_up(nb * 2, 16);
+  return m;
+}
+
+size_t matrix_bytes(const DevMatrix& m) { return (size_t)m.rows * m.row_stride; }
+
+// Uploads one GGUF matrix (rows x cols blocks) through the staging buffer and
+// repacks it into rows dst_row_mul*r + dst_row_add of `dst`.
+void upload_matrix(Context* c, const GgufTensor& t, const DevMatrix& dst, int dst_row_mul,
+                   int dst_row_add, uint8_t* stage, size_t stage_cap) {
+  if (t.type != dst.type)
+    fail(SS_CUDA_ERROR_INVALID_MODEL, "tensor %s has type %d, expected %d", t.name.c_str(), t.type,
+         dst.type);
+  if ((int)t.cols() != dst.cols)
+    fail(SS_CUDA_ERROR_INVALID_MODEL, "tensor %s has %llu columns, expected %d", t.name.c_str(),
+         (unsigned long long)t.cols(), dst.cols);
+  if (t.bytes > stage_cap) fail(SS_CUDA_ERROR_BACKEND, "staging buffer too small");
+  CK(cudaMemcpyAsync(stage, t.data, t.bytes, cudaMemcpyHostToDevice, c->stream));
+  const long long blocks = (long long)t.rows() * (t.cols() / 32);
+  const int threads = 256;
+  const int grid = (int)std::min<long long>((blocks + threads - 1) / threads, 65535);
+  repack_kernel<<<grid, threads, 0, c->stream>>>(stage, (int)t.rows(), (int)t.cols(), t.type,
+                                                 dst.data, dst.row_stride, dst.scale_off,
+                                                 dst_row_mul, dst_row_add);
+  CK(cudaGetLastError());
+}
+
+const GgufTensor& need(const GgufModel& m, const std::string& name) {
+  const GgufTensor* t = m.find(name);
+  if (!t) fail(SS_CUDA_ERROR_INVALID_MODEL, "GGUF has no tensor %s", name.c_str());
+  return *t;
+}
+
+float* upload_f32(Context* c, const GgufTensor& t, size_t n) {
+  if (t.type != kF32) fail(SS_CUDA_ERROR_INVALID_MODEL, "%s must be F32", t.name.c_str());
+  if (t.bytes < n * 4) fail(SS_CUDA_ERROR_INVALID_MODEL, "%s is too small", t.name.c_str());
+  float* p = dev_alloc<float>(c, n);
+  CK(cudaMemcpyAsync(p, t.data, n * 4, cudaMemcpyHostToDevice, c->stream));
+  return p;
+}
+
+void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt) {
+  GgufModel g;
+  std::string err;
+  if (!gguf_parse(base, size, &g, &err)) fail(SS_CUDA_ERROR_INVALID_MODEL, "%s", err.c_str());
+  if (g.arch.find("llama") == std::string::npos)
+    fail(SS_CUDA_ERROR_INVALID_MODEL, "architecture '%s' is not llama", g.arch.c_str());
+  c->d = (int)g.hidden;
+  c->L = (int)g.n_layers;
+  c->nh = (int)g.n_heads;
+  c->nkv = g.n_kv_heads ? (int)g.n_kv_heads : c->nh;
+  c->ff = (int)g.ffn;
+  c->eps = g.rms_eps;
+  c->theta = g.rope_theta;
+  if (c->d <= 0 || c->L <= 0 || c->nh <= 0 || c->ff <= 0)
+    fail(SS_CUDA_ERROR_INVALID_MODEL, "missing llama dimensions in GGUF metadata");
+  const GgufTensor& wq0 = need(g, "blk.0.attn_q.weight");
+  // head_dim, rope_dim, vocab clamp: SlipStream/src/core/layer_scheduler.c:161-197
+  c->hd = g.key_length ? (int)g.key_length : (int)(wq0.rows() / (uint64_t)c->nh);
+  c->rope_dim = g.rope_dim ? (int)g.rope_dim : c->hd;
+  const GgufTensor& embd = need(g, "token_embd.weight");
+  const GgufTensor* out = g.find("output.weight");
+  int vocab = (int)g.vocab;
+  if (out && (int)out->rows() < vocab) vocab = (int)out->rows();
+  if ((int)embd.rows() < vocab) vocab = (int)embd.rows();
+  c->vocab = vocab;
+  if (c->nh % c->nkv) fail(SS_CUDA_ERROR_INVALID_MODEL, "heads %% kv_heads != 0");
+  if (c->nh / c->nkv > 8) fail(SS_CUDA_ERROR_INVALID_MODEL, "GQA group above 8 is not supported");
+  if (c->hd % 32 || c->hd > 256 || c->rope_dim > c->hd || c->rope_dim % 2)
+    fail(SS_CUDA_ERROR_INVALID_MODEL, "head_dim %d / rope_dim %d unsupported", c->hd, c->rope_dim);
+  // context: engine.c:99-106 (default from the file, capped at 8192)
+  uint32_t ctx = ctx_opt ? ctx_opt : g.context_length;
+  if (ctx == 0 || ctx > 8192) ctx = 8192;
+  c->ctx = (int)ctx;
+  c->wtype = wq0.type;
+  if (c->wtype != kQ4_0 && c->wtype != kQ8_0)
+    fail(SS_CUDA_ERROR_INVALID_MODEL, "weight type %d unsupported (Q4_0 / Q8_0)", c->wtype);
+  c->attn_scale = 1.0f / sqrtf((float)c->hd);  // layer_scheduler.c:421
+
+  const int qd = c->nh * c->hd, kvd = c->nkv * c->hd;
+  size_t max_bytes = 0;
+  for (const auto& t : g.tensors) max_bytes = std::max<size_t>(max_bytes, t.bytes);
+  uint8_t* stage = nullptr;
+  CK(cudaMalloc(&stage, max_bytes));
+
+  try {
+    // embeddings: F32 rows (layer_scheduler.c:585-587)
+    if (embd.type != kF32) fail(SS_CUDA_ERROR_INVALID_MODEL, "token_embd.weight must be F32");
+    if ((int)embd.cols() != c->d) fail(SS_CUDA_ERROR_INVALID_MODEL, "token_embd width mismatch");
+    c->embd = upload_f32(c, embd, (size_t)embd.rows() * c->d);
+    c->weight_bytes += (size_t)embd.rows() * c->d * 4;
+    c->layers.resize((size_t)c->L);
+    for (int l = 0; l < c->L; l++) {
+      Layer& ly = c->layers[(size_t)l];
+      auto nm = [&](const char* s) { return "blk." + std::to_string(l) + "." + s; };
+      const GgufTensor& wq = need(g, nm("attn_q.weight"));
+      const GgufTensor& wk = need(g, nm("attn_k.weight"));
+      const GgufTensor& wv = need(g, nm("attn_v.weight"));
+      const GgufTensor& wo = need(g, nm("attn_output.weight"));
+      const GgufTensor& wg = need(g, nm("ffn_gate.weight"));
+      const GgufTensor& wu = need(g, nm("ffn_up.weight"));
+      const GgufTensor& wd = need(g, nm("ffn_down.weight"));
+      if ((int)wq.rows() != qd || (int)wk.rows() != kvd || (int)wv.rows() != kvd ||
+          (int)wo.rows() != c->d || (int)wo.cols() != qd || (int)wg.rows() != c->ff ||
+          (int)wu.rows() != c->ff || (int)wd.rows() != c->d || (int)wd.cols() != c->ff)
+        fail(SS_CUDA_ERROR_INVALID_MODEL, "layer %d tensor shapes do not match the metadata", l);
+      ly.qkv = layout(qd + 2 * kvd, c->d, c->wtype);
+      ly.o = layout(c->d, qd, c->wtype);
+      ly.gu = layout(2 * c->ff, c->d, c->wtype);
+      ly.down = layout(c->d, c->ff, c->wtype);
+      const size_t b0 = matrix_bytes(ly.qkv), b1 = matrix_bytes(ly.o), b2 = matrix_bytes(ly.gu),
+                   b3 = matrix_bytes(ly.down);
+      ly.block = dev_alloc<uint8_t>(c, b0 + b1 + b2 + b3);
+      CK(cudaMemsetAsync(ly.block, 0, b0 + b1 + b2 + b3, c->stream));
+      ly.qkv.data = ly.block;
+      ly.o.data = ly.block + b0;
+      ly.gu.data = ly.block + b0 + b1;
+      ly.down.data = ly.block + b0 + b1 + b2;
+      c->weight_bytes += b0 + b1 + b2 + b3;
+      upload_matrix(c, wq, ly.qkv, 1, 0, stage, max_bytes);
+      upload_matrix(c, wk, ly.qkv, 1, qd, stage, max_bytes);
+      upload_matrix(c, wv, ly.qkv, 1, qd + kvd, stage, max_bytes);
+      upload_matrix(c, wo, ly.o, 1, 0, stage, max_bytes);
+      upload_matrix(c, wg, ly.gu, 2, 0, stage, max_bytes);
+      upload_matrix(c, wu, ly.gu, 2, 1, stage, max_bytes);
+      upload_matrix(c, wd, ly.down, 1, 0, stage, max_bytes);
+      ly.attn_norm = upload_f32(c, need(g, nm("attn_norm.weight")), (size_t)c->d);
+      ly.ffn_norm = upload_f32(c, need(g, nm("ffn_norm.weight")), (size_t)c->d);
+      CK(cudaStreamSynchronize(c->stream));  // staging buffer reuse
+    }
+    c->out_norm = upload_f32(c, need(g, "output_norm.weight"), (size_t)c->d);
+    if (!out) fail(SS_CUDA_ERROR_INVALID_MODEL, "tied embeddings (no output.weight) unsupported");
+    c->lm_head = layout(c->vocab, c->d, out->type);
+    if (out->type != kQ4_0 && out->type != kQ8_0)
+      fail(SS_CUDA_ERROR_INVALID_MODEL, "output.weight type %d unsupported", out->type);
+    c->lm_block = dev_alloc<uint8_t>(c, matrix_bytes(c->lm_head));
+    c->lm_head.data = c->lm_block;
+    c->weight_bytes += matrix_bytes(c->lm_head);
+    // only the first `vocab` rows are addressable (layer_scheduler.c:189-197)
+    GgufTensor head = *out;
+    head.dims[1] = (uint64_t)c->vocab;
+    head.bytes = (uint64_t)c->vocab * (head.cols() / 32) * ggml_type_size(head.type);
+    upload_matrix(c, head, c->lm_head, 1, 0, stage, max_bytes);
+    CK(cudaStreamSynchronize(c->stream));
+  } catch (...) {
+    cudaFree(stage);
+    throw;
+  }
+  CK(cudaFree(stage));
+}
+
+void alloc_state(Context* c) {
+  const int kvd = c->nkv * c->hd, qd = c->nh * c->hd;
+  const size_t rows = (size_t)c->L * c->ctx;
+  c->kc = dev_alloc<int8_t>(c, rows * kvd);
+  c->vc = dev_alloc<int8_t>(c, rows * kvd);
+  c->ks = dev_alloc<float>(c, rows);
+  c->vs = dev_alloc<float>(c, rows);
+  c->amax_k = dev_alloc<unsigned int>(c, rows);
+  c->amax_v = dev_alloc<unsigned int>(c, rows);
+  c->kv_bytes = rows * (2 * (size_t)kvd + 16);
+  c->h = dev_alloc<float>(c, (size_t)c->d);
+  c->qkv = dev_alloc<float>(c, (size_t)qd + 2 * kvd);
+  c->attn_out = dev_alloc<float>(c, (size_t)std::max(qd, c->d));
+  c->act = dev_alloc<float>(c, (size_t)c->ff);
+  c->logits = dev_alloc<float>(c, (size_t)c->vocab);
+  // attention split: ~2 CTAs per SM over the kv heads
+  c->attn_nsplit = std::max(1, std::min(64, (2 * c->sm_count + c->nkv - 1) / c->nkv));
+  c->attn_chunk_max = (c->ctx + c->attn_nsplit - 1) / c->attn_nsplit;
+  const int g = c->nh / c->nkv;
+  c->attn_smem = ((size_t)g * c->attn_chunk_max + 64) * sizeof(float);
+  if (c->attn_smem > 200 * 1024) fail(SS_CUDA_ERROR_INVALID_PARAMS, "context too long for attention");
+  c->part_o = dev_alloc<float>(c, (size_t)c->nkv * c->attn_nsplit * g * c->hd);
+  c->part_ml = dev_alloc<float>(c, (size_t)c->nkv * c->attn_nsplit * g * 2);
+  c->attn_cnt = dev_alloc<unsigned int>(c, (size_t)c->nkv);
+  c->am_part = dev_alloc<unsigned long long>(c, 4096);
+  c->am_cnt = dev_alloc<unsigned int>(c, 1);
+  c->seq_tokens = dev_alloc<int>(c, (size_t)c->ctx + 1);
+  c->ctrl = dev_alloc<Ctrl>(c, 1);
+  CK(cudaMemsetAsync(c->attn_cnt, 0, sizeof(unsigned) * c->nkv, c->stream));
+  CK(cudaMemsetAsync(c->am_cnt, 0, sizeof(unsigned), c->stream));
+  CK(cudaMemsetAsync(c->seq_tokens, 0, sizeof(int) * (c->ctx + 1), c->stream));
+  CK(cudaMemsetAsync(c->ctrl, 0, sizeof(Ctrl), c->stream));
+  // RoPE table, computed with the reference's float expressions
+  // (SlipStream/src/core/tensor.c:250-254) so cos/sin match it exactly.
+  const int half = c->rope_dim / 2;
+  std::vector<float2> tab((size_t)c->ctx * half);
+  for (int pos = 0; pos < c->ctx; pos++)
+    for (int j = 0; j < half; j++) {
+      const float freq = 1.0f / powf(c->theta, (float)(2 * j) / (float)c->rope_dim);
+      const float angle = (float)pos * freq;
+      tab[(size_t)pos * half + j] = make_float2(cosf(angle), sinf(angle));
+    }
+  c->rope_tab = dev_alloc<float2>(c, tab.size());
+  CK(cudaMemcpy(c->rope_tab, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+  CK(cudaMallocHost(&c->h_logits, sizeof(float) * (size_t)c->vocab));
+  CK(cudaMallocHost(&c->h_small, sizeof(int) * 64));
+  c->embed_blocks = std::max(1, std::min(16, (c->d + 255) / 256));
+}
+
+void plan_all(Context* c) {
+  const Layer& l0 = c->layers[0];
+  c->g_qkv = plan_gemv(c, gemv_fn_type<XSrc::RmsNorm, Epi::QKV, kG>(c->wtype), l0.qkv);
+  c->g_o = plan_gemv(c, gemv_fn_type<XSrc::Plain, Epi::Residual, kG>(c->wtype), l0.o);
+  c->g_gu = plan_gemv(c, gemv_fn_type<XSrc::RmsNorm, Epi::SwiGLU, kG>(c->wtype), l0.gu);
+  c->g_down = plan_gemv(c, gemv_fn_type<XSrc::Plain, Epi::Residual, kG>(c->wtype), l0.down);
+  c->g_head = plan_gemv(c, gemv_fn_type<XSrc::RmsNorm, Epi::Argmax, kG>(c->lm_head.type), c->lm_head);
+  if (c->g_head.ctas > 4096) fail(SS_CUDA_ERROR_INVALID_MODEL, "lm_head grid too large");
+  if (c->hd == 64) CK(cudaFuncSetAttribute(attention_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  if (c->hd == 128) CK(cudaFuncSetAttribute(attention_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  if (c->hd == 32) CK(cudaFuncSetAttribute(attention_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  if (c->hd == 256) CK(cudaFuncSetAttribute(attention_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+}
+
+GemvParams base_params(Context* c) {
+  GemvParams p = {};
+  p.eps = c->eps;
+  p.d_pos = &c->ctrl->pos;
+  p.ctx = c->ctx;
+  p.err = &c->ctrl->err;
+  p.prefetch = 1;
+  return p;
+}
+
+// ---- the kernels of one decode step ------------------------------------
+
+void launch_embed(Context* c, bool pdl) {
+  EmbedParams e{c->embd, c->d, c->vocab, c->L, c->ctx, c->seq_tokens, &c->ctrl->pos,
+                c->h, c->amax_k, c->amax_v, &c->ctrl->err};
+  launch(embed_kernel, dim3(c->embed_blocks), dim3(256), 0, c->stream, pdl, e);
+}
+
+// RMSNorm(h) -> [Wq;Wk;Wv] -> RoPE(q, k), |k| / |v| maxima of this position.
+void launch_qkv(Context* c, int l, bool pdl) {
+  const Layer& ly = c->layers[(size_t)l];
+  const size_t lo = (size_t)l * c->ctx;
+  GemvParams p = base_params(c);
+  p.w = ly.qkv.q();
+  p.x = c->h;
+  p.norm_w = ly.attn_norm;
+  p.out = c->qkv;
+  p.q_rows = c->nh * c->hd;
+  p.kv_rows = c->nkv * c->hd;
+  p.head_dim = c->hd;
+  p.rope_dim = c->rope_dim;
+  p.rope_tab = c->rope_tab;
+  p.amax_k = c->amax_k + lo;
+  p.amax_v = c->amax_v + lo;
+  run_gemv(c, c->g_qkv, p, pdl);
+}
+
+// int8 K/V append + GQA attention over positions 0..pos.
+void launch_attn(Context* c, int l, bool pdl) {
+  const int kvd = c->nkv * c->hd;
+  const size_t lo = (size_t)l * c->ctx;
+  AttnParams a{};
+  a.qkv = c->qkv;
+  a.kc = c->kc + lo * kvd;
+  a.vc = c->vc + lo * kvd;
+  a.ks = c->ks + lo;
+  a.vs = c->vs + lo;
+  a.amax_k = c->amax_k + lo;
+  a.amax_v = c->amax_v + lo;
+  a.d_pos = &c->ctrl->pos;
+  a.part_o = c->part_o;
+  a.part_ml = c->part_ml;
+  a.counters = c->attn_cnt;
+  a.out = c->attn_out;
+  a.nh = c->nh;
+  a.nkv = c->nkv;
+  a.hd = c->hd;
+  a.ctx = c->ctx;
+  a.nsplit = c->attn_nsplit;
+  a.chunk_max = c->attn_chunk_max;
+  a.scale = c->attn_scale;
+  const dim3 grid(c->attn_nsplit, c->nkv);
+  switch (c->hd) {
+    case 32: launch(attention_kernel<1>, grid, dim3(128), c->attn_smem, c->stream, pdl, a); break;
+    case 64: launch(attention_kernel<2>, grid, dim3(128), c->attn_smem, c->stream, pdl, a); break;
+    case 128: launch(attention_kernel<4>, grid, dim3(128), c->attn_smem, c->stream, pdl, a); break;
+    case 256: launch(attention_kernel<8>, grid, dim3(128), c->attn_smem, c->stream, pdl, a); break;
+    default: fail(SS_CUDA_ERROR_INVALID_MODEL, "head_dim %d", c->hd);
+  }
+}
+
+// h = Wo . attn + h
+void launch_o(Context* c, int l, bool pdl) {
+  GemvParams p = base_params(c);
+  p.w = c->layers[(size_t)l].o.q();
+  p.x = c->attn_out;
+  p.out = c->h;
+  p.residual = c->h;
+  run_gemv(c, c->g_o, p, pdl);
+}
+
+// act = up * silu(gate) of RMSNorm(h)
+void launch_gu(Context* c, int l, bool pdl) {
+  const Layer& ly = c->layers[(size_t)l];
+  GemvParams p = base_params(c);
+  p.w = ly.gu.q();
+  p.x = c->h;
+  p.norm_w = ly.ffn_norm;
+  p.out = c->act;
+  run_gemv(c, c->g_gu, p, pdl);
+}
+
+// h = Wdown . act + h
+void launch_down(Context* c, int l, bool pdl) {
+  GemvParams p = base_params(c);
+  p.w = c->layers[(size_t)l].down.q();
+  p.x = c->act;
+  p.out = c->h;
+  p.residual = c->h;
+  run_gemv(c, c->g_down, p, pdl);
+}
+
+// logits = W_out . RMSNorm(h); greedy argmax -> token of pos + 1; pos += 1.
+void launch_head(Context* c, bool pdl) {
+  GemvParams p = base_params(c);
+  p.w = c->lm_head.q();
+  p.x = c->h;
+  p.norm_w = c->out_norm;
+  p.out = c->logits;
+  p.am_part = c->am_part;
+  p.am_count = c->am_cnt;
+  p.seq_tokens = c->seq_tokens;
+  p.fixed_until = &c->ctrl->fixed_until;
+  p.d_pos_rw = &c->ctrl->pos;
+  run_gemv(c, c->g_head, p, pdl);
+}
+
+// Enqueues one decode step (embedding -> L layers -> lm_head + argmax).
+void enqueue_step(Context* c, bool pdl) {
+  launch_embed(c, pdl);
+  for (int l = 0; l < c->L; l++) {
+    launch_qkv(c, l, pdl);
+    launch_attn(c, l, pdl);
+    launch_o(c, l, pdl);
+    launch_gu(c, l, pdl);
+    launch_down(c, l, pdl);
+  }
+  launch_head(c, pdl);
+}
+
+void build_graph(Context* c) {
+  if (c->step_exec || !c->use_graph) return;
+  for (int attempt = 0; attempt < 2; attempt++) {
+    const bool pdl = c->use_pdl && attempt == 0;
+    cudaGraph_t graph = nullptr;
+    CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    try {
+      enqueue_step(c, pdl);
+    } catch (...) {
+      cudaStreamEndCapture(c->stream, &graph);
+      if (graph) cudaGraphDestroy(graph);
+      throw;
+    }
+    CK(cudaStreamEndCapture(c->stream, &graph));
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e == cudaSuccess) {
+      c->step_exec = exec;
+      c->graph_pdl = pdl;
+      return;
+    }
+    cudaGetLastError();
+    if (!pdl) fail(SS_CUDA_ERROR_BACKEND, "cudaGraphInstantiate: %s", cudaGetErrorString(e));
+  }
+}
+
+void run_steps(Context* c, int n) {
+  if (c->cancelled.load()) fail(SS_CUDA_ERROR_CANCELLED, "cancelled");
+  if (n <= 0) return;
+  if (c->host_pos + n > c->ctx)
+    fail(SS_CUDA_ERROR_INVALID_PARAMS, "positions %d..%d exceed the context of %d", c->host_pos,
+         c->host_pos + n - 1, c->ctx);
+  build_graph(c);
+  for (int i = 0; i < n; i++) {
+    if (c->step_exec) CK(cudaGraphLaunch(c->step_exec, c->stream));
+    else enqueue_step(c, c->use_pdl);
+  }
+  c->host_pos += n;
+  c->steps_run += n;
+}
+
+void set_position(Context* c, int pos, int fixed_until) {
+  if (pos < 0 || pos >= c->ctx) fail(SS_CUDA_ERROR_INVALID_PARAMS, "position %d outside 0..%d", pos, c->ctx - 1);
+  c->h_small[0] = pos;
+  c->h_small[1] = fixed_until;
+  CK(cudaMemcpyAsync(c->ctrl, c->h_small, 2 * sizeof(int), cudaMemcpyHostToDevice, c->stream));
+  c->host_pos = pos;
+}
+
+void put_tokens(Context* c, const int32_t* toks, int n, int pos) {
+  for (int i = 0; i < n; i++)
+    if (toks[i] < 0 || toks[i] >= c->vocab)
+      fail(SS_CUDA_ERROR_INVALID_PARAMS, "token %d outside 0..%d", toks[i], c->vocab - 1);
+  if (pos < 0 || pos + n > c->ctx) fail(SS_CUDA_ERROR_INVALID_PARAMS, "tokens past the context");
+  CK(cudaMemcpyAsync(c->seq_tokens + pos, toks, sizeof(int) * n, cudaMemcpyHostToDevice, c->stream));
+}
+
+void check_device_error(Context* c) {
+  int err = 0;
+  CK(cudaMemcpyAsync(&c->h_small[8], &c->ctrl->err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+  err = c->h_small[8];
+  if (err) {
+    CK(cudaMemsetAsync(&c->ctrl->err, 0, sizeof(int), c->stream));
+    fail(SS_CUDA_ERROR_BACKEND, "device reported error bits 0x%x (1: position, 2: token)", err);
+  }
+}
+
+void read_logits(Context* c, float* dst) {
+  CK(cudaMemcpyAsync(c->h_logits, c->logits, sizeof(float) * c->vocab, cudaMemcpyDeviceToHost, c->stream));
+  CK(cudaMemcpyAsync(&c->h_small[16], c->seq_tokens + c->ctx, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+  check_device_error(c);
+  if (dst && dst != c->h_logits) memcpy(dst, c->h_logits, sizeof(float) * c->vocab);
+}
+
+Context* create(const uint8_t* base, uint64_t size, const ss_cuda_options_t* o) {
+  ss_cuda_options_t opts;
+  ss_cuda_default_options(&opts);
+  if (o) memcpy(&opts, o, std::min<size_t>(sizeof(opts), o->struct_size ? o->struct_size : sizeof(opts)));
+  if (opts.max_batch == 0) opts.max_batch = 1;
+  if (opts.max_batch != 1)
+    fail(SS_CUDA_ERROR_INVALID_PARAMS, "max_batch %u: only single-sequence decode is built", opts.max_batch);
+  int dev = opts.device;
+  if (dev < 0) {
+    const char* e = getenv("SS_CUDA_DEVICE");
+    dev = e ? atoi(e) : 0;
+  }
+  int ndev = 0;
+  CK(cudaGetDeviceCount(&ndev));
+  if (dev >= ndev) fail(SS_CUDA_ERROR_INVALID_PARAMS, "device %d of %d", dev, ndev);
+  CK(cudaSetDevice(dev));
+  cudaDeviceProp prop;
+  CK(cudaGetDeviceProperties(&prop, dev));
+  if (prop.major < 10) fail(SS_CUDA_ERROR_BACKEND, "device %s is sm_%d%d; sm_100a required", prop.name, prop.major, prop.minor);
+  auto* c = new Context();
+  c->device = dev;
+  c->sm_count = prop.multiProcessorCount;
+  c->max_batch = (int)opts.max_batch;
+  c->use_pdl = !(opts.flags & SS_CUDA_FLAG_NO_PDL) && !getenv("SS_CUDA_NO_PDL");
+  c->use_graph = !(opts.flags & SS_CUDA_FLAG_NO_GRAPH);
+  try {
+    CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    if (base) {
+      load_model(c, base, size, opts.context_size);
+      alloc_state(c);
+      plan_all(c);
+      CK(cudaStreamSynchronize(c->stream));
+      c->has_model = true;
+    }
+  } catch (...) {
+    ss_cuda_free(reinterpret_cast<ss_cuda_ctx_t*>(c));
+    throw;
+  }
+  return c;
+}
+
+Context* need_model(ss_cuda_ctx_t* ctx) {
+  auto* c = reinterpret_cast<Context*>(ctx);
+  if (!c) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null context");
+  if (!c->has_model) fail(SS_CUDA_ERROR_INVALID_PARAMS, "context has no model");
+  CK(cudaSetDevice(c->device));
+  return c;
+}
+
+// ------------------------------------------------- op-level (Metal twin) path
+
+OpCacheEntry& op_weights(Context* c, const void* mat, int rows, int cols, int type) {
+  auto it = c->op_cache.find(mat);
+  if (it != c->op_cache.end()) {
+    const OpCacheEntry& e = it->second;
+    const int r = e.f32 ? e.m.rows : e.m.rows, cc = e.m.cols;
+    if (r == rows && cc == cols && e.m.type == type) return it->second;
+    fail(SS_CUDA_ERROR_INVALID_PARAMS, "weight pointer reused with a different shape");
+  }
+  OpCacheEntry e;
+  e.m.rows = rows;
+  e.m.cols = cols;
+  e.m.type = type;
+  if (type == kF32) {
+    e.f32 = dev_alloc<float>(c, (size_t)rows * cols);
+    CK(cudaMemcpyAsync(e.f32, mat, sizeof(float) * (size_t)rows * cols, cudaMemcpyHostToDevice, c->stream));
+  } else {
+    e.m = layout(rows, cols, type);
+    e.m.data = dev_alloc<uint8_t>(c, matrix_bytes(e.m));
+    CK(cudaMemsetAsync(e.m.data, 0, matrix_bytes(e.m), c->stream));
+    GgufTensor t;
+    t.name = "matvec operand";
+    t.n_dims = 2;
+    t.dims[0] = (uint64_t)cols;
+    t.dims[1] = (uint64_t)rows;
+    t.type = type;
+    t.bytes = (uint64_t)rows * (cols / 32) * ggml_type_size(type);
+    t.data = static_cast<const uint8_t*>(mat);
+    if (c->op_stage_cap < t.bytes) {
+      if (c->op_stage) CK(cudaFree(c->op_stage));
+      c->op_stage = nullptr;
+      CK(cudaMalloc(&c->op_stage, t.bytes));
+      c->op_stage_cap = t.bytes;
+    }
+    upload_matrix(c, t, e.m, 1, 0, c->op_stage, c->op_stage_cap);
+  }
+  return c->op_cache.emplace(mat, e).first->second;
+}
+
+bool op_matvec(ss_cuda_ctx_t* ctx, float* out, const void* mat, const float* vec, int rows, int cols,
+               int type) {
+  return guard([&] {
+           auto* c = reinterpret_cast<Context*>(ctx);
+           if (!c || !out || !mat || !vec || rows <= 0 || cols <= 0)
+             fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad matvec arguments");
+           if (type != kF32 && cols % 32) fail(SS_CUDA_ERROR_INVALID_PARAMS, "cols %% 32 != 0");
+           CK(cudaSetDevice(c->device));
+           OpCacheEntry& w = op_weights(c, mat, rows, cols, type);
+           const int slot = c->in_batch ? c->batch_count : 0;
+           if (c->in_batch && slot >= 64) fail(SS_CUDA_ERROR_INVALID_PARAMS, "more than 64 matvecs in a batch");
+           if ((int)c->op_slots.size() <= slot) c->op_slots.resize((size_t)slot + 1);
+           auto& s = c->op_slots[(size_t)slot];
+           if (s.x_cap < (size_t)cols) {
+             if (s.d_x) CK(cudaFree(s.d_x));
+             s.d_x = nullptr;
+             CK(cudaMalloc(&s.d_x, sizeof(float) * cols));
+             s.x_cap = (size_t)cols;
+           }
+           if (s.out_cap < (size_t)rows) {
+             if (s.d_out) CK(cudaFree(s.d_out));
+             s.d_out = nullptr;
+             CK(cudaMalloc(&s.d_out, sizeof(float) * rows));
+             s.out_cap = (size_t)rows;
+           }
+           CK(cudaMemcpyAsync(s.d_x, vec, sizeof(float) * cols, cudaMemcpyHostToDevice, c->stream));
+           if (type == kF32) {
+             const int threads = 256;
+             const int grid = (rows * 32 + threads - 1) / threads;
+             matvec_f32_kernel<<<grid, threads, 0, c->stream>>>(w.f32, s.d_x, s.d_out, rows, cols);
+             CK(cudaGetLastError());
+           } else {
+             GemvFn fn = gemv_fn_type<XSrc::Plain, Epi::Store, kG>(type);
+             GemvLaunch g = plan_gemv(c, fn, w.m);
+             GemvParams p = base_params(c);
+             p.w = w.m.q();
+             p.x = s.d_x;
+             p.out = s.d_out;
+             p.prefetch = 0;
+             run_gemv(c, g, p, false);
+           }
+           if (c->in_batch) {
+             s.host_out = out;
+             s.out_n = (size_t)rows;
+             c->batch_count++;
+           } else {
+             CK(cudaMemcpyAsync(out, s.d_out, sizeof(float) * rows, cudaMemcpyDeviceToHost, c->stream));
+             CK(cudaStreamSynchronize(c->stream));
+           }
+         }) == SS_CUDA_OK;
+}
+
+}  // namespace
+}  // namespace ss
+
+using namespace ss;
+
+// ======================================================================= C ABI
+
+SS_API void ss_cuda_default_options(ss_cuda_options_t* o) {
+  if (!o) return;
+  memset(o, 0, sizeof(*o));
+  o->struct_size = sizeof(*o);
+  o->device = -1;
+  o->max_batch = 1;
+}
+
+SS_API int ss_cuda_abi_version(void) { return SS_CUDA_ABI_VERSION; }
+
+SS_API const char* ss_cuda_last_error(void) { return g_err.c_str(); }
+
+SS_API ss_cuda_ctx_t* ss_cuda_init(const void* gguf_base, uint64_t gguf_size, const ss_cuda_options_t* opts) {
+  Context* c = nullptr;
+  const int rc = guard([&] { c = create(static_cast<const uint8_t*>(gguf_base), gguf_size, opts); });
+  return rc == SS_CUDA_OK ? reinterpret_cast<ss_cuda_ctx_t*>(c) : nullptr;
+}
+
+SS_API ss_cuda_ctx_t* ss_cuda_init_file(const char* path, const ss_cuda_options_t* opts) {
+  Context* c = nullptr;
+  const int rc = guard([&] {
+    if (!path) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null path");
+    const int fd = open(path, O_RDONLY);
+    if (fd < 0) fail(SS_CUDA_ERROR_FILE_NOT_FOUND, "cannot open %s", path);
+    struct stat st;
+    if (fstat(fd, &st) != 0) { close(fd); fail(SS_CUDA_ERROR_FILE_NOT_FOUND, "cannot stat %s", path); }
+    void* map = mmap(nullptr, (size_t)st.st_size, PROT_READ, MAP_SHARED, fd, 0);
+    close(fd);
+    if (map == MAP_FAILED) fail(SS_CUDA_ERROR_INVALID_MODEL, "mmap of %s failed", path);
+    madvise(map, (size_t)st.st_size, MADV_SEQUENTIAL);
+    try {
+      c = create(static_cast<const uint8_t*>(map), (uint64_t)st.st_size, opts);
+    } catch (...) {
+      munmap(map, (size_t)st.st_size);
+      throw;
+    }
+    munmap(map, (size_t)st.st_size);
+  });
+  return rc == SS_CUDA_OK ? reinterpret_cast<ss_cuda_ctx_t*>(c) : nullptr;
+}
+
+SS_API void ss_cuda_free(ss_cuda_ctx_t* ctx) {
+  auto* c = reinterpret_cast<Context*>(ctx);
+  if (!c) return;
+  cudaSetDevice(c->device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  if (c->step_exec) cudaGraphExecDestroy(c->step_exec);
+  for (void* p : c->allocations) cudaFree(p);
+  for (auto& s : c->op_slots) {
+    if (s.d_x) cudaFree(s.d_x);
+    if (s.d_out) cudaFree(s.d_out);
+  }
+  if (c->op_stage) cudaFree(c->op_stage);
+  if (c->h_logits) cudaFreeHost(c->h_logits);
+  if (c->h_small) cudaFreeHost(c->h_small);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+}
+
+SS_API int ss_cuda_model_dims(const ss_cuda_ctx_t* ctx, int32_t* dims) {
+  return guard([&] {
+    auto* c = reinterpret_cast<const Context*>(ctx);
+    if (!c || !dims) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null argument");
+    const int32_t v[12] = {c->vocab, c->d, c->L, c->nh, c->nkv, c->hd, c->ff, c->ctx, c->rope_dim,
+                           c->wtype, c->max_batch, c->device};
+    memcpy(dims, v, sizeof(v));
+  });
+}
+
+SS_API int ss_cuda_stats(const ss_cuda_ctx_t* ctx, int64_t* out, int32_t n) {
+  return guard([&] {
+    auto* c = reinterpret_cast<const Context*>(ctx);
+    if (!c || !out) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null argument");
+    const int64_t v[8] = {c->has_model ? 2 + 5LL * c->L : 0,
+                          (int64_t)c->weight_bytes,
+                          (int64_t)c->kv_bytes,
+                          c->attn_nsplit,
+                          c->graph_pdl ? 1 : 0,
+                          c->steps_run,
+                          c->g_qkv.ctas,
+                          c->g_down.ctas};
+    for (int i = 0; i < n && i < 8; i++) out[i] = v[i];
+  });
+}
+
+SS_API bool ss_cuda_should_use_gpu(int32_t rows, int32_t cols) {
+  (void)rows;
+  (void)cols;
+  return true;  // every matvec runs on the GPU; there is no CPU fallback
+}
+
+SS_API bool ss_cuda_matvec(ss_cuda_ctx_t* ctx, float* out, const float* mat, const float* vec, int32_t rows, int32_t cols) {
+  return op_matvec(ctx, out, mat, vec, rows, cols, kF32);
+}
+SS_API bool ss_cuda_matvec_q4_0(ss_cuda_ctx_t* ctx, float* out, const void* mat, const float* vec, int32_t rows, int32_t cols) {
+  return op_matvec(ctx, out, mat, vec, rows, cols, kQ4_0);
+}
+SS_API bool ss_cuda_matvec_q8_0(ss_cuda_ctx_t* ctx, float* out, const void* mat, const float* vec, int32_t rows, int32_t cols) {
+  return op_matvec(ctx, out, mat, vec, rows, cols, kQ8_0);
+}
+
+SS_API void ss_cuda_begin_batch(ss_cuda_ctx_t* ctx) {
+  auto* c = reinterpret_cast<Context*>(ctx);
+  if (!c || c->in_batch) return;
+  c->in_batch = true;
+  c->batch_count = 0;
+}
+
+SS_API void ss_cuda_end_batch(ss_cuda_ctx_t* ctx) {
+  auto* c = reinterpret_cast<Context*>(ctx);
+  if (!c || !c->in_batch) return;
+  guard([&] {
+    CK(cudaSetDevice(c->device));
+    for (int i = 0; i < c->batch_count; i++) {
+      auto& s = c->op_slots[(size_t)i];
+      CK(cudaMemcpyAsync(s.host_out, s.d_out, sizeof(float) * s.out_n, cudaMemcpyDeviceToHost, c->stream));
+    }
+    CK(cudaStreamSynchronize(c->stream));
+  });
+  c->in_batch = false;
+  c->batch_count = 0;
+}
+
+SS_API float* ss_cuda_scheduler_forward(ss_cuda_ctx_t* ctx, int32_t token_id, int32_t pos) {
+  float* res = nullptr;
+  guard([&] {
+    Context* c = need_model(ctx);
+    if (c->cancelled.load()) fail(SS_CUDA_ERROR_CANCELLED, "cancelled");
+    put_tokens(c, &token_id, 1, pos);
+    set_position(c, pos, pos + 1);
+    run_steps(c, 1);
+    read_logits(c, nullptr);
+    res = c->h_logits;
+  });
+  return res;
+}
+
+SS_API float* ss_cuda_scheduler_prefill(ss_cuda_ctx_t* ctx, const int32_t* tokens, int32_t n, int32_t start_pos) {
+  float* res = nullptr;
+  guard([&] {
+    Context* c = need_model(ctx);
+    if (!tokens || n <= 0) fail(SS_CUDA_ERROR_INVALID_PARAMS, "empty prompt");
+    if (c->cancelled.load()) fail(SS_CUDA_ERROR_CANCELLED, "cancelled");
+    put_tokens(c, tokens, n, start_pos);
+    set_position(c, start_pos, start_pos + n);
+    run_steps(c, n);
+    read_logits(c, nullptr);
+    res = c->h_logits;
+  });
+  return res;
+}
+
+SS_API void ss_cuda_reset(ss_cuda_ctx_t* ctx) {
+  guard([&] {
+    Context* c = need_model(ctx);
+    const size_t rows = (size_t)c->L * c->ctx, kvd = (size_t)c->nkv * c->hd;
+    CK(cudaMemsetAsync(c->kc, 0, rows * kvd, c->stream));
+    CK(cudaMemsetAsync(c->vc, 0, rows * kvd, c->stream));
+    CK(cudaMemsetAsync(c->ks, 0, rows * 4, c->stream));
+    CK(cudaMemsetAsync(c->vs, 0, rows * 4, c->stream));
+    CK(cudaMemsetAsync(c->amax_k, 0, rows * 4, c->stream));
+    CK(cudaMemsetAsync(c->amax_v, 0, rows * 4, c->stream));
+    CK(cudaMemsetAsync(c->h, 0, sizeof(float) * c->d, c->stream));
+    CK(cudaMemsetAsync(c->ctrl, 0, sizeof(Ctrl), c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    c->host_pos = 0;
+    c->cancelled.store(false);
+  });
+}
+
+SS_API void ss_cuda_scheduler_reset(ss_cuda_ctx_t* ctx) { ss_cuda_reset(ctx); }
+
+SS_API void ss_cuda_cancel(ss_cuda_ctx_t* ctx) {
+  auto* c = reinterpret_cast<Context*>(ctx);
+  if (c) c->cancelled.store(true);
+}
+
+SS_API int ss_cuda_forward(ss_cuda_ctx_t* ctx, const int32_t* token_ids, int32_t n_seq, int32_t pos,
+                           float* logits_out, int32_t* argmax_out) {
+  return guard([&] {
+    Context* c = need_model(ctx);
+    if (!token_ids || n_seq != 1) fail(SS_CUDA_ERROR_INVALID_PARAMS, "n_seq must be 1");
+    put_tokens(c, token_ids, 1, pos);
+    set_position(c, pos, pos + 1);
+    run_steps(c, 1);
+    if (logits_out) {
+      read_logits(c, logits_out);
+    } else {
+      CK(cudaMemcpyAsync(&c->h_small[16], c->seq_tokens + c->ctx, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+      check_device_error(c);
+    }
+    if (argmax_out) *argmax_out = c->h_small[16];
+  });
+}
+
+SS_API int ss_cuda_prefill(ss_cuda_ctx_t* ctx, const int32_t* tokens, int32_t n, int32_t start_pos, float* logits_out) {
+  int tok = -1;
+  const int rc = guard([&] {
+    Context* c = need_model(ctx);
+    if (!tokens || n <= 0) fail(SS_CUDA_ERROR_INVALID_PARAMS, "empty prompt");
+    put_tokens(c, tokens, n, start_pos);
+    set_position(c, start_pos, start_pos + n);
+    run_steps(c, n);
+    read_logits(c, logits_out ? logits_out : nullptr);
+    tok = c->h_small[16];
+  });
+  return rc == SS_CUDA_OK ? tok : rc;
+}
+
+SS_API int ss_cuda_decode_begin(ss_cuda_ctx_t* ctx, int32_t token, int32_t pos) {
+  return guard([&] {
+    Context* c = need_model(ctx);
+    put_tokens(c, &token, 1, pos);
+    set_position(c, pos, pos + 1);
+  });
+}
+
+SS_API int ss_cuda_decode_steps(ss_cuda_ctx_t* ctx, int32_t n_steps) {
+  return guard([&] {
+    Context* c = need_model(ctx);
+    run_steps(c, n_steps);
+  });
+}
+
+SS_API int ss_cuda_decode_read(ss_cuda_ctx_t* ctx, int32_t first_pos, int32_t n, int32_t* ids_out) {
+  return guard([&] {
+    Context* c = need_model(ctx);
+    if (!ids_out || n < 0 || first_pos < 0 || first_pos + n > c->ctx + 1)
+      fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad token range");
+    check_device_error(c);
+    CK(cudaMemcpy(ids_out, c->seq_tokens + first_pos, sizeof(int) * n, cudaMemcpyDeviceToHost));
+  });
+}
+
+SS_API int ss_cuda_decode_greedy(ss_cuda_ctx_t* ctx, int32_t token, int32_t start_pos, int32_t n_steps, int32_t* ids_out) {
+  return guard([&] {
+    Context* c = need_model(ctx);
+    if (!ids_out || n_steps <= 0) fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad arguments");
+    if (start_pos + n_steps >= c->ctx + 1) fail(SS_CUDA_ERROR_INVALID_PARAMS, "decode runs past the context");
+    put_tokens(c, &token, 1, start_pos);
+    set_position(c, start_pos, start_pos + 1);
+    run_steps(c, n_steps);
+    check_device_error(c);
+    // tokens of positions start_pos+1 .. start_pos+n_steps; the last one may sit
+    // at index ctx (the last-argmax slot) when it falls past the context
+    const int in_ctx = std::min(n_steps, c->ctx - 1 - start_pos);
+    if (in_ctx > 0)
+      CK(cudaMemcpy(ids_out, c->seq_tokens + start_pos + 1, sizeof(int) * in_ctx, cudaMemcpyDeviceToHost));
+    if (in_ctx < n_steps)
+      CK(cudaMemcpy(ids_out + in_ctx, c->seq_tokens + c->ctx, sizeof(int), cudaMemcpyDeviceToHost));
+  });
+}
+
+SS_API void* ss_cuda_stream(ss_cuda_ctx_t* ctx) {
+  auto* c = reinterpret_cast<Context*>(ctx);
+  return c ? (void*)c->stream : nullptr;
+}
+
+SS_API int ss_cuda_dequantize_tensor(ss_cuda_ctx_t* ctx, const char* name, float* out, int64_t n) {
+  return guard([&] {
+    Context* c = need_model(ctx);
+    if (!name || !out) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null argument");
+    std::string s(name);
+    const DevMatrix* m = nullptr;
+    int mul = 1, add = 0, rows = 0;
+    const int qd = c->nh * c->hd, kvd = c->nkv * c->hd;
+    if (s == "output.weight") { m = &c->lm_head; rows = c->vocab; }
+    else if (s.rfind("blk.", 0) == 0) {
+      const int l = atoi(s.c_str() + 4);
+      const size_t dot = s.find('.', 4);
+      if (l < 0 || l >= c->L || dot == std::string::npos) fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad tensor %s", name);
+      const std::string suf = s.substr(dot + 1);
+      const Layer& ly = c->layers[(size_t)l];
+      if (suf == "attn_q.weight") { m = &ly.qkv; rows = qd; }
+      else if (suf == "attn_k.weight") { m = &ly.qkv; rows = kvd; add = qd; }
+      else if (suf == "attn_v.weight") { m = &ly.qkv; rows = kvd; add = qd + kvd; }
+      else if (suf == "attn_output.weight") { m = &ly.o; rows = c->d; }
+      else if (suf == "ffn_gate.weight") { m = &ly.gu; rows = c->ff; mul = 2; }
+      else if (suf == "ffn_up.weight") { m = &ly.gu; rows = c->ff; mul = 2; add = 1; }
+      else if (suf == "ffn_down.weight") { m = &ly.down; rows = c->d; }
+    }
+    if (!m) fail(SS_CUDA_ERROR_INVALID_PARAMS, "no quantized tensor %s", name);
+    if (n != (int64_t)rows * m->cols) fail(SS_CUDA_ERROR_INVALID_PARAMS, "n must be rows*cols = %lld", (long long)rows * m->cols);
+    float* d_out = nullptr;
+    CK(cudaMalloc(&d_out, sizeof(float) * (size_t)n));
+    dequant_rows_kernel<<<1024, 256, 0, c->stream>>>(m->data, rows, m->cols, m->type, m->row_stride,
+                                                    m->scale_off, mul, add, d_out);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, d_out, sizeof(float) * (size_t)n, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(d_out);
+    CK(e);
+  });
+}
+
+SS_API int ss_cuda_dequantize(int32_t type, const void* blocks, int64_t n, float* out) {
+  return guard([&] {
+    if (!blocks || !out || n <= 0 || n % 32) fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad arguments");
+    if (type != kQ4_0 && type != kQ8_0) fail(SS_CUDA_ERROR_INVALID_PARAMS, "type %d", type);
+    const size_t in_bytes = (size_t)(n / 32) * ggml_type_size(type);
+    uint8_t* d_in = nullptr;
+    float* d_out = nullptr;
+    CK(cudaMalloc(&d_in, in_bytes));
+    cudaError_t e = cudaMalloc(&d_out, sizeof(float) * (size_t)n);
+    if (e == cudaSuccess) e = cudaMemcpy(d_in, blocks, in_bytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+      dequant_blocks_kernel<<<1024, 256>>>(d_in, n, type, d_out);
+      e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(out, d_out, sizeof(float) * (size_t)n, cudaMemcpyDeviceToHost);
+    cudaFree(d_in);
+    if (d_out) cudaFree(d_out);
+    CK(e);
+  });
+}
+
+SS_API int ss_cuda_time_kernel(ss_cuda_ctx_t* ctx, int32_t which, int32_t iters, float* ms_per_launch) {
+  return guard([&] {
+    Context* c = need_model(ctx);
+    if (which < 0 || which > 5 || iters <= 0 || !ms_per_launch) fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad arguments");
+    cudaEvent_t e0, e1;
+    CK(cudaEventCreate(&e0));
+    CK(cudaEventCreate(&e1));
+    auto one = [&](int i) {
+      const int l = i % c->L;
+      switch (which) {
+        case 0: launch_qkv(c, l, false); break;
+        case 1: launch_attn(c, l, false); break;
+        case 2: launch_o(c, l, false); break;
+        case 3: launch_gu(c, l, false); break;
+        case 4: launch_down(c, l, false); break;
+        default: launch_head(c, false); break;
+      }
+    };
+    for (int i = 0; i < 3; i++) one(i);  // warm-up
+    CK(cudaEventRecord(e0, c->stream));
+    for (int i = 0; i < iters; i++) one(i);
+    CK(cudaEventRecord(e1, c->stream));
+    CK(cudaEventSynchronize(e1));
+    float ms = 0.0f;
+    CK(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    *ms_per_launch = ms / (float)iters;
+    if (which == 5) {  // the lm_head advanced the device position; restore it
+      CK(cudaMemcpyAsync(c->ctrl, &c->host_pos, sizeof(int), cudaMemcpyHostToDevice, c->stream));
+      CK(cudaStreamSynchronize(c->stream));
+    }
+  });
+}
+
+SS_API int64_t ss_cuda_kernel_bytes(const ss_cuda_ctx_t* ctx, int32_t which) {
+  auto* c = reinterpret_cast<const Context*>(ctx);
+  if (!c || !c->has_model) return -1;
+  const Layer& l0 = c->layers[0];
+  switch (which) {
+    case 0: return (int64_t)matrix_bytes(l0.qkv);
+    case 2: return (int64_t)matrix_bytes(l0.o);
+    case 3: return (int64_t)matrix_bytes(l0.gu);
+    case 4: return (int64_t)matrix_bytes(l0.down);
+    case 5: return (int64_t)matrix_bytes(c->lm_head);
+    default: return -1;
+  }
+}
+
+SS_API int ss_cuda_kv_row(ss_cuda_ctx_t* ctx, int32_t layer, int32_t pos, int8_t* k, int8_t* v,
+                          float* k_scale, float* v_scale) {
+  return guard([&] {
+    Context* c = need_model(ctx);
+    if (layer < 0 || layer >= c->L || pos < 0 || pos >= c->ctx || !k || !v || !k_scale || !v_scale)
+      fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad kv_row arguments");
+    const size_t kvd = (size_t)c->nkv * c->hd, vi = (size_t)layer * c->ctx + pos;
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaMemcpy(k, c->kc + vi * kvd, kvd, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(v, c->vc + vi * kvd, kvd, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(k_scale, c->ks + vi, 4, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(v_scale, c->vs + vi, 4, cudaMemcpyDeviceToHost));
+  });
+}

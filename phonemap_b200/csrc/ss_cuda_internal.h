@@ -1,0 +1,129 @@
+// ss_cuda_internal.h -- context state of the CUDA backend (host side).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "attention.cuh"
+#include "gemv.cuh"
+#include "misc_kernels.cuh"
+
+namespace ss {
+
+// A repacked quantized matrix in device memory (layout in gemv.cuh).
+struct DevMatrix {
+  uint8_t* data = nullptr;
+  int rows = 0, cols = 0, row_stride = 0, scale_off = 0, type = 0;
+  QMatrix q() const { return QMatrix{data, rows, cols, row_stride, scale_off, type}; }
+};
+
+// Launch geometry of one GEMV (see gemv.cuh for the work split).
+struct GemvLaunch {
+  const void* fn = nullptr;
+  int threads = 0, ctas = 0, rows_per_cta = 0;
+  size_t smem = 0;
+};
+
+struct Layer {
+  DevMatrix qkv, o, gu, down;  // gu rows interleave gate (even) and up (odd)
+  float* attn_norm = nullptr;
+  float* ffn_norm = nullptr;
+  uint8_t* block = nullptr;    // one allocation holding the four matrices
+};
+
+// Device control block of the decode step.
+struct Ctrl {
+  int pos;          // position processed by the next step
+  int fixed_until;  // positions below this hold caller-provided tokens
+  int err;          // sticky device error bits
+  int pad;
+};
+
+struct OpCacheEntry {
+  DevMatrix m;
+  float* f32 = nullptr;  // F32 matrices stay row-major
+};
+
+struct Context {
+  int device = 0;
+  int sm_count = 0;
+  cudaStream_t stream = nullptr;
+  bool has_model = false;
+  bool use_pdl = true;
+  bool use_graph = true;
+  std::atomic<bool> cancelled{false};
+
+  // model dims
+  int vocab = 0, d = 0, L = 0, nh = 0, nkv = 0, hd = 0, rope_dim = 0, ff = 0, ctx = 0, wtype = 0;
+  int max_batch = 1;
+  float eps = 1e-5f, theta = 10000.0f, attn_scale = 1.0f;
+
+  // weights
+  float* embd = nullptr;
+  float* out_norm = nullptr;
+  DevMatrix lm_head;
+  uint8_t* lm_block = nullptr;
+  std::vector<Layer> layers;
+  size_t weight_bytes = 0;
+
+  // KV cache [L][ctx][kvd] + scales/maxima [L][ctx]
+  int8_t* kc = nullptr;
+  int8_t* vc = nullptr;
+  float* ks = nullptr;
+  float* vs = nullptr;
+  unsigned int* amax_k = nullptr;
+  unsigned int* amax_v = nullptr;
+  size_t kv_bytes = 0;
+
+  // activations / scratch
+  float* h = nullptr;
+  float* qkv = nullptr;
+  float* attn_out = nullptr;
+  float* act = nullptr;
+  float* logits = nullptr;
+  float* part_o = nullptr;
+  float* part_ml = nullptr;
+  unsigned int* attn_cnt = nullptr;
+  unsigned long long* am_part = nullptr;
+  unsigned int* am_cnt = nullptr;
+  int* seq_tokens = nullptr;  // [ctx + 1]; [ctx] = last argmax
+  Ctrl* ctrl = nullptr;
+  float2* rope_tab = nullptr;
+
+  // pinned host staging
+  float* h_logits = nullptr;
+  int* h_small = nullptr;  // 64 ints
+
+  // launch geometry
+  GemvLaunch g_qkv, g_o, g_gu, g_down, g_head;
+  int attn_nsplit = 1, attn_chunk_max = 1;
+  size_t attn_smem = 0;
+  int embed_blocks = 1;
+
+  cudaGraphExec_t step_exec = nullptr;
+  bool graph_pdl = false;
+  int host_pos = 0;  // host shadow of ctrl->pos for bounds checks
+  long long steps_run = 0;
+
+  // op-level (Metal-twin) state
+  std::unordered_map<const void*, OpCacheEntry> op_cache;
+  struct BatchSlot {
+    float* d_x = nullptr;
+    float* d_out = nullptr;
+    size_t x_cap = 0, out_cap = 0;
+    float* host_out = nullptr;
+    size_t out_n = 0;
+  };
+  std::vector<BatchSlot> op_slots;
+  bool in_batch = false;
+  int batch_count = 0;
+  uint8_t* op_stage = nullptr;
+  size_t op_stage_cap = 0;
+
+  std::vector<void*> allocations;
+};
+
+}  // namespace ss

@@ -1,0 +1,288 @@
+"""Python binding of the CUDA backend's C ABI (include/slipstream_cuda.h).
+
+``CudaModel`` mirrors the reference's scheduler entry points
+(``ss_scheduler_forward`` / ``ss_scheduler_prefill`` / ``ss_scheduler_reset``,
+SlipStream/src/core/layer_scheduler.h:107-132) and the Metal-shaped op-level
+calls (``ss_metal_matvec_q4_0`` ..., SlipStream/src/backends/metal_backend.h:
+27-70) one to one.  There is no CPU fallback: if the native library is missing
+or the GPU call fails, these functions raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+from . import build
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_i32p = ctypes.POINTER(ctypes.c_int32)
+_i64p = ctypes.POINTER(ctypes.c_int64)
+
+Q4_0, Q8_0, F32 = 2, 8, 0
+
+# every symbol include/slipstream_cuda.h declares
+EXPORTED = [
+    "ss_cuda_default_options", "ss_cuda_init", "ss_cuda_init_file", "ss_cuda_free",
+    "ss_cuda_last_error", "ss_cuda_abi_version", "ss_cuda_model_dims", "ss_cuda_stats",
+    "ss_cuda_should_use_gpu", "ss_cuda_matvec", "ss_cuda_matvec_q4_0", "ss_cuda_matvec_q8_0",
+    "ss_cuda_begin_batch", "ss_cuda_end_batch", "ss_cuda_scheduler_forward",
+    "ss_cuda_scheduler_prefill", "ss_cuda_scheduler_reset", "ss_cuda_forward",
+    "ss_cuda_prefill", "ss_cuda_decode_greedy", "ss_cuda_decode_begin", "ss_cuda_decode_steps",
+    "ss_cuda_decode_read", "ss_cuda_stream", "ss_cuda_reset", "ss_cuda_cancel",
+    "ss_cuda_dequantize_tensor", "ss_cuda_dequantize", "ss_cuda_kv_row",
+    "ss_cuda_time_kernel", "ss_cuda_kernel_bytes",
+]
+
+
+class SSCudaError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+
+
+class Options(ctypes.Structure):
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32), ("device", ctypes.c_int32),
+        ("context_size", ctypes.c_uint32), ("max_batch", ctypes.c_uint32),
+        ("hbm_budget_bytes", ctypes.c_uint64), ("flags", ctypes.c_uint32),
+    ]
+
+
+FLAG_NO_PDL = 1
+FLAG_NO_GRAPH = 2
+
+_lib = None
+
+
+def library_path() -> str:
+    return build.CUDA_LIB
+
+
+def load_library() -> ctypes.CDLL:
+    """Load libslipstream_cuda.so; raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = library_path()
+    if not os.path.exists(path):
+        raise ImportError(f"CUDA backend not built: {path} is missing "
+                          "(run `python -m phonemap_b200.build`)")
+    lib = ctypes.CDLL(path)
+    vp = ctypes.c_void_p
+    lib.ss_cuda_default_options.argtypes = [ctypes.POINTER(Options)]
+    lib.ss_cuda_init.argtypes = [vp, ctypes.c_uint64, ctypes.POINTER(Options)]
+    lib.ss_cuda_init.restype = vp
+    lib.ss_cuda_init_file.argtypes = [ctypes.c_char_p, ctypes.POINTER(Options)]
+    lib.ss_cuda_init_file.restype = vp
+    lib.ss_cuda_free.argtypes = [vp]
+    lib.ss_cuda_last_error.restype = ctypes.c_char_p
+    lib.ss_cuda_model_dims.argtypes = [vp, _i32p]
+    lib.ss_cuda_stats.argtypes = [vp, _i64p, ctypes.c_int32]
+    lib.ss_cuda_should_use_gpu.argtypes = [ctypes.c_int32, ctypes.c_int32]
+    lib.ss_cuda_should_use_gpu.restype = ctypes.c_bool
+    for fn in ("ss_cuda_matvec", "ss_cuda_matvec_q4_0", "ss_cuda_matvec_q8_0"):
+        getattr(lib, fn).argtypes = [vp, _f32p, vp, _f32p, ctypes.c_int32, ctypes.c_int32]
+        getattr(lib, fn).restype = ctypes.c_bool
+    for fn in ("ss_cuda_begin_batch", "ss_cuda_end_batch", "ss_cuda_reset",
+               "ss_cuda_scheduler_reset", "ss_cuda_cancel"):
+        getattr(lib, fn).argtypes = [vp]
+    lib.ss_cuda_scheduler_forward.argtypes = [vp, ctypes.c_int32, ctypes.c_int32]
+    lib.ss_cuda_scheduler_forward.restype = _f32p
+    lib.ss_cuda_scheduler_prefill.argtypes = [vp, _i32p, ctypes.c_int32, ctypes.c_int32]
+    lib.ss_cuda_scheduler_prefill.restype = _f32p
+    lib.ss_cuda_forward.argtypes = [vp, _i32p, ctypes.c_int32, ctypes.c_int32, _f32p, _i32p]
+    lib.ss_cuda_prefill.argtypes = [vp, _i32p, ctypes.c_int32, ctypes.c_int32, _f32p]
+    lib.ss_cuda_decode_greedy.argtypes = [vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _i32p]
+    lib.ss_cuda_decode_begin.argtypes = [vp, ctypes.c_int32, ctypes.c_int32]
+    lib.ss_cuda_decode_steps.argtypes = [vp, ctypes.c_int32]
+    lib.ss_cuda_decode_read.argtypes = [vp, ctypes.c_int32, ctypes.c_int32, _i32p]
+    lib.ss_cuda_stream.argtypes = [vp]
+    lib.ss_cuda_stream.restype = vp
+    lib.ss_cuda_dequantize_tensor.argtypes = [vp, ctypes.c_char_p, _f32p, ctypes.c_int64]
+    lib.ss_cuda_dequantize.argtypes = [ctypes.c_int32, vp, ctypes.c_int64, _f32p]
+    lib.ss_cuda_kv_row.argtypes = [vp, ctypes.c_int32, ctypes.c_int32, vp, vp, _f32p, _f32p]
+    lib.ss_cuda_time_kernel.argtypes = [vp, ctypes.c_int32, ctypes.c_int32, _f32p]
+    lib.ss_cuda_kernel_bytes.argtypes = [vp, ctypes.c_int32]
+    lib.ss_cuda_kernel_bytes.restype = ctypes.c_int64
+    _lib = lib
+    return lib
+
+
+def _check(rc: int) -> int:
+    if rc < 0:
+        raise SSCudaError(rc, load_library().ss_cuda_last_error().decode())
+    return rc
+
+
+def _f(a: np.ndarray):
+    return a.ctypes.data_as(_f32p)
+
+
+def _i(a: np.ndarray):
+    return a.ctypes.data_as(_i32p)
+
+
+def default_options(**kw) -> Options:
+    o = Options()
+    load_library().ss_cuda_default_options(ctypes.byref(o))
+    for k, v in kw.items():
+        setattr(o, k, v)
+    return o
+
+
+class CudaModel:
+    """One decode context on one GPU (one sequence)."""
+
+    def __init__(self, gguf_path: str | None, context_size: int = 0, device: int = -1,
+                 flags: int = 0):
+        lib = load_library()
+        self._lib = lib
+        opts = default_options(context_size=context_size, device=device, flags=flags)
+        if gguf_path is None:
+            h = lib.ss_cuda_init(None, 0, ctypes.byref(opts))
+        else:
+            h = lib.ss_cuda_init_file(gguf_path.encode(), ctypes.byref(opts))
+        if not h:
+            raise SSCudaError(-7, lib.ss_cuda_last_error().decode())
+        self._h = ctypes.c_void_p(h)
+        if gguf_path is not None:
+            dims = np.zeros(12, np.int32)
+            _check(lib.ss_cuda_model_dims(self._h, _i(dims)))
+            (self.vocab, self.hidden, self.n_layers, self.n_heads, self.n_kv_heads,
+             self.head_dim, self.ffn, self.ctx, self.rope_dim, self.wtype, self.max_batch,
+             self.device) = (int(v) for v in dims)
+
+    # ---- scheduler-level twins
+    def scheduler_forward(self, token: int, pos: int) -> np.ndarray:
+        p = self._lib.ss_cuda_scheduler_forward(self._h, int(token), int(pos))
+        if not p:
+            raise SSCudaError(-7, self._lib.ss_cuda_last_error().decode())
+        return np.ctypeslib.as_array(p, shape=(self.vocab,)).copy()
+
+    def scheduler_prefill(self, tokens, start_pos: int = 0) -> np.ndarray:
+        t = np.ascontiguousarray(tokens, np.int32)
+        p = self._lib.ss_cuda_scheduler_prefill(self._h, _i(t), len(t), int(start_pos))
+        if not p:
+            raise SSCudaError(-7, self._lib.ss_cuda_last_error().decode())
+        return np.ctypeslib.as_array(p, shape=(self.vocab,)).copy()
+
+    def reset(self) -> None:
+        self._lib.ss_cuda_reset(self._h)
+
+    def cancel(self) -> None:
+        self._lib.ss_cuda_cancel(self._h)
+
+    # ---- coarse entry points
+    def forward(self, token: int, pos: int, logits: np.ndarray | None = None) -> int:
+        t = np.array([token], np.int32)
+        am = np.zeros(1, np.int32)
+        lp = _f(logits) if logits is not None else None
+        _check(self._lib.ss_cuda_forward(self._h, _i(t), 1, int(pos), lp, _i(am)))
+        return int(am[0])
+
+    def prefill(self, tokens, start_pos: int = 0, logits: np.ndarray | None = None) -> int:
+        t = np.ascontiguousarray(tokens, np.int32)
+        lp = _f(logits) if logits is not None else None
+        return _check(self._lib.ss_cuda_prefill(self._h, _i(t), len(t), int(start_pos), lp))
+
+    def decode_greedy(self, token: int, start_pos: int, n_steps: int) -> list[int]:
+        out = np.zeros(n_steps, np.int32)
+        _check(self._lib.ss_cuda_decode_greedy(self._h, int(token), int(start_pos), int(n_steps),
+                                               _i(out)))
+        return [int(v) for v in out]
+
+    def decode_begin(self, token: int, pos: int) -> None:
+        _check(self._lib.ss_cuda_decode_begin(self._h, int(token), int(pos)))
+
+    def decode_steps(self, n: int) -> None:
+        _check(self._lib.ss_cuda_decode_steps(self._h, int(n)))
+
+    def decode_read(self, first_pos: int, n: int) -> list[int]:
+        out = np.zeros(n, np.int32)
+        _check(self._lib.ss_cuda_decode_read(self._h, int(first_pos), int(n), _i(out)))
+        return [int(v) for v in out]
+
+    def greedy(self, prompt, n_steps: int) -> list[int]:
+        """Prefill + greedy decode; same convention as oracle._Model.greedy."""
+        first = self.prefill(prompt, 0)
+        if n_steps <= 1:
+            return [first][:n_steps]
+        return [first] + self.decode_greedy(first, len(prompt), n_steps - 1)
+
+    def stream(self) -> int:
+        return int(self._lib.ss_cuda_stream(self._h) or 0)
+
+    def stats(self) -> dict:
+        v = np.zeros(8, np.int64)
+        _check(self._lib.ss_cuda_stats(self._h, v.ctypes.data_as(_i64p), 8))
+        keys = ("kernels_per_step", "weight_bytes", "kv_bytes", "attn_splits", "pdl",
+                "steps_run", "qkv_ctas", "down_ctas")
+        return {k: int(x) for k, x in zip(keys, v)}
+
+    KERNELS = {"qkv": 0, "attention": 1, "o": 2, "gate_up": 3, "down": 4, "lm_head": 5}
+
+    def time_kernel(self, which: str, iters: int) -> float:
+        """Average ms per isolated launch of one step kernel (clobbers state)."""
+        ms = np.zeros(1, np.float32)
+        _check(self._lib.ss_cuda_time_kernel(self._h, self.KERNELS[which], int(iters), _f(ms)))
+        return float(ms[0])
+
+    def kernel_bytes(self, which: str) -> int:
+        return int(self._lib.ss_cuda_kernel_bytes(self._h, self.KERNELS[which]))
+
+    # ---- inspection
+    def dequantize_tensor(self, name: str, rows: int, cols: int) -> np.ndarray:
+        out = np.empty(rows * cols, np.float32)
+        _check(self._lib.ss_cuda_dequantize_tensor(self._h, name.encode(), _f(out), out.size))
+        return out.reshape(rows, cols)
+
+    def kv_row(self, layer: int, pos: int):
+        kvd = self.n_kv_heads * self.head_dim
+        k = np.empty(kvd, np.int8)
+        v = np.empty(kvd, np.int8)
+        ks = np.zeros(1, np.float32)
+        vs = np.zeros(1, np.float32)
+        _check(self._lib.ss_cuda_kv_row(self._h, layer, pos, k.ctypes.data, v.ctypes.data,
+                                        _f(ks), _f(vs)))
+        return k, v, float(ks[0]), float(vs[0])
+
+    # ---- op-level twins of the Metal calls
+    def matvec(self, w_bytes: np.ndarray, x: np.ndarray, rows: int, cols: int, wtype: int) -> np.ndarray:
+        out = np.empty(rows, np.float32)
+        xx = np.ascontiguousarray(x, np.float32)
+        fn = {Q4_0: self._lib.ss_cuda_matvec_q4_0, Q8_0: self._lib.ss_cuda_matvec_q8_0,
+              F32: self._lib.ss_cuda_matvec}[wtype]
+        if not fn(self._h, _f(out), w_bytes.ctypes.data, _f(xx), rows, cols):
+            raise SSCudaError(-7, self._lib.ss_cuda_last_error().decode())
+        return out
+
+    def begin_batch(self) -> None:
+        self._lib.ss_cuda_begin_batch(self._h)
+
+    def end_batch(self) -> None:
+        self._lib.ss_cuda_end_batch(self._h)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._lib.ss_cuda_free(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def dequantize_blocks(wtype: int, blocks: np.ndarray, n: int) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    _check(load_library().ss_cuda_dequantize(wtype, blocks.ctypes.data, n, _f(out)))
+    return out

@@ -1,0 +1,42 @@
+"""The C ABI library loads and exports every entry point include/slipstream_cuda.h
+declares (no GPU calls)."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+from phonemap_b200 import build, runtime
+
+HEADER = os.path.join(build.INCLUDE, "slipstream_cuda.h")
+
+
+def declared_functions() -> list[str]:
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(ss_cuda_\w+)\s*\(", text)))
+
+
+def test_header_and_binding_agree():
+    assert declared_functions() == sorted(runtime.EXPORTED)
+
+
+def test_library_exports_every_declared_symbol():
+    if not os.path.exists(build.CUDA_LIB):
+        build.build_cuda()
+    lib = ctypes.CDLL(build.CUDA_LIB)
+    missing = [f for f in declared_functions() if not hasattr(lib, f)]
+    assert not missing, f"not exported: {missing}"
+    assert lib.ss_cuda_abi_version() == 1
+    lib.ss_cuda_should_use_gpu.restype = ctypes.c_bool
+    assert lib.ss_cuda_should_use_gpu(1, 1)
+
+
+def test_kernels_are_sm100a():
+    """Built for sm_100a only (cubin arch tag)."""
+    import subprocess
+    out = subprocess.run(["cuobjdump", "--list-elf", build.CUDA_LIB], capture_output=True,
+                         text=True)
+    if out.returncode != 0:
+        return
+    assert "sm_100a" in out.stdout
