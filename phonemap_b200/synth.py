@@ -3,7 +3,7 @@
 ``ensure_gguf(cfg)`` returns the path of the GGUF file for a
 ``configs.ModelConfig``, writing it with the native writer
 (``csrc/synth_gguf.c``) the first time.  Files are cached under
-``$SS_GGUF_CACHE`` (default ``<repo>/.gguf_cache``) by a hash of every
+``$SS_GGUF_CACHE`` (default ``$TMPDIR/ss_gguf_cache``) by a hash of every
 parameter that determines their bytes, so the same configuration yields the
 same bytes on every host.
 """
@@ -48,7 +48,7 @@ def _writer():
 
 
 def cache_dir() -> str:
-    d = os.environ.get("SS_GGUF_CACHE") or os.path.join(build.ROOT, ".gguf_cache")
+    d = os.environ.get("SS_GGUF_CACHE") or os.path.join(tempfile.gettempdir(), "ss_gguf_cache")
     os.makedirs(d, exist_ok=True)
     return d
 
