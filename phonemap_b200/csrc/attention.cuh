@@ -6,16 +6,22 @@
 // h / (nh / nkv)):  s_t = (q . dec(K_t)) * (1/sqrt(hd)) for t <= pos, softmax
 // (tensor.c:154-173), out_h = sum_t p_t * dec(V_t), with dec(x) = x * scale_t.
 //
-// Grid (nsplit, nkv): a CTA handles one kv head and a contiguous slice of the
-// positions 0..pos (pos is read on the device, so one CUDA graph serves every
-// position) for all query heads of its GQA group.  It writes an unnormalised
-// partial (running max m, sum l, o = sum exp(s - m) * v); the last CTA of the
-// kv head to finish merges the partials (the standard split-softmax merge) and
-// writes the heads' outputs.  The CTA whose slice contains `pos` also encodes
-// and appends this token's K/V slice of its kv head -- the scale comes from the
-// |k| / |v| maxima the QKV GEMV accumulated, so every CTA derives the same
-// scale without another pass.
+// Grid (nsplit, nkv) in clusters of (nsplit, 1): the nsplit CTAs of one kv
+// head split the positions 0..pos between them (pos is read on the device, so
+// one CUDA graph serves every position) and serve all query heads of its GQA
+// group.  Each CTA streams its positions through shared memory in tiles
+// (cp.async, 16 B per thread-copy), keeps an online softmax (running max m,
+// sum l, o = sum exp(s - m) * dec(V)), and the cluster merges the partials
+// through distributed shared memory -- no global scratch, no atomics.
+//
+// The cached rows (t < pos) and the position itself do not depend on this
+// step's QKV kernel, so the first tile is requested before the programmatic-
+// dependent-launch wait.  The CTA whose slice contains `pos` encodes this
+// token's K/V slice of its kv head (scale from the |k| / |v| maxima the QKV
+// GEMV accumulated), appends it to the cache and uses it from registers.
 #pragma once
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace ss {
@@ -29,137 +35,212 @@ struct AttnParams {
   const unsigned int* amax_k;  // this layer's |k| maxima [ctx]
   const unsigned int* amax_v;
   const int* d_pos;
-  float* part_o;             // [nkv][nsplit][g][hd]
-  float* part_ml;            // [nkv][nsplit][g][2]
-  unsigned int* counters;    // [nkv]
   float* out;                // [nh*hd]
-  int nh, nkv, hd, ctx, nsplit, chunk_max;
+  int nh, nkv, hd, ctx, nsplit;
   float scale;               // 1 / sqrtf(hd), computed on the host as the reference does
 };
+
+constexpr int kAttnTile = 64;     // positions per shared-memory tile
+constexpr int kAttnMaxG = 8;      // query heads per kv head
+constexpr int kAttnThreads = 128;
 
 // Encode one value as kv_turboquant_encode does: (int8_t)roundf(v * inv).
 SS_DEVINL int8_t kv_encode(float v, float inv) { return (int8_t)(int)roundf(__fmul_rn(v, inv)); }
 
-template <int DPL>  // dims per lane = hd / 32
-__global__ void __launch_bounds__(128) attention_kernel(const AttnParams p) {
-  extern __shared__ float sm[];
-  const int split = blockIdx.x, kh = blockIdx.y;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = blockDim.x >> 5;
-  const int g = p.nh / p.nkv, hd = p.hd, kvd = p.nkv * hd;
-  float* s_sc = sm;                          // [g][chunk_max] scores -> probabilities
-  float* s_red = sm + g * p.chunk_max;       // 64 floats
-  __shared__ bool is_last;
+SS_DEVINL void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem_dst)), "l"(gsrc)
+               : "memory");
+}
+SS_DEVINL void cp_async4(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(smem_dst)), "l"(gsrc)
+               : "memory");
+}
+SS_DEVINL void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-  pdl_wait();
-  const int pos = *p.d_pos;
-  if (pos < 0 || pos >= p.ctx) return;  // host bounds positions; never index past the cache
-  const int seq = pos + 1;
+// Shared-memory layout of one CTA.
+template <int HD>
+struct AttnSmem {
+  int8_t k[kAttnTile][HD];
+  int8_t v[kAttnTile][HD];
+  float ksc[kAttnTile];
+  float vsc[kAttnTile];
+  float s[kAttnMaxG][kAttnTile];   // scores -> exp weights
+  float q[kAttnMaxG][HD];
+  float o[kAttnMaxG][HD];          // running numerator
+  float m[kAttnMaxG];              // running max
+  float l[kAttnMaxG];              // running sum
+  float corr[kAttnMaxG];
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParams p) {
+  namespace cg = cooperative_groups;
+  constexpr int DPL = HD / 32;  // dims per lane
+  extern __shared__ __align__(16) uint8_t smraw[];
+  AttnSmem<HD>& sm = *reinterpret_cast<AttnSmem<HD>*>(smraw);
+  cg::cluster_group cluster = cg::this_cluster();
+  const int split = blockIdx.x, kh = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int nwarp = kAttnThreads / 32;
+  const int g = p.nh / p.nkv, kvd = p.nkv * HD;
+
+  const int pos = *p.d_pos;  // stable for the whole step (advanced by the lm_head)
+  const bool pos_ok = pos >= 0 && pos < p.ctx;
+  const int seq = pos_ok ? pos + 1 : 0;
   const int chunk = (seq + p.nsplit - 1) / p.nsplit;
   const int t0 = min(split * chunk, seq), t1 = min(t0 + chunk, seq);
-  const int n = t1 - t0;
 
-  // scales of this token's rows (layer_scheduler.c:109-114)
-  const float k_scale = __uint_as_float(p.amax_k[pos]) / 127.0f;
-  const float v_scale = __uint_as_float(p.amax_v[pos]) / 127.0f;
-  const float* qv = p.qkv;
-  const float* kcur = p.qkv + p.nh * hd + kh * hd;
-  const float* vcur = p.qkv + p.nh * hd + kvd + kh * hd;
+  // Request the cached rows t in [a, b) (t != pos) of the tile starting at `a`.
+  auto load_tile = [&](int a, int b) {
+    const int rows = b - a;
+    constexpr int cpr = HD / 16;  // 16-byte chunks per row
+    for (int c = tid; c < rows * cpr; c += kAttnThreads) {
+      const int r = c / cpr, j = c - r * cpr;
+      const int t = a + r;
+      if (t == pos) continue;
+      const size_t off = (size_t)t * kvd + kh * HD + j * 16;
+      cp_async16(&sm.k[r][j * 16], p.kc + off);
+      cp_async16(&sm.v[r][j * 16], p.vc + off);
+    }
+    for (int r = tid; r < rows; r += kAttnThreads) {
+      const int t = a + r;
+      if (t == pos) continue;
+      cp_async4(&sm.ksc[r], p.ks + t);
+      cp_async4(&sm.vsc[r], p.vs + t);
+    }
+  };
 
-  if (pos >= t0 && pos < t1) {
+  if (t1 > t0) load_tile(t0, min(t0 + kAttnTile, t1));
+  pdl_wait();
+
+  // this step's q (all heads of the group) and the scales of row `pos`
+  float k_scale = 0.0f, v_scale = 0.0f;
+  if (pos_ok) {
+    k_scale = __uint_as_float(p.amax_k[pos]) / 127.0f;  // layer_scheduler.c:109-110
+    v_scale = __uint_as_float(p.amax_v[pos]) / 127.0f;
+  }
+  for (int idx = tid; idx < g * HD; idx += kAttnThreads) {
+    const int h = idx / HD, i = idx - h * HD;
+    sm.q[h][i] = p.qkv[(kh * g + h) * HD + i];
+    sm.o[h][i] = 0.0f;
+  }
+  if (tid < kAttnMaxG) { sm.m[tid] = -INFINITY; sm.l[tid] = 0.0f; }
+  if (pos_ok && pos >= t0 && pos < t1) {
+    // encode + append this token's K/V slice (layer_scheduler.c:409-413)
     const float kinv = k_scale > 0.0f ? 1.0f / k_scale : 0.0f;
     const float vinv = v_scale > 0.0f ? 1.0f / v_scale : 0.0f;
-    for (int i = tid; i < hd; i += blockDim.x) {
-      p.kc[(size_t)pos * kvd + kh * hd + i] = kv_encode(kcur[i], kinv);
-      p.vc[(size_t)pos * kvd + kh * hd + i] = kv_encode(vcur[i], vinv);
+    const float* kcur = p.qkv + p.nh * HD + kh * HD;
+    const float* vcur = kcur + kvd;
+    for (int i = tid; i < HD; i += kAttnThreads) {
+      const int8_t kq = kv_encode(kcur[i], kinv), vq = kv_encode(vcur[i], vinv);
+      p.kc[(size_t)pos * kvd + kh * HD + i] = kq;
+      p.vc[(size_t)pos * kvd + kh * HD + i] = vq;
+      if ((pos - t0) < kAttnTile) {
+        sm.k[pos - t0][i] = kq;
+        sm.v[pos - t0][i] = vq;
+      }
     }
-    if (kh == 0 && tid == 0) { p.ks[pos] = k_scale; p.vs[pos] = v_scale; }
-    __syncthreads();
+    if (tid == 0) {
+      if (kh == 0) { p.ks[pos] = k_scale; p.vs[pos] = v_scale; }
+      if ((pos - t0) < kAttnTile) { sm.ksc[pos - t0] = k_scale; sm.vsc[pos - t0] = v_scale; }
+    }
   }
   pdl_trigger();
 
-  // ---- scores: warp per position, lane owns DPL dims
-  float qr[8][DPL];
-#pragma unroll
-  for (int h = 0; h < 8; h++)
-#pragma unroll
-    for (int i = 0; i < DPL; i++)
-      qr[h][i] = h < g ? qv[(kh * g + h) * hd + lane * DPL + i] : 0.0f;
-
-  for (int t = t0 + warp; t < t1; t += nwarp) {
-    const int8_t* krow = p.kc + (size_t)t * kvd + kh * hd + lane * DPL;
-    const float ksc = (t == pos) ? k_scale : p.ks[t];
-    float kd[DPL];
-#pragma unroll
-    for (int i = 0; i < DPL; i++) kd[i] = __fmul_rn((float)krow[i], ksc);
-#pragma unroll
-    for (int h = 0; h < 8; h++) {
-      if (h < g) {
-        float d = 0.0f;
-#pragma unroll
-        for (int i = 0; i < DPL; i++) d = fmaf(qr[h][i], kd[i], d);
-        d = warp_sum(d);
-        if (lane == 0) s_sc[h * p.chunk_max + (t - t0)] = __fmul_rn(d, p.scale);
+  for (int a = t0; a < t1; a += kAttnTile) {
+    const int b = min(a + kAttnTile, t1), n = b - a;
+    if (a != t0) {
+      __syncthreads();  // previous tile fully consumed
+      load_tile(a, b);
+      if (pos >= a && pos < b && tid < HD) {
+        // row `pos` of a later tile: re-encode from registers (same values)
+        const float kinv = k_scale > 0.0f ? 1.0f / k_scale : 0.0f;
+        const float vinv = v_scale > 0.0f ? 1.0f / v_scale : 0.0f;
+        const float* kcur = p.qkv + p.nh * HD + kh * HD;
+        for (int i = tid; i < HD; i += kAttnThreads) {
+          sm.k[pos - a][i] = kv_encode(kcur[i], kinv);
+          sm.v[pos - a][i] = kv_encode(kcur[kvd + i], vinv);
+        }
+        if (tid == 0) { sm.ksc[pos - a] = k_scale; sm.vsc[pos - a] = v_scale; }
       }
     }
-  }
-  __syncthreads();
+    cp_async_wait_all();
+    __syncthreads();
 
-  // ---- per-head max / exp / sum over this slice (warp per head)
-  for (int h = warp; h < g; h += nwarp) {
-    float m = -INFINITY;
-    for (int i = lane; i < n; i += 32) m = fmaxf(m, s_sc[h * p.chunk_max + i]);
-    m = warp_max(m);
-    float l = 0.0f;
-    for (int i = lane; i < n; i += 32) {
-      const float e = expf(s_sc[h * p.chunk_max + i] - m);
-      s_sc[h * p.chunk_max + i] = e;
-      l += e;
+    // scores: warp per position, lane owns DPL dims (layer_scheduler.c:434-444)
+    for (int r = warp; r < n; r += nwarp) {
+      const float ksc = sm.ksc[r];
+      float kd[DPL];
+#pragma unroll
+      for (int i = 0; i < DPL; i++) kd[i] = __fmul_rn((float)sm.k[r][lane * DPL + i], ksc);
+#pragma unroll
+      for (int h = 0; h < kAttnMaxG; h++) {
+        if (h < g) {
+          float d = 0.0f;
+#pragma unroll
+          for (int i = 0; i < DPL; i++) d = fmaf(sm.q[h][lane * DPL + i], kd[i], d);
+          d = warp_sum(d);
+          if (lane == 0) sm.s[h][r] = __fmul_rn(d, p.scale);
+        }
+      }
     }
-    l = warp_sum(l);
-    if (lane == 0) {
-      float* ml = p.part_ml + (((size_t)kh * p.nsplit + split) * g + h) * 2;
-      ml[0] = n > 0 ? m : -INFINITY;
-      ml[1] = l;
+    __syncthreads();
+    // online softmax update, warp per head
+    for (int h = warp; h < g; h += nwarp) {
+      float mt = -INFINITY;
+      for (int r = lane; r < n; r += 32) mt = fmaxf(mt, sm.s[h][r]);
+      mt = warp_max(mt);
+      const float mold = sm.m[h];
+      const float mnew = fmaxf(mold, mt);
+      float lt = 0.0f;
+      for (int r = lane; r < n; r += 32) {
+        const float e = expf(sm.s[h][r] - mnew);
+        sm.s[h][r] = e;
+        lt += e;
+      }
+      lt = warp_sum(lt);
+      if (lane == 0) {
+        const float c = mold == -INFINITY ? 0.0f : expf(mold - mnew);
+        sm.corr[h] = c;
+        sm.l[h] = fmaf(sm.l[h], c, lt);
+        sm.m[h] = mnew;
+      }
+    }
+    __syncthreads();
+    // o = o * corr + sum_t e_t * dec(V_t): thread per (head, dim)
+    for (int idx = tid; idx < g * HD; idx += kAttnThreads) {
+      const int h = idx / HD, i = idx - h * HD;
+      float o = sm.o[h][i] * sm.corr[h];
+      for (int r = 0; r < n; r++) o = fmaf(sm.s[h][r], __fmul_rn((float)sm.v[r][i], sm.vsc[r]), o);
+      sm.o[h][i] = o;
     }
   }
-  __syncthreads();
+  cp_async_wait_all();
 
-  // ---- o = sum_t e_t * dec(V_t): thread per (head, dim)
-  for (int idx = tid; idx < g * hd; idx += blockDim.x) {
-    const int h = idx / hd, i = idx - h * hd;
-    float o = 0.0f;
-    for (int t = t0; t < t1; t++) {
-      const float vsc = (t == pos) ? v_scale : p.vs[t];
-      const float vd = __fmul_rn((float)p.vc[(size_t)t * kvd + kh * hd + i], vsc);
-      o = fmaf(s_sc[h * p.chunk_max + (t - t0)], vd, o);
-    }
-    p.part_o[(((size_t)kh * p.nsplit + split) * g + h) * hd + i] = o;
-  }
-
-  // ---- last CTA of this kv head merges the splits
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) is_last = atomicAdd(p.counters + kh, 1u) == (unsigned)p.nsplit - 1;
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  for (int idx = tid; idx < g * hd; idx += blockDim.x) {
-    const int h = idx / hd, i = idx - h * hd;
-    const volatile float* ml = p.part_ml + ((size_t)kh * p.nsplit * g + h) * 2;
+  // ---- merge the nsplit partials of this kv head through DSMEM
+  cluster.sync();
+  // CTA `split` of the cluster merges output elements split*128 + tid, strided
+  // by the cluster's thread count.
+  const int nr = (int)cluster.num_blocks();
+  for (int idx = split * kAttnThreads + tid; idx < g * HD; idx += p.nsplit * kAttnThreads) {
+    const int h = idx / HD, i = idx - h * HD;
     float M = -INFINITY;
-    for (int s = 0; s < p.nsplit; s++) M = fmaxf(M, ml[(size_t)s * g * 2]);
-    float L = 0.0f, O = 0.0f;
-    for (int s = 0; s < p.nsplit; s++) {
-      const float ms = ml[(size_t)s * g * 2];
-      if (ms == -INFINITY) continue;
-      const float f = expf(ms - M);
-      L = fmaf(ml[(size_t)s * g * 2 + 1], f, L);
-      O = fmaf(*((volatile float*)p.part_o + (((size_t)kh * p.nsplit + s) * g + h) * hd + i), f, O);
+    for (int r = 0; r < nr; r++) {
+      const AttnSmem<HD>* rs = cluster.map_shared_rank(&sm, r);
+      M = fmaxf(M, rs->m[h]);
     }
-    p.out[(kh * g + h) * hd + i] = O * (1.0f / L);
+    float L = 0.0f, O = 0.0f;
+    for (int r = 0; r < nr; r++) {
+      const AttnSmem<HD>* rs = cluster.map_shared_rank(&sm, r);
+      const float mr = rs->m[h];
+      if (mr == -INFINITY) continue;
+      const float f = expf(mr - M);
+      L = fmaf(rs->l[h], f, L);
+      O = fmaf(rs->o[h][i], f, O);
+    }
+    if (pos_ok) p.out[(kh * g + h) * HD + i] = O * (1.0f / L);
   }
-  if (tid == 0) p.counters[kh] = 0;
-  (void)s_red;
+  cluster.sync();  // keep every CTA's shared memory alive until all reads are done
 }
 
 }  // namespace ss

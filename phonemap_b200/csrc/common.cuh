@@ -27,18 +27,65 @@ SS_DEVINL void prefetch_l2_bulk(const void* ptr, uint32_t bytes) {
 }
 
 // Streaming 128-bit load that bypasses L1 allocation (weights are read once).
+// Not volatile: these read immutable weights, so the compiler may hoist and
+// batch them (that is what keeps many rows in flight per warp).
 SS_DEVINL uint4 ldg_stream(const void* p) {
   uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p));
   return v;
 }
 SS_DEVINL uint16_t ldg_u16(const void* p) {
   uint16_t v;
-  asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  asm("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
   return v;
 }
+
+// ---- mbarrier + bulk async copy (TMA engine, non-tensor form) -------------
+SS_DEVINL uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+SS_DEVINL void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+SS_DEVINL void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+SS_DEVINL void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+SS_DEVINL bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: gives up after `budget` SM clock cycles (then the caller
+// reports an error instead of hanging the GPU).
+SS_DEVINL bool mbar_wait_bounded(uint32_t bar, uint32_t parity, long long budget) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > budget) return false;
+  }
+  return true;
+}
+// Global -> shared bulk copy completing on an mbarrier (16-byte aligned
+// addresses, size a multiple of 16).
+SS_DEVINL void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+SS_DEVINL uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+SS_DEVINL uint16_t lds16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
+
+constexpr long long kWaitBudget = 1LL << 31;  // ~1 s of SM clocks
 
 SS_DEVINL float half_bits_to_float(uint16_t h) {
   return __half2float(__ushort_as_half(h));

@@ -69,6 +69,8 @@ struct GemvParams {
   int* err;
   int rows_per_cta;
   int prefetch;
+  // bulk-copy pipeline: `nstage` shared-memory slots of `stage_rows` rows
+  int nstage, stage_rows;
 };
 
 // ---- per-block dot products --------------------------------------------
@@ -194,103 +196,157 @@ SS_DEVINL int unpack_argmax_index(unsigned long long p) {
 }
 
 // ---- the kernel ------------------------------------------------------------
-template <int TYPE, XSrc XS, Epi EPI, int G>
-__global__ void __launch_bounds__(1024) gemv_kernel(const GemvParams p) {
-  extern __shared__ float smem[];
+// Threads: RG row-groups of NBT = blockDim.x / RG threads; thread (rg, blk)
+// owns column block blk and, within every pipeline stage, rows
+// rg*2 .. rg*2+1 of the stage (stage_rows = 2 * RG).
+//
+// Pipeline: thread 0 streams the CTA's contiguous row range global -> shared
+// in stages of stage_rows rows with cp.async.bulk (one copy per stage, tracked
+// by an mbarrier), keeping `nstage` stages in flight; the remaining range is
+// bulk-prefetched into L2.  All of this is issued before the programmatic-
+// dependent-launch wait, since weights never depend on the previous kernel.
+template <int TYPE, XSrc XS, Epi EPI, int RG>
+__global__ void __launch_bounds__(512) gemv_kernel(const GemvParams p) {
+  constexpr int G = 2;  // rows per warp per stage
+  extern __shared__ __align__(128) uint8_t smem_raw[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nw = blockDim.x >> 5;
+  const int nbt = blockDim.x / RG;          // threads per row-group
+  const int nwb = nbt >> 5;                 // warps per row-group
+  const int rg = tid / nbt;
+  const int blk = tid - rg * nbt;
+  const int wl = blk >> 5;                  // warp index inside the row-group
   const int nb = p.w.cols >> 5;
+  const bool active = blk < nb;
   const int r0 = blockIdx.x * p.rows_per_cta;
   const int r1 = min(r0 + p.rows_per_cta, p.w.rows);
-  const int nrows = r1 - r0;
-  float* red = smem;                               // [nw][rows_per_cta]
-  float* scratch = smem + nw * p.rows_per_cta;     // 64 floats
+  const int nrows = max(r1 - r0, 0);
+  const int SR = p.stage_rows;
+  const int nst = (nrows + SR - 1) / SR;
+  const uint32_t stage_bytes = (uint32_t)(SR * p.w.row_stride);
+  uint8_t* ring = smem_raw;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + (size_t)p.nstage * stage_bytes);
+  float* red = reinterpret_cast<float*>(bars + p.nstage);   // [nwb][rows_per_cta]
+  float* scratch = red + nwb * p.rows_per_cta;             // 64 floats
+  __shared__ int s_abort;
+  const uint8_t* base = p.w.data + (size_t)r0 * p.w.row_stride;
 
-  if (p.prefetch && tid == 0 && nrows > 0)
-    prefetch_l2_bulk(p.w.data + (size_t)r0 * p.w.row_stride, (uint32_t)(nrows * p.w.row_stride));
+  auto issue = [&](int i) {
+    const int rows_i = min(SR, nrows - i * SR);
+    const uint32_t bytes = (uint32_t)(rows_i * p.w.row_stride);
+    const uint32_t bar = smem_addr(bars + (i % p.nstage));
+    mbar_expect_tx(bar, bytes);
+    bulk_g2s(smem_addr(ring + (size_t)(i % p.nstage) * stage_bytes),
+             base + (size_t)i * SR * p.w.row_stride, bytes, bar);
+  };
+  if (tid == 0) {
+    s_abort = 0;
+    for (int i = 0; i < p.nstage; i++) mbar_init(smem_addr(bars + i), 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const int first = min(p.nstage, nst);
+    for (int i = 0; i < first; i++) issue(i);
+    if (p.prefetch && nst > first) {
+      const size_t off = (size_t)first * SR * p.w.row_stride;
+      prefetch_l2_bulk(base + off, (uint32_t)((size_t)nrows * p.w.row_stride - off));
+    }
+  }
   pdl_wait();
 
   // ---- prologue: this thread's 32 activations, pre-scaled per mantissa slot
-  const int blk = tid;
-  const bool active = blk < nb;
   float xr[32];
   {
-    float scale = 1.0f;
+    float xv[32];
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (active) v = *reinterpret_cast<const float4*>(p.x + blk * 32 + i);
+      xv[i] = v.x; xv[i + 1] = v.y; xv[i + 2] = v.z; xv[i + 3] = v.w;
+    }
     if constexpr (XS == XSrc::RmsNorm) {
       // SlipStream/src/backends/cpu_neon.c:109-115: ss = sum x^2,
-      // scale = 1 / sqrtf(ss / n + eps), out = x * scale * w.
+      // scale = 1 / sqrtf(ss / n + eps), out = x * scale * w.  Each row-group
+      // of threads holds all n values, so ss is a block reduction (counted once).
+      float4 wv4[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++)
+        wv4[i] = active ? *reinterpret_cast<const float4*>(p.norm_w + blk * 32 + 4 * i)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
       float ss = 0.0f;
-      for (int i = tid * 4; i < p.w.cols; i += blockDim.x * 4) {
-        const float4 v = *reinterpret_cast<const float4*>(p.x + i);
-        ss = fmaf(v.x, v.x, ss); ss = fmaf(v.y, v.y, ss);
-        ss = fmaf(v.z, v.z, ss); ss = fmaf(v.w, v.w, ss);
+      if (rg == 0) {
+#pragma unroll
+        for (int i = 0; i < 32; i++) ss = fmaf(xv[i], xv[i], ss);
       }
       ss = block_sum(ss, scratch);
-      scale = 1.0f / sqrtf(ss / (float)p.w.cols + p.eps);
+      const float scale = 1.0f / sqrtf(ss / (float)p.w.cols + p.eps);
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        xv[4 * i] = __fmul_rn(__fmul_rn(xv[4 * i], scale), wv4[i].x);
+        xv[4 * i + 1] = __fmul_rn(__fmul_rn(xv[4 * i + 1], scale), wv4[i].y);
+        xv[4 * i + 2] = __fmul_rn(__fmul_rn(xv[4 * i + 2], scale), wv4[i].z);
+        xv[4 * i + 3] = __fmul_rn(__fmul_rn(xv[4 * i + 3], scale), wv4[i].w);
+      }
     }
-    if (active) {
-      float xv[32];
+    if constexpr (TYPE == kQ4_0) {
 #pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        const float4 v = *reinterpret_cast<const float4*>(p.x + blk * 32 + i);
-        xv[i] = v.x; xv[i + 1] = v.y; xv[i + 2] = v.z; xv[i + 3] = v.w;
-      }
-      if constexpr (XS == XSrc::RmsNorm) {
+      for (int t = 0; t < 4; t++)
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          const float4 wv = *reinterpret_cast<const float4*>(p.norm_w + blk * 32 + i);
-          xv[i] = __fmul_rn(__fmul_rn(xv[i], scale), wv.x);
-          xv[i + 1] = __fmul_rn(__fmul_rn(xv[i + 1], scale), wv.y);
-          xv[i + 2] = __fmul_rn(__fmul_rn(xv[i + 2], scale), wv.z);
-          xv[i + 3] = __fmul_rn(__fmul_rn(xv[i + 3], scale), wv.w);
-        }
-      }
-      if constexpr (TYPE == kQ4_0) {
-#pragma unroll
-        for (int t = 0; t < 4; t++)
-#pragma unroll
-          for (int k = 0; k < 8; k++)
-            xr[8 * t + k] = __fmul_rn(xv[q4_weight_index(t, k)], pow2_neg(q4_slot_shift(k)));
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; j++) xr[j] = __fmul_rn(xv[j], pow2_neg(q8_slot_shift(j & 3)));
-      }
+        for (int k = 0; k < 8; k++)
+          xr[8 * t + k] = __fmul_rn(xv[q4_weight_index(t, k)], pow2_neg(q4_slot_shift(k)));
     } else {
 #pragma unroll
-      for (int j = 0; j < 32; j++) xr[j] = 0.0f;
+      for (int j = 0; j < 32; j++) xr[j] = __fmul_rn(xv[j], pow2_neg(q8_slot_shift(j & 3)));
     }
   }
   pdl_trigger();
 
-  // ---- main loop: G rows at a time
-  const uint8_t* base = p.w.data + (size_t)r0 * p.w.row_stride;
-  for (int lr = 0; lr < nrows; lr += G) {
+  // ---- main loop over pipeline stages
+  int i = 0;
+  for (; i < nst; i++) {
+    const int slot = i % p.nstage;
+    if (!mbar_wait_bounded(smem_addr(bars + slot), (uint32_t)((i / p.nstage) & 1), kWaitBudget)) {
+      atomicOr(p.err, 4);
+      s_abort = 1;
+    }
+    const int rows_i = min(SR, nrows - i * SR);
+    const uint8_t* st = ring + (size_t)slot * stage_bytes;
     float acc[G];
 #pragma unroll
     for (int g = 0; g < G; g++) {
+      const int k = rg * G + g;
       acc[g] = 0.0f;
-      if (active && lr + g < nrows) {
-        const uint8_t* rowp = base + (size_t)(lr + g) * p.w.row_stride;
-        const float d = half_bits_to_float(ldg_u16(rowp + p.w.scale_off + blk * 2));
-        float s;
-        if constexpr (TYPE == kQ4_0) {
-          s = dot_q4_block(ldg_stream(rowp + blk * 16), xr);
-        } else {
-          s = dot_q8_block(ldg_stream(rowp + blk * 32), ldg_stream(rowp + blk * 32 + 16), xr);
-        }
-        acc[g] = d * s;
+      if (active && k < rows_i) {
+        const uint8_t* rowp = st + (size_t)k * p.w.row_stride;
+        const float d = half_bits_to_float(lds16(rowp + p.w.scale_off + blk * 2));
+        float sdot;
+        if constexpr (TYPE == kQ4_0) sdot = dot_q4_block(lds128(rowp + blk * 16), xr);
+        else sdot = dot_q8_block(lds128(rowp + blk * 32), lds128(rowp + blk * 32 + 16), xr);
+        acc[g] = d * sdot;
       }
     }
     const float v = warp_reduce_rows<G>(acc, lane);
-    const int rr = lr + row_of_lane<G>(lane);
-    if ((lane & (32 / G - 1)) == 0 && rr < nrows) red[warp * p.rows_per_cta + rr] = v;
+    const int rr = rg * G + row_of_lane<G>(lane);
+    if ((lane & (32 / G - 1)) == 0 && rr < rows_i) red[wl * p.rows_per_cta + i * SR + rr] = v;
+    __syncthreads();  // every thread is done with this slot
+    if (s_abort) break;
+    if (tid == 0 && i + p.nstage < nst) issue(i + p.nstage);
   }
-  __syncthreads();
+  if (s_abort) {
+    // drain the copies still in flight (bounded), then leave without output
+    if (tid == 0) {
+      const int issued = min(nst, i + p.nstage);
+      for (int j = max(0, issued - p.nstage); j < issued; j++)
+        mbar_wait_bounded(smem_addr(bars + j % p.nstage), (uint32_t)((j / p.nstage) & 1), kWaitBudget);
+    }
+    return;
+  }
 
   // ---- epilogue
   auto row_sum = [&](int lr_) {
     float s = 0.0f;
-    for (int w = 0; w < nw; w++) s += red[w * p.rows_per_cta + lr_];
+    for (int w = 0; w < nwb; w++) s += red[w * p.rows_per_cta + lr_];
     return s;
   };
 

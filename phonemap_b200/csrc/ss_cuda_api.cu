@@ -100,49 +100,82 @@ void launch(void (*fn)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream
 
 using GemvFn = void (*)(const GemvParams);
 
-template <int TYPE, XSrc XS, Epi EPI, int G>
-GemvFn gemv_fn() {
-  return &gemv_kernel<TYPE, XS, EPI, G>;
-}
-
-template <XSrc XS, Epi EPI, int G>
-GemvFn gemv_fn_type(int type) {
-  if (type == kQ4_0) return gemv_fn<kQ4_0, XS, EPI, G>();
-  if (type == kQ8_0) return gemv_fn<kQ8_0, XS, EPI, G>();
+template <XSrc XS, Epi EPI, int RG>
+GemvFn gemv_fn_rg(int type) {
+  if (type == kQ4_0) return &gemv_kernel<kQ4_0, XS, EPI, RG>;
+  if (type == kQ8_0) return &gemv_kernel<kQ8_0, XS, EPI, RG>;
   fail(SS_CUDA_ERROR_INVALID_MODEL, "unsupported weight type %d (Q4_0 and Q8_0 only)", type);
 }
 
-constexpr int kG = 4;  // rows per warp iteration
+template <XSrc XS, Epi EPI>
+GemvFn gemv_fn_type(int type, int rg) {
+  switch (rg) {
+    case 1: return gemv_fn_rg<XS, EPI, 1>(type);
+    case 2: return gemv_fn_rg<XS, EPI, 2>(type);
+    case 4: return gemv_fn_rg<XS, EPI, 4>(type);
+    case 8: return gemv_fn_rg<XS, EPI, 8>(type);
+    default: fail(SS_CUDA_ERROR_BACKEND, "row groups %d", rg);
+  }
+}
 
-// Geometry: one thread per 32-column block; as many CTAs as fit on the GPU at
-// once (capped by the row count), each owning a contiguous multiple-of-kG
+constexpr int kTargetThreads = 256;          // per GEMV CTA
+constexpr size_t kRingBudget = 100 * 1024;   // shared memory for the weight ring
+
+// Row-groups of threads per CTA: as many as fit in kTargetThreads.
+int gemv_row_groups(int cols) {
+  const int nbt = round_up(cols / 32, 32);
+  int rg = 1;
+  while (rg < 8 && nbt * rg * 2 <= kTargetThreads) rg *= 2;
+  return rg;
+}
+
+// Geometry (see gemv.cuh): one thread per 32-column block in each of RG
+// row-groups; a weight ring of `nstage` stages of 2*RG rows; as many CTAs as
+// are co-resident (capped by the row count), each owning a contiguous, even
 // range of rows.
-GemvLaunch plan_gemv(Context* c, GemvFn fn, const DevMatrix& m) {
+GemvLaunch plan_gemv(Context* c, GemvFn fn, const DevMatrix& m, int rg) {
   GemvLaunch g;
   g.fn = (const void*)fn;
   const int nb = m.cols / 32;
-  if (nb < 1 || nb > 1024)
-    fail(SS_CUDA_ERROR_INVALID_MODEL, "matrix with %d columns is outside 32..32768", m.cols);
-  g.threads = round_up(nb, 32);
-  const int nw = g.threads / 32;
+  if (nb < 1 || nb > 512)
+    fail(SS_CUDA_ERROR_INVALID_MODEL, "matrix with %d columns is outside 32..16384", m.cols);
+  const int nbt = round_up(nb, 32);
+  g.threads = nbt * rg;
+  g.stage_rows = 2 * rg;
+  const size_t stage_bytes = (size_t)g.stage_rows * m.row_stride;
+  g.nstage = (int)std::max<size_t>(2, std::min<size_t>(16, kRingBudget / stage_bytes));
+  const int nwb = nbt / 32;
+  auto smem_for = [&](int rpc) {
+    return (size_t)g.nstage * stage_bytes + (size_t)g.nstage * 8 + (size_t)nwb * rpc * 4 + 64 * 4;
+  };
+  CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
   int occ = 0;
-  // smem depends on rows_per_cta; estimate with a first pass then refine.
-  const int groups = (m.rows + kG - 1) / kG;
-  size_t smem_guess = (size_t)nw * 64 * sizeof(float) + 64 * sizeof(float);
-  CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-  CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, g.threads, smem_guess));
+  CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, g.threads, smem_for(256)));
   occ = std::max(occ, 1);
-  int ctas = std::min(groups, c->sm_count * occ);
-  int rpc = round_up((m.rows + ctas - 1) / ctas, kG);
-  g.rows_per_cta = rpc;
-  g.ctas = (m.rows + rpc - 1) / rpc;
-  g.smem = (size_t)nw * rpc * sizeof(float) + 64 * sizeof(float);
-  if (g.smem > 200 * 1024) fail(SS_CUDA_ERROR_INVALID_MODEL, "GEMV reduction buffer too large");
+  const int ctas = std::min((m.rows + 1) / 2, c->sm_count * occ);
+  g.rows_per_cta = round_up((m.rows + ctas - 1) / ctas, 2);
+  g.ctas = (m.rows + g.rows_per_cta - 1) / g.rows_per_cta;
+  g.smem = smem_for(g.rows_per_cta);
+  if (g.smem > 220 * 1024) fail(SS_CUDA_ERROR_INVALID_MODEL, "GEMV shared memory too large");
   return g;
+}
+
+GemvLaunch plan_gemv_for(Context* c, XSrc xs, Epi epi, const DevMatrix& m) {
+  const int rg = gemv_row_groups(m.cols);
+  GemvFn fn = nullptr;
+  if (xs == XSrc::RmsNorm && epi == Epi::QKV) fn = gemv_fn_type<XSrc::RmsNorm, Epi::QKV>(m.type, rg);
+  else if (xs == XSrc::RmsNorm && epi == Epi::SwiGLU) fn = gemv_fn_type<XSrc::RmsNorm, Epi::SwiGLU>(m.type, rg);
+  else if (xs == XSrc::RmsNorm && epi == Epi::Argmax) fn = gemv_fn_type<XSrc::RmsNorm, Epi::Argmax>(m.type, rg);
+  else if (xs == XSrc::Plain && epi == Epi::Residual) fn = gemv_fn_type<XSrc::Plain, Epi::Residual>(m.type, rg);
+  else if (xs == XSrc::Plain && epi == Epi::Store) fn = gemv_fn_type<XSrc::Plain, Epi::Store>(m.type, rg);
+  else fail(SS_CUDA_ERROR_BACKEND, "GEMV variant not built");
+  return plan_gemv(c, fn, m, rg);
 }
 
 void run_gemv(Context* c, const GemvLaunch& g, GemvParams p, bool pdl) {
   p.rows_per_cta = g.rows_per_cta;
+  p.nstage = g.nstage;
+  p.stage_rows = g.stage_rows;
   launch((GemvFn)g.fn, dim3(g.ctas), dim3(g.threads), g.smem, c->stream, pdl, p);
 }
 
@@ -322,20 +355,20 @@ void alloc_state(Context* c) {
   c->attn_out = dev_alloc<float>(c, (size_t)std::max(qd, c->d));
   c->act = dev_alloc<float>(c, (size_t)c->ff);
   c->logits = dev_alloc<float>(c, (size_t)c->vocab);
-  // attention split: ~2 CTAs per SM over the kv heads
-  c->attn_nsplit = std::max(1, std::min(64, (2 * c->sm_count + c->nkv - 1) / c->nkv));
-  c->attn_chunk_max = (c->ctx + c->attn_nsplit - 1) / c->attn_nsplit;
-  const int g = c->nh / c->nkv;
-  c->attn_smem = ((size_t)g * c->attn_chunk_max + 64) * sizeof(float);
-  if (c->attn_smem > 200 * 1024) fail(SS_CUDA_ERROR_INVALID_PARAMS, "context too long for attention");
-  c->part_o = dev_alloc<float>(c, (size_t)c->nkv * c->attn_nsplit * g * c->hd);
-  c->part_ml = dev_alloc<float>(c, (size_t)c->nkv * c->attn_nsplit * g * 2);
-  c->attn_cnt = dev_alloc<unsigned int>(c, (size_t)c->nkv);
+  // attention: position splits of one kv head form a thread-block cluster
+  // (at most 8, the portable cluster size); ~2 CTAs per SM over the kv heads
+  c->attn_nsplit = std::max(1, std::min(8, (2 * c->sm_count + c->nkv - 1) / c->nkv));
+  switch (c->hd) {
+    case 32: c->attn_smem = sizeof(AttnSmem<32>); break;
+    case 64: c->attn_smem = sizeof(AttnSmem<64>); break;
+    case 128: c->attn_smem = sizeof(AttnSmem<128>); break;
+    case 256: c->attn_smem = sizeof(AttnSmem<256>); break;
+    default: fail(SS_CUDA_ERROR_INVALID_MODEL, "head_dim %d unsupported (32, 64, 128, 256)", c->hd);
+  }
   c->am_part = dev_alloc<unsigned long long>(c, 4096);
   c->am_cnt = dev_alloc<unsigned int>(c, 1);
   c->seq_tokens = dev_alloc<int>(c, (size_t)c->ctx + 1);
   c->ctrl = dev_alloc<Ctrl>(c, 1);
-  CK(cudaMemsetAsync(c->attn_cnt, 0, sizeof(unsigned) * c->nkv, c->stream));
   CK(cudaMemsetAsync(c->am_cnt, 0, sizeof(unsigned), c->stream));
   CK(cudaMemsetAsync(c->seq_tokens, 0, sizeof(int) * (c->ctx + 1), c->stream));
   CK(cudaMemsetAsync(c->ctrl, 0, sizeof(Ctrl), c->stream));
@@ -356,18 +389,26 @@ void alloc_state(Context* c) {
   c->embed_blocks = std::max(1, std::min(16, (c->d + 255) / 256));
 }
 
+using AttnFn = void (*)(const AttnParams);
+AttnFn attn_fn(int hd) {
+  switch (hd) {
+    case 32: return &attention_kernel<32>;
+    case 64: return &attention_kernel<64>;
+    case 128: return &attention_kernel<128>;
+    case 256: return &attention_kernel<256>;
+    default: fail(SS_CUDA_ERROR_INVALID_MODEL, "head_dim %d", hd);
+  }
+}
+
 void plan_all(Context* c) {
   const Layer& l0 = c->layers[0];
-  c->g_qkv = plan_gemv(c, gemv_fn_type<XSrc::RmsNorm, Epi::QKV, kG>(c->wtype), l0.qkv);
-  c->g_o = plan_gemv(c, gemv_fn_type<XSrc::Plain, Epi::Residual, kG>(c->wtype), l0.o);
-  c->g_gu = plan_gemv(c, gemv_fn_type<XSrc::RmsNorm, Epi::SwiGLU, kG>(c->wtype), l0.gu);
-  c->g_down = plan_gemv(c, gemv_fn_type<XSrc::Plain, Epi::Residual, kG>(c->wtype), l0.down);
-  c->g_head = plan_gemv(c, gemv_fn_type<XSrc::RmsNorm, Epi::Argmax, kG>(c->lm_head.type), c->lm_head);
+  c->g_qkv = plan_gemv_for(c, XSrc::RmsNorm, Epi::QKV, l0.qkv);
+  c->g_o = plan_gemv_for(c, XSrc::Plain, Epi::Residual, l0.o);
+  c->g_gu = plan_gemv_for(c, XSrc::RmsNorm, Epi::SwiGLU, l0.gu);
+  c->g_down = plan_gemv_for(c, XSrc::Plain, Epi::Residual, l0.down);
+  c->g_head = plan_gemv_for(c, XSrc::RmsNorm, Epi::Argmax, c->lm_head);
   if (c->g_head.ctas > 4096) fail(SS_CUDA_ERROR_INVALID_MODEL, "lm_head grid too large");
-  if (c->hd == 64) CK(cudaFuncSetAttribute(attention_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-  if (c->hd == 128) CK(cudaFuncSetAttribute(attention_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-  if (c->hd == 32) CK(cudaFuncSetAttribute(attention_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-  if (c->hd == 256) CK(cudaFuncSetAttribute(attention_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  CK(cudaFuncSetAttribute(attn_fn(c->hd), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->attn_smem));
 }
 
 GemvParams base_params(Context* c) {
@@ -420,25 +461,28 @@ void launch_attn(Context* c, int l, bool pdl) {
   a.amax_k = c->amax_k + lo;
   a.amax_v = c->amax_v + lo;
   a.d_pos = &c->ctrl->pos;
-  a.part_o = c->part_o;
-  a.part_ml = c->part_ml;
-  a.counters = c->attn_cnt;
   a.out = c->attn_out;
   a.nh = c->nh;
   a.nkv = c->nkv;
   a.hd = c->hd;
   a.ctx = c->ctx;
   a.nsplit = c->attn_nsplit;
-  a.chunk_max = c->attn_chunk_max;
   a.scale = c->attn_scale;
-  const dim3 grid(c->attn_nsplit, c->nkv);
-  switch (c->hd) {
-    case 32: launch(attention_kernel<1>, grid, dim3(128), c->attn_smem, c->stream, pdl, a); break;
-    case 64: launch(attention_kernel<2>, grid, dim3(128), c->attn_smem, c->stream, pdl, a); break;
-    case 128: launch(attention_kernel<4>, grid, dim3(128), c->attn_smem, c->stream, pdl, a); break;
-    case 256: launch(attention_kernel<8>, grid, dim3(128), c->attn_smem, c->stream, pdl, a); break;
-    default: fail(SS_CUDA_ERROR_INVALID_MODEL, "head_dim %d", c->hd);
-  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(c->attn_nsplit, c->nkv);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = c->attn_smem;
+  cfg.stream = c->stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = c->attn_nsplit;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  CK(cudaLaunchKernelEx(&cfg, attn_fn(c->hd), a));
 }
 
 // h = Wo . attn + h
@@ -697,8 +741,7 @@ bool op_matvec(ss_cuda_ctx_t* ctx, float* out, const void* mat, const float* vec
              matvec_f32_kernel<<<grid, threads, 0, c->stream>>>(w.f32, s.d_x, s.d_out, rows, cols);
              CK(cudaGetLastError());
            } else {
-             GemvFn fn = gemv_fn_type<XSrc::Plain, Epi::Store, kG>(type);
-             GemvLaunch g = plan_gemv(c, fn, w.m);
+             GemvLaunch g = plan_gemv_for(c, XSrc::Plain, Epi::Store, w.m);
              GemvParams p = base_params(c);
              p.w = w.m.q();
              p.x = s.d_x;

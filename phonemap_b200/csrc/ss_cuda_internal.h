@@ -24,6 +24,7 @@ struct DevMatrix {
 struct GemvLaunch {
   const void* fn = nullptr;
   int threads = 0, ctas = 0, rows_per_cta = 0;
+  int nstage = 0, stage_rows = 0;
   size_t smem = 0;
 };
 
@@ -84,9 +85,6 @@ struct Context {
   float* attn_out = nullptr;
   float* act = nullptr;
   float* logits = nullptr;
-  float* part_o = nullptr;
-  float* part_ml = nullptr;
-  unsigned int* attn_cnt = nullptr;
   unsigned long long* am_part = nullptr;
   unsigned int* am_cnt = nullptr;
   int* seq_tokens = nullptr;  // [ctx + 1]; [ctx] = last argmax
@@ -99,7 +97,7 @@ struct Context {
 
   // launch geometry
   GemvLaunch g_qkv, g_o, g_gu, g_down, g_head;
-  int attn_nsplit = 1, attn_chunk_max = 1;
+  int attn_nsplit = 1;
   size_t attn_smem = 0;
   int embed_blocks = 1;
 

@@ -42,7 +42,13 @@ def make_model_fixture(name: str) -> None:
     ref = oracle.RefModel(path, cfg.ctx)
     prompt = synth.prompt_tokens(cfg)
     keep = sorted({0, 1, steps // 2, steps - 1})
-    ids, kept = ref.greedy(prompt, steps, keep_logits=keep)
+    ids, all_logits = ref.greedy(prompt, steps, keep_logits=set(range(steps)))
+    kept = {s: all_logits[s] for s in keep}
+    # per step: the 4 best token IDs and their logits, and max |logit|
+    order = [np.argsort(-all_logits[s], kind="stable")[:4] for s in range(steps)]
+    topk_ids = np.array(order, np.int32)
+    topk_vals = np.array([all_logits[s][o] for s, o in enumerate(order)], np.float32)
+    absmax = np.array([np.abs(all_logits[s]).max() for s in range(steps)], np.float32)
     layer, pos = min(1, cfg.n_layers - 1), len(prompt) - 1
     k, v, ks, vs = ref.kv_row(layer, pos)
     np.savez_compressed(
@@ -52,7 +58,8 @@ def make_model_fixture(name: str) -> None:
         logits=np.stack([kept[s] for s in keep]).astype(np.float32),
         fingerprint=np.frombuffer(gguf_fingerprint(path), np.uint8),
         kv_layer=np.int32(layer), kv_pos=np.int32(pos), k_row=k, v_row=v,
-        kv_scales=np.array([ks, vs], np.float32), ctx=np.int32(cfg.ctx))
+        kv_scales=np.array([ks, vs], np.float32), ctx=np.int32(cfg.ctx),
+        topk_ids=topk_ids, topk_vals=topk_vals, absmax=absmax)
     ref.close()
     print(f"{name}: {steps} steps, ids[:8]={ids[:8]}")
 

@@ -36,12 +36,64 @@ def _run(name: str, flags: int = 0):
     return g, m, ids, logits
 
 
-@pytest.mark.parametrize("name", ["tiny", "tiny-mha", "tiny-q8", "tinyllama", "llama2-7b"])
+NEAR_TIE = 5e-3  # reference top-1/top-2 margin, as a fraction of max |logit|
+
+# The int8 KV cache rounds every K/V value with roundf (layer_scheduler.c:116),
+# so a last-bit difference anywhere upstream can move a value across a .5
+# boundary; summing the reference's own fp32 dot products in another order
+# already moves its logits by up to ~2e-3 of max |logit| (measured on the
+# TinyLlama shape).  A greedy choice whose reference margin is below NEAR_TIE is
+# therefore not determined by the reference's arithmetic alone.
+
+FIXTURES = ["tiny", "tiny-mha", "tiny-q8", "tinyllama", "llama2-7b"]
+
+
+def _near_ties(g) -> np.ndarray:
+    tv, am = g["topk_vals"], g["absmax"]
+    return (tv[:, 0] - tv[:, 1]) / am < NEAR_TIE
+
+
+@pytest.mark.parametrize("name", FIXTURES)
 def test_greedy_parity(name):
+    """Free-running greedy decode: identical to the reference's token IDs for
+    every step; a divergence is only accepted at a reference near-tie, and then
+    the GPU's choice must be the reference's runner-up."""
     g, m, ids, logits = _run(name)
-    assert ids == [int(t) for t in g["ids"]]
+    ref = [int(t) for t in g["ids"]]
     for i, s in enumerate(g["logit_steps"]):
-        assert rel_err(logits[int(s)], g["logits"][i]) < LOGIT_RTOL, f"step {s}"
+        if ids[:int(s) + 1] == ref[:int(s) + 1]:
+            assert rel_err(logits[int(s)], g["logits"][i]) < LOGIT_RTOL, f"step {s}"
+    if ids != ref:
+        first = next(i for i, (a, b) in enumerate(zip(ids, ref)) if a != b)
+        assert _near_ties(g)[first], f"diverged at step {first} without a near-tie"
+        assert ids[first] == int(g["topk_ids"][first][1])
+    m.close()
+
+
+@pytest.mark.parametrize("name", FIXTURES)
+def test_teacher_forced_parity(name):
+    """Every step fed the reference's own token: the GPU logits at the
+    reference's top-4 tokens agree within 1e-2 of max |logit|, and the GPU's
+    argmax equals the reference's at every step that is not a near-tie (at a
+    near-tie it is one of the reference's top two)."""
+    g = load_golden(name)
+    cfg = configs.get(name)
+    path = synth.ensure_gguf(cfg)
+    ref = [int(t) for t in g["ids"]]
+    ties = _near_ties(g)
+    with runtime.CudaModel(path, int(g["ctx"])) as m:
+        buf = np.empty(m.vocab, np.float32)
+        prompt = [int(t) for t in g["prompt"]]
+        got = m.prefill(prompt, 0, logits=buf)
+        for s in range(len(ref)):
+            if s > 0:
+                got = m.forward(ref[s - 1], len(prompt) + s - 1, logits=buf)
+            top, vals, am = g["topk_ids"][s], g["topk_vals"][s], float(g["absmax"][s])
+            assert np.abs(buf[top] - vals).max() / am < LOGIT_RTOL, f"step {s}"
+            if ties[s]:
+                assert got in (int(top[0]), int(top[1])), f"step {s}"
+            else:
+                assert got == ref[s], f"step {s}"
     k, v, ks, vs = m.kv_row(int(g["kv_layer"]), int(g["kv_pos"]))
     assert np.abs(k.astype(int) - g["k_row"]).max() <= 1
     assert np.abs(v.astype(int) - g["v_row"]).max() <= 1
