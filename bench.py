@@ -48,6 +48,9 @@ def parse_args():
     ap.add_argument("--config", default="llama2-7b")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--profile-kernel", default=None,
+                    choices=["qkv", "attention", "o", "gate_up", "down", "lm_head"],
+                    help="time one step kernel in isolation instead of the decode loop")
     return ap.parse_args()
 
 
@@ -357,10 +360,32 @@ def run_ours(args):
     return 0
 
 
+def run_profile_kernel(args):
+    """Times one kernel of the decode step in isolation (3 warm-up + --steps
+    launches, cycling through the layers) and prints its bandwidth -- the small
+    case the ncu captures in profiles/ are taken on."""
+    from phonemap_b200 import configs, runtime, synth
+    cfg = configs.get(args.config)
+    path = synth.ensure_gguf(cfg)
+    m = runtime.CudaModel(path, cfg.ctx, device=0)
+    if args.profile_kernel == "attention":  # give it cached positions to attend over
+        m.prefill(synth.prompt_tokens(cfg), 0)
+    ms = m.time_kernel(args.profile_kernel, args.steps)
+    nbytes = m.kernel_bytes(args.profile_kernel)
+    print(json.dumps({"kernel": args.profile_kernel, "config": cfg.name, "launches": args.steps,
+                      "ms_per_launch": round(ms, 5), "device_bytes": nbytes,
+                      "GBps": round(nbytes / (ms / 1000.0) / 1e9, 1) if nbytes > 0 else None,
+                      "stats": m.stats()}), flush=True)
+    m.close()
+    return 0
+
+
 def main():
     args = parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    if args.profile_kernel:
+        return run_profile_kernel(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

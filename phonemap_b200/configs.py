@@ -90,6 +90,10 @@ CONFIGS: dict[str, ModelConfig] = {
     # Llama-2-70B shape, GQA 64/8
     "llama2-70b": ModelConfig("llama2-70b", 80, 8192, 64, 8, 28672, 32000, 2048,
                               prompt=256, decode=128),
+    # profiling: Llama-2-7B layer shapes, 2 layers (< 1 GB on the device), for
+    # small-case ncu captures of the same kernels
+    "llama2-7b-2l": ModelConfig("llama2-7b-2l", 2, 4096, 32, 32, 11008, 32000, 2048,
+                                prompt=128, decode=256),
     # parity-test shapes (oracle finishes in seconds)
     "tiny": ModelConfig("tiny", 2, 256, 8, 2, 512, 512, 128, norm_jitter=0.1,
                         prompt=8, decode=24, seed=7),

@@ -25,11 +25,16 @@
 // programmatic-dependent-launch wait so the weight stream overlaps the tail of
 // the previous kernel.
 //
-// Dequantisation without int->float conversion: a nibble/byte masked into the
-// mantissa of 2^23 (bit pattern 0x4B000000 | q << s) is the float 2^23 + q*2^s;
-// subtracting the constant 2^23 + zero_point*2^s leaves 2^s * (q - zp) exactly.
-// The 2^s factor is cancelled by pre-scaling the matching activation by 2^-s
-// (exact), so each product equals (q - zp) * x bit for bit.
+// Inner product in exact integer arithmetic: each thread converts its 32
+// activations once per CTA to block fixed point -- m_j = round(x_j * 2^(22-e))
+// with 2^e > max |x_j| of the block, so x_j = m_j * 2^(e-22) to 23 bits -- and
+// splits m_j into three signed base-256 digits (byte planes).  A row's block
+// then costs dp4a instructions only: sum_j (q_j - zp) * m_j =
+// sum_p 256^p * sum_j q_j * s_pj  -  zp * sum_j m_j, exact in int32, with the
+// zero-point term folded into the accumulators' initial values.  Three int->float
+// conversions and two fused multiply-adds combine the planes; the fp16 scale d
+// and 2^(e-22) scale the result.  Q4_0: 8 weights per SHF + 2 LOP3 + 6 dp4a;
+// Q8_0: 4 weights per 3 dp4a.
 #pragma once
 #include "common.cuh"
 
@@ -74,61 +79,95 @@ struct GemvParams {
 };
 
 // ---- per-block dot products --------------------------------------------
-// Order in which a Q4_0 thread consumes the 8 nibbles of word t of its block,
-// as (index of the weight inside the block, bit offset s of the mantissa slot).
-//   k:     0      1        2       3         4       5        6        7
-//   j:    4t   16+4t     4t+1   17+4t      4t+2   18+4t     4t+3    19+4t
-//   s:     0      4        8      12        16       8       12       16
-// (k = 5..7 come from the word shifted right by 12.)
-SS_DEVINL int q4_weight_index(int t, int k) { return (k & 1 ? 16 : 0) + 4 * t + (k >> 1); }
-SS_DEVINL int q4_slot_shift(int k) {
-  return k == 0 ? 0 : k == 1 ? 4 : k == 2 ? 8 : k == 3 ? 12 : k == 4 ? 16 : k == 5 ? 8 : k == 6 ? 12 : 16;
-}
-// Q8_0 word t holds weights 4t..4t+3; bytes 2,3 come from the word >> 16.
-SS_DEVINL int q8_slot_shift(int i) { return (i & 1) ? 8 : 0; }
+// One thread's 32 activations as block fixed point in three signed byte planes
+// (natural order: word w of plane p holds digits p of weights 4w .. 4w+3).
+struct XPlanes {
+  int pl[3][8];
+  int init[3];  // accumulator start: -zero_point * sum_j s_pj
+  float fb;     // 2^(e-22), the value of one unit of m
+};
 
-constexpr unsigned kMagic = 0x4B000000u;  // 2^23
-SS_DEVINL float pow2_neg(int s) {  // 2^-s, exact
-  return s == 0 ? 1.0f : s == 4 ? 0.0625f : s == 8 ? 0.00390625f : s == 12 ? 0.000244140625f
-                                                                    : 0.0000152587890625f;
+SS_DEVINL float pow2i(int k) { return __int_as_float((k + 127) << 23); }  // 2^k, -126 <= k <= 127
+
+template <int ZP>
+SS_DEVINL XPlanes make_planes(const float (&xv)[32]) {
+  XPlanes xp;
+  float amax = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 32; j++) amax = fmaxf(amax, fabsf(xv[j]));
+  int e = 0;
+  if (amax >= 1e-30f) frexpf(amax, &e);  // amax < 2^e
+  const bool live = amax >= 1e-30f;      // smaller blocks contribute nothing measurable
+  const float sc = live ? pow2i(22 - e) : 0.0f;
+  xp.fb = live ? pow2i(e - 22) : 0.0f;
+  int sum[3] = {0, 0, 0};
+#pragma unroll
+  for (int w = 0; w < 8; w++) {
+    unsigned b0 = 0, b1 = 0, b2 = 0;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int m = __float2int_rn(xv[4 * w + i] * sc);  // |m| <= 2^22
+      const int s0 = ((m + 128) & 255) - 128;
+      const int m1 = (m - s0) >> 8;
+      const int s1 = ((m1 + 128) & 255) - 128;
+      const int s2 = (m1 - s1) >> 8;                   // |s2| <= 64
+      b0 |= (unsigned)(s0 & 255) << (8 * i);
+      b1 |= (unsigned)(s1 & 255) << (8 * i);
+      b2 |= (unsigned)(s2 & 255) << (8 * i);
+      sum[0] += s0; sum[1] += s1; sum[2] += s2;
+    }
+    xp.pl[0][w] = (int)b0;
+    xp.pl[1][w] = (int)b1;
+    xp.pl[2][w] = (int)b2;
+  }
+#pragma unroll
+  for (int p = 0; p < 3; p++) xp.init[p] = -ZP * sum[p];
+  return xp;
 }
 
-// Q4_0: sum_j (q_j - 8) * x_j over one block, 2 accumulation chains.
-SS_DEVINL float dot_q4_block(const uint4 q, const float* __restrict__ xr) {
-  float a0 = 0.0f, a1 = 0.0f;
-  const unsigned w4[4] = {q.x, q.y, q.z, q.w};
+SS_DEVINL int dp4a_us(unsigned a, int b, int c) {  // unsigned bytes . signed bytes
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+SS_DEVINL int dp4a_ss(int a, int b, int c) {
+  int d;
+  asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+SS_DEVINL float combine_planes(int a0, int a1, int a2) {  // |a_p| < 2^24: exact conversions
+  return fmaf((float)a2, 65536.0f, fmaf((float)a1, 256.0f, (float)a0));
+}
+
+// Q4_0 block: sum_j (q_j - 8) * m_j, in units of 2^(e-22).
+SS_DEVINL float dot_q4_block(const uint4 q, const XPlanes& xp) {
+  int a0 = xp.init[0], a1 = xp.init[1], a2 = xp.init[2];
+  const unsigned wq[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
   for (int t = 0; t < 4; t++) {
-    const unsigned w = w4[t];
-    const unsigned u = w >> 12;
-    const float* x = xr + 8 * t;
-    a0 = fmaf(__uint_as_float((w & 0x0000000Fu) | kMagic) - 8388616.0f, x[0], a0);
-    a1 = fmaf(__uint_as_float((w & 0x000000F0u) | kMagic) - 8388736.0f, x[1], a1);
-    a0 = fmaf(__uint_as_float((w & 0x00000F00u) | kMagic) - 8390656.0f, x[2], a0);
-    a1 = fmaf(__uint_as_float((w & 0x0000F000u) | kMagic) - 8421376.0f, x[3], a1);
-    a0 = fmaf(__uint_as_float((w & 0x000F0000u) | kMagic) - 8912896.0f, x[4], a0);
-    a1 = fmaf(__uint_as_float((u & 0x00000F00u) | kMagic) - 8390656.0f, x[5], a1);
-    a0 = fmaf(__uint_as_float((u & 0x0000F000u) | kMagic) - 8421376.0f, x[6], a0);
-    a1 = fmaf(__uint_as_float((u & 0x000F0000u) | kMagic) - 8912896.0f, x[7], a1);
+    const unsigned lo = wq[t] & 0x0F0F0F0Fu;          // q[4t .. 4t+3]
+    const unsigned hi = (wq[t] >> 4) & 0x0F0F0F0Fu;   // q[16+4t .. 16+4t+3]
+    a0 = dp4a_us(lo, xp.pl[0][t], a0);
+    a1 = dp4a_us(lo, xp.pl[1][t], a1);
+    a2 = dp4a_us(lo, xp.pl[2][t], a2);
+    a0 = dp4a_us(hi, xp.pl[0][4 + t], a0);
+    a1 = dp4a_us(hi, xp.pl[1][4 + t], a1);
+    a2 = dp4a_us(hi, xp.pl[2][4 + t], a2);
   }
-  return a0 + a1;
+  return combine_planes(a0, a1, a2);
 }
 
-// Q8_0: sum_j q_j * x_j; bytes are biased by 128 (xor 0x80) to be unsigned.
-SS_DEVINL float dot_q8_block(const uint4 qa, const uint4 qb, const float* __restrict__ xr) {
-  float a0 = 0.0f, a1 = 0.0f;
-  const unsigned w8[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+// Q8_0 block: sum_j q_j * m_j, in units of 2^(e-22).
+SS_DEVINL float dot_q8_block(const uint4 qa, const uint4 qb, const XPlanes& xp) {
+  int a0 = 0, a1 = 0, a2 = 0;
+  const unsigned wq[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
   for (int t = 0; t < 8; t++) {
-    const unsigned v = w8[t] ^ 0x80808080u;
-    const unsigned u = v >> 16;
-    const float* x = xr + 4 * t;
-    a0 = fmaf(__uint_as_float((v & 0x00FFu) | kMagic) - 8388736.0f, x[0], a0);
-    a1 = fmaf(__uint_as_float((v & 0xFF00u) | kMagic) - 8421376.0f, x[1], a1);
-    a0 = fmaf(__uint_as_float((u & 0x00FFu) | kMagic) - 8388736.0f, x[2], a0);
-    a1 = fmaf(__uint_as_float((u & 0xFF00u) | kMagic) - 8421376.0f, x[3], a1);
+    a0 = dp4a_ss((int)wq[t], xp.pl[0][t], a0);
+    a1 = dp4a_ss((int)wq[t], xp.pl[1][t], a1);
+    a2 = dp4a_ss((int)wq[t], xp.pl[2][t], a2);
   }
-  return a0 + a1;
+  return combine_planes(a0, a1, a2);
 }
 
 // ---- warp "transpose" reductions -----------------------------------------
@@ -255,8 +294,8 @@ __global__ void __launch_bounds__(512) gemv_kernel(const GemvParams p) {
   }
   pdl_wait();
 
-  // ---- prologue: this thread's 32 activations, pre-scaled per mantissa slot
-  float xr[32];
+  // ---- prologue: this thread's 32 activations as block fixed-point byte planes
+  XPlanes xp;
   {
     float xv[32];
 #pragma unroll
@@ -289,16 +328,7 @@ __global__ void __launch_bounds__(512) gemv_kernel(const GemvParams p) {
         xv[4 * i + 3] = __fmul_rn(__fmul_rn(xv[4 * i + 3], scale), wv4[i].w);
       }
     }
-    if constexpr (TYPE == kQ4_0) {
-#pragma unroll
-      for (int t = 0; t < 4; t++)
-#pragma unroll
-        for (int k = 0; k < 8; k++)
-          xr[8 * t + k] = __fmul_rn(xv[q4_weight_index(t, k)], pow2_neg(q4_slot_shift(k)));
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; j++) xr[j] = __fmul_rn(xv[j], pow2_neg(q8_slot_shift(j & 3)));
-    }
+    xp = make_planes<TYPE == kQ4_0 ? 8 : 0>(xv);
   }
   pdl_trigger();
 
@@ -321,9 +351,9 @@ __global__ void __launch_bounds__(512) gemv_kernel(const GemvParams p) {
         const uint8_t* rowp = st + (size_t)k * p.w.row_stride;
         const float d = half_bits_to_float(lds16(rowp + p.w.scale_off + blk * 2));
         float sdot;
-        if constexpr (TYPE == kQ4_0) sdot = dot_q4_block(lds128(rowp + blk * 16), xr);
-        else sdot = dot_q8_block(lds128(rowp + blk * 32), lds128(rowp + blk * 32 + 16), xr);
-        acc[g] = d * sdot;
+        if constexpr (TYPE == kQ4_0) sdot = dot_q4_block(lds128(rowp + blk * 16), xp);
+        else sdot = dot_q8_block(lds128(rowp + blk * 32), lds128(rowp + blk * 32 + 16), xp);
+        acc[g] = sdot * (d * xp.fb);
       }
     }
     const float v = warp_reduce_rows<G>(acc, lane);

@@ -118,14 +118,25 @@ GemvFn gemv_fn_type(int type, int rg) {
   }
 }
 
-constexpr int kTargetThreads = 256;          // per GEMV CTA
-constexpr size_t kRingBudget = 100 * 1024;   // shared memory for the weight ring
+int env_int(const char* name, int dflt) {
+  const char* v = getenv(name);
+  return v && *v ? atoi(v) : dflt;
+}
 
-// Row-groups of threads per CTA: as many as fit in kTargetThreads.
-int gemv_row_groups(int cols) {
+GemvTuning read_tuning() {
+  GemvTuning t;
+  t.target_threads = env_int("SS_GEMV_THREADS", t.target_threads);
+  t.ring_bytes = (size_t)env_int("SS_GEMV_RING_KB", (int)(t.ring_bytes / 1024)) * 1024;
+  t.prefetch = env_int("SS_GEMV_PREFETCH", t.prefetch);
+  t.max_ctas_per_sm = env_int("SS_GEMV_CTAS_PER_SM", t.max_ctas_per_sm);
+  return t;
+}
+
+// Row-groups of threads per CTA: as many as fit in the target thread count.
+int gemv_row_groups(const GemvTuning& tu, int cols) {
   const int nbt = round_up(cols / 32, 32);
   int rg = 1;
-  while (rg < 8 && nbt * rg * 2 <= kTargetThreads) rg *= 2;
+  while (rg < 8 && nbt * rg * 2 <= tu.target_threads) rg *= 2;
   return rg;
 }
 
@@ -134,6 +145,7 @@ int gemv_row_groups(int cols) {
 // are co-resident (capped by the row count), each owning a contiguous, even
 // range of rows.
 GemvLaunch plan_gemv(Context* c, GemvFn fn, const DevMatrix& m, int rg) {
+  const GemvTuning& tu = c->tuning;
   GemvLaunch g;
   g.fn = (const void*)fn;
   const int nb = m.cols / 32;
@@ -143,7 +155,7 @@ GemvLaunch plan_gemv(Context* c, GemvFn fn, const DevMatrix& m, int rg) {
   g.threads = nbt * rg;
   g.stage_rows = 2 * rg;
   const size_t stage_bytes = (size_t)g.stage_rows * m.row_stride;
-  g.nstage = (int)std::max<size_t>(2, std::min<size_t>(16, kRingBudget / stage_bytes));
+  g.nstage = (int)std::max<size_t>(2, std::min<size_t>(16, tu.ring_bytes / stage_bytes));
   const int nwb = nbt / 32;
   auto smem_for = [&](int rpc) {
     return (size_t)g.nstage * stage_bytes + (size_t)g.nstage * 8 + (size_t)nwb * rpc * 4 + 64 * 4;
@@ -152,6 +164,7 @@ GemvLaunch plan_gemv(Context* c, GemvFn fn, const DevMatrix& m, int rg) {
   int occ = 0;
   CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, g.threads, smem_for(256)));
   occ = std::max(occ, 1);
+  if (tu.max_ctas_per_sm > 0) occ = std::min(occ, tu.max_ctas_per_sm);
   const int ctas = std::min((m.rows + 1) / 2, c->sm_count * occ);
   g.rows_per_cta = round_up((m.rows + ctas - 1) / ctas, 2);
   g.ctas = (m.rows + g.rows_per_cta - 1) / g.rows_per_cta;
@@ -161,7 +174,7 @@ GemvLaunch plan_gemv(Context* c, GemvFn fn, const DevMatrix& m, int rg) {
 }
 
 GemvLaunch plan_gemv_for(Context* c, XSrc xs, Epi epi, const DevMatrix& m) {
-  const int rg = gemv_row_groups(m.cols);
+  const int rg = gemv_row_groups(c->tuning, m.cols);
   GemvFn fn = nullptr;
   if (xs == XSrc::RmsNorm && epi == Epi::QKV) fn = gemv_fn_type<XSrc::RmsNorm, Epi::QKV>(m.type, rg);
   else if (xs == XSrc::RmsNorm && epi == Epi::SwiGLU) fn = gemv_fn_type<XSrc::RmsNorm, Epi::SwiGLU>(m.type, rg);
@@ -417,7 +430,7 @@ GemvParams base_params(Context* c) {
   p.d_pos = &c->ctrl->pos;
   p.ctx = c->ctx;
   p.err = &c->ctrl->err;
-  p.prefetch = 1;
+  p.prefetch = c->tuning.prefetch;
   return p;
 }
 
@@ -645,6 +658,7 @@ Context* create(const uint8_t* base, uint64_t size, const ss_cuda_options_t* o) 
   c->max_batch = (int)opts.max_batch;
   c->use_pdl = !(opts.flags & SS_CUDA_FLAG_NO_PDL) && !getenv("SS_CUDA_NO_PDL");
   c->use_graph = !(opts.flags & SS_CUDA_FLAG_NO_GRAPH);
+  c->tuning = read_tuning();
   try {
     CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     if (base) {

@@ -48,6 +48,15 @@ struct OpCacheEntry {
   float* f32 = nullptr;  // F32 matrices stay row-major
 };
 
+// GEMV geometry knobs (defaults measured on B200; the SS_GEMV_* environment
+// variables override them at context creation, for tuning sweeps).
+struct GemvTuning {
+  int target_threads = 256;        // threads per CTA
+  size_t ring_bytes = 100 * 1024;  // shared memory for the weight ring
+  int prefetch = 1;                // bulk L2 prefetch of the rest of the CTA's rows
+  int max_ctas_per_sm = 0;         // 0 = as many as are co-resident
+};
+
 struct Context {
   int device = 0;
   int sm_count = 0;
@@ -55,6 +64,7 @@ struct Context {
   bool has_model = false;
   bool use_pdl = true;
   bool use_graph = true;
+  GemvTuning tuning;
   std::atomic<bool> cancelled{false};
 
   // model dims

@@ -125,6 +125,41 @@ def test_op_matvec_shapes(rows, cols, t):
     assert np.all(np.abs(got.astype(np.float64) - want) <= 2e-6 * scale + 1e-30)
 
 
+@pytest.mark.parametrize("t", [Q4, Q8])
+def test_op_matvec_extreme_activations(t):
+    """Activations the block fixed-point conversion must survive: all-zero
+    blocks, one dominant element per block, values down to 1e-20, mixed signs,
+    exact powers of two.  Bound: each activation is represented to 2^-23 of its
+    block's max |x|, the integer dot is exact, then two fp32 roundings."""
+    rows, cols = 64, 1024
+    rng = np.random.default_rng(99 + t)
+    nb = rows * cols // 32
+    bsz = 18 if t == Q4 else 34
+    blocks = rng.integers(0, 256, size=(nb, bsz), dtype=np.uint8)
+    blocks[:, 0:2] = (rng.standard_normal(nb) * 0.01).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    raw = np.ascontiguousarray(blocks.reshape(-1))
+    x = rng.standard_normal(cols).astype(np.float32)
+    x[0:32] = 0.0                                   # empty block
+    x[32:64] = 1e-6 * x[32:64]
+    x[40] = 300.0                                   # one dominant element
+    x[64:96] = np.float32(2.0) ** rng.integers(-30, 30, 32).astype(np.float32)
+    x[96:128] = 1e-20 * x[96:128]                   # tiny block
+    x[128:160] = -x[128:160] * 1e4
+    ops = oracle.oracle_ops()
+    import ctypes
+    F = ctypes.POINTER(ctypes.c_float)
+    deq = np.empty(rows * cols, np.float32)
+    ops.sso_dequantize(raw.ctypes.data, deq.ctypes.data_as(F), rows * cols, t)
+    w = deq.reshape(rows, cols).astype(np.float64)
+    xd = x.astype(np.float64)
+    exact = w.dot(xd)
+    blockmax = np.repeat(np.abs(xd).reshape(-1, 32).max(1), 32)
+    bound = 2.0 ** -22 * np.abs(w).dot(blockmax) + 2e-7 * np.abs(w).dot(np.abs(xd)) + 1e-30
+    with runtime.CudaModel(None) as m:
+        got = m.matvec(raw, x, rows, cols, t).astype(np.float64)
+    assert np.all(np.abs(got - exact) <= bound)
+
+
 def test_op_batch_brackets():
     """begin/end batch (twins of ss_metal_begin/end_batch): outputs land at
     end_batch and equal the unbatched results."""
