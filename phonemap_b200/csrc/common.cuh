@@ -67,6 +67,7 @@ SS_DEVINL bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // Bounded wait: gives up after `budget` SM clock cycles (then the caller
 // reports an error instead of hanging the GPU).
 SS_DEVINL bool mbar_wait_bounded(uint32_t bar, uint32_t parity, long long budget) {
+  if (mbar_try_wait(bar, parity)) return true;  // common case: no clock read
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
     if (clock64() - t0 > budget) return false;

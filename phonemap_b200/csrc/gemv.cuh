@@ -84,10 +84,23 @@ struct GemvParams {
 struct XPlanes {
   int pl[3][8];
   int init[3];  // accumulator start: -zero_point * sum_j s_pj
-  float fb;     // 2^(e-22), the value of one unit of m
+  float c[3];   // (1, 256, 65536) * 2^(e-22): value of one unit of each plane
 };
 
 SS_DEVINL float pow2i(int k) { return __int_as_float((k + 127) << 23); }  // 2^k, -126 <= k <= 127
+
+SS_DEVINL int sext8(int v) {  // sign-extend the low byte (prmt sign-replicate mode)
+  int r;
+  asm("prmt.b32 %0, %1, 0, 0x8880;" : "=r"(r) : "r"(v));
+  return r;
+}
+SS_DEVINL unsigned pack_low_bytes(int a, int b, int c, int d) {  // a.b0 | b.b0<<8 | c.b0<<16 | d.b0<<24
+  unsigned ab, cd, r;
+  asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(ab) : "r"(a), "r"(b));
+  asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(cd) : "r"(c), "r"(d));
+  asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(r) : "r"(ab), "r"(cd));
+  return r;
+}
 
 template <int ZP>
 SS_DEVINL XPlanes make_planes(const float (&xv)[32]) {
@@ -95,30 +108,38 @@ SS_DEVINL XPlanes make_planes(const float (&xv)[32]) {
   float amax = 0.0f;
 #pragma unroll
   for (int j = 0; j < 32; j++) amax = fmaxf(amax, fabsf(xv[j]));
-  int e = 0;
-  if (amax >= 1e-30f) frexpf(amax, &e);  // amax < 2^e
-  const bool live = amax >= 1e-30f;      // smaller blocks contribute nothing measurable
+  // 2^e > amax: e = unbiased exponent of amax + 1 (blocks below 1e-30
+  // contribute nothing measurable and become zero)
+  const bool live = amax >= 1e-30f;
+  const int e = (int)((__float_as_uint(amax) >> 23) & 255u) - 126;
   const float sc = live ? pow2i(22 - e) : 0.0f;
-  xp.fb = live ? pow2i(e - 22) : 0.0f;
+  xp.c[0] = live ? pow2i(e - 22) : 0.0f;
+  xp.c[1] = live ? pow2i(e - 14) : 0.0f;
+  xp.c[2] = live ? pow2i(e - 6) : 0.0f;
   int sum[3] = {0, 0, 0};
 #pragma unroll
   for (int w = 0; w < 8; w++) {
-    unsigned b0 = 0, b1 = 0, b2 = 0;
+    int d0[4], d1[4], d2[4];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-      const int m = __float2int_rn(xv[4 * w + i] * sc);  // |m| <= 2^22
-      const int s0 = ((m + 128) & 255) - 128;
-      const int m1 = (m - s0) >> 8;
-      const int s1 = ((m1 + 128) & 255) - 128;
-      const int s2 = (m1 - s1) >> 8;                   // |s2| <= 64
-      b0 |= (unsigned)(s0 & 255) << (8 * i);
-      b1 |= (unsigned)(s1 & 255) << (8 * i);
-      b2 |= (unsigned)(s2 & 255) << (8 * i);
-      sum[0] += s0; sum[1] += s1; sum[2] += s2;
+      // balanced base-256 digits of m = round(x * 2^(22-e)), |m| <= 2^22
+      const int m = __float2int_rn(xv[4 * w + i] * sc);
+      d0[i] = sext8(m);
+      const int m1 = (m - d0[i]) >> 8;
+      d1[i] = sext8(m1);
+      d2[i] = (m1 - d1[i]) >> 8;  // |d2| <= 64
     }
-    xp.pl[0][w] = (int)b0;
-    xp.pl[1][w] = (int)b1;
-    xp.pl[2][w] = (int)b2;
+    xp.pl[0][w] = (int)pack_low_bytes(d0[0], d0[1], d0[2], d0[3]);
+    xp.pl[1][w] = (int)pack_low_bytes(d1[0], d1[1], d1[2], d1[3]);
+    xp.pl[2][w] = (int)pack_low_bytes(d2[0], d2[1], d2[2], d2[3]);
+    if (ZP != 0) {
+#pragma unroll
+      for (int p = 0; p < 3; p++) {
+        int acc;
+        asm("dp4a.s32.s32 %0, %1, 0x01010101, %2;" : "=r"(acc) : "r"(xp.pl[p][w]), "r"(sum[p]));
+        sum[p] = acc;
+      }
+    }
   }
 #pragma unroll
   for (int p = 0; p < 3; p++) xp.init[p] = -ZP * sum[p];
@@ -135,13 +156,16 @@ SS_DEVINL int dp4a_ss(int a, int b, int c) {
   asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
   return d;
 }
-SS_DEVINL float combine_planes(int a0, int a1, int a2) {  // |a_p| < 2^24: exact conversions
-  return fmaf((float)a2, 65536.0f, fmaf((float)a1, 256.0f, (float)a0));
+// fb * (a0 + 256 a1 + 65536 a2); |a_p| < 2^24, so the conversions are exact,
+// and c = (fb, 256 fb, 65536 fb) are exact powers-of-two multiples.
+SS_DEVINL float combine_planes(int a0, int a1, int a2, const float (&c)[3]) {
+  return fmaf((float)a2, c[2], fmaf((float)a1, c[1], (float)a0 * c[0]));
 }
 
-// Q4_0 block: sum_j (q_j - 8) * m_j, in units of 2^(e-22).
+// Q4_0 block: sum_j (q_j - 8) * x_j (x in block fixed point).
 SS_DEVINL float dot_q4_block(const uint4 q, const XPlanes& xp) {
-  int a0 = xp.init[0], a1 = xp.init[1], a2 = xp.init[2];
+  // two accumulators per plane (low / high nibbles): 6 independent chains
+  int a0 = xp.init[0], a1 = xp.init[1], a2 = xp.init[2], b0 = 0, b1 = 0, b2 = 0;
   const unsigned wq[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
   for (int t = 0; t < 4; t++) {
@@ -150,24 +174,28 @@ SS_DEVINL float dot_q4_block(const uint4 q, const XPlanes& xp) {
     a0 = dp4a_us(lo, xp.pl[0][t], a0);
     a1 = dp4a_us(lo, xp.pl[1][t], a1);
     a2 = dp4a_us(lo, xp.pl[2][t], a2);
-    a0 = dp4a_us(hi, xp.pl[0][4 + t], a0);
-    a1 = dp4a_us(hi, xp.pl[1][4 + t], a1);
-    a2 = dp4a_us(hi, xp.pl[2][4 + t], a2);
+    b0 = dp4a_us(hi, xp.pl[0][4 + t], b0);
+    b1 = dp4a_us(hi, xp.pl[1][4 + t], b1);
+    b2 = dp4a_us(hi, xp.pl[2][4 + t], b2);
   }
-  return combine_planes(a0, a1, a2);
+  return combine_planes(a0 + b0, a1 + b1, a2 + b2, xp.c);
 }
 
-// Q8_0 block: sum_j q_j * m_j, in units of 2^(e-22).
+// Q8_0 block: sum_j q_j * x_j (x in block fixed point).
 SS_DEVINL float dot_q8_block(const uint4 qa, const uint4 qb, const XPlanes& xp) {
-  int a0 = 0, a1 = 0, a2 = 0;
-  const unsigned wq[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+  int a0 = 0, a1 = 0, a2 = 0, b0 = 0, b1 = 0, b2 = 0;
+  const unsigned wa[4] = {qa.x, qa.y, qa.z, qa.w};
+  const unsigned wb[4] = {qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-  for (int t = 0; t < 8; t++) {
-    a0 = dp4a_ss((int)wq[t], xp.pl[0][t], a0);
-    a1 = dp4a_ss((int)wq[t], xp.pl[1][t], a1);
-    a2 = dp4a_ss((int)wq[t], xp.pl[2][t], a2);
+  for (int t = 0; t < 4; t++) {
+    a0 = dp4a_ss((int)wa[t], xp.pl[0][t], a0);
+    a1 = dp4a_ss((int)wa[t], xp.pl[1][t], a1);
+    a2 = dp4a_ss((int)wa[t], xp.pl[2][t], a2);
+    b0 = dp4a_ss((int)wb[t], xp.pl[0][4 + t], b0);
+    b1 = dp4a_ss((int)wb[t], xp.pl[1][4 + t], b1);
+    b2 = dp4a_ss((int)wb[t], xp.pl[2][4 + t], b2);
   }
-  return combine_planes(a0, a1, a2);
+  return combine_planes(a0 + b0, a1 + b1, a2 + b2, xp.c);
 }
 
 // ---- warp "transpose" reductions -----------------------------------------
@@ -235,28 +263,44 @@ SS_DEVINL int unpack_argmax_index(unsigned long long p) {
 }
 
 // ---- the kernel ------------------------------------------------------------
-// Threads: RG row-groups of NBT = blockDim.x / RG threads; thread (rg, blk)
-// owns column block blk and, within every pipeline stage, rows
-// rg*2 .. rg*2+1 of the stage (stage_rows = 2 * RG).
+// Warp roles: warp 0 is the producer, warps 1.. the consumers.  Consumers form
+// RG row-groups of NBT = nb rounded up to 32 threads; consumer thread
+// (rg, blk) owns column block blk and, in every pipeline stage, rows
+// rg*G .. rg*G+G-1 of the stage (stage_rows = G * RG).
 //
-// Pipeline: thread 0 streams the CTA's contiguous row range global -> shared
-// in stages of stage_rows rows with cp.async.bulk (one copy per stage, tracked
-// by an mbarrier), keeping `nstage` stages in flight; the remaining range is
-// bulk-prefetched into L2.  All of this is issued before the programmatic-
-// dependent-launch wait, since weights never depend on the previous kernel.
+// Pipeline: the producer's lane 0 streams the CTA's contiguous row range
+// global -> shared in stages of stage_rows rows, one cp.async.bulk per stage,
+// through a ring of `nstage` slots.  Each slot has a "full" mbarrier (completed
+// by the copy's byte count) and an "empty" mbarrier (one arrival per consumer
+// warp), so consumer warps run independently of each other and the producer
+// refills a slot as soon as every warp is done with it.  The first `nstage`
+// copies and a bulk L2 prefetch of the rest of the range are issued before the
+// programmatic-dependent-launch wait: weights never depend on the previous
+// kernel.  Every mbarrier wait is bounded; on expiry the kernel records an
+// error bit, drains its copies and returns without writing outputs.
+SS_DEVINL void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+SS_DEVINL void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+constexpr int kGemvG = 4;  // rows per consumer warp per stage
+
 template <int TYPE, XSrc XS, Epi EPI, int RG>
-__global__ void __launch_bounds__(512) gemv_kernel(const GemvParams p) {
-  constexpr int G = 2;  // rows per warp per stage
+__global__ void __launch_bounds__(544) gemv_kernel(const GemvParams p) {
+  constexpr int G = kGemvG;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nw = blockDim.x >> 5;
-  const int nbt = blockDim.x / RG;          // threads per row-group
-  const int nwb = nbt >> 5;                 // warps per row-group
-  const int rg = tid / nbt;
-  const int blk = tid - rg * nbt;
-  const int wl = blk >> 5;                  // warp index inside the row-group
+  const int ncw = nw - 1;                   // consumer warps
+  const int nwb = ncw / RG;                 // consumer warps per row-group
+  const int cw = warp - 1;                  // consumer warp index (-1: producer)
+  const int rg = cw >= 0 ? cw / nwb : 0;
+  const int wl = cw >= 0 ? cw - rg * nwb : 0;
+  const int blk = wl * 32 + lane;
   const int nb = p.w.cols >> 5;
-  const bool active = blk < nb;
+  const bool active = cw >= 0 && blk < nb;
   const int r0 = blockIdx.x * p.rows_per_cta;
   const int r1 = min(r0 + p.rows_per_cta, p.w.rows);
   const int nrows = max(r1 - r0, 0);
@@ -264,114 +308,151 @@ __global__ void __launch_bounds__(512) gemv_kernel(const GemvParams p) {
   const int nst = (nrows + SR - 1) / SR;
   const uint32_t stage_bytes = (uint32_t)(SR * p.w.row_stride);
   uint8_t* ring = smem_raw;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + (size_t)p.nstage * stage_bytes);
-  float* red = reinterpret_cast<float*>(bars + p.nstage);   // [nwb][rows_per_cta]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + (size_t)p.nstage * stage_bytes);
+  uint64_t* empty = full + p.nstage;
+  float* red = reinterpret_cast<float*>(empty + p.nstage);  // [nwb][rows_per_cta]
   float* scratch = red + nwb * p.rows_per_cta;             // 64 floats
   __shared__ int s_abort;
   const uint8_t* base = p.w.data + (size_t)r0 * p.w.row_stride;
 
-  auto issue = [&](int i) {
-    const int rows_i = min(SR, nrows - i * SR);
-    const uint32_t bytes = (uint32_t)(rows_i * p.w.row_stride);
-    const uint32_t bar = smem_addr(bars + (i % p.nstage));
-    mbar_expect_tx(bar, bytes);
-    bulk_g2s(smem_addr(ring + (size_t)(i % p.nstage) * stage_bytes),
-             base + (size_t)i * SR * p.w.row_stride, bytes, bar);
-  };
   if (tid == 0) {
     s_abort = 0;
-    for (int i = 0; i < p.nstage; i++) mbar_init(smem_addr(bars + i), 1);
+    for (int i = 0; i < p.nstage; i++) {
+      mbar_init(smem_addr(full + i), 1);
+      mbar_init(smem_addr(empty + i), (uint32_t)ncw);
+    }
     mbar_fence_init();
   }
   __syncthreads();
-  if (tid == 0) {
-    const int first = min(p.nstage, nst);
-    for (int i = 0; i < first; i++) issue(i);
-    if (p.prefetch && nst > first) {
-      const size_t off = (size_t)first * SR * p.w.row_stride;
-      prefetch_l2_bulk(base + off, (uint32_t)((size_t)nrows * p.w.row_stride - off));
-    }
-  }
-  pdl_wait();
 
-  // ---- prologue: this thread's 32 activations as block fixed-point byte planes
-  XPlanes xp;
-  {
-    float xv[32];
-#pragma unroll
-    for (int i = 0; i < 32; i += 4) {
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (active) v = *reinterpret_cast<const float4*>(p.x + blk * 32 + i);
-      xv[i] = v.x; xv[i + 1] = v.y; xv[i + 2] = v.z; xv[i + 3] = v.w;
-    }
-    if constexpr (XS == XSrc::RmsNorm) {
-      // SlipStream/src/backends/cpu_neon.c:109-115: ss = sum x^2,
-      // scale = 1 / sqrtf(ss / n + eps), out = x * scale * w.  Each row-group
-      // of threads holds all n values, so ss is a block reduction (counted once).
-      float4 wv4[8];
-#pragma unroll
-      for (int i = 0; i < 8; i++)
-        wv4[i] = active ? *reinterpret_cast<const float4*>(p.norm_w + blk * 32 + 4 * i)
-                        : make_float4(0.f, 0.f, 0.f, 0.f);
-      float ss = 0.0f;
-      if (rg == 0) {
-#pragma unroll
-        for (int i = 0; i < 32; i++) ss = fmaf(xv[i], xv[i], ss);
+  if (cw < 0) {
+    // ---------------- producer warp
+    if (lane == 0) {
+      auto issue = [&](int i) {
+        const int rows_i = min(SR, nrows - i * SR);
+        const uint32_t bytes = (uint32_t)(rows_i * p.w.row_stride);
+        const uint32_t bar = smem_addr(full + (i % p.nstage));
+        mbar_expect_tx(bar, bytes);
+        bulk_g2s(smem_addr(ring + (size_t)(i % p.nstage) * stage_bytes),
+                 base + (size_t)i * SR * p.w.row_stride, bytes, bar);
+      };
+      const int first = min(p.nstage, nst);
+      for (int i = 0; i < first; i++) issue(i);
+      if (p.prefetch && nst > first) {
+        const size_t off = (size_t)first * SR * p.w.row_stride;
+        prefetch_l2_bulk(base + off, (uint32_t)((size_t)nrows * p.w.row_stride - off));
       }
-      ss = block_sum(ss, scratch);
-      const float scale = 1.0f / sqrtf(ss / (float)p.w.cols + p.eps);
-#pragma unroll
-      for (int i = 0; i < 8; i++) {
-        xv[4 * i] = __fmul_rn(__fmul_rn(xv[4 * i], scale), wv4[i].x);
-        xv[4 * i + 1] = __fmul_rn(__fmul_rn(xv[4 * i + 1], scale), wv4[i].y);
-        xv[4 * i + 2] = __fmul_rn(__fmul_rn(xv[4 * i + 2], scale), wv4[i].z);
-        xv[4 * i + 3] = __fmul_rn(__fmul_rn(xv[4 * i + 3], scale), wv4[i].w);
+      int i = first;
+      for (; i < nst; i++) {
+        const int slot = i % p.nstage;
+        if (!mbar_wait_bounded(smem_addr(empty + slot), (uint32_t)((i / p.nstage - 1) & 1),
+                               kWaitBudget)) {
+          atomicOr(p.err, 4);
+          s_abort = 1;
+          break;
+        }
+        issue(i);
+      }
+      if (s_abort) {  // drain what is in flight before the CTA can exit
+        for (int j = max(0, i - p.nstage); j < i; j++)
+          mbar_wait_bounded(smem_addr(full + j % p.nstage), (uint32_t)((j / p.nstage) & 1),
+                            kWaitBudget);
       }
     }
-    xp = make_planes<TYPE == kQ4_0 ? 8 : 0>(xv);
-  }
-  pdl_trigger();
-
-  // ---- main loop over pipeline stages
-  int i = 0;
-  for (; i < nst; i++) {
-    const int slot = i % p.nstage;
-    if (!mbar_wait_bounded(smem_addr(bars + slot), (uint32_t)((i / p.nstage) & 1), kWaitBudget)) {
-      atomicOr(p.err, 4);
-      s_abort = 1;
-    }
-    const int rows_i = min(SR, nrows - i * SR);
-    const uint8_t* st = ring + (size_t)slot * stage_bytes;
-    float acc[G];
+  } else {
+    // ---------------- consumer warps
+    pdl_wait();
+    XPlanes xp;
+    {
+      float xv[32];
 #pragma unroll
-    for (int g = 0; g < G; g++) {
-      const int k = rg * G + g;
-      acc[g] = 0.0f;
-      if (active && k < rows_i) {
-        const uint8_t* rowp = st + (size_t)k * p.w.row_stride;
-        const float d = half_bits_to_float(lds16(rowp + p.w.scale_off + blk * 2));
+      for (int i = 0; i < 32; i += 4) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (active) v = *reinterpret_cast<const float4*>(p.x + blk * 32 + i);
+        xv[i] = v.x; xv[i + 1] = v.y; xv[i + 2] = v.z; xv[i + 3] = v.w;
+      }
+      if constexpr (XS == XSrc::RmsNorm) {
+        // SlipStream/src/backends/cpu_neon.c:109-115: ss = sum x^2,
+        // scale = 1 / sqrtf(ss / n + eps), out = x * scale * w.  Row-group 0
+        // holds all n values, so ss is a sum over its threads.
+        float4 wv4[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+          wv4[i] = active ? *reinterpret_cast<const float4*>(p.norm_w + blk * 32 + 4 * i)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        float ss = 0.0f;
+        if (rg == 0) {
+#pragma unroll
+          for (int i = 0; i < 32; i++) ss = fmaf(xv[i], xv[i], ss);
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) scratch[cw] = ss;
+        named_bar_sync(1, ncw * 32);
+        ss = 0.0f;
+        for (int w = 0; w < ncw; w++) ss += scratch[w];
+        const float scale = 1.0f / sqrtf(ss / (float)p.w.cols + p.eps);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          xv[4 * i] = __fmul_rn(__fmul_rn(xv[4 * i], scale), wv4[i].x);
+          xv[4 * i + 1] = __fmul_rn(__fmul_rn(xv[4 * i + 1], scale), wv4[i].y);
+          xv[4 * i + 2] = __fmul_rn(__fmul_rn(xv[4 * i + 2], scale), wv4[i].z);
+          xv[4 * i + 3] = __fmul_rn(__fmul_rn(xv[4 * i + 3], scale), wv4[i].w);
+        }
+      }
+      xp = make_planes<TYPE == kQ4_0 ? 8 : 0>(xv);
+    }
+    pdl_trigger();
+
+    // Per-thread byte offsets inside a slot, fixed for the whole loop.  Rows
+    // past the end of a partial last stage are computed from stale slot bytes
+    // and never stored; lanes past the last block read block 0 and carry zero
+    // activations (xp is zero for them), so neither needs a per-row test.
+    const int bsafe = active ? blk : 0;
+    const uint32_t ring_base = smem_addr(ring);
+    const uint32_t q_off = (uint32_t)((rg * G) * p.w.row_stride + bsafe * (TYPE == kQ4_0 ? 16 : 32));
+    const uint32_t s_off = (uint32_t)((rg * G) * p.w.row_stride + p.w.scale_off + bsafe * 2);
+    const uint32_t rs = (uint32_t)p.w.row_stride;
+    float* red_w = red + wl * p.rows_per_cta + rg * G + row_of_lane<G>(lane);
+    const bool writer = (lane & (32 / G - 1)) == 0;
+    int slot = 0;
+    uint32_t phase = 0;
+    for (int i = 0; i < nst; i++) {
+      if (!mbar_wait_bounded(smem_addr(full + slot), phase, kWaitBudget)) {
+        atomicOr(p.err, 4);
+        s_abort = 1;
+        break;
+      }
+      const uint32_t st = ring_base + (uint32_t)slot * stage_bytes;
+      uint4 qa[G], qb[G];
+      uint16_t sc[G];
+#pragma unroll
+      for (int g = 0; g < G; g++) {
+        const uint32_t rq = st + q_off + (uint32_t)g * rs;
+        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(sc[g]) : "r"(st + s_off + (uint32_t)g * rs));
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(qa[g].x), "=r"(qa[g].y), "=r"(qa[g].z), "=r"(qa[g].w) : "r"(rq));
+        if constexpr (TYPE == kQ8_0)
+          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(qb[g].x), "=r"(qb[g].y), "=r"(qb[g].z), "=r"(qb[g].w) : "r"(rq + 16));
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(empty + slot));  // slot free for the producer
+      float acc[G];
+#pragma unroll
+      for (int g = 0; g < G; g++) {
         float sdot;
-        if constexpr (TYPE == kQ4_0) sdot = dot_q4_block(lds128(rowp + blk * 16), xp);
-        else sdot = dot_q8_block(lds128(rowp + blk * 32), lds128(rowp + blk * 32 + 16), xp);
-        acc[g] = sdot * (d * xp.fb);
+        if constexpr (TYPE == kQ4_0) sdot = dot_q4_block(qa[g], xp);
+        else sdot = dot_q8_block(qa[g], qb[g], xp);
+        acc[g] = sdot * half_bits_to_float(sc[g]);
       }
+      const float v = warp_reduce_rows<G>(acc, lane);
+      const int rr = rg * G + row_of_lane<G>(lane);
+      if (writer && rr < nrows - i * SR) red_w[i * SR] = v;
+      if (++slot == p.nstage) { slot = 0; phase ^= 1u; }
     }
-    const float v = warp_reduce_rows<G>(acc, lane);
-    const int rr = rg * G + row_of_lane<G>(lane);
-    if ((lane & (32 / G - 1)) == 0 && rr < rows_i) red[wl * p.rows_per_cta + i * SR + rr] = v;
-    __syncthreads();  // every thread is done with this slot
-    if (s_abort) break;
-    if (tid == 0 && i + p.nstage < nst) issue(i + p.nstage);
   }
-  if (s_abort) {
-    // drain the copies still in flight (bounded), then leave without output
-    if (tid == 0) {
-      const int issued = min(nst, i + p.nstage);
-      for (int j = max(0, issued - p.nstage); j < issued; j++)
-        mbar_wait_bounded(smem_addr(bars + j % p.nstage), (uint32_t)((j / p.nstage) & 1), kWaitBudget);
-    }
-    return;
-  }
+  __syncthreads();
+  if (s_abort) return;
 
   // ---- epilogue
   auto row_sum = [&](int lr_) {

@@ -136,7 +136,7 @@ GemvTuning read_tuning() {
 int gemv_row_groups(const GemvTuning& tu, int cols) {
   const int nbt = round_up(cols / 32, 32);
   int rg = 1;
-  while (rg < 8 && nbt * rg * 2 <= tu.target_threads) rg *= 2;
+  while (rg < 8 && nbt * rg * 2 <= tu.target_threads) rg *= 2;  // consumer threads
   return rg;
 }
 
@@ -152,13 +152,13 @@ GemvLaunch plan_gemv(Context* c, GemvFn fn, const DevMatrix& m, int rg) {
   if (nb < 1 || nb > 512)
     fail(SS_CUDA_ERROR_INVALID_MODEL, "matrix with %d columns is outside 32..16384", m.cols);
   const int nbt = round_up(nb, 32);
-  g.threads = nbt * rg;
-  g.stage_rows = 2 * rg;
+  g.threads = 32 + nbt * rg;  // producer warp + consumer row-groups
+  g.stage_rows = kGemvG * rg;
   const size_t stage_bytes = (size_t)g.stage_rows * m.row_stride;
   g.nstage = (int)std::max<size_t>(2, std::min<size_t>(16, tu.ring_bytes / stage_bytes));
   const int nwb = nbt / 32;
   auto smem_for = [&](int rpc) {
-    return (size_t)g.nstage * stage_bytes + (size_t)g.nstage * 8 + (size_t)nwb * rpc * 4 + 64 * 4;
+    return (size_t)g.nstage * stage_bytes + (size_t)g.nstage * 16 + (size_t)nwb * rpc * 4 + 64 * 4;
   };
   CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
   int occ = 0;
