@@ -157,6 +157,22 @@ void ss_cuda_reset(ss_cuda_ctx_t *ctx);
  * (ss_cancel, engine.c:372-379). */
 void ss_cuda_cancel(ss_cuda_ctx_t *ctx);
 
+/* ---- allocation-free greedy argmax (no counterpart in the reference) ----
+ * For callers that cannot allocate device memory where they need a greedy
+ * token -- e.g. while a stream is being captured into a CUDA graph, where
+ * cudaMalloc is not allowed, or inside a host that only hands out buffers from
+ * its own pool.  Writes to *d_index (device memory) the index of the first
+ * maximum of d_values[0..n) (device memory), with ss_argmax's tie rule
+ * (SlipStream/src/core/tensor.c:318-328; NaN never wins).  Enqueued on
+ * `stream` (a cudaStream_t, NULL for the legacy default stream) and
+ * asynchronous; calls no cudaMalloc/cudaFree.  n must be 1 .. 4,194,304
+ * (SS_CUDA_ERROR_INVALID_PARAMS otherwise).  Its scratch is a fixed 8 KiB array
+ * in the library's device image, shared by all calls: calls that overlap on
+ * the GPU race, calls ordered on one stream do not.  The first call on each
+ * device looks the array's address up (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture begins. */
+int ss_cuda_argmax_noalloc(const float *d_values, int32_t n, int32_t *d_index, void *stream);
+
 /* ---- inspection (parity tests) ----
  * fp32 dequantisation of an uploaded weight tensor by GGUF name, rows in GGUF
  * order (n = rows * cols floats), computed on the device from the repacked

@@ -25,7 +25,7 @@ INCLUDE = os.path.join(ROOT, "include")
 CUDA_LIB = os.path.join(LIBDIR, "libslipstream_cuda.so")
 SYNTH_LIB = os.path.join(LIBDIR, "libss_synth.so")
 
-CUDA_SOURCES = ["ss_cuda_api.cu"]
+CUDA_SOURCES = ["ss_cuda_api.cu", "noalloc_argmax.cu"]
 CUDA_HEADERS = ["common.cuh", "gemv.cuh", "attention.cuh", "misc_kernels.cuh",
                 "gguf_view.h", "ss_cuda_internal.h"]
 

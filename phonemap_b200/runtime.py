@@ -32,7 +32,7 @@ EXPORTED = [
     "ss_cuda_prefill", "ss_cuda_decode_greedy", "ss_cuda_decode_begin", "ss_cuda_decode_steps",
     "ss_cuda_decode_read", "ss_cuda_stream", "ss_cuda_reset", "ss_cuda_cancel",
     "ss_cuda_dequantize_tensor", "ss_cuda_dequantize", "ss_cuda_kv_row",
-    "ss_cuda_time_kernel", "ss_cuda_kernel_bytes",
+    "ss_cuda_time_kernel", "ss_cuda_kernel_bytes", "ss_cuda_argmax_noalloc",
 ]
 
 
@@ -106,6 +106,7 @@ def load_library() -> ctypes.CDLL:
     lib.ss_cuda_time_kernel.argtypes = [vp, ctypes.c_int32, ctypes.c_int32, _f32p]
     lib.ss_cuda_kernel_bytes.argtypes = [vp, ctypes.c_int32]
     lib.ss_cuda_kernel_bytes.restype = ctypes.c_int64
+    lib.ss_cuda_argmax_noalloc.argtypes = [vp, ctypes.c_int32, vp, vp]
     _lib = lib
     return lib
 
@@ -280,6 +281,13 @@ class CudaModel:
             self.close()
         except Exception:
             pass
+
+
+def argmax_noalloc(d_values: int, n: int, d_index: int, stream: int = 0) -> None:
+    """ss_cuda_argmax_noalloc on device pointers (asynchronous on `stream`)."""
+    _check(load_library().ss_cuda_argmax_noalloc(ctypes.c_void_p(d_values), int(n),
+                                                  ctypes.c_void_p(d_index),
+                                                  ctypes.c_void_p(stream or None)))
 
 
 def dequantize_blocks(wtype: int, blocks: np.ndarray, n: int) -> np.ndarray:
