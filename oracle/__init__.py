@@ -40,15 +40,17 @@ def _ip(a: np.ndarray):
 
 
 def build_oracle(force: bool = False) -> str:
-    """Compile ss_oracle.c (gcc -O2, no -march: every product/sum rounded
-    separately, like the reference's own -O2 build)."""
+    """Compile ss_oracle.c with gcc -O2 like the reference's own build.
+    -ffp-contract=off keeps every product and sum of the reference order
+    separately rounded; -mfma only makes the explicit fmaf() of the blocked
+    order (sso_set_dot_order(1)) a hardware instruction."""
     src = os.path.join(HERE, "ss_oracle.c")
     hdr = os.path.join(HERE, "ss_oracle.h")
     if (force or not os.path.exists(ORACLE_LIB)
             or os.path.getmtime(ORACLE_LIB) < max(os.path.getmtime(src), os.path.getmtime(hdr))):
         os.makedirs(BUILD_DIR, exist_ok=True)
-        subprocess.run(["gcc", "-std=gnu11", "-O2", "-fopenmp", "-fPIC", "-shared", src,
-                        "-o", ORACLE_LIB, "-lm"], check=True)
+        subprocess.run(["gcc", "-std=gnu11", "-O2", "-mfma", "-ffp-contract=off", "-fopenmp",
+                        "-fPIC", "-shared", src, "-o", ORACLE_LIB, "-lm"], check=True)
     return ORACLE_LIB
 
 
@@ -206,6 +208,11 @@ class OracleModel(_Model):
          self.head_dim, self.ffn, self.max_seq) = (int(v) for v in dims)
         self._prefill = lib.sso_prefill
         self._forward = lib.sso_forward
+        lib.sso_set_dot_order.argtypes = [ctypes.c_void_p, ctypes.c_int]
+
+    def set_dot_order(self, mode: int) -> None:
+        """0: the reference's sequential sums; 1: GPU-shaped blocked order."""
+        self._lib.sso_set_dot_order(self._h, int(mode))
 
     def reset(self):
         self._lib.sso_reset(self._h)

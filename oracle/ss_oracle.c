@@ -98,22 +98,63 @@ static float dot_seq(const float *a, const float *b, int32_t n) {
     return s;
 }
 
+/* Summation order of the quantized matvecs.  0 (default) is the reference's:
+ * one sequential fp32 sum per row.  1 is an equally valid reordering of the
+ * same arithmetic -- per 32-weight block a fused multiply-add chain of
+ * (q - zp) * x, scaled by the block's d, accumulated per block index modulo 32
+ * and combined by a 32-way butterfly (the shape of a GPU reduction) -- used to
+ * measure how far the reference's own outputs move under a different fp32
+ * rounding order (the parity noise floor of a configuration). */
+
+static float dot_blocked(const uint8_t *row, const float *x, int32_t cols, int32_t type) {
+    float lane[32] = {0};
+    const size_t bsz = type_size(type);
+    for (int32_t b = 0; b < cols / 32; b++) {
+        const uint8_t *blk = row + (size_t)b * bsz;
+        uint16_t dh;
+        memcpy(&dh, blk, 2);
+        const float d = sso_f16_to_f32(dh);
+        float p = 0.0f;
+        for (int j = 0; j < 32; j++) {
+            float q;
+            if (type == T_Q4_0) q = (float)((j < 16 ? (blk[2 + j] & 15) : (blk[2 + j - 16] >> 4)) - 8);
+            else q = (float)(int8_t)blk[2 + j];
+            p = fmaf(q, x[b * 32 + j], p);
+        }
+        lane[b % 32] = fmaf(d, p, lane[b % 32]);
+    }
+    for (int off = 16; off >= 1; off >>= 1)
+        for (int l = 0; l < off; l++) lane[l] = lane[l] + lane[l + off];
+    return lane[0];
+}
+
 /* SS/src/core/quantize.c:446-494: per row, dequantize into a temp, then
  * vDSP_dotpr(tmp, x).  F32 matrices use ss_matvec -> ss_neon_dot scalar
  * (SS/src/backends/cpu_neon.c:55-62), the same sequential sum. */
-void sso_dequant_matvec(float *out, const void *w, const float *x, int32_t rows,
-                        int32_t cols, int32_t type) {
+static void matvec_ordered(float *out, const void *w, const float *x, int32_t rows,
+                           int32_t cols, int32_t type, int order) {
     size_t row_bytes = (size_t)(cols / block_size(type)) * type_size(type);
+    const int blocked = order == 1 && (type == T_Q4_0 || type == T_Q8_0);
     #pragma omp parallel
     {
         float *tmp = (float *)malloc((size_t)cols * sizeof(float));
         #pragma omp for schedule(static)
         for (int32_t r = 0; r < rows; r++) {
-            sso_dequantize((const uint8_t *)w + (size_t)r * row_bytes, tmp, cols, type);
-            out[r] = dot_seq(tmp, x, cols);
+            const uint8_t *rp = (const uint8_t *)w + (size_t)r * row_bytes;
+            if (blocked) {
+                out[r] = dot_blocked(rp, x, cols, type);
+            } else {
+                sso_dequantize(rp, tmp, cols, type);
+                out[r] = dot_seq(tmp, x, cols);
+            }
         }
         free(tmp);
     }
+}
+
+void sso_dequant_matvec(float *out, const void *w, const float *x, int32_t rows,
+                        int32_t cols, int32_t type) {
+    matvec_ordered(out, w, x, rows, cols, type, 0);
 }
 
 /* SS/src/backends/cpu_neon.c:109-115 (scalar ss_neon_rmsnorm, reached from
@@ -198,7 +239,10 @@ struct sso_model {
     float *ks, *vs;
     /* working state, SS/src/core/layer_scheduler.h:38-65 */
     float *hidden, *residual, *attn_out, *ffn_buf, *ffn_gate, *q, *k, *v, *logits;
+    int dot_order; /* summation order of the quantized matvecs, see matvec_ordered */
 };
+
+void sso_set_dot_order(sso_model_t *m, int mode) { m->dot_order = mode; }
 
 typedef struct { const uint8_t *p, *end; int ok; } rd_t;
 static uint64_t rd_u(rd_t *r, int n) {
@@ -383,8 +427,9 @@ void sso_kv_row(const sso_model_t *m, int32_t layer, int32_t pos, int8_t *k, int
     *vs = m->vs[vi];
 }
 
-static void matvec(float *out, const tref_t *w, const float *x, int32_t rows, int32_t cols) {
-    sso_dequant_matvec(out, w->data, x, rows, cols, w->type);
+static void matvec(const sso_model_t *m, float *out, const tref_t *w, const float *x,
+                   int32_t rows, int32_t cols) {
+    matvec_ordered(out, w->data, x, rows, cols, w->type, m->dot_order);
 }
 
 /* SS/src/core/layer_scheduler.c:291-567 (process_layer, llama branch). */
@@ -393,9 +438,9 @@ static void process_layer(sso_model_t *m, int32_t l, int32_t pos) {
     int32_t d = m->d, hd = m->hd, nh = m->nh, nkv = m->nkv, kvd = m->kvd;
     memcpy(m->residual, m->hidden, (size_t)d * 4);                       /* :325 */
     sso_rmsnorm(m->hidden, m->residual, (const float *)ly->attn_norm.data, d, m->eps);
-    matvec(m->q, &ly->wq, m->hidden, nh * hd, d);                        /* :356-358 */
-    matvec(m->k, &ly->wk, m->hidden, kvd, d);
-    matvec(m->v, &ly->wv, m->hidden, kvd, d);
+    matvec(m, m->q, &ly->wq, m->hidden, nh * hd, d);                        /* :356-358 */
+    matvec(m, m->k, &ly->wk, m->hidden, kvd, d);
+    matvec(m, m->v, &ly->wv, m->hidden, kvd, d);
     sso_rope(m->q, m->k, nh, nkv, hd, m->rope_dim, pos, m->theta);       /* :405 */
     size_t vi = (size_t)l * m->max_seq + pos;                            /* :410-413 */
     sso_kv_encode(m->k, m->kc + vi * kvd, &m->ks[vi], kvd);
@@ -430,17 +475,17 @@ static void process_layer(sso_model_t *m, int32_t l, int32_t pos) {
         free(scores);
         free(tmp);
     }
-    matvec(m->hidden, &ly->wo, m->attn_out, d, nh * hd);                 /* :471-472 */
+    matvec(m, m->hidden, &ly->wo, m->attn_out, d, nh * hd);                 /* :471-472 */
     for (int32_t i = 0; i < d; i++) m->hidden[i] = m->hidden[i] + m->residual[i];  /* :484 */
     memcpy(m->residual, m->hidden, (size_t)d * 4);                       /* :490 */
     sso_rmsnorm(m->hidden, m->residual, (const float *)ly->ffn_norm.data, d, m->eps);
-    matvec(m->ffn_gate, &ly->wgate, m->hidden, m->ff, d);                /* :512-513 */
-    matvec(m->ffn_buf, &ly->wup, m->hidden, m->ff, d);
+    matvec(m, m->ffn_gate, &ly->wgate, m->hidden, m->ff, d);                /* :512-513 */
+    matvec(m, m->ffn_buf, &ly->wup, m->hidden, m->ff, d);
     for (int32_t i = 0; i < m->ff; i++) {                                /* :533-549 */
         float g = m->ffn_gate[i];
         m->ffn_buf[i] *= g / (1.0f + expf(-g));
     }
-    matvec(m->hidden, &ly->wdown, m->ffn_buf, d, m->ff);                 /* :553-554 */
+    matvec(m, m->hidden, &ly->wdown, m->ffn_buf, d, m->ff);                 /* :553-554 */
     for (int32_t i = 0; i < d; i++) m->hidden[i] = m->hidden[i] + m->residual[i];  /* :566 */
 }
 
@@ -453,7 +498,7 @@ static void head(sso_model_t *m, float *logits_out) {                   /* :634-
     if (m->out_norm.data)
         sso_rmsnorm(m->hidden, m->hidden, (const float *)m->out_norm.data, m->d, m->eps);
     const tref_t *lm = m->out.data ? &m->out : &m->embd;
-    matvec(m->logits, lm, m->hidden, m->vocab, m->d);
+    matvec(m, m->logits, lm, m->hidden, m->vocab, m->d);
     if (logits_out) memcpy(logits_out, m->logits, (size_t)m->vocab * 4);
 }
 

@@ -29,6 +29,12 @@ int sso_embed(sso_model_t *m, const int32_t *tokens, int32_t n, float *out);
 void sso_kv_row(const sso_model_t *m, int32_t layer, int32_t pos, int8_t *k, int8_t *v,
                 float *ks, float *vs);
 
+/* Summation order of this model's quantized matvecs: 0 = the reference's
+ * sequential fp32 sum (default), 1 = a GPU-shaped blocked order (per-block FMA
+ * chains, a 32-way butterfly).  Used to measure a configuration's parity noise
+ * floor.  The single-op sso_dequant_matvec always uses order 0. */
+void sso_set_dot_order(sso_model_t *m, int mode);
+
 /* single ops */
 float sso_f16_to_f32(uint16_t h);
 void sso_dequantize(const void *src, float *dst, int32_t n, int32_t type);
