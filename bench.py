@@ -49,8 +49,12 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile-kernel", default=None,
-                    choices=["qkv", "attention", "o", "gate_up", "down", "lm_head"],
-                    help="time one step kernel in isolation instead of the decode loop")
+                    choices=["qkv", "attention", "o", "gate_up", "down", "lm_head", "step"],
+                    help="time one step kernel in isolation instead of the decode loop "
+                         "(qkv..lm_head need --multi-kernel; step = one whole decode step)")
+    ap.add_argument("--multi-kernel", action="store_true",
+                    help="run the step as 2 + 5*layers kernels (CUDA graph) instead of the "
+                         "persistent single kernel")
     return ap.parse_args()
 
 
@@ -249,7 +253,8 @@ def run_ours(args):
         pg.barrier()
     path = synth.ensure_gguf(cfg)
     torch.cuda.set_device(local)
-    m = runtime.CudaModel(path, cfg.ctx, device=local)
+    flags = runtime.FLAG_MULTI_KERNEL if args.multi_kernel else 0
+    m = runtime.CudaModel(path, cfg.ctx, device=local, flags=flags)
     prompt = synth.prompt_tokens(cfg)
     P, W, K = len(prompt), args.warmup, args.steps
     if P + W + K + 1 > cfg.ctx:
@@ -316,15 +321,26 @@ def run_ours(args):
                "h2d_bytes_per_step": 4 + 8, "d2h_bytes_per_step": 4 * m.vocab + 4 + 4,
                "api": "ss_cuda_forward (host token in, host logits + argmax out, synchronous)"}
 
-    # ---- roofline of the dominant kernel (gate/up GEMV: 2*ff*d Q4_0 weights),
-    # timed live: isolated back-to-back launches cycling through the layers
+    # ---- roofline of the dominant kernel.  Persistent step: the one kernel
+    # is the whole step; its algorithmic bytes are the step's (all weights at
+    # the GGUF's bytes per weight + norms + one embedding row + the int8 K/V
+    # read and append at the average timed position), its duration the CUDA-
+    # event time per step above.  Multi-kernel step: the gate/up GEMV (2*ff*d
+    # weights), timed live in isolated back-to-back launches.
     peak, peak_kind = hbm_peak()
-    bpw = 18 / 32 if cfg.wtype == 2 else 34 / 32
-    gu_bytes = 2 * cfg.ffn * cfg.d_model * bpw + cfg.d_model * 4 * 2 + cfg.ffn * 4
-    gu_ms = m.time_kernel("gate_up", 3 * cfg.n_layers)
-    achieved = gu_bytes / (gu_ms / 1000.0) / 1e9
     step_bytes = cfg.token_bytes(P + W + (K - 1) / 2.0)
     step_gbs = step_bytes / (ms_per_step / 1000.0) / 1e9
+    if stats["persistent"]:
+        kernel_name = "decode_step_kernel (persistent: the whole decode step)"
+        k_bytes, k_ms, achieved = step_bytes, ms_per_step, step_gbs
+        traffic = read_profile_traffic("decode_step", cfg.name)
+    else:
+        kernel_name = "gate/up GEMV + RMSNorm + SwiGLU"
+        bpw = 18 / 32 if cfg.wtype == 2 else 34 / 32
+        k_bytes = 2 * cfg.ffn * cfg.d_model * bpw + cfg.d_model * 4 * 2 + cfg.ffn * 4
+        k_ms = m.time_kernel("gate_up", 3 * cfg.n_layers)
+        achieved = k_bytes / (k_ms / 1000.0) / 1e9
+        traffic = read_profile_traffic("gemv_gate_up", cfg.name)
     m.close()
 
     line = None
@@ -335,17 +351,18 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init GGUF, N(0,0.02) quantized)",
             "config": workload(cfg, args),
-            "roofline": {"bound": "hbm", "kernel": "gate/up GEMV + RMSNorm + SwiGLU",
+            "roofline": {"bound": "hbm", "kernel": kernel_name,
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                         "bytes_per_launch": int(gu_bytes), "ms_per_launch": round(gu_ms, 5),
-                         "traffic": read_profile_traffic("gemv_gate_up", cfg.name)},
+                         "bytes_per_launch": int(k_bytes), "ms_per_launch": round(k_ms, 5),
+                         "traffic": traffic},
             "step_roofline": {"bytes_per_step": int(step_bytes), "achieved": round(step_gbs, 1),
                               "frac": round(step_gbs / peak, 4), "unit": "GB/s",
                               "peak_source": peak_kind},
             "e2e": e2e,
             "gpu_launches": int(stats["kernels_per_step"] * K),
             "clocks": sampler.summary(),
+            "step_impl": "persistent single kernel" if stats["persistent"] else "multi-kernel CUDA graph",
             "pdl": bool(stats["pdl"]),
             "first_ids": ids[:8],
         }
@@ -367,8 +384,10 @@ def run_profile_kernel(args):
     from phonemap_b200 import configs, runtime, synth
     cfg = configs.get(args.config)
     path = synth.ensure_gguf(cfg)
-    m = runtime.CudaModel(path, cfg.ctx, device=0)
-    if args.profile_kernel == "attention":  # give it cached positions to attend over
+    per_kernel = args.profile_kernel != "step"
+    flags = runtime.FLAG_MULTI_KERNEL if (per_kernel or args.multi_kernel) else 0
+    m = runtime.CudaModel(path, cfg.ctx, device=0, flags=flags)
+    if args.profile_kernel in ("attention", "step"):  # give it cached positions to attend over
         m.prefill(synth.prompt_tokens(cfg), 0)
     ms = m.time_kernel(args.profile_kernel, args.steps)
     nbytes = m.kernel_bytes(args.profile_kernel)

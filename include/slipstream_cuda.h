@@ -59,6 +59,12 @@ typedef struct {
 
 #define SS_CUDA_FLAG_NO_PDL 1u   /* launch without programmatic dependent launch */
 #define SS_CUDA_FLAG_NO_GRAPH 2u /* launch kernels one by one instead of a CUDA graph */
+/* Run the decode step as 2 + 5 * layers kernels (a CUDA graph) instead of the
+ * default single persistent kernel; also used automatically when a model's
+ * shapes exceed what the persistent kernel supports. */
+#define SS_CUDA_FLAG_MULTI_KERNEL 4u
+/* Record a per-phase timeline of every persistent step (measurement aid). */
+#define SS_CUDA_FLAG_TRACE 8u
 
 /* Fills defaults: device -1, context 0, batch 1, no budget, no flags. */
 void ss_cuda_default_options(ss_cuda_options_t *opts);
@@ -86,19 +92,33 @@ int ss_cuda_model_dims(const ss_cuda_ctx_t *ctx, int32_t *dims);
  * engine.c:291-302): out[0] kernels launched per decode step, [1] device weight
  * bytes, [2] device KV-cache bytes, [3] attention position splits, [4] 1 when
  * the step graph chains kernels with programmatic dependent launch, [5] decode
- * steps run, [6] CTAs of the QKV GEMV, [7] CTAs of the down GEMV. */
+ * steps run, [6] CTAs of the QKV GEMV, [7] CTAs of the down GEMV (both: the
+ * grid of the persistent step), [8] 1 when the step is the single persistent
+ * kernel, [9] its weight-ring slots. */
 int ss_cuda_stats(const ss_cuda_ctx_t *ctx, int64_t *out, int32_t n);
 
 /* Measurement aid, no reference counterpart: times `iters` back-to-back
  * launches (no programmatic overlap) of one kernel of the decode step --
  * which = 0 QKV GEMV, 1 attention, 2 O GEMV, 3 gate/up GEMV, 4 down GEMV,
- * 5 lm_head GEMV -- cycling through the layers so weights stream from HBM, and
- * writes the average milliseconds per launch.  Clobbers the activations and the
- * current position's K/V; call ss_cuda_reset before decoding again. */
+ * 5 lm_head GEMV -- cycling through the layers so weights stream from HBM --
+ * or 6 the whole decode step (steps at the current position onwards), and
+ * writes the average milliseconds per launch.  0..5 exist only in the
+ * multi-kernel step.  Clobbers the activations and the K/V rows it passes
+ * over; call ss_cuda_reset before decoding again. */
 int ss_cuda_time_kernel(ss_cuda_ctx_t *ctx, int32_t which, int32_t iters, float *ms_per_launch);
 /* Device bytes of the weights one launch of kernel `which` streams (layer 0;
- * repacked layout, i.e. the GGUF bytes plus row padding); -1 if not a GEMV. */
+ * repacked layout, i.e. the GGUF bytes plus row padding; 6: every weight
+ * matrix of the step); -1 if not a GEMV. */
 int64_t ss_cuda_kernel_bytes(const ss_cuda_ctx_t *ctx, int32_t which);
+
+/* Measurement aid, no reference counterpart: the timeline of the last
+ * persistent step (context created with SS_CUDA_FLAG_TRACE).  out[n] with
+ * n = (2 + 5 * layers) * grid * 4, indexed [phase][cta][event]; phases are
+ * 0 embedding, then per layer QKV, attention, O, gate/up, down, then lm_head;
+ * events are global-timer nanoseconds: 0 the phase's input ready, 1 the CTA's
+ * matvec rows done, 2 the CTA done with the phase, 3 the CTA's producer issued
+ * the phase's last weight copy (0 where an event does not apply). */
+int ss_cuda_step_trace(ss_cuda_ctx_t* ctx, int64_t* out, int64_t n);
 
 /* ---- op level: twins of ss_metal_should_use_gpu / ss_metal_matvec* ----
  * (metal_backend.h:27-58).  out[rows] = W[rows x cols] . vec[cols] with host

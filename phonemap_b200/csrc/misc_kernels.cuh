@@ -63,6 +63,59 @@ __global__ void repack_kernel(const uint8_t* __restrict__ src, int rows, int col
   }
 }
 
+// GGUF blocks -> tiled layout (step_kernel.cuh): tiles of 4 rows, the rows'
+// quant bytes row-major, then the nb x 4 fp16 scales block-major.  Source row r
+// goes to destination row r * dst_row_mul + dst_row_add.
+__global__ void repack_tiled_kernel(const uint8_t* __restrict__ src, int rows, int cols, int type,
+                                    uint8_t* __restrict__ dst, int tile_bytes, int dst_row_mul,
+                                    int dst_row_add) {
+  const int nb = cols / 32;
+  const int bsz = type == kQ4_0 ? 18 : 34;
+  const int qsz = bsz - 2;
+  const long long total = (long long)rows * nb;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int r = (int)(i / nb), b = (int)(i - (long long)r * nb);
+    const uint8_t* s = src + i * bsz;
+    const int R = r * dst_row_mul + dst_row_add;
+    uint8_t* tile = dst + (size_t)(R >> 2) * tile_bytes;
+    const int ri = R & 3;
+    tile[4 * nb * qsz + b * 8 + ri * 2] = s[0];
+    tile[4 * nb * qsz + b * 8 + ri * 2 + 1] = s[1];
+    uint8_t* q = tile + (size_t)ri * nb * qsz + b * qsz;
+    for (int j = 0; j < qsz; j++) q[j] = s[2 + j];
+  }
+}
+
+// Dequantise rows of a tiled matrix (rows src_row_mul * r + src_row_add).
+__global__ void dequant_tiled_kernel(const uint8_t* __restrict__ w, int rows, int cols, int type,
+                                     int tile_bytes, int src_row_mul, int src_row_add,
+                                     float* __restrict__ out) {
+  const int nb = cols / 32;
+  const int qsz = type == kQ4_0 ? 16 : 32;
+  const long long total = (long long)rows * cols;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int r = (int)(i / cols), c = (int)(i - (long long)r * cols);
+    const int b = c >> 5, j = c & 31;
+    const int R = r * src_row_mul + src_row_add;
+    const uint8_t* tile = w + (size_t)(R >> 2) * tile_bytes;
+    const int ri = R & 3;
+    const uint8_t* sp = tile + 4 * nb * qsz + b * 8 + ri * 2;
+    const float d = half_bits_to_float((uint16_t)sp[0] | ((uint16_t)sp[1] << 8));
+    const uint8_t* q = tile + (size_t)ri * nb * qsz + b * qsz;
+    float v;
+    if (type == kQ4_0) {
+      const uint8_t byte = q[j & 15];
+      const int qq = j < 16 ? (byte & 0xF) : (byte >> 4);
+      v = __fmul_rn(d, (float)(qq - 8));
+    } else {
+      v = __fmul_rn(d, (float)(int8_t)q[j]);
+    }
+    out[i] = v;
+  }
+}
+
 // Dequantise a row-interleaved matrix back to fp32 rows (for bit-exactness
 // checks against the reference dequantiser, quantize.c:60-72 / :139-149):
 // value = fp32(d) * (q - 8) (Q4_0) or fp32(d) * q (Q8_0), one rounding.

@@ -79,6 +79,7 @@ T* dev_alloc(Context* c, size_t n) {
 }
 
 int round_up(int a, int b) { return (a + b - 1) / b * b; }
+size_t round_up_sz(size_t a, size_t b) { return (a + b - 1) / b * b; }
 
 // ---------------------------------------------------------------- launches
 
@@ -206,7 +207,23 @@ DevMatrix layout(int rows, int cols, int type) {
   return m;
 }
 
-size_t matrix_bytes(const DevMatrix& m) { return (size_t)m.rows * m.row_stride; }
+// Tiled layout of the persistent step kernel (step_kernel.cuh).
+DevMatrix layout_tiled(int rows, int cols, int type) {
+  DevMatrix m;
+  m.rows = rows;
+  m.cols = cols;
+  m.type = type;
+  m.tiled = true;
+  const int nb = cols / 32;
+  const int qsz = type == kQ4_0 ? 16 : 32;
+  m.tile_bytes = kStepTileRows * nb * qsz + round_up(nb * 8, 16);
+  m.ntiles = (rows + kStepTileRows - 1) / kStepTileRows;
+  return m;
+}
+
+size_t matrix_bytes(const DevMatrix& m) {
+  return m.tiled ? (size_t)m.ntiles * m.tile_bytes : (size_t)m.rows * m.row_stride;
+}
 
 // Uploads one GGUF matrix (rows x cols blocks) through the staging buffer and
 // repacks it into rows dst_row_mul*r + dst_row_add of `dst`.
@@ -223,9 +240,14 @@ void upload_matrix(Context* c, const GgufTensor& t, const DevMatrix& dst, int ds
   const long long blocks = (long long)t.rows() * (t.cols() / 32);
   const int threads = 256;
   const int grid = (int)std::min<long long>((blocks + threads - 1) / threads, 65535);
-  repack_kernel<<<grid, threads, 0, c->stream>>>(stage, (int)t.rows(), (int)t.cols(), t.type,
-                                                 dst.data, dst.row_stride, dst.scale_off,
-                                                 dst_row_mul, dst_row_add);
+  if (dst.tiled)
+    repack_tiled_kernel<<<grid, threads, 0, c->stream>>>(stage, (int)t.rows(), (int)t.cols(), t.type,
+                                                         dst.data, dst.tile_bytes, dst_row_mul,
+                                                         dst_row_add);
+  else
+    repack_kernel<<<grid, threads, 0, c->stream>>>(stage, (int)t.rows(), (int)t.cols(), t.type,
+                                                   dst.data, dst.row_stride, dst.scale_off,
+                                                   dst_row_mul, dst_row_add);
   CK(cudaGetLastError());
 }
 
@@ -235,12 +257,102 @@ const GgufTensor& need(const GgufModel& m, const std::string& name) {
   return *t;
 }
 
-float* upload_f32(Context* c, const GgufTensor& t, size_t n) {
+void upload_f32_into(Context* c, const GgufTensor& t, size_t n, float* dst) {
   if (t.type != kF32) fail(SS_CUDA_ERROR_INVALID_MODEL, "%s must be F32", t.name.c_str());
   if (t.bytes < n * 4) fail(SS_CUDA_ERROR_INVALID_MODEL, "%s is too small", t.name.c_str());
+  CK(cudaMemcpyAsync(dst, t.data, n * 4, cudaMemcpyHostToDevice, c->stream));
+}
+
+float* upload_f32(Context* c, const GgufTensor& t, size_t n) {
   float* p = dev_alloc<float>(c, n);
-  CK(cudaMemcpyAsync(p, t.data, n * 4, cudaMemcpyHostToDevice, c->stream));
+  upload_f32_into(c, t, n, p);
   return p;
+}
+
+// ------------------------------------------------------ persistent step plan
+
+using StepFn = void (*)(const StepParams);
+
+template <int T, int H>
+StepFn step_fn_hd(int hd) {
+  switch (hd) {
+    case 32: return &decode_step_kernel<T, H, 32>;
+    case 64: return &decode_step_kernel<T, H, 64>;
+    case 128: return &decode_step_kernel<T, H, 128>;
+    case 256: return &decode_step_kernel<T, H, 256>;
+    default: return nullptr;
+  }
+}
+StepFn step_fn_for(int type, int htype, int hd) {
+  if (type == kQ4_0 && htype == kQ4_0) return step_fn_hd<kQ4_0, kQ4_0>(hd);
+  if (type == kQ4_0 && htype == kQ8_0) return step_fn_hd<kQ4_0, kQ8_0>(hd);
+  if (type == kQ8_0 && htype == kQ8_0) return step_fn_hd<kQ8_0, kQ8_0>(hd);
+  return nullptr;
+}
+
+// Decides whether the persistent step kernel can run this model on this GPU
+// and sizes it: one CTA per SM; the weight ring gets what shared memory is left
+// after the consumers' scratch (row partial sums or the attention task's
+// buffers).  Returns false (multi-kernel step) when a shape is outside what the
+// kernel supports.  SS_STEP_SLOTS caps the ring slots (tuning sweeps).
+bool plan_step(Context* c, int htype) {
+  const int qd = c->nh * c->hd, kvd = c->nkv * c->hd;
+  const int G = c->nh / c->nkv;
+  StepFn fn = step_fn_for(c->wtype, htype, c->hd);
+  if (!fn || G > kAttnMaxG) return false;
+  const int cols[3] = {c->d, qd, c->ff};
+  for (int x : cols)
+    if (x % 32 || x / 32 > kStepMaxNb) return false;
+  if (c->d % 32 || c->ff % 32 || qd % 32) return false;
+  int coop = 0;
+  CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device));
+  if (!coop) return false;
+  const int ncta = c->sm_count;
+  const int nsplit = std::max(1, ncta / c->nkv);
+  if ((long long)G * ((c->ctx + nsplit - 1) / nsplit) > kStepScoreCap) return false;
+  struct Shape { int rows, cols, type; };
+  const Shape shapes[5] = {{qd + 2 * kvd, c->d, c->wtype}, {c->d, qd, c->wtype},
+                           {2 * c->ff, c->d, c->wtype}, {c->d, c->ff, c->wtype},
+                           {c->vocab, c->d, htype}};
+  int slot = 0;
+  size_t red = 0;
+  for (const Shape& sh : shapes) {
+    const DevMatrix m = layout_tiled(sh.rows, sh.cols, sh.type);
+    const int nb = sh.cols / 32, wpr = (nb + 31) / 32, rg = kStepConsumerWarps / wpr;
+    slot = std::max(slot, rg * m.tile_bytes);
+    const size_t rows_cta = (size_t)((m.ntiles + ncta - 1) / ncta) * kStepTileRows;
+    red = std::max(red, (size_t)wpr * rows_cta * sizeof(float));
+  }
+  slot = round_up(slot, 128);
+  const size_t att = sizeof(float) * ((size_t)(kAttnMaxG + kStepConsumerWarps) * c->hd + kStepScoreCap + 16) +
+                     2 * (size_t)c->hd;
+  // the scratch also holds a phase's activation planes
+  const size_t planes = (size_t)(std::max(std::max(c->d, qd), c->ff) / 32) * sizeof(PlaneBlock);
+  const size_t scratch = (std::max(std::max(red, att), planes) + 127) / 128 * 128;
+  cudaFuncAttributes fa;
+  CK(cudaFuncGetAttributes(&fa, fn));
+  // the kernel hands registers from its producer warpgroup to its consumers
+  // (setmaxnreg); that split is exact for this launch count only
+  if (fa.numRegs != kStepLaunchRegs) return false;
+  int optin = 0;
+  CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->device));
+  // [ring][128 B of mbarriers: full, empty per slot + the plane barrier][scratch]
+  const long long avail = (long long)optin - (long long)fa.sharedSizeBytes - (long long)scratch - 128;
+  int nslots = (int)std::min<long long>(7, avail / slot);
+  nslots = std::min(nslots, env_int("SS_STEP_SLOTS", 7));
+  if (nslots < 2) return false;
+  const size_t smem = (size_t)nslots * slot + 128 + scratch;
+  CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int occ = 0;
+  CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kStepThreads, smem));
+  if (occ < 1) return false;
+  c->step_fn = (const void*)fn;
+  c->step_grid = ncta;
+  c->step_nslots = nslots;
+  c->step_slot_bytes = slot;
+  c->step_nsplit = nsplit;
+  c->step_smem = smem;
+  return true;
 }
 
 void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt) {
@@ -282,6 +394,13 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
   c->attn_scale = 1.0f / sqrtf((float)c->hd);  // layer_scheduler.c:421
 
   const int qd = c->nh * c->hd, kvd = c->nkv * c->hd;
+  if (!out) fail(SS_CUDA_ERROR_INVALID_MODEL, "tied embeddings (no output.weight) unsupported");
+  if (out->type != kQ4_0 && out->type != kQ8_0)
+    fail(SS_CUDA_ERROR_INVALID_MODEL, "output.weight type %d unsupported", out->type);
+  c->mega = c->mega && plan_step(c, out->type);
+  auto mat_layout = [&](int rows, int cols, int type) {
+    return c->mega ? layout_tiled(rows, cols, type) : layout(rows, cols, type);
+  };
   size_t max_bytes = 0;
   for (const auto& t : g.tensors) max_bytes = std::max<size_t>(max_bytes, t.bytes);
   uint8_t* stage = nullptr;
@@ -294,6 +413,19 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
     c->embd = upload_f32(c, embd, (size_t)embd.rows() * c->d);
     c->weight_bytes += (size_t)embd.rows() * c->d * 4;
     c->layers.resize((size_t)c->L);
+    // every layer's four matrices in one allocation at a fixed stride (the
+    // persistent step addresses layer l as layer 0 + l * stride), and the
+    // norm weights as [L][d] arrays
+    const DevMatrix s_qkv = mat_layout(qd + 2 * kvd, c->d, c->wtype), s_o = mat_layout(c->d, qd, c->wtype),
+                    s_gu = mat_layout(2 * c->ff, c->d, c->wtype), s_down = mat_layout(c->d, c->ff, c->wtype);
+    const size_t o_o = round_up_sz(matrix_bytes(s_qkv), 256);
+    const size_t o_gu = o_o + round_up_sz(matrix_bytes(s_o), 256);
+    const size_t o_down = o_gu + round_up_sz(matrix_bytes(s_gu), 256);
+    c->layer_stride = o_down + round_up_sz(matrix_bytes(s_down), 256);
+    uint8_t* slab = dev_alloc<uint8_t>(c, c->layer_stride * (size_t)c->L);
+    CK(cudaMemsetAsync(slab, 0, c->layer_stride * (size_t)c->L, c->stream));
+    c->attn_norm_all = dev_alloc<float>(c, (size_t)c->L * c->d);
+    c->ffn_norm_all = dev_alloc<float>(c, (size_t)c->L * c->d);
     for (int l = 0; l < c->L; l++) {
       Layer& ly = c->layers[(size_t)l];
       auto nm = [&](const char* s) { return "blk." + std::to_string(l) + "." + s; };
@@ -308,19 +440,16 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
           (int)wo.rows() != c->d || (int)wo.cols() != qd || (int)wg.rows() != c->ff ||
           (int)wu.rows() != c->ff || (int)wd.rows() != c->d || (int)wd.cols() != c->ff)
         fail(SS_CUDA_ERROR_INVALID_MODEL, "layer %d tensor shapes do not match the metadata", l);
-      ly.qkv = layout(qd + 2 * kvd, c->d, c->wtype);
-      ly.o = layout(c->d, qd, c->wtype);
-      ly.gu = layout(2 * c->ff, c->d, c->wtype);
-      ly.down = layout(c->d, c->ff, c->wtype);
-      const size_t b0 = matrix_bytes(ly.qkv), b1 = matrix_bytes(ly.o), b2 = matrix_bytes(ly.gu),
-                   b3 = matrix_bytes(ly.down);
-      ly.block = dev_alloc<uint8_t>(c, b0 + b1 + b2 + b3);
-      CK(cudaMemsetAsync(ly.block, 0, b0 + b1 + b2 + b3, c->stream));
+      ly.qkv = s_qkv;
+      ly.o = s_o;
+      ly.gu = s_gu;
+      ly.down = s_down;
+      ly.block = slab + (size_t)l * c->layer_stride;
       ly.qkv.data = ly.block;
-      ly.o.data = ly.block + b0;
-      ly.gu.data = ly.block + b0 + b1;
-      ly.down.data = ly.block + b0 + b1 + b2;
-      c->weight_bytes += b0 + b1 + b2 + b3;
+      ly.o.data = ly.block + o_o;
+      ly.gu.data = ly.block + o_gu;
+      ly.down.data = ly.block + o_down;
+      c->weight_bytes += matrix_bytes(s_qkv) + matrix_bytes(s_o) + matrix_bytes(s_gu) + matrix_bytes(s_down);
       upload_matrix(c, wq, ly.qkv, 1, 0, stage, max_bytes);
       upload_matrix(c, wk, ly.qkv, 1, qd, stage, max_bytes);
       upload_matrix(c, wv, ly.qkv, 1, qd + kvd, stage, max_bytes);
@@ -328,15 +457,14 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
       upload_matrix(c, wg, ly.gu, 2, 0, stage, max_bytes);
       upload_matrix(c, wu, ly.gu, 2, 1, stage, max_bytes);
       upload_matrix(c, wd, ly.down, 1, 0, stage, max_bytes);
-      ly.attn_norm = upload_f32(c, need(g, nm("attn_norm.weight")), (size_t)c->d);
-      ly.ffn_norm = upload_f32(c, need(g, nm("ffn_norm.weight")), (size_t)c->d);
+      ly.attn_norm = c->attn_norm_all + (size_t)l * c->d;
+      ly.ffn_norm = c->ffn_norm_all + (size_t)l * c->d;
+      upload_f32_into(c, need(g, nm("attn_norm.weight")), (size_t)c->d, ly.attn_norm);
+      upload_f32_into(c, need(g, nm("ffn_norm.weight")), (size_t)c->d, ly.ffn_norm);
       CK(cudaStreamSynchronize(c->stream));  // staging buffer reuse
     }
     c->out_norm = upload_f32(c, need(g, "output_norm.weight"), (size_t)c->d);
-    if (!out) fail(SS_CUDA_ERROR_INVALID_MODEL, "tied embeddings (no output.weight) unsupported");
-    c->lm_head = layout(c->vocab, c->d, out->type);
-    if (out->type != kQ4_0 && out->type != kQ8_0)
-      fail(SS_CUDA_ERROR_INVALID_MODEL, "output.weight type %d unsupported", out->type);
+    c->lm_head = mat_layout(c->vocab, c->d, out->type);
     c->lm_block = dev_alloc<uint8_t>(c, matrix_bytes(c->lm_head));
     c->lm_head.data = c->lm_block;
     c->weight_bytes += matrix_bytes(c->lm_head);
@@ -352,6 +480,8 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
   }
   CK(cudaFree(stage));
 }
+
+void alloc_step_state(Context* c);
 
 void alloc_state(Context* c) {
   const int kvd = c->nkv * c->hd, qd = c->nh * c->hd;
@@ -400,6 +530,92 @@ void alloc_state(Context* c) {
   CK(cudaMallocHost(&c->h_logits, sizeof(float) * (size_t)c->vocab));
   CK(cudaMallocHost(&c->h_small, sizeof(int) * 64));
   c->embed_blocks = std::max(1, std::min(16, (c->d + 255) / 256));
+  if (c->mega) alloc_step_state(c);
+}
+
+// Buffers of the persistent step kernel and its parameter block.
+void alloc_step_state(Context* c) {
+  const int qd = c->nh * c->hd, kvd = c->nkv * c->hd, ncta = c->step_grid;
+  StepParams& p = c->step_params;
+  p = StepParams{};
+  const Layer& l0 = c->layers[0];
+  p.qkv0 = l0.qkv.t();
+  p.o0 = l0.o.t();
+  p.gu0 = l0.gu.t();
+  p.down0 = l0.down.t();
+  p.layer_stride = (long long)c->layer_stride;
+  p.attn_norm = c->attn_norm_all;
+  p.ffn_norm = c->ffn_norm_all;
+  p.L = c->L;
+  p.head = c->lm_head.t();
+  p.out_norm = c->out_norm;
+  p.embd = c->embd;
+  p.d = c->d;
+  p.qd = qd;
+  p.kvd = kvd;
+  p.ff = c->ff;
+  p.vocab = c->vocab;
+  p.nh = c->nh;
+  p.nkv = c->nkv;
+  p.hd = c->hd;
+  p.rope_dim = c->rope_dim;
+  p.ctx = c->ctx;
+  p.eps = c->eps;
+  p.attn_scale = c->attn_scale;
+  p.rope_tab = c->rope_tab;
+  p.kc = c->kc;
+  p.vc = c->vc;
+  p.ks = c->ks;
+  p.vs = c->vs;
+  p.d_pos = &c->ctrl->pos;
+  p.fixed_until = &c->ctrl->fixed_until;
+  p.err = &c->ctrl->err;
+  p.seq_tokens = c->seq_tokens;
+  p.h = c->h;
+  p.qkv_out = c->qkv;
+  p.attn_out = c->attn_out;
+  p.act = c->act;
+  p.logits = c->logits;
+  p.amax_part = dev_alloc<float2>(c, (size_t)ncta);
+  p.att_part = dev_alloc<float>(c, (size_t)c->nh * c->step_nsplit * (c->hd + 2));
+  // counters, zeroed here and by ss_cuda_reset: grid barrier, abort flag,
+  // attention merge counts [nkv]
+  c->step_sync_words = 4 + (size_t)c->nkv;
+  c->step_sync = dev_alloc<unsigned>(c, c->step_sync_words);
+  CK(cudaMemset(c->step_sync, 0, sizeof(unsigned) * c->step_sync_words));
+  p.grid_bar = c->step_sync;
+  p.abort_flag = c->step_sync + 1;
+  p.cnt_att = c->step_sync + 4;
+  p.am_part = c->am_part;
+  p.am_cnt = c->am_cnt;
+  p.nsplit = c->step_nsplit;
+  p.slot_bytes = c->step_slot_bytes;
+  p.nslots = c->step_nslots;
+  // producer pacing (measured on B200): a few stages in flight per SM keep HBM
+  // busy; SS_STEP_INFLIGHT / SS_STEP_PREFETCH override for tuning sweeps
+  p.inflight = std::max(1, std::min(c->step_nslots, env_int("SS_STEP_INFLIGHT", c->step_nslots)));
+  p.prefetch = env_int("SS_STEP_PREFETCH", 0);
+  if (c->trace) {
+    const size_t n = (size_t)(2 + 5 * c->L) * ncta * 8;
+    c->step_trace = dev_alloc<long long>(c, n);
+    CK(cudaMemset(c->step_trace, 0, n * sizeof(long long)));
+    p.trace = c->step_trace;
+  }
+}
+
+void launch_step(Context* c) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(c->step_grid);
+  cfg.blockDim = dim3(kStepThreads);
+  cfg.dynamicSmemBytes = c->step_smem;
+  cfg.stream = c->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* args[1] = {&c->step_params};
+  CK(cudaLaunchKernelExC(&cfg, c->step_fn, args));
 }
 
 using AttnFn = void (*)(const AttnParams);
@@ -414,6 +630,8 @@ AttnFn attn_fn(int hd) {
 }
 
 void plan_all(Context* c) {
+  CK(cudaFuncSetAttribute(attn_fn(c->hd), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->attn_smem));
+  if (c->mega) return;  // the persistent step was planned before the upload
   const Layer& l0 = c->layers[0];
   c->g_qkv = plan_gemv_for(c, XSrc::RmsNorm, Epi::QKV, l0.qkv);
   c->g_o = plan_gemv_for(c, XSrc::Plain, Epi::Residual, l0.o);
@@ -421,7 +639,6 @@ void plan_all(Context* c) {
   c->g_down = plan_gemv_for(c, XSrc::Plain, Epi::Residual, l0.down);
   c->g_head = plan_gemv_for(c, XSrc::RmsNorm, Epi::Argmax, c->lm_head);
   if (c->g_head.ctas > 4096) fail(SS_CUDA_ERROR_INVALID_MODEL, "lm_head grid too large");
-  CK(cudaFuncSetAttribute(attn_fn(c->hd), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->attn_smem));
 }
 
 GemvParams base_params(Context* c) {
@@ -546,6 +763,10 @@ void launch_head(Context* c, bool pdl) {
 
 // Enqueues one decode step (embedding -> L layers -> lm_head + argmax).
 void enqueue_step(Context* c, bool pdl) {
+  if (c->mega) {
+    launch_step(c);
+    return;
+  }
   launch_embed(c, pdl);
   for (int l = 0; l < c->L; l++) {
     launch_qkv(c, l, pdl);
@@ -558,7 +779,7 @@ void enqueue_step(Context* c, bool pdl) {
 }
 
 void build_graph(Context* c) {
-  if (c->step_exec || !c->use_graph) return;
+  if (c->step_exec || !c->use_graph || c->mega) return;  // one launch per step needs no graph
   for (int attempt = 0; attempt < 2; attempt++) {
     const bool pdl = c->use_pdl && attempt == 0;
     cudaGraph_t graph = nullptr;
@@ -659,6 +880,8 @@ Context* create(const uint8_t* base, uint64_t size, const ss_cuda_options_t* o) 
   c->use_pdl = !(opts.flags & SS_CUDA_FLAG_NO_PDL) && !getenv("SS_CUDA_NO_PDL");
   c->use_graph = !(opts.flags & SS_CUDA_FLAG_NO_GRAPH);
   c->tuning = read_tuning();
+  c->mega = !(opts.flags & SS_CUDA_FLAG_MULTI_KERNEL) && !getenv("SS_CUDA_MULTI_KERNEL");
+  c->trace = (opts.flags & SS_CUDA_FLAG_TRACE) != 0;
   try {
     CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     if (base) {
@@ -854,15 +1077,17 @@ SS_API int ss_cuda_stats(const ss_cuda_ctx_t* ctx, int64_t* out, int32_t n) {
   return guard([&] {
     auto* c = reinterpret_cast<const Context*>(ctx);
     if (!c || !out) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null argument");
-    const int64_t v[8] = {c->has_model ? 2 + 5LL * c->L : 0,
-                          (int64_t)c->weight_bytes,
-                          (int64_t)c->kv_bytes,
-                          c->attn_nsplit,
-                          c->graph_pdl ? 1 : 0,
-                          c->steps_run,
-                          c->g_qkv.ctas,
-                          c->g_down.ctas};
-    for (int i = 0; i < n && i < 8; i++) out[i] = v[i];
+    const int64_t v[10] = {c->has_model ? (c->mega ? 1 : 2 + 5LL * c->L) : 0,
+                           (int64_t)c->weight_bytes,
+                           (int64_t)c->kv_bytes,
+                           c->mega ? c->step_nsplit : c->attn_nsplit,
+                           c->graph_pdl ? 1 : 0,
+                           c->steps_run,
+                           c->mega ? c->step_grid : c->g_qkv.ctas,
+                           c->mega ? c->step_grid : c->g_down.ctas,
+                           c->mega ? 1 : 0,
+                           c->mega ? c->step_nslots : 0};
+    for (int i = 0; i < n && i < 10; i++) out[i] = v[i];
   });
 }
 
@@ -945,6 +1170,9 @@ SS_API void ss_cuda_reset(ss_cuda_ctx_t* ctx) {
     CK(cudaMemsetAsync(c->amax_v, 0, rows * 4, c->stream));
     CK(cudaMemsetAsync(c->h, 0, sizeof(float) * c->d, c->stream));
     CK(cudaMemsetAsync(c->ctrl, 0, sizeof(Ctrl), c->stream));
+    CK(cudaMemsetAsync(c->am_cnt, 0, sizeof(unsigned), c->stream));
+    if (c->step_sync)
+      CK(cudaMemsetAsync(c->step_sync, 0, sizeof(unsigned) * c->step_sync_words, c->stream));
     CK(cudaStreamSynchronize(c->stream));
     c->host_pos = 0;
     c->cancelled.store(false);
@@ -1066,8 +1294,12 @@ SS_API int ss_cuda_dequantize_tensor(ss_cuda_ctx_t* ctx, const char* name, float
     if (n != (int64_t)rows * m->cols) fail(SS_CUDA_ERROR_INVALID_PARAMS, "n must be rows*cols = %lld", (long long)rows * m->cols);
     float* d_out = nullptr;
     CK(cudaMalloc(&d_out, sizeof(float) * (size_t)n));
-    dequant_rows_kernel<<<1024, 256, 0, c->stream>>>(m->data, rows, m->cols, m->type, m->row_stride,
-                                                    m->scale_off, mul, add, d_out);
+    if (m->tiled)
+      dequant_tiled_kernel<<<1024, 256, 0, c->stream>>>(m->data, rows, m->cols, m->type, m->tile_bytes,
+                                                       mul, add, d_out);
+    else
+      dequant_rows_kernel<<<1024, 256, 0, c->stream>>>(m->data, rows, m->cols, m->type, m->row_stride,
+                                                      m->scale_off, mul, add, d_out);
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaMemcpyAsync(out, d_out, sizeof(float) * (size_t)n, cudaMemcpyDeviceToHost, c->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
@@ -1100,13 +1332,19 @@ SS_API int ss_cuda_dequantize(int32_t type, const void* blocks, int64_t n, float
 SS_API int ss_cuda_time_kernel(ss_cuda_ctx_t* ctx, int32_t which, int32_t iters, float* ms_per_launch) {
   return guard([&] {
     Context* c = need_model(ctx);
-    if (which < 0 || which > 5 || iters <= 0 || !ms_per_launch) fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad arguments");
+    if (which < 0 || which > 6 || iters <= 0 || !ms_per_launch) fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad arguments");
+    if (c->mega && which != 6)
+      fail(SS_CUDA_ERROR_INVALID_PARAMS, "per-kernel timing needs the multi-kernel step (SS_CUDA_FLAG_MULTI_KERNEL)");
+    const int pos0 = c->host_pos;
+    if (which == 6 && pos0 + iters + 3 > c->ctx)
+      fail(SS_CUDA_ERROR_INVALID_PARAMS, "%d steps from position %d exceed the context", iters + 3, pos0);
     cudaEvent_t e0, e1;
     CK(cudaEventCreate(&e0));
     CK(cudaEventCreate(&e1));
     auto one = [&](int i) {
       const int l = i % c->L;
       switch (which) {
+        case 6: enqueue_step(c, c->use_pdl); break;
         case 0: launch_qkv(c, l, false); break;
         case 1: launch_attn(c, l, false); break;
         case 2: launch_o(c, l, false); break;
@@ -1125,9 +1363,10 @@ SS_API int ss_cuda_time_kernel(ss_cuda_ctx_t* ctx, int32_t which, int32_t iters,
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
     *ms_per_launch = ms / (float)iters;
-    if (which == 5) {  // the lm_head advanced the device position; restore it
+    if (which >= 5) {  // the lm_head advanced the device position; restore it
       CK(cudaMemcpyAsync(c->ctrl, &c->host_pos, sizeof(int), cudaMemcpyHostToDevice, c->stream));
       CK(cudaStreamSynchronize(c->stream));
+      check_device_error(c);
     }
   });
 }
@@ -1142,8 +1381,25 @@ SS_API int64_t ss_cuda_kernel_bytes(const ss_cuda_ctx_t* ctx, int32_t which) {
     case 3: return (int64_t)matrix_bytes(l0.gu);
     case 4: return (int64_t)matrix_bytes(l0.down);
     case 5: return (int64_t)matrix_bytes(c->lm_head);
+    case 6: {
+      int64_t b = (int64_t)matrix_bytes(c->lm_head);
+      for (const Layer& ly : c->layers)
+        b += (int64_t)(matrix_bytes(ly.qkv) + matrix_bytes(ly.o) + matrix_bytes(ly.gu) + matrix_bytes(ly.down));
+      return b;
+    }
     default: return -1;
   }
+}
+
+SS_API int ss_cuda_step_trace(ss_cuda_ctx_t* ctx, int64_t* out, int64_t n) {
+  return guard([&] {
+    Context* c = need_model(ctx);
+    if (!c->step_trace) fail(SS_CUDA_ERROR_INVALID_PARAMS, "no trace: create the context with SS_CUDA_FLAG_TRACE");
+    const int64_t total = (int64_t)(2 + 5 * c->L) * c->step_grid * 8;
+    if (!out || n != total) fail(SS_CUDA_ERROR_INVALID_PARAMS, "n must be %lld", (long long)total);
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaMemcpy(out, c->step_trace, sizeof(int64_t) * (size_t)n, cudaMemcpyDeviceToHost));
+  });
 }
 
 SS_API int ss_cuda_kv_row(ss_cuda_ctx_t* ctx, int32_t layer, int32_t pos, int8_t* k, int8_t* v,

@@ -10,14 +10,19 @@
 #include "attention.cuh"
 #include "gemv.cuh"
 #include "misc_kernels.cuh"
+#include "step_kernel.cuh"
 
 namespace ss {
 
-// A repacked quantized matrix in device memory (layout in gemv.cuh).
+// A repacked quantized matrix in device memory: row-interleaved (gemv.cuh,
+// the multi-kernel step and the op-level matvecs) or tiled (step_kernel.cuh).
 struct DevMatrix {
   uint8_t* data = nullptr;
   int rows = 0, cols = 0, row_stride = 0, scale_off = 0, type = 0;
+  bool tiled = false;
+  int ntiles = 0, tile_bytes = 0;
   QMatrix q() const { return QMatrix{data, rows, cols, row_stride, scale_off, type}; }
+  TMat t() const { return TMat{data, cols / 32, ntiles, tile_bytes, type, rows}; }
 };
 
 // Launch geometry of one GEMV (see gemv.cuh for the work split).
@@ -64,6 +69,7 @@ struct Context {
   bool has_model = false;
   bool use_pdl = true;
   bool use_graph = true;
+  bool trace = false;
   GemvTuning tuning;
   std::atomic<bool> cancelled{false};
 
@@ -78,6 +84,9 @@ struct Context {
   DevMatrix lm_head;
   uint8_t* lm_block = nullptr;
   std::vector<Layer> layers;
+  size_t layer_stride = 0;           // bytes between layers in the weight slab
+  float* attn_norm_all = nullptr;    // [L][d]
+  float* ffn_norm_all = nullptr;     // [L][d]
   size_t weight_bytes = 0;
 
   // KV cache [L][ctx][kvd] + scales/maxima [L][ctx]
@@ -110,6 +119,16 @@ struct Context {
   int attn_nsplit = 1;
   size_t attn_smem = 0;
   int embed_blocks = 1;
+
+  // persistent single-kernel step (step_kernel.cuh)
+  bool mega = false;
+  const void* step_fn = nullptr;
+  int step_grid = 0, step_nslots = 0, step_slot_bytes = 0, step_nsplit = 1;
+  size_t step_smem = 0;
+  StepParams step_params{};
+  unsigned* step_sync = nullptr;  // counters zeroed by reset (see alloc_step_state)
+  long long* step_trace = nullptr;  // per-phase timeline of the last step (SS_CUDA_FLAG_TRACE)
+  size_t step_sync_words = 0;
 
   cudaGraphExec_t step_exec = nullptr;
   bool graph_pdl = false;

@@ -1,0 +1,967 @@
+// step_kernel.cuh -- one decode step of SlipStream's llama path as a single
+// persistent kernel on sm_100a.
+//
+// Same computation as ss_scheduler_forward (SlipStream/src/core/
+// layer_scheduler.c:571-679): embedding, L x (RMSNorm, Q/K/V matvec + RoPE,
+// int8 KV append + attention, O matvec + residual, RMSNorm, gate/up matvec +
+// SwiGLU, down matvec + residual), final RMSNorm, lm_head, greedy argmax.
+//
+// Execution model.  One CTA per SM (grid = SM count, cooperative launch so all
+// are co-resident), 20 warps: warp 0 is a *producer* that streams every weight
+// tile this CTA will ever touch during the step -- all phases, back to back --
+// from HBM into a shared-memory ring with cp.async.bulk, gated only by ring
+// slots being free, plus a bulk L2 prefetch of the next phase's range.  It
+// never waits for activations, so HBM keeps streaming across phase
+// boundaries.  Warps 4..19 are *consumers*: for each phase they wait at a
+// grid-wide barrier for the phase's input, then consume their share of the
+// ring and write the phase's outputs.  The phases are
+//     EMBED | per layer: QKV, ATT, O, GU, DOWN | HEAD
+// separated by grid barriers (monotonic counter, bounded spin).
+//
+// Weight layout ("tiled"): a matrix is stored as tiles of 4 rows; a tile holds
+// the 4 rows' quant bytes row-major (block b of row i at i*nb*QB + b*QB, the
+// GGUF block bytes unchanged) followed by the nb x 4 fp16 scales block-major
+// (scale of row i, block b at b*8 + i*2), padded to 16 bytes.  A CTA owns a
+// contiguous range of tiles of each matrix, so a ring stage is one bulk copy.
+//
+// Inner product.  As in gemv.cuh: activations in block fixed point (23 bits
+// per 32-element block, three signed byte planes), weights' nibbles / bytes
+// multiplied with dp4a, exact in int32, combined in fp32.  At the start of a
+// matvec phase each consumer thread reads its 32 input values from L2 and
+// converts them (RMSNorm first where the reference has one: ss = sum x^2,
+// scale = 1 / sqrtf(ss / n + eps), x * scale * w, SlipStream/src/backends/
+// cpu_neon.c:109-115); every CTA does this from the same data in the same
+// order, so all use identical activations.  Epilogues only write the phase's
+// output vector.
+//
+// All waits are bounded (about one second of SM clocks); on expiry a CTA sets
+// an error bit and a global abort flag that every other wait also watches, the
+// producer drains its outstanding copies, and the kernel returns.
+#pragma once
+#include "attention.cuh"
+#include "gemv.cuh"
+
+namespace ss {
+
+constexpr int kStepTileRows = 4;
+constexpr int kStepConsumerWarps = 16;
+constexpr int kStepConsumers = kStepConsumerWarps * 32;  // 512
+// Warpgroup 0 (warp 0: the producer; warps 1-3 exit at once) gives registers
+// to the four consumer warpgroups: launched at kStepLaunchRegs per thread, it
+// drops to kStepProducerRegs and the consumers rise to kStepConsumerRegs, so
+// 128 * producer + 512 * consumer == 640 * launch -- the host launches only
+// when the compiled kernel's launch register count is exactly kStepLaunchRegs.
+constexpr int kStepProducerThreads = 128;
+constexpr int kStepThreads = kStepProducerThreads + kStepConsumers;  // 640
+constexpr int kStepLaunchRegs = 96;
+constexpr int kStepProducerRegs = 32;
+constexpr int kStepConsumerRegs = 112;
+static_assert(kStepProducerThreads * kStepProducerRegs + kStepConsumers * kStepConsumerRegs ==
+                  kStepThreads * kStepLaunchRegs,
+              "register split must equal the launch allocation");
+constexpr int kStepMaxNb = kStepConsumers;               // <= 16384 columns
+constexpr int kStepScoreCap = 4096;                      // attention scores per task
+
+// One activation block in block fixed point in shared memory: 112 bytes (7 x
+// 16), no padding -- consumer lane j reads block j with 16-byte loads, and the
+// odd stride spreads a warp's lanes over all banks.
+struct PlaneBlock {
+  int pl[3][8];  // word w of plane p: digits p of elements 4w .. 4w+3
+  int nsum[3];   // -sum_j digit_pj (times the weights' zero point: accumulator start)
+  float c0;      // 2^(e-22): value of one unit of plane 0
+};
+static_assert(sizeof(PlaneBlock) == 112, "PlaneBlock must be 112 bytes");
+
+struct TMat {
+  const uint8_t* w;
+  int nb;          // 32-column blocks per row
+  int ntiles;      // 4-row tiles
+  int tile_bytes;  // bytes per tile (multiple of 16)
+  int type;        // kQ4_0 / kQ8_0
+  int rows;        // real rows (the last tile may carry zero padding rows)
+};
+
+struct StepParams {
+  // layer 0's matrices; layer l's start layer_stride * l bytes further (all
+  // layers live in one allocation), so no descriptor is read from memory
+  TMat qkv0, o0, gu0, down0;  // gu rows interleave gate (even) and up (odd)
+  long long layer_stride;
+  const float* attn_norm;  // [L][d]
+  const float* ffn_norm;   // [L][d]
+  int L;
+  TMat head;
+  const float* out_norm;
+  const float* embd;  // [vocab][d] fp32
+  int d, qd, kvd, ff, vocab, nh, nkv, hd, rope_dim, ctx;
+  float eps, attn_scale;
+  const float2* rope_tab;
+  int8_t* kc;  // [L][ctx][kvd]
+  int8_t* vc;
+  float* ks;   // [L][ctx]
+  float* vs;
+  int* d_pos;          // position of this step; advanced by one at the end
+  const int* fixed_until;
+  int* err;
+  int* seq_tokens;     // [ctx + 1]
+  float* h;            // residual stream [d]
+  float* qkv_out;      // q | k | v
+  float* attn_out;     // [qd]
+  float* act;          // [ff]
+  float* logits;       // [vocab]
+  float2* amax_part;   // [grid] (max |k|, max |v|) of this position
+  float* att_part;     // [nh][nsplit][hd + 2]: m, l, o[hd]
+  unsigned* cnt_att;   // [nkv] splits done per kv head (the last one merges)
+  unsigned* grid_bar;  // [1]
+  unsigned* abort_flag;  // [1]
+  unsigned long long* am_part;  // [grid]
+  unsigned* am_cnt;    // [1]
+  int nsplit;          // attention position splits per kv head
+  int slot_bytes, nslots;
+  int inflight;        // weight stages a producer keeps in flight (not yet landed)
+  int prefetch;        // 1: bulk L2 prefetch of the next weight phase
+  // optional timeline (measurement aid): [phase][cta][8] global-timer ns --
+  // 0 input ready (grid barrier passed), 1 main work done, 2 arrival at the
+  // next barrier, 3 producer issued the phase's last weight stage, 4 first
+  // stage's weights ready, 5 last stage's weights ready, 6 consumer warp 0
+  // done with its rows, 7 producer issued the phase's first stage
+  long long* trace;
+};
+
+// ---------------------------------------------------------------- helpers
+
+SS_DEVINL unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+SS_DEVINL unsigned ld_volatile_u32(const unsigned* p) {
+  return *reinterpret_cast<const volatile unsigned*>(p);
+}
+
+SS_DEVINL long long global_ns() {
+  long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+SS_DEVINL void trace_mark(const StepParams& p, int phase, int what) {
+  if (p.trace) p.trace[((size_t)phase * gridDim.x + blockIdx.x) * 8 + what] = global_ns();
+}
+
+// Balanced contiguous split of n items over g parts.
+SS_DEVINL void part_range(int n, int i, int g, int& a, int& b) {
+  a = (int)(((long long)n * i) / g);
+  b = (int)(((long long)n * (i + 1)) / g);
+}
+
+// Warps per row and row groups of a matrix with nb blocks.
+SS_DEVINL int step_wpr(int nb) { return (nb + 31) >> 5; }
+SS_DEVINL int step_rg(int nb) { return kStepConsumerWarps / step_wpr(nb); }
+
+// Q4_0 row block: sum_j (q_j - 8) * m_j with m in three planes (exact int32),
+// returned as fp32 units of plane 0.  |a0 + 256 a1| < 2^24, so its conversion
+// is exact; one rounding in the final fma.
+SS_DEVINL float step_dot_q4(const uint4 q, const int (&pl)[3][8], const int (&init)[3]) {
+  int a0 = init[0], a1 = init[1], a2 = init[2];
+  const unsigned wq[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int t = 0; t < 4; t++) {
+    const unsigned lo = wq[t] & 0x0F0F0F0Fu;
+    const unsigned hi = (wq[t] >> 4) & 0x0F0F0F0Fu;
+    a0 = dp4a_us(lo, pl[0][t], a0);
+    a1 = dp4a_us(lo, pl[1][t], a1);
+    a2 = dp4a_us(lo, pl[2][t], a2);
+    a0 = dp4a_us(hi, pl[0][4 + t], a0);
+    a1 = dp4a_us(hi, pl[1][4 + t], a1);
+    a2 = dp4a_us(hi, pl[2][4 + t], a2);
+  }
+  return fmaf((float)a2, 65536.0f, (float)(a0 + a1 * 256));
+}
+
+SS_DEVINL float step_dot_q8(const uint4 qa, const uint4 qb, const int (&pl)[3][8]) {
+  int a0 = 0, a1 = 0, a2 = 0;
+  const unsigned wa[4] = {qa.x, qa.y, qa.z, qa.w};
+  const unsigned wb[4] = {qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+  for (int t = 0; t < 4; t++) {
+    a0 = dp4a_ss((int)wa[t], pl[0][t], a0);
+    a1 = dp4a_ss((int)wa[t], pl[1][t], a1);
+    a2 = dp4a_ss((int)wa[t], pl[2][t], a2);
+    a0 = dp4a_ss((int)wb[t], pl[0][4 + t], a0);
+    a1 = dp4a_ss((int)wb[t], pl[1][4 + t], a1);
+    a2 = dp4a_ss((int)wb[t], pl[2][4 + t], a2);
+  }
+  return fmaf((float)a2, 65536.0f, fmaf((float)a1, 256.0f, (float)a0));
+}
+
+// Phases of one step: 0 EMBED, then per layer QKV ATT O GU DOWN, then HEAD.
+enum StepPhase : int { kPhEmbed = 0, kPhQKV, kPhAtt, kPhO, kPhGU, kPhDown, kPhHead };
+
+SS_DEVINL int step_phase_count(int L) { return 2 + 5 * L; }
+SS_DEVINL void step_phase(int k, int L, int& kind, int& layer) {
+  if (k == 0) { kind = kPhEmbed; layer = 0; return; }
+  if (k == 1 + 5 * L) { kind = kPhHead; layer = L - 1; return; }
+  layer = (k - 1) / 5;
+  kind = kPhQKV + (k - 1) % 5;
+}
+SS_DEVINL bool step_phase_has_mat(int kind) { return kind != kPhEmbed && kind != kPhAtt; }
+// Weights a phase streams (kinds with step_phase_has_mat only).
+SS_DEVINL TMat step_phase_mat(const StepParams& p, int kind, int layer) {
+  TMat m;
+  switch (kind) {
+    case kPhQKV: m = p.qkv0; break;
+    case kPhO: m = p.o0; break;
+    case kPhGU: m = p.gu0; break;
+    case kPhDown: m = p.down0; break;
+    default: return p.head;
+  }
+  m.w += (size_t)layer * (size_t)p.layer_stride;
+  return m;
+}
+
+// Shared memory (dynamic): [ring][full][empty barriers][scratch].  The
+// scratch holds, one use at a time, a phase's activation planes, the matvec
+// partial sums, or an attention task's buffers.
+struct StepSmem {
+  uint8_t* ring;
+  uint64_t* full;
+  uint64_t* empty;
+  float* scratch;
+};
+
+// ---------------------------------------------------------------- producer
+
+// `s_cabort` is written by consumers only; the producer just watches it.
+SS_DEVINL void step_producer(const StepParams& p, const StepSmem& sm, const volatile int* s_cabort,
+                             int lane) {
+  if (lane != 0) return;
+  const int ncta = gridDim.x, cta = blockIdx.x;
+  const int nph = step_phase_count(p.L);
+  const int nslots = p.nslots;
+  const uint32_t ring0 = smem_addr(sm.ring), slot_bytes = (uint32_t)p.slot_bytes;
+  int issued = 0;          // stages issued so far
+  int slot = 0;            // issued % nslots
+  uint32_t wraps = 0;      // issued / nslots
+  // landing cursor: the stage `inflight` behind `issued` must have landed
+  // before the next copy is issued, so at most `inflight` copies per SM queue
+  // in the memory system -- more only delays every other load (the
+  // consumers' activations, the grid barrier) without adding bandwidth
+  const int inflight = p.inflight;
+  int lslot = 0;
+  uint32_t lwraps = 0;
+  auto prefetch_phase = [&](int k) {
+    for (; k < nph; k++) {
+      int kind, layer;
+      step_phase(k, p.L, kind, layer);
+      if (!step_phase_has_mat(kind)) continue;
+      if (!p.prefetch) return;
+      const TMat m = step_phase_mat(p, kind, layer);
+      int t0, t1;
+      part_range(m.ntiles, cta, ncta, t0, t1);
+      if (t1 > t0)
+        prefetch_l2_bulk(m.w + (size_t)t0 * m.tile_bytes, (uint32_t)((t1 - t0) * m.tile_bytes));
+      return;
+    }
+  };
+  prefetch_phase(1);
+  bool aborted = false;
+  for (int k = 1; k < nph && !aborted; k++) {
+    int kind, layer;
+    step_phase(k, p.L, kind, layer);
+    if (!step_phase_has_mat(kind)) continue;
+    const TMat mv = step_phase_mat(p, kind, layer);
+    const TMat* m = &mv;
+    // warm L2 with the next weight phase while this one streams; at the last
+    // phase, the first phase of the next step
+    if (kind == kPhHead) prefetch_phase(1);
+    else prefetch_phase(k + 1);
+    int t0, t1;
+    part_range(m->ntiles, cta, ncta, t0, t1);
+    const int rg = step_rg(m->nb);
+    for (int t = t0; t < t1; t += rg) {
+      if (t == t0) trace_mark(p, k, 7);
+      const uint32_t fb = smem_addr(sm.full + slot), eb = smem_addr(sm.empty + slot);
+      if (wraps > 0) {  // the slot's previous stage must have been released
+        const uint32_t par = (wraps - 1) & 1u;
+        bool ok = mbar_try_wait(eb, par);
+        if (!ok) {
+          const long long c0 = clock64();
+          while (!(ok = mbar_try_wait(eb, par))) {
+            if (*s_cabort || ld_volatile_u32(p.abort_flag)) break;
+            if (clock64() - c0 > kWaitBudget) {
+              atomicOr(p.err, 4);
+              atomicExch(p.abort_flag, 1u);
+              break;
+            }
+          }
+        }
+        if (!ok) { aborted = true; break; }
+      }
+      if (issued >= inflight) {
+        const uint32_t lb = smem_addr(sm.full + lslot), lpar = lwraps & 1u;
+        bool ok = mbar_try_wait(lb, lpar);
+        if (!ok) {
+          const long long c0 = clock64();
+          while (!(ok = mbar_try_wait(lb, lpar))) {
+            if (*s_cabort || ld_volatile_u32(p.abort_flag)) break;
+            if (clock64() - c0 > kWaitBudget) {
+              atomicOr(p.err, 4);
+              atomicExch(p.abort_flag, 1u);
+              break;
+            }
+          }
+        }
+        if (!ok) { aborted = true; break; }
+        if (++lslot == nslots) { lslot = 0; lwraps++; }
+      }
+      const int nt = min(rg, t1 - t);
+      const uint32_t bytes = (uint32_t)(nt * m->tile_bytes);
+      mbar_expect_tx(fb, bytes);
+      bulk_g2s(ring0 + (uint32_t)slot * slot_bytes, m->w + (size_t)t * m->tile_bytes, bytes, fb);
+      issued++;
+      if (++slot == nslots) { slot = 0; wraps++; }
+    }
+    trace_mark(p, k, 3);
+  }
+  if (aborted) {
+    // drain: the copies of the last nslots stages may still be in flight
+    for (int g = max(0, issued - nslots); g < issued; g++)
+      mbar_wait_bounded(smem_addr(sm.full + g % nslots), (uint32_t)((g / nslots) & 1), kWaitBudget);
+  }
+}
+
+// ---------------------------------------------------------------- consumers
+
+struct ConsumerCtx {
+  int ctid, lane, cw;  // consumer thread id 0..511, lane, consumer warp 0..15
+  int slot;            // ring slot of the next stage
+  uint32_t phase;      // its full-barrier parity
+  volatile int* s_abort;  // set by consumers when they give up; read by the producer only
+  float* s_red;        // 32 floats of reduction scratch
+  int* s_flag;
+};
+
+SS_DEVINL void cbar() { named_bar_sync(1, kStepConsumers); }
+// Consumer barrier that also ORs a predicate over all consumers: every consumer
+// gets the same answer, so abort decisions never diverge between warps.
+SS_DEVINL bool cbar_any(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n"
+      " barrier.red.or.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "n"(kStepConsumers)
+      : "memory");
+  return r != 0;
+}
+
+// Consumer-block sum; every consumer thread receives the result.
+SS_DEVINL float cblock_sum(float v, ConsumerCtx& cc) {
+  v = warp_sum(v);
+  if (cc.lane == 0) cc.s_red[cc.cw] = v;
+  cbar();
+  float t = 0.0f;
+  for (int w = 0; w < kStepConsumerWarps; w++) t += cc.s_red[w];
+  cbar();
+  return t;
+}
+SS_DEVINL float cblock_max(float v, ConsumerCtx& cc) {
+  v = warp_max(v);
+  if (cc.lane == 0) cc.s_red[cc.cw] = v;
+  cbar();
+  float t = cc.s_red[0];
+  for (int w = 1; w < kStepConsumerWarps; w++) t = fmaxf(t, cc.s_red[w]);
+  cbar();
+  return t;
+}
+
+// Grid barrier: wait until `target` CTA-phase completions were counted.
+SS_DEVINL bool step_grid_wait(const StepParams& p, ConsumerCtx& cc, unsigned target) {
+  bool bad = false;
+  if (cc.ctid == 0) {
+    const long long c0 = clock64();
+    while (true) {
+      const unsigned v = ld_acquire_u32(p.grid_bar);
+      if ((int)(v - target) >= 0) break;
+      if (ld_volatile_u32(p.abort_flag)) { bad = true; break; }
+      if (clock64() - c0 > kWaitBudget) {
+        atomicOr(p.err, 8);
+        atomicExch(p.abort_flag, 1u);
+        bad = true;
+        break;
+      }
+    }
+  }
+  bad = cbar_any(bad);  // the acquire above, then this barrier, order the CTA's reads
+  if (bad && cc.ctid == 0) *cc.s_abort = 1;
+  return !bad;
+}
+// Called by every consumer thread after its last global write of the phase:
+// the consumer barrier orders those writes before thread 0's release-add.
+SS_DEVINL void step_grid_arrive(const StepParams& p, ConsumerCtx& cc) {
+  cbar();
+  if (cc.ctid == 0)
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.grid_bar) : "memory");
+}
+
+// Bounded wait on an mbarrier phase by a whole warp: every lane waits (each
+// needs the barrier's acquire); giving up is a warp vote, so the warp never
+// splits.  Returns false on timeout or when another CTA aborted.
+SS_DEVINL bool warp_wait_phase(const StepParams& p, uint32_t bar, uint32_t par) {
+  if (__all_sync(0xffffffffu, mbar_try_wait(bar, par))) return true;
+  const long long w0 = clock64();
+  while (true) {
+    const bool ok = mbar_try_wait(bar, par);
+    if (__all_sync(0xffffffffu, ok)) return true;
+    const bool late = !ok && (ld_volatile_u32(p.abort_flag) != 0u || clock64() - w0 > kWaitBudget);
+    if (__any_sync(0xffffffffu, late)) {
+      if ((threadIdx.x & 31) == 0) {
+        atomicOr(p.err, 4);
+        atomicExch(p.abort_flag, 1u);
+      }
+      return false;
+    }
+  }
+}
+
+// Block fixed point of the phase's input vector src[nb * 32] into shared
+// memory, consumer thread t building block t (no block is built twice).  With
+// norm_w, RMSNorm first (cpu_neon.c:109-115): ss = sum src^2 (each thread over
+// its block in order, then a warp tree, then the warps in order -- the same in
+// every CTA, so every CTA derives the same scale), scale = 1 / sqrtf(ss / n +
+// eps), x = (src * scale) * w.  Ends with a consumer barrier.
+SS_DEVINL void build_block_planes(const float* src, const float* norm_w, int nb,
+                                                float eps, PlaneBlock* dst, ConsumerCtx& cc) {
+  const int b = cc.ctid;
+  const bool mine = b < nb;
+  float xv[32];
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    const float4 v = mine ? __ldcg(reinterpret_cast<const float4*>(src + b * 32 + i))
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+    xv[i] = v.x; xv[i + 1] = v.y; xv[i + 2] = v.z; xv[i + 3] = v.w;
+  }
+  if (norm_w) {
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; i++) ss = fmaf(xv[i], xv[i], ss);
+    ss = cblock_sum(ss, cc);
+    const float scale = 1.0f / sqrtf(ss / (float)(nb * 32) + eps);
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      const float4 w = mine ? __ldg(reinterpret_cast<const float4*>(norm_w + b * 32 + i))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+      xv[i] = __fmul_rn(__fmul_rn(xv[i], scale), w.x);
+      xv[i + 1] = __fmul_rn(__fmul_rn(xv[i + 1], scale), w.y);
+      xv[i + 2] = __fmul_rn(__fmul_rn(xv[i + 2], scale), w.z);
+      xv[i + 3] = __fmul_rn(__fmul_rn(xv[i + 3], scale), w.w);
+    }
+  }
+  if (mine) {
+    // same digits as make_planes (gemv.cuh), each packed word stored as made
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; j++) amax = fmaxf(amax, fabsf(xv[j]));
+    const bool live = amax >= 1e-30f;
+    const int e = (int)((__float_as_uint(amax) >> 23) & 255u) - 126;
+    const float sc = live ? pow2i(22 - e) : 0.0f;
+    int s0 = 0, s1 = 0, s2 = 0;
+    PlaneBlock* d = dst + b;
+#pragma unroll
+    for (int w = 0; w < 8; w++) {
+      int d0[4], d1[4], d2[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const int m = __float2int_rn(xv[4 * w + i] * sc);
+        d0[i] = sext8(m);
+        const int m1 = (m - d0[i]) >> 8;
+        d1[i] = sext8(m1);
+        d2[i] = (m1 - d1[i]) >> 8;
+        s0 += d0[i];
+        s1 += d1[i];
+        s2 += d2[i];
+      }
+      d->pl[0][w] = (int)pack_low_bytes(d0[0], d0[1], d0[2], d0[3]);
+      d->pl[1][w] = (int)pack_low_bytes(d1[0], d1[1], d1[2], d1[3]);
+      d->pl[2][w] = (int)pack_low_bytes(d2[0], d2[1], d2[2], d2[3]);
+    }
+    d->nsum[0] = -s0;
+    d->nsum[1] = -s1;
+    d->nsum[2] = -s2;
+    d->c0 = live ? pow2i(e - 22) : 0.0f;
+  }
+  cbar();
+}
+
+// Consumes this CTA's tiles of `m` from the ring: red[wl * rows_cta + lr] gets
+// the partial sum of local row lr over the 32 blocks of consumer warp wl of a
+// row group.  Returns rows_cta, or -1 on abort.
+template <int TYPE>
+SS_DEVINL int step_gemv(const StepParams& p, const StepSmem& sm, ConsumerCtx& cc, const TMat& m,
+                        const float* src, const float* norm_w, float* red, int phase) {
+  const int ncta = gridDim.x, cta = blockIdx.x;
+  constexpr int QB = TYPE == kQ4_0 ? 16 : 32;
+  const int nb = m.nb, wpr = step_wpr(nb), RG = kStepConsumerWarps / wpr;
+  const int rg = cc.cw / wpr, wl = cc.cw - rg * wpr;
+  const int blk = wl * 32 + cc.lane;
+  const bool active = rg < RG && blk < nb;
+  int t0, t1;
+  part_range(m.ntiles, cta, ncta, t0, t1);
+  const int rows_cta = (t1 - t0) * kStepTileRows;
+
+  // this thread's block of the input planes, built in shared memory
+  build_block_planes(src, norm_w, nb, p.eps, reinterpret_cast<PlaneBlock*>(red), cc);
+  int pl[3][8];
+  int init[3];
+  float c0;
+  {
+    const int4* sp = reinterpret_cast<const int4*>(reinterpret_cast<const PlaneBlock*>(red) +
+                                                   (active ? blk : 0));
+#pragma unroll
+    for (int p4 = 0; p4 < 6; p4++) {
+      const int4 v = active ? sp[p4] : make_int4(0, 0, 0, 0);
+      pl[p4 >> 1][(p4 & 1) * 4 + 0] = v.x;
+      pl[p4 >> 1][(p4 & 1) * 4 + 1] = v.y;
+      pl[p4 >> 1][(p4 & 1) * 4 + 2] = v.z;
+      pl[p4 >> 1][(p4 & 1) * 4 + 3] = v.w;
+    }
+    const int4 v = active ? sp[6] : make_int4(0, 0, 0, 0);
+    const int zp = TYPE == kQ4_0 ? 8 : 0;
+    init[0] = zp * v.x;  // stored: -sum_j digit_pj
+    init[1] = zp * v.y;
+    init[2] = zp * v.z;
+    c0 = __int_as_float(v.w);
+  }
+  cbar();  // every consumer has its planes before the scratch turns into partial sums
+  bool bad = false;
+
+  const int bsafe = active ? blk : 0;
+  const uint32_t q_off = (uint32_t)(rg * m.tile_bytes + bsafe * QB);
+  const uint32_t s_off = (uint32_t)(rg * m.tile_bytes + kStepTileRows * nb * QB + bsafe * 8);
+  const uint32_t rstride = (uint32_t)(nb * QB);
+  const uint32_t ring0 = smem_addr(sm.ring);
+  const uint32_t slot_bytes = (uint32_t)p.slot_bytes;
+  const int nslots = p.nslots;
+  const bool writer = (cc.lane & 7) == 0;
+  const int my_row = row_of_lane<4>(cc.lane);
+  float* red_w = red + wl * rows_cta + my_row;
+
+  for (int s = 0; t0 + s * RG < t1; s++) {
+    const int slot = cc.slot;
+    const uint32_t par = cc.phase;
+    const uint32_t fb = smem_addr(sm.full + slot);
+    if (!warp_wait_phase(p, fb, par)) {  // leave the loop; every warp still meets the barrier below
+      bad = true;
+      break;
+    }
+    if (cc.ctid == 0 && p.trace) {
+      if (s == 0) trace_mark(p, phase, 4);
+      if (t0 + (s + 1) * RG >= t1) trace_mark(p, phase, 5);
+    }
+    const int tl = s * RG + rg;  // tile of this row group, local to the CTA range
+    const bool has = rg < RG && t0 + tl < t1;
+    const uint32_t st = ring0 + (uint32_t)slot * slot_bytes;
+    uint4 qa[4], qb[4];
+    uint2 scv = make_uint2(0u, 0u);
+    if (has) {
+      asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(scv.x), "=r"(scv.y) : "r"(st + s_off));
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const uint32_t a = st + q_off + (uint32_t)i * rstride;
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(qa[i].x), "=r"(qa[i].y), "=r"(qa[i].z), "=r"(qa[i].w) : "r"(a));
+        if constexpr (TYPE == kQ8_0)
+          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(qb[i].x), "=r"(qb[i].y), "=r"(qb[i].z), "=r"(qb[i].w) : "r"(a + 16));
+      }
+    }
+    __syncwarp();
+    if (cc.lane == 0) mbar_arrive(smem_addr(sm.empty + slot));
+    if (++cc.slot == nslots) { cc.slot = 0; cc.phase ^= 1u; }
+    if (has) {
+      const __half2 h01 = *reinterpret_cast<const __half2*>(&scv.x);
+      const __half2 h23 = *reinterpret_cast<const __half2*>(&scv.y);
+      const float2 d01 = __half22float2(h01), d23 = __half22float2(h23);
+      const float dsc[4] = {d01.x, d01.y, d23.x, d23.y};
+      float acc[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        float r;
+        if constexpr (TYPE == kQ4_0) r = step_dot_q4(qa[i], pl, init);
+        else r = step_dot_q8(qa[i], qb[i], pl);
+        acc[i] = r * (c0 * dsc[i]);
+      }
+      const float v = warp_reduce_rows<4>(acc, cc.lane);
+      if (writer) red_w[tl * kStepTileRows] = v;
+    }
+  }
+  if (cc.ctid == 0) trace_mark(p, phase, 6);
+  bad = cbar_any(bad);  // also: every warp's partial sums are in `red`
+  if (bad) {
+    if (cc.ctid == 0) *cc.s_abort = 1;
+    return -1;
+  }
+  return rows_cta;
+}
+
+SS_DEVINL float row_total(const float* red, int wpr, int rows_cta, int lr) {
+  float s = 0.0f;
+  for (int w = 0; w < wpr; w++) s += red[w * rows_cta + lr];
+  return s;
+}
+
+
+// h[r] += v[r] for the CTA's rows (layer_scheduler.c:484, :566).
+SS_DEVINL void epi_residual(const StepParams& p, ConsumerCtx& cc, const float* red, int wpr,
+                            int rows_cta, int r0) {
+  const int r1 = min(r0 + rows_cta, p.d);
+  for (int r = r0 + cc.ctid; r < r1; r += kStepConsumers)
+    __stcg(p.h + r, __fadd_rn(row_total(red, wpr, rows_cta, r - r0), __ldcg(p.h + r)));
+}
+
+// ---------------------------------------------------------------- attention
+
+// One (kv head, position split) task: encode + append this token's K/V slice
+// of the kv head when the split holds `pos`, scores / softmax / PV over the
+// split's positions for the group's query heads, partial (m, l, o) to global;
+// the last split of the kv head merges them into the attention output.
+template <int HD>
+SS_DEVINL void step_attention_task(const StepParams& p, ConsumerCtx& cc, float* scratch, int layer,
+                                   int pos, int task, float k_scale, float v_scale) {
+  constexpr int DPL = HD / 32;
+  const int G = p.nh / p.nkv;
+  const int kvh = task / p.nsplit, split = task - kvh * p.nsplit;
+  const int seq = pos + 1;
+  const int chunk = (seq + p.nsplit - 1) / p.nsplit;
+  const int t0 = min(split * chunk, seq), t1 = min(t0 + chunk, seq);
+  const int n = t1 - t0;
+  const size_t lrow = (size_t)layer * p.ctx;
+  const int8_t* kc = p.kc + lrow * p.kvd + kvh * HD;
+  const int8_t* vc = p.vc + lrow * p.kvd + kvh * HD;
+  const float* ksl = p.ks + lrow;
+  const float* vsl = p.vs + lrow;
+
+  // scratch: q[G][HD] | scores[G][n] | wsum[16][HD] | kcur, vcur (int8 [HD] each) | ml[2][8]
+  float* q = scratch;
+  float* sc = q + kAttnMaxG * HD;
+  float* wsum = sc + kStepScoreCap;
+  int8_t* kcur = reinterpret_cast<int8_t*>(wsum + kStepConsumerWarps * HD);
+  int8_t* vcur = kcur + HD;
+  float* ml = reinterpret_cast<float*>(vcur + HD);  // m[8], l[8]
+
+  for (int i = cc.ctid; i < G * HD; i += kStepConsumers)
+    q[i] = __ldcg(p.qkv_out + (size_t)kvh * G * HD + i);
+  const bool has_pos = pos >= t0 && pos < t1;
+  if (has_pos) {
+    // kv_turboquant_encode (layer_scheduler.c:101-118) of this kv head's slice
+    const float kinv = k_scale > 0.0f ? 1.0f / k_scale : 0.0f;
+    const float vinv = v_scale > 0.0f ? 1.0f / v_scale : 0.0f;
+    const float* kf = p.qkv_out + p.qd + kvh * HD;
+    const float* vf = kf + p.kvd;
+    for (int i = cc.ctid; i < HD; i += kStepConsumers) {
+      const int8_t kq = kv_encode(__ldcg(kf + i), kinv), vq = kv_encode(__ldcg(vf + i), vinv);
+      kcur[i] = kq;
+      vcur[i] = vq;
+      p.kc[(lrow + pos) * p.kvd + kvh * HD + i] = kq;
+      p.vc[(lrow + pos) * p.kvd + kvh * HD + i] = vq;
+    }
+    if (cc.ctid == 0 && kvh == 0) {
+      p.ks[lrow + pos] = k_scale;
+      p.vs[lrow + pos] = v_scale;
+    }
+  }
+  cbar();
+
+  // scores (layer_scheduler.c:434-444): warp per position, lane owns DPL dims
+  for (int t = t0 + cc.cw; t < t1; t += kStepConsumerWarps) {
+    float kd[DPL];
+    const float ksc = t == pos ? k_scale : ksl[t];
+    const int8_t* kr = t == pos ? kcur : kc + (size_t)t * p.kvd;
+#pragma unroll
+    for (int i = 0; i < DPL; i++) kd[i] = __fmul_rn((float)kr[cc.lane * DPL + i], ksc);
+    for (int g = 0; g < G; g++) {
+      float dsum = 0.0f;
+#pragma unroll
+      for (int i = 0; i < DPL; i++) dsum = fmaf(q[g * HD + cc.lane * DPL + i], kd[i], dsum);
+      dsum = warp_sum(dsum);
+      if (cc.lane == 0) sc[g * n + (t - t0)] = __fmul_rn(dsum, p.attn_scale);
+    }
+  }
+  cbar();
+  // softmax pieces per head (tensor.c:154-173): m, e = exp(s - m), l = sum e
+  if (cc.cw < G) {
+    const int g = cc.cw;
+    float mt = -INFINITY;
+    for (int r = cc.lane; r < n; r += 32) mt = fmaxf(mt, sc[g * n + r]);
+    mt = warp_max(mt);
+    float lt = 0.0f;
+    for (int r = cc.lane; r < n; r += 32) {
+      const float e = expf(sc[g * n + r] - mt);
+      sc[g * n + r] = e;
+      lt += e;
+    }
+    lt = warp_sum(lt);
+    if (cc.lane == 0) { ml[g] = mt; ml[8 + g] = lt; }
+  }
+  cbar();
+  // PV per head: warp over positions, lane over dims, then across warps
+  for (int g = 0; g < G; g++) {
+    float o[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; i++) o[i] = 0.0f;
+    for (int t = t0 + cc.cw; t < t1; t += kStepConsumerWarps) {
+      const float vsc = t == pos ? v_scale : vsl[t];
+      const int8_t* vr = t == pos ? vcur : vc + (size_t)t * p.kvd;
+      const float e = sc[g * n + (t - t0)];
+#pragma unroll
+      for (int i = 0; i < DPL; i++) o[i] = fmaf(e, __fmul_rn((float)vr[cc.lane * DPL + i], vsc), o[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < DPL; i++) wsum[cc.cw * HD + cc.lane * DPL + i] = o[i];
+    cbar();
+    const int qh = kvh * G + g;
+    float* part = p.att_part + ((size_t)qh * p.nsplit + split) * (HD + 2);
+    for (int i = cc.ctid; i < HD; i += kStepConsumers) {
+      float s = 0.0f;
+      for (int w = 0; w < kStepConsumerWarps; w++) s += wsum[w * HD + i];
+      __stcg(part + 2 + i, s);
+    }
+    if (cc.ctid == 0) {
+      __stcg(part, n > 0 ? ml[g] : -INFINITY);
+      __stcg(part + 1, n > 0 ? ml[8 + g] : 0.0f);
+    }
+    cbar();
+  }
+
+  // the last split of this kv head merges the partials
+  __threadfence();
+  cbar();
+  if (cc.ctid == 0) cc.s_flag[0] = atomicAdd(p.cnt_att + kvh, 1u) == (unsigned)(p.nsplit - 1);
+  cbar();
+  if (!cc.s_flag[0]) return;
+  __threadfence();
+  for (int idx = cc.ctid; idx < G * HD; idx += kStepConsumers) {
+    const int g = idx / HD, i = idx - g * HD;
+    const float* base = p.att_part + (size_t)(kvh * G + g) * p.nsplit * (HD + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < p.nsplit; s++) M = fmaxf(M, __ldcg(base + (size_t)s * (HD + 2)));
+    float Ls = 0.0f, O = 0.0f;
+    for (int s = 0; s < p.nsplit; s++) {
+      const float* ps = base + (size_t)s * (HD + 2);
+      const float mr = __ldcg(ps);
+      if (mr == -INFINITY) continue;
+      const float f = expf(mr - M);
+      Ls = fmaf(__ldcg(ps + 1), f, Ls);
+      O = fmaf(__ldcg(ps + 2 + i), f, O);
+    }
+    __stcg(p.attn_out + (size_t)kvh * G * HD + idx, O * (1.0f / Ls));
+  }
+  if (cc.ctid == 0) p.cnt_att[kvh] = 0u;
+}
+
+// ---------------------------------------------------------------- kernel
+
+template <int TYPE, int HTYPE, int HD>
+__global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const StepParams p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ int s_cabort_v;
+  __shared__ float s_red[32];
+  __shared__ int s_flag[4];
+  __shared__ unsigned long long s_best[kStepConsumerWarps];
+  volatile int* s_cabort = &s_cabort_v;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ncta = gridDim.x, cta = blockIdx.x;
+
+  StepSmem sm;
+  sm.ring = smem_raw;
+  sm.full = reinterpret_cast<uint64_t*>(smem_raw + (size_t)p.nslots * p.slot_bytes);
+  sm.empty = sm.full + p.nslots;
+  sm.scratch = reinterpret_cast<float*>(smem_raw + (size_t)p.nslots * p.slot_bytes + 128);
+
+  const int pos = *reinterpret_cast<volatile int*>(p.d_pos);
+  if (pos < 0 || pos >= p.ctx) {
+    if (tid == 0 && cta == 0) atomicOr(p.err, 1);
+    return;  // uniform across the grid: nothing started
+  }
+  if (tid == 0) {
+    s_cabort_v = 0;
+    for (int i = 0; i < p.nslots; i++) {
+      mbar_init(smem_addr(sm.full + i), 1);
+      mbar_init(smem_addr(sm.empty + i), kStepConsumerWarps);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (warp < kStepProducerThreads / 32) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kStepProducerRegs));
+    if (warp == 0) step_producer(p, sm, s_cabort, lane);
+    return;
+  }
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kStepConsumerRegs));
+
+  ConsumerCtx cc;
+  cc.ctid = tid - kStepProducerThreads;
+  cc.lane = lane;
+  cc.cw = warp - kStepProducerThreads / 32;
+  cc.slot = 0;
+  cc.phase = 0;
+  cc.s_abort = s_cabort;
+  cc.s_red = s_red;
+  cc.s_flag = s_flag;
+  float* red = sm.scratch;
+  const int nph = step_phase_count(p.L);
+
+  for (int k = 0; k < nph; k++) {
+    int kind, layer;
+    step_phase(k, p.L, kind, layer);
+    if (k > 0 && !step_grid_wait(p, cc, (unsigned)(k * ncta))) return;
+    if (cc.ctid == 0) trace_mark(p, k, 0);
+
+    if (kind == kPhEmbed) {
+      // h = token_embd[token] (layer_scheduler.c:584-587)
+      int tok = p.seq_tokens[pos];
+      if (tok < 0 || tok >= p.vocab) {
+        if (cc.ctid == 0 && cta == 0) atomicOr(p.err, 2);
+        tok = 0;
+      }
+      const float* row = p.embd + (size_t)tok * p.d;
+      for (int i = cta * kStepConsumers + cc.ctid; i < p.d; i += ncta * kStepConsumers)
+        __stcg(p.h + i, row[i]);
+      if (cc.ctid == 0) trace_mark(p, k, 2);
+      step_grid_arrive(p, cc);
+      continue;
+    }
+
+    if (kind == kPhAtt) {
+      // this position's int8 scales need max |k| / |v| over the whole kv_dim
+      float mk = 0.0f, mv = 0.0f;
+      for (int i = cc.ctid; i < ncta; i += kStepConsumers) {
+        const float2 a = __ldcg(p.amax_part + i);
+        mk = fmaxf(mk, a.x);
+        mv = fmaxf(mv, a.y);
+      }
+      mk = cblock_max(mk, cc);
+      mv = cblock_max(mv, cc);
+      const float k_scale = mk / 127.0f, v_scale = mv / 127.0f;  // layer_scheduler.c:109-110
+      for (int task = cta; task < p.nkv * p.nsplit; task += ncta) {
+        step_attention_task<HD>(p, cc, sm.scratch, layer, pos, task, k_scale, v_scale);
+        cbar();
+      }
+      if (cc.ctid == 0) trace_mark(p, k, 2);
+      step_grid_arrive(p, cc);
+      continue;
+    }
+
+    // ---- matvec phases
+    const TMat m = step_phase_mat(p, kind, layer);
+    // this phase's input: RMSNorm(h) for QKV / GU / lm_head, else the
+    // attention output (O) or the SwiGLU activations (down)
+    const float* src = kind == kPhO ? p.attn_out : kind == kPhDown ? p.act : p.h;
+    const float* nw = kind == kPhQKV  ? p.attn_norm + (size_t)layer * p.d
+                      : kind == kPhGU ? p.ffn_norm + (size_t)layer * p.d
+                      : kind == kPhHead ? p.out_norm : nullptr;
+    int rows_cta;
+    if (kind == kPhHead) rows_cta = step_gemv<HTYPE>(p, sm, cc, m, src, nw, red, k);
+    else rows_cta = step_gemv<TYPE>(p, sm, cc, m, src, nw, red, k);
+    if (rows_cta < 0) return;
+    if (cc.ctid == 0) trace_mark(p, k, 1);
+    const int wpr = step_wpr(m.nb);
+    int t0, t1;
+    part_range(m.ntiles, cta, ncta, t0, t1);
+    const int r0 = t0 * kStepTileRows;
+
+    if (kind == kPhQKV) {
+      // RoPE (non-NeoX, tensor.c:249-274) on q and k rows; |k|, |v| maxima
+      float mk = 0.0f, mv = 0.0f;
+      const int qkv_rows = p.qd + 2 * p.kvd;
+      for (int lp = cc.ctid; 2 * lp < rows_cta; lp += kStepConsumers) {
+        const int r = r0 + 2 * lp;
+        if (r >= qkv_rows) break;
+        float a = row_total(red, wpr, rows_cta, 2 * lp);
+        float b = row_total(red, wpr, rows_cta, 2 * lp + 1);
+        if (r < p.qd + p.kvd) {
+          const int i = r % p.hd;
+          if (i < p.rope_dim) {
+            const float2 cs = p.rope_tab[(size_t)pos * (p.rope_dim >> 1) + (i >> 1)];
+            const float na = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
+            const float nb2 = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
+            a = na;
+            b = nb2;
+          }
+          if (r >= p.qd) mk = fmaxf(mk, fmaxf(fabsf(a), fabsf(b)));
+        } else {
+          mv = fmaxf(mv, fmaxf(fabsf(a), fabsf(b)));
+        }
+        __stcg(p.qkv_out + r, a);
+        __stcg(p.qkv_out + r + 1, b);
+      }
+      mk = cblock_max(mk, cc);
+      mv = cblock_max(mv, cc);
+      if (cc.ctid == 0) __stcg(p.amax_part + cta, make_float2(mk, mv));
+    } else if (kind == kPhO) {
+      epi_residual(p, cc, red, wpr, rows_cta, r0);
+    } else if (kind == kPhGU) {
+      // act = up * g / (1 + expf(-g)) (layer_scheduler.c:533-549)
+      const int a0 = r0 / 2, a1 = min((r0 + rows_cta) / 2, p.ff);
+      for (int j = a0 + cc.ctid; j < a1; j += kStepConsumers) {
+        const int lr = 2 * (j - a0);
+        const float g = row_total(red, wpr, rows_cta, lr);
+        const float u = row_total(red, wpr, rows_cta, lr + 1);
+        __stcg(p.act + j, __fmul_rn(u, __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)))));
+      }
+    } else if (kind == kPhDown) {
+      epi_residual(p, cc, red, wpr, rows_cta, r0);
+    } else {  // kPhHead: logits, greedy argmax (tensor.c:318-328), next token
+      unsigned long long best = 0;
+      const int r1 = min(r0 + rows_cta, p.vocab);
+      for (int r = r0 + cc.ctid; r < r1; r += kStepConsumers) {
+        const float v = row_total(red, wpr, rows_cta, r - r0);
+        __stcg(p.logits + r, v);
+        const unsigned long long pk = pack_argmax(v, r);
+        best = pk > best ? pk : best;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+      }
+      if (lane == 0) s_best[cc.cw] = best;
+      cbar();
+      if (cc.ctid == 0) {
+        unsigned long long b = 0;
+        for (int w = 0; w < kStepConsumerWarps; w++) b = s_best[w] > b ? s_best[w] : b;
+        __stcg(p.am_part + cta, b);
+        __threadfence();
+        s_flag[1] = atomicAdd(p.am_cnt, 1u) == (unsigned)(ncta - 1);
+      }
+      cbar();
+      if (s_flag[1] && cc.cw == 0) {
+        __threadfence();
+        unsigned long long b = 0;
+        for (int i = lane; i < ncta; i += 32) {
+          const unsigned long long v = __ldcg(p.am_part + i);
+          b = v > b ? v : b;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const unsigned long long other = __shfl_xor_sync(0xffffffffu, b, o);
+          b = other > b ? other : b;
+        }
+        if (lane == 0) {
+          const int tok = unpack_argmax_index(b);
+          if (pos + 1 < p.ctx && pos + 1 >= *p.fixed_until) p.seq_tokens[pos + 1] = tok;
+          p.seq_tokens[p.ctx] = tok;
+          *p.d_pos = pos + 1;
+          *p.am_cnt = 0u;
+          *p.grid_bar = 0u;  // every CTA has passed its last grid barrier
+        }
+      }
+      if (cc.ctid == 0) trace_mark(p, k, 2);
+      return;
+    }
+    if (cc.ctid == 0) trace_mark(p, k, 2);
+    step_grid_arrive(p, cc);
+  }
+}
+
+}  // namespace ss

@@ -33,6 +33,7 @@ EXPORTED = [
     "ss_cuda_decode_read", "ss_cuda_stream", "ss_cuda_reset", "ss_cuda_cancel",
     "ss_cuda_dequantize_tensor", "ss_cuda_dequantize", "ss_cuda_kv_row",
     "ss_cuda_time_kernel", "ss_cuda_kernel_bytes", "ss_cuda_argmax_noalloc",
+    "ss_cuda_step_trace",
 ]
 
 
@@ -52,6 +53,8 @@ class Options(ctypes.Structure):
 
 FLAG_NO_PDL = 1
 FLAG_NO_GRAPH = 2
+FLAG_MULTI_KERNEL = 4
+FLAG_TRACE = 8
 
 _lib = None
 
@@ -107,6 +110,7 @@ def load_library() -> ctypes.CDLL:
     lib.ss_cuda_kernel_bytes.argtypes = [vp, ctypes.c_int32]
     lib.ss_cuda_kernel_bytes.restype = ctypes.c_int64
     lib.ss_cuda_argmax_noalloc.argtypes = [vp, ctypes.c_int32, vp, vp]
+    lib.ss_cuda_step_trace.argtypes = [vp, _i64p, ctypes.c_int64]
     _lib = lib
     return lib
 
@@ -216,19 +220,28 @@ class CudaModel:
         return int(self._lib.ss_cuda_stream(self._h) or 0)
 
     def stats(self) -> dict:
-        v = np.zeros(8, np.int64)
-        _check(self._lib.ss_cuda_stats(self._h, v.ctypes.data_as(_i64p), 8))
+        v = np.zeros(10, np.int64)
+        _check(self._lib.ss_cuda_stats(self._h, v.ctypes.data_as(_i64p), 10))
         keys = ("kernels_per_step", "weight_bytes", "kv_bytes", "attn_splits", "pdl",
-                "steps_run", "qkv_ctas", "down_ctas")
+                "steps_run", "qkv_ctas", "down_ctas", "persistent", "ring_slots")
         return {k: int(x) for k, x in zip(keys, v)}
 
-    KERNELS = {"qkv": 0, "attention": 1, "o": 2, "gate_up": 3, "down": 4, "lm_head": 5}
+    KERNELS = {"qkv": 0, "attention": 1, "o": 2, "gate_up": 3, "down": 4, "lm_head": 5, "step": 6}
 
     def time_kernel(self, which: str, iters: int) -> float:
         """Average ms per isolated launch of one step kernel (clobbers state)."""
         ms = np.zeros(1, np.float32)
         _check(self._lib.ss_cuda_time_kernel(self._h, self.KERNELS[which], int(iters), _f(ms)))
         return float(ms[0])
+
+    def step_trace(self) -> np.ndarray:
+        """Timeline of the last persistent step, [phase][cta][event] global-timer
+        ns (context created with FLAG_TRACE; see ss_cuda_step_trace)."""
+        st = self.stats()
+        n = (2 + 5 * self.n_layers) * st["qkv_ctas"] * 8
+        out = np.zeros(n, np.int64)
+        _check(self._lib.ss_cuda_step_trace(self._h, out.ctypes.data_as(_i64p), n))
+        return out.reshape(2 + 5 * self.n_layers, st["qkv_ctas"], 8)
 
     def kernel_bytes(self, which: str) -> int:
         return int(self._lib.ss_cuda_kernel_bytes(self._h, self.KERNELS[which]))

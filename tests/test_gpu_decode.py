@@ -1,7 +1,9 @@
 """GPU decode parity against the reference (golden fixtures made by the
 reference's own CPU path): greedy token IDs identical, logits within 1e-2 of
 max |logit| (or twice the configuration's measured noise floor where that is
-larger, see logit_tol), int8 KV rows within one quantisation step."""
+larger, see logit_tol), int8 KV rows within one quantisation step.  Both step
+implementations are checked: the persistent single kernel (the default) and
+the multi-kernel CUDA graph (SS_CUDA_FLAG_MULTI_KERNEL)."""
 from __future__ import annotations
 
 import numpy as np
@@ -15,6 +17,7 @@ from tests.golden.fingerprint import gguf_fingerprint
 pytestmark = pytest.mark.gpu
 
 LOGIT_RTOL = 1e-2
+PATHS = {"persistent": 0, "multi-kernel": runtime.FLAG_MULTI_KERNEL}
 
 
 def _run(name: str, flags: int = 0):
@@ -23,6 +26,7 @@ def _run(name: str, flags: int = 0):
     path = synth.ensure_gguf(cfg)
     assert gguf_fingerprint(path) == g["fingerprint"].tobytes()
     m = runtime.CudaModel(path, int(g["ctx"]), flags=flags)
+    assert m.stats()["persistent"] == (0 if flags & runtime.FLAG_MULTI_KERNEL else 1)
     prompt = [int(t) for t in g["prompt"]]
     steps = len(g["ids"])
     logits = {}
@@ -67,14 +71,15 @@ def _acceptable_choice(g, step: int, token: int, tol: float) -> bool:
     return float(vals[0] - vals[top.index(token)]) <= tol * float(g["absmax"][step])
 
 
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("name", FIXTURES)
-def test_greedy_parity(name):
+def test_greedy_parity(name, path):
     """Free-running greedy decode: identical to the reference's token IDs; a
     divergence is only accepted at a step where the reference's own top-2 lie
     within the logit tolerance, and the GPU's choice must be acceptable there.
     Logits agree within the tolerance at every recorded step before it."""
     tol = logit_tol(name)
-    g, m, ids, logits = _run(name)
+    g, m, ids, logits = _run(name, PATHS[path])
     ref = [int(t) for t in g["ids"]]
     first = next((i for i, (a, b) in enumerate(zip(ids, ref)) if a != b), len(ref))
     for i, s in enumerate(g["logit_steps"]):
@@ -85,8 +90,9 @@ def test_greedy_parity(name):
     m.close()
 
 
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("name", FIXTURES)
-def test_teacher_forced_parity(name):
+def test_teacher_forced_parity(name, path):
     """Every step fed the reference's own token: the GPU logits at the
     reference's top-4 tokens agree within the tolerance, and the GPU's argmax
     is the reference's at every step whose reference margin exceeds the
@@ -94,9 +100,9 @@ def test_teacher_forced_parity(name):
     tol = logit_tol(name)
     g = load_golden(name)
     cfg = configs.get(name)
-    path = synth.ensure_gguf(cfg)
+    gpath = synth.ensure_gguf(cfg)
     ref = [int(t) for t in g["ids"]]
-    with runtime.CudaModel(path, int(g["ctx"])) as m:
+    with runtime.CudaModel(gpath, int(g["ctx"]), flags=PATHS[path]) as m:
         buf = np.empty(m.vocab, np.float32)
         prompt = [int(t) for t in g["prompt"]]
         got = m.prefill(prompt, 0, logits=buf)
@@ -117,11 +123,12 @@ def test_teacher_forced_parity(name):
                 assert _acceptable_choice(g, s, got, tol), f"step {s}"
 
 
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("name", ["tiny", "tinyllama"])
-def test_device_loop_equals_host_loop(name):
-    """ss_cuda_decode_greedy (tokens fed back on the device, one CUDA graph per
-    step) produces the same tokens as step-by-step ss_cuda_forward."""
-    g, m, ids, _ = _run(name)
+def test_device_loop_equals_host_loop(name, path):
+    """ss_cuda_decode_greedy (tokens fed back on the device, no host round trip
+    between steps) produces the same tokens as step-by-step ss_cuda_forward."""
+    g, m, ids, _ = _run(name, PATHS[path])
     m.reset()
     prompt = [int(t) for t in g["prompt"]]
     first = m.prefill(prompt, 0)
@@ -131,14 +138,38 @@ def test_device_loop_equals_host_loop(name):
 
 
 def test_no_pdl_no_graph_same_result():
-    """PDL/graph chaining changes scheduling only, never results."""
-    _, m1, ids1, lg1 = _run("tiny")
-    _, m2, ids2, lg2 = _run("tiny", flags=runtime.FLAG_NO_PDL | runtime.FLAG_NO_GRAPH)
+    """PDL/graph chaining of the multi-kernel step changes scheduling only,
+    never results."""
+    multi = runtime.FLAG_MULTI_KERNEL
+    _, m1, ids1, lg1 = _run("tiny", flags=multi)
+    _, m2, ids2, lg2 = _run("tiny", flags=multi | runtime.FLAG_NO_PDL | runtime.FLAG_NO_GRAPH)
     assert ids1 == ids2
     for s in lg1:
         np.testing.assert_array_equal(lg1[s], lg2[s])
     m1.close()
     m2.close()
+
+
+@pytest.mark.parametrize("name", ["tiny", "tinyllama"])
+def test_persistent_matches_multi_kernel(name):
+    """The two step implementations agree with each other to fp32 rounding
+    (different summation orders) at every recorded step, on the same tokens."""
+    g = load_golden(name)
+    cfg = configs.get(name)
+    gpath = synth.ensure_gguf(cfg)
+    prompt = [int(t) for t in g["prompt"]]
+    ref = [int(t) for t in g["ids"]]
+    with runtime.CudaModel(gpath, int(g["ctx"])) as a, \
+            runtime.CudaModel(gpath, int(g["ctx"]), flags=runtime.FLAG_MULTI_KERNEL) as b:
+        la = np.empty(a.vocab, np.float32)
+        lb = np.empty(b.vocab, np.float32)
+        a.prefill(prompt, 0, logits=la)
+        b.prefill(prompt, 0, logits=lb)
+        assert rel_err(la, lb) < logit_tol(name)
+        for s in range(1, min(len(ref), 16)):
+            a.forward(ref[s - 1], len(prompt) + s - 1, logits=la)
+            b.forward(ref[s - 1], len(prompt) + s - 1, logits=lb)
+            assert rel_err(la, lb) < logit_tol(name), f"step {s}"
 
 
 def test_scheduler_twins_match_reference_oracle():
@@ -190,9 +221,11 @@ def test_bad_gguf_rejected(tmp_path):
         runtime.CudaModel(str(tmp_path / "missing.gguf"))
 
 
-def test_deterministic_across_runs():
-    _, m1, ids1, lg1 = _run("tiny-q8")
-    _, m2, ids2, lg2 = _run("tiny-q8")
+@pytest.mark.parametrize("name", ["tiny-q8", "tinyllama"])
+def test_deterministic_across_runs(name):
+    """Bitwise-identical logits across runs (no order-dependent atomics)."""
+    _, m1, ids1, lg1 = _run(name)
+    _, m2, ids2, lg2 = _run(name)
     assert ids1 == ids2
     for s in lg1:
         np.testing.assert_array_equal(lg1[s], lg2[s])

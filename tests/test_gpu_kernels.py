@@ -25,16 +25,19 @@ def test_dequant_blocks_bitexact(kind, t):
     np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
+@pytest.mark.parametrize("flags", [0, runtime.FLAG_MULTI_KERNEL], ids=["tiled", "row-interleaved"])
 @pytest.mark.parametrize("name", ["tiny", "tiny-q8"])
-def test_uploaded_tensors_dequantise_bitexact(name):
+def test_uploaded_tensors_dequantise_bitexact(name, flags):
     """Every repacked weight tensor in HBM decodes to exactly the reference
-    dequantisation of the GGUF bytes (covers upload + repack + decode)."""
+    dequantisation of the GGUF bytes (covers upload + repack + decode), in both
+    device layouts: tiled (persistent step) and row-interleaved (multi-kernel)."""
     cfg = configs.get(name)
     path = synth.ensure_gguf(cfg)
     ops = oracle.oracle_ops()
     import ctypes
     from tests.golden.fingerprint import gguf_fingerprint  # noqa: F401
-    with runtime.CudaModel(path, cfg.ctx) as m:
+    with runtime.CudaModel(path, cfg.ctx, flags=flags) as m:
+        assert m.stats()["persistent"] == (0 if flags else 1)
         raw = np.fromfile(path, np.uint8)
         # locate tensors through the oracle's own loader: re-read offsets
         tensors = _tensor_table(path)
