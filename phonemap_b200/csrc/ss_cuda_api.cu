@@ -308,8 +308,8 @@ bool plan_step(Context* c, int htype) {
   CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device));
   if (!coop) return false;
   const int ncta = c->sm_count;
-  const int nsplit = std::max(1, ncta / c->nkv);
-  if ((long long)G * ((c->ctx + nsplit - 1) / nsplit) > kStepScoreCap) return false;
+  const int nsplit = std::max(1, std::min(ncta / c->nkv, kStepMaxSplit));
+  if (c->nkv > ncta || G * c->hd > 2 * kStepConsumers || c->ctx % 4) return false;
   struct Shape { int rows, cols, type; };
   const Shape shapes[5] = {{qd + 2 * kvd, c->d, c->wtype}, {c->d, qd, c->wtype},
                            {2 * c->ff, c->d, c->wtype}, {c->d, c->ff, c->wtype},
@@ -324,8 +324,9 @@ bool plan_step(Context* c, int htype) {
     red = std::max(red, (size_t)wpr * rows_cta * sizeof(float));
   }
   slot = round_up(slot, 128);
-  const size_t att = sizeof(float) * ((size_t)(kAttnMaxG + kStepConsumerWarps) * c->hd + kStepScoreCap + 16) +
-                     2 * (size_t)c->hd;
+  // attention task: q[G][hd] | scores[G][rows per ring stage] | m, l, corr | int8 K/V row
+  const int att_rows = (round_up(slot, 128) - 96) / (2 * c->hd + 8);
+  const size_t att = sizeof(float) * ((size_t)G * c->hd + (size_t)G * att_rows + 24) + 2 * (size_t)c->hd;
   // the scratch also holds a phase's activation planes
   const size_t planes = (size_t)(std::max(std::max(c->d, qd), c->ff) / 32) * sizeof(PlaneBlock);
   const size_t scratch = (std::max(std::max(red, att), planes) + 127) / 128 * 128;
@@ -577,15 +578,13 @@ void alloc_step_state(Context* c) {
   p.act = c->act;
   p.logits = c->logits;
   p.amax_part = dev_alloc<float2>(c, (size_t)ncta);
-  p.att_part = dev_alloc<float>(c, (size_t)c->nh * c->step_nsplit * (c->hd + 2));
-  // counters, zeroed here and by ss_cuda_reset: grid barrier, abort flag,
-  // attention merge counts [nkv]
-  c->step_sync_words = 4 + (size_t)c->nkv;
+  p.att_part = dev_alloc<float>(c, (size_t)c->nh * c->step_nsplit * (c->hd + 4));
+  // counters, zeroed here and by ss_cuda_reset: grid barrier, abort flag
+  c->step_sync_words = 4;
   c->step_sync = dev_alloc<unsigned>(c, c->step_sync_words);
   CK(cudaMemset(c->step_sync, 0, sizeof(unsigned) * c->step_sync_words));
   p.grid_bar = c->step_sync;
   p.abort_flag = c->step_sync + 1;
-  p.cnt_att = c->step_sync + 4;
   p.am_part = c->am_part;
   p.am_cnt = c->am_cnt;
   p.nsplit = c->step_nsplit;

@@ -60,7 +60,7 @@ static_assert(kStepProducerThreads * kStepProducerRegs + kStepConsumers * kStepC
                   kStepThreads * kStepLaunchRegs,
               "register split must equal the launch allocation");
 constexpr int kStepMaxNb = kStepConsumers;               // <= 16384 columns
-constexpr int kStepScoreCap = 4096;                      // attention scores per task
+constexpr int kStepMaxSplit = 4;                         // attention position splits per kv head
 
 // One activation block in block fixed point in shared memory: 112 bytes (7 x
 // 16), no padding -- consumer lane j reads block j with 16-byte loads, and the
@@ -109,8 +109,7 @@ struct StepParams {
   float* act;          // [ff]
   float* logits;       // [vocab]
   float2* amax_part;   // [grid] (max |k|, max |v|) of this position
-  float* att_part;     // [nh][nsplit][hd + 2]: m, l, o[hd]
-  unsigned* cnt_att;   // [nkv] splits done per kv head (the last one merges)
+  float* att_part;     // [nh][nsplit][hd + 4]: m, l, -, -, o[hd] (merged by the O phase)
   unsigned* grid_bar;  // [1]
   unsigned* abort_flag;  // [1]
   unsigned long long* am_part;  // [grid]
@@ -228,11 +227,27 @@ struct StepSmem {
   float* scratch;
 };
 
+// Attention-stage geometry (shared by producer and consumers; layout in the
+// attention section below).
+SS_DEVINL int step_att_rows(int slot_bytes, int hd) { return (slot_bytes - 96) / (2 * hd + 8); }
+SS_DEVINL void step_att_task(const StepParams& p, int task, int pos, int& kvh, int& split, int& t0,
+                             int& t1) {
+  kvh = task / p.nsplit;
+  split = task - kvh * p.nsplit;
+  const int seq = pos + 1;
+  const int chunk = (seq + p.nsplit - 1) / p.nsplit;
+  t0 = min(split * chunk, seq);
+  t1 = min(t0 + chunk, seq);
+}
+// Byte offsets of the scale blocks inside an attention stage.
+SS_DEVINL int step_att_ks_off(int rows, int hd) { return 2 * rows * hd; }
+SS_DEVINL int step_att_vs_off(int rows, int hd) { return 2 * rows * hd + ((rows + 8) * 4 + 15) / 16 * 16; }
+
 // ---------------------------------------------------------------- producer
 
 // `s_cabort` is written by consumers only; the producer just watches it.
 SS_DEVINL void step_producer(const StepParams& p, const StepSmem& sm, const volatile int* s_cabort,
-                             int lane) {
+                             int lane, int pos) {
   if (lane != 0) return;
   const int ncta = gridDim.x, cta = blockIdx.x;
   const int nph = step_phase_count(p.L);
@@ -264,9 +279,67 @@ SS_DEVINL void step_producer(const StepParams& p, const StepSmem& sm, const vola
   };
   prefetch_phase(1);
   bool aborted = false;
+  // Waits until the next slot may be filled (its previous stage released, and
+  // the stage `inflight` back landed); returns its full barrier, or 0 on abort.
+  auto acquire_slot = [&]() -> uint32_t {
+    const uint32_t fb = smem_addr(sm.full + slot), eb = smem_addr(sm.empty + slot);
+    auto wait = [&](uint32_t bar, uint32_t par) {
+      if (mbar_try_wait(bar, par)) return true;
+      const long long c0 = clock64();
+      while (!mbar_try_wait(bar, par)) {
+        if (*s_cabort || ld_volatile_u32(p.abort_flag)) return false;
+        if (clock64() - c0 > kWaitBudget) {
+          atomicOr(p.err, 4);
+          atomicExch(p.abort_flag, 1u);
+          return false;
+        }
+      }
+      return true;
+    };
+    if (wraps > 0 && !wait(eb, (wraps - 1) & 1u)) return 0u;
+    if (issued >= inflight) {
+      if (!wait(smem_addr(sm.full + lslot), lwraps & 1u)) return 0u;
+      if (++lslot == nslots) { lslot = 0; lwraps++; }
+    }
+    return fb;
+  };
+  auto advance = [&]() {
+    issued++;
+    if (++slot == nslots) { slot = 0; wraps++; }
+  };
   for (int k = 1; k < nph && !aborted; k++) {
     int kind, layer;
     step_phase(k, p.L, kind, layer);
+    if (kind == kPhAtt) {
+      // this CTA's attention task(s): the cached K / V rows and scales
+      const int R = step_att_rows(p.slot_bytes, p.hd);
+      const size_t lrow = (size_t)layer * p.ctx;
+      for (int task = cta; task < p.nkv * p.nsplit && !aborted; task += ncta) {
+        int kvh, split, t0, t1;
+        step_att_task(p, task, pos, kvh, split, t0, t1);
+        const int tend = min(t1, pos);
+        for (int ts = t0; ts < tend; ts += R) {
+          const int te = min(ts + R, tend), nr = te - ts;
+          const uint32_t fb = acquire_slot();
+          if (!fb) { aborted = true; break; }
+          const int sa = ts & ~3, sb = (te + 3) & ~3;
+          const uint32_t sbytes = (uint32_t)((sb - sa) * 4);
+          mbar_expect_tx(fb, (uint32_t)(2 * nr * p.hd) + 2 * sbytes);
+          const uint32_t dst = ring0 + (uint32_t)slot * slot_bytes;
+          const int8_t* kr = p.kc + (lrow + ts) * p.kvd + kvh * p.hd;
+          const int8_t* vr = p.vc + (lrow + ts) * p.kvd + kvh * p.hd;
+          for (int r = 0; r < nr; r++) {
+            bulk_g2s(dst + (uint32_t)(r * p.hd), kr + (size_t)r * p.kvd, (uint32_t)p.hd, fb);
+            bulk_g2s(dst + (uint32_t)((R + r) * p.hd), vr + (size_t)r * p.kvd, (uint32_t)p.hd, fb);
+          }
+          bulk_g2s(dst + (uint32_t)step_att_ks_off(R, p.hd), p.ks + lrow + sa, sbytes, fb);
+          bulk_g2s(dst + (uint32_t)step_att_vs_off(R, p.hd), p.vs + lrow + sa, sbytes, fb);
+          advance();
+        }
+      }
+      trace_mark(p, k, 3);
+      continue;
+    }
     if (!step_phase_has_mat(kind)) continue;
     const TMat mv = step_phase_mat(p, kind, layer);
     const TMat* m = &mv;
@@ -279,46 +352,13 @@ SS_DEVINL void step_producer(const StepParams& p, const StepSmem& sm, const vola
     const int rg = step_rg(m->nb);
     for (int t = t0; t < t1; t += rg) {
       if (t == t0) trace_mark(p, k, 7);
-      const uint32_t fb = smem_addr(sm.full + slot), eb = smem_addr(sm.empty + slot);
-      if (wraps > 0) {  // the slot's previous stage must have been released
-        const uint32_t par = (wraps - 1) & 1u;
-        bool ok = mbar_try_wait(eb, par);
-        if (!ok) {
-          const long long c0 = clock64();
-          while (!(ok = mbar_try_wait(eb, par))) {
-            if (*s_cabort || ld_volatile_u32(p.abort_flag)) break;
-            if (clock64() - c0 > kWaitBudget) {
-              atomicOr(p.err, 4);
-              atomicExch(p.abort_flag, 1u);
-              break;
-            }
-          }
-        }
-        if (!ok) { aborted = true; break; }
-      }
-      if (issued >= inflight) {
-        const uint32_t lb = smem_addr(sm.full + lslot), lpar = lwraps & 1u;
-        bool ok = mbar_try_wait(lb, lpar);
-        if (!ok) {
-          const long long c0 = clock64();
-          while (!(ok = mbar_try_wait(lb, lpar))) {
-            if (*s_cabort || ld_volatile_u32(p.abort_flag)) break;
-            if (clock64() - c0 > kWaitBudget) {
-              atomicOr(p.err, 4);
-              atomicExch(p.abort_flag, 1u);
-              break;
-            }
-          }
-        }
-        if (!ok) { aborted = true; break; }
-        if (++lslot == nslots) { lslot = 0; lwraps++; }
-      }
+      const uint32_t fb = acquire_slot();
+      if (!fb) { aborted = true; break; }
       const int nt = min(rg, t1 - t);
       const uint32_t bytes = (uint32_t)(nt * m->tile_bytes);
       mbar_expect_tx(fb, bytes);
       bulk_g2s(ring0 + (uint32_t)slot * slot_bytes, m->w + (size_t)t * m->tile_bytes, bytes, fb);
-      issued++;
-      if (++slot == nslots) { slot = 0; wraps++; }
+      advance();
     }
     trace_mark(p, k, 3);
   }
@@ -424,31 +464,94 @@ SS_DEVINL bool warp_wait_phase(const StepParams& p, uint32_t bar, uint32_t par) 
 }
 
 // Block fixed point of the phase's input vector src[nb * 32] into shared
-// memory, consumer thread t building block t (no block is built twice).  With
-// norm_w, RMSNorm first (cpu_neon.c:109-115): ss = sum src^2 (each thread over
-// its block in order, then a warp tree, then the warps in order -- the same in
-// every CTA, so every CTA derives the same scale), scale = 1 / sqrtf(ss / n +
-// eps), x = (src * scale) * w.  Ends with a consumer barrier.
-SS_DEVINL void build_block_planes(const float* src, const float* norm_w, int nb,
-                                                float eps, PlaneBlock* dst, ConsumerCtx& cc) {
-  const int b = cc.ctid;
+// memory: TPB consecutive consumer threads build one block together, each
+// converting 32 / TPB elements (the block maximum and the digit sums are
+// combined over the group with shuffles), so no block is built twice and all
+// consumers share the work.  With norm_w, RMSNorm first (cpu_neon.c:109-115):
+// ss = sum src^2 (each thread over its elements in order, then a warp tree,
+// then the warps in order -- the same in every CTA, so every CTA derives the
+// same scale), scale = 1 / sqrtf(ss / n + eps), x = (src * scale) * w.  The
+// digits are those of make_planes (gemv.cuh).  Ends with a consumer barrier.
+//
+// With `att` (the O phase), the input is the attention output, merged here
+// from the position splits' partials (m, l, o): M = max m_s, f_s = e^(m_s-M),
+// out = sum_s f_s o_s / sum_s f_s l_s.
+template <int TPB>
+SS_DEVINL void build_block_planes_t(const float* src, const float* norm_w, const float* att,
+                                    int nsplit, int hd, int nb, float eps, PlaneBlock* dst,
+                                    ConsumerCtx& cc) {
+  constexpr int EPT = 32 / TPB;  // elements per thread
+  constexpr int WPT = EPT / 4;   // packed words per plane per thread
+  const int b = cc.ctid / TPB, q = cc.ctid % TPB;
   const bool mine = b < nb;
-  float xv[32];
+  const int base = b * 32 + q * EPT;
+  float xv[EPT];
+  if (att) {
 #pragma unroll
-  for (int i = 0; i < 32; i += 4) {
-    const float4 v = mine ? __ldcg(reinterpret_cast<const float4*>(src + b * 32 + i))
-                          : make_float4(0.f, 0.f, 0.f, 0.f);
-    xv[i] = v.x; xv[i + 1] = v.y; xv[i + 2] = v.z; xv[i + 3] = v.w;
+    for (int j = 0; j < EPT; j++) xv[j] = 0.0f;
+    if (mine) {
+      // per chunk of 8 elements: all loads first (nsplit <= kStepMaxSplit),
+      // then the merge in split order
+      const int qh = base / hd, i0 = base - qh * hd;  // EPT <= 32 <= hd: one head
+      const float* pb = att + (size_t)qh * nsplit * (hd + 4);
+      float ms[kStepMaxSplit], ls[kStepMaxSplit];
+#pragma unroll
+      for (int sp = 0; sp < kStepMaxSplit; sp++) {
+        ms[sp] = sp < nsplit ? __ldcg(pb + (size_t)sp * (hd + 4)) : -INFINITY;
+        ls[sp] = sp < nsplit ? __ldcg(pb + (size_t)sp * (hd + 4) + 1) : 0.0f;
+      }
+      float M = -INFINITY;
+#pragma unroll
+      for (int sp = 0; sp < kStepMaxSplit; sp++) M = fmaxf(M, ms[sp]);
+      float f[kStepMaxSplit];
+      float L = 0.0f;
+#pragma unroll
+      for (int sp = 0; sp < kStepMaxSplit; sp++) {
+        f[sp] = ms[sp] == -INFINITY ? 0.0f : expf(ms[sp] - M);
+        if (ms[sp] != -INFINITY) L = fmaf(ls[sp], f[sp], L);
+      }
+      const float inv = 1.0f / L;
+#pragma unroll
+      for (int c8 = 0; c8 < EPT; c8 += 8) {
+        float4 ov[kStepMaxSplit][2];
+#pragma unroll
+        for (int sp = 0; sp < kStepMaxSplit; sp++)
+#pragma unroll
+          for (int j = 0; j < 2; j++)
+            ov[sp][j] = sp < nsplit ? __ldcg(reinterpret_cast<const float4*>(pb + (size_t)sp * (hd + 4) + 4 + i0 + c8) + j)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int sp = 0; sp < kStepMaxSplit; sp++) {
+          if (ms[sp] == -INFINITY) continue;
+#pragma unroll
+          for (int j = 0; j < 2; j++) {
+            xv[c8 + 4 * j] = fmaf(ov[sp][j].x, f[sp], xv[c8 + 4 * j]);
+            xv[c8 + 4 * j + 1] = fmaf(ov[sp][j].y, f[sp], xv[c8 + 4 * j + 1]);
+            xv[c8 + 4 * j + 2] = fmaf(ov[sp][j].z, f[sp], xv[c8 + 4 * j + 2]);
+            xv[c8 + 4 * j + 3] = fmaf(ov[sp][j].w, f[sp], xv[c8 + 4 * j + 3]);
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < EPT; j++) xv[j] = xv[j] * inv;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < EPT; i += 4) {
+      const float4 v = mine ? __ldcg(reinterpret_cast<const float4*>(src + base + i))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+      xv[i] = v.x; xv[i + 1] = v.y; xv[i + 2] = v.z; xv[i + 3] = v.w;
+    }
   }
   if (norm_w) {
     float ss = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 32; i++) ss = fmaf(xv[i], xv[i], ss);
+    for (int i = 0; i < EPT; i++) ss = fmaf(xv[i], xv[i], ss);
     ss = cblock_sum(ss, cc);
     const float scale = 1.0f / sqrtf(ss / (float)(nb * 32) + eps);
 #pragma unroll
-    for (int i = 0; i < 32; i += 4) {
-      const float4 w = mine ? __ldg(reinterpret_cast<const float4*>(norm_w + b * 32 + i))
+    for (int i = 0; i < EPT; i += 4) {
+      const float4 w = mine ? __ldg(reinterpret_cast<const float4*>(norm_w + base + i))
                             : make_float4(0.f, 0.f, 0.f, 0.f);
       xv[i] = __fmul_rn(__fmul_rn(xv[i], scale), w.x);
       xv[i + 1] = __fmul_rn(__fmul_rn(xv[i + 1], scale), w.y);
@@ -456,40 +559,59 @@ SS_DEVINL void build_block_planes(const float* src, const float* norm_w, int nb,
       xv[i + 3] = __fmul_rn(__fmul_rn(xv[i + 3], scale), w.w);
     }
   }
-  if (mine) {
-    // same digits as make_planes (gemv.cuh), each packed word stored as made
-    float amax = 0.0f;
+  float amax = 0.0f;
 #pragma unroll
-    for (int j = 0; j < 32; j++) amax = fmaxf(amax, fabsf(xv[j]));
-    const bool live = amax >= 1e-30f;
-    const int e = (int)((__float_as_uint(amax) >> 23) & 255u) - 126;
-    const float sc = live ? pow2i(22 - e) : 0.0f;
-    int s0 = 0, s1 = 0, s2 = 0;
-    PlaneBlock* d = dst + b;
+  for (int j = 0; j < EPT; j++) amax = fmaxf(amax, fabsf(xv[j]));
 #pragma unroll
-    for (int w = 0; w < 8; w++) {
-      int d0[4], d1[4], d2[4];
+  for (int o = 1; o < TPB; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const bool live = amax >= 1e-30f;
+  const int e = (int)((__float_as_uint(amax) >> 23) & 255u) - 126;
+  const float sc = live ? pow2i(22 - e) : 0.0f;
+  int s0 = 0, s1 = 0, s2 = 0;
+  PlaneBlock* d = dst + b;
 #pragma unroll
-      for (int i = 0; i < 4; i++) {
-        const int m = __float2int_rn(xv[4 * w + i] * sc);
-        d0[i] = sext8(m);
-        const int m1 = (m - d0[i]) >> 8;
-        d1[i] = sext8(m1);
-        d2[i] = (m1 - d1[i]) >> 8;
-        s0 += d0[i];
-        s1 += d1[i];
-        s2 += d2[i];
-      }
-      d->pl[0][w] = (int)pack_low_bytes(d0[0], d0[1], d0[2], d0[3]);
-      d->pl[1][w] = (int)pack_low_bytes(d1[0], d1[1], d1[2], d1[3]);
-      d->pl[2][w] = (int)pack_low_bytes(d2[0], d2[1], d2[2], d2[3]);
+  for (int w = 0; w < WPT; w++) {
+    int d0[4], d1[4], d2[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int m = __float2int_rn(xv[4 * w + i] * sc);
+      d0[i] = sext8(m);
+      const int m1 = (m - d0[i]) >> 8;
+      d1[i] = sext8(m1);
+      d2[i] = (m1 - d1[i]) >> 8;
+      s0 += d0[i];
+      s1 += d1[i];
+      s2 += d2[i];
     }
+    if (mine) {
+      d->pl[0][q * WPT + w] = (int)pack_low_bytes(d0[0], d0[1], d0[2], d0[3]);
+      d->pl[1][q * WPT + w] = (int)pack_low_bytes(d1[0], d1[1], d1[2], d1[3]);
+      d->pl[2][q * WPT + w] = (int)pack_low_bytes(d2[0], d2[1], d2[2], d2[3]);
+    }
+  }
+#pragma unroll
+  for (int o = 1; o < TPB; o <<= 1) {
+    s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+    s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+  }
+  if (mine && q == 0) {
     d->nsum[0] = -s0;
     d->nsum[1] = -s1;
     d->nsum[2] = -s2;
     d->c0 = live ? pow2i(e - 22) : 0.0f;
   }
   cbar();
+}
+SS_DEVINL void build_block_planes(const float* src, const float* norm_w, const float* att,
+                                  int nsplit, int hd, int nb, float eps, PlaneBlock* dst,
+                                  ConsumerCtx& cc) {
+  if (nb * 4 <= kStepConsumers)
+    build_block_planes_t<4>(src, norm_w, att, nsplit, hd, nb, eps, dst, cc);
+  else if (nb * 2 <= kStepConsumers)
+    build_block_planes_t<2>(src, norm_w, att, nsplit, hd, nb, eps, dst, cc);
+  else
+    build_block_planes_t<1>(src, norm_w, att, nsplit, hd, nb, eps, dst, cc);
 }
 
 // Consumes this CTA's tiles of `m` from the ring: red[wl * rows_cta + lr] gets
@@ -509,7 +631,8 @@ SS_DEVINL int step_gemv(const StepParams& p, const StepSmem& sm, ConsumerCtx& cc
   const int rows_cta = (t1 - t0) * kStepTileRows;
 
   // this thread's block of the input planes, built in shared memory
-  build_block_planes(src, norm_w, nb, p.eps, reinterpret_cast<PlaneBlock*>(red), cc);
+  build_block_planes(src, norm_w, src == nullptr ? p.att_part : nullptr, p.nsplit, p.hd, nb, p.eps,
+                     reinterpret_cast<PlaneBlock*>(red), cc);
   int pl[3][8];
   int init[3];
   float c0;
@@ -619,37 +742,100 @@ SS_DEVINL void epi_residual(const StepParams& p, ConsumerCtx& cc, const float* r
 }
 
 // ---------------------------------------------------------------- attention
+//
+// Task (kv head kvh, position split): positions [t0, t1) of 0..pos split
+// evenly over nsplit tasks.  The cached rows t < pos of the split never change
+// during a step, so the producer streams them into the ring while the QKV
+// phase runs, in "attention stages" of up to step_att_rows rows:
+//   [K rows: rows x HD int8][V rows][K scales][V scales]
+// each scale block covering positions ts & ~3 .. (te + 3) & ~3 (16-byte aligned
+// copies).  Row `pos` is this step's own K/V, encoded from the QKV output.
 
-// One (kv head, position split) task: encode + append this token's K/V slice
-// of the kv head when the split holds `pos`, scores / softmax / PV over the
-// split's positions for the group's query heads, partial (m, l, o) to global;
-// the last split of the kv head merges them into the attention output.
+// Scores, online-softmax update and PV for `nr` rows whose int8 K / V (row
+// stride HD) and scales are in shared memory (layer_scheduler.c:415-468,
+// softmax tensor.c:154-173 in online form: running max m, sum l, o).  Every
+// consumer calls it; `sc` holds the group's scores, `ml` m[8], l[8], corr[8].
 template <int HD>
-SS_DEVINL void step_attention_task(const StepParams& p, ConsumerCtx& cc, float* scratch, int layer,
-                                   int pos, int task, float k_scale, float v_scale) {
+SS_DEVINL void att_rows(const StepParams& p, ConsumerCtx& cc, const int8_t* K, const int8_t* V,
+                        const float* ksc, const float* vsc, int nr, const float* q, float* sc,
+                        int scs, float* ml, int G, float (&o)[2]) {
   constexpr int DPL = HD / 32;
+  for (int r = cc.cw; r < nr; r += kStepConsumerWarps) {
+    float kd[DPL];
+    const float s = ksc[r];
+#pragma unroll
+    for (int i = 0; i < DPL; i++) kd[i] = __fmul_rn((float)K[r * HD + cc.lane * DPL + i], s);
+    for (int g = 0; g < G; g++) {
+      float dsum = 0.0f;
+#pragma unroll
+      for (int i = 0; i < DPL; i++) dsum = fmaf(q[g * HD + cc.lane * DPL + i], kd[i], dsum);
+      dsum = warp_sum(dsum);
+      if (cc.lane == 0) sc[g * scs + r] = __fmul_rn(dsum, p.attn_scale);
+    }
+  }
+  cbar();
+  if (cc.cw < G) {
+    const int g = cc.cw;
+    float mt = -INFINITY;
+    for (int r = cc.lane; r < nr; r += 32) mt = fmaxf(mt, sc[g * scs + r]);
+    mt = warp_max(mt);
+    const float mold = ml[g];
+    const float mnew = fmaxf(mold, mt);
+    float lt = 0.0f;
+    for (int r = cc.lane; r < nr; r += 32) {
+      const float e = expf(sc[g * scs + r] - mnew);
+      sc[g * scs + r] = e;
+      lt += e;
+    }
+    lt = warp_sum(lt);
+    if (cc.lane == 0) {
+      const float c = mold == -INFINITY ? 0.0f : expf(mold - mnew);
+      ml[16 + g] = c;
+      ml[8 + g] = fmaf(ml[8 + g], c, lt);
+      ml[g] = mnew;
+    }
+  }
+  cbar();
+#pragma unroll
+  for (int k = 0; k < 2; k++) {
+    const int item = cc.ctid + k * kStepConsumers;
+    if (item < G * HD) {
+      const int g = item / HD, i = item - g * HD;
+      float acc = o[k] * ml[16 + g];
+      for (int r = 0; r < nr; r++)
+        acc = fmaf(sc[g * scs + r], __fmul_rn((float)V[r * HD + i], vsc[r]), acc);
+      o[k] = acc;
+    }
+  }
+}
+
+// One task: append this token's K/V slice of the kv head when the split holds
+// `pos`, attention over the split's positions (ring stages, then row pos) for
+// the group's query heads, partial (m, l, o) to att_part.  The O phase merges
+// the splits.  Returns false on abort.
+template <int HD>
+SS_DEVINL bool step_attention_task(const StepParams& p, const StepSmem& sm, ConsumerCtx& cc,
+                                   float* scratch, int layer, int pos, int task, float k_scale,
+                                   float v_scale) {
   const int G = p.nh / p.nkv;
-  const int kvh = task / p.nsplit, split = task - kvh * p.nsplit;
-  const int seq = pos + 1;
-  const int chunk = (seq + p.nsplit - 1) / p.nsplit;
-  const int t0 = min(split * chunk, seq), t1 = min(t0 + chunk, seq);
-  const int n = t1 - t0;
+  int kvh, split, t0, t1;
+  step_att_task(p, task, pos, kvh, split, t0, t1);
+  const int tend = min(t1, pos);  // cached rows [t0, tend); row pos separately
+  const int R = step_att_rows(p.slot_bytes, HD);
   const size_t lrow = (size_t)layer * p.ctx;
-  const int8_t* kc = p.kc + lrow * p.kvd + kvh * HD;
-  const int8_t* vc = p.vc + lrow * p.kvd + kvh * HD;
-  const float* ksl = p.ks + lrow;
-  const float* vsl = p.vs + lrow;
 
-  // scratch: q[G][HD] | scores[G][n] | wsum[16][HD] | kcur, vcur (int8 [HD] each) | ml[2][8]
+  // scratch: q[G][HD] | sc[G][R] | ml[24] | kcur[HD], vcur[HD] (int8)
   float* q = scratch;
-  float* sc = q + kAttnMaxG * HD;
-  float* wsum = sc + kStepScoreCap;
-  int8_t* kcur = reinterpret_cast<int8_t*>(wsum + kStepConsumerWarps * HD);
+  float* sc = q + G * HD;
+  float* ml = sc + G * R;
+  int8_t* kcur = reinterpret_cast<int8_t*>(ml + 24);
   int8_t* vcur = kcur + HD;
-  float* ml = reinterpret_cast<float*>(vcur + HD);  // m[8], l[8]
-
   for (int i = cc.ctid; i < G * HD; i += kStepConsumers)
     q[i] = __ldcg(p.qkv_out + (size_t)kvh * G * HD + i);
+  if (cc.ctid < 8) {
+    ml[cc.ctid] = -INFINITY;
+    ml[8 + cc.ctid] = 0.0f;
+  }
   const bool has_pos = pos >= t0 && pos < t1;
   if (has_pos) {
     // kv_turboquant_encode (layer_scheduler.c:101-118) of this kv head's slice
@@ -671,91 +857,48 @@ SS_DEVINL void step_attention_task(const StepParams& p, ConsumerCtx& cc, float* 
   }
   cbar();
 
-  // scores (layer_scheduler.c:434-444): warp per position, lane owns DPL dims
-  for (int t = t0 + cc.cw; t < t1; t += kStepConsumerWarps) {
-    float kd[DPL];
-    const float ksc = t == pos ? k_scale : ksl[t];
-    const int8_t* kr = t == pos ? kcur : kc + (size_t)t * p.kvd;
-#pragma unroll
-    for (int i = 0; i < DPL; i++) kd[i] = __fmul_rn((float)kr[cc.lane * DPL + i], ksc);
-    for (int g = 0; g < G; g++) {
-      float dsum = 0.0f;
-#pragma unroll
-      for (int i = 0; i < DPL; i++) dsum = fmaf(q[g * HD + cc.lane * DPL + i], kd[i], dsum);
-      dsum = warp_sum(dsum);
-      if (cc.lane == 0) sc[g * n + (t - t0)] = __fmul_rn(dsum, p.attn_scale);
+  float o[2] = {0.0f, 0.0f};
+  const uint32_t ring0 = smem_addr(sm.ring);
+  bool bad = false;
+  for (int ts = t0; ts < tend; ts += R) {
+    const int nr = min(R, tend - ts);
+    // every warp agrees before att_rows (which has consumer barriers)
+    if (cbar_any(!warp_wait_phase(p, smem_addr(sm.full + cc.slot), cc.phase))) {
+      bad = true;
+      break;
     }
+    const uint8_t* st = sm.ring + (size_t)cc.slot * p.slot_bytes;
+    const int8_t* K = reinterpret_cast<const int8_t*>(st);
+    const int8_t* V = K + R * HD;
+    const int sa = ts & ~3;
+    const float* ksc = reinterpret_cast<const float*>(st + step_att_ks_off(R, HD)) + (ts - sa);
+    const float* vsc = reinterpret_cast<const float*>(st + step_att_vs_off(R, HD)) + (ts - sa);
+    att_rows<HD>(p, cc, K, V, ksc, vsc, nr, q, sc, R, ml, G, o);
+    __syncwarp();
+    if (cc.lane == 0) mbar_arrive(smem_addr(sm.empty + cc.slot));
+    if (++cc.slot == p.nslots) { cc.slot = 0; cc.phase ^= 1u; }
+    cbar();  // scores of this stage consumed before the next overwrites them
   }
-  cbar();
-  // softmax pieces per head (tensor.c:154-173): m, e = exp(s - m), l = sum e
-  if (cc.cw < G) {
-    const int g = cc.cw;
-    float mt = -INFINITY;
-    for (int r = cc.lane; r < n; r += 32) mt = fmaxf(mt, sc[g * n + r]);
-    mt = warp_max(mt);
-    float lt = 0.0f;
-    for (int r = cc.lane; r < n; r += 32) {
-      const float e = expf(sc[g * n + r] - mt);
-      sc[g * n + r] = e;
-      lt += e;
-    }
-    lt = warp_sum(lt);
-    if (cc.lane == 0) { ml[g] = mt; ml[8 + g] = lt; }
-  }
-  cbar();
-  // PV per head: warp over positions, lane over dims, then across warps
-  for (int g = 0; g < G; g++) {
-    float o[DPL];
-#pragma unroll
-    for (int i = 0; i < DPL; i++) o[i] = 0.0f;
-    for (int t = t0 + cc.cw; t < t1; t += kStepConsumerWarps) {
-      const float vsc = t == pos ? v_scale : vsl[t];
-      const int8_t* vr = t == pos ? vcur : vc + (size_t)t * p.kvd;
-      const float e = sc[g * n + (t - t0)];
-#pragma unroll
-      for (int i = 0; i < DPL; i++) o[i] = fmaf(e, __fmul_rn((float)vr[cc.lane * DPL + i], vsc), o[i]);
-    }
-#pragma unroll
-    for (int i = 0; i < DPL; i++) wsum[cc.cw * HD + cc.lane * DPL + i] = o[i];
-    cbar();
-    const int qh = kvh * G + g;
-    float* part = p.att_part + ((size_t)qh * p.nsplit + split) * (HD + 2);
-    for (int i = cc.ctid; i < HD; i += kStepConsumers) {
-      float s = 0.0f;
-      for (int w = 0; w < kStepConsumerWarps; w++) s += wsum[w * HD + i];
-      __stcg(part + 2 + i, s);
-    }
-    if (cc.ctid == 0) {
-      __stcg(part, n > 0 ? ml[g] : -INFINITY);
-      __stcg(part + 1, n > 0 ? ml[8 + g] : 0.0f);
-    }
+  (void)ring0;
+  if (bad) return false;
+  if (has_pos) {
+    att_rows<HD>(p, cc, kcur, vcur, &k_scale, &v_scale, 1, q, sc, R, ml, G, o);
     cbar();
   }
-
-  // the last split of this kv head merges the partials
-  __threadfence();
-  cbar();
-  if (cc.ctid == 0) cc.s_flag[0] = atomicAdd(p.cnt_att + kvh, 1u) == (unsigned)(p.nsplit - 1);
-  cbar();
-  if (!cc.s_flag[0]) return;
-  __threadfence();
-  for (int idx = cc.ctid; idx < G * HD; idx += kStepConsumers) {
-    const int g = idx / HD, i = idx - g * HD;
-    const float* base = p.att_part + (size_t)(kvh * G + g) * p.nsplit * (HD + 2);
-    float M = -INFINITY;
-    for (int s = 0; s < p.nsplit; s++) M = fmaxf(M, __ldcg(base + (size_t)s * (HD + 2)));
-    float Ls = 0.0f, O = 0.0f;
-    for (int s = 0; s < p.nsplit; s++) {
-      const float* ps = base + (size_t)s * (HD + 2);
-      const float mr = __ldcg(ps);
-      if (mr == -INFINITY) continue;
-      const float f = expf(mr - M);
-      Ls = fmaf(__ldcg(ps + 1), f, Ls);
-      O = fmaf(__ldcg(ps + 2 + i), f, O);
+#pragma unroll
+  for (int k = 0; k < 2; k++) {
+    const int item = cc.ctid + k * kStepConsumers;
+    if (item < G * HD) {
+      const int g = item / HD, i = item - g * HD;
+      float* part = p.att_part + ((size_t)(kvh * G + g) * p.nsplit + split) * (HD + 4);
+      __stcg(part + 4 + i, o[k]);
+      if (i == 0) {
+        __stcg(part, ml[g]);
+        __stcg(part + 1, ml[8 + g]);
+      }
     }
-    __stcg(p.attn_out + (size_t)kvh * G * HD + idx, O * (1.0f / Ls));
   }
-  if (cc.ctid == 0) p.cnt_att[kvh] = 0u;
+  return true;
 }
 
 // ---------------------------------------------------------------- kernel
@@ -794,7 +937,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
 
   if (warp < kStepProducerThreads / 32) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kStepProducerRegs));
-    if (warp == 0) step_producer(p, sm, s_cabort, lane);
+    if (warp == 0) step_producer(p, sm, s_cabort, lane, pos);
     return;
   }
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kStepConsumerRegs));
@@ -840,12 +983,25 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         mk = fmaxf(mk, a.x);
         mv = fmaxf(mv, a.y);
       }
-      mk = cblock_max(mk, cc);
-      mv = cblock_max(mv, cc);
+      mk = warp_max(mk);
+      mv = warp_max(mv);
+      if (cc.lane == 0) { s_red[cc.cw] = mk; s_red[16 + cc.cw] = mv; }
+      cbar();
+      mk = 0.0f;
+      mv = 0.0f;
+      for (int w = 0; w < kStepConsumerWarps; w++) {
+        mk = fmaxf(mk, s_red[w]);
+        mv = fmaxf(mv, s_red[16 + w]);
+      }
       const float k_scale = mk / 127.0f, v_scale = mv / 127.0f;  // layer_scheduler.c:109-110
-      for (int task = cta; task < p.nkv * p.nsplit; task += ncta) {
-        step_attention_task<HD>(p, cc, sm.scratch, layer, pos, task, k_scale, v_scale);
+      bool ok = true;
+      for (int task = cta; ok && task < p.nkv * p.nsplit; task += ncta) {
+        ok = step_attention_task<HD>(p, sm, cc, sm.scratch, layer, pos, task, k_scale, v_scale);
         cbar();
+      }
+      if (!ok) {
+        if (cc.ctid == 0) *s_cabort = 1;
+        return;
       }
       if (cc.ctid == 0) trace_mark(p, k, 2);
       step_grid_arrive(p, cc);
@@ -855,8 +1011,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     // ---- matvec phases
     const TMat m = step_phase_mat(p, kind, layer);
     // this phase's input: RMSNorm(h) for QKV / GU / lm_head, else the
-    // attention output (O) or the SwiGLU activations (down)
-    const float* src = kind == kPhO ? p.attn_out : kind == kPhDown ? p.act : p.h;
+    // attention output (O: merged from the split partials, src == nullptr) or
+    // the SwiGLU activations (down)
+    const float* src = kind == kPhO ? nullptr : kind == kPhDown ? p.act : p.h;
     const float* nw = kind == kPhQKV  ? p.attn_norm + (size_t)layer * p.d
                       : kind == kPhGU ? p.ffn_norm + (size_t)layer * p.d
                       : kind == kPhHead ? p.out_norm : nullptr;
