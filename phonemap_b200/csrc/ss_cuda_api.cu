@@ -310,6 +310,7 @@ bool plan_step(Context* c, int htype) {
   const int ncta = c->sm_count;
   const int nsplit = std::max(1, std::min(ncta / c->nkv, kStepMaxSplit));
   if (c->nkv > ncta || G * c->hd > 2 * kStepConsumers || c->ctx % 4) return false;
+  if (qd / 32 > kStepConsumers / 2) return false;  // attention output merged in <= 2 rounds
   struct Shape { int rows, cols, type; };
   const Shape shapes[5] = {{qd + 2 * kvd, c->d, c->wtype}, {c->d, qd, c->wtype},
                            {2 * c->ff, c->d, c->wtype}, {c->d, c->ff, c->wtype},

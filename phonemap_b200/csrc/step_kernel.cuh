@@ -464,154 +464,157 @@ SS_DEVINL bool warp_wait_phase(const StepParams& p, uint32_t bar, uint32_t par) 
 }
 
 // Block fixed point of the phase's input vector src[nb * 32] into shared
-// memory: TPB consecutive consumer threads build one block together, each
-// converting 32 / TPB elements (the block maximum and the digit sums are
-// combined over the group with shuffles), so no block is built twice and all
-// consumers share the work.  With norm_w, RMSNorm first (cpu_neon.c:109-115):
-// ss = sum src^2 (each thread over its elements in order, then a warp tree,
-// then the warps in order -- the same in every CTA, so every CTA derives the
-// same scale), scale = 1 / sqrtf(ss / n + eps), x = (src * scale) * w.  The
-// digits are those of make_planes (gemv.cuh).  Ends with a consumer barrier.
+// memory.  Four consecutive consumer threads build one block together, each
+// converting 8 elements (the block maximum and the digit sums are combined
+// over the four with shuffles); with more than 128 blocks the consumers take
+// R rounds of 128 blocks, every load issued before any conversion.  No block
+// is built twice.  With norm_w, RMSNorm first (cpu_neon.c:109-115): ss = sum
+// src^2 (each thread over its elements in order, then a warp tree, then the
+// warps in order -- the same in every CTA, so every CTA derives the same
+// scale), scale = 1 / sqrtf(ss / n + eps), x = (src * scale) * w.  The digits
+// are those of make_planes (gemv.cuh).  Ends with a consumer barrier.
 //
 // With `att` (the O phase), the input is the attention output, merged here
 // from the position splits' partials (m, l, o): M = max m_s, f_s = e^(m_s-M),
 // out = sum_s f_s o_s / sum_s f_s l_s.
-template <int TPB>
-SS_DEVINL void build_block_planes_t(const float* src, const float* norm_w, const float* att,
+template <int R>
+SS_DEVINL void build_block_planes_r(const float* src, const float* norm_w, const float* att,
                                     int nsplit, int hd, int nb, float eps, PlaneBlock* dst,
                                     ConsumerCtx& cc) {
-  constexpr int EPT = 32 / TPB;  // elements per thread
-  constexpr int WPT = EPT / 4;   // packed words per plane per thread
-  const int b = cc.ctid / TPB, q = cc.ctid % TPB;
-  const bool mine = b < nb;
-  const int base = b * 32 + q * EPT;
-  float xv[EPT];
-  if (att) {
+  constexpr int EPT = 8;
+  const int q = cc.ctid & 3;
+  float xv[R][EPT];
 #pragma unroll
-    for (int j = 0; j < EPT; j++) xv[j] = 0.0f;
-    if (mine) {
-      // per chunk of 8 elements: all loads first (nsplit <= kStepMaxSplit),
-      // then the merge in split order
-      const int qh = base / hd, i0 = base - qh * hd;  // EPT <= 32 <= hd: one head
+  for (int r = 0; r < R; r++) {
+    const int b = (cc.ctid + r * kStepConsumers) >> 2;
+    const bool mine = b < nb;
+    const int base = b * 32 + q * EPT;
+#pragma unroll
+    for (int j = 0; j < EPT; j++) xv[r][j] = 0.0f;
+    if (!mine) continue;
+    if (R <= 2 && att) {  // the attention output: qd <= 8192
+      const int qh = base / hd, i0 = base - qh * hd;  // 8 elements of one head
       const float* pb = att + (size_t)qh * nsplit * (hd + 4);
       float ms[kStepMaxSplit], ls[kStepMaxSplit];
+      float4 ov[kStepMaxSplit][2];
 #pragma unroll
       for (int sp = 0; sp < kStepMaxSplit; sp++) {
-        ms[sp] = sp < nsplit ? __ldcg(pb + (size_t)sp * (hd + 4)) : -INFINITY;
-        ls[sp] = sp < nsplit ? __ldcg(pb + (size_t)sp * (hd + 4) + 1) : 0.0f;
+        const float* ps = pb + (size_t)sp * (hd + 4);
+        ms[sp] = sp < nsplit ? __ldcg(ps) : -INFINITY;
+        ls[sp] = sp < nsplit ? __ldcg(ps + 1) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 2; j++)
+          ov[sp][j] = sp < nsplit ? __ldcg(reinterpret_cast<const float4*>(ps + 4 + i0) + j)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
       }
       float M = -INFINITY;
 #pragma unroll
       for (int sp = 0; sp < kStepMaxSplit; sp++) M = fmaxf(M, ms[sp]);
-      float f[kStepMaxSplit];
       float L = 0.0f;
 #pragma unroll
       for (int sp = 0; sp < kStepMaxSplit; sp++) {
-        f[sp] = ms[sp] == -INFINITY ? 0.0f : expf(ms[sp] - M);
-        if (ms[sp] != -INFINITY) L = fmaf(ls[sp], f[sp], L);
+        if (ms[sp] == -INFINITY) continue;
+        const float f = expf(ms[sp] - M);
+        L = fmaf(ls[sp], f, L);
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+          xv[r][4 * j] = fmaf(ov[sp][j].x, f, xv[r][4 * j]);
+          xv[r][4 * j + 1] = fmaf(ov[sp][j].y, f, xv[r][4 * j + 1]);
+          xv[r][4 * j + 2] = fmaf(ov[sp][j].z, f, xv[r][4 * j + 2]);
+          xv[r][4 * j + 3] = fmaf(ov[sp][j].w, f, xv[r][4 * j + 3]);
+        }
       }
       const float inv = 1.0f / L;
 #pragma unroll
-      for (int c8 = 0; c8 < EPT; c8 += 8) {
-        float4 ov[kStepMaxSplit][2];
+      for (int j = 0; j < EPT; j++) xv[r][j] = xv[r][j] * inv;
+    } else {
 #pragma unroll
-        for (int sp = 0; sp < kStepMaxSplit; sp++)
-#pragma unroll
-          for (int j = 0; j < 2; j++)
-            ov[sp][j] = sp < nsplit ? __ldcg(reinterpret_cast<const float4*>(pb + (size_t)sp * (hd + 4) + 4 + i0 + c8) + j)
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int sp = 0; sp < kStepMaxSplit; sp++) {
-          if (ms[sp] == -INFINITY) continue;
-#pragma unroll
-          for (int j = 0; j < 2; j++) {
-            xv[c8 + 4 * j] = fmaf(ov[sp][j].x, f[sp], xv[c8 + 4 * j]);
-            xv[c8 + 4 * j + 1] = fmaf(ov[sp][j].y, f[sp], xv[c8 + 4 * j + 1]);
-            xv[c8 + 4 * j + 2] = fmaf(ov[sp][j].z, f[sp], xv[c8 + 4 * j + 2]);
-            xv[c8 + 4 * j + 3] = fmaf(ov[sp][j].w, f[sp], xv[c8 + 4 * j + 3]);
-          }
-        }
+      for (int i = 0; i < EPT; i += 4) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(src + base + i));
+        xv[r][i] = v.x; xv[r][i + 1] = v.y; xv[r][i + 2] = v.z; xv[r][i + 3] = v.w;
       }
-#pragma unroll
-      for (int j = 0; j < EPT; j++) xv[j] = xv[j] * inv;
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < EPT; i += 4) {
-      const float4 v = mine ? __ldcg(reinterpret_cast<const float4*>(src + base + i))
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
-      xv[i] = v.x; xv[i + 1] = v.y; xv[i + 2] = v.z; xv[i + 3] = v.w;
     }
   }
   if (norm_w) {
     float ss = 0.0f;
 #pragma unroll
-    for (int i = 0; i < EPT; i++) ss = fmaf(xv[i], xv[i], ss);
+    for (int r = 0; r < R; r++)
+#pragma unroll
+      for (int i = 0; i < EPT; i++) ss = fmaf(xv[r][i], xv[r][i], ss);
     ss = cblock_sum(ss, cc);
     const float scale = 1.0f / sqrtf(ss / (float)(nb * 32) + eps);
 #pragma unroll
-    for (int i = 0; i < EPT; i += 4) {
-      const float4 w = mine ? __ldg(reinterpret_cast<const float4*>(norm_w + base + i))
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
-      xv[i] = __fmul_rn(__fmul_rn(xv[i], scale), w.x);
-      xv[i + 1] = __fmul_rn(__fmul_rn(xv[i + 1], scale), w.y);
-      xv[i + 2] = __fmul_rn(__fmul_rn(xv[i + 2], scale), w.z);
-      xv[i + 3] = __fmul_rn(__fmul_rn(xv[i + 3], scale), w.w);
-    }
-  }
-  float amax = 0.0f;
+    for (int r = 0; r < R; r++) {
+      const int b = (cc.ctid + r * kStepConsumers) >> 2;
+      if (b >= nb) continue;
+      const float* wp = norm_w + b * 32 + q * EPT;
 #pragma unroll
-  for (int j = 0; j < EPT; j++) amax = fmaxf(amax, fabsf(xv[j]));
-#pragma unroll
-  for (int o = 1; o < TPB; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  const bool live = amax >= 1e-30f;
-  const int e = (int)((__float_as_uint(amax) >> 23) & 255u) - 126;
-  const float sc = live ? pow2i(22 - e) : 0.0f;
-  int s0 = 0, s1 = 0, s2 = 0;
-  PlaneBlock* d = dst + b;
-#pragma unroll
-  for (int w = 0; w < WPT; w++) {
-    int d0[4], d1[4], d2[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const int m = __float2int_rn(xv[4 * w + i] * sc);
-      d0[i] = sext8(m);
-      const int m1 = (m - d0[i]) >> 8;
-      d1[i] = sext8(m1);
-      d2[i] = (m1 - d1[i]) >> 8;
-      s0 += d0[i];
-      s1 += d1[i];
-      s2 += d2[i];
-    }
-    if (mine) {
-      d->pl[0][q * WPT + w] = (int)pack_low_bytes(d0[0], d0[1], d0[2], d0[3]);
-      d->pl[1][q * WPT + w] = (int)pack_low_bytes(d1[0], d1[1], d1[2], d1[3]);
-      d->pl[2][q * WPT + w] = (int)pack_low_bytes(d2[0], d2[1], d2[2], d2[3]);
+      for (int i = 0; i < EPT; i += 4) {
+        const float4 w = __ldg(reinterpret_cast<const float4*>(wp + i));
+        xv[r][i] = __fmul_rn(__fmul_rn(xv[r][i], scale), w.x);
+        xv[r][i + 1] = __fmul_rn(__fmul_rn(xv[r][i + 1], scale), w.y);
+        xv[r][i + 2] = __fmul_rn(__fmul_rn(xv[r][i + 2], scale), w.z);
+        xv[r][i + 3] = __fmul_rn(__fmul_rn(xv[r][i + 3], scale), w.w);
+      }
     }
   }
 #pragma unroll
-  for (int o = 1; o < TPB; o <<= 1) {
-    s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-    s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-  }
-  if (mine && q == 0) {
-    d->nsum[0] = -s0;
-    d->nsum[1] = -s1;
-    d->nsum[2] = -s2;
-    d->c0 = live ? pow2i(e - 22) : 0.0f;
+  for (int r = 0; r < R; r++) {
+    const int b = (cc.ctid + r * kStepConsumers) >> 2;
+    const bool mine = b < nb;
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < EPT; j++) amax = fmaxf(amax, fabsf(xv[r][j]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const bool live = amax >= 1e-30f;
+    const int e = (int)((__float_as_uint(amax) >> 23) & 255u) - 126;
+    const float sc = live ? pow2i(22 - e) : 0.0f;
+    int s0 = 0, s1 = 0, s2 = 0;
+    PlaneBlock* d = dst + b;
+#pragma unroll
+    for (int w = 0; w < 2; w++) {
+      int d0[4], d1[4], d2[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const int m = __float2int_rn(xv[r][4 * w + i] * sc);
+        d0[i] = sext8(m);
+        const int m1 = (m - d0[i]) >> 8;
+        d1[i] = sext8(m1);
+        d2[i] = (m1 - d1[i]) >> 8;
+        s0 += d0[i];
+        s1 += d1[i];
+        s2 += d2[i];
+      }
+      if (mine) {
+        d->pl[0][q * 2 + w] = (int)pack_low_bytes(d0[0], d0[1], d0[2], d0[3]);
+        d->pl[1][q * 2 + w] = (int)pack_low_bytes(d1[0], d1[1], d1[2], d1[3]);
+        d->pl[2][q * 2 + w] = (int)pack_low_bytes(d2[0], d2[1], d2[2], d2[3]);
+      }
+    }
+#pragma unroll
+    for (int o = 1; o < 4; o <<= 1) {
+      s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    }
+    if (mine && q == 0) {
+      d->nsum[0] = -s0;
+      d->nsum[1] = -s1;
+      d->nsum[2] = -s2;
+      d->c0 = live ? pow2i(e - 22) : 0.0f;
+    }
   }
   cbar();
 }
 SS_DEVINL void build_block_planes(const float* src, const float* norm_w, const float* att,
                                   int nsplit, int hd, int nb, float eps, PlaneBlock* dst,
                                   ConsumerCtx& cc) {
-  if (nb * 4 <= kStepConsumers)
-    build_block_planes_t<4>(src, norm_w, att, nsplit, hd, nb, eps, dst, cc);
-  else if (nb * 2 <= kStepConsumers)
-    build_block_planes_t<2>(src, norm_w, att, nsplit, hd, nb, eps, dst, cc);
-  else
-    build_block_planes_t<1>(src, norm_w, att, nsplit, hd, nb, eps, dst, cc);
+  constexpr int per = kStepConsumers / 4;  // blocks per round
+  if (nb <= per) build_block_planes_r<1>(src, norm_w, att, nsplit, hd, nb, eps, dst, cc);
+  else if (nb <= 2 * per) build_block_planes_r<2>(src, norm_w, att, nsplit, hd, nb, eps, dst, cc);
+  else if (nb <= 3 * per) build_block_planes_r<3>(src, norm_w, att, nsplit, hd, nb, eps, dst, cc);
+  else build_block_planes_r<4>(src, norm_w, att, nsplit, hd, nb, eps, dst, cc);
 }
 
 // Consumes this CTA's tiles of `m` from the ring: red[wl * rows_cta + lr] gets
@@ -1052,9 +1055,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         __stcg(p.qkv_out + r, a);
         __stcg(p.qkv_out + r + 1, b);
       }
-      mk = cblock_max(mk, cc);
-      mv = cblock_max(mv, cc);
-      if (cc.ctid == 0) __stcg(p.amax_part + cta, make_float2(mk, mv));
+      mk = warp_max(mk);
+      mv = warp_max(mv);
+      if (lane == 0) { s_red[cc.cw] = mk; s_red[16 + cc.cw] = mv; }
+      cbar();
+      if (cc.ctid == 0) {
+        for (int w = 1; w < kStepConsumerWarps; w++) {
+          mk = fmaxf(mk, s_red[w]);
+          mv = fmaxf(mv, s_red[16 + w]);
+        }
+        __stcg(p.amax_part + cta, make_float2(mk, mv));
+      }
     } else if (kind == kPhO) {
       epi_residual(p, cc, red, wpr, rows_cta, r0);
     } else if (kind == kPhGU) {
