@@ -28,7 +28,7 @@ namespace ss {
 
 struct AttnParams {
   const float* qkv;          // q [nh*hd] (roped) | k [kvd] (roped) | v [kvd]
-  int8_t* kc;                // this layer's cache rows [ctx][kvd]
+  int8_t* kc;                // this layer's cache rows, head-major [nkv][ctx][hd]
   int8_t* vc;
   float* ks;                 // this layer's scales [ctx]
   float* vs;
@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
       const int r = c / cpr, j = c - r * cpr;
       const int t = a + r;
       if (t == pos) continue;
-      const size_t off = (size_t)t * kvd + kh * HD + j * 16;
+      const size_t off = ((size_t)kh * p.ctx + t) * HD + j * 16;  // head-major rows
       cp_async16(&sm.k[r][j * 16], p.kc + off);
       cp_async16(&sm.v[r][j * 16], p.vc + off);
     }
@@ -133,8 +133,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
     const float* vcur = kcur + kvd;
     for (int i = tid; i < HD; i += kAttnThreads) {
       const int8_t kq = kv_encode(kcur[i], kinv), vq = kv_encode(vcur[i], vinv);
-      p.kc[(size_t)pos * kvd + kh * HD + i] = kq;
-      p.vc[(size_t)pos * kvd + kh * HD + i] = vq;
+      p.kc[((size_t)kh * p.ctx + pos) * HD + i] = kq;
+      p.vc[((size_t)kh * p.ctx + pos) * HD + i] = vq;
       if ((pos - t0) < kAttnTile) {
         sm.k[pos - t0][i] = kq;
         sm.v[pos - t0][i] = vq;

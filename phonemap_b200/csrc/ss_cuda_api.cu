@@ -310,7 +310,8 @@ bool plan_step(Context* c, int htype) {
   const int ncta = c->sm_count;
   const int nsplit = std::max(1, std::min(ncta / c->nkv, kStepMaxSplit));
   if (c->nkv > ncta || G * c->hd > 2 * kStepConsumers || c->ctx % 4) return false;
-  if (qd / 32 > kStepConsumers / 2) return false;  // attention output merged in <= 2 rounds
+  if (qd / 32 > kStepConsumers / 2) return false;    // attention output merged in <= 2 rounds
+  if (c->d / 32 > kStepConsumers / 2) return false;  // RMSNorm inputs converted in <= 2 rounds
   struct Shape { int rows, cols, type; };
   const Shape shapes[5] = {{qd + 2 * kvd, c->d, c->wtype}, {c->d, qd, c->wtype},
                            {2 * c->ff, c->d, c->wtype}, {c->d, c->ff, c->wtype},
@@ -325,9 +326,7 @@ bool plan_step(Context* c, int htype) {
     red = std::max(red, (size_t)wpr * rows_cta * sizeof(float));
   }
   slot = round_up(slot, 128);
-  // attention task: q[G][hd] | scores[G][rows per ring stage] | m, l, corr | int8 K/V row
-  const int att_rows = (round_up(slot, 128) - 96) / (2 * c->hd + 8);
-  const size_t att = sizeof(float) * ((size_t)G * c->hd + (size_t)G * att_rows + 24) + 2 * (size_t)c->hd;
+  const size_t att = step_att_scratch_bytes(G, c->hd, slot);
   // the scratch also holds a phase's activation planes
   const size_t planes = (size_t)(std::max(std::max(c->d, qd), c->ff) / 32) * sizeof(PlaneBlock);
   const size_t scratch = (std::max(std::max(red, att), planes) + 127) / 128 * 128;
@@ -595,6 +594,7 @@ void alloc_step_state(Context* c) {
   // busy; SS_STEP_INFLIGHT / SS_STEP_PREFETCH override for tuning sweeps
   p.inflight = std::max(1, std::min(c->step_nslots, env_int("SS_STEP_INFLIGHT", c->step_nslots)));
   p.prefetch = env_int("SS_STEP_PREFETCH", 0);
+  p.split_rows = std::max(16, env_int("SS_STEP_SPLIT_ROWS", 64));
   if (c->trace) {
     const size_t n = (size_t)(2 + 5 * c->L) * ncta * 8;
     c->step_trace = dev_alloc<long long>(c, n);
@@ -843,7 +843,9 @@ void check_device_error(Context* c) {
   err = c->h_small[8];
   if (err) {
     CK(cudaMemsetAsync(&c->ctrl->err, 0, sizeof(int), c->stream));
-    fail(SS_CUDA_ERROR_BACKEND, "device reported error bits 0x%x (1: position, 2: token)", err);
+    fail(SS_CUDA_ERROR_BACKEND,
+         "device reported error bits 0x%x (1: position, 2: token, 4: ring wait, 8: grid barrier, "
+         "16: shared-memory plan)", err);
   }
 }
 
@@ -1408,10 +1410,14 @@ SS_API int ss_cuda_kv_row(ss_cuda_ctx_t* ctx, int32_t layer, int32_t pos, int8_t
     Context* c = need_model(ctx);
     if (layer < 0 || layer >= c->L || pos < 0 || pos >= c->ctx || !k || !v || !k_scale || !v_scale)
       fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad kv_row arguments");
+    // the device cache is head-major ([L][nkv][ctx][hd]); gather the row
     const size_t kvd = (size_t)c->nkv * c->hd, vi = (size_t)layer * c->ctx + pos;
+    const size_t off = (size_t)layer * c->ctx * kvd + (size_t)pos * c->hd;
     CK(cudaStreamSynchronize(c->stream));
-    CK(cudaMemcpy(k, c->kc + vi * kvd, kvd, cudaMemcpyDeviceToHost));
-    CK(cudaMemcpy(v, c->vc + vi * kvd, kvd, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy2D(k, (size_t)c->hd, c->kc + off, (size_t)c->ctx * c->hd, (size_t)c->hd, (size_t)c->nkv,
+                    cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy2D(v, (size_t)c->hd, c->vc + off, (size_t)c->ctx * c->hd, (size_t)c->hd, (size_t)c->nkv,
+                    cudaMemcpyDeviceToHost));
     CK(cudaMemcpy(k_scale, c->ks + vi, 4, cudaMemcpyDeviceToHost));
     CK(cudaMemcpy(v_scale, c->vs + vi, 4, cudaMemcpyDeviceToHost));
   });

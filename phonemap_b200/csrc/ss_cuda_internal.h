@@ -89,7 +89,8 @@ struct Context {
   float* ffn_norm_all = nullptr;     // [L][d]
   size_t weight_bytes = 0;
 
-  // KV cache [L][ctx][kvd] + scales/maxima [L][ctx]
+  // KV cache [L][nkv][ctx][hd] (head-major; the reference's is [L][ctx][kvd],
+  // ss_cuda_kv_row gathers a position) + scales/maxima [L][ctx]
   int8_t* kc = nullptr;
   int8_t* vc = nullptr;
   float* ks = nullptr;

@@ -95,7 +95,7 @@ struct StepParams {
   int d, qd, kvd, ff, vocab, nh, nkv, hd, rope_dim, ctx;
   float eps, attn_scale;
   const float2* rope_tab;
-  int8_t* kc;  // [L][ctx][kvd]
+  int8_t* kc;  // [L][nkv][ctx][hd] (head-major: a head's positions are contiguous)
   int8_t* vc;
   float* ks;   // [L][ctx]
   float* vs;
@@ -117,6 +117,7 @@ struct StepParams {
   int nsplit;          // attention position splits per kv head
   int slot_bytes, nslots;
   int inflight;        // weight stages a producer keeps in flight (not yet landed)
+  int split_rows;      // cached positions per attention split (see step_nsplit)
   int prefetch;        // 1: bulk L2 prefetch of the next weight phase
   // optional timeline (measurement aid): [phase][cta][8] global-timer ns --
   // 0 input ready (grid barrier passed), 1 main work done, 2 arrival at the
@@ -229,13 +230,30 @@ struct StepSmem {
 
 // Attention-stage geometry (shared by producer and consumers; layout in the
 // attention section below).
-SS_DEVINL int step_att_rows(int slot_bytes, int hd) { return (slot_bytes - 96) / (2 * hd + 8); }
+__host__ __device__ __forceinline__ int step_att_rows(int slot_bytes, int hd) {
+  return (slot_bytes - 96) / (2 * hd + 8);
+}
+// Shared-memory scratch of an attention task (layout in step_attention_task):
+// q[G][hd] | scores[max(G * rows per stage, consumers)] | m, l, corr [24] |
+// int8 K and V rows of this position.  One function for host and kernel.
+__host__ __device__ __forceinline__ size_t step_att_scratch_bytes(int G, int hd, int slot_bytes) {
+  const int sc = G * step_att_rows(slot_bytes, hd);
+  return sizeof(float) * ((size_t)G * hd + (size_t)(sc > kStepConsumers ? sc : kStepConsumers) + 24) +
+         2 * (size_t)hd;
+}
+// Position splits of this step: one per p.split_rows cached positions, at most
+// p.nsplit (more splits: shorter attention tasks; fewer: less for the O phase
+// to merge).
+SS_DEVINL int step_nsplit(const StepParams& p, int pos) {
+  return max(1, min(p.nsplit, (pos + p.split_rows) / p.split_rows));
+}
 SS_DEVINL void step_att_task(const StepParams& p, int task, int pos, int& kvh, int& split, int& t0,
                              int& t1) {
-  kvh = task / p.nsplit;
-  split = task - kvh * p.nsplit;
+  const int ns = step_nsplit(p, pos);
+  kvh = task / ns;
+  split = task - kvh * ns;
   const int seq = pos + 1;
-  const int chunk = (seq + p.nsplit - 1) / p.nsplit;
+  const int chunk = (seq + ns - 1) / ns;
   t0 = min(split * chunk, seq);
   t1 = min(t0 + chunk, seq);
 }
@@ -314,7 +332,7 @@ SS_DEVINL void step_producer(const StepParams& p, const StepSmem& sm, const vola
       // this CTA's attention task(s): the cached K / V rows and scales
       const int R = step_att_rows(p.slot_bytes, p.hd);
       const size_t lrow = (size_t)layer * p.ctx;
-      for (int task = cta; task < p.nkv * p.nsplit && !aborted; task += ncta) {
+      for (int task = cta; task < p.nkv * step_nsplit(p, pos) && !aborted; task += ncta) {
         int kvh, split, t0, t1;
         step_att_task(p, task, pos, kvh, split, t0, t1);
         const int tend = min(t1, pos);
@@ -326,12 +344,9 @@ SS_DEVINL void step_producer(const StepParams& p, const StepSmem& sm, const vola
           const uint32_t sbytes = (uint32_t)((sb - sa) * 4);
           mbar_expect_tx(fb, (uint32_t)(2 * nr * p.hd) + 2 * sbytes);
           const uint32_t dst = ring0 + (uint32_t)slot * slot_bytes;
-          const int8_t* kr = p.kc + (lrow + ts) * p.kvd + kvh * p.hd;
-          const int8_t* vr = p.vc + (lrow + ts) * p.kvd + kvh * p.hd;
-          for (int r = 0; r < nr; r++) {
-            bulk_g2s(dst + (uint32_t)(r * p.hd), kr + (size_t)r * p.kvd, (uint32_t)p.hd, fb);
-            bulk_g2s(dst + (uint32_t)((R + r) * p.hd), vr + (size_t)r * p.kvd, (uint32_t)p.hd, fb);
-          }
+          const size_t row0 = lrow * p.kvd + ((size_t)kvh * p.ctx + ts) * p.hd;  // head-major
+          bulk_g2s(dst, p.kc + row0, (uint32_t)(nr * p.hd), fb);
+          bulk_g2s(dst + (uint32_t)(R * p.hd), p.vc + row0, (uint32_t)(nr * p.hd), fb);
           bulk_g2s(dst + (uint32_t)step_att_ks_off(R, p.hd), p.ks + lrow + sa, sbytes, fb);
           bulk_g2s(dst + (uint32_t)step_att_vs_off(R, p.hd), p.vs + lrow + sa, sbytes, fb);
           advance();
@@ -535,7 +550,19 @@ SS_DEVINL void build_block_planes_r(const float* src, const float* norm_w, const
       }
     }
   }
-  if (norm_w) {
+  if (R <= 2 && norm_w) {  // RMSNorm inputs: d <= 8192
+    // the weights are requested before the reduction, so both loads overlap
+    float wv[R][EPT];
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      const int b = (cc.ctid + r * kStepConsumers) >> 2;
+#pragma unroll
+      for (int i = 0; i < EPT; i += 4) {
+        const float4 w = b < nb ? __ldg(reinterpret_cast<const float4*>(norm_w + b * 32 + q * EPT + i))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        wv[r][i] = w.x; wv[r][i + 1] = w.y; wv[r][i + 2] = w.z; wv[r][i + 3] = w.w;
+      }
+    }
     float ss = 0.0f;
 #pragma unroll
     for (int r = 0; r < R; r++)
@@ -544,19 +571,9 @@ SS_DEVINL void build_block_planes_r(const float* src, const float* norm_w, const
     ss = cblock_sum(ss, cc);
     const float scale = 1.0f / sqrtf(ss / (float)(nb * 32) + eps);
 #pragma unroll
-    for (int r = 0; r < R; r++) {
-      const int b = (cc.ctid + r * kStepConsumers) >> 2;
-      if (b >= nb) continue;
-      const float* wp = norm_w + b * 32 + q * EPT;
+    for (int r = 0; r < R; r++)
 #pragma unroll
-      for (int i = 0; i < EPT; i += 4) {
-        const float4 w = __ldg(reinterpret_cast<const float4*>(wp + i));
-        xv[r][i] = __fmul_rn(__fmul_rn(xv[r][i], scale), w.x);
-        xv[r][i + 1] = __fmul_rn(__fmul_rn(xv[r][i + 1], scale), w.y);
-        xv[r][i + 2] = __fmul_rn(__fmul_rn(xv[r][i + 2], scale), w.z);
-        xv[r][i + 3] = __fmul_rn(__fmul_rn(xv[r][i + 3], scale), w.w);
-      }
-    }
+      for (int i = 0; i < EPT; i++) xv[r][i] = __fmul_rn(__fmul_rn(xv[r][i], scale), wv[r][i]);
   }
 #pragma unroll
   for (int r = 0; r < R; r++) {
@@ -622,7 +639,7 @@ SS_DEVINL void build_block_planes(const float* src, const float* norm_w, const f
 // row group.  Returns rows_cta, or -1 on abort.
 template <int TYPE>
 SS_DEVINL int step_gemv(const StepParams& p, const StepSmem& sm, ConsumerCtx& cc, const TMat& m,
-                        const float* src, const float* norm_w, float* red, int phase) {
+                        const float* src, const float* norm_w, float* red, int phase, int pos) {
   const int ncta = gridDim.x, cta = blockIdx.x;
   constexpr int QB = TYPE == kQ4_0 ? 16 : 32;
   const int nb = m.nb, wpr = step_wpr(nb), RG = kStepConsumerWarps / wpr;
@@ -634,7 +651,8 @@ SS_DEVINL int step_gemv(const StepParams& p, const StepSmem& sm, ConsumerCtx& cc
   const int rows_cta = (t1 - t0) * kStepTileRows;
 
   // this thread's block of the input planes, built in shared memory
-  build_block_planes(src, norm_w, src == nullptr ? p.att_part : nullptr, p.nsplit, p.hd, nb, p.eps,
+  build_block_planes(src, norm_w, src == nullptr ? p.att_part : nullptr, step_nsplit(p, pos), p.hd,
+                     nb, p.eps,
                      reinterpret_cast<PlaneBlock*>(red), cc);
   int pl[3][8];
   int init[3];
@@ -763,17 +781,36 @@ SS_DEVINL void att_rows(const StepParams& p, ConsumerCtx& cc, const int8_t* K, c
                         const float* ksc, const float* vsc, int nr, const float* q, float* sc,
                         int scs, float* ml, int G, float (&o)[2]) {
   constexpr int DPL = HD / 32;
-  for (int r = cc.cw; r < nr; r += kStepConsumerWarps) {
-    float kd[DPL];
-    const float s = ksc[r];
+  constexpr int U = 4;  // rows per warp at a time: their shuffle reductions overlap
+  for (int rb = cc.cw; rb < nr; rb += U * kStepConsumerWarps) {
+    float kd[U][DPL];
 #pragma unroll
-    for (int i = 0; i < DPL; i++) kd[i] = __fmul_rn((float)K[r * HD + cc.lane * DPL + i], s);
+    for (int u = 0; u < U; u++) {
+      const int r = rb + u * kStepConsumerWarps;
+      const float s = r < nr ? ksc[r] : 0.0f;
+#pragma unroll
+      for (int i = 0; i < DPL; i++)
+        kd[u][i] = r < nr ? __fmul_rn((float)K[r * HD + cc.lane * DPL + i], s) : 0.0f;
+    }
     for (int g = 0; g < G; g++) {
-      float dsum = 0.0f;
+      float ds[U];
 #pragma unroll
-      for (int i = 0; i < DPL; i++) dsum = fmaf(q[g * HD + cc.lane * DPL + i], kd[i], dsum);
-      dsum = warp_sum(dsum);
-      if (cc.lane == 0) sc[g * scs + r] = __fmul_rn(dsum, p.attn_scale);
+      for (int u = 0; u < U; u++) {
+        ds[u] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < DPL; i++) ds[u] = fmaf(q[g * HD + cc.lane * DPL + i], kd[u][i], ds[u]);
+      }
+#pragma unroll
+      for (int o2 = 16; o2 > 0; o2 >>= 1)
+#pragma unroll
+        for (int u = 0; u < U; u++) ds[u] += __shfl_xor_sync(0xffffffffu, ds[u], o2);
+      if (cc.lane == 0) {
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+          const int r = rb + u * kStepConsumerWarps;
+          if (r < nr) sc[g * scs + r] = __fmul_rn(ds[u], p.attn_scale);
+        }
+      }
     }
   }
   cbar();
@@ -799,13 +836,18 @@ SS_DEVINL void att_rows(const StepParams& p, ConsumerCtx& cc, const int8_t* K, c
     }
   }
   cbar();
+  // PV: item (g, i) of the group's outputs; with fewer items than consumers,
+  // `ngrp` thread groups take interleaved rows (reduced at the end of the task)
+  const int items = G * HD;
+  const int ngrp = items >= kStepConsumers ? 1 : kStepConsumers / items;
+  const int grp = items >= kStepConsumers ? 0 : cc.ctid / items;
 #pragma unroll
   for (int k = 0; k < 2; k++) {
-    const int item = cc.ctid + k * kStepConsumers;
-    if (item < G * HD) {
+    const int item = items >= kStepConsumers ? cc.ctid + k * kStepConsumers : cc.ctid % items;
+    if (item < items && (k == 0 || items > kStepConsumers)) {
       const int g = item / HD, i = item - g * HD;
       float acc = o[k] * ml[16 + g];
-      for (int r = 0; r < nr; r++)
+      for (int r = grp; r < nr; r += ngrp)
         acc = fmaf(sc[g * scs + r], __fmul_rn((float)V[r * HD + i], vsc[r]), acc);
       o[k] = acc;
     }
@@ -816,10 +858,36 @@ SS_DEVINL void att_rows(const StepParams& p, ConsumerCtx& cc, const int8_t* K, c
 // `pos`, attention over the split's positions (ring stages, then row pos) for
 // the group's query heads, partial (m, l, o) to att_part.  The O phase merges
 // the splits.  Returns false on abort.
+// This thread's share of a task's inputs, loaded before the k / v maxima are
+// known: q items ctid and ctid + 512 of the group, and element ctid of the kv
+// head's current k and v rows.
+struct AttInputs {
+  float q[2];
+  float k, v;
+};
+SS_DEVINL AttInputs att_load_inputs(const StepParams& p, const ConsumerCtx& cc, int task, int pos,
+                                    int hd) {
+  AttInputs in;
+  in.q[0] = in.q[1] = in.k = in.v = 0.0f;
+  const int G = p.nh / p.nkv;
+  if (task >= p.nkv * step_nsplit(p, pos)) return in;  // this CTA has no task: nothing to load
+  int kvh, split, t0, t1;
+  step_att_task(p, task, pos, kvh, split, t0, t1);
+#pragma unroll
+  for (int k = 0; k < 2; k++) {
+    const int item = cc.ctid + k * kStepConsumers;
+    in.q[k] = item < G * hd ? __ldcg(p.qkv_out + (size_t)kvh * G * hd + item) : 0.0f;
+  }
+  const bool has_pos = pos >= t0 && pos < t1;
+  in.k = has_pos && cc.ctid < hd ? __ldcg(p.qkv_out + p.qd + kvh * hd + cc.ctid) : 0.0f;
+  in.v = has_pos && cc.ctid < hd ? __ldcg(p.qkv_out + p.qd + p.kvd + kvh * hd + cc.ctid) : 0.0f;
+  return in;
+}
+
 template <int HD>
 SS_DEVINL bool step_attention_task(const StepParams& p, const StepSmem& sm, ConsumerCtx& cc,
                                    float* scratch, int layer, int pos, int task, float k_scale,
-                                   float v_scale) {
+                                   float v_scale, int phase, const AttInputs& in) {
   const int G = p.nh / p.nkv;
   int kvh, split, t0, t1;
   step_att_task(p, task, pos, kvh, split, t0, t1);
@@ -827,14 +895,16 @@ SS_DEVINL bool step_attention_task(const StepParams& p, const StepSmem& sm, Cons
   const int R = step_att_rows(p.slot_bytes, HD);
   const size_t lrow = (size_t)layer * p.ctx;
 
-  // scratch: q[G][HD] | sc[G][R] | ml[24] | kcur[HD], vcur[HD] (int8)
+  // scratch: q[G][HD] | sc[max(G * R, consumers)] (scores, then the row-group
+  // reduction) | ml[24] | kcur[HD], vcur[HD] (int8)
   float* q = scratch;
   float* sc = q + G * HD;
-  float* ml = sc + G * R;
+  float* ml = sc + max(G * R, kStepConsumers);
   int8_t* kcur = reinterpret_cast<int8_t*>(ml + 24);
   int8_t* vcur = kcur + HD;
-  for (int i = cc.ctid; i < G * HD; i += kStepConsumers)
-    q[i] = __ldcg(p.qkv_out + (size_t)kvh * G * HD + i);
+#pragma unroll
+  for (int k = 0; k < 2; k++)
+    if (cc.ctid + k * kStepConsumers < G * HD) q[cc.ctid + k * kStepConsumers] = in.q[k];
   if (cc.ctid < 8) {
     ml[cc.ctid] = -INFINITY;
     ml[8 + cc.ctid] = 0.0f;
@@ -844,14 +914,13 @@ SS_DEVINL bool step_attention_task(const StepParams& p, const StepSmem& sm, Cons
     // kv_turboquant_encode (layer_scheduler.c:101-118) of this kv head's slice
     const float kinv = k_scale > 0.0f ? 1.0f / k_scale : 0.0f;
     const float vinv = v_scale > 0.0f ? 1.0f / v_scale : 0.0f;
-    const float* kf = p.qkv_out + p.qd + kvh * HD;
-    const float* vf = kf + p.kvd;
-    for (int i = cc.ctid; i < HD; i += kStepConsumers) {
-      const int8_t kq = kv_encode(__ldcg(kf + i), kinv), vq = kv_encode(__ldcg(vf + i), vinv);
+    if (cc.ctid < HD) {
+      const int i = cc.ctid;
+      const int8_t kq = kv_encode(in.k, kinv), vq = kv_encode(in.v, vinv);
       kcur[i] = kq;
       vcur[i] = vq;
-      p.kc[(lrow + pos) * p.kvd + kvh * HD + i] = kq;
-      p.vc[(lrow + pos) * p.kvd + kvh * HD + i] = vq;
+      p.kc[lrow * p.kvd + ((size_t)kvh * p.ctx + pos) * HD + i] = kq;
+      p.vc[lrow * p.kvd + ((size_t)kvh * p.ctx + pos) * HD + i] = vq;
     }
     if (cc.ctid == 0 && kvh == 0) {
       p.ks[lrow + pos] = k_scale;
@@ -863,6 +932,7 @@ SS_DEVINL bool step_attention_task(const StepParams& p, const StepSmem& sm, Cons
   float o[2] = {0.0f, 0.0f};
   const uint32_t ring0 = smem_addr(sm.ring);
   bool bad = false;
+  bool pos_done = false;
   for (int ts = t0; ts < tend; ts += R) {
     const int nr = min(R, tend - ts);
     // every warp agrees before att_rows (which has consumer barriers)
@@ -870,13 +940,33 @@ SS_DEVINL bool step_attention_task(const StepParams& p, const StepSmem& sm, Cons
       bad = true;
       break;
     }
-    const uint8_t* st = sm.ring + (size_t)cc.slot * p.slot_bytes;
-    const int8_t* K = reinterpret_cast<const int8_t*>(st);
-    const int8_t* V = K + R * HD;
+    if (cc.ctid == 0 && ts == t0) trace_mark(p, phase, 4);
+    uint8_t* st = sm.ring + (size_t)cc.slot * p.slot_bytes;
+    int8_t* K = reinterpret_cast<int8_t*>(st);
+    int8_t* V = K + R * HD;
     const int sa = ts & ~3;
-    const float* ksc = reinterpret_cast<const float*>(st + step_att_ks_off(R, HD)) + (ts - sa);
-    const float* vsc = reinterpret_cast<const float*>(st + step_att_vs_off(R, HD)) + (ts - sa);
-    att_rows<HD>(p, cc, K, V, ksc, vsc, nr, q, sc, R, ml, G, o);
+    float* ksc = reinterpret_cast<float*>(st + step_att_ks_off(R, HD)) + (ts - sa);
+    float* vsc = reinterpret_cast<float*>(st + step_att_vs_off(R, HD)) + (ts - sa);
+    int n = nr;
+    if (has_pos && ts + nr == tend && nr < R) {
+      // row pos joins the last stage (the slot is ours until released; the
+      // scale blocks have room past the copied range)
+      for (int i = cc.ctid; i < HD; i += kStepConsumers) {
+        K[nr * HD + i] = kcur[i];
+        V[nr * HD + i] = vcur[i];
+      }
+      if (cc.ctid == 0) {
+        ksc[nr] = k_scale;
+        vsc[nr] = v_scale;
+      }
+      // these generic writes must be ordered before the producer's next bulk
+      // copy (async proxy) into this slot
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      pos_done = true;
+      n = nr + 1;
+      cbar();
+    }
+    att_rows<HD>(p, cc, K, V, ksc, vsc, n, q, sc, R, ml, G, o);
     __syncwarp();
     if (cc.lane == 0) mbar_arrive(smem_addr(sm.empty + cc.slot));
     if (++cc.slot == p.nslots) { cc.slot = 0; cc.phase ^= 1u; }
@@ -884,16 +974,29 @@ SS_DEVINL bool step_attention_task(const StepParams& p, const StepSmem& sm, Cons
   }
   (void)ring0;
   if (bad) return false;
-  if (has_pos) {
+  if (cc.ctid == 0) trace_mark(p, phase, 5);
+  if (has_pos && !pos_done) {
     att_rows<HD>(p, cc, kcur, vcur, &k_scale, &v_scale, 1, q, sc, R, ml, G, o);
     cbar();
+  }
+  const int items = G * HD;
+  if (items < kStepConsumers) {
+    // sum the row groups' partial outputs (groups in order)
+    float* red = sc;  // scores are consumed; [ngrp][items]
+    red[cc.ctid] = o[0];
+    cbar();
+    if (cc.ctid < items) {
+      float t = 0.0f;
+      for (int j = 0; j < kStepConsumers / items; j++) t += red[j * items + cc.ctid];
+      o[0] = t;
+    }
   }
 #pragma unroll
   for (int k = 0; k < 2; k++) {
     const int item = cc.ctid + k * kStepConsumers;
-    if (item < G * HD) {
+    if (item < items) {
       const int g = item / HD, i = item - g * HD;
-      float* part = p.att_part + ((size_t)(kvh * G + g) * p.nsplit + split) * (HD + 4);
+      float* part = p.att_part + ((size_t)(kvh * G + g) * step_nsplit(p, pos) + split) * (HD + 4);
       __stcg(part + 4 + i, o[k]);
       if (i == 0) {
         __stcg(part, ml[g]);
@@ -901,6 +1004,7 @@ SS_DEVINL bool step_attention_task(const StepParams& p, const StepSmem& sm, Cons
       }
     }
   }
+  if (cc.ctid == 0) trace_mark(p, phase, 6);
   return true;
 }
 
@@ -927,6 +1031,18 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
   if (pos < 0 || pos >= p.ctx) {
     if (tid == 0 && cta == 0) atomicOr(p.err, 1);
     return;  // uniform across the grid: nothing started
+  }
+  {
+    // the scratch must hold the attention task's buffers (the host sizes it
+    // with the same function); uniform across the grid
+    uint32_t dyn;
+    asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
+    const size_t need = (size_t)p.nslots * p.slot_bytes + 128 +
+                        step_att_scratch_bytes(p.nh / p.nkv, HD, p.slot_bytes);
+    if (need > dyn) {
+      if (tid == 0 && cta == 0) atomicOr(p.err, 16);
+      return;
+    }
   }
   if (tid == 0) {
     s_cabort_v = 0;
@@ -979,6 +1095,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     }
 
     if (kind == kPhAtt) {
+      // this step's q / k / v of the CTA's task, requested before the maxima
+      const AttInputs ain = att_load_inputs(p, cc, cta, pos, HD);
       // this position's int8 scales need max |k| / |v| over the whole kv_dim
       float mk = 0.0f, mv = 0.0f;
       for (int i = cc.ctid; i < ncta; i += kStepConsumers) {
@@ -998,8 +1116,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
       }
       const float k_scale = mk / 127.0f, v_scale = mv / 127.0f;  // layer_scheduler.c:109-110
       bool ok = true;
-      for (int task = cta; ok && task < p.nkv * p.nsplit; task += ncta) {
-        ok = step_attention_task<HD>(p, sm, cc, sm.scratch, layer, pos, task, k_scale, v_scale);
+      for (int task = cta; ok && task < p.nkv * step_nsplit(p, pos); task += ncta) {
+        ok = step_attention_task<HD>(p, sm, cc, sm.scratch, layer, pos, task, k_scale, v_scale, k,
+                                     task == cta ? ain : att_load_inputs(p, cc, task, pos, HD));
         cbar();
       }
       if (!ok) {
@@ -1021,8 +1140,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                       : kind == kPhGU ? p.ffn_norm + (size_t)layer * p.d
                       : kind == kPhHead ? p.out_norm : nullptr;
     int rows_cta;
-    if (kind == kPhHead) rows_cta = step_gemv<HTYPE>(p, sm, cc, m, src, nw, red, k);
-    else rows_cta = step_gemv<TYPE>(p, sm, cc, m, src, nw, red, k);
+    if (kind == kPhHead) rows_cta = step_gemv<HTYPE>(p, sm, cc, m, src, nw, red, k, pos);
+    else rows_cta = step_gemv<TYPE>(p, sm, cc, m, src, nw, red, k, pos);
     if (rows_cta < 0) return;
     if (cc.ctid == 0) trace_mark(p, k, 1);
     const int wpr = step_wpr(m.nb);
