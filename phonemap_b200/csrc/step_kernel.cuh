@@ -118,7 +118,7 @@ struct StepParams {
   int slot_bytes, nslots;
   int inflight;        // weight stages a producer keeps in flight (not yet landed)
   int split_rows;      // cached positions per attention split (see step_nsplit)
-  int prefetch;        // 1: bulk L2 prefetch of the next weight phase
+  int prefetch;        // weight stages the L2 prefetch runs ahead of the bulk copies (0: off)
   // optional timeline (measurement aid): [phase][cta][8] global-timer ns --
   // 0 input ready (grid barrier passed), 1 main work done, 2 arrival at the
   // next barrier, 3 producer issued the phase's last weight stage, 4 first
@@ -281,21 +281,36 @@ SS_DEVINL void step_producer(const StepParams& p, const StepSmem& sm, const vola
   const int inflight = p.inflight;
   int lslot = 0;
   uint32_t lwraps = 0;
-  auto prefetch_phase = [&](int k) {
-    for (; k < nph; k++) {
+  // L2 prefetch `p.prefetch` weight stages ahead of the bulk copies, across
+  // phase boundaries (0: off): while the consumers sit at a barrier and the
+  // ring is full, HBM keeps loading the stages after the ring into L2, a
+  // stage at a time, so no large burst queues ahead of the consumers' loads
+  struct Ahead {
+    int k = 0, t = 0, t1 = 0, rg = 1;
+    TMat m;
+  } ah;
+  auto ahead_next = [&](const uint8_t*& ptr, uint32_t& bytes) -> bool {
+    while (ah.t >= ah.t1) {
+      if (++ah.k >= nph) return false;
       int kind, layer;
-      step_phase(k, p.L, kind, layer);
+      step_phase(ah.k, p.L, kind, layer);
       if (!step_phase_has_mat(kind)) continue;
-      if (!p.prefetch) return;
-      const TMat m = step_phase_mat(p, kind, layer);
-      int t0, t1;
-      part_range(m.ntiles, cta, ncta, t0, t1);
-      if (t1 > t0)
-        prefetch_l2_bulk(m.w + (size_t)t0 * m.tile_bytes, (uint32_t)((t1 - t0) * m.tile_bytes));
-      return;
+      ah.m = step_phase_mat(p, kind, layer);
+      part_range(ah.m.ntiles, cta, ncta, ah.t, ah.t1);
+      ah.rg = step_rg(ah.m.nb);
     }
+    const int nt = min(ah.rg, ah.t1 - ah.t);
+    ptr = ah.m.w + (size_t)ah.t * ah.m.tile_bytes;
+    bytes = (uint32_t)(nt * ah.m.tile_bytes);
+    ah.t += ah.rg;
+    return true;
   };
-  prefetch_phase(1);
+  auto prefetch_one = [&]() {
+    const uint8_t* ptr;
+    uint32_t bytes;
+    if (ahead_next(ptr, bytes)) prefetch_l2_bulk(ptr, bytes);
+  };
+  for (int i = 0; i < p.prefetch; i++) prefetch_one();  // the window's first stages
   bool aborted = false;
   // Waits until the next slot may be filled (its previous stage released, and
   // the stage `inflight` back landed); returns its full barrier, or 0 on abort.
@@ -358,10 +373,6 @@ SS_DEVINL void step_producer(const StepParams& p, const StepSmem& sm, const vola
     if (!step_phase_has_mat(kind)) continue;
     const TMat mv = step_phase_mat(p, kind, layer);
     const TMat* m = &mv;
-    // warm L2 with the next weight phase while this one streams; at the last
-    // phase, the first phase of the next step
-    if (kind == kPhHead) prefetch_phase(1);
-    else prefetch_phase(k + 1);
     int t0, t1;
     part_range(m->ntiles, cta, ncta, t0, t1);
     const int rg = step_rg(m->nb);
@@ -374,6 +385,7 @@ SS_DEVINL void step_producer(const StepParams& p, const StepSmem& sm, const vola
       mbar_expect_tx(fb, bytes);
       bulk_g2s(ring0 + (uint32_t)slot * slot_bytes, m->w + (size_t)t * m->tile_bytes, bytes, fb);
       advance();
+      if (p.prefetch) prefetch_one();  // keep the L2 window p.prefetch stages ahead
     }
     trace_mark(p, k, 3);
   }
@@ -756,10 +768,11 @@ SS_DEVINL float row_total(const float* red, int wpr, int rows_cta, int lr) {
 
 // h[r] += v[r] for the CTA's rows (layer_scheduler.c:484, :566).
 SS_DEVINL void epi_residual(const StepParams& p, ConsumerCtx& cc, const float* red, int wpr,
-                            int rows_cta, int r0) {
+                            int rows_cta, int r0, float h_pre) {
   const int r1 = min(r0 + rows_cta, p.d);
   for (int r = r0 + cc.ctid; r < r1; r += kStepConsumers)
-    __stcg(p.h + r, __fadd_rn(row_total(red, wpr, rows_cta, r - r0), __ldcg(p.h + r)));
+    __stcg(p.h + r, __fadd_rn(row_total(red, wpr, rows_cta, r - r0),
+                              r == r0 + cc.ctid ? h_pre : __ldcg(p.h + r)));
 }
 
 // ---------------------------------------------------------------- attention
@@ -1139,15 +1152,30 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     const float* nw = kind == kPhQKV  ? p.attn_norm + (size_t)layer * p.d
                       : kind == kPhGU ? p.ffn_norm + (size_t)layer * p.d
                       : kind == kPhHead ? p.out_norm : nullptr;
+    int t0, t1;
+    part_range(m.ntiles, cta, ncta, t0, t1);
+    const int r0 = t0 * kStepTileRows;
+    // the epilogue's other inputs (this thread's first row or row pair), requested
+    // now so they arrive while the weights stream: the RoPE cos/sin (QKV) and the
+    // residual h (O, DOWN -- no phase writes h between here and the epilogue)
+    float2 cs_pre = make_float2(1.0f, 0.0f);
+    float h_pre = 0.0f;
+    {
+      const int rows = (t1 - t0) * kStepTileRows;
+      if (kind == kPhQKV) {
+        const int r = r0 + 2 * cc.ctid, i = r % p.hd;
+        if (2 * cc.ctid < rows && r < p.qd + p.kvd && i < p.rope_dim)
+          cs_pre = __ldg(p.rope_tab + (size_t)pos * (p.rope_dim >> 1) + (i >> 1));
+      } else if (kind == kPhO || kind == kPhDown) {
+        if (cc.ctid < rows && r0 + cc.ctid < p.d) h_pre = __ldcg(p.h + r0 + cc.ctid);
+      }
+    }
     int rows_cta;
     if (kind == kPhHead) rows_cta = step_gemv<HTYPE>(p, sm, cc, m, src, nw, red, k, pos);
     else rows_cta = step_gemv<TYPE>(p, sm, cc, m, src, nw, red, k, pos);
     if (rows_cta < 0) return;
     if (cc.ctid == 0) trace_mark(p, k, 1);
     const int wpr = step_wpr(m.nb);
-    int t0, t1;
-    part_range(m.ntiles, cta, ncta, t0, t1);
-    const int r0 = t0 * kStepTileRows;
 
     if (kind == kPhQKV) {
       // RoPE (non-NeoX, tensor.c:249-274) on q and k rows; |k|, |v| maxima
@@ -1161,7 +1189,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         if (r < p.qd + p.kvd) {
           const int i = r % p.hd;
           if (i < p.rope_dim) {
-            const float2 cs = p.rope_tab[(size_t)pos * (p.rope_dim >> 1) + (i >> 1)];
+            const float2 cs = lp == cc.ctid ? cs_pre : p.rope_tab[(size_t)pos * (p.rope_dim >> 1) + (i >> 1)];
             const float na = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
             const float nb2 = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
             a = na;
@@ -1186,7 +1214,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         __stcg(p.amax_part + cta, make_float2(mk, mv));
       }
     } else if (kind == kPhO) {
-      epi_residual(p, cc, red, wpr, rows_cta, r0);
+      epi_residual(p, cc, red, wpr, rows_cta, r0, h_pre);
     } else if (kind == kPhGU) {
       // act = up * g / (1 + expf(-g)) (layer_scheduler.c:533-549)
       const int a0 = r0 / 2, a1 = min((r0 + rows_cta) / 2, p.ff);
@@ -1197,7 +1225,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         __stcg(p.act + j, __fmul_rn(u, __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)))));
       }
     } else if (kind == kPhDown) {
-      epi_residual(p, cc, red, wpr, rows_cta, r0);
+      epi_residual(p, cc, red, wpr, rows_cta, r0, h_pre);
     } else {  // kPhHead: logits, greedy argmax (tensor.c:318-328), next token
       unsigned long long best = 0;
       const int r1 = min(r0 + rows_cta, p.vocab);
