@@ -13,8 +13,11 @@ than L2, so no L2 flush is needed between steps.
 
 Prints one JSON line on rank 0.  --impl reference times the reference's own CPU
 path (oracle/_ref, or the repository's C restatement when the reference build is
-absent) on the host cores instead.  With --gpus N (torchrun) every rank decodes
-an independent replica on its own GPU; time is the max over ranks.
+absent) on the host cores instead.  With --gpus N (torchrun, one rank per GPU)
+the N ranks decode the same sequence tensor-parallel (heads, FFN rows and
+vocabulary split N ways, NCCL all-reduces between the kernels): strong
+scaling, value = the sequence's tokens/s; --replicas instead decodes an
+independent replica per GPU (weak scaling).  Time is the max over ranks.
 """
 from __future__ import annotations
 
@@ -55,6 +58,8 @@ def parse_args():
     ap.add_argument("--multi-kernel", action="store_true",
                     help="run the step as 2 + 5*layers kernels (CUDA graph) instead of the "
                          "persistent single kernel")
+    ap.add_argument("--replicas", action="store_true",
+                    help="with --gpus N: N independent replicas instead of one tensor-parallel group")
     return ap.parse_args()
 
 
@@ -212,7 +217,9 @@ def workload(cfg, args):
         "batch": 1,
         "ctx": cfg.ctx,
         "l2": "inputs larger than L2 (weights streamed per step exceed the 126 MB L2)",
-        "parallelism": "replicas" if args.gpus > 1 else "single GPU",
+        "parallelism": ("single GPU" if args.gpus <= 1 else
+                        f"dp{args.gpus} (independent replicas)" if args.replicas else
+                        f"tp{args.gpus} (tensor parallel over NCCL)"),
     }
 
 
@@ -254,7 +261,15 @@ def run_ours(args):
     path = synth.ensure_gguf(cfg)
     torch.cuda.set_device(local)
     flags = runtime.FLAG_MULTI_KERNEL if args.multi_kernel else 0
-    m = runtime.CudaModel(path, cfg.ctx, device=local, flags=flags)
+    tp = world if (world > 1 and not args.replicas) else 1
+    if tp > 1:
+        nid = [runtime.tp_unique_id() if rank == 0 else None]
+        pg.broadcast_object_list(nid, src=0)
+        m = runtime.CudaModel(path, cfg.ctx, device=local, flags=flags, tp_rank=rank, tp_size=tp,
+                              tp_nccl_id=nid[0])
+    else:
+        m = runtime.CudaModel(path, cfg.ctx, device=local, flags=flags)
+    seqs = world // tp  # sequences decoded concurrently by the whole job
     prompt = synth.prompt_tokens(cfg)
     P, W, K = len(prompt), args.warmup, args.steps
     if P + W + K + 1 > cfg.ctx:
@@ -291,7 +306,7 @@ def run_ours(args):
         ms = float(t.item())
         pg.barrier()
     ms_per_step = ms / K
-    value = world * K / (ms / 1000.0)
+    value = seqs * K / (ms / 1000.0)
     stats = m.stats()
 
     # ---- end to end through the public C ABI with host buffers: per step the
@@ -317,7 +332,7 @@ def run_ours(args):
             t = torch.tensor([dt], device="cuda")
             pg.all_reduce(t, op=pg.ReduceOp.MAX)
             dt = float(t.item())
-        e2e = {"value": round(world * K / dt, 2), "unit": "tokens/s",
+        e2e = {"value": round(seqs * K / dt, 2), "unit": "tokens/s",
                "h2d_bytes_per_step": 4 + 8, "d2h_bytes_per_step": 4 * m.vocab + 4 + 4,
                "api": "ss_cuda_forward (host token in, host logits + argmax out, synchronous)"}
 
@@ -326,7 +341,9 @@ def run_ours(args):
     # the GGUF's bytes per weight + norms + one embedding row + the int8 K/V
     # read and append at the average timed position), its duration the CUDA-
     # event time per step above.  Multi-kernel step: the gate/up GEMV (2*ff*d
-    # weights), timed live in isolated back-to-back launches.
+    # weights; this rank's ff/tp rows under tensor parallelism), timed live in
+    # isolated back-to-back launches.  The step roofline of a tensor-parallel
+    # group is the whole model's bytes per token against tp GPUs' bandwidth.
     peak, peak_kind = hbm_peak()
     step_bytes = cfg.token_bytes(P + W + (K - 1) / 2.0)
     step_gbs = step_bytes / (ms_per_step / 1000.0) / 1e9
@@ -337,7 +354,8 @@ def run_ours(args):
     else:
         kernel_name = "gate/up GEMV + RMSNorm + SwiGLU"
         bpw = 18 / 32 if cfg.wtype == 2 else 34 / 32
-        k_bytes = 2 * cfg.ffn * cfg.d_model * bpw + cfg.d_model * 4 * 2 + cfg.ffn * 4
+        ff_l = cfg.ffn // tp
+        k_bytes = 2 * ff_l * cfg.d_model * bpw + cfg.d_model * 4 * 2 + ff_l * 4
         k_ms = m.time_kernel("gate_up", 3 * cfg.n_layers)
         achieved = k_bytes / (k_ms / 1000.0) / 1e9
         traffic = read_profile_traffic("gemv_gate_up", cfg.name)
@@ -348,7 +366,8 @@ def run_ours(args):
         line = {
             "metric": "decode tokens/s (batch 1)", "value": round(value, 2), "unit": "tokens/s",
             "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms_per_step, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "strong" if tp > 1 else "weak",
+            "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init GGUF, N(0,0.02) quantized)",
             "config": workload(cfg, args),
             "roofline": {"bound": "hbm", "kernel": kernel_name,
@@ -357,12 +376,14 @@ def run_ours(args):
                          "bytes_per_launch": int(k_bytes), "ms_per_launch": round(k_ms, 5),
                          "traffic": traffic},
             "step_roofline": {"bytes_per_step": int(step_bytes), "achieved": round(step_gbs, 1),
-                              "frac": round(step_gbs / peak, 4), "unit": "GB/s",
-                              "peak_source": peak_kind},
+                              "frac": round(step_gbs / (tp * peak), 4), "unit": "GB/s",
+                              "peak": round(tp * peak, 1), "peak_source": peak_kind,
+                              "gpus_per_sequence": tp},
             "e2e": e2e,
             "gpu_launches": int(stats["kernels_per_step"] * K),
             "clocks": sampler.summary(),
-            "step_impl": "persistent single kernel" if stats["persistent"] else "multi-kernel CUDA graph",
+            "step_impl": ("persistent single kernel" if stats["persistent"] else
+                          "multi-kernel CUDA graph" + (" with NCCL all-reduces" if tp > 1 else "")),
             "pdl": bool(stats["pdl"]),
             "first_ids": ids[:8],
         }

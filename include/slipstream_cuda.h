@@ -55,6 +55,12 @@ typedef struct {
     uint32_t max_batch;        /* sequences decoded together (>= 1) */
     uint64_t hbm_budget_bytes; /* 0 = every layer resident in HBM */
     uint32_t flags;            /* SS_CUDA_FLAG_* */
+    /* Tensor parallelism (one process per GPU): tp_size GPUs share one model,
+     * Q/K/V and gate/up sharded by heads / rows, O and down by columns (an
+     * all-reduce after each), lm_head by vocabulary rows.  0 or 1 = off. */
+    int32_t tp_rank;
+    int32_t tp_size;
+    uint8_t tp_nccl_id[128];   /* from ss_cuda_tp_unique_id on rank 0, the same on every rank */
 } ss_cuda_options_t;
 
 #define SS_CUDA_FLAG_NO_PDL 1u   /* launch without programmatic dependent launch */
@@ -66,8 +72,13 @@ typedef struct {
 /* Record a per-phase timeline of every persistent step (measurement aid). */
 #define SS_CUDA_FLAG_TRACE 8u
 
-/* Fills defaults: device -1, context 0, batch 1, no budget, no flags. */
+/* Fills defaults: device -1, context 0, batch 1, no budget, no flags, no
+ * tensor parallelism. */
 void ss_cuda_default_options(ss_cuda_options_t *opts);
+
+/* An NCCL unique id (128 bytes) for a tensor-parallel group: call on rank 0,
+ * hand the bytes to every rank's ss_cuda_options_t.tp_nccl_id. */
+int ss_cuda_tp_unique_id(uint8_t *id_out);
 
 /* ---- lifecycle (twin of ss_metal_init / ss_metal_free, metal_backend.h:21,75) ----
  * Uploads and repacks every weight tensor of the llama GGUF held in
@@ -85,7 +96,8 @@ const char *ss_cuda_last_error(void);
 int ss_cuda_abi_version(void);
 
 /* dims[0..11] = vocab, hidden, layers, heads, kv_heads, head_dim, ffn,
- * context (positions), rope_dim, weight type, max_batch, device. */
+ * context (positions), rope_dim, weight type, max_batch, device (the whole
+ * model's, also under tensor parallelism). */
 int ss_cuda_model_dims(const ss_cuda_ctx_t *ctx, int32_t *dims);
 
 /* Counters (no reference counterpart; profiling aid like the recap at
@@ -201,7 +213,9 @@ int ss_cuda_argmax_noalloc(const float *d_values, int32_t n, int32_t *d_index, v
 int ss_cuda_dequantize_tensor(ss_cuda_ctx_t *ctx, const char *name, float *out, int64_t n);
 /* Device dequantisation of raw GGUF blocks (host in, host out); no context. */
 int ss_cuda_dequantize(int32_t type, const void *blocks, int64_t n, float *out);
-/* int8 K/V row and scales of (layer, pos) (layer_scheduler.h:19-34 layout). */
+/* int8 K/V row and scales of (layer, pos) (layer_scheduler.h:19-34 layout).
+ * Under tensor parallelism: this rank's kv heads (n_kv_heads / tp_size * head_dim
+ * bytes each), with the group-wide scale. */
 int ss_cuda_kv_row(ss_cuda_ctx_t *ctx, int32_t layer, int32_t pos, int8_t *k, int8_t *v,
                    float *k_scale, float *v_scale);
 

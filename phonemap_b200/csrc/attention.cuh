@@ -32,7 +32,7 @@ struct AttnParams {
   int8_t* vc;
   float* ks;                 // this layer's scales [ctx]
   float* vs;
-  const unsigned int* amax_k;  // this layer's |k| maxima [ctx]
+  const unsigned int* amax_k;  // this layer's |k| maximum of the current position (one slot)
   const unsigned int* amax_v;
   const int* d_pos;
   float* out;                // [nh*hd]
@@ -116,8 +116,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
   // this step's q (all heads of the group) and the scales of row `pos`
   float k_scale = 0.0f, v_scale = 0.0f;
   if (pos_ok) {
-    k_scale = __uint_as_float(p.amax_k[pos]) / 127.0f;  // layer_scheduler.c:109-110
-    v_scale = __uint_as_float(p.amax_v[pos]) / 127.0f;
+    k_scale = __uint_as_float(*p.amax_k) / 127.0f;  // layer_scheduler.c:109-110
+    v_scale = __uint_as_float(*p.amax_v) / 127.0f;
   }
   for (int idx = tid; idx < g * HD; idx += kAttnThreads) {
     const int h = idx / HD, i = idx - h * HD;

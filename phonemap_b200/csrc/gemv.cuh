@@ -62,9 +62,12 @@ struct GemvParams {
   int q_rows, kv_rows, head_dim, rope_dim;
   const float2* rope_tab;    // [ctx][rope_dim/2] (cos, sin)
   const int* d_pos;
-  unsigned int* amax_k;      // slot for (layer, pos) = amax_k[pos] (already offset by layer)
+  unsigned int* amax_k;      // this layer's slot for the current position's maximum
   unsigned int* amax_v;
   // Argmax epilogue
+  int index_base;               // global index of row 0 (tensor parallelism: vocab slice start)
+  unsigned long long* tp_best;  // non-null: the last CTA leaves the packed best here (an
+                                // all-reduce and tp_finish_kernel complete the step)
   unsigned long long* am_part;  // one packed (value, index) per CTA
   unsigned int* am_count;
   int* seq_tokens;              // token of every position
@@ -465,7 +468,9 @@ __global__ void __launch_bounds__(544) gemv_kernel(const GemvParams p) {
     for (int lr = tid; lr < nrows; lr += blockDim.x) {
       const int r = r0 + lr;
       float v = row_sum(lr);
-      if constexpr (EPI == Epi::Residual) v = __fadd_rn(v, p.residual[r]);
+      // (tensor parallelism: only rank 0 adds the residual before the all-reduce)
+      if constexpr (EPI == Epi::Residual)
+        if (p.residual) v = __fadd_rn(v, p.residual[r]);
       p.out[r] = v;
     }
   } else if constexpr (EPI == Epi::SwiGLU) {
@@ -508,8 +513,8 @@ __global__ void __launch_bounds__(544) gemv_kernel(const GemvParams p) {
     if (tid == 0) {
       float a = 0.0f, b = 0.0f;
       for (int w = 0; w < nw; w++) { a = fmaxf(a, scratch[w]); b = fmaxf(b, scratch[32 + w]); }
-      if (a > 0.0f) atomicMax(p.amax_k + pos, float_as_ordered(a));
-      if (b > 0.0f) atomicMax(p.amax_v + pos, float_as_ordered(b));
+      if (a > 0.0f) atomicMax(p.amax_k, float_as_ordered(a));
+      if (b > 0.0f) atomicMax(p.amax_v, float_as_ordered(b));
     }
   } else if constexpr (EPI == Epi::Argmax) {
     unsigned long long best = 0;
@@ -517,7 +522,7 @@ __global__ void __launch_bounds__(544) gemv_kernel(const GemvParams p) {
       const int r = r0 + lr;
       const float v = row_sum(lr);
       if (p.out) p.out[r] = v;
-      const unsigned long long pk = pack_argmax(v, r);
+      const unsigned long long pk = pack_argmax(v, p.index_base + r);
       best = pk > best ? pk : best;
     }
 #pragma unroll
@@ -551,7 +556,12 @@ __global__ void __launch_bounds__(544) gemv_kernel(const GemvParams p) {
       }
       if (lane == 0) wbest[warp] = b;
       __syncthreads();
-      if (tid == 0) {
+      if (tid == 0 && p.tp_best) {
+        unsigned long long bb = 0;
+        for (int w = 0; w < nw; w++) bb = wbest[w] > bb ? wbest[w] : bb;
+        *p.tp_best = bb;
+        *p.am_count = 0;
+      } else if (tid == 0) {
         unsigned long long bb = 0;
         for (int w = 0; w < nw; w++) bb = wbest[w] > bb ? wbest[w] : bb;
         const int tok = unpack_argmax_index(bb);

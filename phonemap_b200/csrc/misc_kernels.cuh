@@ -5,16 +5,15 @@
 namespace ss {
 
 // Step entry: h = token_embd[token at pos] (SlipStream/src/core/layer_scheduler.c:
-// 584-587, F32 embeddings) and clear this position's |k| / |v| maxima slots of
-// every layer before the QKV GEMVs accumulate into them.
+// 584-587, F32 embeddings) and clear the |k| / |v| maxima slots of every layer
+// before the QKV GEMVs accumulate into them.
 struct EmbedParams {
   const float* embd;    // [vocab][d] fp32
   int d, vocab, n_layers, ctx;
   const int* seq_tokens;
   const int* d_pos;
   float* h;
-  unsigned int* amax_k;  // [L][ctx]
-  unsigned int* amax_v;
+  unsigned int* amax;    // [L][2]: |k|, |v| maxima of the current position
   int* err;
 };
 
@@ -34,20 +33,31 @@ __global__ void embed_kernel(const EmbedParams p) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.d; i += gridDim.x * blockDim.x)
     p.h[i] = row[i];
   if (blockIdx.x == 0)
-    for (int l = threadIdx.x; l < p.n_layers; l += blockDim.x) {
-      p.amax_k[(size_t)l * p.ctx + pos] = 0u;
-      p.amax_v[(size_t)l * p.ctx + pos] = 0u;
-    }
+    for (int i = threadIdx.x; i < 2 * p.n_layers; i += blockDim.x) p.amax[i] = 0u;
   pdl_trigger();
+}
+
+// Tensor parallelism: the argmax all-reduce left the global best (value, index)
+// in *best; write the token of pos + 1 and advance the position, as the
+// argmax epilogue does without tensor parallelism.
+__global__ void tp_finish_kernel(const unsigned long long* best, int* d_pos, const int* fixed_until,
+                                 int* seq_tokens, int ctx) {
+  const int tok = 0x7fffffff - (int)(unsigned)(*best & 0xffffffffu);
+  const int pos = *d_pos;
+  if (pos + 1 < ctx && pos + 1 >= *fixed_until) seq_tokens[pos + 1] = tok;
+  seq_tokens[ctx] = tok;
+  *d_pos = pos + 1;
 }
 
 // GGUF blocks (AoS, 18 B Q4_0 / 34 B Q8_0 per 32 weights) -> row-interleaved
 // layout (see gemv.cuh).  Source row r goes to destination row
 // r * dst_row_mul + dst_row_add, so gate/up rows can be interleaved and
-// Q/K/V stacked.  One thread per block.
+// Q/K/V stacked; of each source row (src_nb blocks) blocks src_b0 .. src_b0 +
+// cols/32 are taken (a column slice, for tensor parallelism).  One thread per
+// block.
 __global__ void repack_kernel(const uint8_t* __restrict__ src, int rows, int cols, int type,
                               uint8_t* __restrict__ dst, int row_stride, int scale_off,
-                              int dst_row_mul, int dst_row_add) {
+                              int dst_row_mul, int dst_row_add, int src_nb, int src_b0) {
   const int nb = cols / 32;
   const int bsz = type == kQ4_0 ? 18 : 34;
   const int qsz = bsz - 2;
@@ -55,7 +65,7 @@ __global__ void repack_kernel(const uint8_t* __restrict__ src, int rows, int col
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
     const int r = (int)(i / nb), b = (int)(i - (long long)r * nb);
-    const uint8_t* s = src + i * bsz;
+    const uint8_t* s = src + ((long long)r * src_nb + src_b0 + b) * bsz;
     uint8_t* drow = dst + (size_t)(r * dst_row_mul + dst_row_add) * row_stride;
     drow[scale_off + 2 * b] = s[0];
     drow[scale_off + 2 * b + 1] = s[1];
@@ -68,7 +78,7 @@ __global__ void repack_kernel(const uint8_t* __restrict__ src, int rows, int col
 // goes to destination row r * dst_row_mul + dst_row_add.
 __global__ void repack_tiled_kernel(const uint8_t* __restrict__ src, int rows, int cols, int type,
                                     uint8_t* __restrict__ dst, int tile_bytes, int dst_row_mul,
-                                    int dst_row_add) {
+                                    int dst_row_add, int src_nb, int src_b0) {
   const int nb = cols / 32;
   const int bsz = type == kQ4_0 ? 18 : 34;
   const int qsz = bsz - 2;
@@ -76,7 +86,7 @@ __global__ void repack_tiled_kernel(const uint8_t* __restrict__ src, int rows, i
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
     const int r = (int)(i / nb), b = (int)(i - (long long)r * nb);
-    const uint8_t* s = src + i * bsz;
+    const uint8_t* s = src + ((long long)r * src_nb + src_b0 + b) * bsz;
     const int R = r * dst_row_mul + dst_row_add;
     uint8_t* tile = dst + (size_t)(R >> 2) * tile_bytes;
     const int ri = R & 3;

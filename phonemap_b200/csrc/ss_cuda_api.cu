@@ -55,6 +55,14 @@ struct Error : std::runtime_error {
     }                                                                                     \
   } while (0)
 
+#define NK(call)                                                                          \
+  do {                                                                                    \
+    ncclResult_t r_ = (call);                                                             \
+    if (r_ != ncclSuccess)                                                                \
+      fail(SS_CUDA_ERROR_BACKEND, "%s failed: %s (%s:%d)", #call,                         \
+           nccl_api().GetErrorString(r_), __FILE__, __LINE__);                            \
+  } while (0)
+
 template <typename F>
 int guard(F&& f) {
   try {
@@ -225,29 +233,37 @@ size_t matrix_bytes(const DevMatrix& m) {
   return m.tiled ? (size_t)m.ntiles * m.tile_bytes : (size_t)m.rows * m.row_stride;
 }
 
-// Uploads one GGUF matrix (rows x cols blocks) through the staging buffer and
-// repacks it into rows dst_row_mul*r + dst_row_add of `dst`.
+// Uploads rows [row0, row0 + nrows) of one GGUF matrix through the staging
+// buffer, and of each row the 32-column blocks [b0, b0 + dst.cols / 32) (the
+// whole row when not sharded), repacked into rows dst_row_mul*r + dst_row_add
+// of `dst`.  nrows < 0: all rows.
 void upload_matrix(Context* c, const GgufTensor& t, const DevMatrix& dst, int dst_row_mul,
-                   int dst_row_add, uint8_t* stage, size_t stage_cap) {
+                   int dst_row_add, uint8_t* stage, size_t stage_cap, int row0 = 0, int nrows = -1,
+                   int b0 = 0) {
   if (t.type != dst.type)
     fail(SS_CUDA_ERROR_INVALID_MODEL, "tensor %s has type %d, expected %d", t.name.c_str(), t.type,
          dst.type);
-  if ((int)t.cols() != dst.cols)
-    fail(SS_CUDA_ERROR_INVALID_MODEL, "tensor %s has %llu columns, expected %d", t.name.c_str(),
-         (unsigned long long)t.cols(), dst.cols);
-  if (t.bytes > stage_cap) fail(SS_CUDA_ERROR_BACKEND, "staging buffer too small");
-  CK(cudaMemcpyAsync(stage, t.data, t.bytes, cudaMemcpyHostToDevice, c->stream));
-  const long long blocks = (long long)t.rows() * (t.cols() / 32);
+  const int src_nb = (int)(t.cols() / 32), nb = dst.cols / 32;
+  if (nrows < 0) nrows = (int)t.rows() - row0;
+  if (b0 < 0 || b0 + nb > src_nb || row0 < 0 || row0 + nrows > (int)t.rows())
+    fail(SS_CUDA_ERROR_INVALID_MODEL, "tensor %s: slice rows %d+%d blocks %d+%d outside %llu x %d",
+         t.name.c_str(), row0, nrows, b0, nb, (unsigned long long)t.rows(), src_nb);
+  const size_t row_bytes = (size_t)src_nb * ggml_type_size(t.type);
+  const size_t bytes = (size_t)nrows * row_bytes;
+  if (bytes > stage_cap) fail(SS_CUDA_ERROR_BACKEND, "staging buffer too small");
+  CK(cudaMemcpyAsync(stage, t.data + (size_t)row0 * row_bytes, bytes, cudaMemcpyHostToDevice,
+                     c->stream));
+  const long long blocks = (long long)nrows * nb;
   const int threads = 256;
   const int grid = (int)std::min<long long>((blocks + threads - 1) / threads, 65535);
   if (dst.tiled)
-    repack_tiled_kernel<<<grid, threads, 0, c->stream>>>(stage, (int)t.rows(), (int)t.cols(), t.type,
-                                                         dst.data, dst.tile_bytes, dst_row_mul,
-                                                         dst_row_add);
+    repack_tiled_kernel<<<grid, threads, 0, c->stream>>>(stage, nrows, dst.cols, t.type, dst.data,
+                                                         dst.tile_bytes, dst_row_mul, dst_row_add,
+                                                         src_nb, b0);
   else
-    repack_kernel<<<grid, threads, 0, c->stream>>>(stage, (int)t.rows(), (int)t.cols(), t.type,
-                                                   dst.data, dst.row_stride, dst.scale_off,
-                                                   dst_row_mul, dst_row_add);
+    repack_kernel<<<grid, threads, 0, c->stream>>>(stage, nrows, dst.cols, t.type, dst.data,
+                                                   dst.row_stride, dst.scale_off, dst_row_mul,
+                                                   dst_row_add, src_nb, b0);
   CK(cudaGetLastError());
 }
 
@@ -382,6 +398,26 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
   if ((int)embd.rows() < vocab) vocab = (int)embd.rows();
   c->vocab = vocab;
   if (c->nh % c->nkv) fail(SS_CUDA_ERROR_INVALID_MODEL, "heads %% kv_heads != 0");
+  // tensor parallelism: this rank keeps nh/tp q heads, nkv/tp kv heads, ff/tp
+  // FFN rows and vocab/tp lm_head rows; c->nh, c->nkv, c->ff become the local
+  // counts (the full ones stay in *_full)
+  c->nh_full = c->nh;
+  c->nkv_full = c->nkv;
+  c->ff_full = c->ff;
+  c->vocab_l = c->vocab;
+  c->vocab_off = 0;
+  if (c->tp_size > 1) {
+    const int tp = c->tp_size;
+    if (c->nh % tp || c->nkv % tp || c->ff % (32 * tp) || c->vocab % tp)
+      fail(SS_CUDA_ERROR_INVALID_MODEL,
+           "tensor parallelism %d needs heads (%d), kv heads (%d), ffn/32 (%d) and vocab (%d) divisible by it",
+           tp, c->nh, c->nkv, c->ff / 32, c->vocab);
+    c->nh /= tp;
+    c->nkv /= tp;
+    c->ff /= tp;
+    c->vocab_l = c->vocab / tp;
+    c->vocab_off = c->tp_rank * c->vocab_l;
+  }
   if (c->nh / c->nkv > 8) fail(SS_CUDA_ERROR_INVALID_MODEL, "GQA group above 8 is not supported");
   if (c->hd % 32 || c->hd > 256 || c->rope_dim > c->hd || c->rope_dim % 2)
     fail(SS_CUDA_ERROR_INVALID_MODEL, "head_dim %d / rope_dim %d unsupported", c->hd, c->rope_dim);
@@ -394,11 +430,12 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
     fail(SS_CUDA_ERROR_INVALID_MODEL, "weight type %d unsupported (Q4_0 / Q8_0)", c->wtype);
   c->attn_scale = 1.0f / sqrtf((float)c->hd);  // layer_scheduler.c:421
 
-  const int qd = c->nh * c->hd, kvd = c->nkv * c->hd;
+  const int qd = c->nh * c->hd, kvd = c->nkv * c->hd;  // this rank's
+  const int r = c->tp_rank;
   if (!out) fail(SS_CUDA_ERROR_INVALID_MODEL, "tied embeddings (no output.weight) unsupported");
   if (out->type != kQ4_0 && out->type != kQ8_0)
     fail(SS_CUDA_ERROR_INVALID_MODEL, "output.weight type %d unsupported", out->type);
-  c->mega = c->mega && plan_step(c, out->type);
+  c->mega = c->mega && c->tp_size <= 1 && plan_step(c, out->type);
   auto mat_layout = [&](int rows, int cols, int type) {
     return c->mega ? layout_tiled(rows, cols, type) : layout(rows, cols, type);
   };
@@ -437,9 +474,11 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
       const GgufTensor& wg = need(g, nm("ffn_gate.weight"));
       const GgufTensor& wu = need(g, nm("ffn_up.weight"));
       const GgufTensor& wd = need(g, nm("ffn_down.weight"));
-      if ((int)wq.rows() != qd || (int)wk.rows() != kvd || (int)wv.rows() != kvd ||
-          (int)wo.rows() != c->d || (int)wo.cols() != qd || (int)wg.rows() != c->ff ||
-          (int)wu.rows() != c->ff || (int)wd.rows() != c->d || (int)wd.cols() != c->ff)
+      const int qd_f = c->nh_full * c->hd, kvd_f = c->nkv_full * c->hd;
+      if ((int)wq.rows() != qd_f || (int)wk.rows() != kvd_f || (int)wv.rows() != kvd_f ||
+          (int)wo.rows() != c->d || (int)wo.cols() != qd_f || (int)wg.rows() != c->ff_full ||
+          (int)wu.rows() != c->ff_full || (int)wd.rows() != c->d || (int)wd.cols() != c->ff_full ||
+          (int)wq.cols() != c->d || (int)wg.cols() != c->d)
         fail(SS_CUDA_ERROR_INVALID_MODEL, "layer %d tensor shapes do not match the metadata", l);
       ly.qkv = s_qkv;
       ly.o = s_o;
@@ -451,13 +490,15 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
       ly.gu.data = ly.block + o_gu;
       ly.down.data = ly.block + o_down;
       c->weight_bytes += matrix_bytes(s_qkv) + matrix_bytes(s_o) + matrix_bytes(s_gu) + matrix_bytes(s_down);
-      upload_matrix(c, wq, ly.qkv, 1, 0, stage, max_bytes);
-      upload_matrix(c, wk, ly.qkv, 1, qd, stage, max_bytes);
-      upload_matrix(c, wv, ly.qkv, 1, qd + kvd, stage, max_bytes);
-      upload_matrix(c, wo, ly.o, 1, 0, stage, max_bytes);
-      upload_matrix(c, wg, ly.gu, 2, 0, stage, max_bytes);
-      upload_matrix(c, wu, ly.gu, 2, 1, stage, max_bytes);
-      upload_matrix(c, wd, ly.down, 1, 0, stage, max_bytes);
+      // rank r's shard (the whole matrix without tensor parallelism): rows of
+      // its heads / FFN rows, and for O and down the matching column blocks
+      upload_matrix(c, wq, ly.qkv, 1, 0, stage, max_bytes, r * qd, qd);
+      upload_matrix(c, wk, ly.qkv, 1, qd, stage, max_bytes, r * kvd, kvd);
+      upload_matrix(c, wv, ly.qkv, 1, qd + kvd, stage, max_bytes, r * kvd, kvd);
+      upload_matrix(c, wo, ly.o, 1, 0, stage, max_bytes, 0, -1, r * qd / 32);
+      upload_matrix(c, wg, ly.gu, 2, 0, stage, max_bytes, r * c->ff, c->ff);
+      upload_matrix(c, wu, ly.gu, 2, 1, stage, max_bytes, r * c->ff, c->ff);
+      upload_matrix(c, wd, ly.down, 1, 0, stage, max_bytes, 0, -1, r * c->ff / 32);
       ly.attn_norm = c->attn_norm_all + (size_t)l * c->d;
       ly.ffn_norm = c->ffn_norm_all + (size_t)l * c->d;
       upload_f32_into(c, need(g, nm("attn_norm.weight")), (size_t)c->d, ly.attn_norm);
@@ -465,15 +506,13 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
       CK(cudaStreamSynchronize(c->stream));  // staging buffer reuse
     }
     c->out_norm = upload_f32(c, need(g, "output_norm.weight"), (size_t)c->d);
-    c->lm_head = mat_layout(c->vocab, c->d, out->type);
+    c->lm_head = mat_layout(c->vocab_l, c->d, out->type);
     c->lm_block = dev_alloc<uint8_t>(c, matrix_bytes(c->lm_head));
     c->lm_head.data = c->lm_block;
     c->weight_bytes += matrix_bytes(c->lm_head);
-    // only the first `vocab` rows are addressable (layer_scheduler.c:189-197)
-    GgufTensor head = *out;
-    head.dims[1] = (uint64_t)c->vocab;
-    head.bytes = (uint64_t)c->vocab * (head.cols() / 32) * ggml_type_size(head.type);
-    upload_matrix(c, head, c->lm_head, 1, 0, stage, max_bytes);
+    // only the first `vocab` rows are addressable (layer_scheduler.c:189-197);
+    // this rank's slice of them
+    upload_matrix(c, *out, c->lm_head, 1, 0, stage, max_bytes, c->vocab_off, c->vocab_l);
     CK(cudaStreamSynchronize(c->stream));
   } catch (...) {
     cudaFree(stage);
@@ -491,14 +530,18 @@ void alloc_state(Context* c) {
   c->vc = dev_alloc<int8_t>(c, rows * kvd);
   c->ks = dev_alloc<float>(c, rows);
   c->vs = dev_alloc<float>(c, rows);
-  c->amax_k = dev_alloc<unsigned int>(c, rows);
-  c->amax_v = dev_alloc<unsigned int>(c, rows);
+  c->amax = dev_alloc<unsigned int>(c, 2 * (size_t)c->L);
   c->kv_bytes = rows * (2 * (size_t)kvd + 16);
   c->h = dev_alloc<float>(c, (size_t)c->d);
   c->qkv = dev_alloc<float>(c, (size_t)qd + 2 * kvd);
   c->attn_out = dev_alloc<float>(c, (size_t)std::max(qd, c->d));
   c->act = dev_alloc<float>(c, (size_t)c->ff);
-  c->logits = dev_alloc<float>(c, (size_t)c->vocab);
+  c->logits = dev_alloc<float>(c, (size_t)c->vocab_l);
+  if (c->tp_size > 1) {
+    c->hpart = dev_alloc<float>(c, (size_t)c->d);
+    c->tp_best = dev_alloc<unsigned long long>(c, 1);
+    c->logits_full = dev_alloc<float>(c, (size_t)c->vocab);
+  }
   // attention: position splits of one kv head form a thread-block cluster
   // (at most 8, the portable cluster size); ~2 CTAs per SM over the kv heads
   c->attn_nsplit = std::max(1, std::min(8, (2 * c->sm_count + c->nkv - 1) / c->nkv));
@@ -655,14 +698,13 @@ GemvParams base_params(Context* c) {
 
 void launch_embed(Context* c, bool pdl) {
   EmbedParams e{c->embd, c->d, c->vocab, c->L, c->ctx, c->seq_tokens, &c->ctrl->pos,
-                c->h, c->amax_k, c->amax_v, &c->ctrl->err};
+                c->h, c->amax, &c->ctrl->err};
   launch(embed_kernel, dim3(c->embed_blocks), dim3(256), 0, c->stream, pdl, e);
 }
 
 // RMSNorm(h) -> [Wq;Wk;Wv] -> RoPE(q, k), |k| / |v| maxima of this position.
 void launch_qkv(Context* c, int l, bool pdl) {
   const Layer& ly = c->layers[(size_t)l];
-  const size_t lo = (size_t)l * c->ctx;
   GemvParams p = base_params(c);
   p.w = ly.qkv.q();
   p.x = c->h;
@@ -673,8 +715,8 @@ void launch_qkv(Context* c, int l, bool pdl) {
   p.head_dim = c->hd;
   p.rope_dim = c->rope_dim;
   p.rope_tab = c->rope_tab;
-  p.amax_k = c->amax_k + lo;
-  p.amax_v = c->amax_v + lo;
+  p.amax_k = c->amax + 2 * (size_t)l;
+  p.amax_v = c->amax + 2 * (size_t)l + 1;
   run_gemv(c, c->g_qkv, p, pdl);
 }
 
@@ -688,8 +730,8 @@ void launch_attn(Context* c, int l, bool pdl) {
   a.vc = c->vc + lo * kvd;
   a.ks = c->ks + lo;
   a.vs = c->vs + lo;
-  a.amax_k = c->amax_k + lo;
-  a.amax_v = c->amax_v + lo;
+  a.amax_k = c->amax + 2 * (size_t)l;
+  a.amax_v = c->amax + 2 * (size_t)l + 1;
   a.d_pos = &c->ctrl->pos;
   a.out = c->attn_out;
   a.nh = c->nh;
@@ -715,14 +757,23 @@ void launch_attn(Context* c, int l, bool pdl) {
   CK(cudaLaunchKernelEx(&cfg, attn_fn(c->hd), a));
 }
 
-// h = Wo . attn + h
+// Tensor parallelism: sum of the ranks' row-parallel partials into h.  Rank
+// 0's partial already holds the residual, so the sum is h + W . x.
+void tp_reduce_h(Context* c) {
+  NK(nccl_api().AllReduce(c->hpart, c->h, (size_t)c->d, ncclFloat32, ncclSum, c->comm, c->stream));
+}
+
+// h = Wo . attn + h  (tensor parallelism: this rank's heads' columns, then the
+// all-reduce)
 void launch_o(Context* c, int l, bool pdl) {
   GemvParams p = base_params(c);
   p.w = c->layers[(size_t)l].o.q();
   p.x = c->attn_out;
-  p.out = c->h;
-  p.residual = c->h;
+  const bool tp = c->tp_size > 1;
+  p.out = tp ? c->hpart : c->h;
+  p.residual = (!tp || c->tp_rank == 0) ? c->h : nullptr;
   run_gemv(c, c->g_o, p, pdl);
+  if (tp) tp_reduce_h(c);
 }
 
 // act = up * silu(gate) of RMSNorm(h)
@@ -736,14 +787,17 @@ void launch_gu(Context* c, int l, bool pdl) {
   run_gemv(c, c->g_gu, p, pdl);
 }
 
-// h = Wdown . act + h
+// h = Wdown . act + h  (tensor parallelism: this rank's FFN columns, then
+// the all-reduce)
 void launch_down(Context* c, int l, bool pdl) {
   GemvParams p = base_params(c);
   p.w = c->layers[(size_t)l].down.q();
   p.x = c->act;
-  p.out = c->h;
-  p.residual = c->h;
+  const bool tp = c->tp_size > 1;
+  p.out = tp ? c->hpart : c->h;
+  p.residual = (!tp || c->tp_rank == 0) ? c->h : nullptr;
   run_gemv(c, c->g_down, p, pdl);
+  if (tp) tp_reduce_h(c);
 }
 
 // logits = W_out . RMSNorm(h); greedy argmax -> token of pos + 1; pos += 1.
@@ -758,6 +812,17 @@ void launch_head(Context* c, bool pdl) {
   p.seq_tokens = c->seq_tokens;
   p.fixed_until = &c->ctrl->fixed_until;
   p.d_pos_rw = &c->ctrl->pos;
+  if (c->tp_size > 1) {
+    // this rank's vocab slice: its best (value, global index) -> max over the
+    // ranks -> the token of pos + 1 (the same packed order as one GPU's)
+    p.index_base = c->vocab_off;
+    p.tp_best = c->tp_best;
+    run_gemv(c, c->g_head, p, pdl);
+    NK(nccl_api().AllReduce(c->tp_best, c->tp_best, 1, ncclUint64, ncclMax, c->comm, c->stream));
+    launch(tp_finish_kernel, dim3(1), dim3(1), 0, c->stream, false, (const unsigned long long*)c->tp_best,
+           &c->ctrl->pos, (const int*)&c->ctrl->fixed_until, c->seq_tokens, c->ctx);
+    return;
+  }
   run_gemv(c, c->g_head, p, pdl);
 }
 
@@ -770,6 +835,9 @@ void enqueue_step(Context* c, bool pdl) {
   launch_embed(c, pdl);
   for (int l = 0; l < c->L; l++) {
     launch_qkv(c, l, pdl);
+    if (c->tp_size > 1)  // one int8 scale over the whole kv_dim: max over the ranks' slices
+      NK(nccl_api().AllReduce(c->amax + 2 * (size_t)l, c->amax + 2 * (size_t)l, 2, ncclUint32, ncclMax,
+                              c->comm, c->stream));
     launch_attn(c, l, pdl);
     launch_o(c, l, pdl);
     launch_gu(c, l, pdl);
@@ -850,7 +918,12 @@ void check_device_error(Context* c) {
 }
 
 void read_logits(Context* c, float* dst) {
-  CK(cudaMemcpyAsync(c->h_logits, c->logits, sizeof(float) * c->vocab, cudaMemcpyDeviceToHost, c->stream));
+  const float* src = c->logits;
+  if (c->tp_size > 1) {  // every rank gathers the full logits (a collective: all ranks call it)
+    NK(nccl_api().AllGather(c->logits, c->logits_full, (size_t)c->vocab_l, ncclFloat32, c->comm, c->stream));
+    src = c->logits_full;
+  }
+  CK(cudaMemcpyAsync(c->h_logits, src, sizeof(float) * c->vocab, cudaMemcpyDeviceToHost, c->stream));
   CK(cudaMemcpyAsync(&c->h_small[16], c->seq_tokens + c->ctx, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
   check_device_error(c);
   if (dst && dst != c->h_logits) memcpy(dst, c->h_logits, sizeof(float) * c->vocab);
@@ -884,7 +957,22 @@ Context* create(const uint8_t* base, uint64_t size, const ss_cuda_options_t* o) 
   c->tuning = read_tuning();
   c->mega = !(opts.flags & SS_CUDA_FLAG_MULTI_KERNEL) && !getenv("SS_CUDA_MULTI_KERNEL");
   c->trace = (opts.flags & SS_CUDA_FLAG_TRACE) != 0;
+  c->tp_size = opts.tp_size > 1 ? opts.tp_size : 1;
+  c->tp_rank = c->tp_size > 1 ? opts.tp_rank : 0;
   try {
+    if (c->tp_size > 1) {
+      if (c->tp_rank < 0 || c->tp_rank >= c->tp_size)
+        fail(SS_CUDA_ERROR_INVALID_PARAMS, "tp_rank %d outside 0..%d", c->tp_rank, c->tp_size - 1);
+      if (!nccl_api().ok) fail(SS_CUDA_ERROR_BACKEND, "tensor parallelism needs libnccl.so.2 (not found)");
+      // the collectives sit between kernels of the multi-kernel step; a graph
+      // with NCCL inside is built without programmatic dependent launch
+      c->mega = false;
+      c->use_pdl = false;
+      ncclUniqueId id;
+      static_assert(sizeof(id) == sizeof(opts.tp_nccl_id), "NCCL unique id size");
+      memcpy(&id, opts.tp_nccl_id, sizeof(id));
+      NK(nccl_api().CommInitRank(&c->comm, c->tp_size, id, c->tp_rank));
+    }
     CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     if (base) {
       load_model(c, base, size, opts.context_size);
@@ -1052,7 +1140,8 @@ SS_API void ss_cuda_free(ss_cuda_ctx_t* ctx) {
   if (!c) return;
   cudaSetDevice(c->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
-  if (c->step_exec) cudaGraphExecDestroy(c->step_exec);
+  if (c->step_exec) cudaGraphExecDestroy(c->step_exec);  // before the communicator it uses
+  if (c->comm) nccl_api().CommDestroy(c->comm);
   for (void* p : c->allocations) cudaFree(p);
   for (auto& s : c->op_slots) {
     if (s.d_x) cudaFree(s.d_x);
@@ -1065,11 +1154,22 @@ SS_API void ss_cuda_free(ss_cuda_ctx_t* ctx) {
   delete c;
 }
 
+SS_API int ss_cuda_tp_unique_id(uint8_t* id_out) {
+  return guard([&] {
+    if (!id_out) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null argument");
+    if (!nccl_api().ok) fail(SS_CUDA_ERROR_BACKEND, "libnccl.so.2 not found");
+    ncclUniqueId id;
+    NK(nccl_api().GetUniqueId(&id));
+    memcpy(id_out, &id, sizeof(id));
+  });
+}
+
 SS_API int ss_cuda_model_dims(const ss_cuda_ctx_t* ctx, int32_t* dims) {
   return guard([&] {
     auto* c = reinterpret_cast<const Context*>(ctx);
     if (!c || !dims) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null argument");
-    const int32_t v[12] = {c->vocab, c->d, c->L, c->nh, c->nkv, c->hd, c->ff, c->ctx, c->rope_dim,
+    // the whole model's dimensions, also under tensor parallelism
+    const int32_t v[12] = {c->vocab, c->d, c->L, c->nh_full, c->nkv_full, c->hd, c->ff_full, c->ctx, c->rope_dim,
                            c->wtype, c->max_batch, c->device};
     memcpy(dims, v, sizeof(v));
   });
@@ -1079,7 +1179,7 @@ SS_API int ss_cuda_stats(const ss_cuda_ctx_t* ctx, int64_t* out, int32_t n) {
   return guard([&] {
     auto* c = reinterpret_cast<const Context*>(ctx);
     if (!c || !out) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null argument");
-    const int64_t v[10] = {c->has_model ? (c->mega ? 1 : 2 + 5LL * c->L) : 0,
+    const int64_t v[10] = {c->has_model ? (c->mega ? 1 : 2 + 5LL * c->L + (c->tp_size > 1)) : 0,
                            (int64_t)c->weight_bytes,
                            (int64_t)c->kv_bytes,
                            c->mega ? c->step_nsplit : c->attn_nsplit,
@@ -1168,8 +1268,7 @@ SS_API void ss_cuda_reset(ss_cuda_ctx_t* ctx) {
     CK(cudaMemsetAsync(c->vc, 0, rows * kvd, c->stream));
     CK(cudaMemsetAsync(c->ks, 0, rows * 4, c->stream));
     CK(cudaMemsetAsync(c->vs, 0, rows * 4, c->stream));
-    CK(cudaMemsetAsync(c->amax_k, 0, rows * 4, c->stream));
-    CK(cudaMemsetAsync(c->amax_v, 0, rows * 4, c->stream));
+    CK(cudaMemsetAsync(c->amax, 0, 2 * sizeof(unsigned) * c->L, c->stream));
     CK(cudaMemsetAsync(c->h, 0, sizeof(float) * c->d, c->stream));
     CK(cudaMemsetAsync(c->ctrl, 0, sizeof(Ctrl), c->stream));
     CK(cudaMemsetAsync(c->am_cnt, 0, sizeof(unsigned), c->stream));

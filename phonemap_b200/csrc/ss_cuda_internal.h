@@ -11,6 +11,7 @@
 #include "gemv.cuh"
 #include "misc_kernels.cuh"
 #include "step_kernel.cuh"
+#include "tp_nccl.h"
 
 namespace ss {
 
@@ -73,8 +74,17 @@ struct Context {
   GemvTuning tuning;
   std::atomic<bool> cancelled{false};
 
-  // model dims
+  // model dims (nh, nkv, ff: this rank's under tensor parallelism)
   int vocab = 0, d = 0, L = 0, nh = 0, nkv = 0, hd = 0, rope_dim = 0, ff = 0, ctx = 0, wtype = 0;
+  int nh_full = 0, nkv_full = 0, ff_full = 0;
+  int vocab_l = 0, vocab_off = 0;  // this rank's lm_head rows
+
+  // tensor parallelism (multi-kernel step + NCCL)
+  int tp_rank = 0, tp_size = 1;
+  ncclComm_t comm = nullptr;
+  float* hpart = nullptr;               // row-parallel partial outputs [d]
+  unsigned long long* tp_best = nullptr;  // packed (value, index) of the argmax
+  float* logits_full = nullptr;         // gathered logits [vocab]
   int max_batch = 1;
   float eps = 1e-5f, theta = 10000.0f, attn_scale = 1.0f;
 
@@ -95,8 +105,7 @@ struct Context {
   int8_t* vc = nullptr;
   float* ks = nullptr;
   float* vs = nullptr;
-  unsigned int* amax_k = nullptr;
-  unsigned int* amax_v = nullptr;
+  unsigned int* amax = nullptr;  // [L][2] |k|, |v| maxima of the current position
   size_t kv_bytes = 0;
 
   // activations / scratch

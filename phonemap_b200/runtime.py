@@ -33,7 +33,7 @@ EXPORTED = [
     "ss_cuda_decode_read", "ss_cuda_stream", "ss_cuda_reset", "ss_cuda_cancel",
     "ss_cuda_dequantize_tensor", "ss_cuda_dequantize", "ss_cuda_kv_row",
     "ss_cuda_time_kernel", "ss_cuda_kernel_bytes", "ss_cuda_argmax_noalloc",
-    "ss_cuda_step_trace",
+    "ss_cuda_step_trace", "ss_cuda_tp_unique_id",
 ]
 
 
@@ -48,6 +48,8 @@ class Options(ctypes.Structure):
         ("struct_size", ctypes.c_uint32), ("device", ctypes.c_int32),
         ("context_size", ctypes.c_uint32), ("max_batch", ctypes.c_uint32),
         ("hbm_budget_bytes", ctypes.c_uint64), ("flags", ctypes.c_uint32),
+        ("tp_rank", ctypes.c_int32), ("tp_size", ctypes.c_int32),
+        ("tp_nccl_id", ctypes.c_uint8 * 128),
     ]
 
 
@@ -111,6 +113,7 @@ def load_library() -> ctypes.CDLL:
     lib.ss_cuda_kernel_bytes.restype = ctypes.c_int64
     lib.ss_cuda_argmax_noalloc.argtypes = [vp, ctypes.c_int32, vp, vp]
     lib.ss_cuda_step_trace.argtypes = [vp, _i64p, ctypes.c_int64]
+    lib.ss_cuda_tp_unique_id.argtypes = [vp]
     _lib = lib
     return lib
 
@@ -137,14 +140,28 @@ def default_options(**kw) -> Options:
     return o
 
 
+def tp_unique_id() -> bytes:
+    """An NCCL unique id for a tensor-parallel group (call on rank 0)."""
+    buf = (ctypes.c_uint8 * 128)()
+    _check(load_library().ss_cuda_tp_unique_id(buf))
+    return bytes(buf)
+
+
 class CudaModel:
     """One decode context on one GPU (one sequence)."""
 
     def __init__(self, gguf_path: str | None, context_size: int = 0, device: int = -1,
-                 flags: int = 0):
+                 flags: int = 0, tp_rank: int = 0, tp_size: int = 1, tp_nccl_id: bytes = b""):
+        """tp_size > 1: this process is rank tp_rank of a tensor-parallel group
+        whose NCCL id (tp_unique_id() on rank 0) is tp_nccl_id."""
         lib = load_library()
         self._lib = lib
-        opts = default_options(context_size=context_size, device=device, flags=flags)
+        opts = default_options(context_size=context_size, device=device, flags=flags,
+                               tp_rank=tp_rank, tp_size=tp_size)
+        if tp_size > 1:
+            if len(tp_nccl_id) != 128:
+                raise ValueError("tp_nccl_id must be the 128 bytes of tp_unique_id()")
+            ctypes.memmove(opts.tp_nccl_id, tp_nccl_id, 128)
         if gguf_path is None:
             h = lib.ss_cuda_init(None, 0, ctypes.byref(opts))
         else:
@@ -152,6 +169,7 @@ class CudaModel:
         if not h:
             raise SSCudaError(-7, lib.ss_cuda_last_error().decode())
         self._h = ctypes.c_void_p(h)
+        self.tp_rank, self.tp_size = (tp_rank, tp_size) if tp_size > 1 else (0, 1)
         if gguf_path is not None:
             dims = np.zeros(12, np.int32)
             _check(lib.ss_cuda_model_dims(self._h, _i(dims)))
@@ -253,7 +271,9 @@ class CudaModel:
         return out.reshape(rows, cols)
 
     def kv_row(self, layer: int, pos: int):
-        kvd = self.n_kv_heads * self.head_dim
+        """int8 K/V row of one position (this rank's kv heads under tensor
+        parallelism) and its two scales."""
+        kvd = self.n_kv_heads // self.tp_size * self.head_dim
         k = np.empty(kvd, np.int8)
         v = np.empty(kvd, np.int8)
         ks = np.zeros(1, np.float32)
