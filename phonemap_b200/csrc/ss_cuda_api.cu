@@ -331,7 +331,7 @@ bool plan_step(Context* c, int htype) {
   struct Shape { int rows, cols, type; };
   const Shape shapes[5] = {{qd + 2 * kvd, c->d, c->wtype}, {c->d, qd, c->wtype},
                            {2 * c->ff, c->d, c->wtype}, {c->d, c->ff, c->wtype},
-                           {c->vocab, c->d, htype}};
+                           {c->vocab_l, c->d, htype}};
   int slot = 0;
   size_t red = 0;
   for (const Shape& sh : shapes) {
@@ -435,6 +435,7 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
   if (!out) fail(SS_CUDA_ERROR_INVALID_MODEL, "tied embeddings (no output.weight) unsupported");
   if (out->type != kQ4_0 && out->type != kQ8_0)
     fail(SS_CUDA_ERROR_INVALID_MODEL, "output.weight type %d unsupported", out->type);
+  // tensor parallelism runs the multi-kernel step (NCCL between kernels)
   c->mega = c->mega && c->tp_size <= 1 && plan_step(c, out->type);
   auto mat_layout = [&](int rows, int cols, int type) {
     return c->mega ? layout_tiled(rows, cols, type) : layout(rows, cols, type);
@@ -929,6 +930,31 @@ void read_logits(Context* c, float* dst) {
   if (dst && dst != c->h_logits) memcpy(dst, c->h_logits, sizeof(float) * c->vocab);
 }
 
+// Tensor parallelism: all ranks have reached this point (a collective on the
+// library's communicator, then a host wait).
+void tp_barrier(Context* c) {
+  NK(nccl_api().AllReduce(c->tp_best, c->tp_best, 1, ncclUint64, ncclMax, c->comm, c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+}
+
+// Tensor parallelism, after the model is loaded on every rank: every rank
+// must have planned the same step (an all-gather of the plan), then a barrier.
+void tp_setup(Context* c) {
+  const int tp = c->tp_size;
+  int* dv = dev_alloc<int>(c, 2 * (size_t)tp);
+  c->h_small[0] = c->mega ? 1 : 0;
+  c->h_small[1] = c->mega ? c->step_grid : 0;
+  CK(cudaMemcpyAsync(dv + 2 * c->tp_rank, c->h_small, 2 * sizeof(int), cudaMemcpyHostToDevice, c->stream));
+  NK(nccl_api().AllGather(dv + 2 * c->tp_rank, dv, 2, ncclInt32, c->comm, c->stream));
+  CK(cudaMemcpyAsync(c->h_small, dv, 2 * sizeof(int) * tp, cudaMemcpyDeviceToHost, c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+  for (int r = 1; r < tp; r++)
+    if (c->h_small[2 * r] != c->h_small[0] || c->h_small[2 * r + 1] != c->h_small[1])
+      fail(SS_CUDA_ERROR_BACKEND, "tensor-parallel ranks planned different steps (rank 0: %d/%d, rank %d: %d/%d)",
+           c->h_small[0], c->h_small[1], r, c->h_small[2 * r], c->h_small[2 * r + 1]);
+  tp_barrier(c);
+}
+
 Context* create(const uint8_t* base, uint64_t size, const ss_cuda_options_t* o) {
   ss_cuda_options_t opts;
   ss_cuda_default_options(&opts);
@@ -978,6 +1004,7 @@ Context* create(const uint8_t* base, uint64_t size, const ss_cuda_options_t* o) 
       load_model(c, base, size, opts.context_size);
       alloc_state(c);
       plan_all(c);
+      if (c->tp_size > 1) tp_setup(c);
       CK(cudaStreamSynchronize(c->stream));
       c->has_model = true;
     }

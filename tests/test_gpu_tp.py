@@ -4,7 +4,9 @@ identical (a divergence only where the reference's own top-2 lie within the
 logit tolerance), logits within the tolerance, and rank 0's int8 K/V row --
 its kv heads, quantised with the scale of the whole kv_dim after the max
 all-reduce -- within one quantisation step of the reference's.  Sharding
-changes only the fp32 summation order of the O and down projections."""
+changes only the fp32 summation order of the O and down projections.  Tensor
+parallelism runs the multi-kernel step (NCCL between its kernels), whatever
+step the flags ask for."""
 from __future__ import annotations
 
 import numpy as np
@@ -12,7 +14,7 @@ import pytest
 
 from phonemap_b200 import configs, synth, tp
 from tests.conftest import load_golden, rel_err
-from tests.test_gpu_decode import _acceptable_choice, logit_tol
+from tests.test_gpu_decode import PATHS, _acceptable_choice, logit_tol
 
 pytestmark = pytest.mark.gpu
 
@@ -31,8 +33,9 @@ CASES = [(2, "tiny"), (2, "tiny-mha"), (2, "tiny-q8"), (2, "tinyllama"), (2, "ll
          (4, "tinyllama"), (4, "llama2-7b"), (8, "llama2-7b")]
 
 
+@pytest.mark.parametrize("path", ["multi-kernel"])
 @pytest.mark.parametrize("n,name", CASES, ids=[f"tp{n}-{m}" for n, m in CASES])
-def test_tp_greedy_parity(n, name):
+def test_tp_greedy_parity(n, name, path):
     if _gpus() < n:
         pytest.skip(f"needs {n} GPUs")
     cfg = configs.get(name)
@@ -41,7 +44,7 @@ def test_tp_greedy_parity(n, name):
     tol = logit_tol(name)
     prompt = [int(t) for t in g["prompt"]]
     ref = [int(t) for t in g["ids"]]
-    r = tp.greedy(synth.ensure_gguf(cfg), int(g["ctx"]), prompt, len(ref), n,
+    r = tp.greedy(synth.ensure_gguf(cfg), int(g["ctx"]), prompt, len(ref), n, flags=PATHS[path],
                   kv_at=(int(g["kv_layer"]), int(g["kv_pos"])))
     assert r["stats"]["persistent"] == 0
     ids, logits = r["ids"], r["logits"]
@@ -60,8 +63,9 @@ def test_tp_greedy_parity(n, name):
     np.testing.assert_allclose([ks, vs], g["kv_scales"], rtol=max(1e-3, tol))
 
 
+@pytest.mark.parametrize("path", ["multi-kernel"])
 @pytest.mark.parametrize("name", ["tiny", "tinyllama"])
-def test_tp_teacher_forced(name):
+def test_tp_teacher_forced(name, path):
     """Every step fed the reference's token: logits at the reference's top-4
     within the tolerance, argmax the reference's wherever its margin exceeds
     the tolerance."""
@@ -72,7 +76,7 @@ def test_tp_teacher_forced(name):
     tol = logit_tol(name)
     ref = [int(t) for t in g["ids"]]
     r = tp.greedy(synth.ensure_gguf(cfg), int(g["ctx"]), [int(t) for t in g["prompt"]], len(ref), 2,
-                  teacher=ref)
+                  teacher=ref, flags=PATHS[path])
     for s in range(len(ref)):
         top, vals, am = g["topk_ids"][s], g["topk_vals"][s], float(g["absmax"][s])
         assert np.abs(r["logits"][s][top] - vals).max() / am < tol, f"step {s}"
