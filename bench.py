@@ -58,6 +58,9 @@ def parse_args():
     ap.add_argument("--multi-kernel", action="store_true",
                     help="run the step as 2 + 5*layers kernels (CUDA graph) instead of the "
                          "persistent single kernel")
+    ap.add_argument("--hbm-budget-layers", type=float, default=None,
+                    help="HBM budget for the layers' weights, in layers (layer streaming); "
+                         "default 4 for llama2-13b (its configuration), else all resident")
     ap.add_argument("--replicas", action="store_true",
                     help="with --gpus N: N independent replicas instead of one tensor-parallel group")
     return ap.parse_args()
@@ -220,7 +223,18 @@ def workload(cfg, args):
         "parallelism": ("single GPU" if args.gpus <= 1 else
                         f"dp{args.gpus} (independent replicas)" if args.replicas else
                         f"tp{args.gpus} (tensor parallel over NCCL)"),
+        **({"hbm_budget_layers": budget_layers_of(cfg, args),
+            "weights": f"{'Q4_0' if cfg.wtype == 2 else 'Q8_0'}, layers past the resident ones "
+                       "copied from the host-mapped model file every step (layer streaming)"}
+           if budget_layers_of(cfg, args) else {}),
     }
+
+
+def budget_layers_of(cfg, args):
+    """HBM budget for the layers' weights, in layers (0: all resident)."""
+    if args.hbm_budget_layers is not None:
+        return args.hbm_budget_layers
+    return 4 if cfg.name == "llama2-13b" else 0
 
 
 def run_reference(args):
@@ -262,7 +276,13 @@ def run_ours(args):
     torch.cuda.set_device(local)
     flags = runtime.FLAG_MULTI_KERNEL if args.multi_kernel else 0
     tp = world if (world > 1 and not args.replicas) else 1
-    if tp > 1:
+    budget_layers = budget_layers_of(cfg, args)
+    budget = int(budget_layers * (cfg.layer_bytes() + 4096)) if budget_layers else 0
+    if budget and tp > 1:
+        raise SystemExit("layer streaming runs on one GPU (use --replicas with --gpus N)")
+    if budget:
+        m = runtime.CudaModel(path, cfg.ctx, device=local, flags=flags, hbm_budget_bytes=budget)
+    elif tp > 1:
         nid = [runtime.tp_unique_id() if rank == 0 else None]
         pg.broadcast_object_list(nid, src=0)
         m = runtime.CudaModel(path, cfg.ctx, device=local, flags=flags, tp_rank=rank, tp_size=tp,
@@ -347,6 +367,19 @@ def run_ours(args):
     peak, peak_kind = hbm_peak()
     step_bytes = cfg.token_bytes(P + W + (K - 1) / 2.0)
     step_gbs = step_bytes / (ms_per_step / 1000.0) / 1e9
+    host_link = None
+    if stats["streamed_bytes"]:
+        # layer streaming: the step is bound by the host-to-device copies of the
+        # streamed layers; their rate against a measured pinned-memory copy
+        h2d = measure_h2d_gbs(local)
+        got = stats["streamed_bytes"] / (ms_per_step / 1000.0) / 1e9
+        host_link = {"bound": "host-link", "bytes_per_step": int(stats["streamed_bytes"]),
+                     "achieved": round(got, 2), "peak": round(h2d, 2), "unit": "GB/s",
+                     "frac": round(got / h2d, 4),
+                     "peak_source": "measured here: 1 GiB pinned host-to-device cudaMemcpyAsync",
+                     "resident_layers": stats["resident_layers"], "layers": cfg.n_layers,
+                     "source": {1: "registered model mapping", 2: "pinned host copy",
+                                3: "pageable memory"}.get(stats["stream_source"], "?")}
     if stats["persistent"]:
         kernel_name = "decode_step_kernel (persistent: the whole decode step)"
         k_bytes, k_ms, achieved = step_bytes, ms_per_step, step_gbs
@@ -381,6 +414,7 @@ def run_ours(args):
                               "gpus_per_sequence": tp},
             "e2e": e2e,
             "gpu_launches": int(stats["kernels_per_step"] * K),
+            **({"host_link": host_link} if host_link else {}),
             "clocks": sampler.summary(),
             "step_impl": ("persistent single kernel" if stats["persistent"] else
                           "multi-kernel CUDA graph" + (" with NCCL all-reduces" if tp > 1 else "")),
@@ -396,6 +430,27 @@ def run_ours(args):
         pg.barrier()
         pg.destroy_process_group()
     return 0
+
+
+def measure_h2d_gbs(device: int) -> float:
+    """Pinned host-to-device copy bandwidth (1 GiB, 3 copies after a warm-up)."""
+    import torch
+    n = 1 << 30
+    src = torch.empty(n, dtype=torch.uint8, pin_memory=True)
+    dst = torch.empty(n, dtype=torch.uint8, device=f"cuda:{device}")
+    s = torch.cuda.Stream(device=device)
+    with torch.cuda.stream(s):
+        dst.copy_(src, non_blocking=True)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(3):
+            dst.copy_(src, non_blocking=True)
+        e1.record(s)
+    e1.synchronize()
+    gbs = 3 * n / (e0.elapsed_time(e1) / 1000.0) / 1e9
+    del src, dst
+    return gbs
 
 
 def run_profile_kernel(args):

@@ -53,7 +53,13 @@ typedef struct {
     int32_t device;            /* CUDA ordinal; -1 = $SS_CUDA_DEVICE or 0 */
     uint32_t context_size;     /* positions (0 = GGUF context_length), capped at 8192 as engine.c:103-106 */
     uint32_t max_batch;        /* sequences decoded together (>= 1) */
-    uint64_t hbm_budget_bytes; /* 0 = every layer resident in HBM */
+    /* Bytes of HBM for the layers' weights; 0 = every layer resident.  When the
+     * layers need more, layers past the first (budget / layer bytes - 3) stay in
+     * host memory and are copied into two HBM slots every step (layer
+     * streaming; needs room for 3 layers, single GPU, multi-kernel step).  The
+     * GGUF bytes given to ss_cuda_init must then stay mapped while the context
+     * lives (ss_cuda_init_file keeps its own mapping). */
+    uint64_t hbm_budget_bytes;
     uint32_t flags;            /* SS_CUDA_FLAG_* */
     /* Tensor parallelism (one process per GPU): tp_size GPUs share one model,
      * Q/K/V and gate/up sharded by heads / rows, O and down by columns (an
@@ -106,7 +112,11 @@ int ss_cuda_model_dims(const ss_cuda_ctx_t *ctx, int32_t *dims);
  * the step graph chains kernels with programmatic dependent launch, [5] decode
  * steps run, [6] CTAs of the QKV GEMV, [7] CTAs of the down GEMV (both: the
  * grid of the persistent step), [8] 1 when the step is the single persistent
- * kernel, [9] its weight-ring slots. */
+ * kernel, [9] its weight-ring slots, [10] layers resident in HBM (all of them
+ * unless streaming), [11] bytes copied from host memory per step (layer
+ * streaming), [12] device bytes of one layer's four matrices, [13] where
+ * streamed layers are copied from: 1 the registered model mapping, 2 a pinned
+ * host copy, 3 pageable memory (0: not streaming). */
 int ss_cuda_stats(const ss_cuda_ctx_t *ctx, int64_t *out, int32_t n);
 
 /* Measurement aid, no reference counterpart: times `iters` back-to-back

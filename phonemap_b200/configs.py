@@ -52,12 +52,16 @@ class ModelConfig:
         blob = json.dumps({k: getattr(self, k) for k in keys}, sort_keys=True)
         return hashlib.sha1(blob.encode()).hexdigest()[:12]
 
+    def layer_bytes(self) -> int:
+        """GGUF bytes of one layer's seven quantized matrices."""
+        bpw = 18 / 32 if self.wtype == Q4_0 else 34 / 32
+        d, qd, kvd, ff = self.d_model, self.n_heads * self.head_dim, self.kv_dim, self.ffn
+        return int((d * qd + 2 * d * kvd + qd * d + 3 * d * ff) * bpw)
+
     def weight_bytes(self) -> int:
         """Quantized bytes streamed per decode token (all layers + lm_head)."""
         bpw = 18 / 32 if self.wtype == Q4_0 else 34 / 32
-        d, qd, kvd, ff = self.d_model, self.n_heads * self.head_dim, self.kv_dim, self.ffn
-        per_layer = (d * qd + 2 * d * kvd + qd * d + 3 * d * ff) * bpw
-        return int(per_layer * self.n_layers + self.vocab * d * bpw)
+        return int(self.layer_bytes() * self.n_layers + self.vocab * self.d_model * bpw)
 
     def token_bytes(self, pos: float) -> float:
         """Algorithmic HBM bytes for one decode token at position ``pos``.

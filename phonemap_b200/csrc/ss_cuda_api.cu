@@ -19,6 +19,7 @@
 #include <cstring>
 #include <stdexcept>
 #include <string>
+#include <thread>
 
 #include "gguf_view.h"
 #include "slipstream_cuda.h"
@@ -233,6 +234,22 @@ size_t matrix_bytes(const DevMatrix& m) {
   return m.tiled ? (size_t)m.ntiles * m.tile_bytes : (size_t)m.rows * m.row_stride;
 }
 
+// Repacks nrows GGUF rows (src_nb blocks each, already in device memory) into
+// rows dst_row_mul*r + dst_row_add of `dst`, taking blocks [b0, b0 + dst.cols/32).
+void repack_into(const uint8_t* src, int nrows, int src_nb, int b0, int type, const DevMatrix& dst,
+                 int dst_row_mul, int dst_row_add, cudaStream_t stream) {
+  const long long blocks = (long long)nrows * (dst.cols / 32);
+  const int threads = 256;
+  const int grid = (int)std::min<long long>((blocks + threads - 1) / threads, 65535);
+  if (dst.tiled)
+    repack_tiled_kernel<<<grid, threads, 0, stream>>>(src, nrows, dst.cols, type, dst.data, dst.tile_bytes,
+                                                      dst_row_mul, dst_row_add, src_nb, b0);
+  else
+    repack_kernel<<<grid, threads, 0, stream>>>(src, nrows, dst.cols, type, dst.data, dst.row_stride,
+                                                dst.scale_off, dst_row_mul, dst_row_add, src_nb, b0);
+  CK(cudaGetLastError());
+}
+
 // Uploads rows [row0, row0 + nrows) of one GGUF matrix through the staging
 // buffer, and of each row the 32-column blocks [b0, b0 + dst.cols / 32) (the
 // whole row when not sharded), repacked into rows dst_row_mul*r + dst_row_add
@@ -253,18 +270,7 @@ void upload_matrix(Context* c, const GgufTensor& t, const DevMatrix& dst, int ds
   if (bytes > stage_cap) fail(SS_CUDA_ERROR_BACKEND, "staging buffer too small");
   CK(cudaMemcpyAsync(stage, t.data + (size_t)row0 * row_bytes, bytes, cudaMemcpyHostToDevice,
                      c->stream));
-  const long long blocks = (long long)nrows * nb;
-  const int threads = 256;
-  const int grid = (int)std::min<long long>((blocks + threads - 1) / threads, 65535);
-  if (dst.tiled)
-    repack_tiled_kernel<<<grid, threads, 0, c->stream>>>(stage, nrows, dst.cols, t.type, dst.data,
-                                                         dst.tile_bytes, dst_row_mul, dst_row_add,
-                                                         src_nb, b0);
-  else
-    repack_kernel<<<grid, threads, 0, c->stream>>>(stage, nrows, dst.cols, t.type, dst.data,
-                                                   dst.row_stride, dst.scale_off, dst_row_mul,
-                                                   dst_row_add, src_nb, b0);
-  CK(cudaGetLastError());
+  repack_into(stage, nrows, src_nb, b0, t.type, dst, dst_row_mul, dst_row_add, c->stream);
 }
 
 const GgufTensor& need(const GgufModel& m, const std::string& name) {
@@ -435,8 +441,19 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
   if (!out) fail(SS_CUDA_ERROR_INVALID_MODEL, "tied embeddings (no output.weight) unsupported");
   if (out->type != kQ4_0 && out->type != kQ8_0)
     fail(SS_CUDA_ERROR_INVALID_MODEL, "output.weight type %d unsupported", out->type);
-  // tensor parallelism runs the multi-kernel step (NCCL between kernels)
-  c->mega = c->mega && c->tp_size <= 1 && plan_step(c, out->type);
+  // layer streaming: the layers' GGUF bytes exceed the HBM budget
+  {
+    uint64_t raw = 0;
+    for (const char* nm : {"attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"})
+      raw += need(g, std::string("blk.0.") + nm + ".weight").bytes;
+    if (c->hbm_budget && raw * (uint64_t)c->L > c->hbm_budget) {
+      if (c->tp_size > 1)
+        fail(SS_CUDA_ERROR_INVALID_PARAMS, "layer streaming with tensor parallelism is not supported");
+      c->streaming = true;
+    }
+  }
+  // tensor parallelism and layer streaming run the multi-kernel step
+  c->mega = c->mega && c->tp_size <= 1 && !c->streaming && plan_step(c, out->type);
   auto mat_layout = [&](int rows, int cols, int type) {
     return c->mega ? layout_tiled(rows, cols, type) : layout(rows, cols, type);
   };
@@ -461,8 +478,23 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
     const size_t o_gu = o_o + round_up_sz(matrix_bytes(s_o), 256);
     const size_t o_down = o_gu + round_up_sz(matrix_bytes(s_gu), 256);
     c->layer_stride = o_down + round_up_sz(matrix_bytes(s_down), 256);
-    uint8_t* slab = dev_alloc<uint8_t>(c, c->layer_stride * (size_t)c->L);
-    CK(cudaMemsetAsync(slab, 0, c->layer_stride * (size_t)c->L, c->stream));
+    // streaming: the budget holds the resident layers, two slots and the raw
+    // bytes of the layer being repacked (about one more layer)
+    int hbm_layers = c->L;
+    c->n_resident = c->L;
+    if (c->streaming) {
+      const uint64_t fit = c->hbm_budget / c->layer_stride;
+      if (fit < 3)
+        fail(SS_CUDA_ERROR_INVALID_PARAMS,
+             "HBM budget of %llu bytes holds %llu layers of %zu bytes; streaming needs 3 (two slots and "
+             "the staging of one layer)",
+             (unsigned long long)c->hbm_budget, (unsigned long long)fit, c->layer_stride);
+      c->n_resident = (int)std::min<uint64_t>(fit - 3, (uint64_t)c->L - 2);
+      hbm_layers = c->n_resident + 2;
+      c->stream_src.resize((size_t)c->L);
+    }
+    uint8_t* slab = dev_alloc<uint8_t>(c, c->layer_stride * (size_t)hbm_layers);
+    CK(cudaMemsetAsync(slab, 0, c->layer_stride * (size_t)hbm_layers, c->stream));
     c->attn_norm_all = dev_alloc<float>(c, (size_t)c->L * c->d);
     c->ffn_norm_all = dev_alloc<float>(c, (size_t)c->L * c->d);
     for (int l = 0; l < c->L; l++) {
@@ -485,12 +517,40 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
       ly.o = s_o;
       ly.gu = s_gu;
       ly.down = s_down;
-      ly.block = slab + (size_t)l * c->layer_stride;
+      const int place = l < c->n_resident ? l : c->n_resident + (l - c->n_resident) % 2;
+      ly.block = slab + (size_t)place * c->layer_stride;
       ly.qkv.data = ly.block;
       ly.o.data = ly.block + o_o;
       ly.gu.data = ly.block + o_gu;
       ly.down.data = ly.block + o_down;
-      c->weight_bytes += matrix_bytes(s_qkv) + matrix_bytes(s_o) + matrix_bytes(s_gu) + matrix_bytes(s_down);
+      if (l < c->n_resident || !c->streaming)
+        c->weight_bytes += matrix_bytes(s_qkv) + matrix_bytes(s_o) + matrix_bytes(s_gu) + matrix_bytes(s_down);
+      ly.attn_norm = c->attn_norm_all + (size_t)l * c->d;
+      ly.ffn_norm = c->ffn_norm_all + (size_t)l * c->d;
+      upload_f32_into(c, need(g, nm("attn_norm.weight")), (size_t)c->d, ly.attn_norm);
+      upload_f32_into(c, need(g, nm("ffn_norm.weight")), (size_t)c->d, ly.ffn_norm);
+      if (l >= c->n_resident) {
+        // streamed: remember where its bytes are; every step copies them in
+        auto& src = c->stream_src[(size_t)l];
+        const GgufTensor* ts[7] = {&wq, &wk, &wv, &wo, &wg, &wu, &wd};
+        const int which[7] = {0, 0, 0, 1, 2, 2, 3}, mul[7] = {1, 1, 1, 1, 2, 2, 1},
+                  add[7] = {0, qd, qd + kvd, 0, 0, 1, 0};
+        size_t off = 0;
+        for (int i = 0; i < 7; i++) {
+          Context::StreamTensor st;
+          st.t = *ts[i];
+          st.raw_off = off;
+          st.which = which[i];
+          st.mul = mul[i];
+          st.add = add[i];
+          src.push_back(st);
+          off += round_up_sz(ts[i]->bytes, 256);
+        }
+        c->stream_raw_bytes = std::max(c->stream_raw_bytes, off);
+        c->streamed_bytes += off;
+        CK(cudaStreamSynchronize(c->stream));
+        continue;
+      }
       // rank r's shard (the whole matrix without tensor parallelism): rows of
       // its heads / FFN rows, and for O and down the matching column blocks
       upload_matrix(c, wq, ly.qkv, 1, 0, stage, max_bytes, r * qd, qd);
@@ -500,10 +560,6 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
       upload_matrix(c, wg, ly.gu, 2, 0, stage, max_bytes, r * c->ff, c->ff);
       upload_matrix(c, wu, ly.gu, 2, 1, stage, max_bytes, r * c->ff, c->ff);
       upload_matrix(c, wd, ly.down, 1, 0, stage, max_bytes, 0, -1, r * c->ff / 32);
-      ly.attn_norm = c->attn_norm_all + (size_t)l * c->d;
-      ly.ffn_norm = c->ffn_norm_all + (size_t)l * c->d;
-      upload_f32_into(c, need(g, nm("attn_norm.weight")), (size_t)c->d, ly.attn_norm);
-      upload_f32_into(c, need(g, nm("ffn_norm.weight")), (size_t)c->d, ly.ffn_norm);
       CK(cudaStreamSynchronize(c->stream));  // staging buffer reuse
     }
     c->out_norm = upload_f32(c, need(g, "output_norm.weight"), (size_t)c->d);
@@ -511,6 +567,10 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
     c->lm_block = dev_alloc<uint8_t>(c, matrix_bytes(c->lm_head));
     c->lm_head.data = c->lm_block;
     c->weight_bytes += matrix_bytes(c->lm_head);
+    if (c->streaming) {
+      c->stream_raw = dev_alloc<uint8_t>(c, c->stream_raw_bytes);
+      c->weight_bytes += 2 * c->layer_stride + c->stream_raw_bytes;  // the slots and the staging
+    }
     // only the first `vocab` rows are addressable (layer_scheduler.c:189-197);
     // this rank's slice of them
     upload_matrix(c, *out, c->lm_head, 1, 0, stage, max_bytes, c->vocab_off, c->vocab_l);
@@ -827,14 +887,46 @@ void launch_head(Context* c, bool pdl) {
   run_gemv(c, c->g_head, p, pdl);
 }
 
+// Layer streaming: copies streamed layer l's GGUF bytes from host memory into
+// the staging buffer and repacks them into the layer's slot, on the copy
+// stream, then marks the slot ready.  The copy stream runs these in layer
+// order, so the staging buffer is free again when the next copy starts.
+void enqueue_layer_copy(Context* c, int l) {
+  const Layer& ly = c->layers[(size_t)l];
+  const int slot = (l - c->n_resident) % 2;
+  for (const Context::StreamTensor& st : c->stream_src[(size_t)l])
+    CK(cudaMemcpyAsync(c->stream_raw + st.raw_off, st.t.data, st.t.bytes, cudaMemcpyHostToDevice,
+                       c->copy_stream));
+  for (const Context::StreamTensor& st : c->stream_src[(size_t)l]) {
+    const DevMatrix& dst = st.which == 0 ? ly.qkv : st.which == 1 ? ly.o : st.which == 2 ? ly.gu : ly.down;
+    const int src_nb = (int)(st.t.cols() / 32);
+    repack_into(c->stream_raw + st.raw_off, (int)st.t.rows(), src_nb, 0, st.t.type, dst, st.mul, st.add,
+                c->copy_stream);
+  }
+  CK(cudaEventRecord(c->ev_ready[slot], c->copy_stream));
+}
+
 // Enqueues one decode step (embedding -> L layers -> lm_head + argmax).
+// Streaming: the first two streamed layers' copies start with the step (their
+// slots were last used by the previous step, which is complete in stream
+// order); every later one starts when the layer two before it, which used the
+// same slot, has finished its kernels.
 void enqueue_step(Context* c, bool pdl) {
   if (c->mega) {
     launch_step(c);
     return;
   }
+  const int R = c->n_resident;
+  if (c->streaming) {
+    CK(cudaEventRecord(c->ev_fork, c->stream));
+    CK(cudaStreamWaitEvent(c->copy_stream, c->ev_fork, 0));
+    enqueue_layer_copy(c, R);
+    enqueue_layer_copy(c, R + 1);
+  }
   launch_embed(c, pdl);
   for (int l = 0; l < c->L; l++) {
+    const bool streamed = c->streaming && l >= R;
+    if (streamed) CK(cudaStreamWaitEvent(c->stream, c->ev_ready[(l - R) % 2], 0));
     launch_qkv(c, l, pdl);
     if (c->tp_size > 1)  // one int8 scale over the whole kv_dim: max over the ranks' slices
       NK(nccl_api().AllReduce(c->amax + 2 * (size_t)l, c->amax + 2 * (size_t)l, 2, ncclUint32, ncclMax,
@@ -843,6 +935,12 @@ void enqueue_step(Context* c, bool pdl) {
     launch_o(c, l, pdl);
     launch_gu(c, l, pdl);
     launch_down(c, l, pdl);
+    if (streamed && l + 2 < c->L) {
+      const int slot = (l - R) % 2;
+      CK(cudaEventRecord(c->ev_free[slot], c->stream));
+      CK(cudaStreamWaitEvent(c->copy_stream, c->ev_free[slot], 0));
+      enqueue_layer_copy(c, l + 2);
+    }
   }
   launch_head(c, pdl);
 }
@@ -955,6 +1053,70 @@ void tp_setup(Context* c) {
   tp_barrier(c);
 }
 
+// Copies n bytes with a few host threads (a one-time copy of the streamed
+// layers into pinned memory).
+void parallel_memcpy(uint8_t* dst, const uint8_t* src, size_t n) {
+  const unsigned hw = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+  const size_t chunk = (n + hw - 1) / hw;
+  std::vector<std::thread> ts;
+  for (unsigned i = 0; i < hw; i++) {
+    const size_t a = (size_t)i * chunk, e = std::min(n, a + chunk);
+    if (a >= e) break;
+    ts.emplace_back([=] { memcpy(dst + a, src + a, e - a); });
+  }
+  for (auto& t : ts) t.join();
+}
+
+// Layer streaming: the copy stream and its events, and DMA-able sources for
+// the copies, so that they run at the host link's rate and can sit in the
+// step's CUDA graph: the model's bytes registered with CUDA (read-only), or,
+// where the platform does not register a read-only file mapping, the streamed
+// layers' bytes copied once into pinned host memory.  Only when neither is
+// possible do the copies come from pageable memory, which a graph cannot hold:
+// the step then runs without one.  The bytes must stay mapped while the
+// context lives (the registered case reads them every step).
+void setup_streaming(Context* c, const uint8_t* base, uint64_t size) {
+  c->use_pdl = false;  // the step is bound by the host link; plain stream order around the copies
+  CK(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking));
+  CK(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming));
+  for (int i = 0; i < 2; i++) {
+    CK(cudaEventCreateWithFlags(&c->ev_ready[i], cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&c->ev_free[i], cudaEventDisableTiming));
+  }
+  int ro = 0;
+  cudaDeviceGetAttribute(&ro, cudaDevAttrHostRegisterReadOnlySupported, c->device);
+  const uintptr_t page = (uintptr_t)sysconf(_SC_PAGESIZE);
+  const uintptr_t a = (uintptr_t)base & ~(page - 1);
+  const uintptr_t e = ((uintptr_t)base + size + page - 1) & ~(page - 1);
+  // SS_STREAM_SOURCE=pinned / pageable skips the better sources (test coverage
+  // of the fallbacks)
+  const char* force = getenv("SS_STREAM_SOURCE");
+  const bool allow_reg = !force || !strcmp(force, "registered");
+  const bool allow_pin = !force || strcmp(force, "pageable") != 0;
+  if (allow_reg && ro && cudaHostRegister((void*)a, e - a, cudaHostRegisterReadOnly) == cudaSuccess) {
+    c->host_reg = (void*)a;
+    return;
+  }
+  cudaGetLastError();
+  if (!allow_pin || cudaHostAlloc(&c->host_pinned, c->streamed_bytes, cudaHostAllocDefault) != cudaSuccess) {
+    cudaGetLastError();
+    c->host_pinned = nullptr;
+    c->use_graph = false;
+    return;
+  }
+  size_t at = 0;
+  for (auto& layer : c->stream_src) {
+    if (layer.empty()) continue;
+    size_t span = 0;
+    for (Context::StreamTensor& st : layer) {
+      parallel_memcpy(c->host_pinned + at + st.raw_off, st.t.data, st.t.bytes);
+      st.t.data = c->host_pinned + at + st.raw_off;
+      span = std::max(span, st.raw_off + round_up_sz(st.t.bytes, 256));
+    }
+    at += span;
+  }
+}
+
 Context* create(const uint8_t* base, uint64_t size, const ss_cuda_options_t* o) {
   ss_cuda_options_t opts;
   ss_cuda_default_options(&opts);
@@ -985,6 +1147,7 @@ Context* create(const uint8_t* base, uint64_t size, const ss_cuda_options_t* o) 
   c->trace = (opts.flags & SS_CUDA_FLAG_TRACE) != 0;
   c->tp_size = opts.tp_size > 1 ? opts.tp_size : 1;
   c->tp_rank = c->tp_size > 1 ? opts.tp_rank : 0;
+  c->hbm_budget = opts.hbm_budget_bytes;
   try {
     if (c->tp_size > 1) {
       if (c->tp_rank < 0 || c->tp_rank >= c->tp_size)
@@ -1002,6 +1165,7 @@ Context* create(const uint8_t* base, uint64_t size, const ss_cuda_options_t* o) 
     CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     if (base) {
       load_model(c, base, size, opts.context_size);
+      if (c->streaming) setup_streaming(c, base, size);
       alloc_state(c);
       plan_all(c);
       if (c->tp_size > 1) tp_setup(c);
@@ -1157,7 +1321,12 @@ SS_API ss_cuda_ctx_t* ss_cuda_init_file(const char* path, const ss_cuda_options_
       munmap(map, (size_t)st.st_size);
       throw;
     }
-    munmap(map, (size_t)st.st_size);
+    if (c->streaming) {  // streamed layers are read from the mapping every step
+      c->owned_map = map;
+      c->owned_map_bytes = (size_t)st.st_size;
+    } else {
+      munmap(map, (size_t)st.st_size);
+    }
   });
   return rc == SS_CUDA_OK ? reinterpret_cast<ss_cuda_ctx_t*>(c) : nullptr;
 }
@@ -1178,6 +1347,12 @@ SS_API void ss_cuda_free(ss_cuda_ctx_t* ctx) {
   if (c->h_logits) cudaFreeHost(c->h_logits);
   if (c->h_small) cudaFreeHost(c->h_small);
   if (c->stream) cudaStreamDestroy(c->stream);
+  if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
+  for (cudaEvent_t ev : {c->ev_fork, c->ev_ready[0], c->ev_ready[1], c->ev_free[0], c->ev_free[1]})
+    if (ev) cudaEventDestroy(ev);
+  if (c->host_reg) cudaHostUnregister(c->host_reg);
+  if (c->host_pinned) cudaFreeHost(c->host_pinned);
+  if (c->owned_map) munmap(c->owned_map, c->owned_map_bytes);
   delete c;
 }
 
@@ -1206,7 +1381,9 @@ SS_API int ss_cuda_stats(const ss_cuda_ctx_t* ctx, int64_t* out, int32_t n) {
   return guard([&] {
     auto* c = reinterpret_cast<const Context*>(ctx);
     if (!c || !out) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null argument");
-    const int64_t v[10] = {c->has_model ? (c->mega ? 1 : 2 + 5LL * c->L + (c->tp_size > 1)) : 0,
+    const int64_t v[14] = {c->has_model ? (c->mega ? 1 : 2 + 5LL * c->L + (c->tp_size > 1) +
+                                                   (c->streaming ? 7LL * (c->L - c->n_resident) : 0))
+                                       : 0,
                            (int64_t)c->weight_bytes,
                            (int64_t)c->kv_bytes,
                            c->mega ? c->step_nsplit : c->attn_nsplit,
@@ -1215,8 +1392,12 @@ SS_API int ss_cuda_stats(const ss_cuda_ctx_t* ctx, int64_t* out, int32_t n) {
                            c->mega ? c->step_grid : c->g_qkv.ctas,
                            c->mega ? c->step_grid : c->g_down.ctas,
                            c->mega ? 1 : 0,
-                           c->mega ? c->step_nslots : 0};
-    for (int i = 0; i < n && i < 10; i++) out[i] = v[i];
+                           c->mega ? c->step_nslots : 0,
+                           c->n_resident,
+                           (int64_t)c->streamed_bytes,
+                           (int64_t)c->layer_stride,
+                           !c->streaming ? 0 : c->host_reg ? 1 : c->host_pinned ? 2 : 3};
+    for (int i = 0; i < n && i < 14; i++) out[i] = v[i];
   });
 }
 
@@ -1420,6 +1601,14 @@ SS_API int ss_cuda_dequantize_tensor(ss_cuda_ctx_t* ctx, const char* name, float
     }
     if (!m) fail(SS_CUDA_ERROR_INVALID_PARAMS, "no quantized tensor %s", name);
     if (n != (int64_t)rows * m->cols) fail(SS_CUDA_ERROR_INVALID_PARAMS, "n must be rows*cols = %lld", (long long)rows * m->cols);
+    if (c->streaming && s.rfind("blk.", 0) == 0) {
+      const int l = atoi(s.c_str() + 4);
+      if (l >= c->n_resident) {  // a streamed layer: bring it into its slot first
+        CK(cudaStreamSynchronize(c->stream));
+        enqueue_layer_copy(c, l);
+        CK(cudaStreamWaitEvent(c->stream, c->ev_ready[(l - c->n_resident) % 2], 0));
+      }
+    }
     float* d_out = nullptr;
     CK(cudaMalloc(&d_out, sizeof(float) * (size_t)n));
     if (m->tiled)

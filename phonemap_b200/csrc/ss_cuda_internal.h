@@ -9,6 +9,7 @@
 
 #include "attention.cuh"
 #include "gemv.cuh"
+#include "gguf_view.h"
 #include "misc_kernels.cuh"
 #include "step_kernel.cuh"
 #include "tp_nccl.h"
@@ -98,6 +99,31 @@ struct Context {
   float* attn_norm_all = nullptr;    // [L][d]
   float* ffn_norm_all = nullptr;     // [L][d]
   size_t weight_bytes = 0;
+
+  // layer streaming (hbm_budget_bytes below the layers' size; multi-kernel
+  // step): layers [n_resident, L) stay in host memory and pass through two HBM
+  // slots every step -- layer l uses slot (l - n_resident) % 2.  Their GGUF
+  // bytes are copied by DMA into `stream_raw` on `copy_stream` and repacked
+  // into the slot; events order copy, repack and the layer's kernels.
+  struct StreamTensor {
+    GgufTensor t;          // the GGUF tensor (host pointer into the file)
+    size_t raw_off = 0;    // its place in stream_raw
+    int which = 0;         // 0 qkv, 1 o, 2 gu, 3 down (destination matrix)
+    int mul = 1, add = 0;  // destination rows mul * r + add
+  };
+  bool streaming = false;
+  int n_resident = 0;
+  uint64_t hbm_budget = 0;
+  std::vector<std::vector<StreamTensor>> stream_src;  // [layer] (empty for resident layers)
+  uint8_t* stream_raw = nullptr;
+  size_t stream_raw_bytes = 0;      // one layer's GGUF bytes (padded per tensor)
+  size_t streamed_bytes = 0;        // host-to-device bytes per step
+  cudaStream_t copy_stream = nullptr;
+  cudaEvent_t ev_fork = nullptr, ev_ready[2] = {nullptr, nullptr}, ev_free[2] = {nullptr, nullptr};
+  void* host_reg = nullptr;         // the model file's range registered with CUDA (read-only)
+  uint8_t* host_pinned = nullptr;   // else: the streamed layers' bytes copied into pinned memory
+  void* owned_map = nullptr;        // ss_cuda_init_file's mapping, kept while streaming
+  size_t owned_map_bytes = 0;
 
   // KV cache [L][nkv][ctx][hd] (head-major; the reference's is [L][ctx][kvd],
   // ss_cuda_kv_row gathers a position) + scales/maxima [L][ctx]

@@ -151,13 +151,17 @@ class CudaModel:
     """One decode context on one GPU (one sequence)."""
 
     def __init__(self, gguf_path: str | None, context_size: int = 0, device: int = -1,
-                 flags: int = 0, tp_rank: int = 0, tp_size: int = 1, tp_nccl_id: bytes = b""):
+                 flags: int = 0, tp_rank: int = 0, tp_size: int = 1, tp_nccl_id: bytes = b"",
+                 hbm_budget_bytes: int = 0):
         """tp_size > 1: this process is rank tp_rank of a tensor-parallel group
-        whose NCCL id (tp_unique_id() on rank 0) is tp_nccl_id."""
+        whose NCCL id (tp_unique_id() on rank 0) is tp_nccl_id.
+        hbm_budget_bytes > 0: HBM for the layers' weights; layers beyond it are
+        streamed from the model file every step (layer streaming)."""
         lib = load_library()
         self._lib = lib
         opts = default_options(context_size=context_size, device=device, flags=flags,
-                               tp_rank=tp_rank, tp_size=tp_size)
+                               tp_rank=tp_rank, tp_size=tp_size,
+                               hbm_budget_bytes=int(hbm_budget_bytes))
         if tp_size > 1:
             if len(tp_nccl_id) != 128:
                 raise ValueError("tp_nccl_id must be the 128 bytes of tp_unique_id()")
@@ -238,10 +242,11 @@ class CudaModel:
         return int(self._lib.ss_cuda_stream(self._h) or 0)
 
     def stats(self) -> dict:
-        v = np.zeros(10, np.int64)
-        _check(self._lib.ss_cuda_stats(self._h, v.ctypes.data_as(_i64p), 10))
+        v = np.zeros(14, np.int64)
+        _check(self._lib.ss_cuda_stats(self._h, v.ctypes.data_as(_i64p), 14))
         keys = ("kernels_per_step", "weight_bytes", "kv_bytes", "attn_splits", "pdl",
-                "steps_run", "qkv_ctas", "down_ctas", "persistent", "ring_slots")
+                "steps_run", "qkv_ctas", "down_ctas", "persistent", "ring_slots",
+                "resident_layers", "streamed_bytes", "layer_bytes", "stream_source")
         return {k: int(x) for k, x in zip(keys, v)}
 
     KERNELS = {"qkv": 0, "attention": 1, "o": 2, "gate_up": 3, "down": 4, "lm_head": 5, "step": 6}

@@ -1,0 +1,153 @@
+"""Layer streaming (hbm_budget_bytes below the layers' size): layers past the
+resident ones are copied from the model file into two HBM slots every step and
+repacked there.  The kernels and the weights they see are those of the
+resident multi-kernel step, so results must be bit-identical to it, and the
+reference's golden token IDs hold as for every other path."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from phonemap_b200 import configs, runtime, synth
+from tests.conftest import load_golden, rel_err
+from tests.test_gpu_decode import _acceptable_choice, logit_tol
+
+pytestmark = pytest.mark.gpu
+
+
+def _decode(m, prompt, steps):
+    buf = np.empty(m.vocab, np.float32)
+    ids = [m.prefill(prompt, 0, logits=buf)]
+    logits = [buf.copy()]
+    pos = len(prompt)
+    for _ in range(1, steps):
+        ids.append(m.forward(ids[-1], pos, logits=buf))
+        logits.append(buf.copy())
+        pos += 1
+    return ids, logits
+
+
+def _layer_bytes(path, ctx):
+    with runtime.CudaModel(path, ctx, flags=runtime.FLAG_MULTI_KERNEL) as m:
+        return m.stats()["layer_bytes"]
+
+
+@pytest.mark.parametrize("flags", [0, runtime.FLAG_NO_GRAPH], ids=["graph", "no-graph"])
+def test_streaming_bit_identical_to_resident(flags):
+    name = "tinyllama"
+    g = load_golden(name)
+    cfg = configs.get(name)
+    path = synth.ensure_gguf(cfg)
+    ctx = int(g["ctx"])
+    prompt = [int(t) for t in g["prompt"]]
+    steps = 24
+    with runtime.CudaModel(path, ctx, flags=runtime.FLAG_MULTI_KERNEL | flags) as a:
+        ids_a, lg_a = _decode(a, prompt, steps)
+        layer = a.stats()["layer_bytes"]
+    # 7 layers of budget: 4 resident, two slots, the staging of one layer
+    with runtime.CudaModel(path, ctx, flags=flags, hbm_budget_bytes=7 * layer) as b:
+        st = b.stats()
+        assert st["persistent"] == 0
+        assert st["resident_layers"] == 4
+        assert st["streamed_bytes"] > 0
+        ids_b, lg_b = _decode(b, prompt, steps)
+        assert ids_b == ids_a
+        for x, y in zip(lg_a, lg_b):
+            np.testing.assert_array_equal(x, y)
+        # the device-resident loop streams the same way
+        b.reset()
+        first = b.prefill(prompt, 0)
+        assert [first] + b.decode_greedy(first, len(prompt), steps - 1) == ids_a
+
+
+def test_streaming_golden_parity():
+    """Streamed decode against the reference's fixtures, as the resident paths."""
+    name = "tinyllama"
+    g = load_golden(name)
+    cfg = configs.get(name)
+    path = synth.ensure_gguf(cfg)
+    ctx = int(g["ctx"])
+    tol = logit_tol(name)
+    layer = _layer_bytes(path, ctx)
+    ref = [int(t) for t in g["ids"]]
+    with runtime.CudaModel(path, ctx, hbm_budget_bytes=5 * layer) as m:
+        assert m.stats()["resident_layers"] == 2
+        ids, logits = _decode(m, [int(t) for t in g["prompt"]], len(ref))
+        k, v, _, _ = m.kv_row(int(g["kv_layer"]), int(g["kv_pos"]))
+    first = next((i for i, (a, b) in enumerate(zip(ids, ref)) if a != b), len(ref))
+    for i, s in enumerate(g["logit_steps"]):
+        if int(s) <= first:
+            assert rel_err(logits[int(s)], g["logits"][i]) < tol, f"step {s}"
+    if first < len(ref):
+        assert _acceptable_choice(g, first, ids[first], tol), f"diverged at step {first}"
+    assert np.abs(k.astype(int) - g["k_row"]).max() <= 1
+    assert np.abs(v.astype(int) - g["v_row"]).max() <= 1
+
+
+def _truth(path, tname):
+    """The reference's dequantisation of a GGUF tensor (oracle, the same C
+    restatement the resident upload tests use)."""
+    import ctypes
+
+    import oracle
+    from tests.test_gpu_kernels import _tensor_table
+    off, rows, cols, typ = _tensor_table(path)[tname]
+    raw = np.fromfile(path, np.uint8, count=rows * cols // 32 * (18 if typ == 2 else 34), offset=off)
+    want = np.empty(rows * cols, np.float32)
+    oracle.oracle_ops().sso_dequantize(raw.ctypes.data, want.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+                                       rows * cols, typ)
+    return want.reshape(rows, cols)
+
+
+@pytest.mark.parametrize("source", ["default", "pageable"])
+def test_streaming_dequantize_streamed_layer(source, monkeypatch):
+    """Weights of resident and streamed layers read back through
+    ss_cuda_dequantize_tensor (the call brings a streamed layer into its slot
+    first) are the reference's dequantisation of the GGUF bytes, before and
+    after decode steps have cycled the slots -- with the copies from the best
+    source the platform offers and from pageable memory (the last fallback)."""
+    if source != "default":
+        monkeypatch.setenv("SS_STREAM_SOURCE", source)
+    cfg = configs.get("tinyllama")
+    path = synth.ensure_gguf(cfg)
+    d, ff, qd, kvd = cfg.d_model, cfg.ffn, cfg.n_heads * cfg.head_dim, cfg.kv_dim
+    shapes = {"attn_q": (qd, d), "attn_k": (kvd, d), "attn_v": (kvd, d), "attn_output": (d, qd),
+              "ffn_gate": (ff, d), "ffn_up": (ff, d), "ffn_down": (d, ff)}
+    layer = _layer_bytes(path, 64)
+    report = []
+    with runtime.CudaModel(path, 64, hbm_budget_bytes=4 * layer) as b:
+        assert b.stats()["resident_layers"] == 1
+        if source == "pageable":
+            assert b.stats()["stream_source"] == 3
+        for when in ("before", "after"):
+            if when == "after":
+                b.prefill(synth.prompt_tokens(cfg)[:4], 0)
+            for l in (0, 1, 20):
+                for t, (r, c) in shapes.items():
+                    tname = f"blk.{l}.{t}.weight"
+                    got = b.dequantize_tensor(tname, r, c)
+                    ok = bool(np.array_equal(got, _truth(path, tname)))
+                    report.append((when, tname, ok))
+    bad = [x for x in report if not x[2]]
+    print("mismatched:", bad)
+    assert not bad
+
+
+def test_resident_deep_layer_dequantize():
+    """The resident multi-kernel upload of a deep layer reads back as the
+    reference's dequantisation (the streamed tests' counterpart)."""
+    cfg = configs.get("tinyllama")
+    path = synth.ensure_gguf(cfg)
+    with runtime.CudaModel(path, 64, flags=runtime.FLAG_MULTI_KERNEL) as a:
+        for t, (r, c) in {"ffn_down": (cfg.d_model, cfg.ffn), "attn_v": (cfg.kv_dim, cfg.d_model)}.items():
+            tname = f"blk.20.{t}.weight"
+            np.testing.assert_array_equal(a.dequantize_tensor(tname, r, c), _truth(path, tname))
+
+
+def test_streaming_budget_too_small():
+    cfg = configs.get("tinyllama")
+    path = synth.ensure_gguf(cfg)
+    layer = _layer_bytes(path, 64)
+    with pytest.raises(runtime.SSCudaError) as e:
+        runtime.CudaModel(path, 64, hbm_budget_bytes=2 * layer)
+    assert "streaming needs 3" in str(e.value)
