@@ -281,8 +281,13 @@ SS_DEVINL int unpack_argmax_index(unsigned long long p) {
 // programmatic-dependent-launch wait: weights never depend on the previous
 // kernel.  Every mbarrier wait is bounded; on expiry the kernel records an
 // error bit, drains its copies and returns without writing outputs.
+// Named barrier over `count` threads.  The non-aligned form: it waits for all
+// non-exited threads of each arriving warp itself, so it stays correct when a
+// warp reaches it diverged -- single-thread work (`if (tid == 0) ...`) often
+// directly precedes it, and nothing forces the compiler to reconverge before an
+// opaque asm statement (bar.sync, the aligned form, requires that).
 SS_DEVINL void named_bar_sync(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+  asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 SS_DEVINL void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");

@@ -293,23 +293,29 @@ float* upload_f32(Context* c, const GgufTensor& t, size_t n) {
 
 // ------------------------------------------------------ persistent step plan
 
-using StepFn = void (*)(const StepParams);
+using StepFn = void (*)(const StepParams, const StepTp);
 
-template <int T, int H>
+template <int T, int H, bool TP>
 StepFn step_fn_hd(int hd) {
   switch (hd) {
-    case 32: return &decode_step_kernel<T, H, 32>;
-    case 64: return &decode_step_kernel<T, H, 64>;
-    case 128: return &decode_step_kernel<T, H, 128>;
-    case 256: return &decode_step_kernel<T, H, 256>;
+    case 32: return &decode_step_kernel<T, H, 32, TP>;
+    case 64: return &decode_step_kernel<T, H, 64, TP>;
+    case 128: return &decode_step_kernel<T, H, 128, TP>;
+    case 256: return &decode_step_kernel<T, H, 256, TP>;
     default: return nullptr;
   }
 }
-StepFn step_fn_for(int type, int htype, int hd) {
-  if (type == kQ4_0 && htype == kQ4_0) return step_fn_hd<kQ4_0, kQ4_0>(hd);
-  if (type == kQ4_0 && htype == kQ8_0) return step_fn_hd<kQ4_0, kQ8_0>(hd);
-  if (type == kQ8_0 && htype == kQ8_0) return step_fn_hd<kQ8_0, kQ8_0>(hd);
+template <bool TP>
+StepFn step_fn_tp(int type, int htype, int hd) {
+  if (type == kQ4_0 && htype == kQ4_0) return step_fn_hd<kQ4_0, kQ4_0, TP>(hd);
+  if (type == kQ4_0 && htype == kQ8_0) return step_fn_hd<kQ4_0, kQ8_0, TP>(hd);
+  if (type == kQ8_0 && htype == kQ8_0) return step_fn_hd<kQ8_0, kQ8_0, TP>(hd);
   return nullptr;
+}
+// The single-GPU step, or (tp) the tensor-parallel one with its exchanges
+// inside the kernel.
+StepFn step_fn_for(int type, int htype, int hd, bool tp) {
+  return tp ? step_fn_tp<true>(type, htype, hd) : step_fn_tp<false>(type, htype, hd);
 }
 
 // Decides whether the persistent step kernel can run this model on this GPU
@@ -320,7 +326,7 @@ StepFn step_fn_for(int type, int htype, int hd) {
 bool plan_step(Context* c, int htype) {
   const int qd = c->nh * c->hd, kvd = c->nkv * c->hd;
   const int G = c->nh / c->nkv;
-  StepFn fn = step_fn_for(c->wtype, htype, c->hd);
+  StepFn fn = step_fn_for(c->wtype, htype, c->hd, c->tp_size > 1);
   if (!fn || G > kAttnMaxG) return false;
   const int cols[3] = {c->d, qd, c->ff};
   for (int x : cols)
@@ -452,8 +458,8 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
       c->streaming = true;
     }
   }
-  // tensor parallelism and layer streaming run the multi-kernel step
-  c->mega = c->mega && c->tp_size <= 1 && !c->streaming && plan_step(c, out->type);
+  // layer streaming runs the multi-kernel step
+  c->mega = c->mega && !c->streaming && plan_step(c, out->type);
   auto mat_layout = [&](int rows, int cols, int type) {
     return c->mega ? layout_tiled(rows, cols, type) : layout(rows, cols, type);
   };
@@ -718,7 +724,7 @@ void launch_step(Context* c) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  void* args[1] = {&c->step_params};
+  void* args[2] = {&c->step_params, &c->step_tp};
   CK(cudaLaunchKernelExC(&cfg, c->step_fn, args));
 }
 
@@ -1003,16 +1009,37 @@ void put_tokens(Context* c, const int32_t* toks, int n, int pos) {
   CK(cudaMemcpyAsync(c->seq_tokens + pos, toks, sizeof(int) * n, cudaMemcpyHostToDevice, c->stream));
 }
 
+// Checks builds: the tensor-parallel step's record, to stderr.
+void dump_step_dbg(Context* c) {
+  const unsigned* d = c->dbg_host;
+  if (!d) return;
+  fprintf(stderr, "[step checks rank %d] consumer thread 0 per CTA (16 * (1 + phase) + sub-step, "
+          "0x8...05: in a cross-rank wait):", c->tp_rank);
+  for (int i = 0; i < c->step_grid; i++) fprintf(stderr, "%s%x", i % 16 ? " " : "\n  ", d[StepDbg::kCons + i]);
+  fprintf(stderr, "\n[step checks rank %d] argmax exchange stage %u\n", c->tp_rank, d[StepDbg::kHead]);
+  for (int i = 0; i < c->step_grid; i++) {
+    const unsigned* e = d + StepDbg::kBad + 4 * i;
+    if (e[0]) fprintf(stderr, "[step checks rank %d] cta %d violation %u at %u: rank %u offset %u\n",
+                      c->tp_rank, i, e[0], e[1], e[2], e[3]);
+  }
+}
+
 void check_device_error(Context* c) {
   int err = 0;
   CK(cudaMemcpyAsync(&c->h_small[8], &c->ctrl->err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
-  CK(cudaStreamSynchronize(c->stream));
+  {
+    const cudaError_t e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) {
+      dump_step_dbg(c);
+      fail(SS_CUDA_ERROR_BACKEND, "cudaStreamSynchronize failed: %s", cudaGetErrorString(e));
+    }
+  }
   err = c->h_small[8];
   if (err) {
     CK(cudaMemsetAsync(&c->ctrl->err, 0, sizeof(int), c->stream));
     fail(SS_CUDA_ERROR_BACKEND,
          "device reported error bits 0x%x (1: position, 2: token, 4: ring wait, 8: grid barrier, "
-         "16: shared-memory plan)", err);
+         "16: shared-memory plan, 32: cross-GPU barrier)", err);
   }
 }
 
@@ -1050,7 +1077,44 @@ void tp_setup(Context* c) {
     if (c->h_small[2 * r] != c->h_small[0] || c->h_small[2 * r + 1] != c->h_small[1])
       fail(SS_CUDA_ERROR_BACKEND, "tensor-parallel ranks planned different steps (rank 0: %d/%d, rank %d: %d/%d)",
            c->h_small[0], c->h_small[1], r, c->h_small[2 * r], c->h_small[2 * r + 1]);
-  tp_barrier(c);
+  if (c->mega) {
+    // the persistent step's exchange block, mapped by every peer (CUDA IPC;
+    // the 64-byte handles travel by an NCCL all-gather)
+    if (tp > kStepMaxTp) fail(SS_CUDA_ERROR_INVALID_PARAMS, "tensor parallelism above %d", kStepMaxTp);
+    const size_t xb = StepXchg::bytes(tp, c->step_grid, c->d);
+    c->xchg = dev_alloc<uint8_t>(c, xb);
+    CK(cudaMemsetAsync(c->xchg, 0, xb, c->stream));
+    cudaIpcMemHandle_t mine;
+    CK(cudaIpcGetMemHandle(&mine, c->xchg));
+    uint8_t* dh = dev_alloc<uint8_t>(c, sizeof(mine) * (size_t)tp);
+    std::vector<cudaIpcMemHandle_t> all((size_t)tp);
+    CK(cudaMemcpyAsync(dh + sizeof(mine) * c->tp_rank, &mine, sizeof(mine), cudaMemcpyHostToDevice, c->stream));
+    NK(nccl_api().AllGather(dh + sizeof(mine) * c->tp_rank, dh, sizeof(mine), ncclUint8, c->comm, c->stream));
+    CK(cudaMemcpyAsync(all.data(), dh, sizeof(mine) * tp, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    StepTp& t = c->step_tp;
+    t = StepTp{};
+    t.tp = tp;
+    t.rank = c->tp_rank;
+    t.vocab_off = c->vocab_off;
+#ifdef SS_STEP_CHECKS
+    t.xbytes = (long long)xb;
+    CK(cudaHostAlloc(&c->dbg_host, sizeof(unsigned) * StepDbg::kWords, cudaHostAllocMapped));
+    memset(c->dbg_host, 0, sizeof(unsigned) * StepDbg::kWords);
+    CK(cudaHostGetDevicePointer(&t.dbg, c->dbg_host, 0));
+#endif
+    for (int r = 0; r < tp; r++) {
+      if (r == c->tp_rank) {
+        t.xpeer[r] = c->xchg;
+        continue;
+      }
+      void* ptr = nullptr;
+      CK(cudaIpcOpenMemHandle(&ptr, all[(size_t)r], cudaIpcMemLazyEnablePeerAccess));
+      c->xpeer_open.push_back(ptr);
+      t.xpeer[r] = static_cast<uint8_t*>(ptr);
+    }
+  }
+  tp_barrier(c);  // every block zeroed and mapped before any rank's first step
 }
 
 // Copies n bytes with a few host threads (a one-time copy of the streamed
@@ -1153,9 +1217,9 @@ Context* create(const uint8_t* base, uint64_t size, const ss_cuda_options_t* o) 
       if (c->tp_rank < 0 || c->tp_rank >= c->tp_size)
         fail(SS_CUDA_ERROR_INVALID_PARAMS, "tp_rank %d outside 0..%d", c->tp_rank, c->tp_size - 1);
       if (!nccl_api().ok) fail(SS_CUDA_ERROR_BACKEND, "tensor parallelism needs libnccl.so.2 (not found)");
-      // the collectives sit between kernels of the multi-kernel step; a graph
-      // with NCCL inside is built without programmatic dependent launch
-      c->mega = false;
+      // the multi-kernel step's collectives sit between its kernels; a graph
+      // with NCCL inside is built without programmatic dependent launch.  The
+      // persistent step exchanges inside the kernel (tp_setup).
       c->use_pdl = false;
       ncclUniqueId id;
       static_assert(sizeof(id) == sizeof(opts.tp_nccl_id), "NCCL unique id size");
@@ -1337,7 +1401,13 @@ SS_API void ss_cuda_free(ss_cuda_ctx_t* ctx) {
   cudaSetDevice(c->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
   if (c->step_exec) cudaGraphExecDestroy(c->step_exec);  // before the communicator it uses
-  if (c->comm) nccl_api().CommDestroy(c->comm);
+  if (c->comm) {
+    // no rank unmaps or frees an exchange block while a peer may still use it
+    if (c->has_model && c->xchg) guard([&] { tp_barrier(c); });
+    for (void* ptr : c->xpeer_open) cudaIpcCloseMemHandle(ptr);
+    if (c->has_model && c->xchg) guard([&] { tp_barrier(c); });
+    nccl_api().CommDestroy(c->comm);
+  }
   for (void* p : c->allocations) cudaFree(p);
   for (auto& s : c->op_slots) {
     if (s.d_x) cudaFree(s.d_x);
@@ -1346,6 +1416,7 @@ SS_API void ss_cuda_free(ss_cuda_ctx_t* ctx) {
   if (c->op_stage) cudaFree(c->op_stage);
   if (c->h_logits) cudaFreeHost(c->h_logits);
   if (c->h_small) cudaFreeHost(c->h_small);
+  if (c->dbg_host) cudaFreeHost(c->dbg_host);
   if (c->stream) cudaStreamDestroy(c->stream);
   if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
   for (cudaEvent_t ev : {c->ev_fork, c->ev_ready[0], c->ev_ready[1], c->ev_free[0], c->ev_free[1]})
@@ -1482,7 +1553,10 @@ SS_API void ss_cuda_reset(ss_cuda_ctx_t* ctx) {
     CK(cudaMemsetAsync(c->am_cnt, 0, sizeof(unsigned), c->stream));
     if (c->step_sync)
       CK(cudaMemsetAsync(c->step_sync, 0, sizeof(unsigned) * c->step_sync_words, c->stream));
+    if (c->xchg) CK(cudaMemsetAsync(c->xchg, 0, StepXchg::kCounters, c->stream));
     CK(cudaStreamSynchronize(c->stream));
+    // tensor parallelism: every rank's counters are zero before any rank's next step
+    if (c->xchg) tp_barrier(c);
     c->host_pos = 0;
     c->cancelled.store(false);
   });

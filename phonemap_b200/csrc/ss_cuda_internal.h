@@ -162,6 +162,10 @@ struct Context {
   int step_grid = 0, step_nslots = 0, step_slot_bytes = 0, step_nsplit = 1;
   size_t step_smem = 0;
   StepParams step_params{};
+  StepTp step_tp{};                     // tensor parallelism (TP instantiation of the step)
+  uint8_t* xchg = nullptr;              // its exchange block (StepXchg), mapped by the peers
+  std::vector<void*> xpeer_open;        // the peers' blocks mapped here (CUDA IPC)
+  unsigned* dbg_host = nullptr;         // checks builds: the TP step's record (host-mapped)
   unsigned* step_sync = nullptr;  // counters zeroed by reset (see alloc_step_state)
   long long* step_trace = nullptr;  // per-phase timeline of the last step (SS_CUDA_FLAG_TRACE)
   size_t step_sync_words = 0;

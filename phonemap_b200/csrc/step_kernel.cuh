@@ -37,6 +37,23 @@
 // All waits are bounded (about one second of SM clocks); on expiry a CTA sets
 // an error bit and a global abort flag that every other wait also watches, the
 // producer drains its outstanding copies, and the kernel returns.
+//
+// Tensor parallelism (the TP instantiation; one process per GPU): each rank
+// runs the step on its shard -- its q / kv heads and FFN rows, the matching
+// columns of O and down, its slice of the vocabulary -- and the exchanges run
+// inside the kernel over NVLink, through one exchange block per rank that
+// every peer has mapped (StepXchg):
+//   * QKV: each CTA stores its (max |k|, max |v|) into every rank's block; the
+//     int8 scales use the maximum over all ranks' CTAs (one scale over the
+//     whole kv_dim, layer_scheduler.c:101-111);
+//   * O, DOWN (row-parallel): each CTA stores its rows' partial sums into every
+//     rank's block (rank 0's carries the residual); the next phases read h as
+//     the sum of the tp partials in rank order, so every rank holds the same h;
+//   * HEAD: each rank's best (value, index) goes to every rank; all pick the
+//     same token.
+// The barrier after QKV, O and DOWN counts the arrivals of every rank's CTAs
+// on a monotonic 64-bit counter in each rank's block (system-scope release /
+// acquire); the other barriers stay local.
 #pragma once
 #include "attention.cuh"
 #include "gemv.cuh"
@@ -61,6 +78,48 @@ static_assert(kStepProducerThreads * kStepProducerRegs + kStepConsumers * kStepC
               "register split must equal the launch allocation");
 constexpr int kStepMaxNb = kStepConsumers;               // <= 16384 columns
 constexpr int kStepMaxSplit = 4;                         // attention position splits per kv head
+constexpr int kStepMaxTp = 8;                            // tensor-parallel ranks
+
+// Tensor parallelism: the group and every rank's exchange block.
+struct StepTp {
+  int tp, rank;
+  int vocab_off;                 // global index of this rank's first lm_head row
+  int pad;
+  uint8_t* xpeer[kStepMaxTp];    // [rank] is this rank's own block
+#ifdef SS_STEP_CHECKS
+  long long xbytes;              // bytes of one exchange block
+  unsigned* dbg;                 // host-mapped record (StepDbg)
+#endif
+};
+
+// Checks builds (compiled with -DSS_STEP_CHECKS, never the shipped library):
+// the tensor-parallel step records its progress into host-mapped memory, which
+// the host can read after a fault, and checks every peer store against the
+// exchange block's bounds (skipping and recording a bad one).  Word offsets:
+struct StepDbg {
+  static constexpr int kCons = 0;     // [cta] consumer thread 0: 16 * (1 + phase) + sub-step
+  static constexpr int kProd = 256;   // [cta] producer: 1 + phase being issued
+  static constexpr int kBad = 512;    // [cta][4] last violation: code, where, rank, offset
+  static constexpr int kHead = 1536;  // argmax exchange stage of the last CTA
+  static constexpr int kWords = 2048;
+};
+
+// Exchange block of one rank, same layout on every rank (byte offsets).
+struct StepXchg {
+  static constexpr int kBar = 0;     // u64: arrivals of all ranks' CTAs at cross-rank barriers
+  static constexpr int kHead = 64;   // u64: arrivals of all ranks' argmax
+  static constexpr int kStep = 128;  // u64: steps this rank has run (read only by it)
+  static constexpr int kBest = 256;  // u64 [tp]: each rank's best (value, index) of this step
+  static constexpr int kAm = 512;    // float2 [tp][grid]: each rank's CTAs' (max |k|, max |v|)
+  static constexpr int kCounters = 512;  // bytes ss_cuda_reset zeroes
+  // float [2][tp][d]: partial h of the O (slot 0) and DOWN (slot 1) phases
+  __host__ __device__ static size_t h_off(int tp, int grid) {
+    return ((size_t)kAm + (size_t)tp * grid * 8 + 255) / 256 * 256;
+  }
+  __host__ __device__ static size_t bytes(int tp, int grid, int d) {
+    return h_off(tp, grid) + 2 * (size_t)tp * d * sizeof(float);
+  }
+};
 
 // One activation block in block fixed point in shared memory: 112 bytes (7 x
 // 16), no padding -- consumer lane j reads block j with 16-byte loads, and the
@@ -470,6 +529,115 @@ SS_DEVINL void step_grid_arrive(const StepParams& p, ConsumerCtx& cc) {
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.grid_bar) : "memory");
 }
 
+// ---- cross-rank barrier and exchange blocks (tensor parallelism)
+SS_DEVINL unsigned long long ld_acquire_sys_u64(const unsigned long long* a) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+  return v;
+}
+SS_DEVINL void red_release_sys_add_u64(unsigned long long* a, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
+}
+SS_DEVINL unsigned long long* xchg_u64(const StepTp& t, int rank, int off) {
+  return reinterpret_cast<unsigned long long*>(t.xpeer[rank] + off);
+}
+SS_DEVINL float2* xchg_am(const StepTp& t, int rank) {
+  return reinterpret_cast<float2*>(t.xpeer[rank] + StepXchg::kAm);
+}
+#ifdef SS_STEP_CHECKS
+SS_DEVINL void dbg_mark(const StepTp& t, int word, unsigned v) {
+  if (!t.dbg) return;
+  *reinterpret_cast<volatile unsigned*>(t.dbg + word) = v;
+  __threadfence_system();
+}
+// A store of `bytes` at `ptr` into rank `rank`'s block must land inside it.
+SS_DEVINL bool xchg_ok(const StepTp& t, int rank, const void* ptr, int bytes, unsigned where) {
+  const long long off = reinterpret_cast<const uint8_t*>(ptr) - t.xpeer[rank];
+  if (rank >= 0 && rank < t.tp && t.xpeer[rank] != nullptr && off >= 0 && off + bytes <= t.xbytes &&
+      (off % bytes) == 0)
+    return true;
+  if (t.dbg) {
+    volatile unsigned* e = t.dbg + StepDbg::kBad + 4 * blockIdx.x;
+    e[1] = where;
+    e[2] = (unsigned)rank;
+    e[3] = (unsigned)off;
+    e[0] = 2u;
+    __threadfence_system();
+  }
+  return false;
+}
+#define SS_TP_MARK(t, word, v) dbg_mark((t), (word), (v))
+#define SS_TP_OK(t, rank, ptr, bytes, where) xchg_ok((t), (rank), (ptr), (bytes), (where))
+#else
+#define SS_TP_MARK(t, word, v) ((void)0)
+#define SS_TP_OK(t, rank, ptr, bytes, where) true
+#endif
+// Partial-h slot `s` (0: O, 1: DOWN) of rank `rank`'s block: [tp][d].
+SS_DEVINL float* xchg_h(const StepTp& t, int rank, int s, int d) {
+  return reinterpret_cast<float*>(t.xpeer[rank] + StepXchg::h_off(t.tp, gridDim.x)) + (size_t)s * t.tp * d;
+}
+// Peers may still be launching their step: the cross-rank waits get a longer
+// budget than the local ones.
+constexpr long long kXWaitBudget = 4 * kWaitBudget;
+
+// Waits until this rank's counter holds the arrivals of the `ncross` cross
+// phases of this step after the `epoch` earlier steps (3 per layer each), every
+// CTA of every rank arriving once per phase.
+SS_DEVINL bool step_xwait(const StepParams& p, const StepTp& t, ConsumerCtx& cc, unsigned long long epoch,
+                          unsigned ncross) {
+  bool bad = false;
+  if (cc.ctid == 0) {
+    const unsigned long long per = (unsigned long long)gridDim.x * (unsigned long long)t.tp;
+    const unsigned long long target = (epoch * 3ull * (unsigned long long)p.L + ncross) * per;
+    const unsigned long long* ctr = xchg_u64(t, t.rank, StepXchg::kBar);
+    SS_TP_MARK(t, StepDbg::kCons + blockIdx.x, 0x80000000u | (ncross << 8) | 5u);
+    const long long c0 = clock64();
+    while (true) {
+      if ((long long)(ld_acquire_sys_u64(ctr) - target) >= 0) break;
+      if (ld_volatile_u32(p.abort_flag)) { bad = true; break; }
+      if (clock64() - c0 > kXWaitBudget) {
+        atomicOr(p.err, 32);
+        atomicExch(p.abort_flag, 1u);
+        bad = true;
+        break;
+      }
+    }
+  }
+  bad = cbar_any(bad);
+  if (bad && cc.ctid == 0) *cc.s_abort = 1;
+  return !bad;
+}
+// Arrival at a cross-rank barrier: after the consumer barrier, thread 0's
+// system-scope release-adds (one per rank) publish every consumer's stores of
+// the phase -- the peer stores included -- to all ranks.
+SS_DEVINL void step_xarrive(const StepTp& t, ConsumerCtx& cc) {
+  cbar();
+  if (cc.ctid == 0)
+    for (int r = 0; r < t.tp; r++)
+      if (SS_TP_OK(t, r, xchg_u64(t, r, StepXchg::kBar), 8, 50u))
+        red_release_sys_add_u64(xchg_u64(t, r, StepXchg::kBar), 1ull);
+}
+// Phases whose outputs other ranks read.
+SS_DEVINL bool step_cross(int kind) { return kind == kPhQKV || kind == kPhO || kind == kPhDown; }
+// Barrier arrivals before phase k: local ones (EMBED, ATT, GU of each layer)
+// and cross-rank ones (QKV, O, DOWN of each layer).
+SS_DEVINL void step_bar_counts(int k, unsigned& nloc, unsigned& ncross) {
+  const unsigned f = (unsigned)(k - 1) / 5, rr = (unsigned)(k - 1) % 5;
+  ncross = 3 * f + (rr + 1) / 2;
+  nloc = 1 + 2 * f + rr / 2;
+}
+// Where h lives for phase (kind, layer) under tensor parallelism: p.h (the
+// embedding, before layer 0's O), else the tp partials of the last O (slot 0)
+// or DOWN (slot 1) exchange -- the h that QKV / GU / lm_head normalise and that
+// the O / DOWN epilogues add to.
+SS_DEVINL const float* step_hsrc(const StepParams& p, const StepTp& t, int kind, int layer, int& n) {
+  n = t.tp;
+  if (kind == kPhGU || kind == kPhDown) return xchg_h(t, t.rank, 0, p.d);
+  if (kind == kPhHead || layer > 0) return xchg_h(t, t.rank, 1, p.d);
+  n = 1;
+  return p.h;
+}
+
 // Bounded wait on an mbarrier phase by a whole warp: every lane waits (each
 // needs the barrier's acquire); giving up is a warp vote, so the warp never
 // splits.  Returns false on timeout or when another CTA aborted.
@@ -503,11 +671,12 @@ SS_DEVINL bool warp_wait_phase(const StepParams& p, uint32_t bar, uint32_t par) 
 //
 // With `att` (the O phase), the input is the attention output, merged here
 // from the position splits' partials (m, l, o): M = max m_s, f_s = e^(m_s-M),
-// out = sum_s f_s o_s / sum_s f_s l_s.
-template <int R>
-SS_DEVINL void build_block_planes_r(const float* src, const float* norm_w, const float* att,
-                                    int nsplit, int hd, int nb, float eps, PlaneBlock* dst,
-                                    ConsumerCtx& cc) {
+// out = sum_s f_s o_s / sum_s f_s l_s.  MULTI (tensor parallelism): the input
+// is the sum of nsrc vectors sstride apart, added in order.
+template <int R, bool MULTI>
+SS_DEVINL void build_block_planes_r(const float* src, int nsrc, int sstride, const float* norm_w,
+                                    const float* att, int nsplit, int hd, int nb, float eps,
+                                    PlaneBlock* dst, ConsumerCtx& cc) {
   constexpr int EPT = 8;
   const int q = cc.ctid & 3;
   float xv[R][EPT];
@@ -559,6 +728,18 @@ SS_DEVINL void build_block_planes_r(const float* src, const float* norm_w, const
       for (int i = 0; i < EPT; i += 4) {
         const float4 v = __ldcg(reinterpret_cast<const float4*>(src + base + i));
         xv[r][i] = v.x; xv[r][i + 1] = v.y; xv[r][i + 2] = v.z; xv[r][i + 3] = v.w;
+      }
+      if constexpr (MULTI) {
+        for (int s2 = 1; s2 < nsrc; s2++) {
+#pragma unroll
+          for (int i = 0; i < EPT; i += 4) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(src + (size_t)s2 * sstride + base + i));
+            xv[r][i] = __fadd_rn(xv[r][i], v.x);
+            xv[r][i + 1] = __fadd_rn(xv[r][i + 1], v.y);
+            xv[r][i + 2] = __fadd_rn(xv[r][i + 2], v.z);
+            xv[r][i + 3] = __fadd_rn(xv[r][i + 3], v.w);
+          }
+        }
       }
     }
   }
@@ -636,22 +817,28 @@ SS_DEVINL void build_block_planes_r(const float* src, const float* norm_w, const
   }
   cbar();
 }
-SS_DEVINL void build_block_planes(const float* src, const float* norm_w, const float* att,
-                                  int nsplit, int hd, int nb, float eps, PlaneBlock* dst,
-                                  ConsumerCtx& cc) {
+template <bool MULTI>
+SS_DEVINL void build_block_planes(const float* src, int nsrc, int sstride, const float* norm_w,
+                                  const float* att, int nsplit, int hd, int nb, float eps,
+                                  PlaneBlock* dst, ConsumerCtx& cc) {
   constexpr int per = kStepConsumers / 4;  // blocks per round
-  if (nb <= per) build_block_planes_r<1>(src, norm_w, att, nsplit, hd, nb, eps, dst, cc);
-  else if (nb <= 2 * per) build_block_planes_r<2>(src, norm_w, att, nsplit, hd, nb, eps, dst, cc);
-  else if (nb <= 3 * per) build_block_planes_r<3>(src, norm_w, att, nsplit, hd, nb, eps, dst, cc);
-  else build_block_planes_r<4>(src, norm_w, att, nsplit, hd, nb, eps, dst, cc);
+  if (nb <= per)
+    build_block_planes_r<1, MULTI>(src, nsrc, sstride, norm_w, att, nsplit, hd, nb, eps, dst, cc);
+  else if (nb <= 2 * per)
+    build_block_planes_r<2, MULTI>(src, nsrc, sstride, norm_w, att, nsplit, hd, nb, eps, dst, cc);
+  else if (nb <= 3 * per)
+    build_block_planes_r<3, MULTI>(src, nsrc, sstride, norm_w, att, nsplit, hd, nb, eps, dst, cc);
+  else
+    build_block_planes_r<4, MULTI>(src, nsrc, sstride, norm_w, att, nsplit, hd, nb, eps, dst, cc);
 }
 
 // Consumes this CTA's tiles of `m` from the ring: red[wl * rows_cta + lr] gets
 // the partial sum of local row lr over the 32 blocks of consumer warp wl of a
 // row group.  Returns rows_cta, or -1 on abort.
-template <int TYPE>
+template <int TYPE, bool MULTI>
 SS_DEVINL int step_gemv(const StepParams& p, const StepSmem& sm, ConsumerCtx& cc, const TMat& m,
-                        const float* src, const float* norm_w, float* red, int phase, int pos) {
+                        const float* src, int nsrc, const float* norm_w, float* red, int phase,
+                        int pos) {
   const int ncta = gridDim.x, cta = blockIdx.x;
   constexpr int QB = TYPE == kQ4_0 ? 16 : 32;
   const int nb = m.nb, wpr = step_wpr(nb), RG = kStepConsumerWarps / wpr;
@@ -663,9 +850,8 @@ SS_DEVINL int step_gemv(const StepParams& p, const StepSmem& sm, ConsumerCtx& cc
   const int rows_cta = (t1 - t0) * kStepTileRows;
 
   // this thread's block of the input planes, built in shared memory
-  build_block_planes(src, norm_w, src == nullptr ? p.att_part : nullptr, step_nsplit(p, pos), p.hd,
-                     nb, p.eps,
-                     reinterpret_cast<PlaneBlock*>(red), cc);
+  build_block_planes<MULTI>(src, nsrc, p.d, norm_w, src == nullptr ? p.att_part : nullptr,
+                            step_nsplit(p, pos), p.hd, nb, p.eps, reinterpret_cast<PlaneBlock*>(red), cc);
   int pl[3][8];
   int init[3];
   float c0;
@@ -765,6 +951,29 @@ SS_DEVINL float row_total(const float* red, int wpr, int rows_cta, int lr) {
   return s;
 }
 
+
+// Residual h of row r under tensor parallelism: the sum of nsrc partials
+// (stride d) in rank order.
+SS_DEVINL float h_sum(const float* hs, int nsrc, int d, int r) {
+  float v = __ldcg(hs + r);
+  for (int q = 1; q < nsrc; q++) v = __fadd_rn(v, __ldcg(hs + (size_t)q * d + r));
+  return v;
+}
+// Tensor parallelism: this rank's partial rows of the CTA (rank 0 adds the old
+// h, read from (hs, nsrc); h_pre is its value at the thread's first row) go to
+// slot `xs` of every rank's exchange block.
+SS_DEVINL void epi_residual_tp(const StepParams& p, const StepTp& t, ConsumerCtx& cc, const float* red,
+                               int wpr, int rows_cta, int r0, float h_pre, const float* hs, int nsrc, int xs) {
+  const int r1 = min(r0 + rows_cta, p.d);
+  for (int r = r0 + cc.ctid; r < r1; r += kStepConsumers) {
+    float v = row_total(red, wpr, rows_cta, r - r0);
+    if (t.rank == 0) v = __fadd_rn(v, r == r0 + cc.ctid ? h_pre : h_sum(hs, nsrc, p.d, r));
+    for (int q = 0; q < t.tp; q++) {
+      float* dst = xchg_h(t, q, xs, p.d) + (size_t)t.rank * p.d + r;
+      if (SS_TP_OK(t, q, dst, 4, 20u + xs)) __stcg(dst, v);
+    }
+  }
+}
 
 // h[r] += v[r] for the CTA's rows (layer_scheduler.c:484, :566).
 SS_DEVINL void epi_residual(const StepParams& p, ConsumerCtx& cc, const float* red, int wpr,
@@ -1023,13 +1232,14 @@ SS_DEVINL bool step_attention_task(const StepParams& p, const StepSmem& sm, Cons
 
 // ---------------------------------------------------------------- kernel
 
-template <int TYPE, int HTYPE, int HD>
-__global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const StepParams p) {
+template <int TYPE, int HTYPE, int HD, bool TP>
+__global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const StepParams p, const StepTp t) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ int s_cabort_v;
   __shared__ float s_red[32];
   __shared__ int s_flag[4];
   __shared__ unsigned long long s_best[kStepConsumerWarps];
+  __shared__ unsigned long long s_epoch;  // tensor parallelism: steps this rank ran before
   volatile int* s_cabort = &s_cabort_v;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ncta = gridDim.x, cta = blockIdx.x;
@@ -1085,11 +1295,29 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
   cc.s_flag = s_flag;
   float* red = sm.scratch;
   const int nph = step_phase_count(p.L);
+  if constexpr (TP) {
+    if (cc.ctid == 0)  // read by consumer thread 0 only (its barrier waits, the argmax)
+      s_epoch = *reinterpret_cast<volatile unsigned long long*>(xchg_u64(t, t.rank, StepXchg::kStep));
+  }
 
   for (int k = 0; k < nph; k++) {
     int kind, layer;
     step_phase(k, p.L, kind, layer);
-    if (k > 0 && !step_grid_wait(p, cc, (unsigned)(k * ncta))) return;
+    if constexpr (TP) {
+      if (cc.ctid == 0) SS_TP_MARK(t, StepDbg::kCons + cta, 16u * (unsigned)(k + 1) + 0u);
+      if (k > 0) {
+        int pkind, player;
+        step_phase(k - 1, p.L, pkind, player);
+        unsigned nloc, ncross;
+        step_bar_counts(k, nloc, ncross);
+        if (!(step_cross(pkind) ? step_xwait(p, t, cc, s_epoch, ncross)
+                                : step_grid_wait(p, cc, nloc * (unsigned)ncta)))
+          return;
+      }
+      if (cc.ctid == 0) SS_TP_MARK(t, StepDbg::kCons + cta, 16u * (unsigned)(k + 1) + 1u);
+    } else {
+      if (k > 0 && !step_grid_wait(p, cc, (unsigned)(k * ncta))) return;
+    }
     if (cc.ctid == 0) trace_mark(p, k, 0);
 
     if (kind == kPhEmbed) {
@@ -1111,9 +1339,16 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
       // this step's q / k / v of the CTA's task, requested before the maxima
       const AttInputs ain = att_load_inputs(p, cc, cta, pos, HD);
       // this position's int8 scales need max |k| / |v| over the whole kv_dim
+      // (tensor parallelism: over every rank's CTAs)
       float mk = 0.0f, mv = 0.0f;
-      for (int i = cc.ctid; i < ncta; i += kStepConsumers) {
-        const float2 a = __ldcg(p.amax_part + i);
+      const float2* amp = p.amax_part;
+      int nam = ncta;
+      if constexpr (TP) {
+        amp = xchg_am(t, t.rank);
+        nam = ncta * t.tp;
+      }
+      for (int i = cc.ctid; i < nam; i += kStepConsumers) {
+        const float2 a = __ldcg(amp + i);
         mk = fmaxf(mk, a.x);
         mv = fmaxf(mv, a.y);
       }
@@ -1148,7 +1383,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     // this phase's input: RMSNorm(h) for QKV / GU / lm_head, else the
     // attention output (O: merged from the split partials, src == nullptr) or
     // the SwiGLU activations (down)
-    const float* src = kind == kPhO ? nullptr : kind == kPhDown ? p.act : p.h;
+    const float* hin = p.h;
+    int nsrc = 1;
+    if constexpr (TP) hin = step_hsrc(p, t, kind, layer, nsrc);
+    const float* src = kind == kPhO ? nullptr : kind == kPhDown ? p.act : hin;
+    if (kind == kPhO || kind == kPhDown) nsrc = 1;
     const float* nw = kind == kPhQKV  ? p.attn_norm + (size_t)layer * p.d
                       : kind == kPhGU ? p.ffn_norm + (size_t)layer * p.d
                       : kind == kPhHead ? p.out_norm : nullptr;
@@ -1167,13 +1406,24 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         if (2 * cc.ctid < rows && r < p.qd + p.kvd && i < p.rope_dim)
           cs_pre = __ldg(p.rope_tab + (size_t)pos * (p.rope_dim >> 1) + (i >> 1));
       } else if (kind == kPhO || kind == kPhDown) {
-        if (cc.ctid < rows && r0 + cc.ctid < p.d) h_pre = __ldcg(p.h + r0 + cc.ctid);
+        if constexpr (TP) {
+          if (t.rank == 0 && cc.ctid < rows && r0 + cc.ctid < p.d) {
+            int nres;
+            const float* hres = step_hsrc(p, t, kind, layer, nres);
+            h_pre = h_sum(hres, nres, p.d, r0 + cc.ctid);
+          }
+        } else {
+          if (cc.ctid < rows && r0 + cc.ctid < p.d) h_pre = __ldcg(p.h + r0 + cc.ctid);
+        }
       }
     }
     int rows_cta;
-    if (kind == kPhHead) rows_cta = step_gemv<HTYPE>(p, sm, cc, m, src, nw, red, k, pos);
-    else rows_cta = step_gemv<TYPE>(p, sm, cc, m, src, nw, red, k, pos);
+    if (kind == kPhHead) rows_cta = step_gemv<HTYPE, TP>(p, sm, cc, m, src, nsrc, nw, red, k, pos);
+    else rows_cta = step_gemv<TYPE, TP>(p, sm, cc, m, src, nsrc, nw, red, k, pos);
     if (rows_cta < 0) return;
+    if constexpr (TP) {
+      if (cc.ctid == 0) SS_TP_MARK(t, StepDbg::kCons + cta, 16u * (unsigned)(k + 1) + 2u);
+    }
     if (cc.ctid == 0) trace_mark(p, k, 1);
     const int wpr = step_wpr(m.nb);
 
@@ -1211,10 +1461,23 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
           mk = fmaxf(mk, s_red[w]);
           mv = fmaxf(mv, s_red[16 + w]);
         }
-        __stcg(p.amax_part + cta, make_float2(mk, mv));
+        if constexpr (TP) {
+          for (int q = 0; q < t.tp; q++) {
+            float2* dst = xchg_am(t, q) + t.rank * ncta + cta;
+            if (SS_TP_OK(t, q, dst, 8, 30u)) __stcg(dst, make_float2(mk, mv));
+          }
+        } else {
+          __stcg(p.amax_part + cta, make_float2(mk, mv));
+        }
       }
     } else if (kind == kPhO) {
-      epi_residual(p, cc, red, wpr, rows_cta, r0, h_pre);
+      if constexpr (TP) {
+        int nres;
+        const float* hres = step_hsrc(p, t, kind, layer, nres);
+        epi_residual_tp(p, t, cc, red, wpr, rows_cta, r0, h_pre, hres, nres, 0);
+      } else {
+        epi_residual(p, cc, red, wpr, rows_cta, r0, h_pre);
+      }
     } else if (kind == kPhGU) {
       // act = up * g / (1 + expf(-g)) (layer_scheduler.c:533-549)
       const int a0 = r0 / 2, a1 = min((r0 + rows_cta) / 2, p.ff);
@@ -1225,14 +1488,21 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         __stcg(p.act + j, __fmul_rn(u, __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)))));
       }
     } else if (kind == kPhDown) {
-      epi_residual(p, cc, red, wpr, rows_cta, r0, h_pre);
+      if constexpr (TP) {
+        int nres;
+        const float* hres = step_hsrc(p, t, kind, layer, nres);
+        epi_residual_tp(p, t, cc, red, wpr, rows_cta, r0, h_pre, hres, nres, 1);
+      } else {
+        epi_residual(p, cc, red, wpr, rows_cta, r0, h_pre);
+      }
     } else {  // kPhHead: logits, greedy argmax (tensor.c:318-328), next token
       unsigned long long best = 0;
-      const int r1 = min(r0 + rows_cta, p.vocab);
+      // tensor parallelism: this rank's vocabulary rows, global indices
+      const int r1 = min(r0 + rows_cta, TP ? m.rows : p.vocab);
       for (int r = r0 + cc.ctid; r < r1; r += kStepConsumers) {
         const float v = row_total(red, wpr, rows_cta, r - r0);
         __stcg(p.logits + r, v);
-        const unsigned long long pk = pack_argmax(v, r);
+        const unsigned long long pk = pack_argmax(v, TP ? t.vocab_off + r : r);
         best = pk > best ? pk : best;
       }
 #pragma unroll
@@ -1262,7 +1532,42 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
           const unsigned long long other = __shfl_xor_sync(0xffffffffu, b, o);
           b = other > b ? other : b;
         }
-        if (lane == 0) {
+        bool ok = true;
+        if constexpr (TP) {
+          if (lane == 0) {
+            // every rank's best to every rank, then the best of the tp
+            SS_TP_MARK(t, StepDbg::kHead, 1u);
+            for (int q = 0; q < t.tp; q++) {
+              unsigned long long* dst = xchg_u64(t, q, StepXchg::kBest) + t.rank;
+              if (SS_TP_OK(t, q, dst, 8, 40u)) __stcg(dst, b);
+              if (SS_TP_OK(t, q, xchg_u64(t, q, StepXchg::kHead), 8, 41u))
+                red_release_sys_add_u64(xchg_u64(t, q, StepXchg::kHead), 1ull);
+            }
+            SS_TP_MARK(t, StepDbg::kHead, 2u);
+            const unsigned long long epoch = s_epoch;
+            const unsigned long long target = (epoch + 1ull) * (unsigned long long)t.tp;
+            const unsigned long long* ctr = xchg_u64(t, t.rank, StepXchg::kHead);
+            const long long c0 = clock64();
+            while ((long long)(ld_acquire_sys_u64(ctr) - target) < 0) {
+              if (clock64() - c0 > kXWaitBudget) {
+                atomicOr(p.err, 32);
+                atomicExch(p.abort_flag, 1u);
+                ok = false;
+                break;
+              }
+            }
+            if (ok) {
+              const unsigned long long* bs = xchg_u64(t, t.rank, StepXchg::kBest);
+              for (int q = 0; q < t.tp; q++) {
+                const unsigned long long v = __ldcg(bs + q);
+                b = v > b ? v : b;
+              }
+              *xchg_u64(t, t.rank, StepXchg::kStep) = epoch + 1ull;
+            }
+            SS_TP_MARK(t, StepDbg::kHead, ok ? 3u : 4u);
+          }
+        }
+        if (lane == 0 && ok) {
           const int tok = unpack_argmax_index(b);
           if (pos + 1 < p.ctx && pos + 1 >= *p.fixed_until) p.seq_tokens[pos + 1] = tok;
           p.seq_tokens[p.ctx] = tok;
@@ -1275,7 +1580,14 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
       return;
     }
     if (cc.ctid == 0) trace_mark(p, k, 2);
-    step_grid_arrive(p, cc);
+    if constexpr (TP) {
+      if (cc.ctid == 0) SS_TP_MARK(t, StepDbg::kCons + cta, 16u * (unsigned)(k + 1) + 3u);
+      if (step_cross(kind)) step_xarrive(t, cc);
+      else step_grid_arrive(p, cc);
+      if (cc.ctid == 0) SS_TP_MARK(t, StepDbg::kCons + cta, 16u * (unsigned)(k + 1) + 4u);
+    } else {
+      step_grid_arrive(p, cc);
+    }
   }
 }
 

@@ -4,15 +4,15 @@ identical (a divergence only where the reference's own top-2 lie within the
 logit tolerance), logits within the tolerance, and rank 0's int8 K/V row --
 its kv heads, quantised with the scale of the whole kv_dim after the max
 all-reduce -- within one quantisation step of the reference's.  Sharding
-changes only the fp32 summation order of the O and down projections.  Tensor
-parallelism runs the multi-kernel step (NCCL between its kernels), whatever
-step the flags ask for."""
+changes only the fp32 summation order of the O and down projections.  Both
+step implementations: the persistent kernel (exchanges through peer memory
+inside the kernel) and the multi-kernel graph (NCCL between kernels)."""
 from __future__ import annotations
 
 import numpy as np
 import pytest
 
-from phonemap_b200 import configs, synth, tp
+from phonemap_b200 import configs, runtime, synth, tp
 from tests.conftest import load_golden, rel_err
 from tests.test_gpu_decode import PATHS, _acceptable_choice, logit_tol
 
@@ -33,7 +33,7 @@ CASES = [(2, "tiny"), (2, "tiny-mha"), (2, "tiny-q8"), (2, "tinyllama"), (2, "ll
          (4, "tinyllama"), (4, "llama2-7b"), (8, "llama2-7b")]
 
 
-@pytest.mark.parametrize("path", ["multi-kernel"])
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("n,name", CASES, ids=[f"tp{n}-{m}" for n, m in CASES])
 def test_tp_greedy_parity(n, name, path):
     if _gpus() < n:
@@ -46,7 +46,7 @@ def test_tp_greedy_parity(n, name, path):
     ref = [int(t) for t in g["ids"]]
     r = tp.greedy(synth.ensure_gguf(cfg), int(g["ctx"]), prompt, len(ref), n, flags=PATHS[path],
                   kv_at=(int(g["kv_layer"]), int(g["kv_pos"])))
-    assert r["stats"]["persistent"] == 0
+    assert r["stats"]["persistent"] == (0 if PATHS[path] & runtime.FLAG_MULTI_KERNEL else 1)
     ids, logits = r["ids"], r["logits"]
     first = next((i for i, (a, b) in enumerate(zip(ids, ref)) if a != b), len(ref))
     for i, s in enumerate(g["logit_steps"]):
@@ -63,7 +63,7 @@ def test_tp_greedy_parity(n, name, path):
     np.testing.assert_allclose([ks, vs], g["kv_scales"], rtol=max(1e-3, tol))
 
 
-@pytest.mark.parametrize("path", ["multi-kernel"])
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("name", ["tiny", "tinyllama"])
 def test_tp_teacher_forced(name, path):
     """Every step fed the reference's token: logits at the reference's top-4
