@@ -210,7 +210,7 @@ def dist_setup(args):
     return world, rank, local, pg
 
 
-def workload(cfg, args):
+def workload(cfg, args, persistent=True):
     return {
         "workload": (f"{cfg.name}-shaped llama decoder, {'Q4_0' if cfg.wtype == 2 else 'Q8_0'} "
                      f"weights, greedy decode at batch 1 after a {cfg.prompt}-token prompt"),
@@ -222,7 +222,9 @@ def workload(cfg, args):
         "l2": "inputs larger than L2 (weights streamed per step exceed the 126 MB L2)",
         "parallelism": ("single GPU" if args.gpus <= 1 else
                         f"dp{args.gpus} (independent replicas)" if args.replicas else
-                        f"tp{args.gpus} (tensor parallel over NCCL)"),
+                        f"tp{args.gpus} (tensor parallel; "
+                        + ("exchanges over NVLink peer memory inside the persistent step)" if persistent
+                           else "NCCL all-reduces between the step's kernels)")),
         **({"hbm_budget_layers": budget_layers_of(cfg, args),
             "weights": f"{'Q4_0' if cfg.wtype == 2 else 'Q8_0'}, layers past the resident ones "
                        "copied from the host-mapped model file every step (layer streaming)"}
@@ -381,9 +383,12 @@ def run_ours(args):
                      "source": {1: "registered model mapping", 2: "pinned host copy",
                                 3: "pageable memory"}.get(stats["stream_source"], "?")}
     if stats["persistent"]:
-        kernel_name = "decode_step_kernel (persistent: the whole decode step)"
-        k_bytes, k_ms, achieved = step_bytes, ms_per_step, step_gbs
-        traffic = read_profile_traffic("decode_step", cfg.name)
+        # tensor parallelism: each rank's kernel streams its 1/tp of the bytes
+        kernel_name = "decode_step_kernel (persistent: the whole decode step" + (
+            f", one rank of {tp})" if tp > 1 else ")")
+        k_bytes, k_ms = step_bytes / tp, ms_per_step
+        achieved = k_bytes / (k_ms / 1000.0) / 1e9
+        traffic = read_profile_traffic("decode_step", cfg.name) if tp == 1 else None
     else:
         kernel_name = "gate/up GEMV + RMSNorm + SwiGLU"
         bpw = 18 / 32 if cfg.wtype == 2 else 34 / 32
@@ -402,7 +407,7 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "strong" if tp > 1 else "weak",
             "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init GGUF, N(0,0.02) quantized)",
-            "config": workload(cfg, args),
+            "config": workload(cfg, args, bool(stats["persistent"])),
             "roofline": {"bound": "hbm", "kernel": kernel_name,
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
@@ -416,7 +421,9 @@ def run_ours(args):
             "gpu_launches": int(stats["kernels_per_step"] * K),
             **({"host_link": host_link} if host_link else {}),
             "clocks": sampler.summary(),
-            "step_impl": ("persistent single kernel" if stats["persistent"] else
+            "step_impl": ("persistent single kernel" + (" (tensor-parallel: in-kernel peer-memory exchanges)"
+                                                        if tp > 1 else "")
+                          if stats["persistent"] else
                           "multi-kernel CUDA graph" + (" with NCCL all-reduces" if tp > 1 else "")),
             "pdl": bool(stats["pdl"]),
             "first_ids": ids[:8],
