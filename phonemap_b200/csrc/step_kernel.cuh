@@ -530,14 +530,15 @@ SS_DEVINL void step_grid_arrive(const StepParams& p, ConsumerCtx& cc) {
 }
 
 // ---- cross-rank barrier and exchange blocks (tensor parallelism)
-SS_DEVINL unsigned long long ld_acquire_sys_u64(const unsigned long long* a) {
+SS_DEVINL unsigned long long ld_relaxed_sys_u64(const unsigned long long* a) {
   unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
   return v;
 }
-SS_DEVINL void red_release_sys_add_u64(unsigned long long* a, unsigned long long v) {
-  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
+SS_DEVINL void red_relaxed_sys_add_u64(unsigned long long* a, unsigned long long v) {
+  asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
 }
+SS_DEVINL void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 SS_DEVINL unsigned long long* xchg_u64(const StepTp& t, int rank, int off) {
   return reinterpret_cast<unsigned long long*>(t.xpeer[rank] + off);
 }
@@ -593,7 +594,8 @@ SS_DEVINL bool step_xwait(const StepParams& p, const StepTp& t, ConsumerCtx& cc,
     SS_TP_MARK(t, StepDbg::kCons + blockIdx.x, 0x80000000u | (ncross << 8) | 5u);
     const long long c0 = clock64();
     while (true) {
-      if ((long long)(ld_acquire_sys_u64(ctr) - target) >= 0) break;
+      // relaxed polling; one acquire fence once the count is there
+      if ((long long)(ld_relaxed_sys_u64(ctr) - target) >= 0) break;
       if (ld_volatile_u32(p.abort_flag)) { bad = true; break; }
       if (clock64() - c0 > kXWaitBudget) {
         atomicOr(p.err, 32);
@@ -602,20 +604,24 @@ SS_DEVINL bool step_xwait(const StepParams& p, const StepTp& t, ConsumerCtx& cc,
         break;
       }
     }
+    fence_acq_rel_sys();
   }
   bad = cbar_any(bad);
   if (bad && cc.ctid == 0) *cc.s_abort = 1;
   return !bad;
 }
 // Arrival at a cross-rank barrier: after the consumer barrier, thread 0's
-// system-scope release-adds (one per rank) publish every consumer's stores of
-// the phase -- the peer stores included -- to all ranks.
+// system-scope fence and then its adds (one per rank) publish every consumer's
+// stores of the phase -- the peer stores included -- to all ranks (a release
+// made of one fence and relaxed adds).
 SS_DEVINL void step_xarrive(const StepTp& t, ConsumerCtx& cc) {
   cbar();
-  if (cc.ctid == 0)
+  if (cc.ctid == 0) {
+    fence_acq_rel_sys();
     for (int r = 0; r < t.tp; r++)
       if (SS_TP_OK(t, r, xchg_u64(t, r, StepXchg::kBar), 8, 50u))
-        red_release_sys_add_u64(xchg_u64(t, r, StepXchg::kBar), 1ull);
+        red_relaxed_sys_add_u64(xchg_u64(t, r, StepXchg::kBar), 1ull);
+  }
 }
 // Phases whose outputs other ranks read.
 SS_DEVINL bool step_cross(int kind) { return kind == kPhQKV || kind == kPhO || kind == kPhDown; }
@@ -1540,15 +1546,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
             for (int q = 0; q < t.tp; q++) {
               unsigned long long* dst = xchg_u64(t, q, StepXchg::kBest) + t.rank;
               if (SS_TP_OK(t, q, dst, 8, 40u)) __stcg(dst, b);
-              if (SS_TP_OK(t, q, xchg_u64(t, q, StepXchg::kHead), 8, 41u))
-                red_release_sys_add_u64(xchg_u64(t, q, StepXchg::kHead), 1ull);
             }
+            fence_acq_rel_sys();
+            for (int q = 0; q < t.tp; q++)
+              if (SS_TP_OK(t, q, xchg_u64(t, q, StepXchg::kHead), 8, 41u))
+                red_relaxed_sys_add_u64(xchg_u64(t, q, StepXchg::kHead), 1ull);
             SS_TP_MARK(t, StepDbg::kHead, 2u);
             const unsigned long long epoch = s_epoch;
             const unsigned long long target = (epoch + 1ull) * (unsigned long long)t.tp;
             const unsigned long long* ctr = xchg_u64(t, t.rank, StepXchg::kHead);
             const long long c0 = clock64();
-            while ((long long)(ld_acquire_sys_u64(ctr) - target) < 0) {
+            while ((long long)(ld_relaxed_sys_u64(ctr) - target) < 0) {
               if (clock64() - c0 > kXWaitBudget) {
                 atomicOr(p.err, 32);
                 atomicExch(p.abort_flag, 1u);
@@ -1556,6 +1564,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                 break;
               }
             }
+            fence_acq_rel_sys();
             if (ok) {
               const unsigned long long* bs = xchg_u64(t, t.rank, StepXchg::kBest);
               for (int q = 0; q < t.tp; q++) {
