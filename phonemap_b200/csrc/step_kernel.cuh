@@ -623,14 +623,18 @@ SS_DEVINL void step_xarrive(const StepTp& t, ConsumerCtx& cc) {
         red_relaxed_sys_add_u64(xchg_u64(t, r, StepXchg::kBar), 1ull);
   }
 }
-// Phases whose outputs other ranks read.
+// Phases whose outputs other ranks read: their CTAs arrive at the cross-rank
+// counter (QKV: its K/V maxima, and also at the local barrier, since the
+// attention phase needs only this rank's q / k / v).  The phases after O and
+// DOWN wait at the cross-rank counter; every other phase at the local barrier.
 SS_DEVINL bool step_cross(int kind) { return kind == kPhQKV || kind == kPhO || kind == kPhDown; }
-// Barrier arrivals before phase k: local ones (EMBED, ATT, GU of each layer)
-// and cross-rank ones (QKV, O, DOWN of each layer).
+SS_DEVINL bool step_cross_wait(int prev_kind) { return prev_kind == kPhO || prev_kind == kPhDown; }
+// Arrivals before phase k: local (EMBED, then QKV, ATT, GU of each layer) and
+// cross-rank (QKV, O, DOWN of each layer).
 SS_DEVINL void step_bar_counts(int k, unsigned& nloc, unsigned& ncross) {
   const unsigned f = (unsigned)(k - 1) / 5, rr = (unsigned)(k - 1) % 5;
-  ncross = 3 * f + (rr + 1) / 2;
-  nloc = 1 + 2 * f + rr / 2;
+  nloc = 1 + 3 * f + (rr > 0) + (rr > 1) + (rr > 3);
+  ncross = 3 * f + (rr > 0) + (rr > 2);
 }
 // Where h lives for phase (kind, layer) under tensor parallelism: p.h (the
 // embedding, before layer 0's O), else the tp partials of the last O (slot 0)
@@ -1316,8 +1320,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         step_phase(k - 1, p.L, pkind, player);
         unsigned nloc, ncross;
         step_bar_counts(k, nloc, ncross);
-        if (!(step_cross(pkind) ? step_xwait(p, t, cc, s_epoch, ncross)
-                                : step_grid_wait(p, cc, nloc * (unsigned)ncta)))
+        if (!(step_cross_wait(pkind) ? step_xwait(p, t, cc, s_epoch, ncross)
+                                     : step_grid_wait(p, cc, nloc * (unsigned)ncta)))
           return;
       }
       if (cc.ctid == 0) SS_TP_MARK(t, StepDbg::kCons + cta, 16u * (unsigned)(k + 1) + 1u);
@@ -1345,28 +1349,44 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
       // this step's q / k / v of the CTA's task, requested before the maxima
       const AttInputs ain = att_load_inputs(p, cc, cta, pos, HD);
       // this position's int8 scales need max |k| / |v| over the whole kv_dim
-      // (tensor parallelism: over every rank's CTAs)
+      // (tensor parallelism: over every rank's CTAs; only a CTA whose task
+      // holds this position encodes a K/V row, so only such a CTA waits for
+      // the other ranks' QKV phase -- the phase started at a local barrier)
       float mk = 0.0f, mv = 0.0f;
       const float2* amp = p.amax_part;
       int nam = ncta;
+      bool need_scale = true;
       if constexpr (TP) {
         amp = xchg_am(t, t.rank);
         nam = ncta * t.tp;
+        need_scale = false;
+        for (int task = cta; task < p.nkv * step_nsplit(p, pos); task += ncta) {
+          int kvh, split, a0, a1;
+          step_att_task(p, task, pos, kvh, split, a0, a1);
+          need_scale = need_scale || (pos >= a0 && pos < a1);
+        }
+        if (need_scale) {  // uniform across the CTA
+          unsigned nloc, ncross;
+          step_bar_counts(k, nloc, ncross);  // ncross counts this layer's QKV
+          if (!step_xwait(p, t, cc, s_epoch, ncross)) return;
+        }
       }
-      for (int i = cc.ctid; i < nam; i += kStepConsumers) {
-        const float2 a = __ldcg(amp + i);
-        mk = fmaxf(mk, a.x);
-        mv = fmaxf(mv, a.y);
-      }
-      mk = warp_max(mk);
-      mv = warp_max(mv);
-      if (cc.lane == 0) { s_red[cc.cw] = mk; s_red[16 + cc.cw] = mv; }
-      cbar();
-      mk = 0.0f;
-      mv = 0.0f;
-      for (int w = 0; w < kStepConsumerWarps; w++) {
-        mk = fmaxf(mk, s_red[w]);
-        mv = fmaxf(mv, s_red[16 + w]);
+      if (need_scale) {
+        for (int i = cc.ctid; i < nam; i += kStepConsumers) {
+          const float2 a = __ldcg(amp + i);
+          mk = fmaxf(mk, a.x);
+          mv = fmaxf(mv, a.y);
+        }
+        mk = warp_max(mk);
+        mv = warp_max(mv);
+        if (cc.lane == 0) { s_red[cc.cw] = mk; s_red[16 + cc.cw] = mv; }
+        cbar();
+        mk = 0.0f;
+        mv = 0.0f;
+        for (int w = 0; w < kStepConsumerWarps; w++) {
+          mk = fmaxf(mk, s_red[w]);
+          mv = fmaxf(mv, s_red[16 + w]);
+        }
       }
       const float k_scale = mk / 127.0f, v_scale = mv / 127.0f;  // layer_scheduler.c:109-110
       bool ok = true;
@@ -1591,8 +1611,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     if (cc.ctid == 0) trace_mark(p, k, 2);
     if constexpr (TP) {
       if (cc.ctid == 0) SS_TP_MARK(t, StepDbg::kCons + cta, 16u * (unsigned)(k + 1) + 3u);
+      if (kind != kPhO && kind != kPhDown) step_grid_arrive(p, cc);
       if (step_cross(kind)) step_xarrive(t, cc);
-      else step_grid_arrive(p, cc);
       if (cc.ctid == 0) SS_TP_MARK(t, StepDbg::kCons + cta, 16u * (unsigned)(k + 1) + 4u);
     } else {
       step_grid_arrive(p, cc);
