@@ -193,6 +193,27 @@ def synth_prompt(cfg):
 
 # ---------------------------------------------------------------- main paths
 
+def share_from_rank0(pg, make):
+    """Rank 0's value of make() on every rank (an object broadcast; make is
+    called on rank 0 only) -- how the tensor-parallel group's NCCL id reaches
+    every rank."""
+    box = [make() if pg is None or pg.get_rank() == 0 else None]
+    if pg is not None:
+        pg.broadcast_object_list(box, src=0)
+    return box[0]
+
+
+def max_over_ranks(pg, x: float, device: str = "cuda") -> float:
+    """The largest x over the ranks (every rank gets it): multi-GPU times are
+    the slowest rank's."""
+    if pg is None:
+        return x
+    import torch
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
 def dist_setup(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -285,10 +306,9 @@ def run_ours(args):
     if budget:
         m = runtime.CudaModel(path, cfg.ctx, device=local, flags=flags, hbm_budget_bytes=budget)
     elif tp > 1:
-        nid = [runtime.tp_unique_id() if rank == 0 else None]
-        pg.broadcast_object_list(nid, src=0)
+        nid = share_from_rank0(pg, runtime.tp_unique_id)
         m = runtime.CudaModel(path, cfg.ctx, device=local, flags=flags, tp_rank=rank, tp_size=tp,
-                              tp_nccl_id=nid[0])
+                              tp_nccl_id=nid)
     else:
         m = runtime.CudaModel(path, cfg.ctx, device=local, flags=flags)
     seqs = world // tp  # sequences decoded concurrently by the whole job
@@ -323,9 +343,7 @@ def run_ours(args):
     ms = ev0.elapsed_time(ev1)
     ids = m.decode_read(P + 1, W + K)
     if pg:
-        t = torch.tensor([ms], device="cuda")
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        ms = float(t.item())
+        ms = max_over_ranks(pg, ms)
         pg.barrier()
     ms_per_step = ms / K
     value = seqs * K / (ms / 1000.0)
@@ -350,10 +368,7 @@ def run_ours(args):
             tok = m.forward(tok, pos, logits=logits)
             pos += 1
         dt = time.perf_counter() - t0
-        if pg:
-            t = torch.tensor([dt], device="cuda")
-            pg.all_reduce(t, op=pg.ReduceOp.MAX)
-            dt = float(t.item())
+        dt = max_over_ranks(pg, dt)
         e2e = {"value": round(seqs * K / dt, 2), "unit": "tokens/s",
                "h2d_bytes_per_step": 4 + 8, "d2h_bytes_per_step": 4 * m.vocab + 4 + 4,
                "api": "ss_cuda_forward (host token in, host logits + argmax out, synchronous)"}
