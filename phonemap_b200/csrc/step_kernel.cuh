@@ -480,16 +480,6 @@ SS_DEVINL bool cbar_any(bool pred) {
   return r != 0;
 }
 
-// Consumer-block sum; every consumer thread receives the result.
-SS_DEVINL float cblock_sum(float v, ConsumerCtx& cc) {
-  v = warp_sum(v);
-  if (cc.lane == 0) cc.s_red[cc.cw] = v;
-  cbar();
-  float t = 0.0f;
-  for (int w = 0; w < kStepConsumerWarps; w++) t += cc.s_red[w];
-  cbar();
-  return t;
-}
 SS_DEVINL float cblock_max(float v, ConsumerCtx& cc) {
   v = warp_max(v);
   if (cc.lane == 0) cc.s_red[cc.cw] = v;
@@ -673,18 +663,21 @@ SS_DEVINL bool warp_wait_phase(const StepParams& p, uint32_t bar, uint32_t par) 
 // converting 8 elements (the block maximum and the digit sums are combined
 // over the four with shuffles); with more than 128 blocks the consumers take
 // R rounds of 128 blocks, every load issued before any conversion.  No block
-// is built twice.  With norm_w, RMSNorm first (cpu_neon.c:109-115): ss = sum
-// src^2 (each thread over its elements in order, then a warp tree, then the
-// warps in order -- the same in every CTA, so every CTA derives the same
-// scale), scale = 1 / sqrtf(ss / n + eps), x = (src * scale) * w.  The digits
-// are those of make_planes (gemv.cuh).  Ends with a consumer barrier.
+// is built twice.  With norm_w, RMSNorm (cpu_neon.c:109-115): the planes hold
+// x = src * w, and the returned scale = 1 / sqrtf(ss / n + eps) multiplies each
+// block's unit in the matvec instead (it is uniform over the vector), so the
+// sum of squares ss = sum src^2 (each thread over its elements in order, then a
+// warp tree, then the warps in order -- the same in every CTA) needs no
+// barrier before the conversion: the warps' sums are added after the closing
+// one.  The digits are those of make_planes (gemv.cuh).  Ends with a consumer
+// barrier; returns 1 without norm_w.
 //
 // With `att` (the O phase), the input is the attention output, merged here
 // from the position splits' partials (m, l, o): M = max m_s, f_s = e^(m_s-M),
 // out = sum_s f_s o_s / sum_s f_s l_s.  MULTI (tensor parallelism): the input
 // is the sum of nsrc vectors sstride apart, added in order.
 template <int R, bool MULTI>
-SS_DEVINL void build_block_planes_r(const float* src, int nsrc, int sstride, const float* norm_w,
+SS_DEVINL float build_block_planes_r(const float* src, int nsrc, int sstride, const float* norm_w,
                                     const float* att, int nsplit, int hd, int nb, float eps,
                                     PlaneBlock* dst, ConsumerCtx& cc) {
   constexpr int EPT = 8;
@@ -771,12 +764,12 @@ SS_DEVINL void build_block_planes_r(const float* src, int nsrc, int sstride, con
     for (int r = 0; r < R; r++)
 #pragma unroll
       for (int i = 0; i < EPT; i++) ss = fmaf(xv[r][i], xv[r][i], ss);
-    ss = cblock_sum(ss, cc);
-    const float scale = 1.0f / sqrtf(ss / (float)(nb * 32) + eps);
+    ss = warp_sum(ss);
+    if (cc.lane == 0) cc.s_red[cc.cw] = ss;  // added up after the closing barrier
 #pragma unroll
     for (int r = 0; r < R; r++)
 #pragma unroll
-      for (int i = 0; i < EPT; i++) xv[r][i] = __fmul_rn(__fmul_rn(xv[r][i], scale), wv[r][i]);
+      for (int i = 0; i < EPT; i++) xv[r][i] = __fmul_rn(xv[r][i], wv[r][i]);
   }
 #pragma unroll
   for (int r = 0; r < R; r++) {
@@ -826,20 +819,26 @@ SS_DEVINL void build_block_planes_r(const float* src, int nsrc, int sstride, con
     }
   }
   cbar();
+  if (R <= 2 && norm_w) {
+    float t = 0.0f;
+    for (int w = 0; w < kStepConsumerWarps; w++) t += cc.s_red[w];
+    return 1.0f / sqrtf(t / (float)(nb * 32) + eps);
+  }
+  return 1.0f;
 }
 template <bool MULTI>
-SS_DEVINL void build_block_planes(const float* src, int nsrc, int sstride, const float* norm_w,
-                                  const float* att, int nsplit, int hd, int nb, float eps,
-                                  PlaneBlock* dst, ConsumerCtx& cc) {
+SS_DEVINL float build_block_planes(const float* src, int nsrc, int sstride, const float* norm_w,
+                                   const float* att, int nsplit, int hd, int nb, float eps,
+                                   PlaneBlock* dst, ConsumerCtx& cc) {
   constexpr int per = kStepConsumers / 4;  // blocks per round
   if (nb <= per)
-    build_block_planes_r<1, MULTI>(src, nsrc, sstride, norm_w, att, nsplit, hd, nb, eps, dst, cc);
+    return build_block_planes_r<1, MULTI>(src, nsrc, sstride, norm_w, att, nsplit, hd, nb, eps, dst, cc);
   else if (nb <= 2 * per)
-    build_block_planes_r<2, MULTI>(src, nsrc, sstride, norm_w, att, nsplit, hd, nb, eps, dst, cc);
+    return build_block_planes_r<2, MULTI>(src, nsrc, sstride, norm_w, att, nsplit, hd, nb, eps, dst, cc);
   else if (nb <= 3 * per)
-    build_block_planes_r<3, MULTI>(src, nsrc, sstride, norm_w, att, nsplit, hd, nb, eps, dst, cc);
+    return build_block_planes_r<3, MULTI>(src, nsrc, sstride, norm_w, att, nsplit, hd, nb, eps, dst, cc);
   else
-    build_block_planes_r<4, MULTI>(src, nsrc, sstride, norm_w, att, nsplit, hd, nb, eps, dst, cc);
+    return build_block_planes_r<4, MULTI>(src, nsrc, sstride, norm_w, att, nsplit, hd, nb, eps, dst, cc);
 }
 
 // Consumes this CTA's tiles of `m` from the ring: red[wl * rows_cta + lr] gets
@@ -859,9 +858,11 @@ SS_DEVINL int step_gemv(const StepParams& p, const StepSmem& sm, ConsumerCtx& cc
   part_range(m.ntiles, cta, ncta, t0, t1);
   const int rows_cta = (t1 - t0) * kStepTileRows;
 
-  // this thread's block of the input planes, built in shared memory
-  build_block_planes<MULTI>(src, nsrc, p.d, norm_w, src == nullptr ? p.att_part : nullptr,
-                            step_nsplit(p, pos), p.hd, nb, p.eps, reinterpret_cast<PlaneBlock*>(red), cc);
+  // this thread's block of the input planes, built in shared memory; the
+  // RMSNorm scale (1 without a norm) joins each block's unit
+  const float nscale =
+      build_block_planes<MULTI>(src, nsrc, p.d, norm_w, src == nullptr ? p.att_part : nullptr,
+                                step_nsplit(p, pos), p.hd, nb, p.eps, reinterpret_cast<PlaneBlock*>(red), cc);
   int pl[3][8];
   int init[3];
   float c0;
@@ -881,7 +882,7 @@ SS_DEVINL int step_gemv(const StepParams& p, const StepSmem& sm, ConsumerCtx& cc
     init[0] = zp * v.x;  // stored: -sum_j digit_pj
     init[1] = zp * v.y;
     init[2] = zp * v.z;
-    c0 = __int_as_float(v.w);
+    c0 = __int_as_float(v.w) * nscale;
   }
   cbar();  // every consumer has its planes before the scratch turns into partial sums
   bool bad = false;
