@@ -116,7 +116,9 @@ int ss_cuda_model_dims(const ss_cuda_ctx_t *ctx, int32_t *dims);
  * unless streaming), [11] bytes copied from host memory per step (layer
  * streaming), [12] device bytes of one layer's four matrices, [13] where
  * streamed layers are copied from: 1 the registered model mapping, 2 a pinned
- * host copy, 3 pageable memory (0: not streaming). */
+ * host copy, 3 pageable memory (0: not streaming), [14] the binary version the
+ * loaded kernels were compiled for (cudaFuncAttributes::binaryVersion; 100 =
+ * sm_100a). */
 int ss_cuda_stats(const ss_cuda_ctx_t *ctx, int64_t *out, int32_t n);
 
 /* Measurement aid, no reference counterpart: times `iters` back-to-back
@@ -204,15 +206,19 @@ void ss_cuda_cancel(ss_cuda_ctx_t *ctx);
  * token -- e.g. while a stream is being captured into a CUDA graph, where
  * cudaMalloc is not allowed, or inside a host that only hands out buffers from
  * its own pool.  Writes to *d_index (device memory) the index of the first
- * maximum of d_values[0..n) (device memory), with ss_argmax's tie rule
- * (SlipStream/src/core/tensor.c:318-328; NaN never wins).  Enqueued on
- * `stream` (a cudaStream_t, NULL for the legacy default stream) and
- * asynchronous; calls no cudaMalloc/cudaFree.  n must be 1 .. 4,194,304
- * (SS_CUDA_ERROR_INVALID_PARAMS otherwise).  Its scratch is a fixed 8 KiB array
- * in the library's device image, shared by all calls: calls that overlap on
- * the GPU race, calls ordered on one stream do not.  The first call on each
- * device looks the array's address up (cudaGetSymbolAddress) with that device
- * current; make that first call before any stream capture begins. */
+ * maximum of d_values[0..n) (device memory).  The rule: scanning from index 0,
+ * the answer moves only to a strictly greater value, so the first maximum wins
+ * ties, -0.0 and +0.0 tie, a NaN after index 0 never wins, and a NaN at index 0
+ * makes the answer 0.  Enqueued on `stream` (a cudaStream_t, NULL for the
+ * legacy default stream) and asynchronous; calls no cudaMalloc/cudaFree.  n
+ * must be 1 .. 4,194,304 and both pointers non-NULL
+ * (SS_CUDA_ERROR_INVALID_PARAMS otherwise, nothing enqueued).  Its scratch is a
+ * fixed 8 KiB array in the library's device image, shared by all calls: calls
+ * that overlap on the GPU race, calls ordered on one stream do not.  The first
+ * call on each device looks the array's address up (cudaGetSymbolAddress)
+ * with that device current and keeps it for the life of the process; make that
+ * first call before any stream capture begins, and do not reset the device
+ * (cudaDeviceReset) after it -- the kept address would be stale. */
 int ss_cuda_argmax_noalloc(const float *d_values, int32_t n, int32_t *d_index, void *stream);
 
 /* ---- inspection (parity tests) ----

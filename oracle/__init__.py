@@ -85,15 +85,16 @@ class _Model:
             raise RuntimeError("forward failed")
         return out
 
-    def greedy(self, prompt, n_steps: int, keep_logits=()) -> tuple[list[int], dict]:
+    def greedy(self, prompt, n_steps: int, keep_logits=(), start_pos: int = 0) -> tuple[list[int], dict]:
         """Prefill then greedy decode, as engine.c:211-289 with temperature 0.
+        The prompt's first token sits at `start_pos` (0 as in engine.c).
 
         Returns the generated IDs (the first comes from the prefill logits) and
         {step: logits} for the requested steps (step 0 = prefill logits)."""
         kept = {}
-        logits = self.prefill(prompt, 0)
+        logits = self.prefill(prompt, start_pos)
         ids = []
-        pos = len(prompt)
+        pos = start_pos + len(prompt)
         for step in range(n_steps):
             if step in keep_logits:
                 kept[step] = logits.copy()

@@ -36,7 +36,20 @@ import sys
 import tempfile
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-DEFAULT_SRC = "/root/reference/SlipStream"
+
+
+def default_src() -> str:
+    """The reference's SlipStream directory: $SS_REFERENCE_SRC, else
+    ``<reference_path>/SlipStream`` from the repository's BASELINE.json."""
+    env = os.environ.get("SS_REFERENCE_SRC")
+    if env:
+        return env
+    try:
+        import json
+        with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+            return os.path.join(json.load(f)["reference_path"], "SlipStream")
+    except (OSError, KeyError, ValueError):
+        return ""
 
 CORE_SOURCES = [
     "src/core/engine.c",
@@ -190,7 +203,7 @@ def build(src: str, out: str, cc: str = "gcc") -> list[str]:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--src", default=os.environ.get("SS_REFERENCE_SRC", DEFAULT_SRC))
+    ap.add_argument("--src", default=default_src())
     ap.add_argument("--out", default=os.path.join(HERE, "_ref"))
     args = ap.parse_args()
     if not os.path.isdir(os.path.join(args.src, "src", "core")):

@@ -98,6 +98,14 @@ CONFIGS: dict[str, ModelConfig] = {
     # small-case ncu captures of the same kernels
     "llama2-7b-2l": ModelConfig("llama2-7b-2l", 2, 4096, 32, 32, 11008, 32000, 2048,
                                 prompt=128, decode=256),
+    # Llama-2-70B layer shapes (d 8192, GQA 64/8, FFN 28672), 4 layers: every
+    # kernel instantiation of configs[4] in a 3 GB file, for the parity suite
+    "llama2-70b-4l": ModelConfig("llama2-70b-4l", 4, 8192, 64, 8, 28672, 32000, 2048,
+                                 prompt=256, decode=128),
+    # Llama-3-8B layer shapes, 2 layers: the Q8_0 / 128256-vocab kernels in a
+    # small file (profiling and quick checks)
+    "llama3-8b-2l": ModelConfig("llama3-8b-2l", 2, 4096, 32, 8, 14336, 128256, 4096,
+                                wtype=Q8_0, rope_theta=500000.0, prompt=512, decode=256),
     # parity-test shapes (oracle finishes in seconds)
     "tiny": ModelConfig("tiny", 2, 256, 8, 2, 512, 512, 128, norm_jitter=0.1,
                         prompt=8, decode=24, seed=7),

@@ -253,12 +253,24 @@ SS_DEVINL int row_of_lane(int lane) {
   return ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
 }
 
-// Packs (value, index) so that unsigned max picks the larger value and, among
-// equal values, the lower index (ss_argmax, SlipStream/src/core/tensor.c:318-328).
+// Packs (value, index) so that the unsigned maximum over all elements is the
+// index ss_argmax returns (SlipStream/src/core/tensor.c:318-328: start from
+// x[0], move only on a strict `>`):
+//   * a larger value wins; among equal values the lower index (the first);
+//   * -0.0 and +0.0 compare equal there, so both map to the key of +0.0;
+//   * a NaN at index > 0 never compares greater, so it gets the lowest key;
+//   * a NaN at index 0 is never replaced (nothing compares greater than it),
+//     so it gets the highest key and index 0 wins outright.
+// A NaN anywhere else with every other value NaN leaves index 0 (lowest key,
+// lowest index), as the reference does.
 SS_DEVINL unsigned long long pack_argmax(float v, int idx) {
-  unsigned b = __float_as_uint(v);
-  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-  if (v != v) b = 0;  // NaN never wins
+  unsigned b;
+  if (v != v) {
+    b = idx == 0 ? 0xffffffffu : 0u;
+  } else {
+    b = v == 0.0f ? 0u : __float_as_uint(v);  // -0.0 -> +0.0
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  }
   return ((unsigned long long)b << 32) | (unsigned)(0x7fffffff - idx);
 }
 SS_DEVINL int unpack_argmax_index(unsigned long long p) {

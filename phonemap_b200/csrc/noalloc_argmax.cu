@@ -80,7 +80,9 @@ argmax_noalloc_kernel(const float* __restrict__ v, int n, int* __restrict__ out,
   if (tid == 0) {
     unsigned long long bb = 0;
     for (int w = 0; w < kNoAllocThreads / 32; w++) bb = wbest[w] > bb ? wbest[w] : bb;
-    *out = unpack_argmax_index(bb);
+    // every element packs above 0 (index 0 always exists), so bb == 0 cannot
+    // happen for n >= 1; index 0 is the answer of an empty scan all the same
+    *out = bb == 0 ? 0 : unpack_argmax_index(bb);
     scratch->count = 0;
   }
 }

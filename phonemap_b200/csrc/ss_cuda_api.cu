@@ -1452,7 +1452,11 @@ SS_API int ss_cuda_stats(const ss_cuda_ctx_t* ctx, int64_t* out, int32_t n) {
   return guard([&] {
     auto* c = reinterpret_cast<const Context*>(ctx);
     if (!c || !out) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null argument");
-    const int64_t v[14] = {c->has_model ? (c->mega ? 1 : 2 + 5LL * c->L + (c->tp_size > 1) +
+    // architecture the loaded kernels were compiled for (100 = sm_100a)
+    cudaFuncAttributes fa{};
+    const int64_t arch = cudaFuncGetAttributes(&fa, embed_kernel) == cudaSuccess ? fa.binaryVersion : -1;
+    cudaGetLastError();
+    const int64_t v[15] = {c->has_model ? (c->mega ? 1 : 2 + 5LL * c->L + (c->tp_size > 1) +
                                                    (c->streaming ? 7LL * (c->L - c->n_resident) : 0))
                                        : 0,
                            (int64_t)c->weight_bytes,
@@ -1467,8 +1471,9 @@ SS_API int ss_cuda_stats(const ss_cuda_ctx_t* ctx, int64_t* out, int32_t n) {
                            c->n_resident,
                            (int64_t)c->streamed_bytes,
                            (int64_t)c->layer_stride,
-                           !c->streaming ? 0 : c->host_reg ? 1 : c->host_pinned ? 2 : 3};
-    for (int i = 0; i < n && i < 14; i++) out[i] = v[i];
+                           !c->streaming ? 0 : c->host_reg ? 1 : c->host_pinned ? 2 : 3,
+                           arch};
+    for (int i = 0; i < n && i < 15; i++) out[i] = v[i];
   });
 }
 

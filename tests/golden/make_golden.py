@@ -12,9 +12,17 @@ sources by oracle/build_ref.py) on the seeded synthetic GGUF models and records:
   nibbles, subnormal/negative scales), dequant-matvec, RMSNorm, RoPE, softmax,
   argmax ties.
 
-Usage: python tests/golden/make_golden.py [config ...]   (default: small set)
-Needs /root/reference (the reference sources) -- fixtures are committed so the
-tests never need it.
+Usage: python tests/golden/make_golden.py [fixture ...]   (default: small set)
+Needs the reference sources (oracle/build_ref.py finds them) -- fixtures are
+committed so the tests never need them.
+
+A fixture is named after its configuration, or after the configuration plus a
+suffix when it runs a shorter prompt or starts past position 0 (SPECS below):
+the large configurations run a short prompt and a few steps so the reference's
+CPU path finishes in minutes, and ``llama3-8b-p600`` starts its prompt at
+position 600 -- past the reference's 512-position cap (layer_scheduler.c:202,
+430), which the ctx8k build raises -- on a cache whose earlier rows are the
+reset zeros on both sides.
 """
 from __future__ import annotations
 
@@ -32,24 +40,37 @@ from tests.golden.fingerprint import gguf_fingerprint  # noqa: E402
 
 OUT = os.path.dirname(os.path.abspath(__file__))
 
-STEPS = {"tiny": 24, "tiny-mha": 20, "tiny-q8": 20, "tinyllama": 64, "llama2-7b": 64}
+# fixture -> (configuration, prompt tokens (None: the configuration's), steps,
+# position of the first prompt token)
+SPECS = {
+    "tiny": ("tiny", None, 24, 0),
+    "tiny-mha": ("tiny-mha", None, 20, 0),
+    "tiny-q8": ("tiny-q8", None, 20, 0),
+    "tinyllama": ("tinyllama", None, 64, 0),
+    "llama2-7b": ("llama2-7b", None, 64, 0),
+    "llama3-8b": ("llama3-8b", 16, 16, 0),
+    "llama3-8b-p600": ("llama3-8b", 8, 8, 600),
+    "llama2-13b": ("llama2-13b", 16, 16, 0),
+    "llama2-70b-4l": ("llama2-70b-4l", 16, 16, 0),
+    "llama2-70b": ("llama2-70b", 8, 8, 0),
+}
 
 
 def make_model_fixture(name: str) -> None:
-    cfg = configs.get(name)
-    steps = STEPS.get(name, 64)
+    cname, nprompt, steps, start = SPECS.get(name, (name, None, 64, 0))
+    cfg = configs.get(cname)
     path = synth.ensure_gguf(cfg)
     ref = oracle.RefModel(path, cfg.ctx)
-    prompt = synth.prompt_tokens(cfg)
+    prompt = synth.prompt_tokens(cfg, nprompt)
     keep = sorted({0, 1, steps // 2, steps - 1})
-    ids, all_logits = ref.greedy(prompt, steps, keep_logits=set(range(steps)))
+    ids, all_logits = ref.greedy(prompt, steps, keep_logits=set(range(steps)), start_pos=start)
     kept = {s: all_logits[s] for s in keep}
     # per step: the 4 best token IDs and their logits, and max |logit|
     order = [np.argsort(-all_logits[s], kind="stable")[:4] for s in range(steps)]
     topk_ids = np.array(order, np.int32)
     topk_vals = np.array([all_logits[s][o] for s, o in enumerate(order)], np.float32)
     absmax = np.array([np.abs(all_logits[s]).max() for s in range(steps)], np.float32)
-    layer, pos = min(1, cfg.n_layers - 1), len(prompt) - 1
+    layer, pos = min(1, cfg.n_layers - 1), start + len(prompt) - 1
     k, v, ks, vs = ref.kv_row(layer, pos)
     np.savez_compressed(
         os.path.join(OUT, f"{name}.npz"),
@@ -59,7 +80,8 @@ def make_model_fixture(name: str) -> None:
         fingerprint=np.frombuffer(gguf_fingerprint(path), np.uint8),
         kv_layer=np.int32(layer), kv_pos=np.int32(pos), k_row=k, v_row=v,
         kv_scales=np.array([ks, vs], np.float32), ctx=np.int32(cfg.ctx),
-        topk_ids=topk_ids, topk_vals=topk_vals, absmax=absmax)
+        topk_ids=topk_ids, topk_vals=topk_vals, absmax=absmax,
+        config=np.array(cname), start_pos=np.int32(start))
     ref.close()
     print(f"{name}: {steps} steps, ids[:8]={ids[:8]}")
 
@@ -145,6 +167,40 @@ def make_ops_fixture() -> None:
     print("ops: written")
 
 
+def make_argmax_fixture() -> None:
+    """argmax.npz: expected ss_argmax results of the edge-case arrays (the big
+    ones are regenerated by the tests from the same seed) and the reference's
+    greedy token for each crafted ``tiny`` model (tests/golden/crafted.py)."""
+    import ctypes
+    import tempfile
+
+    from tests.golden import crafted
+    lib = oracle.ref_ops()
+    f32p = ctypes.POINTER(ctypes.c_float)
+    fx = {}
+    for k, a in crafted.argmax_arrays().items():
+        fx[f"want_{k}"] = np.int32(lib.ssr_argmax(a.ctypes.data_as(f32p), a.size))
+        if a.size < 64:
+            fx[f"in_{k}"] = a
+    cfg = configs.get("tiny")
+    src = synth.ensure_gguf(cfg)
+    prompt = synth.prompt_tokens(cfg)
+    with tempfile.TemporaryDirectory() as td:
+        for case in crafted.CASES:
+            dst = os.path.join(td, f"tiny-{case}.gguf")
+            crafted.make_crafted(case, src, dst)
+            ref = oracle.RefModel(dst, cfg.ctx)
+            lg = ref.prefill(prompt, 0)
+            fx[f"model_{case}"] = np.int32(lib.ssr_argmax(lg.ctypes.data_as(f32p), lg.size))
+            fx[f"model_{case}_nnan"] = np.int32(np.isnan(lg).sum())
+            fx[f"model_{case}_nzero"] = np.int32((lg == 0).sum())
+            ref.close()
+            print(case, int(fx[f"model_{case}"]), "nan", int(fx[f"model_{case}_nnan"]),
+                  "zeros", int(fx[f"model_{case}_nzero"]), "max", np.nanmax(lg))
+    np.savez_compressed(os.path.join(OUT, "argmax.npz"), **fx)
+    print("argmax: written", {k: int(v) for k, v in fx.items() if k.startswith("want_")})
+
+
 def main() -> int:
     if not oracle.ref_available() and not oracle.build_ref():
         print("reference build unavailable", file=sys.stderr)
@@ -153,6 +209,8 @@ def main() -> int:
     for n in names:
         if n == "ops":
             make_ops_fixture()
+        elif n == "argmax":
+            make_argmax_fixture()
         else:
             make_model_fixture(n)
     return 0

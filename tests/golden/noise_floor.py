@@ -36,13 +36,14 @@ OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "noise_floor.json
 
 
 def measure(name: str, steps: int) -> dict:
-    cfg = configs.get(name)
     g = np.load(os.path.join(os.path.dirname(OUT), f"{name}.npz"))
+    cfg = configs.get(str(g["config"]) if "config" in g.files else name)
+    start = int(g["start_pos"]) if "start_pos" in g.files else 0
     m = oracle.OracleModel(synth.ensure_gguf(cfg), int(g["ctx"]))
     m.set_dot_order(1)
     prompt = [int(t) for t in g["prompt"]]
     ref_ids = [int(t) for t in g["ids"]]
-    logits = m.prefill(prompt, 0)
+    logits = m.prefill(prompt, start)
     ref0 = g["logits"][0]
     d = logits.astype(np.float64) - ref0
     res = {"prefill_inf_rel": float(np.abs(d).max() / np.abs(ref0).max()),
@@ -51,7 +52,7 @@ def measure(name: str, steps: int) -> dict:
     steps = min(steps, len(ref_ids))
     kept = {int(s): i for i, s in enumerate(g["logit_steps"])}
     for s in range(1, steps):
-        logits = m.forward(ref_ids[s - 1], len(prompt) + s - 1)
+        logits = m.forward(ref_ids[s - 1], start + len(prompt) + s - 1)
         if s in kept:
             ref = g["logits"][kept[s]]
             worst = max(worst, float(np.abs(logits - ref).max() / np.abs(ref).max()))

@@ -20,20 +20,47 @@ LOGIT_RTOL = 1e-2
 PATHS = {"persistent": 0, "multi-kernel": runtime.FLAG_MULTI_KERNEL}
 
 
+def fixture_config(g: dict, name: str):
+    """The configuration a fixture was made from (its own name for the older
+    fixtures) and the position of its first prompt token."""
+    cname = str(g["config"]) if "config" in g else name
+    return configs.get(cname), int(g["start_pos"]) if "start_pos" in g else 0
+
+
+def report(name: str, path: str, **kw) -> None:
+    """Parity figures of one run: printed, and appended as a JSON line to
+    $SS_PARITY_REPORT when that is set."""
+    import json
+    import os
+    rec = {"fixture": name, "path": path, **kw}
+    print("parity", json.dumps(rec))
+    out = os.environ.get("SS_PARITY_REPORT")
+    if out:
+        with open(out, "a") as f:
+            f.write(json.dumps(rec) + "\n")
+
+
 def _run(name: str, flags: int = 0):
     g = load_golden(name)
-    cfg = configs.get(name)
+    cfg, start = fixture_config(g, name)
     path = synth.ensure_gguf(cfg)
     assert gguf_fingerprint(path) == g["fingerprint"].tobytes()
     m = runtime.CudaModel(path, int(g["ctx"]), flags=flags)
-    assert m.stats()["persistent"] == (0 if flags & runtime.FLAG_MULTI_KERNEL else 1)
+    if flags & runtime.FLAG_MULTI_KERNEL:
+        assert m.stats()["persistent"] == 0
+    elif not m.stats()["persistent"]:
+        # a shape beyond the persistent kernel's limits (the 70B FFN width,
+        # 896 column blocks, on one GPU) runs the multi-kernel step, which the
+        # multi-kernel parameter of the same test covers
+        m.close()
+        pytest.skip(f"{name}: persistent step not eligible on one GPU")
     prompt = [int(t) for t in g["prompt"]]
     steps = len(g["ids"])
     logits = {}
     buf = np.empty(m.vocab, np.float32)
-    ids = [m.prefill(prompt, 0, logits=buf)]
+    ids = [m.prefill(prompt, start, logits=buf)]
     logits[0] = buf.copy()
-    pos = len(prompt)
+    pos = start + len(prompt)
     for s in range(1, steps):
         ids.append(m.forward(ids[-1], pos, logits=buf))
         logits[s] = buf.copy()
@@ -49,7 +76,8 @@ def _run(name: str, flags: int = 0):
 # per configuration (oracle, sso_set_dot_order(1)).  Where twice the floor
 # exceeds 1e-2 (the 32-layer Llama-2-7B shape with a 128-token prompt), the
 # tolerance is twice the floor, and the report says so.
-FIXTURES = ["tiny", "tiny-mha", "tiny-q8", "tinyllama", "llama2-7b"]
+FIXTURES = ["tiny", "tiny-mha", "tiny-q8", "tinyllama", "llama2-7b", "llama3-8b",
+            "llama3-8b-p600", "llama2-13b", "llama2-70b-4l"]
 
 
 def logit_tol(name: str) -> float:
@@ -82,9 +110,13 @@ def test_greedy_parity(name, path):
     g, m, ids, logits = _run(name, PATHS[path])
     ref = [int(t) for t in g["ids"]]
     first = next((i for i, (a, b) in enumerate(zip(ids, ref)) if a != b), len(ref))
-    for i, s in enumerate(g["logit_steps"]):
-        if int(s) <= first:
-            assert rel_err(logits[int(s)], g["logits"][i]) < tol, f"step {s}"
+    errs = {int(s): rel_err(logits[int(s)], g["logits"][i])
+            for i, s in enumerate(g["logit_steps"]) if int(s) <= first}
+    report(name, path, mode="free-running", steps=len(ref), first_divergence=first,
+           identical_ids=first == len(ref), max_rel_logit_err=max(errs.values()),
+           rel_logit_err_by_step=errs, tol=tol, meets_north_star_1e2=max(errs.values()) < 1e-2)
+    for s, e in errs.items():
+        assert e < tol, f"step {s}"
     if first < len(ref):
         assert _acceptable_choice(g, first, ids[first], tol), f"diverged at step {first}"
     m.close()
@@ -99,13 +131,14 @@ def test_teacher_forced_parity(name, path):
     tolerance (elsewhere it must be an acceptable choice)."""
     tol = logit_tol(name)
     g = load_golden(name)
-    cfg = configs.get(name)
+    cfg, start = fixture_config(g, name)
     gpath = synth.ensure_gguf(cfg)
     ref = [int(t) for t in g["ids"]]
+    worst = 0.0
     with runtime.CudaModel(gpath, int(g["ctx"]), flags=PATHS[path]) as m:
         buf = np.empty(m.vocab, np.float32)
         prompt = [int(t) for t in g["prompt"]]
-        got = m.prefill(prompt, 0, logits=buf)
+        got = m.prefill(prompt, start, logits=buf)
         # int8 K/V row written by the prompt: within one quantisation step
         k, v, ks, vs = m.kv_row(int(g["kv_layer"]), int(g["kv_pos"]))
         assert np.abs(k.astype(int) - g["k_row"]).max() <= 1
@@ -114,13 +147,15 @@ def test_teacher_forced_parity(name, path):
         np.testing.assert_allclose([ks, vs], g["kv_scales"], rtol=max(1e-3, tol))
         for s in range(len(ref)):
             if s > 0:
-                got = m.forward(ref[s - 1], len(prompt) + s - 1, logits=buf)
+                got = m.forward(ref[s - 1], start + len(prompt) + s - 1, logits=buf)
             top, vals, am = g["topk_ids"][s], g["topk_vals"][s], float(g["absmax"][s])
+            worst = max(worst, float(np.abs(buf[top] - vals).max() / am))
             assert np.abs(buf[top] - vals).max() / am < tol, f"step {s}"
             if float(vals[0] - vals[1]) > tol * am:
                 assert got == ref[s], f"step {s}"
             else:
                 assert _acceptable_choice(g, s, got, tol), f"step {s}"
+    report(name, path, mode="teacher-forced", steps=len(ref), max_rel_top4_err=worst, tol=tol)
 
 
 @pytest.mark.parametrize("path", PATHS)
@@ -229,3 +264,19 @@ def test_deterministic_across_runs(name):
     assert ids1 == ids2
     for s in lg1:
         np.testing.assert_array_equal(lg1[s], lg2[s])
+
+
+@pytest.mark.parametrize("path", PATHS)
+@pytest.mark.parametrize("case", ["nan0", "zeros", "allzero", "negzero"])
+def test_argmax_rule_through_lm_head(case, path, tmp_path):
+    """The greedy token of the lm_head epilogue follows ss_argmax
+    (tensor.c:318-328) on crafted lm_head rows (tests/golden/crafted.py): a
+    NaN logit at index 0, ties between equal rows, +0.0 against -0.0.  The
+    expected token is the reference's own on the same bytes."""
+    from tests.golden import crafted
+    want = int(load_golden("argmax")[f"model_{case}"])
+    cfg = configs.get("tiny")
+    dst = str(tmp_path / f"tiny-{case}.gguf")
+    crafted.make_crafted(case, synth.ensure_gguf(cfg), dst)
+    with runtime.CudaModel(dst, cfg.ctx, flags=PATHS[path]) as m:
+        assert m.prefill(synth.prompt_tokens(cfg), 0) == want

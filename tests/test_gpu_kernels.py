@@ -179,3 +179,11 @@ def test_op_batch_brackets():
     # inside a batch the arrays are filled at end_batch (ctypes wrote into them)
     np.testing.assert_array_equal(a, ref1)
     np.testing.assert_array_equal(b, ref2)
+
+
+def test_loaded_kernels_are_sm100a():
+    """The kernels the context runs were compiled for sm_100a
+    (cudaFuncAttributes::binaryVersion 100, ss_cuda_stats[14])."""
+    cfg = configs.get("tiny")
+    with runtime.CudaModel(synth.ensure_gguf(cfg), cfg.ctx) as m:
+        assert m.stats()["kernel_arch"] == 100

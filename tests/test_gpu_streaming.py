@@ -151,3 +151,30 @@ def test_streaming_budget_too_small():
     with pytest.raises(runtime.SSCudaError) as e:
         runtime.CudaModel(path, 64, hbm_budget_bytes=2 * layer)
     assert "streaming needs 3" in str(e.value)
+
+
+def test_streaming_llama2_13b_golden_parity():
+    """Configuration 4 as the benchmark runs it: the 13B shape with an HBM
+    budget of 4 layers (1 resident, 39 streamed every step), against the
+    reference's fixture (short prompt, 16 greedy steps)."""
+    from tests.test_gpu_decode import report
+    name = "llama2-13b"
+    g = load_golden(name)
+    cfg = configs.get(name)
+    path = synth.ensure_gguf(cfg)
+    ctx = int(g["ctx"])
+    tol = logit_tol(name)
+    layer = _layer_bytes(path, ctx)
+    ref = [int(t) for t in g["ids"]]
+    with runtime.CudaModel(path, ctx, hbm_budget_bytes=4 * layer) as m:
+        assert m.stats()["resident_layers"] == 1
+        ids, logits = _decode(m, [int(t) for t in g["prompt"]], len(ref))
+    first = next((i for i, (a, b) in enumerate(zip(ids, ref)) if a != b), len(ref))
+    errs = {int(s): rel_err(logits[int(s)], g["logits"][i])
+            for i, s in enumerate(g["logit_steps"]) if int(s) <= first}
+    report(name, "streamed", mode="free-running", steps=len(ref), first_divergence=first,
+           identical_ids=first == len(ref), max_rel_logit_err=max(errs.values()), tol=tol)
+    for s, e in errs.items():
+        assert e < tol, f"step {s}"
+    if first < len(ref):
+        assert _acceptable_choice(g, first, ids[first], tol), f"diverged at step {first}"

@@ -81,3 +81,14 @@ def test_kv_encode(ops):
     ops.sso_kv_encode(fp(v), q.ctypes.data, fp(sc), 8)
     assert sc[0] == np.float32(1.0)
     assert list(q) == [127, -127, 1, -1, 2, 64, -3, 0]
+
+
+def test_argmax_edge_cases(ops):
+    """The restatement's argmax against the reference's on NaN / signed-zero /
+    tie / infinity cases (tests/golden/argmax.npz, made by the reference)."""
+    from tests.golden import crafted
+    g = load_golden("argmax")
+    for name, a in crafted.argmax_arrays().items():
+        assert ops.sso_argmax(fp(a), a.size) == int(g[f"want_{name}"]), name
+        if f"in_{name}" in g:
+            np.testing.assert_array_equal(g[f"in_{name}"].view(np.uint32), a.view(np.uint32))

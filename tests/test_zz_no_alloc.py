@@ -16,6 +16,8 @@ import numpy as np
 import pytest
 
 from phonemap_b200 import configs, runtime, synth
+from tests.conftest import load_golden
+from tests.golden import crafted
 
 pytestmark = pytest.mark.gpu
 
@@ -56,5 +58,22 @@ def test_ties_large_and_sizes():
     assert _noalloc(big) == int(np.argmax(big))
     big[[1000, 700000]] = big.max() + 1.0
     assert _noalloc(big) == 1000
+    # refused before anything is enqueued: too large, empty, NULL pointers
     with pytest.raises(runtime.SSCudaError):
         runtime.argmax_noalloc(1, (1 << 22) + 1, 1)
+    with pytest.raises(runtime.SSCudaError):
+        runtime.argmax_noalloc(1, 0, 1)
+    with pytest.raises(runtime.SSCudaError):
+        runtime.argmax_noalloc(0, 16, 1)
+    with pytest.raises(runtime.SSCudaError):
+        runtime.argmax_noalloc(1, 16, 0)
+
+
+def test_reference_rule_edge_cases():
+    """The reference's scan rule (first maximum; -0.0 ties +0.0; NaN after
+    index 0 never wins; NaN at index 0 keeps index 0) on the cases whose
+    expected index the reference's own ss_argmax gave (tests/golden/argmax.npz),
+    including 4,194,304 values -- the size limit, every partial slot in use."""
+    g = load_golden("argmax")
+    for name, values in crafted.argmax_arrays().items():
+        assert _noalloc(values) == int(g[f"want_{name}"]), name
