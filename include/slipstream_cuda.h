@@ -201,6 +201,16 @@ void ss_cuda_reset(ss_cuda_ctx_t *ctx);
  * (ss_cancel, engine.c:372-379). */
 void ss_cuda_cancel(ss_cuda_ctx_t *ctx);
 
+/* Test aid, no reference counterpart: makes the next persistent decode step
+ * fail on the device without faulting -- its producer issues no copy for the
+ * first weight stage of `phase` (1 = layer 0's QKV, 5 l + 1 + {0 QKV, 2 O, 3
+ * gate/up, 4 down} = layer l's phases, 5 L + 1 = the lm_head), and every wait
+ * of that step gives up after ~2 ms of clocks instead of ~1 s.  The step then
+ * returns SS_CUDA_ERROR_BACKEND (device error bit 4, a ring wait ran out);
+ * ss_cuda_reset makes the context usable again.  Single-GPU persistent step
+ * only (SS_CUDA_ERROR_INVALID_PARAMS otherwise). */
+int ss_cuda_test_fail_next_step(ss_cuda_ctx_t *ctx, int32_t phase);
+
 /* ---- allocation-free greedy argmax (no counterpart in the reference) ----
  * For callers that cannot allocate device memory where they need a greedy
  * token -- e.g. while a stream is being captured into a CUDA graph, where

@@ -87,6 +87,8 @@ SS_DEVINL uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*
 SS_DEVINL uint16_t lds16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
 
 constexpr long long kWaitBudget = 1LL << 31;  // ~1 s of SM clocks
+// the budget of one failure-path test step (ss_cuda_test_fail_next_step)
+constexpr long long kTestWaitBudget = 1LL << 22;  // ~2 ms
 
 SS_DEVINL float half_bits_to_float(uint16_t h) {
   return __half2float(__ushort_as_half(h));

@@ -306,6 +306,7 @@ SS_DEVINL void mbar_arrive(uint32_t bar) {
 }
 
 constexpr int kGemvG = 4;  // rows per consumer warp per stage
+constexpr int kGemvMaxNb = 512;  // column blocks of one GEMV: one per consumer thread of a row-group
 
 template <int TYPE, XSrc XS, Epi EPI, int RG>
 __global__ void __launch_bounds__(544) gemv_kernel(const GemvParams p) {

@@ -159,8 +159,8 @@ GemvLaunch plan_gemv(Context* c, GemvFn fn, const DevMatrix& m, int rg) {
   GemvLaunch g;
   g.fn = (const void*)fn;
   const int nb = m.cols / 32;
-  if (nb < 1 || nb > 512)
-    fail(SS_CUDA_ERROR_INVALID_MODEL, "matrix with %d columns is outside 32..16384", m.cols);
+  if (nb < 1 || nb > kGemvMaxNb)
+    fail(SS_CUDA_ERROR_INVALID_MODEL, "matrix with %d columns is outside 32..%d", m.cols, 32 * kGemvMaxNb);
   const int nbt = round_up(nb, 32);
   g.threads = 32 + nbt * rg;  // producer warp + consumer row-groups
   g.stage_rows = kGemvG * rg;
@@ -478,12 +478,20 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
     // every layer's four matrices in one allocation at a fixed stride (the
     // persistent step addresses layer l as layer 0 + l * stride), and the
     // norm weights as [L][d] arrays
+    // an FFN wider than one GEMV's columns: down as two column halves
+    const bool split_down = !c->mega && c->ff / 32 > kGemvMaxNb;
+    if (split_down && (c->tp_size > 1 || c->streaming || c->ff % 64 || c->ff / 64 > kGemvMaxNb))
+      fail(SS_CUDA_ERROR_INVALID_MODEL,
+           "FFN width %d needs the down projection split in two, which supports one GPU without "
+           "streaming and widths up to %d", c->ff, 64 * kGemvMaxNb);
+    const int down_cols = split_down ? c->ff / 2 : c->ff;
     const DevMatrix s_qkv = mat_layout(qd + 2 * kvd, c->d, c->wtype), s_o = mat_layout(c->d, qd, c->wtype),
-                    s_gu = mat_layout(2 * c->ff, c->d, c->wtype), s_down = mat_layout(c->d, c->ff, c->wtype);
+                    s_gu = mat_layout(2 * c->ff, c->d, c->wtype), s_down = mat_layout(c->d, down_cols, c->wtype);
     const size_t o_o = round_up_sz(matrix_bytes(s_qkv), 256);
     const size_t o_gu = o_o + round_up_sz(matrix_bytes(s_o), 256);
     const size_t o_down = o_gu + round_up_sz(matrix_bytes(s_gu), 256);
-    c->layer_stride = o_down + round_up_sz(matrix_bytes(s_down), 256);
+    const size_t o_down2 = o_down + round_up_sz(matrix_bytes(s_down), 256);
+    c->layer_stride = split_down ? o_down2 + round_up_sz(matrix_bytes(s_down), 256) : o_down2;
     // streaming: the budget holds the resident layers, two slots and the raw
     // bytes of the layer being repacked (about one more layer)
     int hbm_layers = c->L;
@@ -529,8 +537,13 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
       ly.o.data = ly.block + o_o;
       ly.gu.data = ly.block + o_gu;
       ly.down.data = ly.block + o_down;
+      if (split_down) {
+        ly.down2 = s_down;
+        ly.down2.data = ly.block + o_down2;
+      }
       if (l < c->n_resident || !c->streaming)
-        c->weight_bytes += matrix_bytes(s_qkv) + matrix_bytes(s_o) + matrix_bytes(s_gu) + matrix_bytes(s_down);
+        c->weight_bytes += matrix_bytes(s_qkv) + matrix_bytes(s_o) + matrix_bytes(s_gu) +
+                           (split_down ? 2 : 1) * matrix_bytes(s_down);
       ly.attn_norm = c->attn_norm_all + (size_t)l * c->d;
       ly.ffn_norm = c->ffn_norm_all + (size_t)l * c->d;
       upload_f32_into(c, need(g, nm("attn_norm.weight")), (size_t)c->d, ly.attn_norm);
@@ -566,6 +579,7 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
       upload_matrix(c, wg, ly.gu, 2, 0, stage, max_bytes, r * c->ff, c->ff);
       upload_matrix(c, wu, ly.gu, 2, 1, stage, max_bytes, r * c->ff, c->ff);
       upload_matrix(c, wd, ly.down, 1, 0, stage, max_bytes, 0, -1, r * c->ff / 32);
+      if (split_down) upload_matrix(c, wd, ly.down2, 1, 0, stage, max_bytes, 0, -1, down_cols / 32);
       CK(cudaStreamSynchronize(c->stream));  // staging buffer reuse
     }
     c->out_norm = upload_f32(c, need(g, "output_norm.weight"), (size_t)c->d);
@@ -705,6 +719,8 @@ void alloc_step_state(Context* c) {
   p.inflight = std::max(1, std::min(c->step_nslots, env_int("SS_STEP_INFLIGHT", c->step_nslots)));
   p.prefetch = env_int("SS_STEP_PREFETCH", 0);
   p.split_rows = std::max(16, env_int("SS_STEP_SPLIT_ROWS", 64));
+  p.wait_budget = kWaitBudget;
+  p.test_withhold = -1;
   if (c->trace) {
     const size_t n = (size_t)(2 + 5 * c->L) * ncta * 8;
     c->step_trace = dev_alloc<long long>(c, n);
@@ -724,7 +740,14 @@ void launch_step(Context* c) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  void* args[2] = {&c->step_params, &c->step_tp};
+  StepParams p = c->step_params;
+  if (c->test_fail_phase > 0) {
+    // one step of the failure-path test (ss_cuda_test_fail_next_step)
+    p.test_withhold = c->test_fail_phase;
+    p.wait_budget = kTestWaitBudget;
+    c->test_fail_phase = 0;
+  }
+  void* args[2] = {&p, &c->step_tp};
   CK(cudaLaunchKernelExC(&cfg, c->step_fn, args));
 }
 
@@ -857,13 +880,21 @@ void launch_gu(Context* c, int l, bool pdl) {
 // h = Wdown . act + h  (tensor parallelism: this rank's FFN columns, then
 // the all-reduce)
 void launch_down(Context* c, int l, bool pdl) {
+  const Layer& ly = c->layers[(size_t)l];
   GemvParams p = base_params(c);
-  p.w = c->layers[(size_t)l].down.q();
+  p.w = ly.down.q();
   p.x = c->act;
   const bool tp = c->tp_size > 1;
   p.out = tp ? c->hpart : c->h;
   p.residual = (!tp || c->tp_rank == 0) ? c->h : nullptr;
   run_gemv(c, c->g_down, p, pdl);
+  if (ly.down2.cols) {
+    // the second half of the FFN columns adds to the h the first half wrote
+    // (one GPU only: the split is refused with tensor parallelism)
+    p.w = ly.down2.q();
+    p.x = c->act + ly.down.cols;
+    run_gemv(c, c->g_down, p, pdl);
+  }
   if (tp) tp_reduce_h(c);
 }
 
@@ -1457,6 +1488,7 @@ SS_API int ss_cuda_stats(const ss_cuda_ctx_t* ctx, int64_t* out, int32_t n) {
     const int64_t arch = cudaFuncGetAttributes(&fa, embed_kernel) == cudaSuccess ? fa.binaryVersion : -1;
     cudaGetLastError();
     const int64_t v[15] = {c->has_model ? (c->mega ? 1 : 2 + 5LL * c->L + (c->tp_size > 1) +
+                                                   (c->layers[0].down2.cols ? (int64_t)c->L : 0) +
                                                    (c->streaming ? 7LL * (c->L - c->n_resident) : 0))
                                        : 0,
                            (int64_t)c->weight_bytes,
@@ -1569,6 +1601,17 @@ SS_API void ss_cuda_reset(ss_cuda_ctx_t* ctx) {
 
 SS_API void ss_cuda_scheduler_reset(ss_cuda_ctx_t* ctx) { ss_cuda_reset(ctx); }
 
+SS_API int ss_cuda_test_fail_next_step(ss_cuda_ctx_t* ctx, int32_t phase) {
+  return guard([&] {
+    Context* c = need_model(ctx);
+    if (!c->mega) fail(SS_CUDA_ERROR_INVALID_PARAMS, "only the persistent step has this test aid");
+    if (c->tp_size > 1) fail(SS_CUDA_ERROR_INVALID_PARAMS, "single-GPU contexts only");
+    if (phase < 1 || phase > 1 + 5 * c->L) fail(SS_CUDA_ERROR_INVALID_PARAMS, "phase %d", phase);
+    if ((phase - 1) % 5 == 1) fail(SS_CUDA_ERROR_INVALID_PARAMS, "phase %d streams no weights", phase);
+    c->test_fail_phase = phase;
+  });
+}
+
 SS_API void ss_cuda_cancel(ss_cuda_ctx_t* ctx) {
   auto* c = reinterpret_cast<Context*>(ctx);
   if (c) c->cancelled.store(true);
@@ -1676,7 +1719,32 @@ SS_API int ss_cuda_dequantize_tensor(ss_cuda_ctx_t* ctx, const char* name, float
       else if (suf == "attn_output.weight") { m = &ly.o; rows = c->d; }
       else if (suf == "ffn_gate.weight") { m = &ly.gu; rows = c->ff; mul = 2; }
       else if (suf == "ffn_up.weight") { m = &ly.gu; rows = c->ff; mul = 2; add = 1; }
-      else if (suf == "ffn_down.weight") { m = &ly.down; rows = c->d; }
+      else if (suf == "ffn_down.weight") {
+        m = &ly.down;
+        rows = c->d;
+        if (ly.down2.cols) {
+          // the two column halves, each dequantised and placed side by side
+          if (n != (int64_t)rows * 2 * m->cols) fail(SS_CUDA_ERROR_INVALID_PARAMS, "n must be rows*cols");
+          const size_t half = (size_t)rows * m->cols;
+          float* d_tmp = nullptr;
+          CK(cudaMalloc(&d_tmp, sizeof(float) * half));
+          cudaError_t e = cudaSuccess;
+          for (int k = 0; k < 2 && e == cudaSuccess; k++) {
+            const DevMatrix& mk = k ? ly.down2 : ly.down;
+            dequant_rows_kernel<<<1024, 256, 0, c->stream>>>(mk.data, rows, mk.cols, mk.type, mk.row_stride,
+                                                            mk.scale_off, 1, 0, d_tmp);
+            e = cudaGetLastError();
+            if (e == cudaSuccess)
+              e = cudaMemcpy2DAsync(out + (size_t)k * mk.cols, sizeof(float) * 2 * mk.cols, d_tmp,
+                                    sizeof(float) * mk.cols, sizeof(float) * mk.cols, rows,
+                                    cudaMemcpyDeviceToHost, c->stream);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+          }
+          cudaFree(d_tmp);
+          CK(e);
+          return;
+        }
+      }
     }
     if (!m) fail(SS_CUDA_ERROR_INVALID_PARAMS, "no quantized tensor %s", name);
     if (n != (int64_t)rows * m->cols) fail(SS_CUDA_ERROR_INVALID_PARAMS, "n must be rows*cols = %lld", (long long)rows * m->cols);
@@ -1775,12 +1843,13 @@ SS_API int64_t ss_cuda_kernel_bytes(const ss_cuda_ctx_t* ctx, int32_t which) {
     case 0: return (int64_t)matrix_bytes(l0.qkv);
     case 2: return (int64_t)matrix_bytes(l0.o);
     case 3: return (int64_t)matrix_bytes(l0.gu);
-    case 4: return (int64_t)matrix_bytes(l0.down);
+    case 4: return (int64_t)(matrix_bytes(l0.down) + (l0.down2.cols ? matrix_bytes(l0.down2) : 0));
     case 5: return (int64_t)matrix_bytes(c->lm_head);
     case 6: {
       int64_t b = (int64_t)matrix_bytes(c->lm_head);
       for (const Layer& ly : c->layers)
-        b += (int64_t)(matrix_bytes(ly.qkv) + matrix_bytes(ly.o) + matrix_bytes(ly.gu) + matrix_bytes(ly.down));
+        b += (int64_t)(matrix_bytes(ly.qkv) + matrix_bytes(ly.o) + matrix_bytes(ly.gu) + matrix_bytes(ly.down) +
+                       (ly.down2.cols ? matrix_bytes(ly.down2) : 0));
       return b;
     }
     default: return -1;

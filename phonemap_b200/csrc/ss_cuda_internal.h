@@ -37,6 +37,10 @@ struct GemvLaunch {
 
 struct Layer {
   DevMatrix qkv, o, gu, down;  // gu rows interleave gate (even) and up (odd)
+  // FFN widths beyond one GEMV's 16384 columns (the 70B shape on one GPU, the
+  // multi-kernel step): `down` holds the first half of the FFN columns and
+  // `down2` the second; both GEMVs add into h in turn.  down2.cols == 0: unsplit.
+  DevMatrix down2;
   float* attn_norm = nullptr;
   float* ffn_norm = nullptr;
   uint8_t* block = nullptr;    // one allocation holding the four matrices
@@ -72,6 +76,7 @@ struct Context {
   bool use_pdl = true;
   bool use_graph = true;
   bool trace = false;
+  int test_fail_phase = 0;  // > 0: the next persistent step runs the failure-path test
   GemvTuning tuning;
   std::atomic<bool> cancelled{false};
 

@@ -184,6 +184,13 @@ struct StepParams {
   // stage's weights ready, 5 last stage's weights ready, 6 consumer warp 0
   // done with its rows, 7 producer issued the phase's first stage
   long long* trace;
+  // every bounded wait gives up after this many SM clocks (kWaitBudget; the
+  // cross-rank waits 4x); a failure-path test shortens it for one step
+  long long wait_budget;
+  // test aid (ss_cuda_test_fail_next_step): the producer issues no copy for
+  // the first weight stage of phase `test_withhold` (-1: off), so that stage's
+  // consumers wait until their budget runs out and the step reports an error
+  int test_withhold;
 };
 
 // ---------------------------------------------------------------- helpers
@@ -380,7 +387,7 @@ SS_DEVINL void step_producer(const StepParams& p, const StepSmem& sm, const vola
       const long long c0 = clock64();
       while (!mbar_try_wait(bar, par)) {
         if (*s_cabort || ld_volatile_u32(p.abort_flag)) return false;
-        if (clock64() - c0 > kWaitBudget) {
+        if (clock64() - c0 > p.wait_budget) {
           atomicOr(p.err, 4);
           atomicExch(p.abort_flag, 1u);
           return false;
@@ -441,6 +448,10 @@ SS_DEVINL void step_producer(const StepParams& p, const StepSmem& sm, const vola
       if (!fb) { aborted = true; break; }
       const int nt = min(rg, t1 - t);
       const uint32_t bytes = (uint32_t)(nt * m->tile_bytes);
+      if (k == p.test_withhold && t == t0) {  // test aid: this stage never lands
+        advance();
+        continue;
+      }
       mbar_expect_tx(fb, bytes);
       bulk_g2s(ring0 + (uint32_t)slot * slot_bytes, m->w + (size_t)t * m->tile_bytes, bytes, fb);
       advance();
@@ -451,7 +462,7 @@ SS_DEVINL void step_producer(const StepParams& p, const StepSmem& sm, const vola
   if (aborted) {
     // drain: the copies of the last nslots stages may still be in flight
     for (int g = max(0, issued - nslots); g < issued; g++)
-      mbar_wait_bounded(smem_addr(sm.full + g % nslots), (uint32_t)((g / nslots) & 1), kWaitBudget);
+      mbar_wait_bounded(smem_addr(sm.full + g % nslots), (uint32_t)((g / nslots) & 1), p.wait_budget);
   }
 }
 
@@ -499,7 +510,7 @@ SS_DEVINL bool step_grid_wait(const StepParams& p, ConsumerCtx& cc, unsigned tar
       const unsigned v = ld_acquire_u32(p.grid_bar);
       if ((int)(v - target) >= 0) break;
       if (ld_volatile_u32(p.abort_flag)) { bad = true; break; }
-      if (clock64() - c0 > kWaitBudget) {
+      if (clock64() - c0 > p.wait_budget) {
         atomicOr(p.err, 8);
         atomicExch(p.abort_flag, 1u);
         bad = true;
@@ -569,7 +580,7 @@ SS_DEVINL float* xchg_h(const StepTp& t, int rank, int s, int d) {
 }
 // Peers may still be launching their step: the cross-rank waits get a longer
 // budget than the local ones.
-constexpr long long kXWaitBudget = 4 * kWaitBudget;
+SS_DEVINL long long xwait_budget(const StepParams& p) { return 4 * p.wait_budget; }
 
 // Waits until this rank's counter holds the arrivals of the `ncross` cross
 // phases of this step after the `epoch` earlier steps (3 per layer each), every
@@ -587,7 +598,7 @@ SS_DEVINL bool step_xwait(const StepParams& p, const StepTp& t, ConsumerCtx& cc,
       // relaxed polling; one acquire fence once the count is there
       if ((long long)(ld_relaxed_sys_u64(ctr) - target) >= 0) break;
       if (ld_volatile_u32(p.abort_flag)) { bad = true; break; }
-      if (clock64() - c0 > kXWaitBudget) {
+      if (clock64() - c0 > xwait_budget(p)) {
         atomicOr(p.err, 32);
         atomicExch(p.abort_flag, 1u);
         bad = true;
@@ -647,7 +658,7 @@ SS_DEVINL bool warp_wait_phase(const StepParams& p, uint32_t bar, uint32_t par) 
   while (true) {
     const bool ok = mbar_try_wait(bar, par);
     if (__all_sync(0xffffffffu, ok)) return true;
-    const bool late = !ok && (ld_volatile_u32(p.abort_flag) != 0u || clock64() - w0 > kWaitBudget);
+    const bool late = !ok && (ld_volatile_u32(p.abort_flag) != 0u || clock64() - w0 > p.wait_budget);
     if (__any_sync(0xffffffffu, late)) {
       if ((threadIdx.x & 31) == 0) {
         atomicOr(p.err, 4);
@@ -1578,7 +1589,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
             const unsigned long long* ctr = xchg_u64(t, t.rank, StepXchg::kHead);
             const long long c0 = clock64();
             while ((long long)(ld_relaxed_sys_u64(ctr) - target) < 0) {
-              if (clock64() - c0 > kXWaitBudget) {
+              if (clock64() - c0 > xwait_budget(p)) {
                 atomicOr(p.err, 32);
                 atomicExch(p.abort_flag, 1u);
                 ok = false;

@@ -33,7 +33,7 @@ EXPORTED = [
     "ss_cuda_decode_read", "ss_cuda_stream", "ss_cuda_reset", "ss_cuda_cancel",
     "ss_cuda_dequantize_tensor", "ss_cuda_dequantize", "ss_cuda_kv_row",
     "ss_cuda_time_kernel", "ss_cuda_kernel_bytes", "ss_cuda_argmax_noalloc",
-    "ss_cuda_step_trace", "ss_cuda_tp_unique_id",
+    "ss_cuda_step_trace", "ss_cuda_tp_unique_id", "ss_cuda_test_fail_next_step",
 ]
 
 
@@ -111,6 +111,7 @@ def load_library() -> ctypes.CDLL:
     lib.ss_cuda_time_kernel.argtypes = [vp, ctypes.c_int32, ctypes.c_int32, _f32p]
     lib.ss_cuda_kernel_bytes.argtypes = [vp, ctypes.c_int32]
     lib.ss_cuda_kernel_bytes.restype = ctypes.c_int64
+    lib.ss_cuda_test_fail_next_step.argtypes = [vp, ctypes.c_int32]
     lib.ss_cuda_argmax_noalloc.argtypes = [vp, ctypes.c_int32, vp, vp]
     lib.ss_cuda_step_trace.argtypes = [vp, _i64p, ctypes.c_int64]
     lib.ss_cuda_tp_unique_id.argtypes = [vp]
@@ -237,6 +238,11 @@ class CudaModel:
         if n_steps <= 1:
             return [first][:n_steps]
         return [first] + self.decode_greedy(first, len(prompt), n_steps - 1)
+
+    def test_fail_next_step(self, phase: int) -> None:
+        """Test aid: the next persistent step withholds one weight copy and
+        reports an error after its shortened waits run out."""
+        _check(self._lib.ss_cuda_test_fail_next_step(self._h, int(phase)))
 
     def stream(self) -> int:
         return int(self._lib.ss_cuda_stream(self._h) or 0)

@@ -280,3 +280,28 @@ def test_argmax_rule_through_lm_head(case, path, tmp_path):
     crafted.make_crafted(case, synth.ensure_gguf(cfg), dst)
     with runtime.CudaModel(dst, cfg.ctx, flags=PATHS[path]) as m:
         assert m.prefill(synth.prompt_tokens(cfg), 0) == want
+
+
+@pytest.mark.parametrize("phase_of", ["qkv0", "down1", "head"])
+def test_bounded_wait_expires_then_reset_recovers(phase_of):
+    """A device wait that runs out (the producer withholds one weight stage:
+    ss_cuda_test_fail_next_step) ends the step with SS_CUDA_ERROR_BACKEND and
+    the ring-wait error bit -- no fault, no hang -- and after ss_cuda_reset
+    the same context decodes the reference's tokens again."""
+    g = load_golden("tiny")
+    cfg = configs.get("tiny")
+    L = cfg.n_layers
+    phase = {"qkv0": 1, "down1": 5 * 1 + 1 + 4, "head": 5 * L + 1}[phase_of]
+    prompt = [int(t) for t in g["prompt"]]
+    ref = [int(t) for t in g["ids"]]
+    with runtime.CudaModel(synth.ensure_gguf(cfg), int(g["ctx"])) as m:
+        first = m.prefill(prompt, 0)
+        assert first == ref[0]
+        m.test_fail_next_step(phase)
+        with pytest.raises(runtime.SSCudaError) as e:
+            m.forward(first, len(prompt))
+        assert e.value.code == -7 and "ring wait" in str(e.value)
+        m.reset()
+        first = m.prefill(prompt, 0)
+        ids = [first] + m.decode_greedy(first, len(prompt), 7)
+        assert ids == ref[:8]
