@@ -143,7 +143,11 @@ def test_teacher_forced_parity(name, path):
         k, v, ks, vs = m.kv_row(int(g["kv_layer"]), int(g["kv_pos"]))
         assert np.abs(k.astype(int) - g["k_row"]).max() <= 1
         assert np.abs(v.astype(int) - g["v_row"]).max() <= 1
-        assert (k == g["k_row"]).mean() > 0.98 and (v == g["v_row"]).mean() > 0.98
+        # the share of exactly equal int8 values: a last-bit difference upstream
+        # moves a value across a roundf .5 boundary, more often the deeper the
+        # configuration's noise floor (4-layer 70B shape: about 2% differ by one)
+        same = 0.98 if logit_tol(name) <= LOGIT_RTOL else 0.95
+        assert (k == g["k_row"]).mean() > same and (v == g["v_row"]).mean() > same
         np.testing.assert_allclose([ks, vs], g["kv_scales"], rtol=max(1e-3, tol))
         for s in range(len(ref)):
             if s > 0:
