@@ -231,6 +231,16 @@ int ss_cuda_test_fail_next_step(ss_cuda_ctx_t *ctx, int32_t phase);
  * (cudaDeviceReset) after it -- the kept address would be stale. */
 int ss_cuda_argmax_noalloc(const float *d_values, int32_t n, int32_t *d_index, void *stream);
 
+/* Many-token twin of the op-level matvec (ss_cuda_matvec_q4_0 / _q8_0 for
+ * n_tokens vectors at once, the pass over the weights shared): out[t] = W . x[t]
+ * for the uploaded quantized tensor `name` (GGUF name, this rank's rows under
+ * tensor parallelism), x as [n_tokens][cols] and out as [n_tokens][rows], host
+ * memory, n_tokens 1..32.  Runs on the tensor cores (tcgen05, int8 planes of
+ * the activations against the weights' int8 values, per-block fp16 scales in
+ * fp32) -- the product the prompt and multi-sequence paths use.  Needs the
+ * persistent step's weight layout (SS_CUDA_ERROR_INVALID_PARAMS otherwise). */
+int ss_cuda_matmul_batch(ss_cuda_ctx_t *ctx, const char *name, const float *x, int32_t n_tokens, float *out);
+
 /* ---- inspection (parity tests) ----
  * fp32 dequantisation of an uploaded weight tensor by GGUF name, rows in GGUF
  * order (n = rows * cols floats), computed on the device from the repacked

@@ -1373,10 +1373,76 @@ bool op_matvec(ss_cuda_ctx_t* ctx, float* out, const void* mat, const float* vec
          }) == SS_CUDA_OK;
 }
 
+#include "qgemm_host.inc"
+
+// A quantized weight tensor by GGUF name: its device matrix and where its rows
+// sit there (row r of the tensor is matrix row r * mul + add).
+const DevMatrix* find_named(Context* c, const std::string& s, int& rows, int& mul, int& add) {
+  mul = 1;
+  add = 0;
+  rows = 0;
+  const int qd = c->nh * c->hd, kvd = c->nkv * c->hd;
+  if (s == "output.weight") { rows = c->vocab_l; return &c->lm_head; }
+  if (s.rfind("blk.", 0) != 0) return nullptr;
+  const int l = atoi(s.c_str() + 4);
+  const size_t dot = s.find('.', 4);
+  if (l < 0 || l >= c->L || dot == std::string::npos) return nullptr;
+  const std::string suf = s.substr(dot + 1);
+  const Layer& ly = c->layers[(size_t)l];
+  if (suf == "attn_q.weight") { rows = qd; return &ly.qkv; }
+  if (suf == "attn_k.weight") { rows = kvd; add = qd; return &ly.qkv; }
+  if (suf == "attn_v.weight") { rows = kvd; add = qd + kvd; return &ly.qkv; }
+  if (suf == "attn_output.weight") { rows = c->d; return &ly.o; }
+  if (suf == "ffn_gate.weight") { rows = c->ff; mul = 2; return &ly.gu; }
+  if (suf == "ffn_up.weight") { rows = c->ff; mul = 2; add = 1; return &ly.gu; }
+  if (suf == "ffn_down.weight") { rows = c->d; return ly.down2.cols ? nullptr : &ly.down; }
+  return nullptr;
+}
+
 }  // namespace
 }  // namespace ss
 
 using namespace ss;
+
+SS_API int ss_cuda_matmul_batch(ss_cuda_ctx_t* ctx, const char* name, const float* x, int32_t n_tokens,
+                                float* out) {
+  return guard([&] {
+    Context* c = need_model(ctx);
+    if (!name || !x || !out) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null argument");
+    if (n_tokens < 1 || n_tokens > kQgMaxT) fail(SS_CUDA_ERROR_INVALID_PARAMS, "n_tokens must be 1..%d", kQgMaxT);
+    int rows, mul, add;
+    const DevMatrix* m = find_named(c, name, rows, mul, add);
+    if (!m) fail(SS_CUDA_ERROR_INVALID_PARAMS, "no quantized tensor %s", name);
+    if (!m->tiled) fail(SS_CUDA_ERROR_INVALID_PARAMS, "the many-token product needs the persistent step's layout");
+    const int T = n_tokens, K = m->cols, R = m->rows;
+    float* d_x = nullptr;
+    float* d_y = nullptr;
+    CK(cudaMalloc(&d_x, sizeof(float) * (size_t)T * K));
+    cudaError_t e = cudaMalloc(&d_y, sizeof(float) * (size_t)T * R);
+    std::vector<float> y((size_t)T * R);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d_x, x, sizeof(float) * (size_t)T * K, cudaMemcpyHostToDevice, c->stream);
+    int nsplit = 0;
+    if (e == cudaSuccess) {
+      try {
+        nsplit = qg_product(c, *m, d_x, K, nullptr, T);
+      } catch (...) {
+        cudaFree(d_x);
+        cudaFree(d_y);
+        throw;
+      }
+      qg_sum_kernel<<<256, 256, 0, c->stream>>>(c->qg_out, nsplit, T, R, d_y);
+      e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(y.data(), d_y, sizeof(float) * y.size(), cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(d_x);
+    cudaFree(d_y);
+    CK(e);
+    check_device_error(c);
+    for (int t = 0; t < T; t++)
+      for (int r = 0; r < rows; r++) out[(size_t)t * rows + r] = y[(size_t)t * R + (size_t)r * mul + add];
+  });
+}
 
 // ======================================================================= C ABI
 

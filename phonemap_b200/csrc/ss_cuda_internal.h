@@ -11,6 +11,7 @@
 #include "gemv.cuh"
 #include "gguf_view.h"
 #include "misc_kernels.cuh"
+#include "qgemm.cuh"
 #include "step_kernel.cuh"
 #include "tp_nccl.h"
 
@@ -77,6 +78,16 @@ struct Context {
   bool use_graph = true;
   bool trace = false;
   int test_fail_phase = 0;  // > 0: the next persistent step runs the failure-path test
+  // many-token tensor-core product (qgemm.cuh): tensor maps per weight
+  // matrix, activation planes, partial sums
+  std::unordered_map<const void*, QgMaps> qg_maps;
+  int8_t* qg_xq = nullptr;
+  size_t qg_xq_bytes = 0;
+  float* qg_xc = nullptr;
+  size_t qg_xc_floats = 0;
+  float* qg_scale = nullptr;
+  float* qg_out = nullptr;
+  size_t qg_out_floats = 0;
   GemvTuning tuning;
   std::atomic<bool> cancelled{false};
 

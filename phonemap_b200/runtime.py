@@ -34,6 +34,7 @@ EXPORTED = [
     "ss_cuda_dequantize_tensor", "ss_cuda_dequantize", "ss_cuda_kv_row",
     "ss_cuda_time_kernel", "ss_cuda_kernel_bytes", "ss_cuda_argmax_noalloc",
     "ss_cuda_step_trace", "ss_cuda_tp_unique_id", "ss_cuda_test_fail_next_step",
+    "ss_cuda_matmul_batch",
 ]
 
 
@@ -111,6 +112,7 @@ def load_library() -> ctypes.CDLL:
     lib.ss_cuda_time_kernel.argtypes = [vp, ctypes.c_int32, ctypes.c_int32, _f32p]
     lib.ss_cuda_kernel_bytes.argtypes = [vp, ctypes.c_int32]
     lib.ss_cuda_kernel_bytes.restype = ctypes.c_int64
+    lib.ss_cuda_matmul_batch.argtypes = [vp, ctypes.c_char_p, _f32p, ctypes.c_int32, _f32p]
     lib.ss_cuda_test_fail_next_step.argtypes = [vp, ctypes.c_int32]
     lib.ss_cuda_argmax_noalloc.argtypes = [vp, ctypes.c_int32, vp, vp]
     lib.ss_cuda_step_trace.argtypes = [vp, _i64p, ctypes.c_int64]
@@ -238,6 +240,14 @@ class CudaModel:
         if n_steps <= 1:
             return [first][:n_steps]
         return [first] + self.decode_greedy(first, len(prompt), n_steps - 1)
+
+    def matmul_batch(self, name: str, x: np.ndarray, rows: int) -> np.ndarray:
+        """out[t] = W(name) . x[t] for the rows of x ([n_tokens][cols]) on the
+        tensor cores (ss_cuda_matmul_batch)."""
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty((x.shape[0], rows), np.float32)
+        _check(self._lib.ss_cuda_matmul_batch(self._h, name.encode(), _f(x), x.shape[0], _f(out)))
+        return out
 
     def test_fail_next_step(self, phase: int) -> None:
         """Test aid: the next persistent step withholds one weight copy and
