@@ -77,6 +77,9 @@ typedef struct {
 #define SS_CUDA_FLAG_MULTI_KERNEL 4u
 /* Record a per-phase timeline of every persistent step (measurement aid). */
 #define SS_CUDA_FLAG_TRACE 8u
+/* Ingest prompts by replaying the decode step once per token (the reference's
+ * token-by-token order) instead of the many-token tensor-core step. */
+#define SS_CUDA_FLAG_STEP_PREFILL 16u
 
 /* Fills defaults: device -1, context 0, batch 1, no budget, no flags, no
  * tensor parallelism. */

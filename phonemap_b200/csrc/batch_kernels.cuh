@@ -1,0 +1,245 @@
+// batch_kernels.cuh -- the many-token decoder step around the tensor-core
+// product (qgemm.cuh): T tokens, each with its own sequence and position,
+// through every layer at once.  Serves the prompt (ss_scheduler_prefill,
+// SlipStream/src/core/layer_scheduler.c:681-803: the reference runs the prompt
+// token by token, layer-major; each token's layer l depends only on the cache
+// rows of earlier positions at layer l, so writing the batch's K/V rows first
+// and then attending causally gives the same result) and several sequences
+// decoded together.
+//
+// Per layer (process_layer, layer_scheduler.c:291-567): RMSNorm -> QKV
+// product -> RoPE + int8 K/V append (bt_qkv_kernel) -> attention over each
+// token's own cache rows (bt_attn_kernel) -> O product + residual -> RMSNorm
+// -> gate/up product -> SwiGLU -> down product + residual.  The products
+// leave per-split partial sums; each consumer below adds them in split order.
+#pragma once
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace ss {
+
+// Where token t of the batch goes: its sequence, position, and token id.
+struct BatchTokens {
+  const int* tok;   // [T]
+  const int* pos;   // [T]
+  const int* seq;   // [T]
+};
+
+// KV cache of every sequence: sequence s, layer l at kc + s * seq_stride +
+// l * ctx * kvd, head-major [nkv][ctx][hd] inside a layer; scales at
+// ks + s * sc_stride + l * ctx.
+struct BatchKv {
+  int8_t* kc;
+  int8_t* vc;
+  float* ks;
+  float* vs;
+  size_t seq_stride, sc_stride;
+  int ctx;
+};
+
+SS_DEVINL float split_sum(const float* part, int nsplit, size_t n, size_t i) {
+  float v = part[i];
+  for (int s = 1; s < nsplit; s++) v += part[(size_t)s * n + i];
+  return v;
+}
+
+// h[t] = token_embd[tok[t]] (layer_scheduler.c:584-587); tokens outside the
+// vocabulary set error bit 2 and read row 0.
+__global__ void bt_embed_kernel(const float* __restrict__ embd, int d, int vocab, BatchTokens bt, int T,
+                                float* __restrict__ h, int* err) {
+  const int t = blockIdx.y;
+  int tok = bt.tok[t];
+  if (tok < 0 || tok >= vocab) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(err, 2);
+    tok = 0;
+  }
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < d; i += gridDim.x * blockDim.x)
+    h[(size_t)t * d + i] = embd[(size_t)tok * d + i];
+}
+
+// q|k|v of every token = the product's split sums, with RoPE on q and k
+// (non-NeoX, tensor.c:249-274, the table built on the host with the
+// reference's expressions): q to qout[t], k | v (fp32) to kvtmp[t], and the
+// largest |k| and |v| of each token into amax[t] (float bits as unsigned:
+// non-negative floats order like their bits, so the maximum is exact and
+// independent of the order).  One thread per (q, k) or (k, k+1) pair.
+__global__ void bt_qkv_kernel(const float* __restrict__ part, int nsplit, int T, int rows, int qd, int kvd,
+                              int hd, int rope_dim, const float2* __restrict__ rope_tab, BatchTokens bt,
+                              float* __restrict__ qout, float* __restrict__ kvtmp, unsigned* __restrict__ amax) {
+  const int t = blockIdx.y;
+  const int pr = blockIdx.x * blockDim.x + threadIdx.x;
+  const int r = 2 * pr;
+  float mk = 0.0f, mv = 0.0f;
+  if (r < rows) {
+    const size_t n = (size_t)T * rows;
+    float a = split_sum(part, nsplit, n, (size_t)t * rows + r);
+    float b = split_sum(part, nsplit, n, (size_t)t * rows + r + 1);
+    if (r < qd + kvd) {
+      const int i = r % hd;
+      if (i < rope_dim) {
+        const float2 cs = rope_tab[(size_t)bt.pos[t] * (rope_dim >> 1) + (i >> 1)];
+        const float na = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
+        const float nb = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
+        a = na;
+        b = nb;
+      }
+    }
+    if (r < qd) {
+      qout[(size_t)t * qd + r] = a;
+      qout[(size_t)t * qd + r + 1] = b;
+    } else {
+      kvtmp[(size_t)t * 2 * kvd + (r - qd)] = a;
+      kvtmp[(size_t)t * 2 * kvd + (r - qd) + 1] = b;
+      if (r < qd + kvd) mk = fmaxf(fabsf(a), fabsf(b));
+      else mv = fmaxf(fabsf(a), fabsf(b));
+    }
+  }
+  mk = warp_max(mk);
+  mv = warp_max(mv);
+  if ((threadIdx.x & 31) == 0) {
+    if (mk > 0.0f) atomicMax(amax + 2 * t, __float_as_uint(mk));
+    if (mv > 0.0f) atomicMax(amax + 2 * t + 1, __float_as_uint(mv));
+  }
+}
+
+// The int8 K/V row of each token at (sequence, layer, position) with one
+// scale per row over the whole kv_dim (kv_turboquant_encode,
+// layer_scheduler.c:101-118: scale = max / 127, q = roundf(v / scale)).
+__global__ void bt_kv_encode_kernel(const float* __restrict__ kvtmp, const unsigned* __restrict__ amax, int kvd,
+                                    int hd, BatchTokens bt, BatchKv kv, int layer) {
+  const int t = blockIdx.y;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int pos = bt.pos[t], seq = bt.seq[t];
+  const float k_scale = __uint_as_float(amax[2 * t]) / 127.0f;   // layer_scheduler.c:109-110
+  const float v_scale = __uint_as_float(amax[2 * t + 1]) / 127.0f;
+  if (i < kvd) {
+    const float kinv = k_scale > 0.0f ? 1.0f / k_scale : 0.0f;
+    const float vinv = v_scale > 0.0f ? 1.0f / v_scale : 0.0f;
+    const int kvh = i / hd, j = i - kvh * hd;
+    const size_t o = seq * kv.seq_stride + (size_t)layer * kv.ctx * kvd + ((size_t)kvh * kv.ctx + pos) * hd + j;
+    kv.kc[o] = kv_encode(kvtmp[(size_t)t * 2 * kvd + i], kinv);
+    kv.vc[o] = kv_encode(kvtmp[(size_t)t * 2 * kvd + kvd + i], vinv);
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    kv.ks[seq * kv.sc_stride + (size_t)layer * kv.ctx + pos] = k_scale;
+    kv.vs[seq * kv.sc_stride + (size_t)layer * kv.ctx + pos] = v_scale;
+  }
+}
+
+// Attention of one (query head, token) over positions 0..pos of the token's
+// sequence (layer_scheduler.c:415-468): scores s_j = (q . dec(K_j)) * scale
+// summed in the reference's order (each score one thread, products and sums
+// separately rounded); softmax (tensor.c:154-173: max, expf, sum, times
+// 1/sum); out_i = sum_j p_j * dec(V_j)_i accumulated over j in order, as the
+// reference's saxpy does.  Scores live in shared memory (ctx floats).
+__global__ void __launch_bounds__(256) bt_attn_kernel(const float* __restrict__ q, BatchTokens bt, BatchKv kv,
+                                                      int layer, int nh, int nkv, int hd, float scale,
+                                                      float* __restrict__ out) {
+  extern __shared__ float sm[];  // q[hd] | scores[ctx] | red[64]
+  const int h = blockIdx.x, t = blockIdx.y;
+  const int pos = bt.pos[t], seq = bt.seq[t];
+  const int kvh = h / (nh / nkv), kvd = nkv * hd, qd = nh * hd;
+  float* qs = sm;
+  float* sc = sm + hd;
+  float* red = sc + kv.ctx;
+  for (int i = threadIdx.x; i < hd; i += blockDim.x) qs[i] = q[(size_t)t * qd + (size_t)h * hd + i];
+  __syncthreads();
+  const int8_t* kc = kv.kc + seq * kv.seq_stride + (size_t)layer * kv.ctx * kvd + (size_t)kvh * kv.ctx * hd;
+  const int8_t* vc = kv.vc + seq * kv.seq_stride + (size_t)layer * kv.ctx * kvd + (size_t)kvh * kv.ctx * hd;
+  const float* ks = kv.ks + seq * kv.sc_stride + (size_t)layer * kv.ctx;
+  const float* vs = kv.vs + seq * kv.sc_stride + (size_t)layer * kv.ctx;
+  float mx = -INFINITY;
+  for (int j = threadIdx.x; j <= pos; j += blockDim.x) {
+    const int8_t* kr = kc + (size_t)j * hd;
+    const float s = ks[j];
+    float dot = 0.0f;
+    for (int i = 0; i < hd; i += 16) {
+      const int4 kw = *reinterpret_cast<const int4*>(kr + i);
+      const int8_t* kb = reinterpret_cast<const int8_t*>(&kw);
+#pragma unroll
+      for (int u = 0; u < 16; u++) dot = __fadd_rn(dot, __fmul_rn(qs[i + u], __fmul_rn((float)kb[u], s)));
+    }
+    const float v = __fmul_rn(dot, scale);
+    sc[j] = v;
+    mx = fmaxf(mx, v);
+  }
+  // softmax
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  mx = warp_max(mx);
+  if (lane == 0) red[w] = mx;
+  __syncthreads();
+  mx = -INFINITY;
+  for (int i = 0; i < nw; i++) mx = fmaxf(mx, red[i]);
+  float sum = 0.0f;
+  for (int j = threadIdx.x; j <= pos; j += blockDim.x) {
+    const float e = expf(__fsub_rn(sc[j], mx));
+    sc[j] = e;
+    sum += e;
+  }
+  sum = warp_sum(sum);
+  __syncthreads();
+  if (lane == 0) red[32 + w] = sum;
+  __syncthreads();
+  sum = 0.0f;
+  for (int i = 0; i < nw; i++) sum += red[32 + i];
+  const float inv = 1.0f / sum;
+  // weighted V, element i per thread, positions in order
+  for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+    float acc = 0.0f;
+    for (int j = 0; j <= pos; j++)
+      acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(sc[j], inv), __fmul_rn((float)vc[(size_t)j * hd + i], vs[j])));
+    out[(size_t)t * qd + (size_t)h * hd + i] = acc;
+  }
+}
+
+// h[t][r] += the product (layer_scheduler.c:484, :566).
+__global__ void bt_residual_kernel(const float* __restrict__ part, int nsplit, int T, int rows,
+                                   float* __restrict__ h) {
+  const size_t n = (size_t)T * rows;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    h[i] = __fadd_rn(split_sum(part, nsplit, n, i), h[i]);
+}
+
+// act[t][j] = up * (g / (1 + expf(-g))) (layer_scheduler.c:533-549); the
+// gate/up matrix interleaves gate (even rows) and up (odd rows).
+__global__ void bt_swiglu_kernel(const float* __restrict__ part, int nsplit, int T, int ff,
+                                 float* __restrict__ act) {
+  const size_t n = (size_t)T * 2 * ff, m = (size_t)T * ff;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < m; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t t = i / ff, j = i - t * ff;
+    const float g = split_sum(part, nsplit, n, t * 2 * ff + 2 * j);
+    const float u = split_sum(part, nsplit, n, t * 2 * ff + 2 * j + 1);
+    act[i] = __fmul_rn(u, __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+  }
+}
+
+// Logits of token t (the product's split sums) and the packed (value,
+// index) maximum (pack_argmax: ss_argmax's rule, tensor.c:318-328) into
+// best[t] by atomicMax -- order-independent, so deterministic.
+__global__ void bt_head_kernel(const float* __restrict__ part, int nsplit, int T, int vocab,
+                               float* __restrict__ logits, unsigned long long* __restrict__ best) {
+  const int t = blockIdx.y;
+  const size_t n = (size_t)T * vocab;
+  unsigned long long b = 0;
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < vocab; r += gridDim.x * blockDim.x) {
+    const float v = split_sum(part, nsplit, n, (size_t)t * vocab + r);
+    logits[(size_t)t * vocab + r] = v;
+    const unsigned long long pk = pack_argmax(v, r);
+    b = pk > b ? pk : b;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, b, o);
+    b = other > b ? other : b;
+  }
+  if ((threadIdx.x & 31) == 0 && b) atomicMax(best + t, b);
+}
+
+// next[t] = the index in best[t] (index 0 when nothing was packed).
+__global__ void bt_token_kernel(const unsigned long long* __restrict__ best, int T, int* __restrict__ next) {
+  const int t = threadIdx.x;
+  if (t < T) next[t] = best[t] == 0 ? 0 : unpack_argmax_index(best[t]);
+}
+
+}  // namespace ss

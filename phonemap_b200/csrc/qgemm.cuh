@@ -11,24 +11,30 @@
 // fp32 -- the reference's dequant-matvec (SlipStream/src/core/quantize.c:
 // 446-494) for each token, in another summation order.
 //
-// Numerics (the same as the batch-1 kernels, gemv.cuh): each token's 32-value
-// block is block fixed point -- m_j = round(x_j 2^(22-e)), 2^e > max |x| --
-// split into three signed byte planes (qplanes_kernel).  A block's weights
-// and planes meet in one integer tensor-core product per plane, exact in
-// int32; the planes are combined in fp32 and scaled by d * 2^(e-22).
+// Numerics.  The weights enter the tensor core exactly: Q4_0 values q - 8
+// and Q8_0 values q are small integers, exact in fp16.  Each token's input
+// vector (RMSNormed in the reference's rounding order where the layer has a
+// norm) is scaled by a power of two so its largest element lies in [1, 2) and
+// split into two fp16 pieces, hi = fp16(x) and lo = fp16(x - hi) -- 22 bits of
+// the fp32 value.  One block's dot products are then tensor-core products
+// with fp32 accumulation (both pieces into the same accumulator); each block's
+// result is scaled by its fp16 scale d in fp32 and summed over the blocks, and
+// the token's power of two is undone at the end.
 //
 // Tensor-core mapping (one CTA tile = 128 weight rows):
-//   A (M = 128 rows x K = 32): the block's weights as int8 -- Q4_0 nibbles
-//       unpacked to 16 (q - 8) (exact; the 1/16 joins the scale), Q8_0 bytes
-//       as they are -- written by the math warps into shared memory in the
-//       UMMA canonical K-major layout (8-row x 16-byte core matrices);
-//   B (N = 3 TP x K = 32): the block's activation planes, row p * TP + t for
-//       plane p of token t (TP = T rounded up to 16; padding rows zero),
-//       already in the canonical layout in global memory (qplanes_kernel);
-//   D (128 lanes x N columns of TMEM, int32): one tcgen05.mma per block, two
-//       TMEM buffers so block b's product runs while block b-1 is flushed.
+//   A (M = 128 rows x K = 32 per block): the block's weights as fp16, written
+//       by the math warps into shared memory in the UMMA canonical K-major
+//       layout (8-row x 16-byte core matrices);
+//   B (N = TP x K = 32, two pieces): the block's activation pieces, row t for
+//       token t (TP = T rounded up to 16; padding rows zero), already in the
+//       canonical layout in global memory (qg_pieces_kernel);
+//   D (128 lanes x TP columns of TMEM per block, fp32): four tcgen05.mma
+//       kind::f16 per block (two pieces x two K halves of 16).
+// A stage (KC blocks) is the unit of work of the math warps: they unpack its
+// blocks, one thread issues its 4 KC MMAs into one of two TMEM regions, and
+// while those run the warps flush the previous stage's region.
 // Weights arrive by TMA (cp.async.bulk.tensor, 128-byte swizzle, no
-// multicast) into a ring of stages of KC blocks x 128 rows, with the planes
+// multicast) into a ring of stages of KC blocks x 128 rows, with the pieces
 // of those blocks (cp.async.bulk) and the fp16 scales.
 //
 // Work: units of (128-row tile, contiguous range of K chunks); a unit's
@@ -44,11 +50,11 @@ namespace ss {
 
 constexpr int kQgRows = 128;        // weight rows per tile (UMMA M)
 constexpr int kQgMaxT = 32;         // tokens per product (N = 3 * 32 = 96 at most)
-constexpr int kQgStages = 4;        // ring stages
-constexpr int kQgMathWarps = 8;     // two warpgroups: each covers all 128 TMEM lanes
+constexpr int kQgStages = 3;        // ring stages
+constexpr int kQgMathWarps = 16;    // four warpgroups: each covers all 128 TMEM lanes
 constexpr int kQgThreads = 32 * (1 + kQgMathWarps);
-constexpr int kQgTmemCols = 256;    // two D buffers of up to 96 columns (power of two >= 192)
-constexpr int kQgABytes = kQgRows * 32;  // one block of A in the canonical layout
+constexpr int kQgABytes = kQgRows * 32 * 2;  // one block of A (fp16) in the canonical layout
+constexpr int kQgTmemCols = 512;    // D of two stages: 2 x KC blocks x TP (<= 32) columns
 
 // Blocks per stage: the TMA box's inner extent is 128 bytes (the 128-byte
 // swizzle span): 8 Q4_0 blocks of 16 quant bytes, 4 Q8_0 blocks of 32.
@@ -57,9 +63,9 @@ __host__ __device__ constexpr int qg_kc(int type) { return type == kQ4_0 ? 8 : 4
 struct QGemmParams {
   int rows, nb, type;
   int tiled;            // 1: tiled weight layout (4-row tiles), 0: row-interleaved
-  int T, TP;            // tokens; plane stride in the N dimension (T rounded up to 16)
-  const int8_t* xq;     // [nb][3 TP][32] planes, canonical K-major per block
-  const float* xc;      // [T][nb]: 2^(e-22), the value of one unit of plane 0
+  int T, TP;            // tokens; B rows per piece (T rounded up to 16)
+  const __half* xq;     // [nb][2 pieces][TP][32] activation pieces, canonical K-major per block
+  const float* post;    // [T]: the power of two each token's result is multiplied by
   float* out;           // [nsplit][T][rows] partial products
   int nsplit;           // K ranges per row tile
   int nchunks;          // nb / KC
@@ -68,17 +74,17 @@ struct QGemmParams {
   long long wait_budget;
 };
 
-// Shared memory: [stages][quants 16 KB | scales 2 KB | planes KC*N*32]
-// [A x 2][mbarriers][tmem address].
+// Shared memory: [stages][quants 16 KB | scales 2 KB | pieces KC*2*TP*64]
+// [A: KC blocks][mbarriers][tmem address].
 struct QgSmem {
   static constexpr int kQuant = 16384;   // 128 rows x 128 bytes
   static constexpr int kScale = 2048;    // 128 rows x KC (<= 8) fp16
-  __host__ __device__ static int plane_bytes(int type, int TP) { return qg_kc(type) * 3 * TP * 32; }
+  __host__ __device__ static int plane_bytes(int type, int TP) { return qg_kc(type) * 2 * TP * 64; }
   __host__ __device__ static int stage_bytes(int type, int TP) {
     return (kQuant + kScale + plane_bytes(type, TP) + 1023) / 1024 * 1024;
   }
   __host__ __device__ static int total(int type, int TP) {
-    return 1024 /* alignment slack */ + kQgStages * stage_bytes(type, TP) + 2 * kQgABytes + 256;
+    return 1024 /* alignment slack */ + kQgStages * stage_bytes(type, TP) + qg_kc(type) * kQgABytes + 256;
   }
 };
 
@@ -114,21 +120,45 @@ SS_DEVINL void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync
 // tensor core (async proxy).
 SS_DEVINL void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// D[tmem] (+)= A[smem] * B[smem]^T, kind::i8, one CTA.
-SS_DEVINL void umma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accum) {
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (fp16 operands, fp32
+// accumulator), one CTA; accum = 0 overwrites D.  Executed by a whole warp
+// with warp-uniform operands; one elected lane issues the MMA.
+SS_DEVINL void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accum) {
   asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
+      "{\n .reg .pred p, e;\n elect.sync _|e, 0xffffffff;\n setp.ne.b32 p, %4, 0;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accum), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
       : "memory");
 }
-// Arrives once on `bar` when every tcgen05 operation this thread issued before
-// it has completed (the MMA's shared-memory reads included).
+// Arrives once on `bar` when every tcgen05 operation the issuing lane issued
+// before it has completed (the MMA's shared-memory reads included).  Executed
+// by the whole issuing warp; the elected lane commits.
 SS_DEVINL void umma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+  asm volatile("{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+               " @e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n" ::"r"(bar)
                : "memory");
 }
-// 16 consecutive 32-bit TMEM columns of this thread's lane.
+// 4 / 8 / 16 consecutive 32-bit TMEM columns of this thread's lane.
+SS_DEVINL void tmem_ld4(uint32_t taddr, int* v) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+               : "r"(taddr)
+               : "memory");
+}
+SS_DEVINL void tmem_ld8p(uint32_t taddr, int* v) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                 "=r"(v[7])
+               : "r"(taddr)
+               : "memory");
+}
+SS_DEVINL void tmem_ld8(uint32_t taddr, int (&v)[16]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                 "=r"(v[7])
+               : "r"(taddr)
+               : "memory");
+}
 SS_DEVINL void tmem_ld16(uint32_t taddr, int (&v)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -140,23 +170,23 @@ SS_DEVINL void tmem_ld16(uint32_t taddr, int (&v)[16]) {
 }
 SS_DEVINL void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// Shared-memory matrix descriptor of a K-major operand without swizzle:
-// 8-row x 16-byte core matrices, the two 16-byte halves of K 128 bytes apart
-// (leading byte offset), 8-row groups 256 bytes apart (stride byte offset);
-// version 1 (sm_100).
+// Shared-memory matrix descriptor of a K-major fp16 operand without swizzle:
+// 8-row x 16-byte (8-element) core matrices, the K-adjacent core matrices 128
+// bytes apart (leading byte offset), 8-row groups 512 bytes apart (four core
+// matrices of K = 32: stride byte offset); version 1 (sm_100).  One MMA (K =
+// 16) spans two core matrices along K.
 SS_DEVINL uint64_t umma_desc_kmajor(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(256 >> 4) << 32) |
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(512 >> 4) << 32) |
          (1ull << 46);
 }
-// Instruction descriptor of kind::i8: D s32, A and B s8, both K-major, M x N.
-__host__ __device__ constexpr uint32_t umma_idesc_i8(int M, int N) {
-  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+// Instruction descriptor of kind::f16: D f32, A and B fp16, both K-major, M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
-
-// Exact int -> float for |v| < 2^22 (integer add + float add on the FMA
-// pipes instead of the conversion unit).
-SS_DEVINL float i2f_small(int v) {
-  return __int_as_float(v + 0x4B400000) - 12582912.0f;
+// Byte offset of element (row, k) of a block (K = 32 fp16) in the canonical
+// layout: [row / 8][k / 8][row % 8][k % 8].
+__host__ __device__ constexpr int qg_canon16(int row, int k) {
+  return (row >> 3) * 512 + (k >> 3) * 128 + (row & 7) * 16 + (k & 7) * 2;
 }
 
 // Wait on an mbarrier phase with a budget; false on expiry (error bit 4).
@@ -174,24 +204,57 @@ SS_DEVINL bool qg_wait(uint32_t bar, uint32_t parity, const QGemmParams& p) {
 
 // ---- activation planes -----------------------------------------------------
 
-// Per-token RMSNorm scale (cpu_neon.c:109-115): 1 / sqrtf(sum x^2 / n + eps).
-__global__ void __launch_bounds__(256) qg_rms_kernel(const float* __restrict__ x, int n, int ld, float eps,
-                                                     float* __restrict__ scale) {
-  __shared__ float red[32];
+// Per token (one CTA each, one pass): with a norm, the RMSNorm scale
+// 1 / sqrtf(sum x^2 / n + eps) (cpu_neon.c:109-115); and the power of two
+// 2^-e that brings the token's largest input element (after the norm: the
+// largest |x * w| times the positive scale) near [1, 2): pre[t] = 2^-e,
+// post[t] = 2^e (a zero vector gets 1 and 1).  The pieces only need |x'| well
+// inside the fp16 range, so the exponent of the unrounded product is enough.
+__global__ void __launch_bounds__(512) qg_scale_kernel(const float* __restrict__ x, int n, int ld,
+                                                       const float* __restrict__ norm_w, float eps,
+                                                       float* __restrict__ scale, float* __restrict__ pre,
+                                                       float* __restrict__ post) {
+  __shared__ float red[64];
   const float* xt = x + (size_t)blockIdx.x * ld;
-  float ss = 0.0f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xt[i], xt[i], ss);
-  ss = block_sum(ss, red);
-  if (threadIdx.x == 0) scale[blockIdx.x] = 1.0f / sqrtf(ss / (float)n + eps);
+  float ss = 0.0f, amax = 0.0f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = xt[i];
+    ss = fmaf(v, v, ss);
+    amax = fmaxf(amax, fabsf(norm_w ? v * norm_w[i] : v));
+  }
+  ss = warp_sum(ss);
+  amax = warp_max(amax);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (lane == 0) {
+    red[w] = ss;
+    red[32 + w] = amax;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.0f, m = 0.0f;
+    for (int i = 0; i < nw; i++) {
+      t += red[i];
+      m = fmaxf(m, red[32 + i]);
+    }
+    const float sc = norm_w ? 1.0f / sqrtf(t / (float)n + eps) : 1.0f;
+    m *= sc;
+    int e = m >= 1.17549435e-38f ? (int)((__float_as_uint(m) >> 23) & 255u) - 127 : 0;
+    e = max(-126, min(126, e));
+    scale[blockIdx.x] = sc;
+    pre[blockIdx.x] = pow2i(-e);
+    post[blockIdx.x] = pow2i(e);
+  }
 }
 
-// Block fixed point of token t's block b into B's canonical layout: one warp
-// per (token, block), lane j = element j.  With norm_w: x * scale[t] * w (the
-// reference's rounding order).  Tokens in [T, TP) write zero planes.
-__global__ void __launch_bounds__(256) qg_planes_kernel(const float* __restrict__ x, int ld, int nb,
+// Token t's block b as two fp16 pieces into B's canonical layout: one warp
+// per (token, block), lane j = element j.  x' = (x * scale * w) * pre (or
+// x * pre without a norm), hi = fp16(x'), lo = fp16(x' - hi).  Tokens in
+// [T, TP) write zeros.
+__global__ void __launch_bounds__(256) qg_pieces_kernel(const float* __restrict__ x, int ld, int nb,
                                                         const float* __restrict__ norm_w,
-                                                        const float* __restrict__ scale, int T, int TP,
-                                                        int8_t* __restrict__ xq, float* __restrict__ xc) {
+                                                        const float* __restrict__ scale,
+                                                        const float* __restrict__ pre, int T, int TP,
+                                                        __half* __restrict__ xq) {
   const int lane = threadIdx.x & 31;
   const int b = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int t = blockIdx.y;
@@ -200,24 +263,13 @@ __global__ void __launch_bounds__(256) qg_planes_kernel(const float* __restrict_
   if (t < T) {
     v = x[(size_t)t * ld + b * 32 + lane];
     if (norm_w) v = __fmul_rn(__fmul_rn(v, scale[t]), norm_w[b * 32 + lane]);
+    v = __fmul_rn(v, pre[t]);
   }
-  const float amax = warp_max(fabsf(v));
-  const bool live = amax >= 1e-30f;
-  const int e = (int)((__float_as_uint(amax) >> 23) & 255u) - 126;
-  const int m = live ? __float2int_rn(v * pow2i(22 - e)) : 0;
-  const int d0 = sext8(m);
-  const int m1 = (m - d0) >> 8;
-  const int d1 = sext8(m1);
-  const int d2 = (m1 - d1) >> 8;
-  const int N = 3 * TP;
-  int8_t* blk = xq + (size_t)b * N * 32;
-  const int dig[3] = {d0, d1, d2};
-#pragma unroll
-  for (int pl = 0; pl < 3; pl++) {
-    const int n = pl * TP + t;
-    blk[(n >> 3) * 256 + (lane >> 4) * 128 + (n & 7) * 16 + (lane & 15)] = (int8_t)dig[pl];
-  }
-  if (lane == 0 && t < T) xc[(size_t)t * nb + b] = live ? pow2i(e - 22) : 0.0f;
+  const __half hi = __float2half_rn(v);
+  const __half lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
+  uint8_t* blk = reinterpret_cast<uint8_t*>(xq) + (size_t)b * 2 * TP * 64;
+  *reinterpret_cast<__half*>(blk + qg_canon16(t, lane)) = hi;
+  *reinterpret_cast<__half*>(blk + TP * 64 + qg_canon16(t, lane)) = lo;
 }
 
 // ---- the product -----------------------------------------------------------
@@ -256,23 +308,58 @@ SS_DEVINL bool qg_any(bool pred) {  // barrier over the 256 math threads that OR
   return r != 0;
 }
 
-// Warp 0 (one lane) feeds the ring; warps 1..8 unpack A, issue the MMAs (one
-// thread) and flush D: warp w owns TMEM lanes 32 (w % 4) .. +31 (weight rows),
-// warpgroup g = (w - 1) / 4 the tokens 16 g .. 16 g + 15 of each row.
+// Two words of Q4_0 quant bytes (bytes 8 j .. 8 j + 7 of a block) -> the
+// fp16 values q - 8 of their low (hi = false) or high nibbles, in element
+// order as four fp16 pairs.  fp16 1024 + q is the bit pattern 0x6400 | q.
+SS_DEVINL void q4_to_f16x8(uint32_t w0, uint32_t w1, bool hi, uint32_t (&h)[4]) {
+  const __half2 off = __floats2half2_rn(1032.0f, 1032.0f);
+  const uint32_t w[2] = {hi ? w0 >> 4 : w0, hi ? w1 >> 4 : w1};
+#pragma unroll
+  for (int i = 0; i < 2; i++) {
+    uint32_t p01, p23;
+    asm("prmt.b32 %0, %1, %2, 0x4140;" : "=r"(p01) : "r"(w[i]), "r"(0u));  // bytes 0, 1 -> half lanes
+    asm("prmt.b32 %0, %1, %2, 0x4342;" : "=r"(p23) : "r"(w[i]), "r"(0u));  // bytes 2, 3
+    uint32_t a = (p01 & 0x000F000Fu) | 0x64006400u, c = (p23 & 0x000F000Fu) | 0x64006400u;
+    const __half2 ha = __hsub2(*reinterpret_cast<__half2*>(&a), off);
+    const __half2 hc = __hsub2(*reinterpret_cast<__half2*>(&c), off);
+    h[2 * i] = *reinterpret_cast<const uint32_t*>(&ha);
+    h[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&hc);
+  }
+}
+// Two words of Q8_0 quants -> fp16 q (1024 + (q + 128) - 1152).
+SS_DEVINL void q8_to_f16x8(uint32_t w0, uint32_t w1, uint32_t (&h)[4]) {
+  const __half2 off = __floats2half2_rn(1152.0f, 1152.0f);
+  const uint32_t w[2] = {w0 ^ 0x80808080u, w1 ^ 0x80808080u};
+#pragma unroll
+  for (int i = 0; i < 2; i++) {
+    uint32_t a, c;
+    asm("prmt.b32 %0, %1, %2, 0x4140;" : "=r"(a) : "r"(w[i]), "r"(0x64646464u));
+    asm("prmt.b32 %0, %1, %2, 0x4342;" : "=r"(c) : "r"(w[i]), "r"(0x64646464u));
+    const __half2 ha = __hsub2(*reinterpret_cast<__half2*>(&a), off);
+    const __half2 hc = __hsub2(*reinterpret_cast<__half2*>(&c), off);
+    h[2 * i] = *reinterpret_cast<const uint32_t*>(&ha);
+    h[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&hc);
+  }
+}
+
+// Warp 0 (one lane) feeds the ring; warps 1..16 unpack A, issue the MMAs
+// (one thread) and flush D: warp w owns TMEM lanes 32 (w % 4) .. +31 (weight
+// rows), warpgroup g = (w - 1) / 4 unpacks elements 8 g .. 8 g + 7 of each
+// block (one core matrix) and flushes tokens g TP/4 .. (g + 1) TP/4 - 1.
 template <int TYPE>
-__global__ void __launch_bounds__(kQgThreads, 1)
+__global__ void __maxnreg__(96)
     qgemm_kernel(const QGemmParams p, const __grid_constant__ CUtensorMap qmap,
                  const __grid_constant__ CUtensorMap smap) {
   constexpr int KC = qg_kc(TYPE);
   extern __shared__ uint8_t qg_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(qg_raw) + 1023) & ~(uintptr_t)1023);
-  const int N = 3 * p.TP;
-  const int SB = QgSmem::stage_bytes(TYPE, p.TP);
-  const int PB = QgSmem::plane_bytes(TYPE, p.TP);
-  uint8_t* abuf = smem + kQgStages * SB;                           // 2 x 4 KB, 1024-aligned
-  uint64_t* full = reinterpret_cast<uint64_t*>(abuf + 2 * kQgABytes);
+  const int TP = p.TP;
+  const int SB = QgSmem::stage_bytes(TYPE, TP);
+  const int PB = QgSmem::plane_bytes(TYPE, TP);
+  uint8_t* abuf = smem + kQgStages * SB;                           // KC x 8 KB
+  uint64_t* full = reinterpret_cast<uint64_t*>(abuf + KC * kQgABytes);
   uint64_t* empty = full + kQgStages;
-  uint64_t* dfull = empty + kQgStages;                             // [2]
+  uint64_t* dfull = empty + kQgStages;                             // [2]: MMAs of a stage done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dfull + 2);
   __shared__ int s_abort;
 
@@ -320,8 +407,8 @@ __global__ void __launch_bounds__(kQgThreads, 1)
           mbar_expect_tx(fb, tx);
           tma_load_3d(smem_addr(st), &qmap, c * KC * (TYPE == kQ4_0 ? 16 : 32), 0, 32 * tile, fb);
           tma_load_2d(smem_addr(st + QgSmem::kQuant), &smap, c * KC * 8, 32 * tile, fb);
-          bulk_g2s(smem_addr(st + QgSmem::kQuant + QgSmem::kScale), p.xq + (size_t)c * KC * N * 32,
-                   (uint32_t)PB, fb);
+          bulk_g2s(smem_addr(st + QgSmem::kQuant + QgSmem::kScale),
+                   reinterpret_cast<const uint8_t*>(p.xq) + (size_t)c * PB, (uint32_t)PB, fb);
         }
       }
       // drain: the copies of the last stages may still be landing
@@ -334,130 +421,131 @@ __global__ void __launch_bounds__(kQgThreads, 1)
   // ---------------- math warps
   const int q = warp & 3;                 // TMEM lane quadrant of this warp
   const int r = 32 * q + lane;            // weight row within the tile
-  const int g = (warp - 1) >> 2;          // warpgroup: token half
-  const bool flusher = 16 * g < p.TP;
-  const uint32_t idesc = umma_idesc_i8(kQgRows, N);
+  const int g = (warp - 1) >> 2;          // warpgroup 0..3
+  const int th = TP >> 2;                 // tokens flushed per warpgroup (4 or 8)
+  const uint32_t idesc = umma_idesc_f16(kQgRows, TP);
   const uint32_t t_lane = tmem + ((uint32_t)(32 * q) << 16);
-  const bool issuer = tid == 32;
-  float acc[16];
-  int it = 0;        // blocks issued by this CTA so far (all units)
-  int sc = 0;        // stages consumed
+  const bool issuer = warp == 1;   // the MMA-issuing warp (one elected lane issues)
+  float acc[8];
+  int sc = 0;        // stages consumed (= stages whose MMAs were issued) by this CTA
   bool bad = false;
-  // pending block (issued, not yet flushed)
-  int pend_it = -1, pend_stage = 0, pend_bl = 0, pend_b = 0;
-  bool pend_last_of_stage = false;
+  int pend = -1;     // stage whose MMAs were issued and not yet flushed (its sc)
+  int pend_slot = 0;
+  // this thread's quant bytes of a block: Q4_0 bytes 8 (g & 1) .. +7 (low
+  // nibbles for g < 2, high for g >= 2); Q8_0 bytes 8 g .. 8 g + 7
+  const int qchunk_off = TYPE == kQ4_0 ? 0 : (g >> 1);
+  const uint32_t qbyte = (uint32_t)(8 * (g & 1));
+  const uint64_t adesc0 = umma_desc_kmajor(smem_addr(abuf));
 
-  auto flush_pending = [&]() -> bool {
-    // wait for the MMA of block pend_it; read its D; scale and accumulate
-    const uint32_t db = (uint32_t)(pend_it & 1);
-    if (!qg_wait(smem_addr(dfull + db), (uint32_t)((pend_it >> 1) & 1), p)) return false;
-    tc_fence_after();
-    if (flusher) {
-      int v0[16], v1[16], v2[16];
-      const uint32_t col = t_lane + db * 128 + 16 * g;
-      tmem_ld16(col, v0);
-      tmem_ld16(col + p.TP, v1);
-      tmem_ld16(col + 2 * p.TP, v2);
-      tmem_ld_wait();
-      const uint8_t* sst = smem + pend_stage * SB + QgSmem::kQuant;
-      const uint16_t dh = *reinterpret_cast<const uint16_t*>(sst + (((r >> 2) * KC + pend_bl) * 4 + (r & 3)) * 2);
-      float d = half_bits_to_float(dh);
-      if (TYPE == kQ4_0) d *= 0.0625f;  // A held 16 (q - 8)
+  // Flushes the pending stage: its D region (sc & 1), the scales of its ring
+  // slot; then releases the slot to the producer.
+  auto flush_stage = [&]() {
+    const uint32_t region = (uint32_t)((pend & 1) * KC * TP);
+    const uint8_t* sst = smem + pend_slot * SB + QgSmem::kQuant;
 #pragma unroll
-      for (int i = 0; i < 16; i++) {
-        const int t = 16 * g + i;
-        if (t < p.T) {
-          const float cx = __ldg(p.xc + (size_t)t * p.nb + pend_b);
-          const float v = fmaf(i2f_small(v2[i]), 65536.0f, fmaf(i2f_small(v1[i]), 256.0f, i2f_small(v0[i])));
-          acc[i] = fmaf(v, d * cx, acc[i]);
-        }
+    for (int b0 = 0; b0 < KC; b0 += 4) {  // four blocks' loads in flight per wait
+      int v[4][8];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const uint32_t col = t_lane + region + (uint32_t)((b0 + j) * TP + g * th);
+        if (th == 8) tmem_ld8p(col, v[j]);
+        else tmem_ld4(col, v[j]);
+      }
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float d = half_bits_to_float(
+            *reinterpret_cast<const uint16_t*>(sst + (((r >> 2) * KC + b0 + j) * 4 + (r & 3)) * 2));
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+          if (i < th) acc[i] = fmaf(__int_as_float(v[j][i]), d, acc[i]);
       }
     }
     tc_fence_before();
-    if (pend_last_of_stage) {
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(empty + pend_stage));
-    }
-    pend_it = -1;
-    return true;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_addr(empty + pend_slot));
+    pend = -1;
   };
 
   for (int u = blockIdx.x; u < nunits && !bad; u += gridDim.x) {
     int tile, split, c0, c1;
     qg_unit(p, u, tile, split, c0, c1);
 #pragma unroll
-    for (int i = 0; i < 16; i++) acc[i] = 0.0f;
-    for (int c = c0; c < c1 && !bad; c++, sc++) {
+    for (int i = 0; i < 8; i++) acc[i] = 0.0f;
+    for (int c = c0; c < c1; c++, sc++) {
       const int s = sc % kQgStages;
       bool ok = qg_wait(smem_addr(full + s), (uint32_t)((sc / kQgStages) & 1), p);
+      // A is free once the previous stage's MMAs are done (D also readable)
+      if (ok && pend >= 0) ok = qg_wait(smem_addr(dfull + (pend & 1)), (uint32_t)((pend >> 1) & 1), p);
+      tc_fence_after();
       uint8_t* st = smem + s * SB;
-      const uint32_t qbase = smem_addr(st);
-      for (int bl = 0; bl < KC; bl++, it++) {
-        // unpack block bl of the stage into A[it & 1] (canonical K-major)
-        const uint32_t a = smem_addr(abuf + (it & 1) * kQgABytes) + (uint32_t)((r >> 3) * 256 + (r & 7) * 16);
-        if (ok) {
-          if constexpr (TYPE == kQ4_0) {
-            uint32_t w0, w1;
-            asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];"
-                         : "=r"(w0), "=r"(w1)
-                         : "r"(qbase + r * 128 + ((bl ^ (r & 7)) << 4) + 8 * g));
-            const uint32_t l0 = ((w0 << 4) & 0xF0F0F0F0u) ^ 0x80808080u, l1 = ((w1 << 4) & 0xF0F0F0F0u) ^ 0x80808080u;
-            const uint32_t h0 = (w0 & 0xF0F0F0F0u) ^ 0x80808080u, h1 = (w1 & 0xF0F0F0F0u) ^ 0x80808080u;
-            asm volatile("st.shared.v2.u32 [%0], {%1,%2};" ::"r"(a + 8 * g), "r"(l0), "r"(l1) : "memory");
-            asm volatile("st.shared.v2.u32 [%0], {%1,%2};" ::"r"(a + 128 + 8 * g), "r"(h0), "r"(h1) : "memory");
-          } else {
-            uint32_t w[4];
-            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                         : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
-                         : "r"(qbase + r * 128 + (((2 * bl + g) ^ (r & 7)) << 4)));
-            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a + 128 * g), "r"(w[0]), "r"(w[1]),
-                         "r"(w[2]), "r"(w[3])
-                         : "memory");
-          }
+      const uint32_t qrow = smem_addr(st) + (uint32_t)(r * 128);
+      if (ok) {
+        uint32_t w[KC][2];
+#pragma unroll
+        for (int bl = 0; bl < KC; bl++) {
+          const int chunk = TYPE == kQ4_0 ? bl : 2 * bl + qchunk_off;
+          asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];"
+                       : "=r"(w[bl][0]), "=r"(w[bl][1])
+                       : "r"(qrow + ((chunk ^ (r & 7)) << 4) + qbyte));
         }
-        fence_proxy_async_smem();
-        tc_fence_before();
-        bad = qg_any(!ok);  // every math thread has written its part of A
-        tc_fence_after();
-        if (bad) break;
-        if (issuer) {
-          const uint64_t adesc = umma_desc_kmajor(smem_addr(abuf + (it & 1) * kQgABytes));
-          const uint64_t bdesc =
-              umma_desc_kmajor(smem_addr(st + QgSmem::kQuant + QgSmem::kScale + bl * N * 32));
-          umma_i8(tmem + (uint32_t)((it & 1) * 128), adesc, bdesc, idesc, 0u);
-          umma_commit(smem_addr(dfull + (it & 1)));
+#pragma unroll
+        for (int bl = 0; bl < KC; bl++) {
+          uint32_t h[4];
+          if constexpr (TYPE == kQ4_0) q4_to_f16x8(w[bl][0], w[bl][1], g >= 2, h);
+          else q8_to_f16x8(w[bl][0], w[bl][1], h);
+          const uint32_t a = smem_addr(abuf + bl * kQgABytes) + (uint32_t)qg_canon16(r, 8 * g);
+          asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(h[0]), "r"(h[1]), "r"(h[2]),
+                       "r"(h[3])
+                       : "memory");
         }
-        if (pend_it >= 0) ok = flush_pending();
-        pend_it = it;
-        pend_stage = s;
-        pend_bl = bl;
-        pend_b = c * KC + bl;
-        pend_last_of_stage = bl == KC - 1;
       }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      bad = qg_any(!ok);  // every math thread has written its part of A
+      tc_fence_after();
+      if (bad) break;
+      if (issuer) {
+        const uint32_t dt = tmem + (uint32_t)((sc & 1) * KC * TP);
+        const uint64_t bdesc0 = umma_desc_kmajor(smem_addr(st + QgSmem::kQuant + QgSmem::kScale));
+        // descriptor start addresses advance in 16-byte units
+#pragma unroll
+        for (int bl = 0; bl < KC; bl++)
+#pragma unroll
+          for (int pc = 0; pc < 2; pc++)      // fp16 pieces hi, lo
+#pragma unroll
+            for (int kh = 0; kh < 2; kh++)    // K halves of 16
+              umma_f16(dt + (uint32_t)(bl * TP), adesc0 + (uint64_t)((bl * kQgABytes + 256 * kh) >> 4),
+                       bdesc0 + (uint64_t)((bl * 2 * TP * 64 + pc * TP * 64 + 256 * kh) >> 4), idesc,
+                       (pc | kh) ? 1u : 0u);
+        umma_commit(smem_addr(dfull + (sc & 1)));
+      }
+      // the previous stage, while this stage's MMAs run
+      if (pend >= 0) flush_stage();
+      pend = sc;
+      pend_slot = s;
     }
     if (bad) break;
-    // the unit's last block, then its partial sums
-    const bool ok = flush_pending();
+    // the unit's last stage, then its partial sums
+    bool ok = qg_wait(smem_addr(dfull + (pend & 1)), (uint32_t)((pend >> 1) & 1), p);
     bad = qg_any(!ok);
     if (bad) break;
-    if (flusher) {
-      const int row = tile * kQgRows + r;
-      if (row < p.rows) {
+    tc_fence_after();
+    flush_stage();
+    const int row = tile * kQgRows + r;
+    if (row < p.rows) {
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-          const int t = 16 * g + i;
-          if (t < p.T) p.out[((size_t)split * p.T + t) * p.rows + row] = acc[i];
-        }
+      for (int i = 0; i < 8; i++) {
+        const int t = g * th + i;
+        if (i < th && t < p.T) p.out[((size_t)split * p.T + t) * p.rows + row] = acc[i] * p.post[t];
       }
     }
   }
-  if (bad) {
-    if (tid == 32) {
-      s_abort = 1;
-      // no MMA may still write TMEM when it is freed
-      if (pend_it >= 0)
-        mbar_wait_bounded(smem_addr(dfull + (pend_it & 1)), (uint32_t)((pend_it >> 1) & 1), p.wait_budget);
-    }
+  if (bad && tid == 32) {
+    s_abort = 1;
+    // no MMA may still write TMEM when it is freed: wait for the last commit
+    if (pend >= 0)
+      mbar_wait_bounded(smem_addr(dfull + (pend & 1)), (uint32_t)((pend >> 1) & 1), p.wait_budget);
   }
   tc_fence_before();
   named_bar_sync(1, 32 * kQgMathWarps);

@@ -1240,6 +1240,7 @@ Context* create(const uint8_t* base, uint64_t size, const ss_cuda_options_t* o) 
   c->tuning = read_tuning();
   c->mega = !(opts.flags & SS_CUDA_FLAG_MULTI_KERNEL) && !getenv("SS_CUDA_MULTI_KERNEL");
   c->trace = (opts.flags & SS_CUDA_FLAG_TRACE) != 0;
+  c->flags = opts.flags;
   c->tp_size = opts.tp_size > 1 ? opts.tp_size : 1;
   c->tp_rank = c->tp_size > 1 ? opts.tp_rank : 0;
   c->hbm_budget = opts.hbm_budget_bytes;
@@ -1374,6 +1375,7 @@ bool op_matvec(ss_cuda_ctx_t* ctx, float* out, const void* mat, const float* vec
 }
 
 #include "qgemm_host.inc"
+#include "batch_host.inc"
 
 // A quantized weight tensor by GGUF name: its device matrix and where its rows
 // sit there (row r of the tensor is matrix row r * mul + add).
@@ -1706,9 +1708,16 @@ SS_API int ss_cuda_prefill(ss_cuda_ctx_t* ctx, const int32_t* tokens, int32_t n,
   const int rc = guard([&] {
     Context* c = need_model(ctx);
     if (!tokens || n <= 0) fail(SS_CUDA_ERROR_INVALID_PARAMS, "empty prompt");
+    if (c->cancelled.load()) fail(SS_CUDA_ERROR_CANCELLED, "cancelled");
     put_tokens(c, tokens, n, start_pos);
-    set_position(c, start_pos, start_pos + n);
-    run_steps(c, n);
+    if (bt_eligible(c)) {
+      // the whole prompt through the tensor-core product, 32 tokens per pass
+      bt_prefill(c, tokens, n, start_pos);
+    } else {
+      // the decode step replayed once per prompt token
+      set_position(c, start_pos, start_pos + n);
+      run_steps(c, n);
+    }
     read_logits(c, logits_out ? logits_out : nullptr);
     tok = c->h_small[16];
   });

@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "batch_kernels.cuh"
 #include "gemv.cuh"
 #include "gguf_view.h"
 #include "misc_kernels.cuh"
@@ -81,13 +82,24 @@ struct Context {
   // many-token tensor-core product (qgemm.cuh): tensor maps per weight
   // matrix, activation planes, partial sums
   std::unordered_map<const void*, QgMaps> qg_maps;
-  int8_t* qg_xq = nullptr;
+  __half* qg_xq = nullptr;
   size_t qg_xq_bytes = 0;
-  float* qg_xc = nullptr;
-  size_t qg_xc_floats = 0;
   float* qg_scale = nullptr;
   float* qg_out = nullptr;
   size_t qg_out_floats = 0;
+  // the many-token step (batch_kernels.cuh): hidden states, q, attention
+  // output, SwiGLU activations, logits of up to 32 tokens; token metadata
+  uint32_t flags = 0;
+  float* bt_h = nullptr;
+  float* bt_q = nullptr;
+  float* bt_att = nullptr;
+  float* bt_act = nullptr;
+  float* bt_logits = nullptr;
+  int* bt_meta = nullptr;       // [4][32]: token, position, sequence, greedy token
+  int* bt_meta_host = nullptr;  // pinned staging
+  float* bt_kv = nullptr;       // [32][2 kvd]: k | v of each token before encoding
+  unsigned* bt_amax = nullptr;  // [32][2]: largest |k|, |v| (float bits)
+  unsigned long long* bt_best = nullptr;  // [32]: packed greedy choice
   GemvTuning tuning;
   std::atomic<bool> cancelled{false};
 

@@ -58,6 +58,7 @@ FLAG_NO_PDL = 1
 FLAG_NO_GRAPH = 2
 FLAG_MULTI_KERNEL = 4
 FLAG_TRACE = 8
+FLAG_STEP_PREFILL = 16
 
 _lib = None
 

@@ -309,3 +309,38 @@ def test_bounded_wait_expires_then_reset_recovers(phase_of):
         first = m.prefill(prompt, 0)
         ids = [first] + m.decode_greedy(first, len(prompt), 7)
         assert ids == ref[:8]
+
+
+@pytest.mark.parametrize("name", ["tiny", "tiny-mha", "tiny-q8", "tinyllama"])
+def test_batched_prefill_matches_replay(name):
+    """The prompt through the many-token tensor-core step (32 tokens per pass)
+    against the decode step replayed per token (SS_CUDA_FLAG_STEP_PREFILL, the
+    reference's order): last-token logits within the configuration's
+    tolerance, the int8 K/V rows of every prompt position within one step,
+    and the same greedy continuation."""
+    g = load_golden(name)
+    cfg = configs.get(name)
+    path = synth.ensure_gguf(cfg)
+    prompt = [int(t) for t in g["prompt"]]
+    # a prompt longer than one pass where the context allows it
+    long_prompt = (prompt * 40)[:min(70, cfg.ctx - 10)]
+    tol = logit_tol(name)
+    with runtime.CudaModel(path, cfg.ctx) as a, \
+            runtime.CudaModel(path, cfg.ctx, flags=runtime.FLAG_STEP_PREFILL) as b:
+        for pr in (prompt, long_prompt):
+            a.reset()
+            b.reset()
+            la = np.empty(a.vocab, np.float32)
+            lb = np.empty(b.vocab, np.float32)
+            ta = a.prefill(pr, 0, logits=la)
+            tb = b.prefill(pr, 0, logits=lb)
+            assert rel_err(la, lb) < tol
+            for pos in (0, len(pr) // 2, len(pr) - 1):
+                for layer in (0, cfg.n_layers - 1):
+                    ka, va, ksa, vsa = a.kv_row(layer, pos)
+                    kb, vb, ksb, vsb = b.kv_row(layer, pos)
+                    assert np.abs(ka.astype(int) - kb).max() <= 1
+                    assert np.abs(va.astype(int) - vb).max() <= 1
+                    np.testing.assert_allclose([ksa, vsa], [ksb, vsb], rtol=1e-3)
+            if ta == tb:
+                assert a.decode_greedy(ta, len(pr), 6) == b.decode_greedy(tb, len(pr), 6)
