@@ -52,7 +52,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile-kernel", default=None,
-                    choices=["qkv", "attention", "o", "gate_up", "down", "lm_head", "step"],
+                    choices=["qkv", "attention", "o", "gate_up", "down", "lm_head", "step",
+                             "product_gate_up"],
                     help="time one step kernel in isolation instead of the decode loop "
                          "(qkv..lm_head need --multi-kernel; step = one whole decode step)")
     ap.add_argument("--multi-kernel", action="store_true",
@@ -63,6 +64,9 @@ def parse_args():
                          "default 4 for llama2-13b (its configuration), else all resident")
     ap.add_argument("--replicas", action="store_true",
                     help="with --gpus N: N independent replicas instead of one tensor-parallel group")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="sequences decoded together per GPU (the many-token tensor-core step; "
+                         "with --gpus N, N independent replicas of B sequences)")
     return ap.parse_args()
 
 
@@ -156,10 +160,13 @@ class ClockSampler:
                 "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(inside)}
 
 
-def cpu_reference_run(cfg, path, n_max, budget_s=20.0):
+def cpu_reference_run(cfg, path, n_max, budget_s=20.0, start_pos=0):
     """Times the reference CPU path (oracle/_ref) -- or the C restatement when
     the reference build is absent -- on the host cores: one warm-up token at
-    position 0, then up to n_max tokens (bounded to ~budget_s) at positions 1..
+    start_pos, then up to n_max tokens (bounded to ~budget_s) at the positions
+    after it -- the positions the GPU loop is timed at, so each step attends
+    over as many cache rows (a step's cost does not depend on the rows'
+    contents, so no prompt is ingested first).
     Returns (tokens/s, cores, kind, sample description)."""
     import numpy as np
 
@@ -171,17 +178,18 @@ def cpu_reference_run(cfg, path, n_max, budget_s=20.0):
         model, kind = oracle.OracleModel(path, cfg.ctx), "port"
     tok = synth_prompt(cfg)[0]
     t = time.perf_counter()
-    logits = model.forward(tok, 0)
+    logits = model.forward(tok, start_pos)
     t_warm = time.perf_counter() - t
-    n = int(max(2, min(n_max, budget_s / max(t_warm, 1e-3))))
+    n = int(max(2, min(n_max, budget_s / max(t_warm, 1e-3), cfg.ctx - start_pos - 1)))
     t = time.perf_counter()
     for i in range(n):
         tok = int(np.argmax(logits))
-        logits = model.forward(tok, 1 + i)
+        logits = model.forward(tok, start_pos + 1 + i)
     dt = time.perf_counter() - t
     model.close()
-    sample = (f"{n} greedy decode tokens at positions 1..{n} (after 1 warm-up token at "
-              f"position 0, no prompt prefill) of the same GGUF, {cores} OpenMP threads, "
+    sample = (f"{n} greedy decode tokens at positions {start_pos + 1}..{start_pos + n} (after 1 "
+              f"warm-up token at position {start_pos}; the cache rows before it attended over "
+              f"as at those positions) of the same GGUF, {cores} OpenMP threads, "
               f"{'reference C code built from the PhoneMap sources' if kind == 'reference' else 'C restatement of the reference'}")
     return n / dt, cores, kind, sample
 
@@ -253,6 +261,18 @@ def workload(cfg, args, persistent=True):
     }
 
 
+def batch_workload(cfg, args, world):
+    P, W, K, B = cfg.prompt, args.warmup, args.steps, args.batch
+    return {
+        "workload": (f"{cfg.name}-shaped llama decoder, {'Q4_0' if cfg.wtype == 2 else 'Q8_0'} "
+                     f"weights, {B} sequences decoded together (greedy) after {P}-token prompts each"),
+        "batch": B, "prompt_tokens": P, "ctx": cfg.ctx,
+        "decode_positions": [P + W, P + W + K - 1],
+        "l2": "inputs larger than L2 (weights streamed per step exceed the 126 MB L2)",
+        "parallelism": "single GPU" if world <= 1 else f"dp{world} (independent replicas)",
+    }
+
+
 def budget_layers_of(cfg, args):
     """HBM budget for the layers' weights, in layers (0: all resident)."""
     if args.hbm_budget_layers is not None:
@@ -268,13 +288,17 @@ def run_reference(args):
     cfg = configs.get(args.config)
     path = synth.ensure_gguf(cfg)
     n_max = max(1, args.steps)
-    value, cores, kind, sample = cpu_reference_run(cfg, path, n_max, budget_s=90.0)
+    B = max(1, args.batch)
+    value, cores, kind, sample = cpu_reference_run(cfg, path, n_max, budget_s=90.0,
+                                                   start_pos=cfg.prompt + args.warmup)
+    if B > 1:  # the reference decodes one sequence at a time: B sequences cost B times one
+        sample += f"; the reference has no batched decode, so {B} sequences take {B} times as long"
     line = {
-        "metric": "decode tokens/s (batch 1)", "value": round(value, 4), "unit": "tokens/s",
+        "metric": f"decode tokens/s (batch {B})", "value": round(value, 4), "unit": "tokens/s",
         "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1000.0 / value, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init GGUF)",
-        "config": workload(cfg, args),
+        "config": batch_workload(cfg, args, args.gpus) if B > 1 else workload(cfg, args),
         "cpu_baseline": {"value": round(value, 4), "unit": "tokens/s", "cores": cores,
                          "kind": kind, "sample": sample},
         "e2e": {"value": round(value, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -444,9 +468,139 @@ def run_ours(args):
             "first_ids": ids[:8],
         }
         if world == 1 and not args.no_cpu_baseline:
-            v, cores, kind, sample = cpu_reference_run(cfg, path, K)
+            v, cores, kind, sample = cpu_reference_run(cfg, path, K, start_pos=P + W)
             line["cpu_baseline"] = {"value": round(v, 4), "unit": "tokens/s", "cores": cores,
                                     "kind": kind, "sample": sample}
+        print(json.dumps(line), flush=True)
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+def run_ours_batch(args):
+    """B sequences decoded together on each GPU through the many-token step
+    (one pass of the tensor-core product per layer matrix for all B tokens).
+    value: device-resident greedy loop (ss_cuda_decode_greedy_batch: tokens fed
+    back on the device), B * steps / CUDA-event time; e2e: ss_cuda_forward with
+    n_seq = B from host buffers, logits [B][vocab] and greedy tokens back every
+    step.  With --gpus N each rank runs an independent replica (weak scaling)."""
+    world, rank, local, pg = dist_setup(args)
+    import numpy as np
+    import torch
+
+    from phonemap_b200 import configs, runtime, synth
+    cfg = configs.get(args.config)
+    B = args.batch
+    if rank == 0:
+        synth.ensure_gguf(cfg)
+    if pg:
+        pg.barrier()
+    path = synth.ensure_gguf(cfg)
+    torch.cuda.set_device(local)
+    m = runtime.CudaModel(path, cfg.ctx, device=local, max_batch=B)
+    P, W, K = cfg.prompt, args.warmup, args.steps
+    if P + W + K + 1 > cfg.ctx:
+        raise SystemExit("prompt + warmup + steps exceed the context")
+    rng = np.random.default_rng(7)
+    prompts = rng.integers(0, cfg.vocab, size=(B, P)).astype(np.int32)
+    prompts[0] = np.asarray(synth.prompt_tokens(cfg), np.int32)[:P]
+    stream = torch.cuda.ExternalStream(m.stream(), device=torch.device("cuda", local))
+
+    t0 = time.perf_counter()
+    first = m.prefill_batch(prompts, 0)
+    prefill_s = time.perf_counter() - t0
+    warm = m.decode_greedy_batch(first, P, W)
+    sampler = ClockSampler(local)
+    with sampler:
+        time.sleep(0.05)
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        t_w0 = time.perf_counter()
+        ev0.record(stream)
+        ids = m.decode_greedy_batch(warm[-1], P + W, K)
+        ev1.record(stream)
+        ev1.synchronize()
+        t_w1 = time.perf_counter()
+        sampler.window = (t_w0, t_w1)
+        time.sleep(0.02)
+    ms = ev0.elapsed_time(ev1)
+    ms = max_over_ranks(pg, ms)
+    ms_per_step = ms / K
+    value = world * B * K / (ms / 1000.0)
+    stats = m.stats()
+
+    e2e = None
+    if not args.no_e2e:
+        m.reset()
+        logits = np.empty((B, m.vocab), np.float32)
+        toks = m.prefill_batch(prompts, 0)
+        pos = P
+        for _ in range(W):
+            toks = m.forward_batch(toks, pos, logits=logits)
+            pos += 1
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(K):
+            toks = m.forward_batch(toks, pos, logits=logits)
+            pos += 1
+        dt = max_over_ranks(pg, time.perf_counter() - t0)
+        e2e = {"value": round(world * B * K / dt, 2), "unit": "tokens/s",
+               "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B * m.vocab + 4 * B,
+               "api": "ss_cuda_forward with n_seq = B (host tokens in, host logits [B][vocab] + "
+                      "greedy tokens out, synchronous)"}
+
+    # roofline: the tensor-core gate/up product at B tokens (the kernel alone,
+    # cycling the layers so the weights stream from HBM); algorithmic bytes =
+    # the matrix's GGUF bytes (weights + fp16 scales) + the activation pieces
+    # (B x ff... fp16 hi/lo of d columns) + the fp32 outputs
+    peak, peak_kind = hbm_peak()
+    k_ms = m.time_kernel("product_gate_up", 3 * cfg.n_layers)
+    bpw = 18 / 32 if cfg.wtype == 2 else 34 / 32
+    k_bytes = 2 * cfg.ffn * cfg.d_model * bpw + B * cfg.d_model * 4 + B * 2 * cfg.ffn * 4
+    achieved = k_bytes / (k_ms / 1000.0) / 1e9
+    traffic = read_profile_traffic("qgemm", f"{cfg.name}-b{B}")
+    # one step streams the weights once and each sequence's K/V rows (plus the
+    # other sequences' embedding rows)
+    avg = P + W + (K - 1) / 2.0
+    kv_seq = cfg.n_layers * 2 * (cfg.kv_dim + 4) * (avg + 2)
+    step_bytes = cfg.token_bytes(avg) + (B - 1) * (kv_seq + cfg.d_model * 4)
+    step_gbs = step_bytes / (ms_per_step / 1000.0) / 1e9
+    m.close()
+    if rank == 0:
+        line = {
+            "metric": f"decode tokens/s (batch {B})", "value": round(value, 2), "unit": "tokens/s",
+            "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random-init GGUF, N(0,0.02) quantized; seeded prompts)",
+            "config": batch_workload(cfg, args, world),
+            "roofline": {"bound": "hbm", "kernel": "qgemm_kernel (gate/up, tcgen05 kind::f16, "
+                                                   f"{B} tokens)",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                         "bytes_per_launch": int(k_bytes), "ms_per_launch": round(k_ms, 5),
+                         "traffic": traffic},
+            "step_roofline": {"bytes_per_step": int(step_bytes), "achieved": round(step_gbs, 1),
+                              "frac": round(step_gbs / peak, 4), "unit": "GB/s", "peak": peak,
+                              "peak_source": peak_kind},
+            "e2e": e2e,
+            "gpu_launches": int((stats["kernels_per_step"] if not stats["persistent"] else
+                                 1 + 18 * cfg.n_layers + 5 + 1) * K),
+            "clocks": sampler.summary(),
+            "step_impl": "many-token step: tensor-core product per matrix (CUDA graph per batch shape)",
+            "prefill_s": round(prefill_s, 3),
+            "first_ids": [int(v) for v in ids[:4, 0]],
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            v, cores, kind, sample = cpu_reference_run(cfg, path, K, start_pos=P + W)
+            line["cpu_baseline"] = {"value": round(v, 4), "unit": "tokens/s", "cores": cores,
+                                    "kind": kind, "sample": sample + "; the reference decodes one "
+                                    "sequence at a time, so B sequences take B times as long"}
         print(json.dumps(line), flush=True)
     if pg:
         pg.barrier()
@@ -484,7 +638,9 @@ def run_profile_kernel(args):
     path = synth.ensure_gguf(cfg)
     per_kernel = args.profile_kernel != "step"
     flags = runtime.FLAG_MULTI_KERNEL if (per_kernel or args.multi_kernel) else 0
-    m = runtime.CudaModel(path, cfg.ctx, device=0, flags=flags)
+    if args.profile_kernel == "product_gate_up":
+        flags = 0
+    m = runtime.CudaModel(path, cfg.ctx, device=0, flags=flags, max_batch=max(1, args.batch))
     if args.profile_kernel in ("attention", "step"):  # give it cached positions to attend over
         m.prefill(synth.prompt_tokens(cfg), 0)
     ms = m.time_kernel(args.profile_kernel, args.steps)
@@ -505,6 +661,8 @@ def main():
         return run_profile_kernel(args)
     if args.impl == "reference":
         return run_reference(args)
+    if args.batch > 1:
+        return run_ours_batch(args)
     return run_ours(args)
 
 

@@ -52,7 +52,11 @@ typedef struct {
     uint32_t struct_size;      /* sizeof(ss_cuda_options_t) */
     int32_t device;            /* CUDA ordinal; -1 = $SS_CUDA_DEVICE or 0 */
     uint32_t context_size;     /* positions (0 = GGUF context_length), capped at 8192 as engine.c:103-106 */
-    uint32_t max_batch;        /* sequences decoded together (>= 1) */
+    /* Sequences decoded together (1..32; 0 = 1).  Above 1 each sequence has its
+     * own KV cache (sequence 0's is the single-sequence one), the matrices take
+     * the tiled layout the tensor-core product reads, and ss_cuda_forward /
+     * ss_cuda_prefill_batch accept n_seq > 1; one GPU, no layer streaming. */
+    uint32_t max_batch;
     /* Bytes of HBM for the layers' weights; 0 = every layer resident.  When the
      * layers need more, layers past the first (budget / layer bytes - 3) stay in
      * host memory and are copied into two HBM slots every step (layer
@@ -128,14 +132,16 @@ int ss_cuda_stats(const ss_cuda_ctx_t *ctx, int64_t *out, int32_t n);
  * launches (no programmatic overlap) of one kernel of the decode step --
  * which = 0 QKV GEMV, 1 attention, 2 O GEMV, 3 gate/up GEMV, 4 down GEMV,
  * 5 lm_head GEMV -- cycling through the layers so weights stream from HBM --
- * or 6 the whole decode step (steps at the current position onwards), and
- * writes the average milliseconds per launch.  0..5 exist only in the
- * multi-kernel step.  Clobbers the activations and the K/V rows it passes
+ * or 6 the whole decode step (steps at the current position onwards), or 7
+ * the tensor-core gate/up product of max_batch tokens (the kernel alone, its
+ * activation pieces built once before), and writes the average milliseconds
+ * per launch.  0..5 exist only in the multi-kernel step, 7 only where the
+ * matrices are in the tiled layout.  Clobbers the activations and the K/V rows it passes
  * over; call ss_cuda_reset before decoding again. */
 int ss_cuda_time_kernel(ss_cuda_ctx_t *ctx, int32_t which, int32_t iters, float *ms_per_launch);
 /* Device bytes of the weights one launch of kernel `which` streams (layer 0;
  * repacked layout, i.e. the GGUF bytes plus row padding; 6: every weight
- * matrix of the step); -1 if not a GEMV. */
+ * matrix of the step; 7: the gate/up matrix); -1 if not a GEMV. */
 int64_t ss_cuda_kernel_bytes(const ss_cuda_ctx_t *ctx, int32_t which);
 
 /* Measurement aid, no reference counterpart: the timeline of the last
@@ -173,17 +179,46 @@ float *ss_cuda_scheduler_forward(ss_cuda_ctx_t *ctx, int32_t token_id, int32_t p
 float *ss_cuda_scheduler_prefill(ss_cuda_ctx_t *ctx, const int32_t *tokens, int32_t n,
                                  int32_t start_pos);
 void ss_cuda_scheduler_reset(ss_cuda_ctx_t *ctx);
+/* ss_scheduler_embed (layer_scheduler.c:805-915): the tokens at positions
+ * 0..n-1 (sequence 0's cache rows overwritten), every token's final hidden
+ * state RMSNormed with output_norm, mean-pooled and L2-normalised; returns a
+ * malloc'd float[hidden] the caller frees, as the reference's does (engine.c
+ * ss_embed hands it out), or NULL on error (ss_cuda_last_error). */
+float *ss_cuda_scheduler_embed(ss_cuda_ctx_t *ctx, const int32_t *tokens, int32_t n);
 
 /* ---- coarse entry points (activations and tokens stay on the device) ----
- * One decode step for the sequence at `pos`: token_ids[0] in, optional logits
- * out (host, vocab floats) and greedy argmax out (host, lowest index wins ties
- * as ss_argmax, SlipStream/src/core/tensor.c:318-328). */
+ * One decode step at `pos` (ss_scheduler_forward, layer_scheduler.c:571-679):
+ * n_seq = 1 runs sequence 0 with token_ids[0]; optional logits out (host,
+ * vocab floats) and greedy argmax out (host, lowest index wins ties as
+ * ss_argmax, SlipStream/src/core/tensor.c:318-328).  n_seq > 1 (up to the
+ * context's max_batch) steps sequences 0..n_seq-1 together, token_ids[s] at
+ * position pos of sequence s, through one pass of the tensor-core product:
+ * logits_out [n_seq][vocab] (nullable), argmax_out [n_seq] (nullable); the
+ * single-sequence decode state (ss_cuda_decode_*) is left unchanged. */
 int ss_cuda_forward(ss_cuda_ctx_t *ctx, const int32_t *token_ids, int32_t n_seq, int32_t pos,
                     float *logits_out, int32_t *argmax_out);
+/* The prompts of sequences 0..n_seq-1 (tokens [n_seq][n], all at positions
+ * start_pos..start_pos+n-1), each as ss_cuda_prefill ingests one: the last
+ * token's logits to logits_out [n_seq][vocab] (nullable), its greedy token to
+ * argmax_out [n_seq] (nullable).  Sequence 0 then continues with
+ * ss_cuda_decode_* as after ss_cuda_prefill.  Needs max_batch >= n_seq. */
+int ss_cuda_prefill_batch(ss_cuda_ctx_t *ctx, const int32_t *tokens, int32_t n_seq, int32_t n,
+                          int32_t start_pos, float *logits_out, int32_t *argmax_out);
 /* Prompt ingestion at positions start_pos..start_pos+n-1; logits of the last
  * token to logits_out (nullable); returns the greedy next token (>= 0). */
 int ss_cuda_prefill(ss_cuda_ctx_t *ctx, const int32_t *tokens, int32_t n, int32_t start_pos,
                     float *logits_out);
+/* The same embedding into out[hidden] (host); the prompt runs through the
+ * tensor-core product, 32 tokens per pass (single-GPU contexts with the
+ * weights resident and in the tiled layout: the default, or max_batch > 1). */
+int ss_cuda_embed(ss_cuda_ctx_t *ctx, const int32_t *tokens, int32_t n, float *out);
+/* Greedy decode of sequences 0..n_seq-1 together for n_steps (n_seq <=
+ * max_batch), each step's tokens fed back on the device without a host round
+ * trip: tokens[s] is sequence s's token at start_pos; ids_out [n_steps][n_seq]
+ * receives the tokens generated at positions start_pos + 1 .. start_pos +
+ * n_steps.  The single-sequence decode state is left unchanged. */
+int ss_cuda_decode_greedy_batch(ss_cuda_ctx_t *ctx, const int32_t *tokens, int32_t n_seq,
+                                int32_t start_pos, int32_t n_steps, int32_t *ids_out);
 /* Greedy decode of n_steps tokens, each fed back on the device without a host
  * round trip: the token at start_pos is `token`, ids_out[i] receives the token
  * generated at position start_pos + 1 + i. */

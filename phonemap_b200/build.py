@@ -27,7 +27,8 @@ SYNTH_LIB = os.path.join(LIBDIR, "libss_synth.so")
 
 CUDA_SOURCES = ["ss_cuda_api.cu", "noalloc_argmax.cu"]
 CUDA_HEADERS = ["common.cuh", "gemv.cuh", "attention.cuh", "misc_kernels.cuh",
-                "step_kernel.cuh", "qgemm.cuh", "qgemm_host.inc", "tp_nccl.h", "gguf_view.h",
+                "step_kernel.cuh", "qgemm.cuh", "qgemm_host.inc", "batch_kernels.cuh",
+                "batch_host.inc", "tp_nccl.h", "gguf_view.h",
                 "ss_cuda_internal.h"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -242,4 +242,105 @@ __global__ void bt_token_kernel(const unsigned long long* __restrict__ best, int
   if (t < T) next[t] = best[t] == 0 ? 0 : unpack_argmax_index(best[t]);
 }
 
+// Single-sequence step through the many-token kernels with its token and
+// position on the device, as the decode step reads them (contexts without the
+// persistent step): token seq_tokens[pos] of sequence 0 at pos = ctrl->pos.
+// A position outside the context sets error bit 1, a token outside the
+// vocabulary bit 2; either then reads row 0 / position 0 so every later
+// access stays in bounds.
+__global__ void bt_from_ctrl_kernel(const int* __restrict__ ctrl_pos, const int* __restrict__ seq_tokens, int ctx,
+                                    int vocab, int* __restrict__ meta, int meta_stride, int* err) {
+  if (threadIdx.x != 0) return;
+  int pos = *ctrl_pos;
+  if (pos < 0 || pos >= ctx) {
+    atomicOr(err, 1);
+    pos = 0;
+  }
+  int tok = seq_tokens[pos];
+  if (tok < 0 || tok >= vocab) {
+    atomicOr(err, 2);
+    tok = 0;
+  }
+  meta[0] = tok;
+  meta[meta_stride] = pos;
+  meta[2 * meta_stride] = 0;
+}
+
+// After that step: its logits become the context's, its greedy token goes to
+// seq_tokens[ctx] and, past the caller's tokens, to the next position; the
+// position advances (the decode step's epilogue, gemv.cuh's argmax).
+__global__ void bt_to_ctrl_kernel(int* __restrict__ ctrl_pos, const int* __restrict__ fixed_until,
+                                  int* __restrict__ seq_tokens, int ctx, const int* __restrict__ next,
+                                  const float* __restrict__ row, float* __restrict__ logits, int vocab) {
+  for (int i = threadIdx.x; i < vocab; i += blockDim.x) logits[i] = row[i];
+  if (threadIdx.x == 0) {
+    const int tok = next[0];
+    const int pos = *ctrl_pos;
+    if (pos >= 0 && pos + 1 < ctx && pos + 1 >= *fixed_until) seq_tokens[pos + 1] = tok;
+    seq_tokens[ctx] = tok;
+    *ctrl_pos = pos + 1;
+  }
+}
+
+// ---- sentence embedding (ss_scheduler_embed, layer_scheduler.c:805-915):
+// every prompt token's final hidden state through the final RMSNorm, summed
+// over the tokens in order, times 1/n, then L2-normalised.
+
+// Final RMSNorm scale of each of T tokens, 1 / sqrtf(ss / d + eps) with ss
+// summed sequentially in element order, products and sums rounded apart
+// (ss_rmsnorm -> cpu_neon.c:109-115, as the reference's C compiles).  One
+// thread per token: the sum is one dependent chain either way.
+__global__ void bt_norm_scale_kernel(const float* __restrict__ h, int T, int d, float eps,
+                                     float* __restrict__ scale) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  const float* x = h + (size_t)t * d;
+  float ss = 0.0f;
+  for (int i = 0; i < d; i++) ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
+  scale[t] = 1.0f / sqrtf(__fdiv_rn(ss, (float)d) + eps);
+}
+
+// sum[j] += (h[t][j] * scale[t]) * w[j] for t = 0..T-1 in order (the
+// embedding's running sum, layer_scheduler.c:888-894; w: output_norm).
+__global__ void bt_pool_kernel(const float* __restrict__ h, const float* __restrict__ scale, int T, int d,
+                               const float* __restrict__ w, float* __restrict__ sum) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= d) return;
+  float acc = sum[j];
+  for (int t = 0; t < T; t++) acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(h[(size_t)t * d + j], scale[t]), w[j]));
+  sum[j] = acc;
+}
+
+// out = sum * (1 / n), then times 1 / (sqrtf(sum_j out_j^2) + 1e-12f), the
+// squares summed sequentially in element order (layer_scheduler.c:896-910).
+// One block; the scaled vector is staged in shared memory (d floats).
+__global__ void bt_embed_finish_kernel(const float* __restrict__ sum, int d, int n, float* __restrict__ out) {
+  extern __shared__ float e[];
+  __shared__ float s_scale;
+  const float inv = 1.0f / (float)n;
+  for (int j = threadIdx.x; j < d; j += blockDim.x) e[j] = __fmul_rn(sum[j], inv);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float l2 = 0.0f;
+    for (int j = 0; j < d; j++) l2 = __fadd_rn(l2, __fmul_rn(e[j], e[j]));
+    s_scale = 1.0f / __fadd_rn(sqrtf(l2), 1e-12f);
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < d; j += blockDim.x) out[j] = __fmul_rn(e[j], s_scale);
+}
+
+// Greedy feedback of a batched decode step, on the device: each sequence's
+// greedy token becomes its next input at the next position, and is recorded
+// at ids[(pos + 1) * stride + t] (positions up to ctx).
+__global__ void bt_feed_kernel(int* __restrict__ meta, int meta_stride, int T, int* __restrict__ ids,
+                               int stride, int ctx) {
+  const int t = threadIdx.x;
+  if (t >= T) return;
+  const int next = meta[3 * meta_stride + t];
+  const int pos = meta[meta_stride + t] + 1;
+  if (pos <= ctx) ids[(size_t)pos * stride + t] = next;
+  meta[t] = next;
+  meta[meta_stride + t] = pos < ctx ? pos : ctx - 1;
+}
+
 }  // namespace ss

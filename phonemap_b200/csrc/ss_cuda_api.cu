@@ -460,8 +460,14 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
   }
   // layer streaming runs the multi-kernel step
   c->mega = c->mega && !c->streaming && plan_step(c, out->type);
+  // several sequences decode through the many-token step, which reads the
+  // tiled layout; without the persistent step it then runs every step
+  if (c->max_batch > 1 && (c->streaming || c->tp_size > 1))
+    fail(SS_CUDA_ERROR_INVALID_PARAMS, "max_batch %d: batched decode runs on one GPU with the weights resident",
+         c->max_batch);
+  c->tiled = c->mega || c->max_batch > 1;
   auto mat_layout = [&](int rows, int cols, int type) {
-    return c->mega ? layout_tiled(rows, cols, type) : layout(rows, cols, type);
+    return c->tiled ? layout_tiled(rows, cols, type) : layout(rows, cols, type);
   };
   size_t max_bytes = 0;
   for (const auto& t : g.tensors) max_bytes = std::max<size_t>(max_bytes, t.bytes);
@@ -479,7 +485,7 @@ void load_model(Context* c, const uint8_t* base, uint64_t size, uint32_t ctx_opt
     // persistent step addresses layer l as layer 0 + l * stride), and the
     // norm weights as [L][d] arrays
     // an FFN wider than one GEMV's columns: down as two column halves
-    const bool split_down = !c->mega && c->ff / 32 > kGemvMaxNb;
+    const bool split_down = !c->tiled && c->ff / 32 > kGemvMaxNb;
     if (split_down && (c->tp_size > 1 || c->streaming || c->ff % 64 || c->ff / 64 > kGemvMaxNb))
       fail(SS_CUDA_ERROR_INVALID_MODEL,
            "FFN width %d needs the down projection split in two, which supports one GPU without "
@@ -606,7 +612,7 @@ void alloc_step_state(Context* c);
 
 void alloc_state(Context* c) {
   const int kvd = c->nkv * c->hd, qd = c->nh * c->hd;
-  const size_t rows = (size_t)c->L * c->ctx;
+  const size_t rows = (size_t)c->max_batch * c->L * c->ctx;  // sequence 0 first
   c->kc = dev_alloc<int8_t>(c, rows * kvd);
   c->vc = dev_alloc<int8_t>(c, rows * kvd);
   c->ks = dev_alloc<float>(c, rows);
@@ -764,7 +770,7 @@ AttnFn attn_fn(int hd) {
 
 void plan_all(Context* c) {
   CK(cudaFuncSetAttribute(attn_fn(c->hd), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->attn_smem));
-  if (c->mega) return;  // the persistent step was planned before the upload
+  if (c->tiled) return;  // the persistent step was planned before the upload; no GEMV step
   const Layer& l0 = c->layers[0];
   c->g_qkv = plan_gemv_for(c, XSrc::RmsNorm, Epi::QKV, l0.qkv);
   c->g_o = plan_gemv_for(c, XSrc::Plain, Epi::Residual, l0.o);
@@ -943,6 +949,9 @@ void enqueue_layer_copy(Context* c, int l) {
   CK(cudaEventRecord(c->ev_ready[slot], c->copy_stream));
 }
 
+#include "qgemm_host.inc"
+#include "batch_host.inc"
+
 // Enqueues one decode step (embedding -> L layers -> lm_head + argmax).
 // Streaming: the first two streamed layers' copies start with the step (their
 // slots were last used by the previous step, which is complete in stream
@@ -951,6 +960,10 @@ void enqueue_layer_copy(Context* c, int l) {
 void enqueue_step(Context* c, bool pdl) {
   if (c->mega) {
     launch_step(c);
+    return;
+  }
+  if (bt_only(c)) {
+    bt_dev_step(c);
     return;
   }
   const int R = c->n_resident;
@@ -983,7 +996,8 @@ void enqueue_step(Context* c, bool pdl) {
 }
 
 void build_graph(Context* c) {
-  if (c->step_exec || !c->use_graph || c->mega) return;  // one launch per step needs no graph
+  // one launch per step needs no graph; the many-token step keeps its own
+  if (c->step_exec || !c->use_graph || c->tiled) return;
   for (int attempt = 0; attempt < 2; attempt++) {
     const bool pdl = c->use_pdl && attempt == 0;
     cudaGraph_t graph = nullptr;
@@ -1038,6 +1052,20 @@ void put_tokens(Context* c, const int32_t* toks, int n, int pos) {
       fail(SS_CUDA_ERROR_INVALID_PARAMS, "token %d outside 0..%d", toks[i], c->vocab - 1);
   if (pos < 0 || pos + n > c->ctx) fail(SS_CUDA_ERROR_INVALID_PARAMS, "tokens past the context");
   CK(cudaMemcpyAsync(c->seq_tokens + pos, toks, sizeof(int) * n, cudaMemcpyHostToDevice, c->stream));
+}
+
+// The prompt of sequence 0 (ss_scheduler_prefill, layer_scheduler.c:681-803):
+// through the tensor-core product, 32 tokens per pass, where the weights are
+// in its layout; otherwise the decode step replayed once per prompt token.
+// Afterwards the last token's logits and greedy token are the context's.
+void ingest_prompt(Context* c, const int32_t* tokens, int n, int start_pos) {
+  put_tokens(c, tokens, n, start_pos);
+  if (bt_eligible(c)) {
+    bt_prefill(c, 0, tokens, n, start_pos);
+  } else {
+    set_position(c, start_pos, start_pos + n);
+    run_steps(c, n);
+  }
 }
 
 // Checks builds: the tensor-parallel step's record, to stderr.
@@ -1217,8 +1245,9 @@ Context* create(const uint8_t* base, uint64_t size, const ss_cuda_options_t* o) 
   ss_cuda_default_options(&opts);
   if (o) memcpy(&opts, o, std::min<size_t>(sizeof(opts), o->struct_size ? o->struct_size : sizeof(opts)));
   if (opts.max_batch == 0) opts.max_batch = 1;
-  if (opts.max_batch != 1)
-    fail(SS_CUDA_ERROR_INVALID_PARAMS, "max_batch %u: only single-sequence decode is built", opts.max_batch);
+  if (opts.max_batch > (uint32_t)kQgMaxT)
+    fail(SS_CUDA_ERROR_INVALID_PARAMS, "max_batch %u: at most %d sequences decode together", opts.max_batch,
+         kQgMaxT);
   int dev = opts.device;
   if (dev < 0) {
     const char* e = getenv("SS_CUDA_DEVICE");
@@ -1261,6 +1290,9 @@ Context* create(const uint8_t* base, uint64_t size, const ss_cuda_options_t* o) 
     CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     if (base) {
       load_model(c, base, size, opts.context_size);
+      if (c->max_batch > 1 && !bt_shapes_ok(c))
+        fail(SS_CUDA_ERROR_INVALID_MODEL, "max_batch %d: the weights' blocks do not fit the batched product",
+             c->max_batch);
       if (c->streaming) setup_streaming(c, base, size);
       alloc_state(c);
       plan_all(c);
@@ -1374,8 +1406,6 @@ bool op_matvec(ss_cuda_ctx_t* ctx, float* out, const void* mat, const float* vec
          }) == SS_CUDA_OK;
 }
 
-#include "qgemm_host.inc"
-#include "batch_host.inc"
 
 // A quantized weight tensor by GGUF name: its device matrix and where its rows
 // sit there (row r of the tensor is matrix row r * mul + add).
@@ -1500,6 +1530,10 @@ SS_API void ss_cuda_free(ss_cuda_ctx_t* ctx) {
   cudaSetDevice(c->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
   if (c->step_exec) cudaGraphExecDestroy(c->step_exec);  // before the communicator it uses
+  for (auto& g : c->bt_graphs)
+    if (g.second) cudaGraphExecDestroy(g.second);
+  if (c->bt_dev_exec) cudaGraphExecDestroy(c->bt_dev_exec);
+  if (c->bt_meta_host) cudaFreeHost(c->bt_meta_host);
   if (c->comm) {
     // no rank unmaps or frees an exchange block while a peer may still use it
     if (c->has_model && c->xchg) guard([&] { tp_barrier(c); });
@@ -1555,7 +1589,7 @@ SS_API int ss_cuda_stats(const ss_cuda_ctx_t* ctx, int64_t* out, int32_t n) {
     cudaFuncAttributes fa{};
     const int64_t arch = cudaFuncGetAttributes(&fa, embed_kernel) == cudaSuccess ? fa.binaryVersion : -1;
     cudaGetLastError();
-    const int64_t v[15] = {c->has_model ? (c->mega ? 1 : 2 + 5LL * c->L + (c->tp_size > 1) +
+    const int64_t v[15] = {c->has_model ? (c->mega ? 1 : bt_only(c) ? bt_launches(c, 1) + 2 : 2 + 5LL * c->L + (c->tp_size > 1) +
                                                    (c->layers[0].down2.cols ? (int64_t)c->L : 0) +
                                                    (c->streaming ? 7LL * (c->L - c->n_resident) : 0))
                                        : 0,
@@ -1635,9 +1669,7 @@ SS_API float* ss_cuda_scheduler_prefill(ss_cuda_ctx_t* ctx, const int32_t* token
     Context* c = need_model(ctx);
     if (!tokens || n <= 0) fail(SS_CUDA_ERROR_INVALID_PARAMS, "empty prompt");
     if (c->cancelled.load()) fail(SS_CUDA_ERROR_CANCELLED, "cancelled");
-    put_tokens(c, tokens, n, start_pos);
-    set_position(c, start_pos, start_pos + n);
-    run_steps(c, n);
+    ingest_prompt(c, tokens, n, start_pos);
     read_logits(c, nullptr);
     res = c->h_logits;
   });
@@ -1647,7 +1679,7 @@ SS_API float* ss_cuda_scheduler_prefill(ss_cuda_ctx_t* ctx, const int32_t* token
 SS_API void ss_cuda_reset(ss_cuda_ctx_t* ctx) {
   guard([&] {
     Context* c = need_model(ctx);
-    const size_t rows = (size_t)c->L * c->ctx, kvd = (size_t)c->nkv * c->hd;
+    const size_t rows = (size_t)c->max_batch * c->L * c->ctx, kvd = (size_t)c->nkv * c->hd;
     CK(cudaMemsetAsync(c->kc, 0, rows * kvd, c->stream));
     CK(cudaMemsetAsync(c->vc, 0, rows * kvd, c->stream));
     CK(cudaMemsetAsync(c->ks, 0, rows * 4, c->stream));
@@ -1689,7 +1721,21 @@ SS_API int ss_cuda_forward(ss_cuda_ctx_t* ctx, const int32_t* token_ids, int32_t
                            float* logits_out, int32_t* argmax_out) {
   return guard([&] {
     Context* c = need_model(ctx);
-    if (!token_ids || n_seq != 1) fail(SS_CUDA_ERROR_INVALID_PARAMS, "n_seq must be 1");
+    if (!token_ids || n_seq < 1) fail(SS_CUDA_ERROR_INVALID_PARAMS, "no tokens");
+    if (n_seq > 1) {
+      // sequences 0..n_seq-1 together, one token each at position pos
+      if (c->cancelled.load()) fail(SS_CUDA_ERROR_CANCELLED, "cancelled");
+      if (!bt_eligible(c)) fail(SS_CUDA_ERROR_INVALID_PARAMS, "n_seq %d: the context decodes one sequence", n_seq);
+      bt_decode(c, token_ids, n_seq, pos);
+      if (logits_out)
+        CK(cudaMemcpyAsync(logits_out, c->bt_logits, sizeof(float) * (size_t)n_seq * c->vocab_l,
+                           cudaMemcpyDeviceToHost, c->stream));
+      CK(cudaMemcpyAsync(&c->h_small[32], c->bt_meta + 3 * kQgMaxT, sizeof(int) * n_seq, cudaMemcpyDeviceToHost,
+                         c->stream));
+      check_device_error(c);
+      if (argmax_out) memcpy(argmax_out, &c->h_small[32], sizeof(int) * n_seq);
+      return;
+    }
     put_tokens(c, token_ids, 1, pos);
     set_position(c, pos, pos + 1);
     run_steps(c, 1);
@@ -1709,19 +1755,76 @@ SS_API int ss_cuda_prefill(ss_cuda_ctx_t* ctx, const int32_t* tokens, int32_t n,
     Context* c = need_model(ctx);
     if (!tokens || n <= 0) fail(SS_CUDA_ERROR_INVALID_PARAMS, "empty prompt");
     if (c->cancelled.load()) fail(SS_CUDA_ERROR_CANCELLED, "cancelled");
-    put_tokens(c, tokens, n, start_pos);
-    if (bt_eligible(c)) {
-      // the whole prompt through the tensor-core product, 32 tokens per pass
-      bt_prefill(c, tokens, n, start_pos);
-    } else {
-      // the decode step replayed once per prompt token
-      set_position(c, start_pos, start_pos + n);
-      run_steps(c, n);
-    }
+    ingest_prompt(c, tokens, n, start_pos);
     read_logits(c, logits_out ? logits_out : nullptr);
     tok = c->h_small[16];
   });
   return rc == SS_CUDA_OK ? tok : rc;
+}
+
+SS_API int ss_cuda_prefill_batch(ss_cuda_ctx_t* ctx, const int32_t* tokens, int32_t n_seq, int32_t n,
+                                 int32_t start_pos, float* logits_out, int32_t* argmax_out) {
+  return guard([&] {
+    Context* c = need_model(ctx);
+    if (!tokens || n <= 0 || n_seq < 1) fail(SS_CUDA_ERROR_INVALID_PARAMS, "empty prompt");
+    if (n_seq > c->max_batch)
+      fail(SS_CUDA_ERROR_INVALID_PARAMS, "n_seq %d outside 1..%d (max_batch)", n_seq, c->max_batch);
+    if (!bt_eligible(c)) fail(SS_CUDA_ERROR_INVALID_PARAMS, "the batched prompt needs the many-token step");
+    for (int s = 0; s < n_seq; s++) {
+      if (c->cancelled.load()) fail(SS_CUDA_ERROR_CANCELLED, "cancelled");
+      const int32_t* t = tokens + (size_t)s * n;
+      if (s == 0) put_tokens(c, t, n, start_pos);
+      bt_prefill(c, s, t, n, start_pos);
+      if (logits_out)
+        CK(cudaMemcpyAsync(logits_out + (size_t)s * c->vocab_l, c->bt_logits, sizeof(float) * c->vocab_l,
+                           cudaMemcpyDeviceToHost, c->stream));
+      CK(cudaMemcpyAsync(&c->h_small[32 + s], c->bt_meta + 3 * kQgMaxT, sizeof(int), cudaMemcpyDeviceToHost,
+                         c->stream));
+    }
+    check_device_error(c);
+    if (argmax_out) memcpy(argmax_out, &c->h_small[32], sizeof(int) * n_seq);
+  });
+}
+
+SS_API int ss_cuda_decode_greedy_batch(ss_cuda_ctx_t* ctx, const int32_t* tokens, int32_t n_seq,
+                                      int32_t start_pos, int32_t n_steps, int32_t* ids_out) {
+  return guard([&] {
+    Context* c = need_model(ctx);
+    if (!tokens || !ids_out) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null argument");
+    if (!bt_eligible(c)) fail(SS_CUDA_ERROR_INVALID_PARAMS, "batched decode needs the many-token step");
+    bt_decode_greedy(c, tokens, n_seq, start_pos, n_steps);
+    check_device_error(c);
+    std::vector<int> rows((size_t)n_steps * kQgMaxT);
+    CK(cudaMemcpy(rows.data(), c->bt_ids + (size_t)(start_pos + 1) * kQgMaxT, sizeof(int) * rows.size(),
+                  cudaMemcpyDeviceToHost));
+    for (int k = 0; k < n_steps; k++)
+      for (int s = 0; s < n_seq; s++) ids_out[(size_t)k * n_seq + s] = rows[(size_t)k * kQgMaxT + s];
+  });
+}
+
+SS_API int ss_cuda_embed(ss_cuda_ctx_t* ctx, const int32_t* tokens, int32_t n, float* out) {
+  return guard([&] {
+    Context* c = need_model(ctx);
+    if (!tokens || !out || n <= 0) fail(SS_CUDA_ERROR_INVALID_PARAMS, "empty prompt");
+    if (c->cancelled.load()) fail(SS_CUDA_ERROR_CANCELLED, "cancelled");
+    if (!bt_eligible(c)) fail(SS_CUDA_ERROR_INVALID_PARAMS, "the embedding needs the many-token step");
+    put_tokens(c, tokens, n, 0);
+    bt_embed(c, tokens, n);
+    CK(cudaMemcpyAsync(out, c->bt_emb + c->d, sizeof(float) * c->d, cudaMemcpyDeviceToHost, c->stream));
+    check_device_error(c);
+  });
+}
+
+SS_API float* ss_cuda_scheduler_embed(ss_cuda_ctx_t* ctx, const int32_t* tokens, int32_t n) {
+  auto* c = reinterpret_cast<Context*>(ctx);
+  if (!c || !c->has_model) return nullptr;
+  float* e = static_cast<float*>(malloc(sizeof(float) * (size_t)c->d));
+  if (!e) return nullptr;
+  if (ss_cuda_embed(ctx, tokens, n, e) != SS_CUDA_OK) {
+    free(e);
+    return nullptr;
+  }
+  return e;
 }
 
 SS_API int ss_cuda_decode_begin(ss_cuda_ctx_t* ctx, int32_t token, int32_t pos) {
@@ -1871,9 +1974,14 @@ SS_API int ss_cuda_dequantize(int32_t type, const void* blocks, int64_t n, float
 SS_API int ss_cuda_time_kernel(ss_cuda_ctx_t* ctx, int32_t which, int32_t iters, float* ms_per_launch) {
   return guard([&] {
     Context* c = need_model(ctx);
-    if (which < 0 || which > 6 || iters <= 0 || !ms_per_launch) fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad arguments");
-    if (c->mega && which != 6)
+    if (which < 0 || which > 7 || iters <= 0 || !ms_per_launch) fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad arguments");
+    if (c->tiled && which < 6)
       fail(SS_CUDA_ERROR_INVALID_PARAMS, "per-kernel timing needs the multi-kernel step (SS_CUDA_FLAG_MULTI_KERNEL)");
+    if (which == 7) {
+      if (!bt_eligible(c)) fail(SS_CUDA_ERROR_INVALID_PARAMS, "the tensor-core product needs the tiled layout");
+      bt_prepare(c);
+      qg_product(c, c->layers[0].gu, c->bt_h, c->d, c->layers[0].ffn_norm, c->max_batch, true, false);
+    }
     const int pos0 = c->host_pos;
     if (which == 6 && pos0 + iters + 3 > c->ctx)
       fail(SS_CUDA_ERROR_INVALID_PARAMS, "%d steps from position %d exceed the context", iters + 3, pos0);
@@ -1884,6 +1992,7 @@ SS_API int ss_cuda_time_kernel(ss_cuda_ctx_t* ctx, int32_t which, int32_t iters,
       const int l = i % c->L;
       switch (which) {
         case 6: enqueue_step(c, c->use_pdl); break;
+        case 7: qg_product(c, c->layers[(size_t)l].gu, c->bt_h, c->d, nullptr, c->max_batch, false, true); break;
         case 0: launch_qkv(c, l, false); break;
         case 1: launch_attn(c, l, false); break;
         case 2: launch_o(c, l, false); break;
@@ -1919,6 +2028,7 @@ SS_API int64_t ss_cuda_kernel_bytes(const ss_cuda_ctx_t* ctx, int32_t which) {
     case 2: return (int64_t)matrix_bytes(l0.o);
     case 3: return (int64_t)matrix_bytes(l0.gu);
     case 4: return (int64_t)(matrix_bytes(l0.down) + (l0.down2.cols ? matrix_bytes(l0.down2) : 0));
+    case 7: return (int64_t)matrix_bytes(l0.gu);
     case 5: return (int64_t)matrix_bytes(c->lm_head);
     case 6: {
       int64_t b = (int64_t)matrix_bytes(c->lm_head);

@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <map>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -100,6 +101,14 @@ struct Context {
   float* bt_kv = nullptr;       // [32][2 kvd]: k | v of each token before encoding
   unsigned* bt_amax = nullptr;  // [32][2]: largest |k|, |v| (float bits)
   unsigned long long* bt_best = nullptr;  // [32]: packed greedy choice
+  int* bt_ids = nullptr;                   // [ctx + 1][32]: batched greedy tokens by position
+  float* bt_emb = nullptr;                 // [d] embedding sum | [d] result | [32] norm scales
+  bool bt_ready = false;                   // scratch reserved for 32 tokens, tensor maps built
+  // captured many-token steps: key 2 * T + (head of the last token only);
+  // bt_dev_exec is the single-sequence step that reads its token and position
+  // from the device (contexts without the persistent step)
+  std::map<int, cudaGraphExec_t> bt_graphs;
+  cudaGraphExec_t bt_dev_exec = nullptr;
   GemvTuning tuning;
   std::atomic<bool> cancelled{false};
 
@@ -186,6 +195,9 @@ struct Context {
 
   // persistent single-kernel step (step_kernel.cuh)
   bool mega = false;
+  // matrices in the tiled layout (the persistent step's, which the many-token
+  // product reads): the persistent step, or several sequences decoded together
+  bool tiled = false;
   const void* step_fn = nullptr;
   int step_grid = 0, step_nslots = 0, step_slot_bytes = 0, step_nsplit = 1;
   size_t step_smem = 0;

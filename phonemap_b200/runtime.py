@@ -34,7 +34,8 @@ EXPORTED = [
     "ss_cuda_dequantize_tensor", "ss_cuda_dequantize", "ss_cuda_kv_row",
     "ss_cuda_time_kernel", "ss_cuda_kernel_bytes", "ss_cuda_argmax_noalloc",
     "ss_cuda_step_trace", "ss_cuda_tp_unique_id", "ss_cuda_test_fail_next_step",
-    "ss_cuda_matmul_batch",
+    "ss_cuda_matmul_batch", "ss_cuda_prefill_batch", "ss_cuda_decode_greedy_batch",
+    "ss_cuda_embed", "ss_cuda_scheduler_embed",
 ]
 
 
@@ -101,6 +102,13 @@ def load_library() -> ctypes.CDLL:
     lib.ss_cuda_scheduler_prefill.restype = _f32p
     lib.ss_cuda_forward.argtypes = [vp, _i32p, ctypes.c_int32, ctypes.c_int32, _f32p, _i32p]
     lib.ss_cuda_prefill.argtypes = [vp, _i32p, ctypes.c_int32, ctypes.c_int32, _f32p]
+    lib.ss_cuda_prefill_batch.argtypes = [vp, _i32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                          _f32p, _i32p]
+    lib.ss_cuda_decode_greedy_batch.argtypes = [vp, _i32p, ctypes.c_int32, ctypes.c_int32,
+                                                ctypes.c_int32, _i32p]
+    lib.ss_cuda_embed.argtypes = [vp, _i32p, ctypes.c_int32, _f32p]
+    lib.ss_cuda_scheduler_embed.argtypes = [vp, _i32p, ctypes.c_int32]
+    lib.ss_cuda_scheduler_embed.restype = ctypes.POINTER(ctypes.c_float)
     lib.ss_cuda_decode_greedy.argtypes = [vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _i32p]
     lib.ss_cuda_decode_begin.argtypes = [vp, ctypes.c_int32, ctypes.c_int32]
     lib.ss_cuda_decode_steps.argtypes = [vp, ctypes.c_int32]
@@ -152,20 +160,22 @@ def tp_unique_id() -> bytes:
 
 
 class CudaModel:
-    """One decode context on one GPU (one sequence)."""
+    """One decode context on one GPU (one sequence, or up to max_batch)."""
 
     def __init__(self, gguf_path: str | None, context_size: int = 0, device: int = -1,
                  flags: int = 0, tp_rank: int = 0, tp_size: int = 1, tp_nccl_id: bytes = b"",
-                 hbm_budget_bytes: int = 0):
+                 hbm_budget_bytes: int = 0, max_batch: int = 1):
         """tp_size > 1: this process is rank tp_rank of a tensor-parallel group
         whose NCCL id (tp_unique_id() on rank 0) is tp_nccl_id.
         hbm_budget_bytes > 0: HBM for the layers' weights; layers beyond it are
-        streamed from the model file every step (layer streaming)."""
+        streamed from the model file every step (layer streaming).
+        max_batch > 1: sequences 0..max_batch-1 each keep a KV cache and decode
+        together through forward_batch / prefill_batch."""
         lib = load_library()
         self._lib = lib
         opts = default_options(context_size=context_size, device=device, flags=flags,
                                tp_rank=tp_rank, tp_size=tp_size,
-                               hbm_budget_bytes=int(hbm_budget_bytes))
+                               hbm_budget_bytes=int(hbm_budget_bytes), max_batch=int(max_batch))
         if tp_size > 1:
             if len(tp_nccl_id) != 128:
                 raise ValueError("tp_nccl_id must be the 128 bytes of tp_unique_id()")
@@ -199,6 +209,16 @@ class CudaModel:
             raise SSCudaError(-7, self._lib.ss_cuda_last_error().decode())
         return np.ctypeslib.as_array(p, shape=(self.vocab,)).copy()
 
+    def scheduler_embed(self, tokens) -> np.ndarray:
+        """ss_scheduler_embed's twin: a malloc'd vector, copied and freed here."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        p = self._lib.ss_cuda_scheduler_embed(self._h, _i(t), len(t))
+        if not p:
+            raise SSCudaError(-7, self._lib.ss_cuda_last_error().decode())
+        out = np.ctypeslib.as_array(p, shape=(self.hidden,)).copy()
+        ctypes.CDLL(None).free(ctypes.cast(p, ctypes.c_void_p))
+        return out
+
     def reset(self) -> None:
         self._lib.ss_cuda_reset(self._h)
 
@@ -217,6 +237,50 @@ class CudaModel:
         t = np.ascontiguousarray(tokens, np.int32)
         lp = _f(logits) if logits is not None else None
         return _check(self._lib.ss_cuda_prefill(self._h, _i(t), len(t), int(start_pos), lp))
+
+    def forward_batch(self, tokens, pos: int, logits: np.ndarray | None = None) -> list[int]:
+        """One step of sequences 0..len(tokens)-1 at position pos; greedy tokens.
+        logits: optional float32 [len(tokens), vocab] output."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        am = np.zeros(len(t), np.int32)
+        if logits is not None and (logits.dtype != np.float32 or logits.size < len(t) * self.vocab
+                                   or not logits.flags.c_contiguous):
+            raise ValueError("logits must be contiguous float32 [n_seq, vocab]")
+        lp = _f(logits) if logits is not None else None
+        _check(self._lib.ss_cuda_forward(self._h, _i(t), len(t), int(pos), lp, _i(am)))
+        return [int(v) for v in am]
+
+    def prefill_batch(self, prompts, start_pos: int = 0,
+                      logits: np.ndarray | None = None) -> list[int]:
+        """Prompts [n_seq, n] of sequences 0..n_seq-1; greedy next token of each."""
+        t = np.ascontiguousarray(prompts, np.int32)
+        if t.ndim != 2:
+            raise ValueError("prompts must be [n_seq, n]")
+        am = np.zeros(t.shape[0], np.int32)
+        if logits is not None and (logits.dtype != np.float32 or logits.size < t.shape[0] * self.vocab
+                                   or not logits.flags.c_contiguous):
+            raise ValueError("logits must be contiguous float32 [n_seq, vocab]")
+        lp = _f(logits) if logits is not None else None
+        _check(self._lib.ss_cuda_prefill_batch(self._h, _i(t), t.shape[0], t.shape[1], int(start_pos),
+                                               lp, _i(am)))
+        return [int(v) for v in am]
+
+    def embed(self, tokens) -> np.ndarray:
+        """Mean-pooled, L2-normalised final hidden state of the tokens
+        (ss_scheduler_embed, positions 0..n-1)."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        out = np.empty(self.hidden, np.float32)
+        _check(self._lib.ss_cuda_embed(self._h, _i(t), len(t), _f(out)))
+        return out
+
+    def decode_greedy_batch(self, tokens, start_pos: int, n_steps: int) -> np.ndarray:
+        """Greedy decode of sequences 0..len(tokens)-1 together, fed back on the
+        device; returns int32 [n_steps, n_seq] (positions start_pos+1 ..)."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        out = np.zeros((n_steps, len(t)), np.int32)
+        _check(self._lib.ss_cuda_decode_greedy_batch(self._h, _i(t), len(t), int(start_pos),
+                                                     int(n_steps), _i(out)))
+        return out
 
     def decode_greedy(self, token: int, start_pos: int, n_steps: int) -> list[int]:
         out = np.zeros(n_steps, np.int32)
@@ -267,7 +331,8 @@ class CudaModel:
                 "kernel_arch")
         return {k: int(x) for k, x in zip(keys, v)}
 
-    KERNELS = {"qkv": 0, "attention": 1, "o": 2, "gate_up": 3, "down": 4, "lm_head": 5, "step": 6}
+    KERNELS = {"qkv": 0, "attention": 1, "o": 2, "gate_up": 3, "down": 4, "lm_head": 5, "step": 6,
+               "product_gate_up": 7}
 
     def time_kernel(self, which: str, iters: int) -> float:
         """Average ms per isolated launch of one step kernel (clobbers state)."""

@@ -201,6 +201,38 @@ def make_argmax_fixture() -> None:
     print("argmax: written", {k: int(v) for k, v in fx.items() if k.startswith("want_")})
 
 
+EMBED_CONFIGS = ("tiny", "tiny-mha", "tiny-q8", "tinyllama")
+
+
+def embed_prompts(cfg) -> dict:
+    """The token lists embed.npz holds for a configuration: its prompt, one
+    token, and (where the context allows) 70 tokens -- more than one pass of
+    the GPU's 32-token step."""
+    p = [int(t) for t in synth.prompt_tokens(cfg)]
+    out = {"prompt": p, "one": p[:1]}
+    if cfg.ctx >= 80:
+        rng = np.random.default_rng(99)
+        out["long"] = [int(t) for t in rng.integers(0, cfg.vocab, size=70)]
+    return out
+
+
+def make_embed_fixture() -> None:
+    """embed.npz: ss_scheduler_embed's vector (layer_scheduler.c:805-915),
+    from the reference build, for each configuration's token lists."""
+    fx = {}
+    for cname in EMBED_CONFIGS:
+        cfg = configs.get(cname)
+        path = synth.ensure_gguf(cfg)
+        fx[f"{cname}_fingerprint"] = np.frombuffer(gguf_fingerprint(path), np.uint8)
+        for key, toks in embed_prompts(cfg).items():
+            ref = oracle.RefModel(path, cfg.ctx)
+            fx[f"{cname}_{key}_tokens"] = np.array(toks, np.int32)
+            fx[f"{cname}_{key}_embed"] = ref.embed(toks).astype(np.float32)
+            ref.close()
+    np.savez_compressed(os.path.join(OUT, "embed.npz"), **fx)
+    print(f"embed: {sorted(k for k in fx if k.endswith('_embed'))}")
+
+
 def main() -> int:
     if not oracle.ref_available() and not oracle.build_ref():
         print("reference build unavailable", file=sys.stderr)
@@ -211,6 +243,8 @@ def main() -> int:
             make_ops_fixture()
         elif n == "argmax":
             make_argmax_fixture()
+        elif n == "embed":
+            make_embed_fixture()
         else:
             make_model_fixture(n)
     return 0

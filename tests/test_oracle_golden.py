@@ -77,3 +77,19 @@ def test_noise_floor_fixture_matches_oracle():
     got = measure("tiny", rec["steps"])
     assert abs(got["max_step_inf_rel"] - rec["max_step_inf_rel"]) <= 1e-9
     assert got["prefill_inf_rel"] > 0.0  # the two orders do differ
+
+
+@pytest.mark.parametrize("name", SMALL + ["tinyllama"])
+def test_embed_bitexact(name):
+    """The restatement's sentence embedding (sso_embed) against the reference's
+    ss_scheduler_embed vectors in embed.npz: bit-identical."""
+    g = load_golden("embed")
+    cfg = configs.get(name)
+    path = synth.ensure_gguf(cfg)
+    assert gguf_fingerprint(path) == g[f"{name}_fingerprint"].tobytes()
+    for key in ("prompt", "one", "long"):
+        if f"{name}_{key}_tokens" not in g:
+            continue
+        m = oracle.OracleModel(path, cfg.ctx, cap512=True)
+        np.testing.assert_array_equal(m.embed(g[f"{name}_{key}_tokens"]), g[f"{name}_{key}_embed"])
+        m.close()
