@@ -589,8 +589,7 @@ def run_ours_batch(args):
                               "frac": round(step_gbs / peak, 4), "unit": "GB/s", "peak": peak,
                               "peak_source": peak_kind},
             "e2e": e2e,
-            "gpu_launches": int((stats["kernels_per_step"] if not stats["persistent"] else
-                                 1 + 18 * cfg.n_layers + 5 + 1) * K),
+            "gpu_launches": int(stats["kernels_per_batched_step"] * K),
             "clocks": sampler.summary(),
             "step_impl": "many-token step: tensor-core product per matrix (CUDA graph per batch shape)",
             "prefill_s": round(prefill_s, 3),

@@ -127,70 +127,159 @@ __global__ void bt_kv_encode_kernel(const float* __restrict__ kvtmp, const unsig
   }
 }
 
-// Attention of one (query head, token) over positions 0..pos of the token's
-// sequence (layer_scheduler.c:415-468): scores s_j = (q . dec(K_j)) * scale
-// summed in the reference's order (each score one thread, products and sums
-// separately rounded); softmax (tensor.c:154-173: max, expf, sum, times
-// 1/sum); out_i = sum_j p_j * dec(V_j)_i accumulated over j in order, as the
-// reference's saxpy does.  Scores live in shared memory (ctx floats).
+// Attention (layer_scheduler.c:415-468; softmax tensor.c:154-173) of every
+// token over positions 0..pos of its sequence, split over the positions as
+// flash-decoding does: CTA (kv head, token, slot s) takes the chunks of
+// kBtAttnChunk cached positions s, s + kBtAttnSlots, ... up to pos, for the G
+// query heads that share the kv head.  Per chunk: the int8 K and V rows and
+// their scales are staged in shared memory (coalesced 16-byte loads), scores
+// s_j = (q . k_j) * k_scale_j * (1/sqrt(hd)), then a running softmax (max m,
+// sum l, output o rescaled when m grows).  The slot's (m, l, o) go to `part`;
+// bt_attn_merge_kernel combines the slots.  The result equals the
+// reference's softmax-weighted sum of dec(V_j) up to fp32 rounding order.
+constexpr int kBtAttnChunk = 128;   // positions per chunk
+constexpr int kBtAttnSlots = 16;    // position slots (CTAs) per (kv head, token)
+constexpr int kBtAttnMaxG = 8;      // query heads per kv head
+
+__host__ __device__ constexpr size_t bt_attn_smem(int hd, int G) {
+  // q[G][hd] | scores[G][chunk] | k scale, v scale [chunk] | m, l, corr [G]
+  // | K chunk, V chunk [chunk][hd] int8
+  return (size_t)(G * hd + G * kBtAttnChunk + 2 * kBtAttnChunk + 4 * kBtAttnMaxG) * sizeof(float) +
+         (size_t)2 * kBtAttnChunk * hd;
+}
+
+// part layout: [T][nh][slots][hd + 2]: m, l, then o[hd].
 __global__ void __launch_bounds__(256) bt_attn_kernel(const float* __restrict__ q, BatchTokens bt, BatchKv kv,
                                                       int layer, int nh, int nkv, int hd, float scale,
-                                                      float* __restrict__ out) {
-  extern __shared__ float sm[];  // q[hd] | scores[ctx] | red[64]
-  const int h = blockIdx.x, t = blockIdx.y;
+                                                      float* __restrict__ part) {
+  extern __shared__ float sm[];
+  const int kvh = blockIdx.x, t = blockIdx.y, slot = blockIdx.z;
   const int pos = bt.pos[t], seq = bt.seq[t];
-  const int kvh = h / (nh / nkv), kvd = nkv * hd, qd = nh * hd;
-  float* qs = sm;
-  float* sc = sm + hd;
-  float* red = sc + kv.ctx;
-  for (int i = threadIdx.x; i < hd; i += blockDim.x) qs[i] = q[(size_t)t * qd + (size_t)h * hd + i];
-  __syncthreads();
-  const int8_t* kc = kv.kc + seq * kv.seq_stride + (size_t)layer * kv.ctx * kvd + (size_t)kvh * kv.ctx * hd;
-  const int8_t* vc = kv.vc + seq * kv.seq_stride + (size_t)layer * kv.ctx * kvd + (size_t)kvh * kv.ctx * hd;
+  if (slot * kBtAttnChunk > pos) return;  // no chunk for this slot (the merge skips it)
+  const int G = nh / nkv, kvd = nkv * hd, qd = nh * hd;
+  float* qs = sm;                               // [G][hd]
+  float* sc = qs + G * hd;                      // [G][chunk]
+  float* sks = sc + G * kBtAttnChunk;           // [chunk]
+  float* svs = sks + kBtAttnChunk;              // [chunk]
+  float* sml = svs + kBtAttnChunk;              // m[G] | l[G] | corr[G] | pad
+  int8_t* sk = reinterpret_cast<int8_t*>(sml + 4 * kBtAttnMaxG);
+  int8_t* sv = sk + kBtAttnChunk * hd;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  for (int i = tid; i < G * hd; i += nt) qs[i] = q[(size_t)t * qd + (size_t)kvh * G * hd + i];
+  if (tid < G) {
+    sml[tid] = -INFINITY;
+    sml[kBtAttnMaxG + tid] = 0.0f;
+  }
+  const size_t lbase = seq * kv.seq_stride + (size_t)layer * kv.ctx * kvd + (size_t)kvh * kv.ctx * hd;
+  const int8_t* kc = kv.kc + lbase;
+  const int8_t* vc = kv.vc + lbase;
   const float* ks = kv.ks + seq * kv.sc_stride + (size_t)layer * kv.ctx;
   const float* vs = kv.vs + seq * kv.sc_stride + (size_t)layer * kv.ctx;
-  float mx = -INFINITY;
-  for (int j = threadIdx.x; j <= pos; j += blockDim.x) {
-    const int8_t* kr = kc + (size_t)j * hd;
-    const float s = ks[j];
-    float dot = 0.0f;
-    for (int i = 0; i < hd; i += 16) {
-      const int4 kw = *reinterpret_cast<const int4*>(kr + i);
-      const int8_t* kb = reinterpret_cast<const int8_t*>(&kw);
+  // output elements of this thread: element e of heads hb, hb + hs, ...
+  const int e = tid % hd, hb = tid / hd, hs = nt / hd;  // hd divides 256 (hd <= 256, power of two)
+  float o[kBtAttnMaxG];
 #pragma unroll
-      for (int u = 0; u < 16; u++) dot = __fadd_rn(dot, __fmul_rn(qs[i + u], __fmul_rn((float)kb[u], s)));
+  for (int i = 0; i < kBtAttnMaxG; i++) o[i] = 0.0f;
+  const int vec = hd / 16;
+  for (int ch = slot; ch * kBtAttnChunk <= pos; ch += kBtAttnSlots) {
+    const int c0 = ch * kBtAttnChunk, cn = min(kBtAttnChunk, pos + 1 - c0);
+    __syncthreads();  // the previous chunk is consumed (and q, m, l are set)
+    for (int k = tid; k < cn * vec; k += nt) {
+      reinterpret_cast<int4*>(sk)[k] = __ldcg(reinterpret_cast<const int4*>(kc + (size_t)c0 * hd) + k);
+      reinterpret_cast<int4*>(sv)[k] = __ldcg(reinterpret_cast<const int4*>(vc + (size_t)c0 * hd) + k);
     }
-    const float v = __fmul_rn(dot, scale);
-    sc[j] = v;
-    mx = fmaxf(mx, v);
+    for (int k = tid; k < cn; k += nt) {
+      sks[k] = ks[c0 + k];
+      svs[k] = vs[c0 + k];
+    }
+    __syncthreads();
+    // scores of (head, position) pairs
+    for (int idx = tid; idx < G * cn; idx += nt) {
+      const int h = idx / cn, j = idx - h * cn;
+      const float* qh = qs + h * hd;
+      const int8_t* kr = sk + j * hd;
+      float dot = 0.0f;
+      for (int i = 0; i < hd; i += 16) {
+        const int4 kw = *reinterpret_cast<const int4*>(kr + i);
+        const int8_t* kb = reinterpret_cast<const int8_t*>(&kw);
+#pragma unroll
+        for (int u = 0; u < 16; u++) dot = fmaf(qh[i + u], (float)kb[u], dot);
+      }
+      sc[h * kBtAttnChunk + j] = dot * sks[j] * scale;
+    }
+    __syncthreads();
+    // running softmax per head: warp h (G <= 8 warps)
+    {
+      const int w = tid >> 5, lane = tid & 31;
+      if (w < G) {
+        float mx = -INFINITY;
+        for (int j = lane; j < cn; j += 32) mx = fmaxf(mx, sc[w * kBtAttnChunk + j]);
+        mx = warp_max(mx);
+        const float mo = sml[w], mn = fmaxf(mo, mx);
+        float sum = 0.0f;
+        for (int j = lane; j < cn; j += 32) {
+          const float pj = expf(sc[w * kBtAttnChunk + j] - mn);
+          sc[w * kBtAttnChunk + j] = pj * svs[j];  // the V scale joins the weight
+          sum += pj;
+        }
+        sum = warp_sum(sum);
+        if (lane == 0) {
+          const float corr = mo == -INFINITY ? 0.0f : expf(mo - mn);
+          sml[w] = mn;
+          sml[kBtAttnMaxG + w] = sml[kBtAttnMaxG + w] * corr + sum;
+          sml[2 * kBtAttnMaxG + w] = corr;
+        }
+      }
+    }
+    __syncthreads();
+    // o = o * corr + sum_j w_j v_j
+#pragma unroll
+    for (int i = 0; i < kBtAttnMaxG; i++) {
+      const int h = hb + i * hs;
+      if (h < G) o[i] *= sml[2 * kBtAttnMaxG + h];
+    }
+    for (int j = 0; j < cn; j++) {
+      const float v = (float)sv[j * hd + e];
+#pragma unroll
+      for (int i = 0; i < kBtAttnMaxG; i++) {
+        const int h = hb + i * hs;
+        if (h < G) o[i] = fmaf(sc[h * kBtAttnChunk + j], v, o[i]);
+      }
+    }
   }
-  // softmax
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  mx = warp_max(mx);
-  if (lane == 0) red[w] = mx;
   __syncthreads();
-  mx = -INFINITY;
-  for (int i = 0; i < nw; i++) mx = fmaxf(mx, red[i]);
-  float sum = 0.0f;
-  for (int j = threadIdx.x; j <= pos; j += blockDim.x) {
-    const float e = expf(__fsub_rn(sc[j], mx));
-    sc[j] = e;
-    sum += e;
+#pragma unroll
+  for (int i = 0; i < kBtAttnMaxG; i++) {
+    const int h = hb + i * hs;
+    if (h < G) {
+      float* pp = part + (((size_t)t * nh + (size_t)kvh * G + h) * kBtAttnSlots + slot) * (hd + 2);
+      if (e == 0) {
+        pp[0] = sml[h];
+        pp[1] = sml[kBtAttnMaxG + h];
+      }
+      pp[2 + e] = o[i];
+    }
   }
-  sum = warp_sum(sum);
-  __syncthreads();
-  if (lane == 0) red[32 + w] = sum;
-  __syncthreads();
-  sum = 0.0f;
-  for (int i = 0; i < nw; i++) sum += red[32 + i];
-  const float inv = 1.0f / sum;
-  // weighted V, element i per thread, positions in order
-  for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-    float acc = 0.0f;
-    for (int j = 0; j <= pos; j++)
-      acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(sc[j], inv), __fmul_rn((float)vc[(size_t)j * hd + i], vs[j])));
-    out[(size_t)t * qd + (size_t)h * hd + i] = acc;
+}
+
+// out[t][h][:] = sum_s e^(m_s - M) o_s / sum_s e^(m_s - M) l_s over the
+// slots that held positions (M = max m_s).
+__global__ void bt_attn_merge_kernel(const float* __restrict__ part, BatchTokens bt, int nh, int hd,
+                                     float* __restrict__ out) {
+  const int h = blockIdx.x, t = blockIdx.y, e = threadIdx.x;
+  const int pos = bt.pos[t];
+  const int ns = min(kBtAttnSlots, pos / kBtAttnChunk + 1);
+  const float* pp = part + ((size_t)t * nh + h) * kBtAttnSlots * (hd + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < ns; s++) M = fmaxf(M, pp[(size_t)s * (hd + 2)]);
+  float L = 0.0f, acc = 0.0f;
+  for (int s = 0; s < ns; s++) {
+    const float* ps = pp + (size_t)s * (hd + 2);
+    const float f = expf(ps[0] - M);
+    L = fmaf(ps[1], f, L);
+    if (e < hd) acc = fmaf(ps[2 + e], f, acc);
   }
+  if (e < hd) out[(size_t)t * nh * hd + (size_t)h * hd + e] = acc / L;
 }
 
 // h[t][r] += the product (layer_scheduler.c:484, :566).

@@ -25,17 +25,21 @@
 //   A (M = 128 rows x K = 32 per block): the block's weights as fp16, written
 //       by the math warps into shared memory in the UMMA canonical K-major
 //       layout (8-row x 16-byte core matrices);
-//   B (N = TP x K = 32, two pieces): the block's activation pieces, row t for
-//       token t (TP = T rounded up to 16; padding rows zero), already in the
-//       canonical layout in global memory (qg_pieces_kernel);
-//   D (128 lanes x TP columns of TMEM per block, fp32): four tcgen05.mma
-//       kind::f16 per block (two pieces x two K halves of 16).
-// A stage (KC blocks) is the unit of work of the math warps: they unpack its
-// blocks, one thread issues its 4 KC MMAs into one of two TMEM regions, and
-// while those run the warps flush the previous stage's region.
+//   B (N = 2 TP x K = 32): the block's activation pieces, rows 0..TP-1 the
+//       hi pieces of tokens 0..TP-1 and rows TP..2TP-1 their lo pieces (TP =
+//       T rounded up to 8, 16 or 32; padding rows zero), already in the
+//       canonical layout in global memory (qg_prep_kernel);
+//   D (128 lanes x 2 TP columns of TMEM per block, fp32): two tcgen05.mma
+//       kind::f16 per block (the two K halves of 16); column t holds token
+//       t's hi product, column TP + t its lo product, added at the flush.
+// A group (kQgGroup blocks) is the unit of work of the math warps: they
+// unpack its blocks into one of two A buffers, one elected lane issues its
+// MMAs into one of two TMEM regions, and while those run the warps flush the
+// previous group's region and unpack the next group.
 // Weights arrive by TMA (cp.async.bulk.tensor, 128-byte swizzle, no
-// multicast) into a ring of stages of KC blocks x 128 rows, with the pieces
-// of those blocks (cp.async.bulk) and the fp16 scales.
+// multicast) into a ring of stages of KC blocks x 128 rows (one or two
+// groups), with the pieces of those blocks (cp.async.bulk) and the fp16
+// scales.
 //
 // Work: units of (128-row tile, contiguous range of K chunks); a unit's
 // partial sums go to out[split][t][r] and the consumer of the product adds
@@ -49,12 +53,16 @@
 namespace ss {
 
 constexpr int kQgRows = 128;        // weight rows per tile (UMMA M)
-constexpr int kQgMaxT = 32;         // tokens per product (N = 3 * 32 = 96 at most)
+constexpr int kQgMaxT = 32;         // tokens per product (N = 2 * 32 = 64 at most)
 constexpr int kQgStages = 3;        // ring stages
 constexpr int kQgMathWarps = 16;    // four warpgroups: each covers all 128 TMEM lanes
 constexpr int kQgThreads = 32 * (1 + kQgMathWarps);
 constexpr int kQgABytes = kQgRows * 32 * 2;  // one block of A (fp16) in the canonical layout
-constexpr int kQgTmemCols = 512;    // D of two stages: 2 x KC blocks x TP (<= 32) columns
+constexpr int kQgGroup = 4;         // blocks per MMA group (A buffer, TMEM region)
+constexpr int kQgTmemCols = 512;    // two regions of kQgGroup blocks x 2 TP (<= 64) columns
+
+// Token rows per piece: T rounded up to 8, 16 or 32.
+__host__ __device__ constexpr int qg_tp(int T) { return T <= 8 ? 8 : T <= 16 ? 16 : 32; }
 
 // Blocks per stage: the TMA box's inner extent is 128 bytes (the 128-byte
 // swizzle span): 8 Q4_0 blocks of 16 quant bytes, 4 Q8_0 blocks of 32.
@@ -63,7 +71,7 @@ __host__ __device__ constexpr int qg_kc(int type) { return type == kQ4_0 ? 8 : 4
 struct QGemmParams {
   int rows, nb, type;
   int tiled;            // 1: tiled weight layout (4-row tiles), 0: row-interleaved
-  int T, TP;            // tokens; B rows per piece (T rounded up to 16)
+  int T, TP;            // tokens; B rows per piece (qg_tp(T))
   const __half* xq;     // [nb][2 pieces][TP][32] activation pieces, canonical K-major per block
   const float* post;    // [T]: the power of two each token's result is multiplied by
   float* out;           // [nsplit][T][rows] partial products
@@ -75,7 +83,7 @@ struct QGemmParams {
 };
 
 // Shared memory: [stages][quants 16 KB | scales 2 KB | pieces KC*2*TP*64]
-// [A: KC blocks][mbarriers][tmem address].
+// [A: 2 buffers x kQgGroup blocks][mbarriers][tmem address].
 struct QgSmem {
   static constexpr int kQuant = 16384;   // 128 rows x 128 bytes
   static constexpr int kScale = 2048;    // 128 rows x KC (<= 8) fp16
@@ -84,7 +92,7 @@ struct QgSmem {
     return (kQuant + kScale + plane_bytes(type, TP) + 1023) / 1024 * 1024;
   }
   __host__ __device__ static int total(int type, int TP) {
-    return 1024 /* alignment slack */ + kQgStages * stage_bytes(type, TP) + qg_kc(type) * kQgABytes + 256;
+    return 1024 /* alignment slack */ + kQgStages * stage_bytes(type, TP) + 2 * kQgGroup * kQgABytes + 256;
   }
 };
 
@@ -139,6 +147,12 @@ SS_DEVINL void umma_commit(uint32_t bar) {
                : "memory");
 }
 // 4 / 8 / 16 consecutive 32-bit TMEM columns of this thread's lane.
+SS_DEVINL void tmem_ld2(uint32_t taddr, int* v) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0,%1}, [%2];"
+               : "=r"(v[0]), "=r"(v[1])
+               : "r"(taddr)
+               : "memory");
+}
 SS_DEVINL void tmem_ld4(uint32_t taddr, int* v) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
@@ -204,72 +218,73 @@ SS_DEVINL bool qg_wait(uint32_t bar, uint32_t parity, const QGemmParams& p) {
 
 // ---- activation planes -----------------------------------------------------
 
-// Per token (one CTA each, one pass): with a norm, the RMSNorm scale
-// 1 / sqrtf(sum x^2 / n + eps) (cpu_neon.c:109-115); and the power of two
-// 2^-e that brings the token's largest input element (after the norm: the
-// largest |x * w| times the positive scale) near [1, 2): pre[t] = 2^-e,
-// post[t] = 2^e (a zero vector gets 1 and 1).  The pieces only need |x'| well
-// inside the fp16 range, so the exponent of the unrounded product is enough.
-__global__ void __launch_bounds__(512) qg_scale_kernel(const float* __restrict__ x, int n, int ld,
-                                                       const float* __restrict__ norm_w, float eps,
-                                                       float* __restrict__ scale, float* __restrict__ pre,
-                                                       float* __restrict__ post) {
+// Token t's activation pieces: CTA (t, slice) for token rows t < TP, each
+// slice writing a contiguous range of the blocks.  Every CTA of a token first
+// reduces the whole input row (the same values in the same order, so all
+// agree): with a norm, the RMSNorm scale 1 / sqrtf(sum x^2 / n + eps)
+// (cpu_neon.c:109-115); and the power of two 2^-e that brings the token's
+// largest input element (after the norm: the largest |x * w| times the
+// positive scale) near [1, 2): post[t] = 2^e undoes it at the end (a zero
+// vector gets 1).  The pieces only need |x'| well inside the fp16 range, so
+// the exponent of the unrounded product is enough.  Then each block of the
+// slice: x' = (x * scale * w) * 2^-e (or x * 2^-e without a norm), hi =
+// fp16(x'), lo = fp16(x' - hi), into B's canonical layout.  Rows t >= T
+// write zeros.
+__global__ void __launch_bounds__(512) qg_prep_kernel(const float* __restrict__ x, int n, int ld,
+                                                      const float* __restrict__ norm_w, float eps, int T, int TP,
+                                                      float* __restrict__ post, __half* __restrict__ xq) {
   __shared__ float red[64];
-  const float* xt = x + (size_t)blockIdx.x * ld;
-  float ss = 0.0f, amax = 0.0f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = xt[i];
-    ss = fmaf(v, v, ss);
-    amax = fmaxf(amax, fabsf(norm_w ? v * norm_w[i] : v));
-  }
-  ss = warp_sum(ss);
-  amax = warp_max(amax);
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  if (lane == 0) {
-    red[w] = ss;
-    red[32 + w] = amax;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float t = 0.0f, m = 0.0f;
-    for (int i = 0; i < nw; i++) {
-      t += red[i];
-      m = fmaxf(m, red[32 + i]);
-    }
-    const float sc = norm_w ? 1.0f / sqrtf(t / (float)n + eps) : 1.0f;
-    m *= sc;
-    int e = m >= 1.17549435e-38f ? (int)((__float_as_uint(m) >> 23) & 255u) - 127 : 0;
-    e = max(-126, min(126, e));
-    scale[blockIdx.x] = sc;
-    pre[blockIdx.x] = pow2i(-e);
-    post[blockIdx.x] = pow2i(e);
-  }
-}
-
-// Token t's block b as two fp16 pieces into B's canonical layout: one warp
-// per (token, block), lane j = element j.  x' = (x * scale * w) * pre (or
-// x * pre without a norm), hi = fp16(x'), lo = fp16(x' - hi).  Tokens in
-// [T, TP) write zeros.
-__global__ void __launch_bounds__(256) qg_pieces_kernel(const float* __restrict__ x, int ld, int nb,
-                                                        const float* __restrict__ norm_w,
-                                                        const float* __restrict__ scale,
-                                                        const float* __restrict__ pre, int T, int TP,
-                                                        __half* __restrict__ xq) {
-  const int lane = threadIdx.x & 31;
-  const int b = blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int t = blockIdx.y;
-  if (b >= nb) return;
-  float v = 0.0f;
+  __shared__ float s_sc, s_pre;
+  const int t = blockIdx.x;
+  const int nb = n >> 5;
+  const int b0 = (int)((long long)nb * blockIdx.y / gridDim.y), b1 = (int)((long long)nb * (blockIdx.y + 1) / gridDim.y);
+  const float* xt = x + (size_t)t * ld;
   if (t < T) {
-    v = x[(size_t)t * ld + b * 32 + lane];
-    if (norm_w) v = __fmul_rn(__fmul_rn(v, scale[t]), norm_w[b * 32 + lane]);
-    v = __fmul_rn(v, pre[t]);
+    float ss = 0.0f, amax = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const float v = xt[i];
+      ss = fmaf(v, v, ss);
+      amax = fmaxf(amax, fabsf(norm_w ? v * norm_w[i] : v));
+    }
+    ss = warp_sum(ss);
+    amax = warp_max(amax);
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (lane == 0) {
+      red[w] = ss;
+      red[32 + w] = amax;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float tot = 0.0f, m = 0.0f;
+      for (int i = 0; i < nw; i++) {
+        tot += red[i];
+        m = fmaxf(m, red[32 + i]);
+      }
+      const float sc = norm_w ? 1.0f / sqrtf(tot / (float)n + eps) : 1.0f;
+      m *= sc;
+      int e = m >= 1.17549435e-38f ? (int)((__float_as_uint(m) >> 23) & 255u) - 127 : 0;
+      e = max(-126, min(126, e));
+      s_sc = sc;
+      s_pre = pow2i(-e);
+      if (blockIdx.y == 0) post[t] = pow2i(e);
+    }
+    __syncthreads();
   }
-  const __half hi = __float2half_rn(v);
-  const __half lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
-  uint8_t* blk = reinterpret_cast<uint8_t*>(xq) + (size_t)b * 2 * TP * 64;
-  *reinterpret_cast<__half*>(blk + qg_canon16(t, lane)) = hi;
-  *reinterpret_cast<__half*>(blk + TP * 64 + qg_canon16(t, lane)) = lo;
+  const float sc = t < T ? s_sc : 0.0f, pre = t < T ? s_pre : 0.0f;
+  for (int i = b0 * 32 + threadIdx.x; i < b1 * 32; i += blockDim.x) {
+    const int b = i >> 5, k = i & 31;
+    float v = 0.0f;
+    if (t < T) {
+      v = xt[i];
+      if (norm_w) v = __fmul_rn(__fmul_rn(v, sc), norm_w[i]);
+      v = __fmul_rn(v, pre);
+    }
+    const __half hi = __float2half_rn(v);
+    const __half lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
+    uint8_t* blk = reinterpret_cast<uint8_t*>(xq) + (size_t)b * 2 * TP * 64;
+    *reinterpret_cast<__half*>(blk + qg_canon16(t, k)) = hi;
+    *reinterpret_cast<__half*>(blk + TP * 64 + qg_canon16(t, k)) = lo;
+  }
 }
 
 // ---- the product -----------------------------------------------------------
@@ -343,23 +358,27 @@ SS_DEVINL void q8_to_f16x8(uint32_t w0, uint32_t w1, uint32_t (&h)[4]) {
 }
 
 // Warp 0 (one lane) feeds the ring; warps 1..16 unpack A, issue the MMAs
-// (one thread) and flush D: warp w owns TMEM lanes 32 (w % 4) .. +31 (weight
-// rows), warpgroup g = (w - 1) / 4 unpacks elements 8 g .. 8 g + 7 of each
-// block (one core matrix) and flushes tokens g TP/4 .. (g + 1) TP/4 - 1.
-template <int TYPE>
+// (one elected lane of warp 1) and flush D: warp w owns TMEM lanes
+// 32 (w % 4) .. +31 (weight rows), warpgroup g = (w - 1) / 4 unpacks elements
+// 8 g .. 8 g + 7 of each block (one core matrix) and flushes tokens
+// g TP/4 .. (g + 1) TP/4 - 1.
+template <int TYPE, int TP>
 __global__ void __maxnreg__(96)
     qgemm_kernel(const QGemmParams p, const __grid_constant__ CUtensorMap qmap,
                  const __grid_constant__ CUtensorMap smap) {
   constexpr int KC = qg_kc(TYPE);
+  constexpr int G = kQgGroup;
+  constexpr int NG = KC / G;  // groups per stage
+  static_assert(KC % G == 0, "stage = whole groups");
+  static_assert(TP == 8 || TP == 16 || TP == 32, "token rows per piece");
   extern __shared__ uint8_t qg_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(qg_raw) + 1023) & ~(uintptr_t)1023);
-  const int TP = p.TP;
   const int SB = QgSmem::stage_bytes(TYPE, TP);
   const int PB = QgSmem::plane_bytes(TYPE, TP);
-  uint8_t* abuf = smem + kQgStages * SB;                           // KC x 8 KB
-  uint64_t* full = reinterpret_cast<uint64_t*>(abuf + KC * kQgABytes);
+  uint8_t* abuf = smem + kQgStages * SB;                           // 2 x G x 8 KB
+  uint64_t* full = reinterpret_cast<uint64_t*>(abuf + 2 * G * kQgABytes);
   uint64_t* empty = full + kQgStages;
-  uint64_t* dfull = empty + kQgStages;                             // [2]: MMAs of a stage done
+  uint64_t* dfull = empty + kQgStages;                             // [2]: MMAs of a group done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dfull + 2);
   __shared__ int s_abort;
 
@@ -422,48 +441,61 @@ __global__ void __maxnreg__(96)
   const int q = warp & 3;                 // TMEM lane quadrant of this warp
   const int r = 32 * q + lane;            // weight row within the tile
   const int g = (warp - 1) >> 2;          // warpgroup 0..3
-  const int th = TP >> 2;                 // tokens flushed per warpgroup (4 or 8)
-  const uint32_t idesc = umma_idesc_f16(kQgRows, TP);
+  constexpr int th = TP >> 2;             // tokens flushed per warpgroup (2, 4 or 8)
+  const uint32_t idesc = umma_idesc_f16(kQgRows, 2 * TP);
   const uint32_t t_lane = tmem + ((uint32_t)(32 * q) << 16);
   const bool issuer = warp == 1;   // the MMA-issuing warp (one elected lane issues)
-  float acc[8];
-  int sc = 0;        // stages consumed (= stages whose MMAs were issued) by this CTA
+  float acc[th];
+  int gc = 0;        // groups whose MMAs this CTA issued
+  int sc = 0;        // stages consumed
   bool bad = false;
-  int pend = -1;     // stage whose MMAs were issued and not yet flushed (its sc)
-  int pend_slot = 0;
+  bool okd = true;   // the last wait for a group's MMAs succeeded
+  int pend = -1;     // group whose MMAs were issued and not yet flushed (its gc)
+  int pend_slot = 0, pend_blk = 0;
+  bool pend_last = false;  // the pending group is its stage's last
   // this thread's quant bytes of a block: Q4_0 bytes 8 (g & 1) .. +7 (low
   // nibbles for g < 2, high for g >= 2); Q8_0 bytes 8 g .. 8 g + 7
   const int qchunk_off = TYPE == kQ4_0 ? 0 : (g >> 1);
   const uint32_t qbyte = (uint32_t)(8 * (g & 1));
-  const uint64_t adesc0 = umma_desc_kmajor(smem_addr(abuf));
 
-  // Flushes the pending stage: its D region (sc & 1), the scales of its ring
-  // slot; then releases the slot to the producer.
-  auto flush_stage = [&]() {
-    const uint32_t region = (uint32_t)((pend & 1) * KC * TP);
+  // Flushes the pending group: its TMEM region (pend & 1), the scales of its
+  // blocks; releases the ring slot after the stage's last group.
+  auto flush_group = [&]() {
+    const uint32_t region = (uint32_t)((pend & 1) * G * 2 * TP);
     const uint8_t* sst = smem + pend_slot * SB + QgSmem::kQuant;
+    constexpr int BW = th == 8 ? 2 : 4;  // blocks' loads in flight per wait
 #pragma unroll
-    for (int b0 = 0; b0 < KC; b0 += 4) {  // four blocks' loads in flight per wait
-      int v[4][8];
+    for (int b0 = 0; b0 < G; b0 += BW) {
+      int hv[BW][th], lv[BW][th];
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const uint32_t col = t_lane + region + (uint32_t)((b0 + j) * TP + g * th);
-        if (th == 8) tmem_ld8p(col, v[j]);
-        else tmem_ld4(col, v[j]);
+      for (int j = 0; j < BW; j++) {
+        const uint32_t col = t_lane + region + (uint32_t)((b0 + j) * 2 * TP + g * th);
+        if constexpr (th == 8) {
+          tmem_ld8p(col, hv[j]);
+          tmem_ld8p(col + (uint32_t)TP, lv[j]);
+        } else if constexpr (th == 4) {
+          tmem_ld4(col, hv[j]);
+          tmem_ld4(col + (uint32_t)TP, lv[j]);
+        } else {
+          tmem_ld2(col, hv[j]);
+          tmem_ld2(col + (uint32_t)TP, lv[j]);
+        }
       }
       tmem_ld_wait();
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
+      for (int j = 0; j < BW; j++) {
+        const int blk = pend_blk + b0 + j;
         const float d = half_bits_to_float(
-            *reinterpret_cast<const uint16_t*>(sst + (((r >> 2) * KC + b0 + j) * 4 + (r & 3)) * 2));
+            *reinterpret_cast<const uint16_t*>(sst + (((r >> 2) * KC + blk) * 4 + (r & 3)) * 2));
 #pragma unroll
-        for (int i = 0; i < 8; i++)
-          if (i < th) acc[i] = fmaf(__int_as_float(v[j][i]), d, acc[i]);
+        for (int i = 0; i < th; i++) acc[i] = fmaf(__int_as_float(hv[j][i]) + __int_as_float(lv[j][i]), d, acc[i]);
       }
     }
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(smem_addr(empty + pend_slot));
+    if (pend_last) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(empty + pend_slot));
+    }
     pend = -1;
   };
 
@@ -471,81 +503,92 @@ __global__ void __maxnreg__(96)
     int tile, split, c0, c1;
     qg_unit(p, u, tile, split, c0, c1);
 #pragma unroll
-    for (int i = 0; i < 8; i++) acc[i] = 0.0f;
-    for (int c = c0; c < c1; c++, sc++) {
+    for (int i = 0; i < th; i++) acc[i] = 0.0f;
+    for (int c = c0; c < c1 && !bad; c++, sc++) {
       const int s = sc % kQgStages;
-      bool ok = qg_wait(smem_addr(full + s), (uint32_t)((sc / kQgStages) & 1), p);
-      // A is free once the previous stage's MMAs are done (D also readable)
-      if (ok && pend >= 0) ok = qg_wait(smem_addr(dfull + (pend & 1)), (uint32_t)((pend >> 1) & 1), p);
+      const bool okf = qg_wait(smem_addr(full + s), (uint32_t)((sc / kQgStages) & 1), p);
       tc_fence_after();
       uint8_t* st = smem + s * SB;
       const uint32_t qrow = smem_addr(st) + (uint32_t)(r * 128);
-      if (ok) {
-        uint32_t w[KC][2];
+#pragma unroll 1
+      for (int h = 0; h < NG; h++) {
+        // A buffer (gc & 1) was last read by the MMAs of group gc - 2, which
+        // completed before group gc - 2 was flushed
+        uint8_t* ab = abuf + (gc & 1) * G * kQgABytes;
+        if (okf && okd) {
+          uint32_t w[G][2];
 #pragma unroll
-        for (int bl = 0; bl < KC; bl++) {
-          const int chunk = TYPE == kQ4_0 ? bl : 2 * bl + qchunk_off;
-          asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];"
-                       : "=r"(w[bl][0]), "=r"(w[bl][1])
-                       : "r"(qrow + ((chunk ^ (r & 7)) << 4) + qbyte));
+          for (int bl = 0; bl < G; bl++) {
+            const int chunk = TYPE == kQ4_0 ? h * G + bl : 2 * bl + qchunk_off;
+            asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];"
+                         : "=r"(w[bl][0]), "=r"(w[bl][1])
+                         : "r"(qrow + ((chunk ^ (r & 7)) << 4) + qbyte));
+          }
+#pragma unroll
+          for (int bl = 0; bl < G; bl++) {
+            uint32_t hh[4];
+            if constexpr (TYPE == kQ4_0) q4_to_f16x8(w[bl][0], w[bl][1], g >= 2, hh);
+            else q8_to_f16x8(w[bl][0], w[bl][1], hh);
+            const uint32_t a = smem_addr(ab + bl * kQgABytes) + (uint32_t)qg_canon16(r, 8 * g);
+            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(hh[0]), "r"(hh[1]), "r"(hh[2]),
+                         "r"(hh[3])
+                         : "memory");
+          }
         }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        bad = qg_any(!(okf && okd));  // every math thread has written its part of A
+        tc_fence_after();
+        if (bad) break;
+        if (issuer) {
+          const uint32_t dt = tmem + (uint32_t)((gc & 1) * G * 2 * TP);
+          const uint64_t adesc0 = umma_desc_kmajor(smem_addr(ab));
+          const uint64_t bdesc0 = umma_desc_kmajor(smem_addr(st + QgSmem::kQuant + QgSmem::kScale) +
+                                                   (uint32_t)(h * G * 2 * TP * 64));
+          // descriptor start addresses advance in 16-byte units
 #pragma unroll
-        for (int bl = 0; bl < KC; bl++) {
-          uint32_t h[4];
-          if constexpr (TYPE == kQ4_0) q4_to_f16x8(w[bl][0], w[bl][1], g >= 2, h);
-          else q8_to_f16x8(w[bl][0], w[bl][1], h);
-          const uint32_t a = smem_addr(abuf + bl * kQgABytes) + (uint32_t)qg_canon16(r, 8 * g);
-          asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(h[0]), "r"(h[1]), "r"(h[2]),
-                       "r"(h[3])
-                       : "memory");
-        }
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      bad = qg_any(!ok);  // every math thread has written its part of A
-      tc_fence_after();
-      if (bad) break;
-      if (issuer) {
-        const uint32_t dt = tmem + (uint32_t)((sc & 1) * KC * TP);
-        const uint64_t bdesc0 = umma_desc_kmajor(smem_addr(st + QgSmem::kQuant + QgSmem::kScale));
-        // descriptor start addresses advance in 16-byte units
-#pragma unroll
-        for (int bl = 0; bl < KC; bl++)
-#pragma unroll
-          for (int pc = 0; pc < 2; pc++)      // fp16 pieces hi, lo
+          for (int bl = 0; bl < G; bl++)
 #pragma unroll
             for (int kh = 0; kh < 2; kh++)    // K halves of 16
-              umma_f16(dt + (uint32_t)(bl * TP), adesc0 + (uint64_t)((bl * kQgABytes + 256 * kh) >> 4),
-                       bdesc0 + (uint64_t)((bl * 2 * TP * 64 + pc * TP * 64 + 256 * kh) >> 4), idesc,
-                       (pc | kh) ? 1u : 0u);
-        umma_commit(smem_addr(dfull + (sc & 1)));
+              umma_f16(dt + (uint32_t)(bl * 2 * TP), adesc0 + (uint64_t)((bl * kQgABytes + 256 * kh) >> 4),
+                       bdesc0 + (uint64_t)((bl * 2 * TP * 64 + 256 * kh) >> 4), idesc, kh ? 1u : 0u);
+          umma_commit(smem_addr(dfull + (gc & 1)));
+        }
+        // the previous group, while this group's MMAs run
+        if (pend >= 0) {
+          okd = qg_wait(smem_addr(dfull + (pend & 1)), (uint32_t)((pend >> 1) & 1), p);
+          tc_fence_after();
+          flush_group();
+        }
+        pend = gc;
+        pend_slot = s;
+        pend_blk = h * G;
+        pend_last = h == NG - 1;
+        gc++;
       }
-      // the previous stage, while this stage's MMAs run
-      if (pend >= 0) flush_stage();
-      pend = sc;
-      pend_slot = s;
     }
     if (bad) break;
-    // the unit's last stage, then its partial sums
-    bool ok = qg_wait(smem_addr(dfull + (pend & 1)), (uint32_t)((pend >> 1) & 1), p);
-    bad = qg_any(!ok);
+    // the unit's last group, then its partial sums
+    const bool ok = qg_wait(smem_addr(dfull + (pend & 1)), (uint32_t)((pend >> 1) & 1), p);
+    bad = qg_any(!(ok && okd));
     if (bad) break;
     tc_fence_after();
-    flush_stage();
+    flush_group();
     const int row = tile * kQgRows + r;
     if (row < p.rows) {
 #pragma unroll
-      for (int i = 0; i < 8; i++) {
+      for (int i = 0; i < th; i++) {
         const int t = g * th + i;
-        if (i < th && t < p.T) p.out[((size_t)split * p.T + t) * p.rows + row] = acc[i] * p.post[t];
+        if (t < p.T) p.out[((size_t)split * p.T + t) * p.rows + row] = acc[i] * p.post[t];
       }
     }
   }
   if (bad && tid == 32) {
     s_abort = 1;
     // no MMA may still write TMEM when it is freed: wait for the last commit
-    if (pend >= 0)
-      mbar_wait_bounded(smem_addr(dfull + (pend & 1)), (uint32_t)((pend >> 1) & 1), p.wait_budget);
+    const int last = gc - 1;
+    if (last >= 0)
+      mbar_wait_bounded(smem_addr(dfull + (last & 1)), (uint32_t)((last >> 1) & 1), p.wait_budget);
   }
   tc_fence_before();
   named_bar_sync(1, 32 * kQgMathWarps);

@@ -103,6 +103,7 @@ struct Context {
   unsigned long long* bt_best = nullptr;  // [32]: packed greedy choice
   int* bt_ids = nullptr;                   // [ctx + 1][32]: batched greedy tokens by position
   float* bt_emb = nullptr;                 // [d] embedding sum | [d] result | [32] norm scales
+  float* bt_apart = nullptr;               // attention partials [32][nh][slots][hd + 2]
   bool bt_ready = false;                   // scratch reserved for 32 tokens, tensor maps built
   // captured many-token steps: key 2 * T + (head of the last token only);
   // bt_dev_exec is the single-sequence step that reads its token and position
