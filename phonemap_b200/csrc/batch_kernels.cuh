@@ -12,10 +12,18 @@
 // token's own cache rows (bt_attn_kernel) -> O product + residual -> RMSNorm
 // -> gate/up product -> SwiGLU -> down product + residual.  The products
 // leave per-split partial sums; each consumer below adds them in split order.
+// The elementwise steps between products (residual add, SwiGLU, the merge of
+// the attention slots) run inside the next product's activation prep
+// (bt_prep_kernel), so a layer is 9 kernels.  Every kernel here waits for its
+// predecessor with griddepcontrol (programmatic dependent launch) before it
+// touches global memory, and lets its successor launch at once.
 #pragma once
+#include <cooperative_groups.h>
+
 #include "attention.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
+#include "qgemm.cuh"
 
 namespace ss {
 
@@ -47,8 +55,13 @@ SS_DEVINL float split_sum(const float* part, int nsplit, size_t n, size_t i) {
 // h[t] = token_embd[tok[t]] (layer_scheduler.c:584-587); tokens outside the
 // vocabulary set error bit 2 and read row 0.
 __global__ void bt_embed_kernel(const float* __restrict__ embd, int d, int vocab, BatchTokens bt, int T,
-                                float* __restrict__ h, int* err) {
+                                float* __restrict__ h, int* err, unsigned* __restrict__ zero, int nzero) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.y;
+  // the pass's K/V maxima and greedy-choice words start at zero
+  if (t == 0 && blockIdx.x == 0)
+    for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0u;
   int tok = bt.tok[t];
   if (tok < 0 || tok >= vocab) {
     if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(err, 2);
@@ -67,6 +80,8 @@ __global__ void bt_embed_kernel(const float* __restrict__ embd, int d, int vocab
 __global__ void bt_qkv_kernel(const float* __restrict__ part, int nsplit, int T, int rows, int qd, int kvd,
                               int hd, int rope_dim, const float2* __restrict__ rope_tab, BatchTokens bt,
                               float* __restrict__ qout, float* __restrict__ kvtmp, unsigned* __restrict__ amax) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.y;
   const int pr = blockIdx.x * blockDim.x + threadIdx.x;
   const int r = 2 * pr;
@@ -108,6 +123,8 @@ __global__ void bt_qkv_kernel(const float* __restrict__ part, int nsplit, int T,
 // layer_scheduler.c:101-118: scale = max / 127, q = roundf(v / scale)).
 __global__ void bt_kv_encode_kernel(const float* __restrict__ kvtmp, const unsigned* __restrict__ amax, int kvd,
                                     int hd, BatchTokens bt, BatchKv kv, int layer) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.y;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   const int pos = bt.pos[t], seq = bt.seq[t];
@@ -133,26 +150,42 @@ __global__ void bt_kv_encode_kernel(const float* __restrict__ kvtmp, const unsig
 // kBtAttnChunk cached positions s, s + kBtAttnSlots, ... up to pos, for the G
 // query heads that share the kv head.  Per chunk: the int8 K and V rows and
 // their scales are staged in shared memory (coalesced 16-byte loads), scores
-// s_j = (q . k_j) * k_scale_j * (1/sqrt(hd)), then a running softmax (max m,
-// sum l, output o rescaled when m grows).  The slot's (m, l, o) go to `part`;
-// bt_attn_merge_kernel combines the slots.  The result equals the
-// reference's softmax-weighted sum of dec(V_j) up to fp32 rounding order.
+// s_j = (q . k_j) * k_scale_j * (1/sqrt(hd)) (two threads per position, each
+// K value converted once for all G heads), then a running softmax (max m, sum
+// l, output o rescaled when m grows) and o += p_j v_scale_j v_j (each thread
+// four elements of a group of positions).  The slot's (m, l, o) go to `part`;
+// the O product's prep merges the slots.  The result equals the reference's
+// softmax-weighted sum of dec(V_j) up to fp32 rounding order.
 constexpr int kBtAttnChunk = 128;   // positions per chunk
 constexpr int kBtAttnSlots = 16;    // position slots (CTAs) per (kv head, token)
 constexpr int kBtAttnMaxG = 8;      // query heads per kv head
+constexpr int kBtAttnThreads = 256;
 
 __host__ __device__ constexpr size_t bt_attn_smem(int hd, int G) {
   // q[G][hd] | scores[G][chunk] | k scale, v scale [chunk] | m, l, corr [G]
-  // | K chunk, V chunk [chunk][hd] int8
+  // | K chunk, V chunk [chunk][hd] int8 (after the last chunk: the position
+  // groups' partial outputs [threads / (hd / 4)][G][hd] fp32)
   return (size_t)(G * hd + G * kBtAttnChunk + 2 * kBtAttnChunk + 4 * kBtAttnMaxG) * sizeof(float) +
-         (size_t)2 * kBtAttnChunk * hd;
+         ((size_t)2 * kBtAttnChunk * hd > (size_t)4096 * G ? (size_t)2 * kBtAttnChunk * hd : (size_t)4096 * G);
+}
+
+// Four signed bytes as floats, exactly: byte ^ 0x80 (in [0, 255]) in the low
+// mantissa bits of 2^23, minus 2^23 + 128.
+SS_DEVINL void s8x4_to_f32(uint32_t w, float* f) {
+  const uint32_t u = w ^ 0x80808080u;
+  f[0] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - 8388736.0f;
+  f[1] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - 8388736.0f;
+  f[2] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - 8388736.0f;
+  f[3] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - 8388736.0f;
 }
 
 // part layout: [T][nh][slots][hd + 2]: m, l, then o[hd].
-__global__ void __launch_bounds__(256) bt_attn_kernel(const float* __restrict__ q, BatchTokens bt, BatchKv kv,
-                                                      int layer, int nh, int nkv, int hd, float scale,
-                                                      float* __restrict__ part) {
+__global__ void __launch_bounds__(kBtAttnThreads) bt_attn_kernel(const float* __restrict__ q, BatchTokens bt,
+                                                                 BatchKv kv, int layer, int nh, int nkv, int hd,
+                                                                 float scale, float* __restrict__ part) {
   extern __shared__ float sm[];
+  pdl_wait();
+  pdl_trigger();
   const int kvh = blockIdx.x, t = blockIdx.y, slot = blockIdx.z;
   const int pos = bt.pos[t], seq = bt.seq[t];
   if (slot * kBtAttnChunk > pos) return;  // no chunk for this slot (the merge skips it)
@@ -164,7 +197,8 @@ __global__ void __launch_bounds__(256) bt_attn_kernel(const float* __restrict__ 
   float* sml = svs + kBtAttnChunk;              // m[G] | l[G] | corr[G] | pad
   int8_t* sk = reinterpret_cast<int8_t*>(sml + 4 * kBtAttnMaxG);
   int8_t* sv = sk + kBtAttnChunk * hd;
-  const int tid = threadIdx.x, nt = blockDim.x;
+  float* red = reinterpret_cast<float*>(sk);    // after the last chunk
+  const int tid = threadIdx.x, nt = kBtAttnThreads;
   for (int i = tid; i < G * hd; i += nt) qs[i] = q[(size_t)t * qd + (size_t)kvh * G * hd + i];
   if (tid < G) {
     sml[tid] = -INFINITY;
@@ -175,12 +209,15 @@ __global__ void __launch_bounds__(256) bt_attn_kernel(const float* __restrict__ 
   const int8_t* vc = kv.vc + lbase;
   const float* ks = kv.ks + seq * kv.sc_stride + (size_t)layer * kv.ctx;
   const float* vs = kv.vs + seq * kv.sc_stride + (size_t)layer * kv.ctx;
-  // output elements of this thread: element e of heads hb, hb + hs, ...
-  const int e = tid % hd, hb = tid / hd, hs = nt / hd;  // hd divides 256 (hd <= 256, power of two)
-  float o[kBtAttnMaxG];
+  // PV mapping: element quad eq, position group pg
+  const int nq = hd >> 2, eq = tid % nq, pg = tid / nq, npg = nt / nq;
+  float o[kBtAttnMaxG][4];
 #pragma unroll
-  for (int i = 0; i < kBtAttnMaxG; i++) o[i] = 0.0f;
+  for (int h = 0; h < kBtAttnMaxG; h++)
+#pragma unroll
+    for (int k = 0; k < 4; k++) o[h][k] = 0.0f;
   const int vec = hd / 16;
+  const int half = hd >> 1;
   for (int ch = slot; ch * kBtAttnChunk <= pos; ch += kBtAttnSlots) {
     const int c0 = ch * kBtAttnChunk, cn = min(kBtAttnChunk, pos + 1 - c0);
     __syncthreads();  // the previous chunk is consumed (and q, m, l are set)
@@ -193,19 +230,42 @@ __global__ void __launch_bounds__(256) bt_attn_kernel(const float* __restrict__ 
       svs[k] = vs[c0 + k];
     }
     __syncthreads();
-    // scores of (head, position) pairs
-    for (int idx = tid; idx < G * cn; idx += nt) {
-      const int h = idx / cn, j = idx - h * cn;
-      const float* qh = qs + h * hd;
-      const int8_t* kr = sk + j * hd;
-      float dot = 0.0f;
-      for (int i = 0; i < hd; i += 16) {
-        const int4 kw = *reinterpret_cast<const int4*>(kr + i);
-        const int8_t* kb = reinterpret_cast<const int8_t*>(&kw);
+    // scores: thread pair (2j, 2j+1) takes position j, one half of hd each
+    for (int j0 = 0; j0 < cn; j0 += nt / 2) {
+      const int j = j0 + (tid >> 1), hf = tid & 1;
+      const int jr = min(j, cn - 1);  // past the chunk: a duplicate, not stored
+      float dot[kBtAttnMaxG];
 #pragma unroll
-        for (int u = 0; u < 16; u++) dot = fmaf(qh[i + u], (float)kb[u], dot);
+      for (int h = 0; h < kBtAttnMaxG; h++) dot[h] = 0.0f;
+      const int8_t* kr = sk + jr * hd + hf * half;
+      for (int i = 0; i < half; i += 16) {
+        const uint4 kw = *reinterpret_cast<const uint4*>(kr + i);
+        float kf[16];
+        s8x4_to_f32(kw.x, kf);
+        s8x4_to_f32(kw.y, kf + 4);
+        s8x4_to_f32(kw.z, kf + 8);
+        s8x4_to_f32(kw.w, kf + 12);
+#pragma unroll
+        for (int h = 0; h < kBtAttnMaxG; h++) {
+          if (h < G) {
+            const float4* qv = reinterpret_cast<const float4*>(qs + h * hd + hf * half + i);
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+              const float4 qq = qv[u];
+              dot[h] = fmaf(qq.x, kf[4 * u], dot[h]);
+              dot[h] = fmaf(qq.y, kf[4 * u + 1], dot[h]);
+              dot[h] = fmaf(qq.z, kf[4 * u + 2], dot[h]);
+              dot[h] = fmaf(qq.w, kf[4 * u + 3], dot[h]);
+            }
+          }
+        }
       }
-      sc[h * kBtAttnChunk + j] = dot * sks[j] * scale;
+#pragma unroll
+      for (int h = 0; h < kBtAttnMaxG; h++) dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], 1);
+      if (hf == 0 && j < cn)
+#pragma unroll
+        for (int h = 0; h < kBtAttnMaxG; h++)
+          if (h < G) sc[h * kBtAttnChunk + j] = dot[h] * sks[j] * scale;
     }
     __syncthreads();
     // running softmax per head: warp h (G <= 8 warps)
@@ -232,75 +292,214 @@ __global__ void __launch_bounds__(256) bt_attn_kernel(const float* __restrict__ 
       }
     }
     __syncthreads();
-    // o = o * corr + sum_j w_j v_j
+    // o = o * corr + sum_j w_j v_j over this thread's positions
 #pragma unroll
-    for (int i = 0; i < kBtAttnMaxG; i++) {
-      const int h = hb + i * hs;
-      if (h < G) o[i] *= sml[2 * kBtAttnMaxG + h];
+    for (int h = 0; h < kBtAttnMaxG; h++) {
+      if (h < G) {
+        const float cr = sml[2 * kBtAttnMaxG + h];
+#pragma unroll
+        for (int k = 0; k < 4; k++) o[h][k] *= cr;
+      }
     }
-    for (int j = 0; j < cn; j++) {
-      const float v = (float)sv[j * hd + e];
+    for (int j = pg; j < cn; j += npg) {
+      float vf[4];
+      s8x4_to_f32(*reinterpret_cast<const uint32_t*>(sv + j * hd + 4 * eq), vf);
 #pragma unroll
-      for (int i = 0; i < kBtAttnMaxG; i++) {
-        const int h = hb + i * hs;
-        if (h < G) o[i] = fmaf(sc[h * kBtAttnChunk + j], v, o[i]);
+      for (int h = 0; h < kBtAttnMaxG; h++) {
+        if (h < G) {
+          const float wj = sc[h * kBtAttnChunk + j];
+#pragma unroll
+          for (int k = 0; k < 4; k++) o[h][k] = fmaf(wj, vf[k], o[h][k]);
+        }
       }
     }
   }
+  __syncthreads();  // the staging area becomes the position groups' partials
+#pragma unroll
+  for (int h = 0; h < kBtAttnMaxG; h++)
+    if (h < G)
+      *reinterpret_cast<float4*>(red + ((size_t)pg * G + h) * hd + 4 * eq) = make_float4(o[h][0], o[h][1], o[h][2], o[h][3]);
   __syncthreads();
-#pragma unroll
-  for (int i = 0; i < kBtAttnMaxG; i++) {
-    const int h = hb + i * hs;
-    if (h < G) {
-      float* pp = part + (((size_t)t * nh + (size_t)kvh * G + h) * kBtAttnSlots + slot) * (hd + 2);
-      if (e == 0) {
-        pp[0] = sml[h];
-        pp[1] = sml[kBtAttnMaxG + h];
+  for (int idx = tid; idx < G * hd; idx += nt) {
+    const int h = idx / hd, e = idx - h * hd;
+    float acc = 0.0f;
+    for (int g2 = 0; g2 < npg; g2++) acc += red[((size_t)g2 * G + h) * hd + e];
+    float* pp = part + (((size_t)t * nh + (size_t)kvh * G + h) * kBtAttnSlots + slot) * (hd + 2);
+    if (e == 0) {
+      pp[0] = sml[h];
+      pp[1] = sml[kBtAttnMaxG + h];
+    }
+    pp[2 + e] = acc;
+  }
+}
+
+// ---- activation prep of a product, fused with the elementwise step before it
+
+enum PrepMode : int {
+  kPrepPlain = 0,   // x = the input row
+  kPrepResid = 1,   // x = h + the previous product (residual add, layer_scheduler.c:484, :566);
+                    //     the new h is also written out
+  kPrepSwiGLU = 2,  // x = up * (g / (1 + expf(-g))) of the gate/up product (layer_scheduler.c:533-549)
+  kPrepMerge = 3,   // x = the attention output, merged from the position slots
+};
+
+constexpr int kPrepMaxHeads = 128;  // query heads of one token (merge factors in shared memory)
+
+struct PrepParams {
+  const float* x;       // Plain, Resid: token t's row at x + (t + toff) * ld
+  int ld;
+  int n;                // elements per token (the product's columns)
+  const float* norm_w;  // RMSNorm weight (nullptr: none)
+  float eps;
+  int T, TP, toff;      // tokens; B rows per piece; first source row
+  float* post;          // [T]: the power of two each token's result is multiplied by
+  __half* xq;           // the pieces, [nb][2][TP][32] canonical per block
+  const float* part;    // Resid, SwiGLU: the previous product's partials [nsplit][ptok][prow]
+  int nsplit, ptok, prow;
+  float* h_out;         // Resid: the new residual stream (same row layout as x)
+  const float* apart;   // Merge: attention slots [ptok][nh][slots][hd + 2]
+  BatchTokens bt;
+  int nh, hd;
+};
+
+template <int MODE>
+SS_DEVINL float prep_elem(const PrepParams& p, int tr, int i, const float* mf, const float* minv) {
+  if constexpr (MODE == kPrepPlain) {
+    return p.x[(size_t)tr * p.ld + i];
+  } else if constexpr (MODE == kPrepResid) {
+    const size_t n = (size_t)p.ptok * p.prow;
+    return __fadd_rn(split_sum(p.part, p.nsplit, n, (size_t)tr * p.prow + i), p.x[(size_t)tr * p.ld + i]);
+  } else if constexpr (MODE == kPrepSwiGLU) {
+    const size_t n = (size_t)p.ptok * p.prow;
+    const float g = split_sum(p.part, p.nsplit, n, (size_t)tr * p.prow + 2 * i);
+    const float u = split_sum(p.part, p.nsplit, n, (size_t)tr * p.prow + 2 * i + 1);
+    return __fmul_rn(u, __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+  } else {
+    const int h = i / p.hd, e = i - h * p.hd;
+    const int ns = min(kBtAttnSlots, p.bt.pos[tr] / kBtAttnChunk + 1);
+    const float* pp = p.apart + ((size_t)tr * p.nh + h) * kBtAttnSlots * (p.hd + 2) + 2 + e;
+    float acc = 0.0f;
+#pragma unroll 1
+    for (int s2 = 0; s2 < ns; s2++) acc = fmaf(pp[(size_t)s2 * (p.hd + 2)], mf[h * kBtAttnSlots + s2], acc);
+    return acc * minv[h];
+  }
+}
+
+// The activation pieces of a product (numerics in qgemm.cuh): a cluster of
+// kPrepSlices CTAs per token row t < TP, CTA k computing the mode's values of
+// slice k of the row (contiguous blocks) once, into shared memory, with its
+// partial sum of squares and largest |x * w|; the partials meet through
+// distributed shared memory (added in rank order, so every CTA of the token
+// gets the same RMSNorm scale and power of two); then each CTA writes its
+// slice's pieces (Resid: and the new h).  Rows t >= T write zero pieces.
+constexpr int kPrepSlices = 8;         // CTAs per token (the cluster)
+constexpr int kPrepMaxSlice = 4096;    // elements per slice (rows up to 32768)
+
+template <int MODE>
+__global__ void __launch_bounds__(512) bt_prep_kernel(const PrepParams p) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  __shared__ float vals[kPrepMaxSlice];
+  __shared__ float red[64];
+  __shared__ float s_part[2];  // this CTA's sum of squares, max |x * w|
+  __shared__ float mf[MODE == kPrepMerge ? kPrepMaxHeads * kBtAttnSlots : 1];
+  __shared__ float minv[MODE == kPrepMerge ? kPrepMaxHeads : 1];
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x, tr = t + p.toff;
+  const int slice = (int)cluster.block_rank();
+  const int nb = p.n >> 5;
+  const int b0 = (int)((long long)nb * slice / kPrepSlices), b1 = (int)((long long)nb * (slice + 1) / kPrepSlices);
+  const int i0 = b0 * 32, i1 = b1 * 32;
+  const bool live = t < p.T;
+  if (live) {
+    if constexpr (MODE == kPrepMerge) {
+      // per head of the slice: M = max m_s, f_s = e^(m_s - M), 1 / sum_s f_s l_s
+      const int ns = min(kBtAttnSlots, p.bt.pos[tr] / kBtAttnChunk + 1);
+      const int h0 = i0 / p.hd, h1 = (i1 + p.hd - 1) / p.hd;
+      for (int h = h0 + (int)threadIdx.x; h < h1; h += blockDim.x) {
+        const float* pp = p.apart + ((size_t)tr * p.nh + h) * kBtAttnSlots * (p.hd + 2);
+        float M = -INFINITY;
+        for (int s2 = 0; s2 < ns; s2++) M = fmaxf(M, pp[(size_t)s2 * (p.hd + 2)]);
+        float L = 0.0f;
+        for (int s2 = 0; s2 < ns; s2++) {
+          const float f = expf(pp[(size_t)s2 * (p.hd + 2)] - M);
+          mf[h * kBtAttnSlots + s2] = f;
+          L = fmaf(pp[(size_t)s2 * (p.hd + 2) + 1], f, L);
+        }
+        minv[h] = 1.0f / L;
       }
-      pp[2 + e] = o[i];
+      __syncthreads();
+    }
+    float ss = 0.0f, amax = 0.0f;
+#pragma unroll 1
+    for (int i = i0 + (int)threadIdx.x; i < i1; i += blockDim.x) {
+      const float v = prep_elem<MODE>(p, tr, i, mf, minv);
+      vals[i - i0] = v;
+      ss = fmaf(v, v, ss);
+      amax = fmaxf(amax, fabsf(p.norm_w ? v * p.norm_w[i] : v));
+    }
+    ss = warp_sum(ss);
+    amax = warp_max(amax);
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (lane == 0) {
+      red[w] = ss;
+      red[32 + w] = amax;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float tot = 0.0f, m = 0.0f;
+      for (int i = 0; i < nw; i++) {
+        tot += red[i];
+        m = fmaxf(m, red[32 + i]);
+      }
+      s_part[0] = tot;
+      s_part[1] = m;
     }
   }
-}
-
-// out[t][h][:] = sum_s e^(m_s - M) o_s / sum_s e^(m_s - M) l_s over the
-// slots that held positions (M = max m_s).
-__global__ void bt_attn_merge_kernel(const float* __restrict__ part, BatchTokens bt, int nh, int hd,
-                                     float* __restrict__ out) {
-  const int h = blockIdx.x, t = blockIdx.y, e = threadIdx.x;
-  const int pos = bt.pos[t];
-  const int ns = min(kBtAttnSlots, pos / kBtAttnChunk + 1);
-  const float* pp = part + ((size_t)t * nh + h) * kBtAttnSlots * (hd + 2);
-  float M = -INFINITY;
-  for (int s = 0; s < ns; s++) M = fmaxf(M, pp[(size_t)s * (hd + 2)]);
-  float L = 0.0f, acc = 0.0f;
-  for (int s = 0; s < ns; s++) {
-    const float* ps = pp + (size_t)s * (hd + 2);
-    const float f = expf(ps[0] - M);
-    L = fmaf(ps[1], f, L);
-    if (e < hd) acc = fmaf(ps[2 + e], f, acc);
+  cluster.sync();  // every slice's partials are in place
+  float sc = 0.0f, pre = 0.0f;
+  if (live) {
+    float tot = 0.0f, m = 0.0f;
+    for (int r = 0; r < kPrepSlices; r++) {
+      const float* rp = cluster.map_shared_rank(s_part, r);
+      tot += rp[0];
+      m = fmaxf(m, rp[1]);
+    }
+    sc = p.norm_w ? 1.0f / sqrtf(tot / (float)p.n + p.eps) : 1.0f;
+    m *= sc;
+    int e = m >= 1.17549435e-38f ? (int)((__float_as_uint(m) >> 23) & 255u) - 127 : 0;
+    e = max(-126, min(126, e));
+    pre = pow2i(-e);
+    if (slice == 0 && threadIdx.x == 0) p.post[t] = pow2i(e);
   }
-  if (e < hd) out[(size_t)t * nh * hd + (size_t)h * hd + e] = acc / L;
+  cluster.sync();  // no CTA leaves while another still reads its partials
+  for (int i = i0 + (int)threadIdx.x; i < i1; i += blockDim.x) {
+    const int b = i >> 5, k = i & 31;
+    float v = 0.0f;
+    if (live) {
+      v = vals[i - i0];
+      if constexpr (MODE == kPrepResid) p.h_out[(size_t)tr * p.ld + i] = v;
+      if (p.norm_w) v = __fmul_rn(__fmul_rn(v, sc), p.norm_w[i]);
+      v = __fmul_rn(v, pre);
+    }
+    const __half hi = __float2half_rn(v);
+    const __half lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
+    uint8_t* blk = reinterpret_cast<uint8_t*>(p.xq) + (size_t)b * 2 * p.TP * 64;
+    *reinterpret_cast<__half*>(blk + qg_canon16(t, k)) = hi;
+    *reinterpret_cast<__half*>(blk + p.TP * 64 + qg_canon16(t, k)) = lo;
+  }
 }
 
-// h[t][r] += the product (layer_scheduler.c:484, :566).
+// h[t][r] = the product + h (the last residual add of a pass whose final
+// hidden states are needed without the lm_head: the embedding).
 __global__ void bt_residual_kernel(const float* __restrict__ part, int nsplit, int T, int rows,
-                                   float* __restrict__ h) {
+                                   const float* __restrict__ h, float* __restrict__ h_out) {
+  pdl_wait();
+  pdl_trigger();
   const size_t n = (size_t)T * rows;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-    h[i] = __fadd_rn(split_sum(part, nsplit, n, i), h[i]);
-}
-
-// act[t][j] = up * (g / (1 + expf(-g))) (layer_scheduler.c:533-549); the
-// gate/up matrix interleaves gate (even rows) and up (odd rows).
-__global__ void bt_swiglu_kernel(const float* __restrict__ part, int nsplit, int T, int ff,
-                                 float* __restrict__ act) {
-  const size_t n = (size_t)T * 2 * ff, m = (size_t)T * ff;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < m; i += (size_t)gridDim.x * blockDim.x) {
-    const size_t t = i / ff, j = i - t * ff;
-    const float g = split_sum(part, nsplit, n, t * 2 * ff + 2 * j);
-    const float u = split_sum(part, nsplit, n, t * 2 * ff + 2 * j + 1);
-    act[i] = __fmul_rn(u, __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
-  }
+    h_out[i] = __fadd_rn(split_sum(part, nsplit, n, i), h[i]);
 }
 
 // Logits of token t (the product's split sums) and the packed (value,
@@ -308,6 +507,8 @@ __global__ void bt_swiglu_kernel(const float* __restrict__ part, int nsplit, int
 // best[t] by atomicMax -- order-independent, so deterministic.
 __global__ void bt_head_kernel(const float* __restrict__ part, int nsplit, int T, int vocab,
                                float* __restrict__ logits, unsigned long long* __restrict__ best) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.y;
   const size_t n = (size_t)T * vocab;
   unsigned long long b = 0;
@@ -327,6 +528,8 @@ __global__ void bt_head_kernel(const float* __restrict__ part, int nsplit, int T
 
 // next[t] = the index in best[t] (index 0 when nothing was packed).
 __global__ void bt_token_kernel(const unsigned long long* __restrict__ best, int T, int* __restrict__ next) {
+  pdl_wait();
+  pdl_trigger();
   const int t = threadIdx.x;
   if (t < T) next[t] = best[t] == 0 ? 0 : unpack_argmax_index(best[t]);
 }

@@ -28,7 +28,7 @@
 //   B (N = 2 TP x K = 32): the block's activation pieces, rows 0..TP-1 the
 //       hi pieces of tokens 0..TP-1 and rows TP..2TP-1 their lo pieces (TP =
 //       T rounded up to 8, 16 or 32; padding rows zero), already in the
-//       canonical layout in global memory (qg_prep_kernel);
+//       canonical layout in global memory (bt_prep_kernel);
 //   D (128 lanes x 2 TP columns of TMEM per block, fp32): two tcgen05.mma
 //       kind::f16 per block (the two K halves of 16); column t holds token
 //       t's hi product, column TP + t its lo product, added at the flush.
@@ -218,74 +218,11 @@ SS_DEVINL bool qg_wait(uint32_t bar, uint32_t parity, const QGemmParams& p) {
 
 // ---- activation planes -----------------------------------------------------
 
-// Token t's activation pieces: CTA (t, slice) for token rows t < TP, each
-// slice writing a contiguous range of the blocks.  Every CTA of a token first
-// reduces the whole input row (the same values in the same order, so all
-// agree): with a norm, the RMSNorm scale 1 / sqrtf(sum x^2 / n + eps)
-// (cpu_neon.c:109-115); and the power of two 2^-e that brings the token's
-// largest input element (after the norm: the largest |x * w| times the
-// positive scale) near [1, 2): post[t] = 2^e undoes it at the end (a zero
-// vector gets 1).  The pieces only need |x'| well inside the fp16 range, so
-// the exponent of the unrounded product is enough.  Then each block of the
-// slice: x' = (x * scale * w) * 2^-e (or x * 2^-e without a norm), hi =
-// fp16(x'), lo = fp16(x' - hi), into B's canonical layout.  Rows t >= T
-// write zeros.
-__global__ void __launch_bounds__(512) qg_prep_kernel(const float* __restrict__ x, int n, int ld,
-                                                      const float* __restrict__ norm_w, float eps, int T, int TP,
-                                                      float* __restrict__ post, __half* __restrict__ xq) {
-  __shared__ float red[64];
-  __shared__ float s_sc, s_pre;
-  const int t = blockIdx.x;
-  const int nb = n >> 5;
-  const int b0 = (int)((long long)nb * blockIdx.y / gridDim.y), b1 = (int)((long long)nb * (blockIdx.y + 1) / gridDim.y);
-  const float* xt = x + (size_t)t * ld;
-  if (t < T) {
-    float ss = 0.0f, amax = 0.0f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      const float v = xt[i];
-      ss = fmaf(v, v, ss);
-      amax = fmaxf(amax, fabsf(norm_w ? v * norm_w[i] : v));
-    }
-    ss = warp_sum(ss);
-    amax = warp_max(amax);
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    if (lane == 0) {
-      red[w] = ss;
-      red[32 + w] = amax;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float tot = 0.0f, m = 0.0f;
-      for (int i = 0; i < nw; i++) {
-        tot += red[i];
-        m = fmaxf(m, red[32 + i]);
-      }
-      const float sc = norm_w ? 1.0f / sqrtf(tot / (float)n + eps) : 1.0f;
-      m *= sc;
-      int e = m >= 1.17549435e-38f ? (int)((__float_as_uint(m) >> 23) & 255u) - 127 : 0;
-      e = max(-126, min(126, e));
-      s_sc = sc;
-      s_pre = pow2i(-e);
-      if (blockIdx.y == 0) post[t] = pow2i(e);
-    }
-    __syncthreads();
-  }
-  const float sc = t < T ? s_sc : 0.0f, pre = t < T ? s_pre : 0.0f;
-  for (int i = b0 * 32 + threadIdx.x; i < b1 * 32; i += blockDim.x) {
-    const int b = i >> 5, k = i & 31;
-    float v = 0.0f;
-    if (t < T) {
-      v = xt[i];
-      if (norm_w) v = __fmul_rn(__fmul_rn(v, sc), norm_w[i]);
-      v = __fmul_rn(v, pre);
-    }
-    const __half hi = __float2half_rn(v);
-    const __half lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
-    uint8_t* blk = reinterpret_cast<uint8_t*>(xq) + (size_t)b * 2 * TP * 64;
-    *reinterpret_cast<__half*>(blk + qg_canon16(t, k)) = hi;
-    *reinterpret_cast<__half*>(blk + TP * 64 + qg_canon16(t, k)) = lo;
-  }
-}
+// The pieces are built by bt_prep_kernel (batch_kernels.cuh): per token, the
+// RMSNorm scale 1 / sqrtf(sum x^2 / n + eps) (cpu_neon.c:109-115) where the
+// product has a norm, and a power of two 2^-e that brings the largest input
+// element (after the norm) near [1, 2); x' = (x * scale * w) * 2^-e, hi =
+// fp16(x'), lo = fp16(x' - hi); post[t] = 2^e undoes the scaling at the end.
 
 // ---- the product -----------------------------------------------------------
 
@@ -399,6 +336,9 @@ __global__ void __maxnreg__(96)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // programmatic dependent launch: the weights do not depend on the previous
+  // kernel; the pieces, post[] and the outputs' readers do (pdl_wait below)
+  pdl_trigger();
 
   if (warp == 0) {
     // ---------------- producer
@@ -426,6 +366,7 @@ __global__ void __maxnreg__(96)
           mbar_expect_tx(fb, tx);
           tma_load_3d(smem_addr(st), &qmap, c * KC * (TYPE == kQ4_0 ? 16 : 32), 0, 32 * tile, fb);
           tma_load_2d(smem_addr(st + QgSmem::kQuant), &smap, c * KC * 8, 32 * tile, fb);
+          if (sc == 0) pdl_wait();  // the pieces were written by the previous kernel
           bulk_g2s(smem_addr(st + QgSmem::kQuant + QgSmem::kScale),
                    reinterpret_cast<const uint8_t*>(p.xq) + (size_t)c * PB, (uint32_t)PB, fb);
         }
@@ -438,6 +379,7 @@ __global__ void __maxnreg__(96)
   }
 
   // ---------------- math warps
+  pdl_wait();  // post[] and the outputs' previous readers
   const int q = warp & 3;                 // TMEM lane quadrant of this warp
   const int r = 32 * q + lane;            // weight row within the tile
   const int g = (warp - 1) >> 2;          // warpgroup 0..3

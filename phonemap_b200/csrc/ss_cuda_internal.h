@@ -92,6 +92,9 @@ struct Context {
   // output, SwiGLU activations, logits of up to 32 tokens; token metadata
   uint32_t flags = 0;
   float* bt_h = nullptr;
+  float* bt_h2 = nullptr;       // the residual stream alternates between bt_h and bt_h2
+  int bt_zero_words = 0;        // words of bt_amax (+ bt_best) the pass's first kernel zeroes
+  bool bt_pdl = true;           // programmatic dependent launches in the many-token step
   float* bt_q = nullptr;
   float* bt_att = nullptr;
   float* bt_act = nullptr;
