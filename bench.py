@@ -53,7 +53,7 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile-kernel", default=None,
                     choices=["qkv", "attention", "o", "gate_up", "down", "lm_head", "step",
-                             "product_gate_up"],
+                             "product_gate_up", "product_qkv_l2"],
                     help="time one step kernel in isolation instead of the decode loop "
                          "(qkv..lm_head need --multi-kernel; step = one whole decode step)")
     ap.add_argument("--multi-kernel", action="store_true",
@@ -637,7 +637,7 @@ def run_profile_kernel(args):
     path = synth.ensure_gguf(cfg)
     per_kernel = args.profile_kernel != "step"
     flags = runtime.FLAG_MULTI_KERNEL if (per_kernel or args.multi_kernel) else 0
-    if args.profile_kernel == "product_gate_up":
+    if args.profile_kernel.startswith("product_"):
         flags = 0
     m = runtime.CudaModel(path, cfg.ctx, device=0, flags=flags, max_batch=max(1, args.batch))
     if args.profile_kernel in ("attention", "step"):  # give it cached positions to attend over

@@ -136,14 +136,16 @@ int ss_cuda_stats(const ss_cuda_ctx_t *ctx, int64_t *out, int32_t n);
  * 5 lm_head GEMV -- cycling through the layers so weights stream from HBM --
  * or 6 the whole decode step (steps at the current position onwards), or 7
  * the tensor-core gate/up product of max_batch tokens (the kernel alone, its
- * activation pieces built once before), and writes the average milliseconds
- * per launch.  0..5 exist only in the multi-kernel step, 7 only where the
- * matrices are in the tiled layout.  Clobbers the activations and the K/V rows it passes
+ * activation pieces built once before), or 8 the same for layer 0's Q/K/V
+ * matrix at every launch (L2-resident where it fits), and writes the average
+ * milliseconds per launch.  0..5 exist only in the multi-kernel step, 7 and 8
+ * only where the matrices are in the tiled layout.  Clobbers the activations and the K/V rows it passes
  * over; call ss_cuda_reset before decoding again. */
 int ss_cuda_time_kernel(ss_cuda_ctx_t *ctx, int32_t which, int32_t iters, float *ms_per_launch);
 /* Device bytes of the weights one launch of kernel `which` streams (layer 0;
  * repacked layout, i.e. the GGUF bytes plus row padding; 6: every weight
- * matrix of the step; 7: the gate/up matrix); -1 if not a GEMV. */
+ * matrix of the step; 7: the gate/up matrix; 8: the Q/K/V matrix); -1 if not
+ * a GEMV. */
 int64_t ss_cuda_kernel_bytes(const ss_cuda_ctx_t *ctx, int32_t which);
 
 /* Measurement aid, no reference counterpart: the timeline of the last

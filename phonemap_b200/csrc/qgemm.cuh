@@ -56,7 +56,7 @@ constexpr int kQgRows = 128;        // weight rows per tile (UMMA M)
 constexpr int kQgMaxT = 32;         // tokens per product (N = 2 * 32 = 64 at most)
 constexpr int kQgStages = 3;        // ring stages
 constexpr int kQgMathWarps = 16;    // four warpgroups: each covers all 128 TMEM lanes
-constexpr int kQgThreads = 32 * (1 + kQgMathWarps);
+constexpr int kQgThreads = 32 * (2 + kQgMathWarps);  // producer, MMA issuer, math warps
 constexpr int kQgABytes = kQgRows * 32 * 2;  // one block of A (fp16) in the canonical layout
 constexpr int kQgGroup = 4;         // blocks per MMA group (A buffer, TMEM region)
 constexpr int kQgTmemCols = 512;    // two regions of kQgGroup blocks x 2 TP (<= 64) columns
@@ -294,11 +294,13 @@ SS_DEVINL void q8_to_f16x8(uint32_t w0, uint32_t w1, uint32_t (&h)[4]) {
   }
 }
 
-// Warp 0 (one lane) feeds the ring; warps 1..16 unpack A, issue the MMAs
-// (one elected lane of warp 1) and flush D: warp w owns TMEM lanes
-// 32 (w % 4) .. +31 (weight rows), warpgroup g = (w - 1) / 4 unpacks elements
+// Warp roles: warp 0 (one lane) feeds the ring; warp 1 issues the MMAs (one
+// elected lane); warps 2..17 unpack A and flush D -- warp w owns TMEM lanes
+// 32 (w % 4) .. +31 (weight rows), warpgroup g = (w - 2) / 4 unpacks elements
 // 8 g .. 8 g + 7 of each block (one core matrix) and flushes tokens
-// g TP/4 .. (g + 1) TP/4 - 1.
+// g TP/4 .. (g + 1) TP/4 - 1.  The roles meet only at mbarriers: a group's A
+// written (a_ready, 16 warp arrivals), its MMAs done (dfull, a commit), its
+// TMEM region flushed (d_free, 16 arrivals), a stage's slot free (empty).
 template <int TYPE, int TP>
 __global__ void __maxnreg__(96)
     qgemm_kernel(const QGemmParams p, const __grid_constant__ CUtensorMap qmap,
@@ -316,7 +318,9 @@ __global__ void __maxnreg__(96)
   uint64_t* full = reinterpret_cast<uint64_t*>(abuf + 2 * G * kQgABytes);
   uint64_t* empty = full + kQgStages;
   uint64_t* dfull = empty + kQgStages;                             // [2]: MMAs of a group done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dfull + 2);
+  uint64_t* a_ready = dfull + 2;                                   // [2]: A of a group written
+  uint64_t* d_free = a_ready + 2;                                  // [2]: TMEM region flushed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_free + 2);
   __shared__ int s_abort;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -327,8 +331,11 @@ __global__ void __maxnreg__(96)
       mbar_init(smem_addr(full + i), 1);
       mbar_init(smem_addr(empty + i), kQgMathWarps);
     }
-    mbar_init(smem_addr(dfull), 1);
-    mbar_init(smem_addr(dfull + 1), 1);
+    for (int i = 0; i < 2; i++) {
+      mbar_init(smem_addr(dfull + i), 1);
+      mbar_init(smem_addr(a_ready + i), kQgMathWarps);
+      mbar_init(smem_addr(d_free + i), kQgMathWarps);
+    }
     mbar_fence_init();
   }
   if (warp == 1) tmem_alloc(smem_addr(tmem_slot), kQgTmemCols);
@@ -339,6 +346,21 @@ __global__ void __maxnreg__(96)
   // programmatic dependent launch: the weights do not depend on the previous
   // kernel; the pieces, post[] and the outputs' readers do (pdl_wait below)
   pdl_trigger();
+  // bounded wait that also gives up when another role aborted
+  auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+    const uint32_t a = smem_addr(bar);
+    if (mbar_try_wait(a, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(a, parity)) {
+      if (*(volatile int*)&s_abort) return false;
+      if (clock64() - t0 > p.wait_budget) {
+        atomicOr(p.err, 4);
+        *(volatile int*)&s_abort = 1;
+        return false;
+      }
+    }
+    return true;
+  };
 
   if (warp == 0) {
     // ---------------- producer
@@ -351,15 +373,9 @@ __global__ void __maxnreg__(96)
         qg_unit(p, u, tile, split, c0, c1);
         for (int c = c0; c < c1; c++, sc++) {
           const int s = sc % kQgStages;
-          if (sc >= kQgStages) {
-            const uint32_t par = (uint32_t)(((sc / kQgStages) - 1) & 1);
-            if (!mbar_try_wait(smem_addr(empty + s), par)) {
-              const long long t0 = clock64();
-              while (!mbar_try_wait(smem_addr(empty + s), par)) {
-                if (*(volatile int*)&s_abort || clock64() - t0 > p.wait_budget) { bad = true; break; }
-              }
-              if (bad) break;
-            }
+          if (sc >= kQgStages && !wait(empty + s, (uint32_t)(((sc / kQgStages) - 1) & 1))) {
+            bad = true;
+            break;
           }
           uint8_t* st = smem + s * SB;
           const uint32_t fb = smem_addr(full + s);
@@ -378,21 +394,64 @@ __global__ void __maxnreg__(96)
     return;
   }
 
-  // ---------------- math warps
+  const uint32_t idesc = umma_idesc_f16(kQgRows, 2 * TP);
+  if (warp == 1) {
+    // ---------------- MMA issuer (the whole warp runs the loop; one elected lane issues)
+    int gc = 0, sc = 0;
+    bool bad = false;
+    for (int u = blockIdx.x; u < nunits && !bad; u += gridDim.x) {
+      int tile, split, c0, c1;
+      qg_unit(p, u, tile, split, c0, c1);
+      for (int c = c0; c < c1 && !bad; c++, sc++) {
+        const int s = sc % kQgStages;
+        bad = !wait(full + s, (uint32_t)((sc / kQgStages) & 1));
+        uint8_t* st = smem + s * SB;
+        for (int h = 0; h < NG && !bad; h++, gc++) {
+          if (!wait(a_ready + (gc & 1), (uint32_t)((gc >> 1) & 1)) ||
+              (gc >= 2 && !wait(d_free + (gc & 1), (uint32_t)(((gc - 2) >> 1) & 1)))) {
+            bad = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t dt = tmem + (uint32_t)((gc & 1) * G * 2 * TP);
+          const uint64_t adesc0 = umma_desc_kmajor(smem_addr(abuf + (gc & 1) * G * kQgABytes));
+          const uint64_t bdesc0 = umma_desc_kmajor(smem_addr(st + QgSmem::kQuant + QgSmem::kScale) +
+                                                   (uint32_t)(h * G * 2 * TP * 64));
+          // descriptor start addresses advance in 16-byte units
+#pragma unroll
+          for (int bl = 0; bl < G; bl++)
+#pragma unroll
+            for (int kh = 0; kh < 2; kh++)  // K halves of 16
+              umma_f16(dt + (uint32_t)(bl * 2 * TP), adesc0 + (uint64_t)((bl * kQgABytes + 256 * kh) >> 4),
+                       bdesc0 + (uint64_t)((bl * 2 * TP * 64 + 256 * kh) >> 4), idesc, kh ? 1u : 0u);
+          umma_commit(smem_addr(dfull + (gc & 1)));
+        }
+      }
+    }
+    // no MMA may still write TMEM when it is freed: wait for the last commit
+    if (gc > 0) {
+      const int last = gc - 1;
+      mbar_wait_bounded(smem_addr(dfull + (last & 1)), (uint32_t)((last >> 1) & 1), p.wait_budget);
+    }
+    tc_fence_before();
+    named_bar_sync(1, 32 * (kQgMathWarps + 1));
+    tc_fence_after();
+    tmem_dealloc(tmem, kQgTmemCols);
+    return;
+  }
+
+  // ---------------- math warps (2..17)
   pdl_wait();  // post[] and the outputs' previous readers
   const int q = warp & 3;                 // TMEM lane quadrant of this warp
   const int r = 32 * q + lane;            // weight row within the tile
-  const int g = (warp - 1) >> 2;          // warpgroup 0..3
+  const int g = (warp - 2) >> 2;          // warpgroup 0..3
   constexpr int th = TP >> 2;             // tokens flushed per warpgroup (2, 4 or 8)
-  const uint32_t idesc = umma_idesc_f16(kQgRows, 2 * TP);
   const uint32_t t_lane = tmem + ((uint32_t)(32 * q) << 16);
-  const bool issuer = warp == 1;   // the MMA-issuing warp (one elected lane issues)
   float acc[th];
-  int gc = 0;        // groups whose MMAs this CTA issued
+  int gc = 0;        // groups unpacked by this CTA
   int sc = 0;        // stages consumed
   bool bad = false;
-  bool okd = true;   // the last wait for a group's MMAs succeeded
-  int pend = -1;     // group whose MMAs were issued and not yet flushed (its gc)
+  int pend = -1;     // group whose MMAs were requested and not yet flushed (its gc)
   int pend_slot = 0, pend_blk = 0;
   bool pend_last = false;  // the pending group is its stage's last
   // this thread's quant bytes of a block: Q4_0 bytes 8 (g & 1) .. +7 (low
@@ -400,8 +459,9 @@ __global__ void __maxnreg__(96)
   const int qchunk_off = TYPE == kQ4_0 ? 0 : (g >> 1);
   const uint32_t qbyte = (uint32_t)(8 * (g & 1));
 
-  // Flushes the pending group: its TMEM region (pend & 1), the scales of its
-  // blocks; releases the ring slot after the stage's last group.
+  // Flushes the pending group (its MMAs done): its TMEM region (pend & 1),
+  // the scales of its blocks; frees the region, and the ring slot after the
+  // stage's last group.
   auto flush_group = [&]() {
     const uint32_t region = (uint32_t)((pend & 1) * G * 2 * TP);
     const uint8_t* sst = smem + pend_slot * SB + QgSmem::kQuant;
@@ -433,10 +493,11 @@ __global__ void __maxnreg__(96)
         for (int i = 0; i < th; i++) acc[i] = fmaf(__int_as_float(hv[j][i]) + __int_as_float(lv[j][i]), d, acc[i]);
       }
     }
-    if (pend_last) {
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(empty + pend_slot));
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive(smem_addr(d_free + (pend & 1)));
+      if (pend_last) mbar_arrive(smem_addr(empty + pend_slot));
     }
     pend = -1;
   };
@@ -448,57 +509,43 @@ __global__ void __maxnreg__(96)
     for (int i = 0; i < th; i++) acc[i] = 0.0f;
     for (int c = c0; c < c1 && !bad; c++, sc++) {
       const int s = sc % kQgStages;
-      const bool okf = qg_wait(smem_addr(full + s), (uint32_t)((sc / kQgStages) & 1), p);
-      tc_fence_after();
-      uint8_t* st = smem + s * SB;
-      const uint32_t qrow = smem_addr(st) + (uint32_t)(r * 128);
+      if (!wait(full + s, (uint32_t)((sc / kQgStages) & 1))) {
+        bad = true;
+        break;
+      }
+      const uint32_t qrow = smem_addr(smem + s * SB) + (uint32_t)(r * 128);
 #pragma unroll 1
-      for (int h = 0; h < NG; h++) {
+      for (int h = 0; h < NG; h++, gc++) {
         // A buffer (gc & 1) was last read by the MMAs of group gc - 2, which
-        // completed before group gc - 2 was flushed
+        // completed before group gc - 2 was flushed (below, one group ago)
         uint8_t* ab = abuf + (gc & 1) * G * kQgABytes;
-        if (okf && okd) {
-          uint32_t w[G][2];
+        uint32_t w[G][2];
 #pragma unroll
-          for (int bl = 0; bl < G; bl++) {
-            const int chunk = TYPE == kQ4_0 ? h * G + bl : 2 * bl + qchunk_off;
-            asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];"
-                         : "=r"(w[bl][0]), "=r"(w[bl][1])
-                         : "r"(qrow + ((chunk ^ (r & 7)) << 4) + qbyte));
-          }
+        for (int bl = 0; bl < G; bl++) {
+          const int chunk = TYPE == kQ4_0 ? h * G + bl : 2 * bl + qchunk_off;
+          asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];"
+                       : "=r"(w[bl][0]), "=r"(w[bl][1])
+                       : "r"(qrow + ((chunk ^ (r & 7)) << 4) + qbyte));
+        }
 #pragma unroll
-          for (int bl = 0; bl < G; bl++) {
-            uint32_t hh[4];
-            if constexpr (TYPE == kQ4_0) q4_to_f16x8(w[bl][0], w[bl][1], g >= 2, hh);
-            else q8_to_f16x8(w[bl][0], w[bl][1], hh);
-            const uint32_t a = smem_addr(ab + bl * kQgABytes) + (uint32_t)qg_canon16(r, 8 * g);
-            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(hh[0]), "r"(hh[1]), "r"(hh[2]),
-                         "r"(hh[3])
-                         : "memory");
-          }
+        for (int bl = 0; bl < G; bl++) {
+          uint32_t hh[4];
+          if constexpr (TYPE == kQ4_0) q4_to_f16x8(w[bl][0], w[bl][1], g >= 2, hh);
+          else q8_to_f16x8(w[bl][0], w[bl][1], hh);
+          const uint32_t a = smem_addr(ab + bl * kQgABytes) + (uint32_t)qg_canon16(r, 8 * g);
+          asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(hh[0]), "r"(hh[1]), "r"(hh[2]),
+                       "r"(hh[3])
+                       : "memory");
         }
         fence_proxy_async_smem();
-        tc_fence_before();
-        bad = qg_any(!(okf && okd));  // every math thread has written its part of A
-        tc_fence_after();
-        if (bad) break;
-        if (issuer) {
-          const uint32_t dt = tmem + (uint32_t)((gc & 1) * G * 2 * TP);
-          const uint64_t adesc0 = umma_desc_kmajor(smem_addr(ab));
-          const uint64_t bdesc0 = umma_desc_kmajor(smem_addr(st + QgSmem::kQuant + QgSmem::kScale) +
-                                                   (uint32_t)(h * G * 2 * TP * 64));
-          // descriptor start addresses advance in 16-byte units
-#pragma unroll
-          for (int bl = 0; bl < G; bl++)
-#pragma unroll
-            for (int kh = 0; kh < 2; kh++)    // K halves of 16
-              umma_f16(dt + (uint32_t)(bl * 2 * TP), adesc0 + (uint64_t)((bl * kQgABytes + 256 * kh) >> 4),
-                       bdesc0 + (uint64_t)((bl * 2 * TP * 64 + 256 * kh) >> 4), idesc, kh ? 1u : 0u);
-          umma_commit(smem_addr(dfull + (gc & 1)));
-        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(a_ready + (gc & 1)));
         // the previous group, while this group's MMAs run
         if (pend >= 0) {
-          okd = qg_wait(smem_addr(dfull + (pend & 1)), (uint32_t)((pend >> 1) & 1), p);
+          if (!wait(dfull + (pend & 1), (uint32_t)((pend >> 1) & 1))) {
+            bad = true;
+            break;
+          }
           tc_fence_after();
           flush_group();
         }
@@ -506,14 +553,14 @@ __global__ void __maxnreg__(96)
         pend_slot = s;
         pend_blk = h * G;
         pend_last = h == NG - 1;
-        gc++;
       }
     }
     if (bad) break;
     // the unit's last group, then its partial sums
-    const bool ok = qg_wait(smem_addr(dfull + (pend & 1)), (uint32_t)((pend >> 1) & 1), p);
-    bad = qg_any(!(ok && okd));
-    if (bad) break;
+    if (!wait(dfull + (pend & 1), (uint32_t)((pend >> 1) & 1))) {
+      bad = true;
+      break;
+    }
     tc_fence_after();
     flush_group();
     const int row = tile * kQgRows + r;
@@ -525,17 +572,8 @@ __global__ void __maxnreg__(96)
       }
     }
   }
-  if (bad && tid == 32) {
-    s_abort = 1;
-    // no MMA may still write TMEM when it is freed: wait for the last commit
-    const int last = gc - 1;
-    if (last >= 0)
-      mbar_wait_bounded(smem_addr(dfull + (last & 1)), (uint32_t)((last >> 1) & 1), p.wait_budget);
-  }
   tc_fence_before();
-  named_bar_sync(1, 32 * kQgMathWarps);
-  tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, kQgTmemCols);
+  named_bar_sync(1, 32 * (kQgMathWarps + 1));
 }
 
 }  // namespace ss

@@ -1975,13 +1975,14 @@ SS_API int ss_cuda_dequantize(int32_t type, const void* blocks, int64_t n, float
 SS_API int ss_cuda_time_kernel(ss_cuda_ctx_t* ctx, int32_t which, int32_t iters, float* ms_per_launch) {
   return guard([&] {
     Context* c = need_model(ctx);
-    if (which < 0 || which > 7 || iters <= 0 || !ms_per_launch) fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad arguments");
+    if (which < 0 || which > 8 || iters <= 0 || !ms_per_launch) fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad arguments");
     if (c->tiled && which < 6)
       fail(SS_CUDA_ERROR_INVALID_PARAMS, "per-kernel timing needs the multi-kernel step (SS_CUDA_FLAG_MULTI_KERNEL)");
-    if (which == 7) {
+    if (which >= 7) {
       if (!bt_eligible(c)) fail(SS_CUDA_ERROR_INVALID_PARAMS, "the tensor-core product needs the tiled layout");
       bt_prepare(c);
-      qg_product(c, c->layers[0].gu, c->bt_h, c->d, c->layers[0].ffn_norm, c->max_batch, true, false);
+      const DevMatrix& m0 = which == 7 ? c->layers[0].gu : c->layers[0].qkv;
+      qg_product(c, m0, c->bt_h, c->d, nullptr, c->max_batch, true, false);
     }
     const int pos0 = c->host_pos;
     if (which == 6 && pos0 + iters + 3 > c->ctx)
@@ -1994,6 +1995,7 @@ SS_API int ss_cuda_time_kernel(ss_cuda_ctx_t* ctx, int32_t which, int32_t iters,
       switch (which) {
         case 6: enqueue_step(c, c->use_pdl); break;
         case 7: qg_product(c, c->layers[(size_t)l].gu, c->bt_h, c->d, nullptr, c->max_batch, false, true); break;
+        case 8: qg_product(c, c->layers[0].qkv, c->bt_h, c->d, nullptr, c->max_batch, false, true); break;
         case 0: launch_qkv(c, l, false); break;
         case 1: launch_attn(c, l, false); break;
         case 2: launch_o(c, l, false); break;
@@ -2030,6 +2032,7 @@ SS_API int64_t ss_cuda_kernel_bytes(const ss_cuda_ctx_t* ctx, int32_t which) {
     case 3: return (int64_t)matrix_bytes(l0.gu);
     case 4: return (int64_t)(matrix_bytes(l0.down) + (l0.down2.cols ? matrix_bytes(l0.down2) : 0));
     case 7: return (int64_t)matrix_bytes(l0.gu);
+    case 8: return (int64_t)matrix_bytes(l0.qkv);
     case 5: return (int64_t)matrix_bytes(c->lm_head);
     case 6: {
       int64_t b = (int64_t)matrix_bytes(c->lm_head);

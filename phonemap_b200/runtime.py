@@ -332,7 +332,7 @@ class CudaModel:
         return {k: int(x) for k, x in zip(keys, v)}
 
     KERNELS = {"qkv": 0, "attention": 1, "o": 2, "gate_up": 3, "down": 4, "lm_head": 5, "step": 6,
-               "product_gate_up": 7}
+               "product_gate_up": 7, "product_qkv_l2": 8}
 
     def time_kernel(self, which: str, iters: int) -> float:
         """Average ms per isolated launch of one step kernel (clobbers state)."""

@@ -30,7 +30,8 @@ def _divisible(cfg, n: int) -> bool:
 
 
 CASES = [(2, "tiny"), (2, "tiny-mha"), (2, "tiny-q8"), (2, "tinyllama"), (2, "llama2-7b"),
-         (4, "tinyllama"), (4, "llama2-7b"), (8, "llama2-7b")]
+         (4, "tinyllama"), (4, "llama2-7b"), (8, "llama2-7b"), (2, "llama3-8b"), (4, "llama3-8b"),
+         (8, "llama3-8b")]
 
 
 @pytest.mark.parametrize("path", PATHS)
