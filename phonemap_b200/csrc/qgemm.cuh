@@ -23,8 +23,9 @@
 //
 // Tensor-core mapping (one CTA tile = 128 weight rows):
 //   A (M = 128 rows x K = 32 per block): the block's weights as fp16, written
-//       by the math warps into shared memory in the UMMA canonical K-major
-//       layout (8-row x 16-byte core matrices);
+//       by the math warps into tensor memory with tcgen05.st (row r in lane r,
+//       two consecutive K elements per 32-bit column: 16 columns per block),
+//       so the unpacked weights never pass through shared memory;
 //   B (N = 2 TP x K = 32): the block's activation pieces, rows 0..TP-1 the
 //       hi pieces of tokens 0..TP-1 and rows TP..2TP-1 their lo pieces (TP =
 //       T rounded up to 8, 16 or 32; padding rows zero), already in the
@@ -32,10 +33,10 @@
 //   D (128 lanes x 2 TP columns of TMEM per block, fp32): two tcgen05.mma
 //       kind::f16 per block (the two K halves of 16); column t holds token
 //       t's hi product, column TP + t its lo product, added at the flush.
-// A group (kQgGroup blocks) is the unit of work of the math warps: they
-// unpack its blocks into one of two A buffers, one elected lane issues its
-// MMAs into one of two TMEM regions, and while those run the warps flush the
-// previous group's region and unpack the next group.
+// A group (qg_group(TP) blocks) is the unit of work of the math warps: they
+// unpack its blocks into one of two TMEM A buffers, one elected lane issues
+// its MMAs into one of two TMEM D regions, and while those run the warps flush
+// the previous group's region and unpack the next group.
 // Weights arrive by TMA (cp.async.bulk.tensor, 128-byte swizzle, no
 // multicast) into a ring of stages of KC blocks x 128 rows (one or two
 // groups), with the pieces of those blocks (cp.async.bulk) and the fp16
@@ -54,15 +55,17 @@ namespace ss {
 
 constexpr int kQgRows = 128;        // weight rows per tile (UMMA M)
 constexpr int kQgMaxT = 32;         // tokens per product (N = 2 * 32 = 64 at most)
-constexpr int kQgStages = 3;        // ring stages
+constexpr int kQgStages = 4;        // ring stages
 constexpr int kQgMathWarps = 16;    // four warpgroups: each covers all 128 TMEM lanes
 constexpr int kQgThreads = 32 * (2 + kQgMathWarps);  // producer, MMA issuer, math warps
-constexpr int kQgABytes = kQgRows * 32 * 2;  // one block of A (fp16) in the canonical layout
-constexpr int kQgGroup = 4;         // blocks per MMA group (A buffer, TMEM region)
-constexpr int kQgTmemCols = 512;    // two regions of kQgGroup blocks x 2 TP (<= 64) columns
+constexpr int kQgACols = 16;        // TMEM columns of one block of A (128 rows x 32 fp16)
+constexpr int kQgTmemCols = 512;    // D regions, then A buffers
 
 // Token rows per piece: T rounded up to 8, 16 or 32.
 __host__ __device__ constexpr int qg_tp(int T) { return T <= 8 ? 8 : T <= 16 ? 16 : 32; }
+// Blocks per MMA group (one A buffer, one D region): two D regions of
+// G x 2 TP columns and two A buffers of G x 16 columns fit the 512 TMEM columns.
+__host__ __device__ constexpr int qg_group(int TP) { return TP == 32 ? 2 : 4; }
 
 // Blocks per stage: the TMA box's inner extent is 128 bytes (the 128-byte
 // swizzle span): 8 Q4_0 blocks of 16 quant bytes, 4 Q8_0 blocks of 32.
@@ -83,7 +86,7 @@ struct QGemmParams {
 };
 
 // Shared memory: [stages][quants 16 KB | scales 2 KB | pieces KC*2*TP*64]
-// [A: 2 buffers x kQgGroup blocks][mbarriers][tmem address].
+// [mbarriers][tmem address].  A lives in TMEM.
 struct QgSmem {
   static constexpr int kQuant = 16384;   // 128 rows x 128 bytes
   static constexpr int kScale = 2048;    // 128 rows x KC (<= 8) fp16
@@ -92,7 +95,7 @@ struct QgSmem {
     return (kQuant + kScale + plane_bytes(type, TP) + 1023) / 1024 * 1024;
   }
   __host__ __device__ static int total(int type, int TP) {
-    return 1024 /* alignment slack */ + kQgStages * stage_bytes(type, TP) + 2 * kQgGroup * kQgABytes + 256;
+    return 1024 /* alignment slack */ + kQgStages * stage_bytes(type, TP) + 256;
   }
 };
 
@@ -138,6 +141,21 @@ SS_DEVINL void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint3
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accum), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
       : "memory");
 }
+// The same with A in tensor memory (a_tmem: the column of its K = 16 slice).
+SS_DEVINL void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n elect.sync _|e, 0xffffffff;\n setp.ne.b32 p, %4, 0;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+// Four consecutive 32-bit TMEM columns of this thread's lane (whole warp).
+SS_DEVINL void tmem_st4(uint32_t taddr, const uint32_t (&v)[4]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(v[0]), "r"(v[1]),
+               "r"(v[2]), "r"(v[3])
+               : "memory");
+}
+SS_DEVINL void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // Arrives once on `bar` when every tcgen05 operation the issuing lane issued
 // before it has completed (the MMA's shared-memory reads included).  Executed
 // by the whole issuing warp; the elected lane commits.
@@ -306,16 +324,17 @@ __global__ void __maxnreg__(96)
     qgemm_kernel(const QGemmParams p, const __grid_constant__ CUtensorMap qmap,
                  const __grid_constant__ CUtensorMap smap) {
   constexpr int KC = qg_kc(TYPE);
-  constexpr int G = kQgGroup;
+  constexpr int G = qg_group(TP);
   constexpr int NG = KC / G;  // groups per stage
+  constexpr uint32_t kACol0 = 2 * G * 2 * TP;  // TMEM: D regions, then the two A buffers
+  static_assert(kACol0 + 2 * G * kQgACols <= kQgTmemCols, "TMEM columns");
   static_assert(KC % G == 0, "stage = whole groups");
   static_assert(TP == 8 || TP == 16 || TP == 32, "token rows per piece");
   extern __shared__ uint8_t qg_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(qg_raw) + 1023) & ~(uintptr_t)1023);
   const int SB = QgSmem::stage_bytes(TYPE, TP);
   const int PB = QgSmem::plane_bytes(TYPE, TP);
-  uint8_t* abuf = smem + kQgStages * SB;                           // 2 x G x 8 KB
-  uint64_t* full = reinterpret_cast<uint64_t*>(abuf + 2 * G * kQgABytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kQgStages * SB);
   uint64_t* empty = full + kQgStages;
   uint64_t* dfull = empty + kQgStages;                             // [2]: MMAs of a group done
   uint64_t* a_ready = dfull + 2;                                   // [2]: A of a group written
@@ -414,16 +433,17 @@ __global__ void __maxnreg__(96)
           }
           tc_fence_after();
           const uint32_t dt = tmem + (uint32_t)((gc & 1) * G * 2 * TP);
-          const uint64_t adesc0 = umma_desc_kmajor(smem_addr(abuf + (gc & 1) * G * kQgABytes));
+          const uint32_t at = tmem + kACol0 + (uint32_t)((gc & 1) * G * kQgACols);
           const uint64_t bdesc0 = umma_desc_kmajor(smem_addr(st + QgSmem::kQuant + QgSmem::kScale) +
                                                    (uint32_t)(h * G * 2 * TP * 64));
-          // descriptor start addresses advance in 16-byte units
+          // descriptor start addresses advance in 16-byte units; a K half of
+          // A is 8 TMEM columns
 #pragma unroll
           for (int bl = 0; bl < G; bl++)
 #pragma unroll
             for (int kh = 0; kh < 2; kh++)  // K halves of 16
-              umma_f16(dt + (uint32_t)(bl * 2 * TP), adesc0 + (uint64_t)((bl * kQgABytes + 256 * kh) >> 4),
-                       bdesc0 + (uint64_t)((bl * 2 * TP * 64 + 256 * kh) >> 4), idesc, kh ? 1u : 0u);
+              umma_f16_ts(dt + (uint32_t)(bl * 2 * TP), at + (uint32_t)(bl * kQgACols + 8 * kh),
+                          bdesc0 + (uint64_t)((bl * 2 * TP * 64 + 256 * kh) >> 4), idesc, kh ? 1u : 0u);
           umma_commit(smem_addr(dfull + (gc & 1)));
         }
       }
@@ -517,12 +537,14 @@ __global__ void __maxnreg__(96)
 #pragma unroll 1
       for (int h = 0; h < NG; h++, gc++) {
         // A buffer (gc & 1) was last read by the MMAs of group gc - 2, which
-        // completed before group gc - 2 was flushed (below, one group ago)
-        uint8_t* ab = abuf + (gc & 1) * G * kQgABytes;
+        // completed before group gc - 2 was flushed (below, one group ago);
+        // this warp writes its 32 lanes, columns 4 g .. 4 g + 3 of each block
+        const uint32_t ab = t_lane + kACol0 + (uint32_t)((gc & 1) * G * kQgACols + 4 * g);
         uint32_t w[G][2];
 #pragma unroll
         for (int bl = 0; bl < G; bl++) {
-          const int chunk = TYPE == kQ4_0 ? h * G + bl : 2 * bl + qchunk_off;
+          const int blk = h * G + bl;  // block within the stage
+          const int chunk = TYPE == kQ4_0 ? blk : 2 * blk + qchunk_off;
           asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];"
                        : "=r"(w[bl][0]), "=r"(w[bl][1])
                        : "r"(qrow + ((chunk ^ (r & 7)) << 4) + qbyte));
@@ -532,12 +554,10 @@ __global__ void __maxnreg__(96)
           uint32_t hh[4];
           if constexpr (TYPE == kQ4_0) q4_to_f16x8(w[bl][0], w[bl][1], g >= 2, hh);
           else q8_to_f16x8(w[bl][0], w[bl][1], hh);
-          const uint32_t a = smem_addr(ab + bl * kQgABytes) + (uint32_t)qg_canon16(r, 8 * g);
-          asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(hh[0]), "r"(hh[1]), "r"(hh[2]),
-                       "r"(hh[3])
-                       : "memory");
+          tmem_st4(ab + (uint32_t)(bl * kQgACols), hh);
         }
-        fence_proxy_async_smem();
+        tmem_st_wait();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_addr(a_ready + (gc & 1)));
         // the previous group, while this group's MMAs run
