@@ -127,7 +127,8 @@ int ss_cuda_model_dims(const ss_cuda_ctx_t *ctx, int32_t *dims);
  * loaded kernels were compiled for (cudaFuncAttributes::binaryVersion; 100 =
  * sm_100a), [15] kernels launched per step of several sequences decoded
  * together (the many-token step with every token's lm_head and the greedy
- * feedback; 0 where the matrices are not in the tiled layout). */
+ * feedback; 0 where the matrices are not in the tiled layout), [16] op-level
+ * matvecs served (ss_cuda_matvec*). */
 int ss_cuda_stats(const ss_cuda_ctx_t *ctx, int64_t *out, int32_t n);
 
 /* Measurement aid, no reference counterpart: times `iters` back-to-back

@@ -109,11 +109,16 @@ class _Model:
 class RefModel(_Model):
     """The reference C implementation (oracle/_ref)."""
 
-    def __init__(self, gguf_path: str, ctx: int, ctx8k: bool | None = None):
+    def __init__(self, gguf_path: str, ctx: int, ctx8k: bool | None = None, cuda_hook: bool = False):
+        """cuda_hook: the integration build (libss_ref_cuda.so, the reference
+        with the CUDA backend in its ss_matmul_dispatch); attach_cuda() hands
+        it a context."""
         if ctx8k is None:
             ctx8k = ctx > 512
-        lib_path = os.path.join(REF_DIR, "libss_ref_ctx8k.so" if ctx8k else "libss_ref.so")
-        lib = ctypes.CDLL(lib_path)
+        name = "libss_ref_cuda.so" if cuda_hook else "libss_ref_ctx8k.so" if ctx8k else "libss_ref.so"
+        lib = ctypes.CDLL(os.path.join(REF_DIR, name))
+        if cuda_hook:
+            lib.ssr_attach_cuda.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         lib.ssr_load.restype = ctypes.c_void_p
         lib.ssr_load.argtypes = [ctypes.c_char_p, ctypes.c_uint32]
         for fn in ("ssr_free", "ssr_reset"):
@@ -137,6 +142,10 @@ class RefModel(_Model):
 
     def reset(self):
         self._lib.ssr_reset(self._h)
+
+    def attach_cuda(self, cuda_ctx) -> None:
+        """Give the hooked reference's scheduler a CUDA context (None detaches)."""
+        self._lib.ssr_attach_cuda(self._h, cuda_ctx)
 
     def embed(self, tokens) -> np.ndarray:
         toks = np.ascontiguousarray(tokens, dtype=np.int32)

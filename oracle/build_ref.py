@@ -22,6 +22,16 @@ repository; only the built ``.so`` and test binaries land in ``oracle/_ref/``):
    built with 512 (faithful); ``libss_ref_ctx8k.so`` with 8192 (the "patched
    oracle" needed by configurations that run past 512 positions).
 
+A fifth build, ``libss_ref_cuda.so``, is the reference with this
+repository's CUDA backend plugged in the way a maintainer would (INTEGRATION.md
+section 4): ``ss_scheduler_t`` gains a ``cuda_ctx`` next to its ``metal_ctx``
+(layer_scheduler.h:80) and ``ss_matmul_dispatch`` (layer_scheduler.c:248-279)
+gains an ``#ifdef SS_HAS_CUDA`` branch before its CPU fallback that calls
+``ss_cuda_matvec_q4_0`` / ``_q8_0`` / ``ss_cuda_matvec`` (include/
+slipstream_cuda.h) -- the reference's own scheduler, with every projection
+served by the GPU.  It links against ``phonemap_b200/lib/libslipstream_cuda.so``
+(built first) and is only made when that library exists.
+
 Usage: ``python oracle/build_ref.py [--src <SlipStream dir>] [--out oracle/_ref]``
 Exit status 0 when built, 2 when the reference tree is absent.
 """
@@ -170,6 +180,46 @@ def prepare_tree(src: str, dst: str) -> None:
         f.write(text)
 
 
+CUDA_BRANCH = """#ifdef SS_HAS_CUDA
+    if (sched->cuda_ctx && ss_cuda_should_use_gpu(rows, cols)) {
+        bool cuda_ok = false;
+        if (type == GGML_TYPE_Q4_0)
+            cuda_ok = ss_cuda_matvec_q4_0((ss_cuda_ctx_t *)sched->cuda_ctx, out, mat, vec, rows, cols);
+        else if (type == GGML_TYPE_Q8_0)
+            cuda_ok = ss_cuda_matvec_q8_0((ss_cuda_ctx_t *)sched->cuda_ctx, out, mat, vec, rows, cols);
+        else if (type == GGML_TYPE_F32)
+            cuda_ok = ss_cuda_matvec((ss_cuda_ctx_t *)sched->cuda_ctx, out, (const float *)mat, vec, rows, cols);
+        if (cuda_ok) return;
+    }
+#endif
+
+"""
+
+
+def add_cuda_hook(tree: str) -> None:
+    """The integration a maintainer adds, applied
+    to the temporary copy: the context field and the dispatch branch."""
+    hdr = os.path.join(tree, "src/core/layer_scheduler.h")
+    with open(hdr) as f:
+        text = f.read()
+    anchor = "void             *metal_ctx;"
+    if text.count(anchor) != 1:
+        raise RuntimeError("metal_ctx field not found once in layer_scheduler.h")
+    text = text.replace(anchor, anchor + "\n    void             *cuda_ctx;   /* ss_cuda_ctx_t (SS_HAS_CUDA) */")
+    with open(hdr, "w") as f:
+        f.write(text)
+    sched = os.path.join(tree, "src/core/layer_scheduler.c")
+    with open(sched) as f:
+        text = f.read()
+    anchor = "    // Fallback: execute on CPU NEON natively."
+    if text.count(anchor) != 1:
+        raise RuntimeError("CPU fallback anchor not found once in layer_scheduler.c")
+    text = text.replace(anchor, CUDA_BRANCH + anchor)
+    text = "#ifdef SS_HAS_CUDA\n#include \"slipstream_cuda.h\"\n#endif\n" + text
+    with open(sched, "w") as f:
+        f.write(text)
+
+
 def build(src: str, out: str, cc: str = "gcc") -> list[str]:
     os.makedirs(out, exist_ok=True)
     built = []
@@ -185,6 +235,23 @@ def build(src: str, out: str, cc: str = "gcc") -> list[str]:
             target = os.path.join(out, name)
             cmd = [cc, *flags, f"-DSS_REF_MAX_SEQ={cap}", "-shared", *inc, *srcs,
                    os.path.join(HERE, "ref_driver.c"), "-o", target, "-lm"]
+            subprocess.run(cmd, check=True)
+            built.append(target)
+        # the reference with the CUDA backend in its dispatch (needs the built library)
+        repo = os.path.dirname(HERE)
+        cuda_lib = os.path.join(repo, "phonemap_b200", "lib", "libslipstream_cuda.so")
+        if os.path.exists(cuda_lib):
+            hooked = os.path.join(tmp, "hooked")
+            prepare_tree(src, hooked)
+            add_cuda_hook(hooked)
+            hinc = ["-I", os.path.join(HERE, "shims"), "-I", os.path.join(repo, "include"),
+                    "-I", os.path.join(hooked, "include"), "-I", os.path.join(hooked, "src")]
+            target = os.path.join(out, "libss_ref_cuda.so")
+            rpath = os.path.relpath(os.path.dirname(cuda_lib), out)
+            cmd = [cc, *flags, "-DSS_REF_MAX_SEQ=8192", "-DSS_HAS_CUDA", "-shared", *hinc,
+                   *[os.path.join(hooked, x) for x in CORE_SOURCES], os.path.join(HERE, "ref_driver.c"),
+                   "-o", target, "-L", os.path.dirname(cuda_lib), "-lslipstream_cuda",
+                   f"-Wl,-rpath,$ORIGIN/{rpath}", "-lm"]
             subprocess.run(cmd, check=True)
             built.append(target)
         # the reference's own unit tests, linked against the same objects

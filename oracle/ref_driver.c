@@ -28,6 +28,13 @@ void *ssr_load(const char *path, uint32_t context_size) {
 
 void ssr_free(void *m) { ss_model_free((ss_model_t *)m); }
 
+#ifdef SS_HAS_CUDA
+/* The integration build (build_ref.py, libss_ref_cuda.so): hand the
+ * scheduler a CUDA context, as ss_model_load would next to the Metal one
+ * (engine.c:87-96); ss_matmul_dispatch then sends the projections to it. */
+void ssr_attach_cuda(void *m, void *cuda_ctx) { ((ss_model_t *)m)->scheduler->cuda_ctx = cuda_ctx; }
+#endif
+
 /* dims[0..7] = vocab, hidden, layers, heads, kv_heads, head_dim, ffn, max_seq */
 void ssr_dims(void *m, int32_t *dims) {
     ss_scheduler_t *s = ((ss_model_t *)m)->scheduler;

@@ -1403,6 +1403,7 @@ bool op_matvec(ss_cuda_ctx_t* ctx, float* out, const void* mat, const float* vec
              CK(cudaMemcpyAsync(out, s.d_out, sizeof(float) * rows, cudaMemcpyDeviceToHost, c->stream));
              CK(cudaStreamSynchronize(c->stream));
            }
+           c->ops_run++;
          }) == SS_CUDA_OK;
 }
 
@@ -1589,7 +1590,7 @@ SS_API int ss_cuda_stats(const ss_cuda_ctx_t* ctx, int64_t* out, int32_t n) {
     cudaFuncAttributes fa{};
     const int64_t arch = cudaFuncGetAttributes(&fa, embed_kernel) == cudaSuccess ? fa.binaryVersion : -1;
     cudaGetLastError();
-    const int64_t v[16] = {c->has_model ? (c->mega ? 1 : bt_only(c) ? bt_launches(c, 1) + 2 : 2 + 5LL * c->L + (c->tp_size > 1) +
+    const int64_t v[17] = {c->has_model ? (c->mega ? 1 : bt_only(c) ? bt_launches(c, 1) + 2 : 2 + 5LL * c->L + (c->tp_size > 1) +
                                                    (c->layers[0].down2.cols ? (int64_t)c->L : 0) +
                                                    (c->streaming ? 7LL * (c->L - c->n_resident) : 0))
                                        : 0,
@@ -1607,8 +1608,9 @@ SS_API int ss_cuda_stats(const ss_cuda_ctx_t* ctx, int64_t* out, int32_t n) {
                            (int64_t)c->layer_stride,
                            !c->streaming ? 0 : c->host_reg ? 1 : c->host_pinned ? 2 : 3,
                            arch,
-                           c->has_model && c->tiled ? bt_launches(c, 1) + 1 : 0};
-    for (int i = 0; i < n && i < 16; i++) out[i] = v[i];
+                           c->has_model && c->tiled ? bt_launches(c, 1) + 1 : 0,
+                           c->ops_run};
+    for (int i = 0; i < n && i < 17; i++) out[i] = v[i];
   });
 }
 

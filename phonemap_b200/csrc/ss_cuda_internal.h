@@ -218,6 +218,7 @@ struct Context {
   bool graph_pdl = false;
   int host_pos = 0;  // host shadow of ctrl->pos for bounds checks
   long long steps_run = 0;
+  long long ops_run = 0;  // op-level matvecs served (ss_cuda_matvec*)
 
   // op-level (Metal-twin) state
   std::unordered_map<const void*, OpCacheEntry> op_cache;

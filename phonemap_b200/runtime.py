@@ -323,12 +323,12 @@ class CudaModel:
         return int(self._lib.ss_cuda_stream(self._h) or 0)
 
     def stats(self) -> dict:
-        v = np.zeros(16, np.int64)
-        _check(self._lib.ss_cuda_stats(self._h, v.ctypes.data_as(_i64p), 16))
+        v = np.zeros(17, np.int64)
+        _check(self._lib.ss_cuda_stats(self._h, v.ctypes.data_as(_i64p), 17))
         keys = ("kernels_per_step", "weight_bytes", "kv_bytes", "attn_splits", "pdl",
                 "steps_run", "qkv_ctas", "down_ctas", "persistent", "ring_slots",
                 "resident_layers", "streamed_bytes", "layer_bytes", "stream_source",
-                "kernel_arch", "kernels_per_batched_step")
+                "kernel_arch", "kernels_per_batched_step", "matvecs_run")
         return {k: int(x) for k, x in zip(keys, v)}
 
     KERNELS = {"qkv": 0, "attention": 1, "o": 2, "gate_up": 3, "down": 4, "lm_head": 5, "step": 6,

@@ -6,6 +6,8 @@ import ctypes
 import os
 import re
 
+import pytest
+
 from phonemap_b200 import build, runtime
 
 HEADER = os.path.join(build.INCLUDE, "slipstream_cuda.h")
@@ -36,3 +38,17 @@ def test_built_for_sm100a_only():
     """The build compiles for sm_100a and nothing else (the loaded kernels'
     binary version is checked on the GPU: tests/test_gpu_kernels.py)."""
     assert build.ARCH_FLAGS == ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def test_integration_build_links_backend():
+    """oracle/_ref/libss_ref_cuda.so (the reference with the INTEGRATION.md
+    hook, where the reference sources were present at build time) loads and
+    binds this library's matvec entry points."""
+    import ctypes
+
+    import oracle
+    path = os.path.join(oracle.REF_DIR, "libss_ref_cuda.so")
+    if not os.path.exists(path):
+        pytest.skip("integration build absent")
+    lib = ctypes.CDLL(path)
+    assert hasattr(lib, "ssr_attach_cuda") and hasattr(lib, "ssr_forward")
