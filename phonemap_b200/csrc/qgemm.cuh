@@ -56,8 +56,9 @@ namespace ss {
 constexpr int kQgRows = 128;        // weight rows per tile (UMMA M)
 constexpr int kQgMaxT = 32;         // tokens per product (N = 2 * 32 = 64 at most)
 constexpr int kQgStages = 4;        // ring stages
-constexpr int kQgMathWarps = 16;    // four warpgroups: each covers all 128 TMEM lanes
-constexpr int kQgThreads = 32 * (2 + kQgMathWarps);  // producer, MMA issuer, math warps
+constexpr int kQgUnpackWarps = 16;  // four warpgroups: each covers all 128 TMEM lanes
+constexpr int kQgFlushWarps = 8;    // two per TMEM lane quadrant (each half of the tokens)
+constexpr int kQgThreads = 32 * (2 + kQgUnpackWarps + kQgFlushWarps);  // + producer, MMA issuer
 constexpr int kQgACols = 16;        // TMEM columns of one block of A (128 rows x 32 fp16)
 constexpr int kQgTmemCols = 512;    // D regions, then A buffers
 
@@ -221,19 +222,6 @@ __host__ __device__ constexpr int qg_canon16(int row, int k) {
   return (row >> 3) * 512 + (k >> 3) * 128 + (row & 7) * 16 + (k & 7) * 2;
 }
 
-// Wait on an mbarrier phase with a budget; false on expiry (error bit 4).
-SS_DEVINL bool qg_wait(uint32_t bar, uint32_t parity, const QGemmParams& p) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > p.wait_budget) {
-      atomicOr(p.err, 4);
-      return false;
-    }
-  }
-  return true;
-}
-
 // ---- activation planes -----------------------------------------------------
 
 // The pieces are built by bt_prep_kernel (batch_kernels.cuh): per token, the
@@ -265,17 +253,6 @@ SS_DEVINL void qg_unit(const QGemmParams& p, int u, int& tile, int& split, int& 
   split = u - tile * p.nsplit;
   c0 = (int)((long long)p.nchunks * split / p.nsplit);
   c1 = (int)((long long)p.nchunks * (split + 1) / p.nsplit);
-}
-
-SS_DEVINL bool qg_any(bool pred) {  // barrier over the 256 math threads that ORs a predicate
-  uint32_t r;
-  asm volatile(
-      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n"
-      " barrier.red.or.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}\n"
-      : "=r"(r)
-      : "r"((uint32_t)pred), "n"(32 * kQgMathWarps)
-      : "memory");
-  return r != 0;
 }
 
 // Two words of Q4_0 quant bytes (bytes 8 j .. 8 j + 7 of a block) -> the
@@ -313,14 +290,17 @@ SS_DEVINL void q8_to_f16x8(uint32_t w0, uint32_t w1, uint32_t (&h)[4]) {
 }
 
 // Warp roles: warp 0 (one lane) feeds the ring; warp 1 issues the MMAs (one
-// elected lane); warps 2..17 unpack A and flush D -- warp w owns TMEM lanes
-// 32 (w % 4) .. +31 (weight rows), warpgroup g = (w - 2) / 4 unpacks elements
-// 8 g .. 8 g + 7 of each block (one core matrix) and flushes tokens
-// g TP/4 .. (g + 1) TP/4 - 1.  The roles meet only at mbarriers: a group's A
-// written (a_ready, 16 warp arrivals), its MMAs done (dfull, a commit), its
-// TMEM region flushed (d_free, 16 arrivals), a stage's slot free (empty).
+// elected lane); warps 2..17 unpack A -- warp w writes TMEM lanes
+// 32 (w % 4) .. +31 (weight rows), warpgroup g = (w - 2) / 4 elements
+// 8 g .. 8 g + 7 of each block (one core matrix); warps 18..25 flush D -- the
+// same lane quadrants, tokens (w - 18) / 4 * TP/2 .. + TP/2 - 1.  The roles
+// meet only at mbarriers: a group's A written (a_ready, 16 warp arrivals),
+// its MMAs done (dfull, a commit), its TMEM region flushed (d_free, 8
+// arrivals), a stage's slot free (empty: its quants unpacked and its last
+// group flushed, 24 arrivals).  Unpacking the next group, the MMAs of this
+// one and the flush of the previous one run at the same time.
 template <int TYPE, int TP>
-__global__ void __maxnreg__(96)
+__global__ void __maxnreg__(72)
     qgemm_kernel(const QGemmParams p, const __grid_constant__ CUtensorMap qmap,
                  const __grid_constant__ CUtensorMap smap) {
   constexpr int KC = qg_kc(TYPE);
@@ -348,12 +328,12 @@ __global__ void __maxnreg__(96)
     s_abort = 0;
     for (int i = 0; i < kQgStages; i++) {
       mbar_init(smem_addr(full + i), 1);
-      mbar_init(smem_addr(empty + i), kQgMathWarps);
+      mbar_init(smem_addr(empty + i), kQgUnpackWarps + kQgFlushWarps);
     }
     for (int i = 0; i < 2; i++) {
       mbar_init(smem_addr(dfull + i), 1);
-      mbar_init(smem_addr(a_ready + i), kQgMathWarps);
-      mbar_init(smem_addr(d_free + i), kQgMathWarps);
+      mbar_init(smem_addr(a_ready + i), kQgUnpackWarps);
+      mbar_init(smem_addr(d_free + i), kQgFlushWarps);
     }
     mbar_fence_init();
   }
@@ -380,6 +360,7 @@ __global__ void __maxnreg__(96)
     }
     return true;
   };
+  constexpr int kEndWarps = 1 + kQgUnpackWarps + kQgFlushWarps;  // issuer + unpack + flush
 
   if (warp == 0) {
     // ---------------- producer
@@ -454,74 +435,82 @@ __global__ void __maxnreg__(96)
       mbar_wait_bounded(smem_addr(dfull + (last & 1)), (uint32_t)((last >> 1) & 1), p.wait_budget);
     }
     tc_fence_before();
-    named_bar_sync(1, 32 * (kQgMathWarps + 1));
+    named_bar_sync(1, 32 * kEndWarps);
     tc_fence_after();
     tmem_dealloc(tmem, kQgTmemCols);
     return;
   }
 
-  // ---------------- math warps (2..17)
-  pdl_wait();  // post[] and the outputs' previous readers
   const int q = warp & 3;                 // TMEM lane quadrant of this warp
   const int r = 32 * q + lane;            // weight row within the tile
-  const int g = (warp - 2) >> 2;          // warpgroup 0..3
-  constexpr int th = TP >> 2;             // tokens flushed per warpgroup (2, 4 or 8)
   const uint32_t t_lane = tmem + ((uint32_t)(32 * q) << 16);
-  float acc[th];
-  int gc = 0;        // groups unpacked by this CTA
-  int sc = 0;        // stages consumed
-  bool bad = false;
-  int pend = -1;     // group whose MMAs were requested and not yet flushed (its gc)
-  int pend_slot = 0, pend_blk = 0;
-  bool pend_last = false;  // the pending group is its stage's last
-  // this thread's quant bytes of a block: Q4_0 bytes 8 (g & 1) .. +7 (low
-  // nibbles for g < 2, high for g >= 2); Q8_0 bytes 8 g .. 8 g + 7
-  const int qchunk_off = TYPE == kQ4_0 ? 0 : (g >> 1);
-  const uint32_t qbyte = (uint32_t)(8 * (g & 1));
-
-  // Flushes the pending group (its MMAs done): its TMEM region (pend & 1),
-  // the scales of its blocks; frees the region, and the ring slot after the
-  // stage's last group.
-  auto flush_group = [&]() {
-    const uint32_t region = (uint32_t)((pend & 1) * G * 2 * TP);
-    const uint8_t* sst = smem + pend_slot * SB + QgSmem::kQuant;
-    constexpr int BW = th == 8 ? 2 : 4;  // blocks' loads in flight per wait
-#pragma unroll
-    for (int b0 = 0; b0 < G; b0 += BW) {
-      int hv[BW][th], lv[BW][th];
-#pragma unroll
-      for (int j = 0; j < BW; j++) {
-        const uint32_t col = t_lane + region + (uint32_t)((b0 + j) * 2 * TP + g * th);
-        if constexpr (th == 8) {
-          tmem_ld8p(col, hv[j]);
-          tmem_ld8p(col + (uint32_t)TP, lv[j]);
-        } else if constexpr (th == 4) {
-          tmem_ld4(col, hv[j]);
-          tmem_ld4(col + (uint32_t)TP, lv[j]);
-        } else {
-          tmem_ld2(col, hv[j]);
-          tmem_ld2(col + (uint32_t)TP, lv[j]);
+  if (warp < 2 + kQgUnpackWarps) {
+    // ---------------- unpack warps (2..17)
+    const int g = (warp - 2) >> 2;        // warpgroup 0..3
+    // this thread's quant bytes of a block: Q4_0 bytes 8 (g & 1) .. +7 (low
+    // nibbles for g < 2, high for g >= 2); Q8_0 bytes 8 g .. 8 g + 7
+    const int qchunk_off = TYPE == kQ4_0 ? 0 : (g >> 1);
+    const uint32_t qbyte = (uint32_t)(8 * (g & 1));
+    int gc = 0, sc = 0;
+    bool bad = false;
+    for (int u = blockIdx.x; u < nunits && !bad; u += gridDim.x) {
+      int tile, split, c0, c1;
+      qg_unit(p, u, tile, split, c0, c1);
+      for (int c = c0; c < c1 && !bad; c++, sc++) {
+        const int s = sc % kQgStages;
+        if (!wait(full + s, (uint32_t)((sc / kQgStages) & 1))) {
+          bad = true;
+          break;
         }
-      }
-      tmem_ld_wait();
+        const uint32_t qrow = smem_addr(smem + s * SB) + (uint32_t)(r * 128);
+#pragma unroll 1
+        for (int h = 0; h < NG; h++, gc++) {
+          // A buffer (gc & 1) was last read by the MMAs of group gc - 2
+          if (gc >= 2 && !wait(dfull + (gc & 1), (uint32_t)(((gc - 2) >> 1) & 1))) {
+            bad = true;
+            break;
+          }
+          tc_fence_after();
+          // this warp writes its 32 lanes, columns 4 g .. 4 g + 3 of each block
+          const uint32_t ab = t_lane + kACol0 + (uint32_t)((gc & 1) * G * kQgACols + 4 * g);
+          uint32_t w[G][2];
 #pragma unroll
-      for (int j = 0; j < BW; j++) {
-        const int blk = pend_blk + b0 + j;
-        const float d = half_bits_to_float(
-            *reinterpret_cast<const uint16_t*>(sst + (((r >> 2) * KC + blk) * 4 + (r & 3)) * 2));
+          for (int bl = 0; bl < G; bl++) {
+            const int blk = h * G + bl;  // block within the stage
+            const int chunk = TYPE == kQ4_0 ? blk : 2 * blk + qchunk_off;
+            asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];"
+                         : "=r"(w[bl][0]), "=r"(w[bl][1])
+                         : "r"(qrow + ((chunk ^ (r & 7)) << 4) + qbyte));
+          }
 #pragma unroll
-        for (int i = 0; i < th; i++) acc[i] = fmaf(__int_as_float(hv[j][i]) + __int_as_float(lv[j][i]), d, acc[i]);
+          for (int bl = 0; bl < G; bl++) {
+            uint32_t hh[4];
+            if constexpr (TYPE == kQ4_0) q4_to_f16x8(w[bl][0], w[bl][1], g >= 2, hh);
+            else q8_to_f16x8(w[bl][0], w[bl][1], hh);
+            tmem_st4(ab + (uint32_t)(bl * kQgACols), hh);
+          }
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_addr(a_ready + (gc & 1)));
+        }
+        if (bad) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(empty + s));  // this stage's quants are read
       }
     }
     tc_fence_before();
-    __syncwarp();
-    if (lane == 0) {
-      mbar_arrive(smem_addr(d_free + (pend & 1)));
-      if (pend_last) mbar_arrive(smem_addr(empty + pend_slot));
-    }
-    pend = -1;
-  };
+    named_bar_sync(1, 32 * kEndWarps);
+    return;
+  }
 
+  // ---------------- flush warps (18..25)
+  pdl_wait();  // post[] and the outputs' previous readers
+  constexpr int th = TP >> 1;             // tokens flushed per warp (4, 8 or 16)
+  const int t0 = ((warp - 2 - kQgUnpackWarps) >> 2) * th;
+  float acc[th];
+  int gc = 0, sc = 0;
+  bool bad = false;
   for (int u = blockIdx.x; u < nunits && !bad; u += gridDim.x) {
     int tile, split, c0, c1;
     qg_unit(p, u, tile, split, c0, c1);
@@ -529,71 +518,60 @@ __global__ void __maxnreg__(96)
     for (int i = 0; i < th; i++) acc[i] = 0.0f;
     for (int c = c0; c < c1 && !bad; c++, sc++) {
       const int s = sc % kQgStages;
-      if (!wait(full + s, (uint32_t)((sc / kQgStages) & 1))) {
+      if (!wait(full + s, (uint32_t)((sc / kQgStages) & 1))) {  // the stage's scales
         bad = true;
         break;
       }
-      const uint32_t qrow = smem_addr(smem + s * SB) + (uint32_t)(r * 128);
+      const uint8_t* sst = smem + s * SB + QgSmem::kQuant;
 #pragma unroll 1
       for (int h = 0; h < NG; h++, gc++) {
-        // A buffer (gc & 1) was last read by the MMAs of group gc - 2, which
-        // completed before group gc - 2 was flushed (below, one group ago);
-        // this warp writes its 32 lanes, columns 4 g .. 4 g + 3 of each block
-        const uint32_t ab = t_lane + kACol0 + (uint32_t)((gc & 1) * G * kQgACols + 4 * g);
-        uint32_t w[G][2];
+        if (!wait(dfull + (gc & 1), (uint32_t)((gc >> 1) & 1))) {
+          bad = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t region = (uint32_t)((gc & 1) * G * 2 * TP);
 #pragma unroll
         for (int bl = 0; bl < G; bl++) {
-          const int blk = h * G + bl;  // block within the stage
-          const int chunk = TYPE == kQ4_0 ? blk : 2 * blk + qchunk_off;
-          asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];"
-                       : "=r"(w[bl][0]), "=r"(w[bl][1])
-                       : "r"(qrow + ((chunk ^ (r & 7)) << 4) + qbyte));
-        }
+          int hv[th], lv[th];
+          const uint32_t col = t_lane + region + (uint32_t)(bl * 2 * TP + t0);
+          if constexpr (th == 16) {
+            tmem_ld16(col, hv);
+            tmem_ld16(col + (uint32_t)TP, lv);
+          } else if constexpr (th == 8) {
+            tmem_ld8p(col, hv);
+            tmem_ld8p(col + (uint32_t)TP, lv);
+          } else {
+            tmem_ld4(col, hv);
+            tmem_ld4(col + (uint32_t)TP, lv);
+          }
+          const int blk = h * G + bl;
+          const float d = half_bits_to_float(
+              *reinterpret_cast<const uint16_t*>(sst + (((r >> 2) * KC + blk) * 4 + (r & 3)) * 2));
+          tmem_ld_wait();
 #pragma unroll
-        for (int bl = 0; bl < G; bl++) {
-          uint32_t hh[4];
-          if constexpr (TYPE == kQ4_0) q4_to_f16x8(w[bl][0], w[bl][1], g >= 2, hh);
-          else q8_to_f16x8(w[bl][0], w[bl][1], hh);
-          tmem_st4(ab + (uint32_t)(bl * kQgACols), hh);
+          for (int i = 0; i < th; i++) acc[i] = fmaf(__int_as_float(hv[i]) + __int_as_float(lv[i]), d, acc[i]);
         }
-        tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_addr(a_ready + (gc & 1)));
-        // the previous group, while this group's MMAs run
-        if (pend >= 0) {
-          if (!wait(dfull + (pend & 1), (uint32_t)((pend >> 1) & 1))) {
-            bad = true;
-            break;
-          }
-          tc_fence_after();
-          flush_group();
+        if (lane == 0) {
+          mbar_arrive(smem_addr(d_free + (gc & 1)));
+          if (h == NG - 1) mbar_arrive(smem_addr(empty + s));  // the stage's last group is flushed
         }
-        pend = gc;
-        pend_slot = s;
-        pend_blk = h * G;
-        pend_last = h == NG - 1;
       }
     }
     if (bad) break;
-    // the unit's last group, then its partial sums
-    if (!wait(dfull + (pend & 1), (uint32_t)((pend >> 1) & 1))) {
-      bad = true;
-      break;
-    }
-    tc_fence_after();
-    flush_group();
     const int row = tile * kQgRows + r;
     if (row < p.rows) {
 #pragma unroll
       for (int i = 0; i < th; i++) {
-        const int t = g * th + i;
+        const int t = t0 + i;
         if (t < p.T) p.out[((size_t)split * p.T + t) * p.rows + row] = acc[i] * p.post[t];
       }
     }
   }
   tc_fence_before();
-  named_bar_sync(1, 32 * (kQgMathWarps + 1));
+  named_bar_sync(1, 32 * kEndWarps);
 }
 
 }  // namespace ss
