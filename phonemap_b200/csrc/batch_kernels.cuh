@@ -378,9 +378,14 @@ SS_DEVINL float prep_elem(const PrepParams& p, int tr, int i, const float* mf, c
     const int h = i / p.hd, e = i - h * p.hd;
     const int ns = min(kBtAttnSlots, p.bt.pos[tr] / kBtAttnChunk + 1);
     const float* pp = p.apart + ((size_t)tr * p.nh + h) * kBtAttnSlots * (p.hd + 2) + 2 + e;
+    // every slot's load issued before the chain of fmas that uses them
+    float o[kBtAttnSlots];
+#pragma unroll
+    for (int s2 = 0; s2 < kBtAttnSlots; s2++) o[s2] = s2 < ns ? pp[(size_t)s2 * (p.hd + 2)] : 0.0f;
     float acc = 0.0f;
-#pragma unroll 1
-    for (int s2 = 0; s2 < ns; s2++) acc = fmaf(pp[(size_t)s2 * (p.hd + 2)], mf[h * kBtAttnSlots + s2], acc);
+#pragma unroll
+    for (int s2 = 0; s2 < kBtAttnSlots; s2++)
+      if (s2 < ns) acc = fmaf(o[s2], mf[h * kBtAttnSlots + s2], acc);
     return acc * minv[h];
   }
 }
@@ -432,7 +437,7 @@ __global__ void __launch_bounds__(512) bt_prep_kernel(const PrepParams p) {
       __syncthreads();
     }
     float ss = 0.0f, amax = 0.0f;
-#pragma unroll 1
+#pragma unroll 2
     for (int i = i0 + (int)threadIdx.x; i < i1; i += blockDim.x) {
       const float v = prep_elem<MODE>(p, tr, i, mf, minv);
       vals[i - i0] = v;
