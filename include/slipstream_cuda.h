@@ -138,10 +138,13 @@ int ss_cuda_stats(const ss_cuda_ctx_t *ctx, int64_t *out, int32_t n);
  * or 6 the whole decode step (steps at the current position onwards), or 7
  * the tensor-core gate/up product of max_batch tokens (the kernel alone, its
  * activation pieces built once before), or 8 the same for layer 0's Q/K/V
- * matrix at every launch (L2-resident where it fits), and writes the average
- * milliseconds per launch.  0..5 exist only in the multi-kernel step, 7 and 8
- * only where the matrices are in the tiled layout.  Clobbers the activations and the K/V rows it passes
- * over; call ss_cuda_reset before decoding again. */
+ * matrix at every launch (L2-resident where it fits), or 9 / 10 one sampler
+ * draw (ss_cuda_sample) over the last step's logits with temperature 0.8,
+ * top_p 0.95, top_k 40 / temperature 1, top_p 0.95, no top-k, and writes the
+ * average milliseconds per launch.  0..5 exist only in the multi-kernel step,
+ * 7 and 8 only where the matrices are in the tiled layout.  Clobbers the
+ * activations and the K/V rows it passes over; call ss_cuda_reset before
+ * decoding again. */
 int ss_cuda_time_kernel(ss_cuda_ctx_t *ctx, int32_t which, int32_t iters, float *ms_per_launch);
 /* Device bytes of the weights one launch of kernel `which` streams (layer 0;
  * repacked layout, i.e. the GGUF bytes plus row padding; 6: every weight
@@ -236,6 +239,41 @@ int ss_cuda_decode_greedy(ss_cuda_ctx_t *ctx, int32_t token, int32_t start_pos, 
 int ss_cuda_decode_begin(ss_cuda_ctx_t *ctx, int32_t token, int32_t pos);
 int ss_cuda_decode_steps(ss_cuda_ctx_t *ctx, int32_t n_steps);
 int ss_cuda_decode_read(ss_cuda_ctx_t *ctx, int32_t first_pos, int32_t n, int32_t *ids_out);
+/* ---- sampling on the device: ss_sample (SlipStream/src/core/tensor.c:363-451)
+ * temperature <= 0: the greedy argmax (tensor.c:318-328) and the RNG state is
+ * neither read nor changed (rng_state may be NULL).  Otherwise: logits /
+ * temperature (NaN logits as -FLT_MAX), softmax, top-k (top_k in 1..n-1: the
+ * probabilities below the k-th largest are zeroed), top-p (top_p in (0, 1):
+ * the sorted probabilities are added high to low until the sum reaches top_p,
+ * those below the one reached are zeroed), renormalisation, and a draw with
+ * xorshift64 (tensor.c:331-342) that advances *rng_state once -- every
+ * running sum in the reference's order, so the result is the reference's
+ * token for the same logits and state (the exponential is evaluated in double
+ * precision; libm's expf differs in the last bit for about 1 input in 1,600).
+ * One CTA on the context's stream; scratch of 3 floats per logit, grown on
+ * first use.  Synchronous. */
+/* ss_sample over caller logits (host memory, n floats; 1 <= n <= 16,777,216);
+ * works on a context without a model too. */
+int ss_cuda_sample_logits(ss_cuda_ctx_t *ctx, const float *logits, int32_t n, float temperature, float top_p,
+                          int32_t top_k, uint64_t *rng_state, int32_t *token_out);
+/* ss_sample over the logits of the context's last single-sequence step
+ * (ss_cuda_forward / _prefill / _decode_*), which stay on the device.  Tensor
+ * parallelism: every rank calls it (the logits are gathered) and all draw the
+ * same token. */
+int ss_cuda_sample(ss_cuda_ctx_t *ctx, float temperature, float top_p, int32_t top_k, uint64_t *rng_state,
+                   int32_t *token_out);
+/* The generation loop of ss_generate (engine.c:233-289) without a host round
+ * trip per token: ids_out[0] is drawn from the context's current logits (those
+ * for position start_pos, e.g. after a prefill of start_pos tokens), and for
+ * t >= 1 ids_out[t] is drawn from the logits of the decode step that took
+ * ids_out[t - 1] at position start_pos + t - 1.  n_tokens draws and n_tokens - 1
+ * steps (start_pos + n_tokens - 1 <= ctx); *rng_state advances once per draw.
+ * The caller ends the text at an EOS or stop string itself.  Afterwards the
+ * context's position is the last draw's, so ss_cuda_decode_steps continues
+ * from that token. */
+int ss_cuda_decode_sample(ss_cuda_ctx_t *ctx, int32_t start_pos, int32_t n_tokens, float temperature,
+                          float top_p, int32_t top_k, uint64_t *rng_state, int32_t *ids_out);
+
 /* The cudaStream_t all work of this context runs on. */
 void *ss_cuda_stream(ss_cuda_ctx_t *ctx);
 /* Clears the KV cache (ss_scheduler_reset, layer_scheduler.c:917-936). */

@@ -271,3 +271,48 @@ def oracle_ops():
     lib.sso_f16_to_f32.argtypes = [ctypes.c_uint16]
     lib.sso_f16_to_f32.restype = ctypes.c_float
     return lib
+
+
+_u64p = ctypes.POINTER(ctypes.c_uint64)
+
+
+def _sample_args(fn) -> None:
+    fn.argtypes = [_f32p, ctypes.c_int32, ctypes.c_float, ctypes.c_float, ctypes.c_int32, _u64p]
+    fn.restype = ctypes.c_int32
+
+
+def sample(logits: np.ndarray, temperature: float, top_p: float, top_k: int, state: int,
+           exp_mode: int = 0) -> tuple[int, int]:
+    """ss_sample restated (oracle/ss_oracle.c): (token, new RNG state).
+    exp_mode 0 is libm's expf, as the reference; 1 the GPU sampler's
+    double-precision exponential."""
+    lib = ctypes.CDLL(build_oracle())
+    fn = lib.sso_sample
+    fn.argtypes = [_f32p, ctypes.c_int32, ctypes.c_float, ctypes.c_float, ctypes.c_int32, _u64p,
+                   ctypes.c_int]
+    fn.restype = ctypes.c_int32
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    st = ctypes.c_uint64(state)
+    tok = fn(_fp(lg), lg.size, temperature, top_p, int(top_k), ctypes.byref(st), int(exp_mode))
+    return int(tok), int(st.value)
+
+
+def exp_dd(x: np.ndarray) -> np.ndarray:
+    """The GPU sampler's exponential, restated (sso_exp_dd)."""
+    lib = ctypes.CDLL(build_oracle())
+    lib.sso_exp_dd_array.argtypes = [_f32p, _f32p, ctypes.c_int32]
+    xa = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty_like(xa)
+    lib.sso_exp_dd_array(_fp(xa), _fp(out), xa.size)
+    return out
+
+
+def ref_sample(logits: np.ndarray, temperature: float, top_p: float, top_k: int,
+               state: int) -> tuple[int, int]:
+    """The reference's own ss_sample (tensor.c:363-451, oracle/_ref build)."""
+    lib = ctypes.CDLL(os.path.join(REF_DIR, "libss_ref.so"))
+    _sample_args(lib.ss_sample)
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    st = ctypes.c_uint64(state)
+    tok = lib.ss_sample(_fp(lg), lg.size, temperature, top_p, int(top_k), ctypes.byref(st))
+    return int(tok), int(st.value)

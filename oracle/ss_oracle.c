@@ -560,3 +560,125 @@ int sso_embed(sso_model_t *m, const int32_t *tokens, int32_t n, float *out) {
     free(bh);
     return 0;
 }
+
+/* ---------------------------------------------------------------- sampling */
+
+/* e^x rounded to float from a double-precision evaluation (the sampler's
+ * exponential on the GPU, written out the same way here so both round
+ * identically): k = rint(x log2 e), r = x - k ln2 in two fma steps (ln2 split
+ * into a 33-bit head, so k * head is exact, and a tail), e^r by its Taylor
+ * series to degree 13 in Horner form (truncation below 5e-18 for |r| <= ln2/2),
+ * times 2^k built from the exponent bits, then one float rounding.  Every step
+ * is an IEEE basic operation or fma, so any machine gives the same bits. */
+static const double kExpInvFact[14] = {
+    0x1.0000000000000p+0,  0x1.0000000000000p+0,  0x1.0000000000000p-1,  0x1.5555555555555p-3,
+    0x1.5555555555555p-5,  0x1.1111111111111p-7,  0x1.6c16c16c16c17p-10, 0x1.a01a01a01a01ap-13,
+    0x1.a01a01a01a01ap-16, 0x1.71de3a556c734p-19, 0x1.27e4fb7789f5cp-22, 0x1.ae64567f544e4p-26,
+    0x1.1eed8eff8d898p-29, 0x1.6124613a86d09p-33};
+
+float sso_exp_dd(float xf) {
+    if (xf != xf) return xf;
+    if (xf < -200.0f) return 0.0f;
+    if (xf > 200.0f) return INFINITY;
+    const double x = (double)xf;
+    const double k = rint(x * 0x1.71547652b82fep+0);
+    double r = fma(-k, 0x1.62e42ff000000p-1, x);
+    r = fma(-k, -0x1.718432a1b0e26p-35, r);
+    double p = kExpInvFact[13];
+    for (int i = 12; i >= 0; i--) p = fma(p, r, kExpInvFact[i]);
+    const uint64_t bits = (uint64_t)((int64_t)k + 1023) << 52;
+    double s;
+    memcpy(&s, &bits, 8);
+    return (float)(p * s);
+}
+
+void sso_exp_dd_array(const float *x, float *out, int32_t n) {
+    for (int32_t i = 0; i < n; i++) out[i] = sso_exp_dd(x[i]);
+}
+
+/* SS/src/core/tensor.c:331-342: xorshift64, and the top 53 bits as a float in
+ * [0, 1] (the uint64 -> float conversion rounds to nearest). */
+static uint64_t sso_xorshift64(uint64_t *s) {
+    uint64_t x = *s;
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    *s = x;
+    return x;
+}
+float sso_rand_float(uint64_t *state) {
+    return (float)(sso_xorshift64(state) >> 11) / (float)(1ULL << 53);
+}
+
+typedef struct { int32_t id; float p; } sso_cand_t;
+
+/* Descending by probability, NaN read as 0 (tensor.c:350-361). */
+static int sso_cand_cmp(const void *a, const void *b) {
+    float pa = ((const sso_cand_t *)a)->p, pb = ((const sso_cand_t *)b)->p;
+    if (pa != pa) pa = 0.0f;
+    if (pb != pb) pb = 0.0f;
+    return pa > pb ? -1 : pa < pb ? 1 : 0;
+}
+
+/* SS/src/core/tensor.c:363-451 (ss_sample).  temperature <= 0: the greedy
+ * argmax.  Otherwise: NaN logits -> -FLT_MAX, logits / temperature, softmax
+ * (tensor.c:154-173, one sequential fp32 sum), the candidates sorted by
+ * probability (descending), top-k: probabilities below the k-th largest
+ * zeroed; top-p: walk the sorted candidates adding the (top-k filtered)
+ * positive probabilities in order until the sum reaches top_p, the probability
+ * there is the cutoff and those below it are zeroed; renormalise by one more
+ * sequential sum when it is positive; draw r and return the first index whose
+ * running sum exceeds r (the last index when none does).  exp_mode 0 uses
+ * libm's expf as the reference does, 1 sso_exp_dd (the GPU sampler's
+ * exponential).  Ties in the sort can be ordered either way: equal
+ * probabilities add the same values to the running sum in any order. */
+int32_t sso_sample(const float *logits, int32_t n, float temperature, float top_p, int32_t top_k,
+                   uint64_t *rng_state, int exp_mode) {
+    if (temperature <= 0.0f) return sso_argmax(logits, n);
+    float *pr = (float *)malloc((size_t)n * sizeof(float));
+    sso_cand_t *cand = (sso_cand_t *)malloc((size_t)n * sizeof(sso_cand_t));
+    for (int32_t i = 0; i < n; i++) pr[i] = logits[i] != logits[i] ? -FLT_MAX : logits[i] / temperature;
+    float mx = -FLT_MAX;
+    for (int32_t i = 0; i < n; i++) if (pr[i] > mx) mx = pr[i];
+    float sum = 0.0f;
+    for (int32_t i = 0; i < n; i++) {
+        pr[i] = exp_mode ? sso_exp_dd(pr[i] - mx) : expf(pr[i] - mx);
+        sum += pr[i];
+    }
+    const float inv = 1.0f / sum;
+    for (int32_t i = 0; i < n; i++) pr[i] *= inv;
+    for (int32_t i = 0; i < n; i++) {
+        cand[i].id = i;
+        cand[i].p = pr[i] != pr[i] ? 0.0f : pr[i];
+    }
+    qsort(cand, (size_t)n, sizeof(sso_cand_t), sso_cand_cmp);
+    if (top_k > 0 && top_k < n) {
+        const float thr = cand[top_k - 1].p;
+        for (int32_t i = 0; i < n; i++) if (pr[i] < thr) pr[i] = 0.0f;
+    }
+    if (top_p > 0.0f && top_p < 1.0f) {
+        float acc = 0.0f, cutoff = 0.0f;
+        for (int32_t i = 0; i < n; i++) {
+            const float pv = pr[cand[i].id];
+            if (pv > 0.0f) acc += pv;
+            if (acc >= top_p) { cutoff = pv; break; }
+        }
+        for (int32_t i = 0; i < n; i++) if (pr[i] < cutoff) pr[i] = 0.0f;
+    }
+    free(cand);
+    float tot = 0.0f;
+    for (int32_t i = 0; i < n; i++) tot += pr[i];
+    if (tot > 0.0f) {
+        const float rinv = 1.0f / tot;
+        for (int32_t i = 0; i < n; i++) pr[i] *= rinv;
+    }
+    const float r = sso_rand_float(rng_state);
+    float cdf = 0.0f;
+    int32_t pick = n - 1;
+    for (int32_t i = 0; i < n; i++) {
+        cdf += pr[i];
+        if (r < cdf) { pick = i; break; }
+    }
+    free(pr);
+    return pick;
+}

@@ -47,6 +47,14 @@ void sso_kv_encode(const float *src, int8_t *dst, float *scale, int32_t n);
 void sso_softmax(float *x, int32_t n);
 int32_t sso_argmax(const float *x, int32_t n);
 
+/* ss_sample (SlipStream/src/core/tensor.c:363-451); exp_mode 0: libm expf as
+ * the reference, 1: sso_exp_dd, the GPU sampler's exponential. */
+int32_t sso_sample(const float *logits, int32_t n, float temperature, float top_p, int32_t top_k,
+                   uint64_t *rng_state, int exp_mode);
+float sso_exp_dd(float x);
+void sso_exp_dd_array(const float *x, float *out, int32_t n);
+float sso_rand_float(uint64_t *state);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,447 @@
+// sample.cu -- ss_sample (SlipStream/src/core/tensor.c:363-451) on the device.
+//
+// The reference draws a token from a logits vector with four sequential fp32
+// running sums in a fixed order: the softmax denominator (index order,
+// tensor.c:161-165), the top-p walk over the probabilities sorted high to low
+// (tensor.c:404-421), the renormalisation (index order, :426-433) and the CDF
+// walk (index order, :437-448).  Each running sum rounds after every addition,
+// and on a near-flat distribution a different summation order moves the top-p
+// cutoff or the drawn index often, so this kernel keeps the reference's order
+// exactly: one thread adds, in order, while the rest of the CTA produces the
+// next tile of addends (the exponentials, the sorted keys, the filtered
+// probabilities) in shared memory.  Everything else is parallel and exact: the
+// maximum, the element-wise steps (IEEE division and multiplication, no
+// contraction), and the sort (a stable LSD radix sort of the probabilities'
+// bits; equal probabilities add the same values in any order, so ties need no
+// particular order).
+//
+// One CTA of 1024 threads does the whole draw -- the running sums are the
+// critical path and a single SM keeps the vectors (at most a few MB) in L2.
+// The exponential is e^x evaluated in double precision and rounded once to
+// float (the oracle restates the same steps); libm's expf, which the reference
+// calls, rounds differently in about one input in 1,600, which reaches a drawn
+// token only when that last bit moves a running sum across a threshold.
+#include "sample.h"
+
+#include <cfloat>
+#include <cstdint>
+
+namespace ss {
+namespace {
+
+constexpr int kSmpThreads = 1024;
+constexpr int kSmpWarps = kSmpThreads / 32;
+constexpr int kSmpTile = 4096;  // floats per tile of addends
+constexpr int kSmpBins = 256;   // radix digit: 8 bits
+
+struct SmpSmem {
+  float tile[2][kSmpTile];              // addends: tile k in tile[k & 1]
+  unsigned hist[kSmpWarps][kSmpBins];   // per-warp digit counts, then scatter cursors
+  unsigned digit_base[kSmpBins];
+  float redf[kSmpWarps];
+  int redi[kSmpWarps];
+  float bcast[4];
+};
+
+__host__ __device__ __forceinline__ size_t pad_n(int n) { return ((size_t)n + 63) & ~(size_t)63; }
+
+// 1/i! for i = 0..13, each rounded to double.
+__constant__ double kSmpInvFact[14] = {
+    0x1.0000000000000p+0,  0x1.0000000000000p+0,  0x1.0000000000000p-1,  0x1.5555555555555p-3,
+    0x1.5555555555555p-5,  0x1.1111111111111p-7,  0x1.6c16c16c16c17p-10, 0x1.a01a01a01a01ap-13,
+    0x1.a01a01a01a01ap-16, 0x1.71de3a556c734p-19, 0x1.27e4fb7789f5cp-22, 0x1.ae64567f544e4p-26,
+    0x1.1eed8eff8d898p-29, 0x1.6124613a86d09p-33};
+
+// e^x rounded to float: k = rint(x log2 e); r = x - k ln2 with ln2 split into
+// a 33-bit head (k * head exact for |k| < 2^20) and a tail; e^r by its Taylor
+// series to degree 13 (truncation < 5e-18 for |r| <= ln2 / 2); times 2^k from
+// the exponent bits; one rounding to float (float subnormals included).  Only
+// IEEE basic operations and fma, so the oracle's C restatement rounds
+// identically.
+__device__ __forceinline__ float smp_exp(float xf) {
+  if (xf != xf) return xf;
+  if (xf < -200.0f) return 0.0f;
+  if (xf > 200.0f) return __int_as_float(0x7f800000);
+  const double x = (double)xf;
+  const double k = rint(__dmul_rn(x, 0x1.71547652b82fep+0));
+  double r = __fma_rn(-k, 0x1.62e42ff000000p-1, x);
+  r = __fma_rn(-k, -0x1.718432a1b0e26p-35, r);
+  double p = kSmpInvFact[13];
+#pragma unroll
+  for (int i = 12; i >= 0; i--) p = __fma_rn(p, r, kSmpInvFact[i]);
+  const double s = __longlong_as_double((long long)((int)k + 1023) << 52);
+  return __double2float_rn(__dmul_rn(p, s));
+}
+
+// Streams the addends fill(0..n-1) through shared memory to thread 0: warps
+// 1..31 produce tile k + 1 while thread 0 runs eat(tile, first index, count)
+// over tile k, in order.  eat returning true ends the stream (every thread
+// leaves together: the end-of-tile barrier ORs the flag).
+template <class Fill, class Eat>
+__device__ __forceinline__ void smp_stream(int n, SmpSmem& sm, Fill fill, Eat eat) {
+  const int tid = threadIdx.x;
+  const int nt = (n + kSmpTile - 1) / kSmpTile;
+  if (tid >= 32) {
+    const int cnt = min(kSmpTile, n);
+    for (int j = tid - 32; j < cnt; j += kSmpThreads - 32) sm.tile[0][j] = fill(j);
+  }
+  __syncthreads();
+  for (int k = 0; k < nt; k++) {
+    bool stop = false;
+    if (tid >= 32) {
+      if (k + 1 < nt) {
+        const int base = (k + 1) * kSmpTile, cnt = min(kSmpTile, n - base);
+        float* t = sm.tile[(k + 1) & 1];
+        for (int j = tid - 32; j < cnt; j += kSmpThreads - 32) t[j] = fill(base + j);
+      }
+    } else if (tid == 0) {
+      const int base = k * kSmpTile;
+      stop = eat(sm.tile[k & 1], base, min(kSmpTile, n - base));
+    }
+    if (__syncthreads_or(stop)) break;
+  }
+}
+
+// s + t[0] + t[1] + ... in order, each addition rounded.
+__device__ __forceinline__ float smp_seq_sum(float s, const float* t, int cnt) {
+  int j = 0;
+  const float4* t4 = reinterpret_cast<const float4*>(t);
+#pragma unroll 4
+  for (; j + 4 <= cnt; j += 4) {
+    const float4 v = t4[j >> 2];
+    s = __fadd_rn(s, v.x);
+    s = __fadd_rn(s, v.y);
+    s = __fadd_rn(s, v.z);
+    s = __fadd_rn(s, v.w);
+  }
+  for (; j < cnt; j++) s = __fadd_rn(s, t[j]);
+  return s;
+}
+
+// The top-p walk over sorted probabilities (tensor.c:408-416): acc adds each
+// positive value in order; the first value at which acc >= top_p is the
+// cutoff.  Adding 0 in place of a non-positive (or NaN) value leaves acc
+// unchanged, so four additions run back to back and one comparison of the
+// fourth finds whether any reached top_p (acc never decreases).
+__device__ __forceinline__ bool smp_topp_walk(float& acc, float& cut, const float* t, int cnt, float top_p) {
+  auto pos = [](float v) { return v > 0.0f ? v : 0.0f; };
+  int j = 0;
+  const float4* t4 = reinterpret_cast<const float4*>(t);
+  for (; j + 4 <= cnt; j += 4) {
+    const float4 v = t4[j >> 2];
+    const float a1 = __fadd_rn(acc, pos(v.x));
+    const float a2 = __fadd_rn(a1, pos(v.y));
+    const float a3 = __fadd_rn(a2, pos(v.z));
+    const float a4 = __fadd_rn(a3, pos(v.w));
+    if (a4 >= top_p) {
+      cut = a1 >= top_p ? v.x : a2 >= top_p ? v.y : a3 >= top_p ? v.z : v.w;
+      acc = a4;
+      return true;
+    }
+    acc = a4;
+  }
+  for (; j < cnt; j++) {
+    acc = __fadd_rn(acc, pos(t[j]));
+    if (acc >= top_p) {
+      cut = t[j];
+      return true;
+    }
+  }
+  return false;
+}
+
+// The CDF walk (tensor.c:440-446): the first index whose running sum exceeds
+// r, or -1.  Each running sum is compared on its own (a NaN one compares
+// false, as in the reference).
+__device__ __forceinline__ int smp_cdf_walk(float& cdf, const float* t, int cnt, float r) {
+  int j = 0;
+  const float4* t4 = reinterpret_cast<const float4*>(t);
+  for (; j + 4 <= cnt; j += 4) {
+    const float4 v = t4[j >> 2];
+    const float c1 = __fadd_rn(cdf, v.x);
+    const float c2 = __fadd_rn(c1, v.y);
+    const float c3 = __fadd_rn(c2, v.z);
+    const float c4 = __fadd_rn(c3, v.w);
+    if (r < c1 || r < c2 || r < c3 || r < c4) return j + (r < c1 ? 0 : r < c2 ? 1 : r < c3 ? 2 : 3);
+    cdf = c4;
+  }
+  for (; j < cnt; j++) {
+    cdf = __fadd_rn(cdf, t[j]);
+    if (r < cdf) return j;
+  }
+  return -1;
+}
+
+// Descending sort of n keys (non-negative floats' bits) from ka, result in ka
+// (kb is the other buffer): four stable passes of 8-bit digits, lowest first.
+// Warp w owns the contiguous keys [w * seg, (w + 1) * seg); within a warp the
+// keys go in index order, 32 at a time, ranked among equal digits with
+// __match_any_sync, so every pass keeps the order of equal digits.
+__device__ void smp_sort_desc(unsigned* ka, unsigned* kb, int n, SmpSmem& sm) {
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int seg = ((n + kSmpWarps - 1) / kSmpWarps + 31) & ~31;
+  const int lo = min(n, w * seg), hi = min(n, lo + seg);
+  const unsigned lt = (1u << lane) - 1u;
+  unsigned* src = ka;
+  unsigned* dst = kb;
+  for (int pass = 0; pass < 4; pass++) {
+    const int sh = 8 * pass;
+    for (int i = tid; i < kSmpWarps * kSmpBins; i += kSmpThreads) (&sm.hist[0][0])[i] = 0u;
+    __syncthreads();
+    for (int base = lo; base < hi; base += 8 * 32) {
+      unsigned d[8];
+#pragma unroll
+      for (int r = 0; r < 8; r++) {
+        const int i = base + r * 32 + lane;
+        d[r] = i < hi ? 255u - ((src[i] >> sh) & 255u) : 256u;
+      }
+#pragma unroll
+      for (int r = 0; r < 8; r++) {
+        const unsigned peers = __match_any_sync(0xffffffffu, d[r]);
+        if (d[r] < 256u && lane == __ffs(peers) - 1) sm.hist[w][d[r]] += (unsigned)__popc(peers);
+        __syncwarp();
+      }
+    }
+    __syncthreads();
+    if (tid < kSmpBins) {
+      unsigned tot = 0;
+      for (int ww = 0; ww < kSmpWarps; ww++) tot += sm.hist[ww][tid];
+      sm.digit_base[tid] = tot;
+    }
+    __syncthreads();
+    if (w == 0) {  // exclusive scan of the 256 digit totals, 8 per lane
+      unsigned v[8], s = 0;
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        v[j] = sm.digit_base[lane * 8 + j];
+        s += v[j];
+      }
+      unsigned inc = s;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned t = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += t;
+      }
+      unsigned run = inc - s;
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        sm.digit_base[lane * 8 + j] = run;
+        run += v[j];
+      }
+    }
+    __syncthreads();
+    if (tid < kSmpBins) {  // cursors: digit-major, then warp order
+      unsigned run = sm.digit_base[tid];
+      for (int ww = 0; ww < kSmpWarps; ww++) {
+        const unsigned h = sm.hist[ww][tid];
+        sm.hist[ww][tid] = run;
+        run += h;
+      }
+    }
+    __syncthreads();
+    for (int base = lo; base < hi; base += 8 * 32) {
+      unsigned key[8], d[8];
+#pragma unroll
+      for (int r = 0; r < 8; r++) {
+        const int i = base + r * 32 + lane;
+        key[r] = i < hi ? src[i] : 0u;
+        d[r] = i < hi ? 255u - ((key[r] >> sh) & 255u) : 256u;
+      }
+#pragma unroll
+      for (int r = 0; r < 8; r++) {
+        const unsigned peers = __match_any_sync(0xffffffffu, d[r]);
+        const unsigned b = d[r] < 256u ? sm.hist[w][d[r]] : 0u;
+        if (d[r] < 256u) dst[b + (unsigned)__popc(peers & lt)] = key[r];
+        __syncwarp();
+        if (d[r] < 256u && lane == __ffs(peers) - 1) sm.hist[w][d[r]] = b + (unsigned)__popc(peers);
+        __syncwarp();
+      }
+    }
+    __syncthreads();
+    unsigned* t = src;
+    src = dst;
+    dst = t;
+  }
+}
+
+// Largest of v over the CTA (no NaN reaches it).
+__device__ __forceinline__ float smp_block_max(float v, SmpSmem& sm) {
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) sm.redf[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float m = sm.redf[0];
+  for (int w = 1; w < kSmpWarps; w++) m = fmaxf(m, sm.redf[w]);
+  __syncthreads();
+  return m;
+}
+
+// ss_argmax (tensor.c:318-328): the first index of the largest value, comparing
+// with '>' from x[0] -- so NaN entries are never chosen, and a NaN x[0] wins.
+__device__ int smp_argmax(const float* x, int n, SmpSmem& sm) {
+  float bv = -__int_as_float(0x7f800000);
+  int bi = -1;
+  for (int i = threadIdx.x; i < n; i += kSmpThreads) {
+    const float v = x[i];
+    if (v > bv) {
+      bv = v;
+      bi = i;
+    }
+  }
+  auto better = [](float v, int i, float bv2, int bi2) {
+    return i >= 0 && (bi2 < 0 || v > bv2 || (v == bv2 && i < bi2));
+  };
+  for (int o = 16; o > 0; o >>= 1) {
+    const float v = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int i = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(v, i, bv, bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sm.redf[threadIdx.x >> 5] = bv;
+    sm.redi[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  float v0 = sm.redf[0];
+  int i0 = sm.redi[0];
+  for (int w = 1; w < kSmpWarps; w++)
+    if (better(sm.redf[w], sm.redi[w], v0, i0)) {
+      v0 = sm.redf[w];
+      i0 = sm.redi[w];
+    }
+  const float x0 = x[0];
+  return (x0 != x0 || i0 < 0) ? 0 : i0;
+}
+
+__global__ void __launch_bounds__(kSmpThreads, 1) sample_kernel(SampleArgs a) {
+  extern __shared__ __align__(16) unsigned char smp_raw[];
+  SmpSmem& sm = *reinterpret_cast<SmpSmem*>(smp_raw);
+  const int n = a.n, tid = threadIdx.x;
+  int tok = 0;
+  if (a.temperature <= 0.0f) {
+    tok = smp_argmax(a.logits, n, sm);  // tensor.c:367-369
+  } else {
+    float* pr = reinterpret_cast<float*>(a.scratch);
+    unsigned* ka = reinterpret_cast<unsigned*>(pr + pad_n(n));
+    unsigned* kb = ka + pad_n(n);
+    const float T = a.temperature;
+    // logits / temperature, NaN -> -FLT_MAX (tensor.c:372-379), and the maximum
+    float m = -FLT_MAX;
+    for (int i = tid; i < n; i += kSmpThreads) {
+      const float l = a.logits[i];
+      const float v = l != l ? -FLT_MAX : __fdiv_rn(l, T);
+      pr[i] = v;
+      if (v > m) m = v;
+    }
+    m = smp_block_max(m, sm);
+    // softmax (tensor.c:154-173): e_i = exp(x_i - max) and their sum in order
+    float sum = 0.0f;
+    smp_stream(
+        n, sm,
+        [&](int i) {
+          const float e = smp_exp(__fsub_rn(pr[i], m));
+          pr[i] = e;
+          return e;
+        },
+        [&](const float* t, int, int cnt) {
+          sum = smp_seq_sum(sum, t, cnt);
+          return false;
+        });
+    if (tid == 0) sm.bcast[0] = sum;
+    __syncthreads();
+    const float inv = __fdiv_rn(1.0f, sm.bcast[0]);
+    const bool use_k = a.top_k > 0 && a.top_k < n;
+    const bool use_p = a.top_p > 0.0f && a.top_p < 1.0f;
+    for (int i = tid; i < n; i += kSmpThreads) {
+      const float p = __fmul_rn(pr[i], inv);
+      pr[i] = p;
+      if (use_k || use_p) ka[i] = p != p ? 0u : __float_as_uint(p);  // NaN sorts as 0 (tensor.c:386-390)
+    }
+    __syncthreads();
+    float thr = 0.0f, cutoff = 0.0f;
+    if (use_k || use_p) {
+      smp_sort_desc(ka, kb, n, sm);
+      if (use_k) thr = __uint_as_float(ka[a.top_k - 1]);  // tensor.c:396-401
+      if (use_p) {  // tensor.c:404-421
+        float acc = 0.0f, cut = 0.0f;
+        smp_stream(
+            n, sm,
+            [&](int i) {
+              const float v = __uint_as_float(ka[i]);
+              return use_k && v < thr ? 0.0f : v;
+            },
+            [&](const float* t, int, int cnt) { return smp_topp_walk(acc, cut, t, cnt, a.top_p); });
+        if (tid == 0) sm.bcast[1] = cut;
+        __syncthreads();
+        cutoff = sm.bcast[1];
+      }
+    }
+    auto filtered = [&](int i) {
+      float p = pr[i];
+      if (use_k && p < thr) p = 0.0f;
+      if (use_p && p < cutoff) p = 0.0f;
+      return p;
+    };
+    // renormalisation (tensor.c:426-433)
+    float tot = 0.0f;
+    smp_stream(n, sm, filtered, [&](const float* t, int, int cnt) {
+      tot = smp_seq_sum(tot, t, cnt);
+      return false;
+    });
+    if (tid == 0) sm.bcast[2] = tot;
+    __syncthreads();
+    tot = sm.bcast[2];
+    const bool renorm = tot > 0.0f;
+    const float rinv = renorm ? __fdiv_rn(1.0f, tot) : 1.0f;
+    // the draw (tensor.c:331-342, 437-448)
+    float r = 0.0f;
+    if (tid == 0) {
+      unsigned long long s = *a.rng;
+      s ^= s << 13;
+      s ^= s >> 7;
+      s ^= s << 17;
+      *a.rng = s;
+      r = __fdiv_rn(__ull2float_rn(s >> 11), 9007199254740992.0f);
+    }
+    int pick = n - 1;
+    float cdf = 0.0f;
+    smp_stream(
+        n, sm,
+        [&](int i) {
+          const float q = filtered(i);
+          return renorm ? __fmul_rn(q, rinv) : q;
+        },
+        [&](const float* t, int base, int cnt) {
+          const int j = smp_cdf_walk(cdf, t, cnt, r);
+          if (j >= 0) pick = base + j;
+          return j >= 0;
+        });
+    tok = pick;
+  }
+  if (tid == 0) {
+    *a.token = tok;
+    if (a.seq_tokens) {
+      const int pos = *a.d_pos;
+      if (pos >= 0 && pos < a.ctx && pos >= *a.fixed_until) a.seq_tokens[pos] = tok;
+      a.seq_tokens[a.ctx] = tok;
+    }
+  }
+}
+
+}  // namespace
+
+size_t sample_scratch_bytes(int n) { return 3 * pad_n(n) * sizeof(float); }
+
+cudaError_t sample_launch(const SampleArgs& a, cudaStream_t s) {
+  // the RNG is read whenever the greedy branch is not taken (NaN included)
+  if (a.n < 1 || a.n > kSampleMaxN || !a.logits || !a.token || !a.scratch || (!(a.temperature <= 0.0f) && !a.rng))
+    return cudaErrorInvalidValue;
+  const cudaError_t e =
+      cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(SmpSmem));
+  if (e != cudaSuccess) return e;
+  sample_kernel<<<1, kSmpThreads, sizeof(SmpSmem), s>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace ss

@@ -1548,6 +1548,8 @@ SS_API void ss_cuda_free(ss_cuda_ctx_t* ctx) {
     if (s.d_out) cudaFree(s.d_out);
   }
   if (c->op_stage) cudaFree(c->op_stage);
+  if (c->smp_dev) cudaFree(c->smp_dev);
+  if (c->smp_host) cudaFreeHost(c->smp_host);
   if (c->h_logits) cudaFreeHost(c->h_logits);
   if (c->h_small) cudaFreeHost(c->h_small);
   if (c->dbg_host) cudaFreeHost(c->dbg_host);
@@ -1874,6 +1876,147 @@ SS_API int ss_cuda_decode_greedy(ss_cuda_ctx_t* ctx, int32_t token, int32_t star
   });
 }
 
+// ------------------------------------------------------------ sampling
+// ss_sample (SlipStream/src/core/tensor.c:363-451) on the device: the
+// context's sampler buffers, one draw, and the generation loop of ss_generate
+// (engine.c:233-289) with the draw between decode steps on the device.
+
+constexpr size_t kSmpInOff = 256;  // caller logits after the RNG state and token
+
+void smp_reserve(Context* c, int n) {
+  if (n < 1 || n > kSampleMaxN) fail(SS_CUDA_ERROR_INVALID_PARAMS, "vocabulary size %d outside 1..%d", n, kSampleMaxN);
+  if (!c->smp_host) CK(cudaHostAlloc(reinterpret_cast<void**>(&c->smp_host), 64, cudaHostAllocDefault));
+  if (n <= c->smp_cap) return;
+  CK(cudaStreamSynchronize(c->stream));
+  if (c->smp_dev) {
+    CK(cudaFree(c->smp_dev));
+    c->smp_dev = nullptr;
+    c->smp_cap = 0;
+  }
+  const size_t bytes = kSmpInOff + round_up_sz((size_t)n * sizeof(float), 256) + sample_scratch_bytes(n);
+  CK(cudaMalloc(reinterpret_cast<void**>(&c->smp_dev), bytes));
+  c->smp_cap = n;
+}
+unsigned long long* smp_rng(Context* c) { return reinterpret_cast<unsigned long long*>(c->smp_dev); }
+int* smp_token(Context* c) { return reinterpret_cast<int*>(c->smp_dev + 8); }
+float* smp_input(Context* c) { return reinterpret_cast<float*>(c->smp_dev + kSmpInOff); }
+void* smp_scratch(Context* c) {
+  return c->smp_dev + kSmpInOff + round_up_sz((size_t)c->smp_cap * sizeof(float), 256);
+}
+
+// One draw from d_logits[n] on the context's stream; with to_seq the token
+// also becomes seq_tokens[ctrl->pos] (and the last-token slot), the input of
+// the next decode step.
+void smp_draw(Context* c, const float* d_logits, int n, float temperature, float top_p, int top_k, bool to_seq) {
+  SampleArgs a;
+  a.logits = d_logits;
+  a.n = n;
+  a.temperature = temperature;
+  a.top_p = top_p;
+  a.top_k = top_k;
+  a.rng = smp_rng(c);
+  a.token = smp_token(c);
+  if (to_seq) {
+    a.seq_tokens = c->seq_tokens;
+    a.d_pos = &c->ctrl->pos;
+    a.fixed_until = &c->ctrl->fixed_until;
+    a.ctx = c->ctx;
+  }
+  a.scratch = smp_scratch(c);
+  const cudaError_t e = sample_launch(a, c->stream);
+  if (e != cudaSuccess) fail(SS_CUDA_ERROR_BACKEND, "sampler launch: %s", cudaGetErrorString(e));
+}
+
+void smp_put_state(Context* c, const uint64_t* rng_state) {
+  c->smp_host[0] = rng_state ? (unsigned long long)*rng_state : 0ull;
+  CK(cudaMemcpyAsync(smp_rng(c), c->smp_host, 8, cudaMemcpyHostToDevice, c->stream));
+}
+// Reads the drawn token and the RNG state back (synchronous).
+int smp_get(Context* c, uint64_t* rng_state) {
+  CK(cudaMemcpyAsync(c->smp_host, smp_rng(c), 16, cudaMemcpyDeviceToHost, c->stream));
+  if (c->has_model) check_device_error(c);
+  else CK(cudaStreamSynchronize(c->stream));
+  if (rng_state) *rng_state = (uint64_t)c->smp_host[0];
+  int tok;
+  memcpy(&tok, reinterpret_cast<const uint8_t*>(c->smp_host) + 8, sizeof(int));
+  return tok;
+}
+
+// The context's full-vocabulary logits of the last single-sequence step
+// (tensor parallelism: every rank gathers them; a collective).
+const float* smp_logits(Context* c) {
+  if (c->tp_size > 1) {
+    NK(nccl_api().AllGather(c->logits, c->logits_full, (size_t)c->vocab_l, ncclFloat32, c->comm, c->stream));
+    return c->logits_full;
+  }
+  return c->logits;
+}
+
+bool smp_needs_rng(float temperature) { return !(temperature <= 0.0f); }
+
+SS_API int ss_cuda_sample_logits(ss_cuda_ctx_t* ctx, const float* logits, int32_t n, float temperature,
+                                 float top_p, int32_t top_k, uint64_t* rng_state, int32_t* token_out) {
+  return guard([&] {
+    auto* c = reinterpret_cast<Context*>(ctx);
+    if (!c) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null context");
+    if (!logits || !token_out) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null argument");
+    if (smp_needs_rng(temperature) && !rng_state) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null RNG state");
+    CK(cudaSetDevice(c->device));
+    smp_reserve(c, n);
+    CK(cudaMemcpyAsync(smp_input(c), logits, sizeof(float) * (size_t)n, cudaMemcpyHostToDevice, c->stream));
+    smp_put_state(c, rng_state);
+    smp_draw(c, smp_input(c), n, temperature, top_p, top_k, false);
+    *token_out = smp_get(c, smp_needs_rng(temperature) ? rng_state : nullptr);
+  });
+}
+
+SS_API int ss_cuda_sample(ss_cuda_ctx_t* ctx, float temperature, float top_p, int32_t top_k, uint64_t* rng_state,
+                          int32_t* token_out) {
+  return guard([&] {
+    Context* c = need_model(ctx);
+    if (!token_out) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null argument");
+    if (smp_needs_rng(temperature) && !rng_state) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null RNG state");
+    smp_reserve(c, c->vocab);
+    smp_put_state(c, rng_state);
+    smp_draw(c, smp_logits(c), c->vocab, temperature, top_p, top_k, false);
+    *token_out = smp_get(c, smp_needs_rng(temperature) ? rng_state : nullptr);
+  });
+}
+
+SS_API int ss_cuda_decode_sample(ss_cuda_ctx_t* ctx, int32_t start_pos, int32_t n_tokens, float temperature,
+                                 float top_p, int32_t top_k, uint64_t* rng_state, int32_t* ids_out) {
+  return guard([&] {
+    Context* c = need_model(ctx);
+    if (!ids_out || n_tokens <= 0) fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad arguments");
+    if (smp_needs_rng(temperature) && !rng_state) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null RNG state");
+    if (start_pos < 0 || start_pos + n_tokens - 1 > c->ctx)
+      fail(SS_CUDA_ERROR_INVALID_PARAMS, "tokens %d..%d past the context of %d", start_pos, start_pos + n_tokens - 1,
+           c->ctx);
+    if (c->cancelled.load()) fail(SS_CUDA_ERROR_CANCELLED, "cancelled");
+    smp_reserve(c, c->vocab);
+    // the draws fill seq_tokens[start_pos ...] (start_pos == ctx: one draw into
+    // the last-token slot, no step); afterwards the position is the last
+    // draw's, so ss_cuda_decode_steps continues from it
+    c->h_small[0] = start_pos;
+    c->h_small[1] = start_pos;
+    CK(cudaMemcpyAsync(c->ctrl, c->h_small, 2 * sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    c->host_pos = start_pos;
+    smp_put_state(c, rng_state);
+    for (int t = 0; t < n_tokens; t++) {
+      smp_draw(c, smp_logits(c), c->vocab, temperature, top_p, top_k, true);
+      if (t + 1 < n_tokens) run_steps(c, 1);  // forward(token, start_pos + t)
+    }
+    smp_get(c, smp_needs_rng(temperature) ? rng_state : nullptr);
+    // tokens of positions start_pos .. start_pos + n_tokens - 1; one at index
+    // ctx (past the context) sits in the last-token slot
+    const int in_ctx = std::max(0, std::min(n_tokens, c->ctx - start_pos));
+    if (in_ctx > 0)
+      CK(cudaMemcpy(ids_out, c->seq_tokens + start_pos, sizeof(int) * in_ctx, cudaMemcpyDeviceToHost));
+    if (in_ctx < n_tokens)
+      CK(cudaMemcpy(ids_out + in_ctx, c->seq_tokens + c->ctx, sizeof(int), cudaMemcpyDeviceToHost));
+  });
+}
+
 SS_API void* ss_cuda_stream(ss_cuda_ctx_t* ctx) {
   auto* c = reinterpret_cast<Context*>(ctx);
   return c ? (void*)c->stream : nullptr;
@@ -1977,7 +2120,7 @@ SS_API int ss_cuda_dequantize(int32_t type, const void* blocks, int64_t n, float
 SS_API int ss_cuda_time_kernel(ss_cuda_ctx_t* ctx, int32_t which, int32_t iters, float* ms_per_launch) {
   return guard([&] {
     Context* c = need_model(ctx);
-    if (which < 0 || which > 8 || iters <= 0 || !ms_per_launch) fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad arguments");
+    if (which < 0 || which > 10 || iters <= 0 || !ms_per_launch) fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad arguments");
     if (c->tiled && which < 6)
       fail(SS_CUDA_ERROR_INVALID_PARAMS, "per-kernel timing needs the multi-kernel step (SS_CUDA_FLAG_MULTI_KERNEL)");
     if (which >= 7) {
@@ -1985,6 +2128,11 @@ SS_API int ss_cuda_time_kernel(ss_cuda_ctx_t* ctx, int32_t which, int32_t iters,
       bt_prepare(c);
       const DevMatrix& m0 = which == 7 ? c->layers[0].gu : c->layers[0].qkv;
       qg_product(c, m0, c->bt_h, c->d, nullptr, c->max_batch, true, false);
+    }
+    if (which >= 9) {  // the sampler over the last step's logits
+      smp_reserve(c, c->vocab);
+      const uint64_t seed = 0x9E3779B97F4A7C15ull;
+      smp_put_state(c, &seed);
     }
     const int pos0 = c->host_pos;
     if (which == 6 && pos0 + iters + 3 > c->ctx)
@@ -1998,6 +2146,8 @@ SS_API int ss_cuda_time_kernel(ss_cuda_ctx_t* ctx, int32_t which, int32_t iters,
         case 6: enqueue_step(c, c->use_pdl); break;
         case 7: qg_product(c, c->layers[(size_t)l].gu, c->bt_h, c->d, nullptr, c->max_batch, false, true); break;
         case 8: qg_product(c, c->layers[0].qkv, c->bt_h, c->d, nullptr, c->max_batch, false, true); break;
+        case 9: smp_draw(c, smp_logits(c), c->vocab, 0.8f, 0.95f, 40, false); break;  // typical settings
+        case 10: smp_draw(c, smp_logits(c), c->vocab, 1.0f, 0.95f, 0, false); break;  // the longest walks
         case 0: launch_qkv(c, l, false); break;
         case 1: launch_attn(c, l, false); break;
         case 2: launch_o(c, l, false); break;
@@ -2016,7 +2166,7 @@ SS_API int ss_cuda_time_kernel(ss_cuda_ctx_t* ctx, int32_t which, int32_t iters,
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
     *ms_per_launch = ms / (float)iters;
-    if (which >= 5) {  // the lm_head advanced the device position; restore it
+    if (which >= 5 && which <= 8) {  // the lm_head advanced the device position; restore it
       CK(cudaMemcpyAsync(c->ctrl, &c->host_pos, sizeof(int), cudaMemcpyHostToDevice, c->stream));
       CK(cudaStreamSynchronize(c->stream));
       check_device_error(c);

@@ -14,6 +14,7 @@
 #include "gguf_view.h"
 #include "misc_kernels.cuh"
 #include "qgemm.cuh"
+#include "sample.h"
 #include "step_kernel.cuh"
 #include "tp_nccl.h"
 
@@ -234,6 +235,12 @@ struct Context {
   int batch_count = 0;
   uint8_t* op_stage = nullptr;
   size_t op_stage_cap = 0;
+
+  // on-device sampling (sample.cu), grown on demand for smp_cap logits:
+  // [RNG state u64][drawn token int] | 256: caller logits | sampler scratch
+  uint8_t* smp_dev = nullptr;
+  int smp_cap = 0;
+  unsigned long long* smp_host = nullptr;  // pinned: RNG state, token
 
   std::vector<void*> allocations;
 };

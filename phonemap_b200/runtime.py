@@ -35,7 +35,8 @@ EXPORTED = [
     "ss_cuda_time_kernel", "ss_cuda_kernel_bytes", "ss_cuda_argmax_noalloc",
     "ss_cuda_step_trace", "ss_cuda_tp_unique_id", "ss_cuda_test_fail_next_step",
     "ss_cuda_matmul_batch", "ss_cuda_prefill_batch", "ss_cuda_decode_greedy_batch",
-    "ss_cuda_embed", "ss_cuda_scheduler_embed",
+    "ss_cuda_embed", "ss_cuda_scheduler_embed", "ss_cuda_sample_logits", "ss_cuda_sample",
+    "ss_cuda_decode_sample",
 ]
 
 
@@ -126,6 +127,11 @@ def load_library() -> ctypes.CDLL:
     lib.ss_cuda_argmax_noalloc.argtypes = [vp, ctypes.c_int32, vp, vp]
     lib.ss_cuda_step_trace.argtypes = [vp, _i64p, ctypes.c_int64]
     lib.ss_cuda_tp_unique_id.argtypes = [vp]
+    u64p = ctypes.POINTER(ctypes.c_uint64)
+    fl, i32 = ctypes.c_float, ctypes.c_int32
+    lib.ss_cuda_sample_logits.argtypes = [vp, _f32p, i32, fl, fl, i32, u64p, _i32p]
+    lib.ss_cuda_sample.argtypes = [vp, fl, fl, i32, u64p, _i32p]
+    lib.ss_cuda_decode_sample.argtypes = [vp, i32, i32, fl, fl, i32, u64p, _i32p]
     _lib = lib
     return lib
 
@@ -299,6 +305,39 @@ class CudaModel:
         _check(self._lib.ss_cuda_decode_read(self._h, int(first_pos), int(n), _i(out)))
         return [int(v) for v in out]
 
+    # ---- sampling on the device (ss_sample, tensor.c:363-451)
+    def sample_logits(self, logits, temperature: float, top_p: float = 1.0, top_k: int = 0,
+                      state: int = 0) -> tuple[int, int]:
+        """ss_sample over host logits: (token, RNG state after the draw)."""
+        lg = np.ascontiguousarray(logits, np.float32)
+        st = ctypes.c_uint64(int(state))
+        tok = ctypes.c_int32(-1)
+        _check(self._lib.ss_cuda_sample_logits(self._h, _f(lg), lg.size, float(temperature),
+                                               float(top_p), int(top_k), ctypes.byref(st),
+                                               ctypes.byref(tok)))
+        return int(tok.value), int(st.value)
+
+    def sample(self, temperature: float, top_p: float = 1.0, top_k: int = 0,
+               state: int = 0) -> tuple[int, int]:
+        """ss_sample over the last step's logits (on the device)."""
+        st = ctypes.c_uint64(int(state))
+        tok = ctypes.c_int32(-1)
+        _check(self._lib.ss_cuda_sample(self._h, float(temperature), float(top_p), int(top_k),
+                                        ctypes.byref(st), ctypes.byref(tok)))
+        return int(tok.value), int(st.value)
+
+    def decode_sample(self, start_pos: int, n_tokens: int, temperature: float, top_p: float = 1.0,
+                      top_k: int = 0, state: int = 0) -> tuple[list[int], int]:
+        """ss_generate's loop on the device: n_tokens draws, the first from the
+        current logits, each next one after a decode step of the previous draw
+        at start_pos, start_pos + 1, ...  Returns (tokens, RNG state)."""
+        out = np.zeros(n_tokens, np.int32)
+        st = ctypes.c_uint64(int(state))
+        _check(self._lib.ss_cuda_decode_sample(self._h, int(start_pos), int(n_tokens),
+                                               float(temperature), float(top_p), int(top_k),
+                                               ctypes.byref(st), _i(out)))
+        return [int(v) for v in out], int(st.value)
+
     def greedy(self, prompt, n_steps: int) -> list[int]:
         """Prefill + greedy decode; same convention as oracle._Model.greedy."""
         first = self.prefill(prompt, 0)
@@ -332,7 +371,7 @@ class CudaModel:
         return {k: int(x) for k, x in zip(keys, v)}
 
     KERNELS = {"qkv": 0, "attention": 1, "o": 2, "gate_up": 3, "down": 4, "lm_head": 5, "step": 6,
-               "product_gate_up": 7, "product_qkv_l2": 8}
+               "product_gate_up": 7, "product_qkv_l2": 8, "sample": 9, "sample_topp": 10}
 
     def time_kernel(self, which: str, iters: int) -> float:
         """Average ms per isolated launch of one step kernel (clobbers state)."""

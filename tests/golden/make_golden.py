@@ -7,6 +7,8 @@ sources by oracle/build_ref.py) on the seeded synthetic GGUF models and records:
 * ``<config>.npz`` -- prompt, greedy token IDs (temperature 0) for N steps,
   logits at a few steps, a fingerprint of the GGUF bytes, and the int8 K/V rows
   plus scales of one (layer, position).
+* ``sample.npz`` -- the reference's ss_sample draws on the cases of
+  ``sample_cases.py``.
 * ``ops.npz`` -- small known-answer vectors of the single ops: Q4_0/Q8_0
   dequantization of seeded blocks (including edge blocks: zero scale, extreme
   nibbles, subnormal/negative scales), dequant-matvec, RMSNorm, RoPE, softmax,
@@ -233,6 +235,21 @@ def make_embed_fixture() -> None:
     print(f"embed: {sorted(k for k in fx if k.endswith('_embed'))}")
 
 
+def make_sample_fixture() -> None:
+    """sample.npz: the reference's ss_sample (tensor.c:363-451) on every case of
+    tests/golden/sample_cases.py -- DRAWS chained draws each: the tokens, the
+    RNG states after each draw, and a digest of the logits drawn from."""
+    from tests.golden import sample_cases as sc
+    fx = {}
+    for name, (make, *_rest) in sc.CASES.items():
+        toks, states = sc.draws(oracle.ref_sample, name)
+        fx[f"{name}/digest"] = np.frombuffer(sc.digest(make()), np.uint8)
+        fx[f"{name}/tokens"] = np.array(toks, np.int32)
+        fx[f"{name}/states"] = np.array(states, np.uint64)
+    np.savez_compressed(os.path.join(OUT, "sample.npz"), **fx)
+    print(f"sample: {len(sc.CASES)} cases")
+
+
 def main() -> int:
     if not oracle.ref_available() and not oracle.build_ref():
         print("reference build unavailable", file=sys.stderr)
@@ -245,6 +262,8 @@ def main() -> int:
             make_argmax_fixture()
         elif n == "embed":
             make_embed_fixture()
+        elif n == "sample":
+            make_sample_fixture()
         else:
             make_model_fixture(n)
     return 0
