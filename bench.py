@@ -51,6 +51,9 @@ def parse_args():
     ap.add_argument("--config", default="llama2-7b")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--sample", default="0.8,0.95,40",
+                    help="temperature,top_p,top_k of the sampled-decode measurement reported beside "
+                         "the greedy one (one GPU); 'off' skips it")
     ap.add_argument("--profile-kernel", default=None,
                     choices=["qkv", "attention", "o", "gate_up", "down", "lm_head", "step",
                              "product_gate_up", "product_qkv_l2"],
@@ -397,6 +400,31 @@ def run_ours(args):
                "h2d_bytes_per_step": 4 + 8, "d2h_bytes_per_step": 4 * m.vocab + 4 + 4,
                "api": "ss_cuda_forward (host token in, host logits + argmax out, synchronous)"}
 
+    # ---- sampled generation (ss_sample on the device between steps,
+    # ss_cuda_decode_sample): K draws and K - 1 steps from the prompt's logits,
+    # device-timed on the context's stream; then one draw alone
+    sampled = None
+    if tp == 1 and args.sample != "off":
+        st, sp, sk = args.sample.split(",")
+        st, sp, sk = float(st), float(sp), int(sk)
+        m.reset()
+        m.prefill(prompt, 0)
+        m.decode_sample(P, min(W, 4) + 1, st, sp, sk, 0x9E3779B97F4A7C15)  # warm-up (sampler buffers)
+        m.reset()
+        m.prefill(prompt, 0)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        s_ids, _ = m.decode_sample(P, K, st, sp, sk, 0x9E3779B97F4A7C15)
+        ev1.record(stream)
+        ev1.synchronize()
+        s_ms = ev0.elapsed_time(ev1)
+        draw_ms = m.time_kernel("sample" if (st, sp, sk) == (0.8, 0.95, 40) else "sample_topp", 20)
+        sampled = {"value": round(K / (s_ms / 1000.0), 2), "unit": "tokens/s",
+                   "settings": {"temperature": st, "top_p": sp, "top_k": sk},
+                   "ms_per_token": round(s_ms / K, 4), "ms_per_draw": round(draw_ms, 4),
+                   "api": "ss_cuda_decode_sample (draws on the device, one CTA, the reference's "
+                          "summation order)", "first_ids": s_ids[:8]}
+
     # ---- roofline of the dominant kernel.  Persistent step: the one kernel
     # is the whole step; its algorithmic bytes are the step's (all weights at
     # the GGUF's bytes per weight + norms + one embedding row + the int8 K/V
@@ -457,6 +485,7 @@ def run_ours(args):
                               "peak": round(tp * peak, 1), "peak_source": peak_kind,
                               "gpus_per_sequence": tp},
             "e2e": e2e,
+            **({"sampled": sampled} if sampled else {}),
             "gpu_launches": int(stats["kernels_per_step"] * K),
             **({"host_link": host_link} if host_link else {}),
             "clocks": sampler.summary(),

@@ -41,6 +41,7 @@ struct SmpSmem {
   float redf[kSmpWarps];
   int redi[kSmpWarps];
   float bcast[4];
+  int bcasti[4];
 };
 
 __host__ __device__ __forceinline__ size_t pad_n(int n) { return ((size_t)n + 63) & ~(size_t)63; }
@@ -102,45 +103,67 @@ __device__ __forceinline__ void smp_stream(int n, SmpSmem& sm, Fill fill, Eat ea
   }
 }
 
+// The sequential walks below read their tile 16 values at a time and issue the
+// next 16 values' loads before the current 16 additions, so each addition
+// waits only for the previous one.
+struct Smp16 {
+  float4 a, b, c, d;
+};
+__device__ __forceinline__ Smp16 smp_ld16(const float* t, int g) {
+  const float4* t4 = reinterpret_cast<const float4*>(t) + 4 * g;
+  return {t4[0], t4[1], t4[2], t4[3]};
+}
+__device__ __forceinline__ float smp_at(const Smp16& v, int k) {
+  const float4& q = k < 4 ? v.a : k < 8 ? v.b : k < 12 ? v.c : v.d;
+  const int r = k & 3;
+  return r == 0 ? q.x : r == 1 ? q.y : r == 2 ? q.z : q.w;
+}
+
 // s + t[0] + t[1] + ... in order, each addition rounded.
 __device__ __forceinline__ float smp_seq_sum(float s, const float* t, int cnt) {
-  int j = 0;
-  const float4* t4 = reinterpret_cast<const float4*>(t);
-#pragma unroll 4
-  for (; j + 4 <= cnt; j += 4) {
-    const float4 v = t4[j >> 2];
-    s = __fadd_rn(s, v.x);
-    s = __fadd_rn(s, v.y);
-    s = __fadd_rn(s, v.z);
-    s = __fadd_rn(s, v.w);
+  const int ng = cnt >> 4;
+  Smp16 cur = ng > 0 ? smp_ld16(t, 0) : Smp16{};
+  for (int g = 0; g < ng; g++) {
+    const Smp16 nxt = smp_ld16(t, min(g + 1, ng - 1));
+#pragma unroll
+    for (int k = 0; k < 16; k++) s = __fadd_rn(s, smp_at(cur, k));
+    cur = nxt;
   }
-  for (; j < cnt; j++) s = __fadd_rn(s, t[j]);
+  for (int j = ng * 16; j < cnt; j++) s = __fadd_rn(s, t[j]);
   return s;
 }
 
 // The top-p walk over sorted probabilities (tensor.c:408-416): acc adds each
 // positive value in order; the first value at which acc >= top_p is the
 // cutoff.  Adding 0 in place of a non-positive (or NaN) value leaves acc
-// unchanged, so four additions run back to back and one comparison of the
-// fourth finds whether any reached top_p (acc never decreases).
+// unchanged, and acc never decreases, so 16 additions run back to back and one
+// comparison of the last finds whether any reached top_p (the group is then
+// walked again one value at a time).
 __device__ __forceinline__ bool smp_topp_walk(float& acc, float& cut, const float* t, int cnt, float top_p) {
   auto pos = [](float v) { return v > 0.0f ? v : 0.0f; };
-  int j = 0;
-  const float4* t4 = reinterpret_cast<const float4*>(t);
-  for (; j + 4 <= cnt; j += 4) {
-    const float4 v = t4[j >> 2];
-    const float a1 = __fadd_rn(acc, pos(v.x));
-    const float a2 = __fadd_rn(a1, pos(v.y));
-    const float a3 = __fadd_rn(a2, pos(v.z));
-    const float a4 = __fadd_rn(a3, pos(v.w));
-    if (a4 >= top_p) {
-      cut = a1 >= top_p ? v.x : a2 >= top_p ? v.y : a3 >= top_p ? v.z : v.w;
-      acc = a4;
-      return true;
+  const int ng = cnt >> 4;
+  Smp16 cur = ng > 0 ? smp_ld16(t, 0) : Smp16{};
+  for (int g = 0; g < ng; g++) {
+    const Smp16 nxt = smp_ld16(t, min(g + 1, ng - 1));
+    float a = acc;
+#pragma unroll
+    for (int k = 0; k < 16; k++) a = __fadd_rn(a, pos(smp_at(cur, k)));
+    if (a >= top_p) {
+      float b = acc;
+#pragma unroll
+      for (int k = 0; k < 16; k++) {
+        b = __fadd_rn(b, pos(smp_at(cur, k)));
+        if (b >= top_p) {
+          cut = smp_at(cur, k);
+          acc = b;
+          return true;
+        }
+      }
     }
-    acc = a4;
+    acc = a;
+    cur = nxt;
   }
-  for (; j < cnt; j++) {
+  for (int j = ng * 16; j < cnt; j++) {
     acc = __fadd_rn(acc, pos(t[j]));
     if (acc >= top_p) {
       cut = t[j];
@@ -151,25 +174,86 @@ __device__ __forceinline__ bool smp_topp_walk(float& acc, float& cut, const floa
 }
 
 // The CDF walk (tensor.c:440-446): the first index whose running sum exceeds
-// r, or -1.  Each running sum is compared on its own (a NaN one compares
-// false, as in the reference).
+// r, or -1.  The addends are non-negative, so a group of 16 can hold the first
+// such index only if its last sum is not <= r (which also catches a NaN sum,
+// which the per-value walk of the group then compares false, as the reference
+// does).
 __device__ __forceinline__ int smp_cdf_walk(float& cdf, const float* t, int cnt, float r) {
-  int j = 0;
-  const float4* t4 = reinterpret_cast<const float4*>(t);
-  for (; j + 4 <= cnt; j += 4) {
-    const float4 v = t4[j >> 2];
-    const float c1 = __fadd_rn(cdf, v.x);
-    const float c2 = __fadd_rn(c1, v.y);
-    const float c3 = __fadd_rn(c2, v.z);
-    const float c4 = __fadd_rn(c3, v.w);
-    if (r < c1 || r < c2 || r < c3 || r < c4) return j + (r < c1 ? 0 : r < c2 ? 1 : r < c3 ? 2 : 3);
-    cdf = c4;
+  const int ng = cnt >> 4;
+  Smp16 cur = ng > 0 ? smp_ld16(t, 0) : Smp16{};
+  for (int g = 0; g < ng; g++) {
+    const Smp16 nxt = smp_ld16(t, min(g + 1, ng - 1));
+    float c = cdf;
+#pragma unroll
+    for (int k = 0; k < 16; k++) c = __fadd_rn(c, smp_at(cur, k));
+    if (!(c <= r)) {
+      float b = cdf;
+#pragma unroll
+      for (int k = 0; k < 16; k++) {
+        b = __fadd_rn(b, smp_at(cur, k));
+        if (r < b) return 16 * g + k;
+      }
+    }
+    cdf = c;
+    cur = nxt;
   }
-  for (; j < cnt; j++) {
+  for (int j = ng * 16; j < cnt; j++) {
     cdf = __fadd_rn(cdf, t[j]);
     if (r < cdf) return j;
   }
   return -1;
+}
+
+// Order-preserving compaction of the filtered probabilities that are not 0
+// (NaN included) into cv / ci (value, index); returns their count.  A running
+// sum in index order skips exactly these zeros: every addend is +0 or
+// positive, so adding +0 leaves the sum's bits unchanged, and the CDF walk can
+// first exceed r only where its sum grows.
+template <class Filter>
+__device__ int smp_compact(int n, Filter filter, float* cv, int* ci, SmpSmem& sm) {
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  int total = 0;
+  for (int base = 0; base < n; base += 4 * kSmpThreads) {
+    const int i0 = base + 4 * tid;
+    float q[4];
+    int c = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      q[j] = i0 + j < n ? filter(i0 + j) : 0.0f;
+      c += q[j] != 0.0f;
+    }
+    int inc = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += t;
+    }
+    if (lane == 31) sm.redi[w] = inc;
+    __syncthreads();
+    if (w == 0) {
+      const int v = sm.redi[lane];
+      int x = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += t;
+      }
+      sm.redi[lane] = x - v;
+      if (lane == 31) sm.bcasti[0] = x;
+    }
+    __syncthreads();
+    int off = total + sm.redi[w] + inc - c;
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+      if (q[j] != 0.0f) {
+        cv[off] = q[j];
+        ci[off] = i0 + j;
+        off++;
+      }
+    total += sm.bcasti[0];
+    __syncthreads();
+  }
+  return total;
 }
 
 // Descending sort of n keys (non-negative floats' bits) from ka, result in ka
@@ -364,9 +448,26 @@ __global__ void __launch_bounds__(kSmpThreads, 1) sample_kernel(SampleArgs a) {
       smp_sort_desc(ka, kb, n, sm);
       if (use_k) thr = __uint_as_float(ka[a.top_k - 1]);  // tensor.c:396-401
       if (use_p) {  // tensor.c:404-421
+        // with top-k, the sorted values past the last one equal to the
+        // threshold are zeroed and cannot move the sum: walk [0, nw) only
+        if (tid == 0) {
+          int lo = n, hi = n;
+          if (use_k) {
+            const unsigned tb = ka[a.top_k - 1];
+            lo = a.top_k;
+            while (lo < hi) {
+              const int mid = (lo + hi) >> 1;
+              if (ka[mid] < tb) hi = mid;
+              else lo = mid + 1;
+            }
+          }
+          sm.bcasti[1] = lo;
+        }
+        __syncthreads();
+        const int nw = sm.bcasti[1];
         float acc = 0.0f, cut = 0.0f;
         smp_stream(
-            n, sm,
+            nw, sm,
             [&](int i) {
               const float v = __uint_as_float(ka[i]);
               return use_k && v < thr ? 0.0f : v;
@@ -383,9 +484,14 @@ __global__ void __launch_bounds__(kSmpThreads, 1) sample_kernel(SampleArgs a) {
       if (use_p && p < cutoff) p = 0.0f;
       return p;
     };
+    // the non-zero filtered probabilities in index order (the sort's keys are
+    // no longer needed: values into ka, indices into kb)
+    float* cv = reinterpret_cast<float*>(ka);
+    int* ci = reinterpret_cast<int*>(kb);
+    const int nz = smp_compact(n, filtered, cv, ci, sm);
     // renormalisation (tensor.c:426-433)
     float tot = 0.0f;
-    smp_stream(n, sm, filtered, [&](const float* t, int, int cnt) {
+    smp_stream(nz, sm, [&](int i) { return cv[i]; }, [&](const float* t, int, int cnt) {
       tot = smp_seq_sum(tot, t, cnt);
       return false;
     });
@@ -407,14 +513,10 @@ __global__ void __launch_bounds__(kSmpThreads, 1) sample_kernel(SampleArgs a) {
     int pick = n - 1;
     float cdf = 0.0f;
     smp_stream(
-        n, sm,
-        [&](int i) {
-          const float q = filtered(i);
-          return renorm ? __fmul_rn(q, rinv) : q;
-        },
+        nz, sm, [&](int i) { return renorm ? __fmul_rn(cv[i], rinv) : cv[i]; },
         [&](const float* t, int base, int cnt) {
           const int j = smp_cdf_walk(cdf, t, cnt, r);
-          if (j >= 0) pick = base + j;
+          if (j >= 0) pick = ci[base + j];
           return j >= 0;
         });
     tok = pick;

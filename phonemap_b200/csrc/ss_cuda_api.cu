@@ -2123,7 +2123,7 @@ SS_API int ss_cuda_time_kernel(ss_cuda_ctx_t* ctx, int32_t which, int32_t iters,
     if (which < 0 || which > 10 || iters <= 0 || !ms_per_launch) fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad arguments");
     if (c->tiled && which < 6)
       fail(SS_CUDA_ERROR_INVALID_PARAMS, "per-kernel timing needs the multi-kernel step (SS_CUDA_FLAG_MULTI_KERNEL)");
-    if (which >= 7) {
+    if (which == 7 || which == 8) {
       if (!bt_eligible(c)) fail(SS_CUDA_ERROR_INVALID_PARAMS, "the tensor-core product needs the tiled layout");
       bt_prepare(c);
       const DevMatrix& m0 = which == 7 ? c->layers[0].gu : c->layers[0].qkv;
