@@ -139,8 +139,9 @@ int ss_cuda_stats(const ss_cuda_ctx_t *ctx, int64_t *out, int32_t n);
  * the tensor-core gate/up product of max_batch tokens (the kernel alone, its
  * activation pieces built once before), or 8 the same for layer 0's Q/K/V
  * matrix at every launch (L2-resident where it fits), or 9 / 10 one sampler
- * draw (ss_cuda_sample) over the last step's logits with temperature 0.8,
- * top_p 0.95, top_k 40 / temperature 1, top_p 0.95, no top-k, and writes the
+ * draw (ss_cuda_sample) over the last step's logits with the reference's
+ * default settings (temperature 0.7, top_p 0.9, top_k 40: ss_default_params,
+ * engine.c:42-51) / temperature 1, top_p 0.95, no top-k, and writes the
  * average milliseconds per launch.  0..5 exist only in the multi-kernel step,
  * 7 and 8 only where the matrices are in the tiled layout.  Clobbers the
  * activations and the K/V rows it passes over; call ss_cuda_reset before

@@ -11,9 +11,11 @@
 // next tile of addends (the exponentials, the sorted keys, the filtered
 // probabilities) in shared memory.  Everything else is parallel and exact: the
 // maximum, the element-wise steps (IEEE division and multiplication, no
-// contraction), and the sort (a stable LSD radix sort of the probabilities'
-// bits; equal probabilities add the same values in any order, so ties need no
-// particular order).
+// contraction), and the ordering for top-k / top-p: with top-k a radix select
+// of the k-th largest probability, then a shared-memory sort of the values at
+// or above it (the only ones the top-p walk can add); with top-p alone a
+// stable LSD radix sort of all of them.  Equal probabilities add the same
+// values in any order, so ties need no particular order.
 //
 // One CTA of 1024 threads does the whole draw -- the running sums are the
 // critical path and a single SM keeps the vectors (at most a few MB) in L2.
@@ -348,6 +350,104 @@ __device__ void smp_sort_desc(unsigned* ka, unsigned* kb, int n, SmpSmem& sm) {
   }
 }
 
+// The key of rank k (1 = largest) among n keys: four 8-bit digit passes from
+// the top, each counting the digits of the keys that match the digits chosen
+// so far (warp-aggregated shared-memory atomics) and choosing the digit whose
+// cumulative count from the top reaches the remaining rank.  Exact; the
+// result is what ka[k - 1] would be after the descending sort.
+__device__ unsigned smp_select_kth(const unsigned* keys, int n, int k, SmpSmem& sm) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  unsigned prefix = 0u, pmask = 0u;
+  int kk = k;
+  for (int b = 3; b >= 0; b--) {
+    const int sh = 8 * b;
+    if (tid < kSmpBins) sm.digit_base[tid] = 0u;
+    __syncthreads();
+    for (int base = 0; base < n; base += 8 * kSmpThreads) {
+      unsigned d[8];
+#pragma unroll
+      for (int r = 0; r < 8; r++) {
+        const int i = base + r * kSmpThreads + tid;
+        const unsigned key = i < n ? keys[i] : 0u;
+        d[r] = (i < n && (key & pmask) == prefix) ? (key >> sh) & 255u : 256u;
+      }
+#pragma unroll
+      for (int r = 0; r < 8; r++) {
+        const unsigned peers = __match_any_sync(0xffffffffu, d[r]);
+        if (d[r] < 256u && lane == __ffs(peers) - 1) atomicAdd(&sm.digit_base[d[r]], (unsigned)__popc(peers));
+      }
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int cum = 0, dstar = 0;
+      for (int dd = 255; dd >= 0; dd--) {
+        const int c = (int)sm.digit_base[dd];
+        if (cum + c >= kk) {
+          dstar = dd;
+          break;
+        }
+        cum += c;
+      }
+      sm.bcasti[2] = (int)(prefix | ((unsigned)dstar << sh));
+      sm.bcasti[3] = kk - cum;
+    }
+    __syncthreads();
+    prefix = (unsigned)sm.bcasti[2];
+    kk = sm.bcasti[3];
+    pmask |= 255u << sh;
+    __syncthreads();  // digit_base and bcasti are reused by the next pass
+  }
+  return prefix;
+}
+
+constexpr int kSmpSmall = 2 * kSmpTile;  // keys the shared-memory sort takes (the two tiles)
+
+// The keys >= tk, gathered (in any order) into shared memory and sorted there
+// high to low (bitonic, padded with 0 to a power of two), then copied to
+// out[0, count).  Returns their count, or -1 (nothing written) when there are
+// more than kSmpSmall of them.
+__device__ int smp_gather_sort(const unsigned* keys, int n, unsigned tk, unsigned* out, SmpSmem& sm) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  unsigned* sk = reinterpret_cast<unsigned*>(&sm.tile[0][0]);
+  if (tid == 0) sm.bcasti[0] = 0;
+  __syncthreads();
+  for (int base = 0; base < n; base += kSmpThreads) {
+    const int i = base + tid;
+    const unsigned key = i < n ? keys[i] : 0u;
+    const bool take = i < n && key >= tk;
+    const unsigned bal = __ballot_sync(0xffffffffu, take);
+    int first = 0;
+    if (lane == 0 && bal) first = atomicAdd(&sm.bcasti[0], __popc(bal));
+    first = __shfl_sync(0xffffffffu, first, 0);
+    const int slot = first + __popc(bal & ((1u << lane) - 1u));
+    if (take && slot < kSmpSmall) sk[slot] = key;
+  }
+  __syncthreads();
+  const int cnt = sm.bcasti[0];
+  if (cnt > kSmpSmall) return -1;  // uniform
+  int np2 = 2;
+  while (np2 < cnt) np2 <<= 1;
+  for (int i = cnt + tid; i < np2; i += kSmpThreads) sk[i] = 0u;
+  __syncthreads();
+  for (int kq = 2; kq <= np2; kq <<= 1)
+    for (int j = kq >> 1; j > 0; j >>= 1) {
+      for (int i = tid; i < np2; i += kSmpThreads) {
+        const int ij = i ^ j;
+        if (ij > i) {
+          const unsigned x = sk[i], y = sk[ij];
+          if ((i & kq) == 0 ? x < y : x > y) {
+            sk[i] = y;
+            sk[ij] = x;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  for (int i = tid; i < cnt; i += kSmpThreads) out[i] = sk[i];
+  __syncthreads();
+  return cnt;
+}
+
 // Largest of v over the CTA (no NaN reaches it).
 __device__ __forceinline__ float smp_block_max(float v, SmpSmem& sm) {
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -444,39 +544,49 @@ __global__ void __launch_bounds__(kSmpThreads, 1) sample_kernel(SampleArgs a) {
     }
     __syncthreads();
     float thr = 0.0f, cutoff = 0.0f;
-    if (use_k || use_p) {
-      smp_sort_desc(ka, kb, n, sm);
-      if (use_k) thr = __uint_as_float(ka[a.top_k - 1]);  // tensor.c:396-401
-      if (use_p) {  // tensor.c:404-421
-        // with top-k, the sorted values past the last one equal to the
-        // threshold are zeroed and cannot move the sum: walk [0, nw) only
-        if (tid == 0) {
-          int lo = n, hi = n;
-          if (use_k) {
-            const unsigned tb = ka[a.top_k - 1];
-            lo = a.top_k;
+    // the probabilities high to low for the top-p walk: sorted[0, nw)
+    const unsigned* sorted = ka;
+    int nw = n;
+    if (use_k) {
+      // the threshold is the k-th largest probability (tensor.c:396-401)
+      const unsigned tk = smp_select_kth(ka, n, a.top_k, sm);
+      thr = __uint_as_float(tk);
+      if (use_p) {
+        // past the values >= the threshold everything is zeroed and cannot
+        // move the walk's sum: only those need sorting
+        nw = smp_gather_sort(ka, n, tk, kb, sm);
+        sorted = kb;
+        if (nw < 0) {  // too many for shared memory: the full sort
+          smp_sort_desc(ka, kb, n, sm);
+          sorted = ka;
+          if (tid == 0) {
+            int lo = a.top_k, hi = n;
             while (lo < hi) {
               const int mid = (lo + hi) >> 1;
-              if (ka[mid] < tb) hi = mid;
+              if (ka[mid] < tk) hi = mid;
               else lo = mid + 1;
             }
+            sm.bcasti[1] = lo;
           }
-          sm.bcasti[1] = lo;
+          __syncthreads();
+          nw = sm.bcasti[1];
         }
-        __syncthreads();
-        const int nw = sm.bcasti[1];
-        float acc = 0.0f, cut = 0.0f;
-        smp_stream(
-            nw, sm,
-            [&](int i) {
-              const float v = __uint_as_float(ka[i]);
-              return use_k && v < thr ? 0.0f : v;
-            },
-            [&](const float* t, int, int cnt) { return smp_topp_walk(acc, cut, t, cnt, a.top_p); });
-        if (tid == 0) sm.bcast[1] = cut;
-        __syncthreads();
-        cutoff = sm.bcast[1];
       }
+    } else if (use_p) {
+      smp_sort_desc(ka, kb, n, sm);
+    }
+    if (use_p) {  // tensor.c:404-421
+      float acc = 0.0f, cut = 0.0f;
+      smp_stream(
+          nw, sm,
+          [&](int i) {
+            const float v = __uint_as_float(sorted[i]);
+            return use_k && v < thr ? 0.0f : v;
+          },
+          [&](const float* t, int, int cnt) { return smp_topp_walk(acc, cut, t, cnt, a.top_p); });
+      if (tid == 0) sm.bcast[1] = cut;
+      __syncthreads();
+      cutoff = sm.bcast[1];
     }
     auto filtered = [&](int i) {
       float p = pr[i];

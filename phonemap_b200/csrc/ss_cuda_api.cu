@@ -2146,7 +2146,7 @@ SS_API int ss_cuda_time_kernel(ss_cuda_ctx_t* ctx, int32_t which, int32_t iters,
         case 6: enqueue_step(c, c->use_pdl); break;
         case 7: qg_product(c, c->layers[(size_t)l].gu, c->bt_h, c->d, nullptr, c->max_batch, false, true); break;
         case 8: qg_product(c, c->layers[0].qkv, c->bt_h, c->d, nullptr, c->max_batch, false, true); break;
-        case 9: smp_draw(c, smp_logits(c), c->vocab, 0.8f, 0.95f, 40, false); break;  // typical settings
+        case 9: smp_draw(c, smp_logits(c), c->vocab, 0.7f, 0.9f, 40, false); break;  // ss_default_params
         case 10: smp_draw(c, smp_logits(c), c->vocab, 1.0f, 0.95f, 0, false); break;  // the longest walks
         case 0: launch_qkv(c, l, false); break;
         case 1: launch_attn(c, l, false); break;
