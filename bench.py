@@ -198,6 +198,24 @@ def cpu_reference_run(cfg, path, n_max, budget_s=20.0, start_pos=0):
     return n / dt, cores, kind, sample
 
 
+def cpu_sample_run(logits, temperature, top_p, top_k, draws=20):
+    """Times the reference's own ss_sample (tensor.c:363-451; oracle/_ref, or
+    the C restatement when the reference build is absent) on the host: `draws`
+    chained draws from one logits vector, one thread (ss_sample is serial).
+    Returns (ms per draw, kind)."""
+    import oracle
+    if oracle.ref_available():
+        fn, kind = oracle.ref_sample, "reference"
+    else:
+        fn, kind = (lambda x, t, p, k, s: oracle.sample(x, t, p, k, s, 0)), "port"
+    state = 0x9E3779B97F4A7C15
+    fn(logits, temperature, top_p, top_k, state)
+    t = time.perf_counter()
+    for _ in range(draws):
+        _, state = fn(logits, temperature, top_p, top_k, state)
+    return (time.perf_counter() - t) / draws * 1000.0, kind
+
+
 def synth_prompt(cfg):
     from phonemap_b200 import synth
     return synth.prompt_tokens(cfg)
@@ -412,7 +430,8 @@ def run_ours(args):
         m.prefill(prompt, 0)
         m.decode_sample(P, min(W, 4) + 1, st, sp, sk, 0x9E3779B97F4A7C15)  # warm-up (sampler buffers)
         m.reset()
-        m.prefill(prompt, 0)
+        first_logits = np.empty(m.vocab, np.float32)
+        m.prefill(prompt, 0, logits=first_logits)
         torch.cuda.synchronize()
         ev0.record(stream)
         s_ids, _ = m.decode_sample(P, K, st, sp, sk, 0x9E3779B97F4A7C15)
@@ -425,6 +444,10 @@ def run_ours(args):
                    "ms_per_token": round(s_ms / K, 4), "ms_per_draw": round(draw_ms, 4),
                    "api": "ss_cuda_decode_sample (draws on the device, one CTA, the reference's "
                           "summation order)", "first_ids": s_ids[:8]}
+        if rank == 0 and not args.no_cpu_baseline:
+            cpu_ms, cpu_kind = cpu_sample_run(first_logits, st, sp, sk)
+            sampled["cpu_baseline"] = {"ms_per_draw": round(cpu_ms, 4), "cores": 1, "kind": cpu_kind,
+                                       "sample": "20 chained ss_sample draws from the prompt's logits"}
 
     # ---- roofline of the dominant kernel.  Persistent step: the one kernel
     # is the whole step; its algorithmic bytes are the step's (all weights at
