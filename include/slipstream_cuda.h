@@ -274,6 +274,17 @@ int ss_cuda_sample(ss_cuda_ctx_t *ctx, float temperature, float top_p, int32_t t
  * from that token. */
 int ss_cuda_decode_sample(ss_cuda_ctx_t *ctx, int32_t start_pos, int32_t n_tokens, float temperature,
                           float top_p, int32_t top_k, uint64_t *rng_state, int32_t *ids_out);
+/* Several sequences sampled together (no reference counterpart: the reference
+ * decodes one sequence; contexts with max_batch > 1): the sampled twin of
+ * ss_cuda_decode_greedy_batch.  tokens[s] is sequence s's token at start_pos;
+ * each of n_steps steps runs sequences 0..n_seq-1 through the many-token step,
+ * draws every sequence's next token from its own logits with ss_sample's rule
+ * and its own RNG state rng_states[s] (one draw each, one CTA per sequence, all
+ * in one launch), and feeds the draws back on the device.  ids_out is
+ * [n_steps][n_seq] (positions start_pos + 1 ..); rng_states is updated. */
+int ss_cuda_decode_sample_batch(ss_cuda_ctx_t *ctx, const int32_t *tokens, int32_t n_seq, int32_t start_pos,
+                                int32_t n_steps, float temperature, float top_p, int32_t top_k,
+                                uint64_t *rng_states, int32_t *ids_out);
 
 /* The cudaStream_t all work of this context runs on. */
 void *ss_cuda_stream(ss_cuda_ctx_t *ctx);

@@ -502,6 +502,13 @@ __global__ void __launch_bounds__(kSmpThreads, 1) sample_kernel(SampleArgs a) {
   extern __shared__ __align__(16) unsigned char smp_raw[];
   SmpSmem& sm = *reinterpret_cast<SmpSmem*>(smp_raw);
   const int n = a.n, tid = threadIdx.x;
+  if (blockIdx.x > 0) {  // draw b of a batch: its own logits, RNG state, token and scratch
+    const int b = blockIdx.x;
+    a.logits += (size_t)b * a.logits_stride;
+    if (a.rng) a.rng += b;
+    a.token += (size_t)b * a.token_stride;
+    a.scratch = static_cast<unsigned char*>(a.scratch) + (size_t)b * a.scratch_stride;
+  }
   int tok = 0;
   if (a.temperature <= 0.0f) {
     tok = smp_argmax(a.logits, n, sm);  // tensor.c:367-369
@@ -649,10 +656,13 @@ cudaError_t sample_launch(const SampleArgs& a, cudaStream_t s) {
   // the RNG is read whenever the greedy branch is not taken (NaN included)
   if (a.n < 1 || a.n > kSampleMaxN || !a.logits || !a.token || !a.scratch || (!(a.temperature <= 0.0f) && !a.rng))
     return cudaErrorInvalidValue;
+  if (a.batch < 1 || (a.batch > 1 && (a.seq_tokens || a.logits_stride < (size_t)a.n || a.token_stride < 1 ||
+                                      a.scratch_stride < sample_scratch_bytes(a.n))))
+    return cudaErrorInvalidValue;
   const cudaError_t e =
       cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(SmpSmem));
   if (e != cudaSuccess) return e;
-  sample_kernel<<<1, kSmpThreads, sizeof(SmpSmem), s>>>(a);
+  sample_kernel<<<a.batch, kSmpThreads, sizeof(SmpSmem), s>>>(a);
   return cudaGetLastError();
 }
 

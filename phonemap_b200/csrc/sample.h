@@ -25,9 +25,16 @@ struct SampleArgs {
   const int* fixed_until = nullptr;
   int ctx = 0;
   void* scratch = nullptr;  // sample_scratch_bytes(n), device
+  // several independent draws in one launch, one CTA each (seq_tokens must be
+  // null): draw b reads logits + b * logits_stride, advances rng[b], writes
+  // token[b * token_stride] and uses scratch + b * scratch_stride bytes
+  int batch = 1;
+  size_t logits_stride = 0;
+  int token_stride = 0;
+  size_t scratch_stride = 0;
 };
 
-// Device scratch one launch over n logits needs (probabilities and two key
+// Device scratch one draw over n logits needs (probabilities and two key
 // arrays of the sort).
 size_t sample_scratch_bytes(int n);
 // Largest n the kernel takes.

@@ -1881,24 +1881,31 @@ SS_API int ss_cuda_decode_greedy(ss_cuda_ctx_t* ctx, int32_t token, int32_t star
 // context's sampler buffers, one draw, and the generation loop of ss_generate
 // (engine.c:233-289) with the draw between decode steps on the device.
 
-constexpr size_t kSmpInOff = 256;  // caller logits after the RNG state and token
+constexpr int kSmpMaxDraws = kQgMaxT;                   // draws per launch (the batch limit)
+constexpr size_t kSmpTokOff = 8 * kSmpMaxDraws;          // tokens after the RNG states
+constexpr size_t kSmpInOff = 512;                        // caller logits after the header
 
-void smp_reserve(Context* c, int n) {
+size_t smp_slice(int n) { return round_up_sz(sample_scratch_bytes(n), 256); }
+
+void smp_reserve(Context* c, int n, int batch = 1) {
   if (n < 1 || n > kSampleMaxN) fail(SS_CUDA_ERROR_INVALID_PARAMS, "vocabulary size %d outside 1..%d", n, kSampleMaxN);
-  if (!c->smp_host) CK(cudaHostAlloc(reinterpret_cast<void**>(&c->smp_host), 64, cudaHostAllocDefault));
-  if (n <= c->smp_cap) return;
+  if (!c->smp_host) CK(cudaHostAlloc(reinterpret_cast<void**>(&c->smp_host), kSmpInOff, cudaHostAllocDefault));
+  if (n <= c->smp_cap && batch <= c->smp_batch) return;
+  n = std::max(n, c->smp_cap);
+  batch = std::max(batch, c->smp_batch);
   CK(cudaStreamSynchronize(c->stream));
   if (c->smp_dev) {
     CK(cudaFree(c->smp_dev));
     c->smp_dev = nullptr;
-    c->smp_cap = 0;
+    c->smp_cap = c->smp_batch = 0;
   }
-  const size_t bytes = kSmpInOff + round_up_sz((size_t)n * sizeof(float), 256) + sample_scratch_bytes(n);
+  const size_t bytes = kSmpInOff + round_up_sz((size_t)n * sizeof(float), 256) + (size_t)batch * smp_slice(n);
   CK(cudaMalloc(reinterpret_cast<void**>(&c->smp_dev), bytes));
   c->smp_cap = n;
+  c->smp_batch = batch;
 }
 unsigned long long* smp_rng(Context* c) { return reinterpret_cast<unsigned long long*>(c->smp_dev); }
-int* smp_token(Context* c) { return reinterpret_cast<int*>(c->smp_dev + 8); }
+int* smp_token(Context* c) { return reinterpret_cast<int*>(c->smp_dev + kSmpTokOff); }
 float* smp_input(Context* c) { return reinterpret_cast<float*>(c->smp_dev + kSmpInOff); }
 void* smp_scratch(Context* c) {
   return c->smp_dev + kSmpInOff + round_up_sz((size_t)c->smp_cap * sizeof(float), 256);
@@ -1927,20 +1934,47 @@ void smp_draw(Context* c, const float* d_logits, int n, float temperature, float
   if (e != cudaSuccess) fail(SS_CUDA_ERROR_BACKEND, "sampler launch: %s", cudaGetErrorString(e));
 }
 
-void smp_put_state(Context* c, const uint64_t* rng_state) {
-  c->smp_host[0] = rng_state ? (unsigned long long)*rng_state : 0ull;
-  CK(cudaMemcpyAsync(smp_rng(c), c->smp_host, 8, cudaMemcpyHostToDevice, c->stream));
+// `batch` draws at once, one per row of d_logits ([batch][stride]), with RNG
+// states smp_rng(c)[0..batch); the tokens go to tokens[b * token_stride].
+void smp_draw_batch(Context* c, const float* d_logits, size_t stride, int n, int batch, float temperature,
+                    float top_p, int top_k, int* tokens, int token_stride) {
+  SampleArgs a;
+  a.logits = d_logits;
+  a.n = n;
+  a.temperature = temperature;
+  a.top_p = top_p;
+  a.top_k = top_k;
+  a.rng = smp_rng(c);
+  a.token = tokens;
+  a.scratch = smp_scratch(c);
+  a.batch = batch;
+  a.logits_stride = stride;
+  a.token_stride = token_stride;
+  a.scratch_stride = smp_slice(c->smp_cap);
+  const cudaError_t e = sample_launch(a, c->stream);
+  if (e != cudaSuccess) fail(SS_CUDA_ERROR_BACKEND, "sampler launch: %s", cudaGetErrorString(e));
 }
-// Reads the drawn token and the RNG state back (synchronous).
-int smp_get(Context* c, uint64_t* rng_state) {
-  CK(cudaMemcpyAsync(c->smp_host, smp_rng(c), 16, cudaMemcpyDeviceToHost, c->stream));
+
+// RNG states of draws 0..n-1 to the device (NULL: zeros; greedy draws never
+// read them).
+void smp_put_states(Context* c, const uint64_t* states, int n) {
+  for (int i = 0; i < n; i++) c->smp_host[i] = states ? (unsigned long long)states[i] : 0ull;
+  CK(cudaMemcpyAsync(smp_rng(c), c->smp_host, 8 * (size_t)n, cudaMemcpyHostToDevice, c->stream));
+}
+void smp_put_state(Context* c, const uint64_t* rng_state) { smp_put_states(c, rng_state, 1); }
+// Reads the header (RNG states, tokens) back, synchronously; copies n states
+// out when `states` is not NULL and returns draw 0's token.
+int smp_get_n(Context* c, uint64_t* states, int n) {
+  CK(cudaMemcpyAsync(c->smp_host, c->smp_dev, kSmpInOff, cudaMemcpyDeviceToHost, c->stream));
   if (c->has_model) check_device_error(c);
   else CK(cudaStreamSynchronize(c->stream));
-  if (rng_state) *rng_state = (uint64_t)c->smp_host[0];
+  if (states)
+    for (int i = 0; i < n; i++) states[i] = (uint64_t)c->smp_host[i];
   int tok;
-  memcpy(&tok, reinterpret_cast<const uint8_t*>(c->smp_host) + 8, sizeof(int));
+  memcpy(&tok, reinterpret_cast<const uint8_t*>(c->smp_host) + kSmpTokOff, sizeof(int));
   return tok;
 }
+int smp_get(Context* c, uint64_t* rng_state) { return smp_get_n(c, rng_state, 1); }
 
 // The context's full-vocabulary logits of the last single-sequence step
 // (tensor parallelism: every rank gathers them; a collective).
@@ -2014,6 +2048,52 @@ SS_API int ss_cuda_decode_sample(ss_cuda_ctx_t* ctx, int32_t start_pos, int32_t 
       CK(cudaMemcpy(ids_out, c->seq_tokens + start_pos, sizeof(int) * in_ctx, cudaMemcpyDeviceToHost));
     if (in_ctx < n_tokens)
       CK(cudaMemcpy(ids_out + in_ctx, c->seq_tokens + c->ctx, sizeof(int), cudaMemcpyDeviceToHost));
+  });
+}
+
+// Sampled decode of sequences 0..n_seq-1 for n_steps, the batched twin of
+// the greedy loop (bt_decode_greedy): after each many-token step one sampler
+// launch draws every sequence's token from its row of logits with its own RNG
+// state (smp_rng(c)[s]), into the greedy-token row the feedback kernel reads.
+void bt_decode_sample(Context* c, const int32_t* tok, int n_seq, int start_pos, int n_steps, float temperature,
+                      float top_p, int top_k) {
+  if (n_steps < 1 || start_pos + n_steps > c->ctx)
+    fail(SS_CUDA_ERROR_INVALID_PARAMS, "decode runs past the context");
+  if (n_seq < 1 || n_seq > c->max_batch)
+    fail(SS_CUDA_ERROR_INVALID_PARAMS, "n_seq %d outside 1..%d (max_batch)", n_seq, c->max_batch);
+  std::vector<int> ps((size_t)n_seq, start_pos), sq((size_t)n_seq);
+  for (int s = 0; s < n_seq; s++) sq[(size_t)s] = s;
+  bt_stage(c, tok, ps.data(), sq.data(), n_seq);
+  for (int k = 0; k < n_steps; k++) {
+    if (c->cancelled.load()) fail(SS_CUDA_ERROR_CANCELLED, "cancelled");
+    bt_launch(c, n_seq, n_seq);
+    smp_draw_batch(c, c->bt_logits, (size_t)c->vocab_l, c->vocab, n_seq, temperature, top_p, top_k,
+                   c->bt_meta + 3 * kQgMaxT, 1);
+    bt_feed_kernel<<<1, kQgMaxT, 0, c->stream>>>(c->bt_meta, kQgMaxT, n_seq, c->bt_ids, kQgMaxT, c->ctx);
+    CK(cudaGetLastError());
+  }
+  c->steps_run += (long long)n_seq * n_steps;
+}
+
+SS_API int ss_cuda_decode_sample_batch(ss_cuda_ctx_t* ctx, const int32_t* tokens, int32_t n_seq, int32_t start_pos,
+                                       int32_t n_steps, float temperature, float top_p, int32_t top_k,
+                                       uint64_t* rng_states, int32_t* ids_out) {
+  return guard([&] {
+    Context* c = need_model(ctx);
+    if (!tokens || !ids_out) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null argument");
+    if (smp_needs_rng(temperature) && !rng_states) fail(SS_CUDA_ERROR_INVALID_PARAMS, "null RNG states");
+    if (!bt_eligible(c)) fail(SS_CUDA_ERROR_INVALID_PARAMS, "batched decode needs the many-token step");
+    if (n_seq < 1 || n_seq > c->max_batch)
+      fail(SS_CUDA_ERROR_INVALID_PARAMS, "n_seq %d outside 1..%d (max_batch)", n_seq, c->max_batch);
+    smp_reserve(c, c->vocab, n_seq);
+    smp_put_states(c, smp_needs_rng(temperature) ? rng_states : nullptr, n_seq);
+    bt_decode_sample(c, tokens, n_seq, start_pos, n_steps, temperature, top_p, top_k);
+    smp_get_n(c, smp_needs_rng(temperature) ? rng_states : nullptr, n_seq);
+    std::vector<int> rows((size_t)n_steps * kQgMaxT);
+    CK(cudaMemcpy(rows.data(), c->bt_ids + (size_t)(start_pos + 1) * kQgMaxT, sizeof(int) * rows.size(),
+                  cudaMemcpyDeviceToHost));
+    for (int k = 0; k < n_steps; k++)
+      for (int s = 0; s < n_seq; s++) ids_out[(size_t)k * n_seq + s] = rows[(size_t)k * kQgMaxT + s];
   });
 }
 

@@ -236,11 +236,12 @@ struct Context {
   uint8_t* op_stage = nullptr;
   size_t op_stage_cap = 0;
 
-  // on-device sampling (sample.cu), grown on demand for smp_cap logits:
-  // [RNG state u64][drawn token int] | 256: caller logits | sampler scratch
+  // on-device sampling (sample.cu), grown on demand for smp_cap logits and
+  // smp_batch draws at once: [32 RNG states u64][32 drawn tokens int] |
+  // caller logits | smp_batch scratch slices
   uint8_t* smp_dev = nullptr;
-  int smp_cap = 0;
-  unsigned long long* smp_host = nullptr;  // pinned: RNG state, token
+  int smp_cap = 0, smp_batch = 0;
+  unsigned long long* smp_host = nullptr;  // pinned copy of the header
 
   std::vector<void*> allocations;
 };

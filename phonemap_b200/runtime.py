@@ -36,7 +36,7 @@ EXPORTED = [
     "ss_cuda_step_trace", "ss_cuda_tp_unique_id", "ss_cuda_test_fail_next_step",
     "ss_cuda_matmul_batch", "ss_cuda_prefill_batch", "ss_cuda_decode_greedy_batch",
     "ss_cuda_embed", "ss_cuda_scheduler_embed", "ss_cuda_sample_logits", "ss_cuda_sample",
-    "ss_cuda_decode_sample",
+    "ss_cuda_decode_sample", "ss_cuda_decode_sample_batch",
 ]
 
 
@@ -132,6 +132,7 @@ def load_library() -> ctypes.CDLL:
     lib.ss_cuda_sample_logits.argtypes = [vp, _f32p, i32, fl, fl, i32, u64p, _i32p]
     lib.ss_cuda_sample.argtypes = [vp, fl, fl, i32, u64p, _i32p]
     lib.ss_cuda_decode_sample.argtypes = [vp, i32, i32, fl, fl, i32, u64p, _i32p]
+    lib.ss_cuda_decode_sample_batch.argtypes = [vp, _i32p, i32, i32, i32, fl, fl, i32, u64p, _i32p]
     _lib = lib
     return lib
 
@@ -337,6 +338,20 @@ class CudaModel:
                                                float(temperature), float(top_p), int(top_k),
                                                ctypes.byref(st), _i(out)))
         return [int(v) for v in out], int(st.value)
+
+    def decode_sample_batch(self, tokens, start_pos: int, n_steps: int, temperature: float,
+                            top_p: float = 1.0, top_k: int = 0,
+                            states=None) -> tuple[np.ndarray, list[int]]:
+        """Sequences 0..len(tokens)-1 decoded together with a draw per sequence
+        each step (its own RNG state); returns (int32 [n_steps, n_seq] tokens of
+        positions start_pos+1 .., the RNG states afterwards)."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        out = np.zeros((n_steps, len(t)), np.int32)
+        st = np.array(states if states is not None else [0] * len(t), np.uint64)
+        _check(self._lib.ss_cuda_decode_sample_batch(
+            self._h, _i(t), len(t), int(start_pos), int(n_steps), float(temperature), float(top_p),
+            int(top_k), st.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), _i(out)))
+        return out, [int(v) for v in st]
 
     def greedy(self, prompt, n_steps: int) -> list[int]:
         """Prefill + greedy decode; same convention as oracle._Model.greedy."""

@@ -11,6 +11,8 @@ ss_cuda_decode_sample) against ss_sample (SlipStream/src/core/tensor.c:
 * the generation loop on the device (engine.c:233-289): its tokens equal a host
   replay that draws with the restatement from the same context's logits step
   by step, on the persistent step and on the many-token step;
+* several sequences sampled together (ss_cuda_decode_sample_batch) against a
+  host replay of the same batched steps;
 * temperature <= 0 is the greedy argmax and leaves the RNG state alone.
 """
 from __future__ import annotations
@@ -154,3 +156,46 @@ def test_sampler_time(name):
         longest = m.time_kernel("sample_topp", 20)
     report(name, "sampler", vocab=cfg.vocab, ms_typical=typical, ms_top_p_only=longest)
     assert typical > 0 and longest > 0
+
+
+@pytest.mark.parametrize("name", ["tinyllama", "tiny-q8"])
+def test_decode_sample_batch_matches_host_replay(name):
+    """Several sequences sampled together (ss_cuda_decode_sample_batch): every
+    sequence's tokens and RNG state equal a host replay that steps the same
+    sequences with host logits (ss_cuda_forward, n_seq > 1) and draws each row
+    with the restatement; temperature 0 is the greedy batched loop."""
+    cfg = configs.get(name)
+    path = synth.ensure_gguf(cfg)
+    n_seq, steps, plen = 4, 12, 8
+    rng = np.random.default_rng(77)
+    prompts = rng.integers(0, cfg.vocab, size=(n_seq, plen)).astype(np.int32)
+    states0 = [int(v) for v in rng.integers(1, 2**62, size=n_seq, dtype=np.int64)]
+    with runtime.CudaModel(path, cfg.ctx, max_batch=n_seq) as m:
+        for t, p, k in [(0.7, 0.9, 40), (1.0, 0.95, 0), (1.3, 1.0, 0)]:
+            m.reset()
+            first = m.prefill_batch(prompts, 0)
+            ids, states = m.decode_sample_batch(first, plen, steps, t, p, k, states0)
+            m.reset()
+            toks = m.prefill_batch(prompts, 0)
+            lg = np.empty((n_seq, m.vocab), np.float32)
+            st, want = list(states0), []
+            for step in range(steps):
+                m.forward_batch(toks, plen + step, logits=lg)
+                nxt = []
+                for s in range(n_seq):
+                    tok, st[s] = oracle.sample(lg[s], t, p, k, st[s], 1)
+                    nxt.append(tok)
+                want.append(nxt)
+                toks = nxt
+            assert ids.tolist() == want, (t, p, k)
+            assert states == st
+        m.reset()
+        first = m.prefill_batch(prompts, 0)
+        ids, states = m.decode_sample_batch(first, plen, steps, 0.0, 0.9, 40, states0)
+        assert states == states0
+        m.reset()
+        first = m.prefill_batch(prompts, 0)
+        assert ids.tolist() == m.decode_greedy_batch(first, plen, steps).tolist()
+        with pytest.raises(runtime.SSCudaError):
+            m.decode_sample_batch([1] * (n_seq + 1), plen, 2, 1.0, 1.0, 0, [1] * (n_seq + 1))
+    report(name, "decode_sample_batch", n_seq=n_seq, steps=steps, settings=3, identical=True)
