@@ -608,6 +608,28 @@ def run_ours_batch(args):
                "api": "ss_cuda_forward with n_seq = B (host tokens in, host logits [B][vocab] + "
                       "greedy tokens out, synchronous)"}
 
+    # sampled: the same B sequences with a draw per sequence each step
+    # (ss_cuda_decode_sample_batch), device-timed like the greedy loop
+    sampled = None
+    if args.sample != "off":
+        st, sp, sk = args.sample.split(",")
+        st, sp, sk = float(st), float(sp), int(sk)
+        seeds = [0x9E3779B97F4A7C15 + 2 * i for i in range(B)]
+        m.reset()
+        first = m.prefill_batch(prompts, 0)
+        warm, _ = m.decode_sample_batch(first, P, max(W, 1), st, sp, sk, seeds)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        s_ids, _ = m.decode_sample_batch(warm[-1], P + max(W, 1), K, st, sp, sk, seeds)
+        ev1.record(stream)
+        ev1.synchronize()
+        s_ms = max_over_ranks(pg, ev0.elapsed_time(ev1))
+        sampled = {"value": round(world * B * K / (s_ms / 1000.0), 2), "unit": "tokens/s",
+                   "settings": {"temperature": st, "top_p": sp, "top_k": sk},
+                   "ms_per_step": round(s_ms / K, 4),
+                   "api": "ss_cuda_decode_sample_batch (one draw per sequence on the device each step)",
+                   "first_ids": s_ids[0].tolist()[:8]}
+
     # roofline: the tensor-core gate/up product at B tokens (the kernel alone,
     # cycling the layers so the weights stream from HBM); algorithmic bytes =
     # the matrix's GGUF bytes (weights + fp16 scales) + the activation pieces
@@ -642,6 +664,7 @@ def run_ours_batch(args):
                               "frac": round(step_gbs / peak, 4), "unit": "GB/s", "peak": peak,
                               "peak_source": peak_kind},
             "e2e": e2e,
+            **({"sampled": sampled} if sampled else {}),
             "gpu_launches": int(stats["kernels_per_batched_step"] * K),
             "clocks": sampler.summary(),
             "step_impl": "many-token step: tensor-core product per matrix (CUDA graph per batch shape)",
