@@ -83,3 +83,28 @@ def test_tp_teacher_forced(name, path):
         assert np.abs(r["logits"][s][top] - vals).max() / am < tol, f"step {s}"
         if float(vals[0] - vals[1]) > tol * am:
             assert r["ids"][s] == ref[s], f"step {s}"
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_tp_sampling(path):
+    """Sampling under tensor parallelism: every rank gathers the logits and
+    draws the same token.  ss_cuda_decode_sample equals a host loop of
+    ss_cuda_sample + ss_cuda_forward; each of those draws is the restatement's
+    (the GPU's exponential) on the step's gathered logits and RNG state; every
+    rank drew the same tokens."""
+    import oracle
+    if _gpus() < 2:
+        pytest.skip("needs 2 GPUs")
+    cfg = configs.get("tinyllama")
+    g = load_golden("tinyllama")
+    prompt = [int(t) for t in g["prompt"]]
+    t, p, k, seed = 0.7, 0.9, 40, 0x9E3779B97F4A7C15
+    r = tp.greedy(synth.ensure_gguf(cfg), int(g["ctx"]), prompt, 16, 2, flags=PATHS[path],
+                  sample=(t, p, k, seed))
+    sd = r["sampled"]
+    assert sd["dev_ids"] == sd["ids"]
+    assert sd["dev_state"] == sd["states"][-1]
+    for i, tok in enumerate(sd["ids"]):
+        assert oracle.sample(sd["logits"][i], t, p, k, sd["states"][i], 1) == (tok, sd["states"][i + 1])
+    for dev_ids, host_ids in r["sampled_ids_other"]:
+        assert dev_ids == sd["dev_ids"] and host_ids == sd["ids"]
