@@ -176,6 +176,13 @@ bool ss_cuda_matvec_q4_0(ss_cuda_ctx_t *ctx, float *out, const void *mat, const 
                          int32_t rows, int32_t cols);
 bool ss_cuda_matvec_q8_0(ss_cuda_ctx_t *ctx, float *out, const void *mat, const float *vec,
                          int32_t rows, int32_t cols);
+/* Twin of ss_metal_matvec_q4_K (metal_backend.h:44-49, kernel metal_backend.m:
+ * 111-154; called from ss_matmul_dispatch, layer_scheduler.c:255-256): W in
+ * Q4_K super-blocks (144 B per 256 weights), cols a multiple of 256.  Each
+ * weight is dequantized as ss_dequantize does (bit-identical); the dot
+ * product is summed in fp32 in the GPU's order (one warp per row). */
+bool ss_cuda_matvec_q4_K(ss_cuda_ctx_t *ctx, float *out, const void *mat, const float *vec,
+                         int32_t rows, int32_t cols);
 /* Twins of ss_metal_begin_batch / ss_metal_end_batch (metal_backend.h:64-70). */
 void ss_cuda_begin_batch(ss_cuda_ctx_t *ctx);
 void ss_cuda_end_batch(ss_cuda_ctx_t *ctx);
@@ -340,7 +347,12 @@ int ss_cuda_matmul_batch(ss_cuda_ctx_t *ctx, const char *name, const float *x, i
  * layout -- bit-identical to ss_dequantize (SlipStream/src/core/quantize.c:
  * 389-442) for Q4_0 / Q8_0. */
 int ss_cuda_dequantize_tensor(ss_cuda_ctx_t *ctx, const char *name, float *out, int64_t n);
-/* Device dequantisation of raw GGUF blocks (host in, host out); no context. */
+/* Device dequantisation of raw GGUF blocks (host in, host out); no context.
+ * Every type of ss_dequantize (SlipStream/src/core/quantize.c:389-442): F32,
+ * F16, Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q8_1 (blocks of 32) and Q2_K, Q3_K, Q4_K,
+ * Q5_K, Q6_K (super-blocks of 256), bit-identical to the reference; n a
+ * multiple of the block size.  Other types: SS_CUDA_ERROR_INVALID_PARAMS (the
+ * reference zero-fills them). */
 int ss_cuda_dequantize(int32_t type, const void *blocks, int64_t n, float *out);
 /* int8 K/V row and scales of (layer, pos) (layer_scheduler.h:19-34 layout).
  * Under tensor parallelism: this rank's kv heads (n_kv_heads / tp_size * head_dim

@@ -187,6 +187,8 @@ CUDA_BRANCH = """#ifdef SS_HAS_CUDA
             cuda_ok = ss_cuda_matvec_q4_0((ss_cuda_ctx_t *)sched->cuda_ctx, out, mat, vec, rows, cols);
         else if (type == GGML_TYPE_Q8_0)
             cuda_ok = ss_cuda_matvec_q8_0((ss_cuda_ctx_t *)sched->cuda_ctx, out, mat, vec, rows, cols);
+        else if (type == GGML_TYPE_Q4_K)
+            cuda_ok = ss_cuda_matvec_q4_K((ss_cuda_ctx_t *)sched->cuda_ctx, out, mat, vec, rows, cols);
         else if (type == GGML_TYPE_F32)
             cuda_ok = ss_cuda_matvec((ss_cuda_ctx_t *)sched->cuda_ctx, out, (const float *)mat, vec, rows, cols);
         if (cuda_ok) return;

@@ -26,7 +26,10 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
-enum { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8 };
+enum {
+    T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8, T_Q8_1 = 9,
+    T_Q2_K = 10, T_Q3_K = 11, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14
+};
 
 /* ---------------------------------------------------------------- numerics */
 
@@ -53,42 +56,201 @@ float sso_f16_to_f32(uint16_t h) {
     return f;
 }
 
-static size_t type_size(int t) { return t == T_F32 ? 4 : t == T_F16 ? 2 : t == T_Q4_0 ? 18 : t == T_Q8_0 ? 34 : 0; }
-static int block_size(int t) { return (t == T_Q4_0 || t == T_Q8_0) ? 32 : 1; }
+/* Bytes per block and values per block (SS/src/core/gguf_loader.c:22-60). */
+static size_t type_size(int t) {
+    switch (t) {
+        case T_F32: return 4;
+        case T_F16: return 2;
+        case T_Q4_0: return 18;
+        case T_Q4_1: return 20;
+        case T_Q5_0: return 22;
+        case T_Q5_1: return 24;
+        case T_Q8_0: return 34;
+        case T_Q8_1: return 40;
+        case T_Q2_K: return 84;
+        case T_Q3_K: return 110;
+        case T_Q4_K: return 144;
+        case T_Q5_K: return 176;
+        case T_Q6_K: return 210;
+        default: return 0;
+    }
+}
+static int block_size(int t) {
+    if (t == T_F32 || t == T_F16) return 1;
+    return t >= T_Q2_K && t <= T_Q6_K ? 256 : 32;
+}
 
-/* SS/src/core/quantize.c:60-72 (Q4_0) and :139-149 (Q8_0), F32 passthrough
- * (:391-393), F16 (dequant_f16). */
+static float half_at(const uint8_t *p) {
+    uint16_t h;
+    memcpy(&h, p, 2);
+    return sso_f16_to_f32(h);
+}
+
+/* The 6-bit scale and min of sub-block j of a Q4_K / Q5_K super-block
+ * (quantize.c:268-276): sub-blocks 0-3 in the low 6 bits of bytes j and j + 4,
+ * 4-7 split between the nibbles of bytes j + 4 and the top 2 bits of bytes
+ * j - 4 and j. */
+static void k4_scale_min(int j, const uint8_t *sc, float *s, float *m) {
+    int a, b;
+    if (j < 4) {
+        a = sc[j] & 63;
+        b = sc[j + 4] & 63;
+    } else {
+        a = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
+        b = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+    }
+    *s = (float)a;
+    *m = (float)b;
+}
+
+/* One block of `type` into out[0 .. block_size): the formulas of
+ * SS/src/core/quantize.c:58-383, each product and difference rounded on its own
+ * (the reference is built without FMA). */
+static void dequant_block(int type, const uint8_t *blk, float *out) {
+    switch (type) {
+        case T_Q4_0: {  /* :60-72 */
+            const float d = half_at(blk);
+            for (int i = 0; i < 16; i++) {
+                out[i] = d * ((int32_t)(blk[2 + i] & 0xF) - 8);
+                out[i + 16] = d * ((int32_t)(blk[2 + i] >> 4) - 8);
+            }
+            break;
+        }
+        case T_Q4_1: {  /* :76-89 */
+            const float d = half_at(blk), mn = half_at(blk + 2);
+            for (int i = 0; i < 16; i++) {
+                out[i] = d * (blk[4 + i] & 0xF) + mn;
+                out[i + 16] = d * (blk[4 + i] >> 4) + mn;
+            }
+            break;
+        }
+        case T_Q5_0: {  /* :93-112: the fifth bits in a 32-bit mask */
+            const float d = half_at(blk);
+            uint32_t hb;
+            memcpy(&hb, blk + 2, 4);
+            for (int i = 0; i < 16; i++) {
+                const int lo = (blk[6 + i] & 0xF) | (int)(((hb >> i) & 1) << 4);
+                const int hi = (blk[6 + i] >> 4) | (int)(((hb >> (i + 16)) & 1) << 4);
+                out[i] = (lo - 16) * d;
+                out[i + 16] = (hi - 16) * d;
+            }
+            break;
+        }
+        case T_Q5_1: {  /* :116-135 */
+            const float d = half_at(blk), mn = half_at(blk + 2);
+            uint32_t hb;
+            memcpy(&hb, blk + 4, 4);
+            for (int i = 0; i < 16; i++) {
+                const int lo = (blk[8 + i] & 0xF) | (int)(((hb >> i) & 1) << 4);
+                const int hi = (blk[8 + i] >> 4) | (int)(((hb >> (i + 16)) & 1) << 4);
+                out[i] = lo * d + mn;
+                out[i + 16] = hi * d + mn;
+            }
+            break;
+        }
+        case T_Q8_0: {  /* :139-149 */
+            const float d = half_at(blk);
+            for (int i = 0; i < 32; i++) out[i] = d * (int8_t)blk[2 + i];
+            break;
+        }
+        case T_Q8_1: {  /* :153-163: an fp32 scale (and an unused fp32 sum) */
+            float d;
+            memcpy(&d, blk, 4);
+            for (int i = 0; i < 32; i++) out[i] = d * (int8_t)blk[8 + i];
+            break;
+        }
+        case T_Q2_K: {  /* :180-215: 16-value groups, 4-bit scale and min each */
+            const uint8_t *sc = blk, *qs = blk + 16;
+            const float d = half_at(blk + 80), mn = half_at(blk + 82);
+            for (int e = 0; e < 256; e++) {
+                const int h = e >> 7, r = e & 31, j = (e & 127) >> 5;
+                const uint8_t s8 = sc[8 * h + 2 * j + (r >> 4)];
+                const float dl = d * (s8 & 0xF), ml = mn * (s8 >> 4);
+                out[e] = dl * ((int8_t)((qs[32 * h + r] >> (2 * j)) & 3)) - ml;
+            }
+            break;
+        }
+        case T_Q3_K: {  /* :219-263: 6-bit scales unpacked from 12 bytes */
+            const uint8_t *hm = blk, *qs = blk + 32;
+            const float d = half_at(blk + 108);
+            int8_t s6[16];
+            for (int i = 0; i < 16; i++) {
+                const int low = i < 8 ? (blk[96 + i] & 0xF) : (blk[96 + i - 8] >> 4);
+                const int top = (blk[104 + (i & 3)] >> (2 * (i >> 2))) & 3;
+                s6[i] = (int8_t)(low | (top << 4));
+            }
+            for (int e = 0; e < 256; e++) {
+                const int h = e >> 7, r = e & 31, j = (e & 127) >> 5;
+                const float dl = d * (s6[8 * h + 2 * j + (r >> 4)] - 32);
+                const int q = (int8_t)((qs[32 * h + r] >> (2 * j)) & 3) - ((hm[r] & (1 << (4 * h + j))) ? 0 : 4);
+                out[e] = dl * q;
+            }
+            break;
+        }
+        case T_Q4_K: {  /* :278-308 */
+            const float d = half_at(blk), mn = half_at(blk + 2);
+            const uint8_t *sc = blk + 4, *qs = blk + 16;
+            for (int c = 0; c < 4; c++) {
+                float s1, m1, s2, m2;
+                k4_scale_min(2 * c, sc, &s1, &m1);
+                k4_scale_min(2 * c + 1, sc, &s2, &m2);
+                const float d1 = d * s1, n1 = mn * m1, d2 = d * s2, n2 = mn * m2;
+                for (int l = 0; l < 32; l++) {
+                    out[64 * c + l] = d1 * (qs[32 * c + l] & 0xF) - n1;
+                    out[64 * c + 32 + l] = d2 * (qs[32 * c + l] >> 4) - n2;
+                }
+            }
+            break;
+        }
+        case T_Q5_K: {  /* :312-348 */
+            const float d = half_at(blk), mn = half_at(blk + 2);
+            const uint8_t *sc = blk + 4, *qh = blk + 16, *qs = blk + 48;
+            for (int c = 0; c < 4; c++) {
+                float s1, m1, s2, m2;
+                k4_scale_min(2 * c, sc, &s1, &m1);
+                k4_scale_min(2 * c + 1, sc, &s2, &m2);
+                const float d1 = d * s1, n1 = mn * m1, d2 = d * s2, n2 = mn * m2;
+                for (int l = 0; l < 32; l++) {
+                    out[64 * c + l] = d1 * ((qs[32 * c + l] & 0xF) + ((qh[l] >> (2 * c)) & 1 ? 16 : 0)) - n1;
+                    out[64 * c + 32 + l] = d2 * ((qs[32 * c + l] >> 4) + ((qh[l] >> (2 * c + 1)) & 1 ? 16 : 0)) - n2;
+                }
+            }
+            break;
+        }
+        case T_Q6_K: {  /* :352-383: (d * scale) * q, two roundings */
+            const float d = half_at(blk + 208);
+            for (int e = 0; e < 256; e++) {
+                const int h = e >> 7, g = (e & 127) >> 5, l = e & 31;
+                const uint8_t *ql = blk + 64 * h, *qh = blk + 128 + 32 * h;
+                const int8_t *sc = (const int8_t *)(blk + 192 + 8 * h);
+                const int lo = (g & 1) ? ql[l + 32] : ql[l];
+                const int nib = (g & 2) ? (lo >> 4) : (lo & 0xF);
+                const int q = (int8_t)(nib | (((qh[l] >> (2 * g)) & 3) << 4)) - 32;
+                out[e] = d * sc[(l >> 4) + 2 * g] * q;
+            }
+            break;
+        }
+        default:
+            memset(out, 0, sizeof(float) * (size_t)block_size(type));
+    }
+}
+
+/* SS/src/core/quantize.c:389-442 (ss_dequantize): F32 copied, F16 converted,
+ * block types block by block; an unknown type gives zeros, as the reference. */
 void sso_dequantize(const void *src, float *dst, int32_t n, int32_t type) {
     const uint8_t *p = (const uint8_t *)src;
     if (type == T_F32) { memcpy(dst, src, (size_t)n * 4); return; }
     if (type == T_F16) {
-        for (int32_t i = 0; i < n; i++) {
-            uint16_t h; memcpy(&h, p + 2 * i, 2);
-            dst[i] = sso_f16_to_f32(h);
-        }
+        for (int32_t i = 0; i < n; i++) dst[i] = half_at(p + 2 * i);
         return;
     }
-    for (int32_t b = 0; b < n / 32; b++) {
-        uint16_t dh;
-        if (type == T_Q4_0) {
-            const uint8_t *blk = p + (size_t)b * 18;
-            memcpy(&dh, blk, 2);
-            float scale = sso_f16_to_f32(dh);
-            for (int i = 0; i < 16; i++) {
-                uint8_t byte = blk[2 + i];
-                dst[b * 32 + i] = scale * ((int32_t)(byte & 0xF) - 8);
-                dst[b * 32 + i + 16] = scale * ((int32_t)(byte >> 4) - 8);
-            }
-        } else if (type == T_Q8_0) {
-            const uint8_t *blk = p + (size_t)b * 34;
-            memcpy(&dh, blk, 2);
-            float scale = sso_f16_to_f32(dh);
-            for (int i = 0; i < 32; i++) dst[b * 32 + i] = scale * (int8_t)blk[2 + i];
-        } else {
-            memset(dst, 0, (size_t)n * 4);
-            return;
-        }
+    const size_t ts = type_size(type);
+    const int bs = block_size(type);
+    if (!ts) {
+        memset(dst, 0, (size_t)n * 4);
+        return;
     }
+    for (int32_t b = 0; b < n / bs; b++) dequant_block(type, p + (size_t)b * ts, dst + (size_t)b * bs);
 }
 
 /* Sequential fp32 dot: the order the reference's vDSP_dotpr calls get. */

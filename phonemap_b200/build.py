@@ -25,10 +25,10 @@ INCLUDE = os.path.join(ROOT, "include")
 CUDA_LIB = os.path.join(LIBDIR, "libslipstream_cuda.so")
 SYNTH_LIB = os.path.join(LIBDIR, "libss_synth.so")
 
-CUDA_SOURCES = ["ss_cuda_api.cu", "noalloc_argmax.cu", "sample.cu"]
+CUDA_SOURCES = ["ss_cuda_api.cu", "noalloc_argmax.cu", "sample.cu", "quant.cu"]
 CUDA_HEADERS = ["common.cuh", "gemv.cuh", "attention.cuh", "misc_kernels.cuh",
                 "step_kernel.cuh", "qgemm.cuh", "qgemm_host.inc", "batch_kernels.cuh",
-                "batch_host.inc", "tp_nccl.h", "gguf_view.h", "sample.h",
+                "batch_host.inc", "tp_nccl.h", "gguf_view.h", "sample.h", "quant.h",
                 "ss_cuda_internal.h"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -12,7 +12,7 @@ constexpr int kWarp = 32;
 constexpr int kMaxGroupRows = 8;
 
 // GGML tensor type ids (SlipStream/src/core/gguf_loader.h:41-55).
-enum : int { kF32 = 0, kF16 = 1, kQ4_0 = 2, kQ8_0 = 8 };
+enum : int { kF32 = 0, kF16 = 1, kQ4_0 = 2, kQ8_0 = 8, kQ4_K = 12 };
 
 // ---- programmatic dependent launch (PTX griddepcontrol, sm_90+) ----------
 // wait: block until the preceding kernel in the stream has completed and its

@@ -152,27 +152,6 @@ __global__ void dequant_rows_kernel(const uint8_t* __restrict__ w, int rows, int
   }
 }
 
-// Dequantise raw GGUF blocks (AoS) to fp32.
-__global__ void dequant_blocks_kernel(const uint8_t* __restrict__ src, long long n, int type,
-                                      float* __restrict__ out) {
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long b = i >> 5;
-    const int j = (int)(i & 31);
-    if (type == kQ4_0) {
-      const uint8_t* blk = src + b * 18;
-      const float d = half_bits_to_float((uint16_t)blk[0] | ((uint16_t)blk[1] << 8));
-      const uint8_t byte = blk[2 + (j & 15)];
-      const int q = j < 16 ? (byte & 0xF) : (byte >> 4);
-      out[i] = __fmul_rn(d, (float)(q - 8));
-    } else {
-      const uint8_t* blk = src + b * 34;
-      const float d = half_bits_to_float((uint16_t)blk[0] | ((uint16_t)blk[1] << 8));
-      out[i] = __fmul_rn(d, (float)(int8_t)blk[2 + j]);
-    }
-  }
-}
-
 // fp32 GEMV (twin of the Metal `matvec` kernel, metal_backend.m:23-46): warp per
 // row, float4 loads.
 __global__ void matvec_f32_kernel(const float* __restrict__ w, const float* __restrict__ x,

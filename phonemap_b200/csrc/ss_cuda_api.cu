@@ -1332,6 +1332,10 @@ OpCacheEntry& op_weights(Context* c, const void* mat, int rows, int cols, int ty
   if (type == kF32) {
     e.f32 = dev_alloc<float>(c, (size_t)rows * cols);
     CK(cudaMemcpyAsync(e.f32, mat, sizeof(float) * (size_t)rows * cols, cudaMemcpyHostToDevice, c->stream));
+  } else if (type == kQ4_K) {
+    const size_t bytes = (size_t)rows * (cols / 256) * 144;
+    e.raw = dev_alloc<uint8_t>(c, bytes);
+    CK(cudaMemcpyAsync(e.raw, mat, bytes, cudaMemcpyHostToDevice, c->stream));
   } else {
     e.m = layout(rows, cols, type);
     e.m.data = dev_alloc<uint8_t>(c, matrix_bytes(e.m));
@@ -1361,7 +1365,8 @@ bool op_matvec(ss_cuda_ctx_t* ctx, float* out, const void* mat, const float* vec
            auto* c = reinterpret_cast<Context*>(ctx);
            if (!c || !out || !mat || !vec || rows <= 0 || cols <= 0)
              fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad matvec arguments");
-           if (type != kF32 && cols % 32) fail(SS_CUDA_ERROR_INVALID_PARAMS, "cols %% 32 != 0");
+           if (type != kF32 && cols % (type == kQ4_K ? 256 : 32))
+             fail(SS_CUDA_ERROR_INVALID_PARAMS, "cols %d not a multiple of the block size", cols);
            CK(cudaSetDevice(c->device));
            OpCacheEntry& w = op_weights(c, mat, rows, cols, type);
            const int slot = c->in_batch ? c->batch_count : 0;
@@ -1386,6 +1391,8 @@ bool op_matvec(ss_cuda_ctx_t* ctx, float* out, const void* mat, const float* vec
              const int grid = (rows * 32 + threads - 1) / threads;
              matvec_f32_kernel<<<grid, threads, 0, c->stream>>>(w.f32, s.d_x, s.d_out, rows, cols);
              CK(cudaGetLastError());
+           } else if (type == kQ4_K) {
+             CK(matvec_q4k_launch(w.raw, s.d_x, s.d_out, rows, cols, c->stream));
            } else {
              GemvLaunch g = plan_gemv_for(c, XSrc::Plain, Epi::Store, w.m);
              GemvParams p = base_params(c);
@@ -1630,6 +1637,9 @@ SS_API bool ss_cuda_matvec_q4_0(ss_cuda_ctx_t* ctx, float* out, const void* mat,
 }
 SS_API bool ss_cuda_matvec_q8_0(ss_cuda_ctx_t* ctx, float* out, const void* mat, const float* vec, int32_t rows, int32_t cols) {
   return op_matvec(ctx, out, mat, vec, rows, cols, kQ8_0);
+}
+SS_API bool ss_cuda_matvec_q4_K(ss_cuda_ctx_t* ctx, float* out, const void* mat, const float* vec, int32_t rows, int32_t cols) {
+  return op_matvec(ctx, out, mat, vec, rows, cols, kQ4_K);
 }
 
 SS_API void ss_cuda_begin_batch(ss_cuda_ctx_t* ctx) {
@@ -2178,18 +2188,17 @@ SS_API int ss_cuda_dequantize_tensor(ss_cuda_ctx_t* ctx, const char* name, float
 
 SS_API int ss_cuda_dequantize(int32_t type, const void* blocks, int64_t n, float* out) {
   return guard([&] {
-    if (!blocks || !out || n <= 0 || n % 32) fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad arguments");
-    if (type != kQ4_0 && type != kQ8_0) fail(SS_CUDA_ERROR_INVALID_PARAMS, "type %d", type);
-    const size_t in_bytes = (size_t)(n / 32) * ggml_type_size(type);
+    if (!blocks || !out || n <= 0) fail(SS_CUDA_ERROR_INVALID_PARAMS, "bad arguments");
+    if (!quant_type_size(type)) fail(SS_CUDA_ERROR_INVALID_PARAMS, "type %d", type);
+    const int bs = quant_block_size(type);
+    if (n % bs) fail(SS_CUDA_ERROR_INVALID_PARAMS, "n %lld not a multiple of the block size %d", (long long)n, bs);
+    const size_t in_bytes = (size_t)(n / bs) * quant_type_size(type);
     uint8_t* d_in = nullptr;
     float* d_out = nullptr;
     CK(cudaMalloc(&d_in, in_bytes));
     cudaError_t e = cudaMalloc(&d_out, sizeof(float) * (size_t)n);
     if (e == cudaSuccess) e = cudaMemcpy(d_in, blocks, in_bytes, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) {
-      dequant_blocks_kernel<<<1024, 256>>>(d_in, n, type, d_out);
-      e = cudaGetLastError();
-    }
+    if (e == cudaSuccess) e = dequant_launch(d_in, n, type, d_out, nullptr);
     if (e == cudaSuccess) e = cudaMemcpy(out, d_out, sizeof(float) * (size_t)n, cudaMemcpyDeviceToHost);
     cudaFree(d_in);
     if (d_out) cudaFree(d_out);

@@ -14,6 +14,7 @@
 #include "gguf_view.h"
 #include "misc_kernels.cuh"
 #include "qgemm.cuh"
+#include "quant.h"
 #include "sample.h"
 #include "step_kernel.cuh"
 #include "tp_nccl.h"
@@ -60,7 +61,8 @@ struct Ctrl {
 
 struct OpCacheEntry {
   DevMatrix m;
-  float* f32 = nullptr;  // F32 matrices stay row-major
+  float* f32 = nullptr;    // F32 matrices stay row-major
+  uint8_t* raw = nullptr;  // Q4_K matrices keep their GGUF bytes
 };
 
 // GEMV geometry knobs (defaults measured on B200; the SS_GEMV_* environment

@@ -20,7 +20,7 @@ _f32p = ctypes.POINTER(ctypes.c_float)
 _i32p = ctypes.POINTER(ctypes.c_int32)
 _i64p = ctypes.POINTER(ctypes.c_int64)
 
-Q4_0, Q8_0, F32 = 2, 8, 0
+Q4_0, Q8_0, F32, Q4_K = 2, 8, 0, 12
 
 # every symbol include/slipstream_cuda.h declares
 EXPORTED = [
@@ -36,7 +36,7 @@ EXPORTED = [
     "ss_cuda_step_trace", "ss_cuda_tp_unique_id", "ss_cuda_test_fail_next_step",
     "ss_cuda_matmul_batch", "ss_cuda_prefill_batch", "ss_cuda_decode_greedy_batch",
     "ss_cuda_embed", "ss_cuda_scheduler_embed", "ss_cuda_sample_logits", "ss_cuda_sample",
-    "ss_cuda_decode_sample", "ss_cuda_decode_sample_batch",
+    "ss_cuda_decode_sample", "ss_cuda_decode_sample_batch", "ss_cuda_matvec_q4_K",
 ]
 
 
@@ -91,7 +91,7 @@ def load_library() -> ctypes.CDLL:
     lib.ss_cuda_stats.argtypes = [vp, _i64p, ctypes.c_int32]
     lib.ss_cuda_should_use_gpu.argtypes = [ctypes.c_int32, ctypes.c_int32]
     lib.ss_cuda_should_use_gpu.restype = ctypes.c_bool
-    for fn in ("ss_cuda_matvec", "ss_cuda_matvec_q4_0", "ss_cuda_matvec_q8_0"):
+    for fn in ("ss_cuda_matvec", "ss_cuda_matvec_q4_0", "ss_cuda_matvec_q8_0", "ss_cuda_matvec_q4_K"):
         getattr(lib, fn).argtypes = [vp, _f32p, vp, _f32p, ctypes.c_int32, ctypes.c_int32]
         getattr(lib, fn).restype = ctypes.c_bool
     for fn in ("ss_cuda_begin_batch", "ss_cuda_end_batch", "ss_cuda_reset",
@@ -429,7 +429,7 @@ class CudaModel:
         out = np.empty(rows, np.float32)
         xx = np.ascontiguousarray(x, np.float32)
         fn = {Q4_0: self._lib.ss_cuda_matvec_q4_0, Q8_0: self._lib.ss_cuda_matvec_q8_0,
-              F32: self._lib.ss_cuda_matvec}[wtype]
+              Q4_K: self._lib.ss_cuda_matvec_q4_K, F32: self._lib.ss_cuda_matvec}[wtype]
         if not fn(self._h, _f(out), w_bytes.ctypes.data, _f(xx), rows, cols):
             raise SSCudaError(-7, self._lib.ss_cuda_last_error().decode())
         return out

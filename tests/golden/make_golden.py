@@ -9,6 +9,8 @@ sources by oracle/build_ref.py) on the seeded synthetic GGUF models and records:
   plus scales of one (layer, position).
 * ``sample.npz`` -- the reference's ss_sample draws on the cases of
   ``sample_cases.py``.
+* ``quant.npz`` -- the reference's dequantization of every block type it
+  handles and its Q4_K matvec, on the inputs of ``quant_cases.py``.
 * ``ops.npz`` -- small known-answer vectors of the single ops: Q4_0/Q8_0
   dequantization of seeded blocks (including edge blocks: zero scale, extreme
   nibbles, subnormal/negative scales), dequant-matvec, RMSNorm, RoPE, softmax,
@@ -250,6 +252,31 @@ def make_sample_fixture() -> None:
     print(f"sample: {len(sc.CASES)} cases")
 
 
+def make_quant_fixture() -> None:
+    """quant.npz: the reference's ss_dequantize (quantize.c:389-442) on the
+    seeded blocks of tests/golden/quant_cases.py, every type it handles, and
+    its ss_dequant_matvec (quantize.c:446-494) on the Q4_K matrix there."""
+    import ctypes
+
+    from tests.golden import quant_cases as qc
+    lib = oracle.ref_ops()
+    f32p = ctypes.POINTER(ctypes.c_float)
+    fx = {}
+    for t in qc.TYPES:
+        raw, n = qc.blocks(t)
+        out = np.empty(n, np.float32)
+        lib.ssr_dequantize(raw.ctypes.data, out.ctypes.data_as(f32p), n, t)
+        fx[f"{qc.NAMES[t]}/blocks"] = raw
+        fx[f"{qc.NAMES[t]}/values"] = out
+    raw, x = qc.q4k_matrix()
+    rows, cols = 48, 1024
+    out = np.empty(rows, np.float32)
+    lib.ssr_dequant_matvec(out.ctypes.data_as(f32p), raw.ctypes.data, x.ctypes.data_as(f32p), rows, cols, 12)
+    fx["q4k_mv/w"], fx["q4k_mv/x"], fx["q4k_mv/out"] = raw, x, out
+    np.savez_compressed(os.path.join(OUT, "quant.npz"), **fx)
+    print(f"quant: {sorted(qc.NAMES.values())}")
+
+
 def main() -> int:
     if not oracle.ref_available() and not oracle.build_ref():
         print("reference build unavailable", file=sys.stderr)
@@ -264,6 +291,8 @@ def main() -> int:
             make_embed_fixture()
         elif n == "sample":
             make_sample_fixture()
+        elif n == "quant":
+            make_quant_fixture()
         else:
             make_model_fixture(n)
     return 0
