@@ -215,12 +215,12 @@ template <class Filter>
 __device__ int smp_compact(int n, Filter filter, float* cv, int* ci, SmpSmem& sm) {
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   int total = 0;
-  for (int base = 0; base < n; base += 4 * kSmpThreads) {
-    const int i0 = base + 4 * tid;
-    float q[4];
+  for (int base = 0; base < n; base += 8 * kSmpThreads) {
+    const int i0 = base + 8 * tid;
+    float q[8];
     int c = 0;
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
+    for (int j = 0; j < 8; j++) {
       q[j] = i0 + j < n ? filter(i0 + j) : 0.0f;
       c += q[j] != 0.0f;
     }
@@ -246,7 +246,7 @@ __device__ int smp_compact(int n, Filter filter, float* cv, int* ci, SmpSmem& sm
     __syncthreads();
     int off = total + sm.redi[w] + inc - c;
 #pragma unroll
-    for (int j = 0; j < 4; j++)
+    for (int j = 0; j < 8; j++)
       if (q[j] != 0.0f) {
         cv[off] = q[j];
         ci[off] = i0 + j;
@@ -378,18 +378,32 @@ __device__ unsigned smp_select_kth(const unsigned* keys, int n, int k, SmpSmem& 
       }
     }
     __syncthreads();
-    if (tid == 0) {
-      int cum = 0, dstar = 0;
-      for (int dd = 255; dd >= 0; dd--) {
-        const int c = (int)sm.digit_base[dd];
-        if (cum + c >= kk) {
-          dstar = dd;
-          break;
-        }
-        cum += c;
+    if (tid < 32) {
+      // lane l holds digits 255 - 8 l - j (j = 0..7, high to low); the lane
+      // whose range holds the kk-th key from the top finds the digit in it
+      unsigned c[8], tot = 0;
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        c[j] = sm.digit_base[255 - 8 * lane - j];
+        tot += c[j];
       }
-      sm.bcasti[2] = (int)(prefix | ((unsigned)dstar << sh));
-      sm.bcasti[3] = kk - cum;
+      unsigned inc = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned t = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += t;
+      }
+      unsigned cum = inc - tot;
+      if (cum < (unsigned)kk && (unsigned)kk <= inc) {
+        for (int j = 0; j < 8; j++) {
+          if (cum + c[j] >= (unsigned)kk) {
+            sm.bcasti[2] = (int)(prefix | ((unsigned)(255 - 8 * lane - j) << sh));
+            sm.bcasti[3] = kk - (int)cum;
+            break;
+          }
+          cum += c[j];
+        }
+      }
     }
     __syncthreads();
     prefix = (unsigned)sm.bcasti[2];
@@ -411,16 +425,23 @@ __device__ int smp_gather_sort(const unsigned* keys, int n, unsigned tk, unsigne
   unsigned* sk = reinterpret_cast<unsigned*>(&sm.tile[0][0]);
   if (tid == 0) sm.bcasti[0] = 0;
   __syncthreads();
-  for (int base = 0; base < n; base += kSmpThreads) {
-    const int i = base + tid;
-    const unsigned key = i < n ? keys[i] : 0u;
-    const bool take = i < n && key >= tk;
-    const unsigned bal = __ballot_sync(0xffffffffu, take);
-    int first = 0;
-    if (lane == 0 && bal) first = atomicAdd(&sm.bcasti[0], __popc(bal));
-    first = __shfl_sync(0xffffffffu, first, 0);
-    const int slot = first + __popc(bal & ((1u << lane) - 1u));
-    if (take && slot < kSmpSmall) sk[slot] = key;
+  for (int base = 0; base < n; base += 4 * kSmpThreads) {
+    unsigned key[4];
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const int i = base + r * kSmpThreads + tid;
+      key[r] = i < n ? keys[i] : 0u;
+    }
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const bool take = base + r * kSmpThreads + tid < n && key[r] >= tk;
+      const unsigned bal = __ballot_sync(0xffffffffu, take);
+      int first = 0;
+      if (lane == 0 && bal) first = atomicAdd(&sm.bcasti[0], __popc(bal));
+      first = __shfl_sync(0xffffffffu, first, 0);
+      const int slot = first + __popc(bal & ((1u << lane) - 1u));
+      if (take && slot < kSmpSmall) sk[slot] = key[r];
+    }
   }
   __syncthreads();
   const int cnt = sm.bcasti[0];
